@@ -1,0 +1,214 @@
+"""ORACLE TEST INFRASTRUCTURE -- builds oracle/_ref/libnnref.so.
+
+Recipe that compiles the reference's own kernel source
+(Experts/NeuroNet_DNG/NeuroNet.cl) for the host CPU.  It reads the file where
+it lies in the reference checkout, extracts the helper block
+(NeuroNet.cl:1-420: defines, IsNaNOrInf, fActivation, Deactivation,
+Local* reductions) and every in-scope kernel by name, rewrites the OpenCL C
+spellings that C++ does not accept (vector literals, address-space
+qualifiers, __local arrays), and compiles the result together with
+oracle/ref_shim.h and oracle/ref_exec.cpp into oracle/_ref/libnnref.so.
+
+Nothing from the reference is committed: the rewritten source is written
+only to oracle/_ref/ (git-ignored).  When the reference checkout is absent
+(e.g. on a machine that only received the built files) the script exits
+without doing anything.
+
+Usage:  python oracle/build_ref.py [--reference DIR] [--force]
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import re
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+OUT_DIR = os.path.join(HERE, "_ref")
+DEFAULT_REFERENCE = "/root/reference"
+CL_RELPATH = os.path.join("Experts", "NeuroNet_DNG", "NeuroNet.cl")
+
+# Every kernel of the hot path (the in-scope subset of NeuroNet.cl).
+KERNELS = [
+    "FeedForward", "CalcOutputGradient", "CalcHiddenGradient",
+    "UpdateWeightsMomentum", "UpdateWeightsAdam",
+    "FeedForwardConv", "CalcHiddenGradientConv",
+    "UpdateWeightsConvMomentum", "UpdateWeightsConvAdam",
+    "AttentionScore", "AttentionOut", "SumMatrix", "AttentionInsideGradients",
+    "Normalize", "NormalizeWeights", "ConcatenateBuffers", "DeconcatenateBuffers",
+    "MHAttentionScore", "MHAttentionOut", "MHAttentionInsideGradients",
+    "Dropout", "BatchFeedForward", "CalcHiddenGradientBatch",
+    "UpdateBatchOptionsMomentum", "UpdateBatchOptionsAdam",
+    "LSTM_FeedForward", "LSTM_ConcatenatedGradient", "LSTM_HiddenGradient",
+    "LSTM_UpdateWeightsAdam",
+    "SoftMax_FeedForward", "SoftMax_HiddenGradient", "SoftMax_OutputGradient",
+    "SoftUpdate", "SoftUpdateAdam",
+    "Transpose", "MH2AttentionOut", "MH2AttentionInsideGradients",
+    "RevInFeedForward", "RevInHiddenGraddient", "Activation", "DeActivation",
+]
+
+
+def _match_close(text: str, start: int, open_ch: str, close_ch: str) -> int:
+    """Index just past the bracket that closes the one at text[start]."""
+    depth = 0
+    i = start
+    while i < len(text):
+        c = text[i]
+        if c == open_ch:
+            depth += 1
+        elif c == close_ch:
+            depth -= 1
+            if depth == 0:
+                return i + 1
+        i += 1
+    raise ValueError("unbalanced brackets")
+
+
+def _strip_comments(text: str) -> str:
+    text = re.sub(r"/\*.*?\*/", " ", text, flags=re.S)
+    return re.sub(r"//[^\n]*", "", text)
+
+
+def extract_kernel(src: str, name: str) -> tuple[str, str, str]:
+    """Return (full kernel text, parameter list text, body text)."""
+    m = re.search(r"__kernel\s+void\s+" + re.escape(name) + r"\s*\(", src)
+    if not m:
+        raise KeyError(name)
+    p_open = m.end() - 1
+    p_close = _match_close(src, p_open, "(", ")")
+    b_open = src.index("{", p_close)
+    b_close = _match_close(src, b_open, "{", "}")
+    return src[m.start():b_close], src[p_open + 1:p_close - 1], src[b_open:b_close]
+
+
+def rewrite(code: str) -> str:
+    """OpenCL C spellings -> C++ (inside namespace ocl of ref_shim.h)."""
+    # __local arrays declared in a body become per-work-group statics.
+    code = re.sub(r"__local\s+(float4|float2|float|int|uint)\s+(\w+)\s*\[",
+                  r"static thread_local \1 \2[", code)
+    code = re.sub(r"\b__local\b", "", code)
+    code = re.sub(r"\b__global\b", "", code)
+    code = re.sub(r"\b__constant\b", "const", code)
+    code = re.sub(r"\b__kernel\b", "", code)
+    # vector literals (floatN)(a,b,...) -> floatN(a,b,...)
+    code = re.sub(r"\(\s*(float[248])\s*\)\s*\(", r"\1(", code)
+    # scalar-to-vector casts (floatN)expr -> floatN(expr)
+    code = re.sub(r"\(\s*(float[248])\s*\)\s*([A-Za-z0-9_.]+)", r"\1(\2)", code)
+    return code
+
+
+def parse_params(params: str) -> list[tuple[str, str]]:
+    """[(kind, name)] with kind in p (pointer), i (int), u (uint), f (float)."""
+    params = _strip_comments(params)
+    out = []
+    for raw in params.split(","):
+        p = " ".join(raw.replace("\n", " ").split())
+        if not p:
+            continue
+        is_ptr = "*" in p
+        name = re.findall(r"[A-Za-z_]\w*", p)[-1]
+        toks = re.findall(r"[A-Za-z_]\w*", p)
+        if is_ptr:
+            kind = "p"
+        elif "float" in toks:
+            kind = "f"
+        elif "uint" in toks or "unsigned" in toks:
+            kind = "u"
+        else:
+            kind = "i"
+        out.append((kind, name, p))
+    return out
+
+
+# Data races in the reference source that a GPU hides (the work-group of these
+# helpers is a single SIMD wavefront, so every lane's load happens before any
+# lane's store) but a sequential work-item executor exposes.  Each patch adds
+# the one barrier that makes the GPU ordering explicit.
+RACE_PATCHES = [
+    # LocalSoftMax (NeuroNet.cl:392-408): every lane reads Temp[0] (the max
+    # returned by LocalMax) and LocalSum then stores Temp[id] with no barrier
+    # in between, so lane 0 may overwrite the max before lane 1 reads it.
+    ("float max=LocalMax(value,loc,Temp);", "float max=LocalMax(value,loc,Temp);\n   BarrierLoc"),
+]
+
+
+def generate(cl_text: str) -> str:
+    first = cl_text.index("__kernel")
+    helpers = cl_text[:first]
+    for old, new in RACE_PATCHES:
+        if helpers.count(old) != 1:
+            raise RuntimeError(f"race patch anchor not found exactly once: {old!r}")
+        helpers = helpers.replace(old, new)
+    parts = ["// GENERATED by oracle/build_ref.py from the reference NeuroNet.cl -- do not commit.",
+             '#include "ref_shim.h"', "namespace ocl {", "#line 1 \"NeuroNet.cl\"",
+             rewrite(helpers)]
+    table = []
+    for name in KERNELS:
+        text, params, body = extract_kernel(cl_text, name)
+        line = cl_text[:cl_text.index(text)].count("\n") + 1
+        parts.append(f'#line {line} "NeuroNet.cl"')
+        parts.append(rewrite(text))
+        plist = parse_params(params)
+        uses_barrier = int(bool(re.search(r"BarrierLoc|barrier\s*\(|Local(Sum|Max|Min|SoftMax|SoftMaxGrad|Sum4)\s*\(",
+                                          body)))
+        table.append((name, plist, uses_barrier))
+    parts.append("}  // namespace ocl")
+    for name, plist, _ in table:
+        args = []
+        for idx, (kind, pname, decl) in enumerate(plist):
+            if kind == "p":
+                base = "uint" if re.search(r"\buint\b", decl) else ("int" if re.search(r"\bint\b", decl) else "float")
+                args.append(f"(ocl::{base} *)a[{idx}]" if base == "uint" else f"({base} *)a[{idx}]")
+            elif kind == "f":
+                args.append(f"*(const float *)a[{idx}]")
+            elif kind == "u":
+                args.append(f"*(const unsigned int *)a[{idx}]")
+            else:
+                args.append(f"*(const int *)a[{idx}]")
+        parts.append(f"static void call_{name}(void **a) {{ ocl::{name}({', '.join(args)}); }}")
+    parts.append("struct RefKernel { const char *name; void (*call)(void **); int uses_barrier; int nargs; const char *argtypes; };")
+    rows = []
+    for name, plist, ub in table:
+        types = "".join(k for k, _, _ in plist)
+        rows.append(f'  {{"{name}", call_{name}, {ub}, {len(plist)}, "{types}"}},')
+    parts.append('extern "C" const RefKernel nnref_table[] = {\n' + "\n".join(rows) + "\n};")
+    parts.append(f'extern "C" const int nnref_table_size = {len(table)};')
+    return "\n".join(parts) + "\n"
+
+
+def build(reference: str, force: bool = False) -> str | None:
+    cl_path = os.path.join(reference, CL_RELPATH)
+    lib = os.path.join(OUT_DIR, "libnnref.so")
+    if not os.path.exists(cl_path):
+        return lib if os.path.exists(lib) else None
+    deps = [cl_path, __file__, os.path.join(HERE, "ref_shim.h"), os.path.join(HERE, "ref_exec.cpp")]
+    if (not force and os.path.exists(lib)
+            and os.path.getmtime(lib) >= max(os.path.getmtime(d) for d in deps)):
+        return lib
+    os.makedirs(OUT_DIR, exist_ok=True)
+    with open(cl_path, "r", encoding="utf-8", errors="replace") as f:
+        cl_text = f.read()
+    gen = os.path.join(OUT_DIR, "nn_ref_gen.cpp")
+    with open(gen, "w") as f:
+        f.write(generate(cl_text))
+    cmd = ["g++", "-O2", "-std=c++17", "-fopenmp", "-fPIC", "-shared", "-w",
+           "-fno-fast-math", "-ffp-contract=off", "-I", HERE,
+           gen, os.path.join(HERE, "ref_exec.cpp"), "-o", lib + ".tmp"]
+    subprocess.run(cmd, check=True)
+    os.replace(lib + ".tmp", lib)
+    return lib
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=os.environ.get("NN_REFERENCE_DIR", DEFAULT_REFERENCE))
+    ap.add_argument("--force", action="store_true")
+    a = ap.parse_args()
+    lib = build(a.reference, a.force)
+    print(lib or "reference checkout not found; nothing built")
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
