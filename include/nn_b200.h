@@ -1,0 +1,169 @@
+/*
+ * nn_b200.h -- C ABI of the B200 NeuroNet kernel library (libnn_b200.so).
+ *
+ * The library is a drop-in for the OpenCL device layer that the MQL5 layer
+ * classes of EAPrognoz/NN_in_Trading drive through COpenCLMy / COpenCL
+ * (Experts/NeuroNet_DNG/NeuroNet_Declarations.mqh:359-513,
+ *  NeuroNet_Core.mqh:241-346 and 14623-15000, macros in
+ *  NeuroNet_Definitions.mqh:56-96).  The same contract is kept:
+ *
+ *   - buffers are int handles owned by the context;
+ *   - kernels are created by id and by their NeuroNet.cl name, and their
+ *     positional arguments PERSIST across executions (callers rebind only
+ *     what changes);
+ *   - argument order is the NeuroNet.cl signature order (the def_k_* indices
+ *     of NeuroNet_Definitions.mqh:560-2540), enum values are ENUM_ACTIVATION /
+ *     ENUM_OPTIMIZATION (NeuroNet_Definitions.mqh:3650-3685);
+ *   - nn_execute takes (dims, offset, global, local) and global/local carry
+ *     the problem shape exactly as the reference kernels read it through
+ *     get_global_size / get_local_size;
+ *   - the queue is in order, nn_execute is asynchronous, nn_buffer_read
+ *     blocks.
+ *
+ * Every entry point returns an int status (NN_OK == 0, negative on error);
+ * nn_last_error gives the text of the last failure.  Types are restricted to
+ * int / float / double / pointers so that MQL5 `#import` can bind them.
+ *
+ * Extensions beyond the reference (used by the batched and data-parallel
+ * training configurations): per-kernel batch count, command lists, and NCCL
+ * data parallelism.
+ */
+#ifndef NN_B200_H
+#define NN_B200_H
+
+#if defined(_WIN32)
+#define NN_API __declspec(dllexport)
+#else
+#define NN_API __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NN_OK 0
+#define NN_ERR_STATE -1       /* no context / wrong call order */
+#define NN_ERR_ARG -2         /* bad argument value */
+#define NN_ERR_HANDLE -3      /* unknown buffer / kernel / list handle */
+#define NN_ERR_KERNEL -4      /* kernel name not in the library */
+#define NN_ERR_BOUNDS -5      /* a buffer is too small for the launch shape */
+#define NN_ERR_CUDA -6        /* CUDA runtime error */
+#define NN_ERR_NCCL -7        /* NCCL error */
+#define NN_ERR_TIMEOUT -8     /* a bounded wait expired */
+#define NN_ERR_UNSUPPORTED -9 /* valid reference call this library does not implement */
+
+/* activation enum, NeuroNet_Definitions.mqh:3650-3669 / NeuroNet.cl:32-39 */
+#define NN_ACT_NONE -1
+#define NN_ACT_TANH 0
+#define NN_ACT_SIGMOID 1
+#define NN_ACT_LRELU 2
+#define NN_ACT_SOFTPLUS 3
+#define NN_ACT_GELU 4
+#define NN_ACT_MINUS_SOFTPLUS 5
+#define NN_ACT_ELU 6
+/* optimization enum, NeuroNet_Definitions.mqh:3671-3685 */
+#define NN_OPT_SGD 0
+#define NN_OPT_ADAM 1
+#define NN_OPT_LS 2
+#define NN_OPT_ADAM_MINI 3
+
+/* ---------------------------------------------------------------- context */
+/* COpenCLMy::Initialize + ContextCreate (NeuroNet_Core.mqh:241-326).
+ * device: CUDA ordinal; flags: reserved (0). */
+NN_API int nn_init(int device, int flags);
+/* COpenCL::Shutdown: frees every buffer, kernel and list of the context. */
+NN_API int nn_shutdown(void);
+/* Text of the last error (CL_ERROR_DESCRIPTION / GetLastError role). */
+NN_API int nn_last_error(char *buf, int len);
+/* COpenCLMy::GetMaxLocalSize (NeuroNet_Declarations.mqh:469). */
+NN_API int nn_max_local_size(int dim);
+/* Wait until every enqueued launch finished (CLExecutionStatus polling);
+ * bounded by timeout_ms (<= 0: wait without bound). */
+NN_API int nn_finish(int timeout_ms);
+/* The context's CUDA stream (cudaStream_t) so that other CUDA code can order
+ * work against it. */
+NN_API void *nn_stream(void);
+
+/* ---------------------------------------------------------------- buffers */
+/* COpenCLMy::AddBuffer / CBufferFloat::BufferCreate
+ * (NeuroNet_Core.mqh:14623-14720, 14881-14920): returns a handle >= 0. */
+NN_API int nn_buffer_create(long long bytes);
+/* COpenCL::BufferFree. */
+NN_API int nn_buffer_free(int handle);
+/* CBufferFloat::BufferWrite / COpenCL::BufferWrite: count floats from src to
+ * element offset `offset`.  Enqueued in order; src is read before return. */
+NN_API int nn_buffer_write(int handle, const float *src, long long offset, long long count);
+/* CBufferFloat::BufferRead / COpenCL::BufferRead: blocking read. */
+NN_API int nn_buffer_read(int handle, float *dst, long long offset, long long count);
+/* Fill count floats from offset with `value` (CBufferFloat::BufferInit). */
+NN_API int nn_buffer_fill(int handle, float value, long long offset, long long count);
+/* Device-to-device copy inside the context (CopyBufferRaw role). */
+NN_API int nn_buffer_copy(int dst, long long dst_offset, int src, long long src_offset, long long count);
+/* Size in bytes, or a negative status. */
+NN_API long long nn_buffer_bytes(int handle);
+/* Device address of a buffer (for interop with other CUDA code). */
+NN_API void *nn_buffer_device_ptr(int handle);
+
+/* ---------------------------------------------------------------- kernels */
+/* COpenCL::KernelCreate(id, name) via the CreateKernel macro
+ * (NeuroNet_Definitions.mqh:56-58, NeuroNet_Core.mqh:23192-23651).
+ * name: a NeuroNet.cl kernel name.  id: any value in [0, 65535]. */
+NN_API int nn_kernel_create(int id, const char *name);
+/* Same, for callers whose strings are UTF-16 (MQL5 `string`). */
+NN_API int nn_kernel_create_w(int id, const unsigned short *name_utf16);
+NN_API int nn_kernel_free(int id);
+/* COpenCL::SetArgumentBuffer / SetArgument (NeuroNet_Definitions.mqh:61-66). */
+NN_API int nn_set_arg_buffer(int id, int arg_index, int buffer_handle);
+NN_API int nn_set_arg_int(int id, int arg_index, int value);
+NN_API int nn_set_arg_float(int id, int arg_index, float value);
+/* Extension: number of independent samples processed by one execution
+ * (default 1).  Per-sample buffers (inputs, outputs, gradients, activations)
+ * hold `batch` consecutive copies of the per-sample layout the reference
+ * kernel reads; parameter buffers (weights, moments, options) are shared.
+ * Forward and input-gradient kernels produce the reference result for every
+ * sample; weight-update kernels average the per-sample weight gradient over
+ * the batch and then apply the reference update arithmetic once. */
+NN_API int nn_set_batch(int id, int batch);
+/* COpenCL::Execute (NeuroNet_Definitions.mqh:69-90): enqueue one execution.
+ * offset may be NULL (must be zero); local may be NULL. */
+NN_API int nn_execute(int id, int dims, const unsigned int *offset, const unsigned int *global,
+               const unsigned int *local);
+/* Number of CUDA kernels this library launched since nn_init. */
+NN_API long long nn_launch_count(void);
+
+/* ----------------------------------------------------------- command lists */
+/* Extension: record the nn_execute calls between begin and end (they are not
+ * run while recording) into a list that nn_cmdlist_run replays with one call.
+ * A replay resolves buffer handles again and re-checks every bound. */
+NN_API int nn_cmdlist_begin(void);
+NN_API int nn_cmdlist_end(void); /* returns the list id (>= 0) */
+NN_API int nn_cmdlist_run(int list);
+/* Overwrite scalar argument arg_index of recorded execution `position`
+ * (e.g. the bias-corrected Adam learning rate of each step). */
+NN_API int nn_cmdlist_set_float(int list, int position, int arg_index, float value);
+NN_API int nn_cmdlist_set_int(int list, int position, int arg_index, int value);
+NN_API int nn_cmdlist_size(int list);
+NN_API int nn_cmdlist_free(int list);
+
+/* ------------------------------------------------------------ data parallel */
+/* Extension: NCCL data parallelism over the GPUs of one node.
+ * nn_dp_unique_id writes the 128-byte ncclUniqueId (rank 0 creates it, the
+ * caller distributes it); nn_dp_init joins the communicator. */
+NN_API int nn_dp_unique_id(unsigned char *id128);
+NN_API int nn_dp_init(int rank, int world, const unsigned char *id128);
+NN_API int nn_dp_shutdown(void);
+/* Sum-allreduce `count` floats of a buffer in place on the context stream,
+ * then scale by `scale` (1/world for a mean). */
+NN_API int nn_dp_allreduce(int handle, long long offset, long long count, float scale);
+/* Deferred-update region: between begin and end, weight-update kernels write
+ * their batch-mean weight gradient into a gradient arena instead of applying
+ * it, and their update (and any NormalizeWeights execution) is queued.  At
+ * nn_dp_update_end the arena is averaged over the ranks with one NCCL
+ * allreduce and the queued updates run in their original order. */
+NN_API int nn_dp_update_begin(void);
+NN_API int nn_dp_update_end(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NN_B200_H */

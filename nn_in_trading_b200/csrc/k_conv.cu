@@ -1,0 +1,337 @@
+// Convolution kernels (CNeuronConvOCL path and the 1x1 "convolutions" of the
+// attention layers): FeedForwardConv, CalcHiddenGradientConv,
+// UpdateWeightsConvAdam, UpdateWeightsConvMomentum.
+//
+// Layout is the reference's: input [variables][inputs], output
+// [variables][units][window_out], weights [variables][window_out][window_in+1]
+// with the bias last.  With a batch, every per-sample buffer holds `batch`
+// consecutive copies of that layout and the weights are shared.
+#include "../../include/nn_b200.h"
+#include "gemm_simt.cuh"
+#include "nn_device.cuh"
+#include "nn_internal.h"
+#include "wgrad.cuh"
+
+namespace nn {
+
+// -------------------------------------------------------- FeedForwardConv
+// NeuroNet.cl:887-932 as a GEMM per variable: rows (sample, unit), columns
+// output channel, k the window offset (im2col view of the strided input).
+struct ConvLoadX {
+  const float *x;
+  int units, step, inputs, var;
+  __device__ __forceinline__ float operator()(int m, int k, int v) const {
+    int b = m / units, u = m - b * units;
+    int pos = u * step + k;
+    return pos < inputs ? nan0(x[((size_t)b * var + v) * inputs + pos]) : 0.f;
+  }
+};
+struct ConvLoadW {  // B(k, n) = W[v][n][k]
+  const float *w;
+  int win, wout;
+  __device__ __forceinline__ float operator()(int k, int n, int v) const {
+    return nan0(w[((size_t)v * wout + n) * (win + 1) + k]);
+  }
+};
+struct ConvEpi {
+  const float *w;
+  float *o;
+  int units, win, wout, var, act;
+  __device__ __forceinline__ void operator()(int m, int n, int v, int, float acc) const {
+    int b = m / units, u = m - b * units;
+    float bias = nan0(w[((size_t)v * wout + n) * (win + 1) + win]);
+    o[(((size_t)b * var + v) * units + u) * wout + n] = activate(acc + bias, act);
+  }
+};
+
+static int k_feedforward_conv(Launch &L) {
+  const int units = (int)L.nd.g[0];
+  const int wout_g = L.nd.dims > 1 ? (int)L.nd.g[1] : 1;
+  const int var = L.nd.dims > 2 ? (int)L.nd.g[2] : 1;
+  const int inputs = L.i(3), step = L.i(4), win = L.i(5), wout = L.i(6), act = L.i(7);
+  if (inputs < 0 || step < 0 || win < 0 || wout < wout_g) return L.fail(NN_ERR_ARG, "FeedForwardConv: bad shape");
+  float *w = L.buf(0, (size_t)var * wout * (win + 1));
+  float *x = L.buf(1, (size_t)L.B * var * inputs);
+  float *o = L.buf(2, (size_t)L.B * var * units * wout);
+  if (!w || !x || !o) return NN_ERR_BOUNDS;
+  GemmShape sh{L.B * units, wout_g, win, var, 1};
+  cudaError_t e = gemm_simt<true, false>(sh, ConvLoadX{x, units, step, inputs, var}, ConvLoadW{w, win, wout},
+                                         ConvEpi{w, o, units, win, wout, var, act}, L.stream);
+  if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
+  L.counted();
+  return NN_OK;
+}
+
+// ------------------------------------------------- CalcHiddenGradientConv
+// NeuroNet.cl:941-986.  General form: one thread per (sample, variable, input)
+// position summing over the windows that cover it.
+__global__ void conv_dgrad_direct_kernel(const float *__restrict__ w, const float *__restrict__ g,
+                                         const float *__restrict__ o, float *__restrict__ ig, int inputs, int var,
+                                         int outputs, int step, int win, int wout, int act, int shift_out, int B) {
+  size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  size_t total = (size_t)B * var * inputs;
+  if (t >= total) return;
+  int i = (int)(t % inputs);
+  size_t bv = t / inputs;
+  int v = (int)(bv % var);
+  size_t b = bv / var;
+  const float *gs = g + shift_out + b * (size_t)var * outputs + (size_t)v * outputs;
+  const float *ws = w + (size_t)v * wout * (win + 1);
+  int start = i < win ? 0 : (i - win) / step + 1;
+  int stop = min(i / step + 1, outputs / wout);
+  float sum = 0.f;
+  for (int h = 0; h < wout; ++h)
+    for (int k = start; k < stop; ++k) {
+      float gr = nan0(gs[k * wout + h]);
+      if (fabsf(gr) > 0.f) sum += nan0(gr * ws[h * (win + 1) + i - k * step]);
+    }
+  ig[t] = deactivate(sum, o[t], act);
+}
+
+// Non-overlapping windows (step == window_in, input fully tiled): one GEMM per
+// variable, rows (sample, window), columns window offset, k output channel.
+struct CDLoadG {
+  const float *g;
+  int n_win, wout, outputs, var;
+  __device__ __forceinline__ float operator()(int m, int h, int v) const {
+    int b = m / n_win, k = m - b * n_win;
+    return nan0(g[((size_t)b * var + v) * outputs + (size_t)k * wout + h]);
+  }
+};
+struct CDLoadW {  // B(h, r) = W[v][h][r]
+  const float *w;
+  int win, wout;
+  __device__ __forceinline__ float operator()(int h, int r, int v) const {
+    return nan0(w[((size_t)v * wout + h) * (win + 1) + r]);
+  }
+};
+struct CDEpi {
+  const float *o;
+  float *ig;
+  int n_win, win, inputs, var, act;
+  __device__ __forceinline__ void operator()(int m, int r, int v, int, float acc) const {
+    int b = m / n_win, k = m - b * n_win;
+    size_t idx = ((size_t)b * var + v) * inputs + (size_t)k * win + r;
+    ig[idx] = deactivate(acc, o[idx], act);
+  }
+};
+
+static int k_calc_hidden_gradient_conv(Launch &L) {
+  const int inputs = (int)L.nd.g[0];
+  const int var = L.nd.dims > 1 ? (int)L.nd.g[1] : 1;
+  const int outputs = L.i(4), step = L.i(5), win = L.i(6), wout = L.i(7), act = L.i(8), shift_out = L.i(9);
+  if (outputs < 0 || step <= 0 || win < 0 || wout <= 0 || shift_out < 0)
+    return L.fail(NN_ERR_ARG, "CalcHiddenGradientConv: bad shape");
+  if (L.B > 1 && shift_out != 0) return L.fail(NN_ERR_UNSUPPORTED, "CalcHiddenGradientConv: shift_out with batch");
+  float *w = L.buf(0, (size_t)var * wout * (win + 1));
+  float *g = L.buf(1, (size_t)shift_out + (size_t)L.B * var * outputs);
+  float *o = L.buf(2, (size_t)L.B * var * inputs);
+  float *ig = L.buf(3, (size_t)L.B * var * inputs);
+  if (!w || !g || !o || !ig) return NN_ERR_BOUNDS;
+  const int n_win = outputs / wout;
+  if (step == win && shift_out == 0 && outputs == n_win * wout && inputs == n_win * win && win > 0) {
+    GemmShape sh{L.B * n_win, win, wout, var, 1};
+    cudaError_t e = gemm_simt<true, true>(sh, CDLoadG{g, n_win, wout, outputs, var}, CDLoadW{w, win, wout},
+                                          CDEpi{o, ig, n_win, win, inputs, var, act}, L.stream);
+    if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
+    L.counted();
+    return NN_OK;
+  }
+  size_t total = (size_t)L.B * var * inputs;
+  conv_dgrad_direct_kernel<<<grid1d(total, 256), 256, 0, L.stream>>>(w, g, o, ig, inputs, var, outputs, step, win,
+                                                                      wout, act, shift_out, L.B);
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
+// ---------------------------------------------------- UpdateWeightsConvAdam
+// NeuroNet.cl:1053-1098.  Weight (v, o, k): grad = sum_t g[v*total*wout + t*wout + o] *
+// x[v*inputs + t*step + k] (x = 1 for the bias column k == window_in), with
+// total = (inputs-(window_in-step)+(step-1))/step and the loop stopping, for
+// k < window_in, at the first t with k + t*window_in >= inputs.  Batched: the
+// mean over samples, then clamp and the reference Adam step (no eps, no l1/l2).
+struct CWLoadG {  // A(m=o, kk=(b,t))
+  const float *g;
+  int total, wout;
+  size_t gstride;  // floats per sample
+  __device__ __forceinline__ float operator()(int o, int kk, int v) const {
+    int b = kk / total, t = kk - b * total;
+    return nan0(g[(size_t)b * gstride + ((size_t)v * total + t) * wout + o]);
+  }
+};
+struct CWLoadX {  // B(kk=(b,t), n=k)
+  const float *x;
+  int total, inputs, step, win, var;
+  __device__ __forceinline__ float operator()(int kk, int n, int v) const {
+    if (n == win) return 1.f;
+    int b = kk / total, t = kk - b * total;
+    if (n + t * win >= inputs) return 0.f;  // the reference's loop exit (uses window_in, not step)
+    return nan0(x[((size_t)b * var + v) * inputs + n + (size_t)t * step]);
+  }
+};
+
+__global__ void adam_conv_apply_kernel(float *w, float *m, float *v, GradSrc G, size_t n, float l, float b1,
+                                       float b2) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float grad = clampf(nan0(G(i)), -kMaxGrad, kMaxGrad);
+  float mt = nan0(b1 * m[i] + (1.f - b1) * grad);
+  float vt = nan0(b2 * v[i] + (1.f - b2) * (grad * grad), 1.f);
+  float weight = nan0(w[i] + nan0(l * mt / sqrtf(vt)));
+  w[i] = weight;
+  m[i] = mt;
+  v[i] = vt;
+}
+
+struct ConvUpdShape {
+  int nw, var, inputs, win, wout, step, total;
+  size_t need_x;   // floats of x per sample read by the loops
+  size_t gstride;  // floats of gradient per sample: var * units * wout
+};
+static int conv_upd_shape(Launch &L, int inputs_idx, int win_idx, int wout_idx, int step_idx, bool adam,
+                          ConvUpdShape *s) {
+  s->nw = (int)L.nd.g[0];
+  s->inputs = L.i(inputs_idx);
+  s->win = L.i(win_idx);
+  s->wout = L.i(wout_idx);
+  s->step = L.i(step_idx);
+  if (s->win < 0 || s->wout <= 0 || s->step <= 0 || s->inputs < 0) return L.fail(NN_ERR_ARG, "conv update: bad shape");
+  int per_var = s->wout * (s->win + 1);
+  if (s->nw % per_var != 0) return L.fail(NN_ERR_ARG, "conv update: weight count not a multiple of wout*(win+1)");
+  s->var = s->nw / per_var;
+  s->total = adam ? (s->inputs - (s->win - s->step) + (s->step - 1)) / s->step
+                  : (s->inputs - s->win + s->step - 1) / s->step;
+  if (s->total < 0) s->total = 0;
+  // largest x position the gradient loops read, per variable
+  long long maxpos = -1;
+  for (int k = 0; k < s->win; ++k) {
+    long long tend = s->inputs > k ? ((long long)s->inputs - k + s->win - 1) / s->win : 0;
+    if (tend > s->total) tend = s->total;
+    if (tend > 0) maxpos = std::max(maxpos, (long long)k + (tend - 1) * s->step);
+  }
+  s->need_x = (size_t)std::max(maxpos + 1, (long long)s->inputs);
+  // A batch holds one layer gradient [var][units][wout] per sample, with units the
+  // number of complete windows (inputs - window_in) / step + 1.
+  int units = s->inputs >= s->win ? (s->inputs - s->win) / s->step + 1 : 1;
+  s->gstride = (size_t)s->var * units * s->wout;
+  return NN_OK;
+}
+
+static int adam_conv_apply_src(const Launch &Lc, GradSrc G) {
+  Launch &L = const_cast<Launch &>(Lc);
+  size_t n = L.nd.g[0];
+  float *w = L.buf(0, n), *m = L.buf(3, n), *v = L.buf(4, n);
+  if (!w || !m || !v) return NN_ERR_BOUNDS;
+  adam_conv_apply_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(w, m, v, G, n, L.f(6), L.f(7), L.f(8));
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+static int adam_conv_apply(const Launch &L, const float *grad) {
+  return adam_conv_apply_src(L, GradSrc{grad, 1, 0, 1.f});
+}
+
+static int k_update_weights_conv_adam(Launch &L) {
+  ConvUpdShape s;
+  int rc = conv_upd_shape(L, 5, 9, 10, 11, true, &s);
+  if (rc) return rc;
+  float *w = L.buf(0, s.nw), *m = L.buf(3, s.nw), *v = L.buf(4, s.nw);
+  float *g = L.buf(1, (size_t)(L.B - 1) * s.gstride + (size_t)s.var * s.total * s.wout);
+  float *x = L.buf(2, (size_t)(L.B * s.var - 1) * s.inputs + s.need_x);
+  if (!w || !m || !v || !g || !x) return NN_ERR_BOUNDS;
+  GradSrc src;
+  if (s.total == 0 || L.B * s.total == 0) {
+    float *z = L.scratch(0, s.nw);
+    if (!z) return NN_ERR_CUDA;
+    cudaMemsetAsync(z, 0, (size_t)s.nw * sizeof(float), L.stream);
+    src = GradSrc{z, 1, 0, 1.f};
+  } else {
+    rc = wgrad_partials<false, true>(L, s.wout, s.win + 1, L.B * s.total, s.var,
+                                     CWLoadG{g, s.total, s.wout, s.gstride},
+                                     CWLoadX{x, s.total, s.inputs, s.step, s.win, s.var}, &src);
+    if (rc) return rc;
+    src.scale = 1.f / (float)L.B;
+  }
+  return finish_update(L, src, (size_t)s.nw, adam_conv_apply, adam_conv_apply_src);
+}
+
+// ------------------------------------------------ UpdateWeightsConvMomentum
+// NeuroNet.cl:996-1043 (with its shift_out = i/(window_in+1) - v indexing and
+// total = (inputs-window_in+step-1)/step).  One thread per weight; batched:
+// the per-sample sums are averaged.
+__global__ void momentum_conv_grad_kernel(float *gout, const float *g, const float *x, int nw, int inputs, int win,
+                                          int wout, int step, int total, int var, int B, size_t gstride) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nw) return;
+  int v = i / ((win + 1) * wout);
+  int shift = i % (win + 1);
+  int shift_out = i / (win + 1) - v;
+  float acc = 0.f;
+  for (int b = 0; b < B; ++b) {
+    const float *gs = g + (size_t)b * gstride + (size_t)v * total * wout;
+    const float *xs = x + (size_t)b * var * inputs + (size_t)v * inputs;
+    float grad = 0.f;
+    for (int t = 0; t < total; ++t) {
+      if (shift != win && (shift + t * win) >= inputs) break;
+      grad += nan0(gs[t * wout + shift_out] * (shift == win ? 1.f : xs[shift + t * step]));
+    }
+    acc += grad;
+  }
+  gout[i] = acc / (float)B;
+}
+
+__global__ void momentum_conv_apply_kernel(float *w, float *dw, const float *grad, int n, float lr, float mom) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float delta = nan0(lr * grad[i]) + mom * dw[i];
+  if (!isnan(delta)) {
+    dw[i] = delta;
+    if (fabsf(delta) > 0.f) w[i] = nan0(w[i] + delta);
+  }
+}
+
+static int momentum_conv_apply(const Launch &Lc, const float *grad) {
+  Launch &L = const_cast<Launch &>(Lc);
+  int n = (int)L.nd.g[0];
+  float *w = L.buf(0, n), *dw = L.buf(3, n);
+  if (!w || !dw) return NN_ERR_BOUNDS;
+  momentum_conv_apply_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(w, dw, grad, n, L.f(5), L.f(6));
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
+static int k_update_weights_conv_momentum(Launch &L) {
+  ConvUpdShape s;
+  int rc = conv_upd_shape(L, 4, 7, 8, 9, false, &s);
+  if (rc) return rc;
+  // largest gradient index of the reference formula (ignoring early loop exits)
+  size_t need_g = 0;
+  if (s.total > 0) {
+    long long v = s.var - 1;
+    long long mx = (long long)(s.total - 1) * s.wout + (v + 1) * s.wout - 1 - v + v * (long long)s.total * s.wout;
+    need_g = (size_t)(mx + 1);
+  }
+  float *w = L.buf(0, s.nw), *dw = L.buf(3, s.nw);
+  float *g = L.buf(1, (size_t)(L.B - 1) * s.gstride + need_g);
+  float *x = L.buf(2, (size_t)(L.B * s.var - 1) * s.inputs + s.need_x);
+  if (!w || !dw || !g || !x) return NN_ERR_BOUNDS;
+  float *grad = L.deferred() ? L.grad_slot(s.nw) : L.scratch(1, s.nw);
+  if (!grad) return NN_ERR_BOUNDS;
+  momentum_conv_grad_kernel<<<grid1d(s.nw, 256), 256, 0, L.stream>>>(grad, g, x, s.nw, s.inputs, s.win, s.wout,
+                                                                      s.step, s.total, s.var, L.B, s.gstride);
+  NN_CHECK_LAUNCH(L);
+  if (L.deferred()) {
+    L.defer(momentum_conv_apply, grad);
+    return NN_OK;
+  }
+  return momentum_conv_apply(L, grad);
+}
+
+const KernelDef kConvKernels[] = {
+    {"FeedForwardConv", "pppiiiii", k_feedforward_conv, false},
+    {"CalcHiddenGradientConv", "ppppiiiiii", k_calc_hidden_gradient_conv, false},
+    {"UpdateWeightsConvAdam", "pppppifffiii", k_update_weights_conv_adam, false},
+    {"UpdateWeightsConvMomentum", "ppppiffiii", k_update_weights_conv_momentum, false},
+};
+const int kNumConvKernels = sizeof(kConvKernels) / sizeof(kConvKernels[0]);
+
+}  // namespace nn

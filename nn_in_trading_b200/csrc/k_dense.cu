@@ -1,0 +1,481 @@
+// Dense-layer kernels of the library (CNeuronBaseOCL path) and the
+// elementwise kernels: FeedForward, CalcOutputGradient, CalcHiddenGradient,
+// UpdateWeightsMomentum, UpdateWeightsAdam, NormalizeWeights, Activation,
+// DeActivation, SoftUpdate, SoftUpdateAdam.
+//
+// Weight layout is the reference's: W[out][in+1] row-major with the bias in
+// the last column, stored on the *source* layer (NeuroNet_Core.mqh:15568).
+#include "../../include/nn_b200.h"
+#include "gemm_simt.cuh"
+#include "nn_device.cuh"
+#include "nn_internal.h"
+#include "wgrad.cuh"
+
+namespace nn {
+
+__global__ void reduce_partials_kernel(float *out, GradSrc src, size_t n) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i < n) out[i] = src(i);
+}
+
+// ------------------------------------------------------------ FeedForward
+// NeuroNet.cl:430-512.  y[b,o] = act(sum_k nan0(nan0(x[b,k]) w[o,k]) + nan0(w[o,in]))
+// Small batches: one warp per output row, lanes striding the row (coalesced).
+template <int MAXB>
+__global__ void ff_rows_kernel(const float *__restrict__ w, const float *__restrict__ x, float *__restrict__ y,
+                               int inputs, int outputs, int B, int act) {
+  int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int lane = threadIdx.x & 31;
+  if (warp >= outputs) return;
+  const float *row = w + (size_t)warp * (inputs + 1);
+  float s[MAXB];
+#pragma unroll
+  for (int b = 0; b < MAXB; ++b) s[b] = 0.f;
+  for (int k = lane; k < inputs; k += 32) {
+    float wk = row[k];
+#pragma unroll
+    for (int b = 0; b < MAXB; ++b)
+      if (b < B) s[b] += nan0(nan0(x[(size_t)b * inputs + k]) * wk);
+  }
+  float bias = nan0(row[inputs]);
+#pragma unroll
+  for (int b = 0; b < MAXB; ++b) {
+    if (b >= B) break;
+    float t = warp_sum(s[b]);
+    if (lane == 0) y[(size_t)b * outputs + warp] = activate(t + bias, act);
+  }
+}
+
+struct FFLoadX {
+  const float *x;
+  int inputs;
+  __device__ __forceinline__ float operator()(int m, int k, int) const { return nan0(x[(size_t)m * inputs + k]); }
+};
+struct FFLoadW {  // B(k, n) = W[n][k]
+  const float *w;
+  int ld;
+  __device__ __forceinline__ float operator()(int k, int n, int) const { return nan0(w[(size_t)n * ld + k]); }
+};
+struct FFEpi {
+  const float *w;
+  float *y;
+  int ld, inputs, outputs, act;
+  __device__ __forceinline__ void operator()(int m, int n, int, int, float acc) const {
+    y[(size_t)m * outputs + n] = activate(acc + nan0(w[(size_t)n * ld + inputs]), act);
+  }
+};
+
+__global__ void ff_flags_kernel(const float *w, const float *x, const float *y, float *flags, int inputs,
+                                int outputs, int B) {
+  size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (t >= (size_t)B * outputs) return;
+  int b = (int)(t / outputs), o = (int)(t % outputs);
+  const float *row = w + (size_t)o * (inputs + 1);
+  bool bad = false;
+  float s = 0.f;
+  for (int k = 0; k < inputs; ++k) {
+    float xi = x[(size_t)b * inputs + k], wk = row[k];
+    bad |= !isfinite(xi) || !isfinite(wk) || !isfinite(xi * wk);
+    s += nan0(nan0(xi) * wk);
+  }
+  bad |= !isfinite(row[inputs]) || !isfinite(s) || !isfinite(y[t]);
+  flags[t] = bad ? 1.f : 0.f;
+}
+
+static int k_feedforward(Launch &L) {
+  const int outputs = (int)L.nd.g[0];
+  const int inputs = L.i(3), act = L.i(4), fe = L.i(6);
+  if (inputs < 0) return L.fail(NN_ERR_ARG, "FeedForward: negative inputs");
+  const int ld = inputs + 1;
+  float *w = L.buf(0, (size_t)outputs * ld);
+  float *x = L.buf(1, (size_t)L.B * inputs);
+  float *y = L.buf(2, (size_t)L.B * outputs);
+  if (!w || !x || !y) return NN_ERR_BOUNDS;
+  float *flags = nullptr;
+  if (fe) {
+    flags = L.buf(5, (size_t)L.B * outputs);
+    if (!flags) return NN_ERR_BOUNDS;
+  }
+  if (L.B <= 4) {
+    unsigned blocks = ceil_div((size_t)outputs * 32, 256);
+    ff_rows_kernel<4><<<blocks, 256, 0, L.stream>>>(w, x, y, inputs, outputs, L.B, act);
+    NN_CHECK_LAUNCH(L);
+  } else {
+    GemmShape sh{L.B, outputs, inputs, 1, 1};
+    cudaError_t e = gemm_simt<true, false>(sh, FFLoadX{x, inputs}, FFLoadW{w, ld},
+                                           FFEpi{w, y, ld, inputs, outputs, act}, L.stream);
+    if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
+    L.counted();
+  }
+  if (fe) {
+    ff_flags_kernel<<<grid1d((size_t)L.B * outputs, 256), 256, 0, L.stream>>>(w, x, y, flags, inputs, outputs, L.B);
+    NN_CHECK_LAUNCH(L);
+  }
+  return NN_OK;
+}
+
+// ----------------------------------------------------- CalcOutputGradient
+// NeuroNet.cl:523-536.  ig = Deactivation(t - o, o, act); the `error` argument is unused.
+__global__ void out_grad_kernel(const float *t, const float *o, float *ig, size_t n, int act) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float out = o[i];
+  ig[i] = isfinite(out) ? deactivate(t[i] - out, out, act) : 0.f;
+}
+
+static int k_calc_output_gradient(Launch &L) {
+  size_t n = (size_t)L.nd.g[0] * L.B;
+  float *t = L.buf(0, n), *o = L.buf(1, n), *ig = L.buf(2, n);
+  if (!t || !o || !ig) return NN_ERR_BOUNDS;
+  out_grad_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(t, o, ig, n, L.i(3));
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
+// ----------------------------------------------------- CalcHiddenGradient
+// NeuroNet.cl:547-613.  ig[b,i] = Deactivation(sum_k nan0(w[k,i]) nan0(g[b,k]), o[b,i], act)
+// Small batches: CTA of 8 warps per 32 columns; warps split the k range.
+template <int MAXB>
+__global__ void chg_cols_kernel(const float *__restrict__ w, const float *__restrict__ g, const float *__restrict__ o,
+                                float *__restrict__ ig, int inputs, int outputs, int B, int act) {
+  __shared__ float part[8][MAXB][33];
+  int col = blockIdx.x * 32 + (threadIdx.x & 31);
+  int wv = threadIdx.x >> 5;
+  float s[MAXB];
+#pragma unroll
+  for (int b = 0; b < MAXB; ++b) s[b] = 0.f;
+  if (col < inputs) {
+    for (int k = wv; k < outputs; k += 8) {
+      float wk = nan0(w[(size_t)k * (inputs + 1) + col]);
+#pragma unroll
+      for (int b = 0; b < MAXB; ++b)
+        if (b < B) s[b] += wk * nan0(g[(size_t)b * outputs + k]);
+    }
+  }
+#pragma unroll
+  for (int b = 0; b < MAXB; ++b) part[wv][b][threadIdx.x & 31] = s[b];
+  __syncthreads();
+  if (wv < MAXB && wv < B && col < inputs) {
+    float t = 0.f;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) t += part[r][wv][threadIdx.x & 31];
+    size_t idx = (size_t)wv * inputs + col;
+    ig[idx] = deactivate(t, o[idx], act);
+  }
+}
+
+struct CHGLoadG {
+  const float *g;
+  int outputs;
+  __device__ __forceinline__ float operator()(int m, int k, int) const { return nan0(g[(size_t)m * outputs + k]); }
+};
+struct CHGLoadW {  // B(k, n) = W[k][n]
+  const float *w;
+  int ld;
+  __device__ __forceinline__ float operator()(int k, int n, int) const { return nan0(w[(size_t)k * ld + n]); }
+};
+struct CHGEpi {
+  const float *o;
+  float *ig;
+  int inputs, act;
+  __device__ __forceinline__ void operator()(int m, int n, int, int, float acc) const {
+    size_t idx = (size_t)m * inputs + n;
+    ig[idx] = deactivate(acc, o[idx], act);
+  }
+};
+
+static int k_calc_hidden_gradient(Launch &L) {
+  const int inputs = (int)L.nd.g[0];
+  const int outputs = L.i(4), act = L.i(5);
+  if (outputs < 0) return L.fail(NN_ERR_ARG, "CalcHiddenGradient: negative outputs");
+  const int ld = inputs + 1;
+  float *w = L.buf(0, (size_t)outputs * ld);
+  float *g = L.buf(1, (size_t)L.B * outputs);
+  float *o = L.buf(2, (size_t)L.B * inputs);
+  float *ig = L.buf(3, (size_t)L.B * inputs);
+  if (!w || !g || !o || !ig) return NN_ERR_BOUNDS;
+  if (L.B <= 4) {
+    chg_cols_kernel<4><<<ceil_div(inputs, 32), 256, 0, L.stream>>>(w, g, o, ig, inputs, outputs, L.B, act);
+    NN_CHECK_LAUNCH(L);
+    return NN_OK;
+  }
+  GemmShape sh{L.B, inputs, outputs, 1, 1};
+  cudaError_t e = gemm_simt<true, true>(sh, CHGLoadG{g, outputs}, CHGLoadW{w, ld}, CHGEpi{o, ig, inputs, act},
+                                        L.stream);
+  if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
+  L.counted();
+  return NN_OK;
+}
+
+// ---------------------------------------------------------- dense updates
+// Batch weight gradient G[o][j] = (1/B) sum_b gsrc(b,o) * inp(b,j), inp(b, inputs) = 1.
+struct WGLoadG {  // A(m=o, k=b)
+  const float *g;
+  int outputs;
+  int clamp_g;  // momentum path clamps the node gradient per sample
+  __device__ __forceinline__ float operator()(int m, int k, int) const {
+    float v = g[(size_t)k * outputs + m];
+    return clamp_g ? clampf(v, -kMaxGrad, kMaxGrad) : nan0(v);
+  }
+};
+struct WGLoadX {  // B(k=b, n=j)
+  const float *x;
+  int inputs;
+  __device__ __forceinline__ float operator()(int k, int n, int) const {
+    return n < inputs ? nan0(x[(size_t)k * inputs + n]) : 1.f;
+  }
+};
+
+// UpdateWeightsAdam arithmetic (NeuroNet.cl:678-693) with a given pre-clamp gradient.
+__global__ void adam_dense_apply_kernel(float *w, float *m, float *v, GradSrc G, int n_out, int n_col, int inputs,
+                                        float l, float b1, float b2) {
+  size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (t >= (size_t)n_out * n_col) return;
+  int i = (int)(t / n_col), j = (int)(t % n_col);
+  size_t wi = (size_t)i * (inputs + 1) + j;
+  float weight = nan0(w[wi]);
+  float mm = nan0(m[wi]);
+  float vv = nan0(v[wi]);
+  float g = clampf(nan0(G(t)), -kMaxGrad, kMaxGrad);
+  float mt = nan0(b1 * mm + (1.f - b1) * g);
+  float vt = nan0(b2 * vv + (1.f - b2) * (g * g));
+  float delta = nan0(l * (mt / (sqrtf(vt) + 1.0e-37f) - (kL1 * signf(weight) + kL2 * weight)));
+  if (fabsf(delta) > 0.f) w[wi] = nan0(w[wi] + delta);
+  m[wi] = mt;
+  v[wi] = vt;
+}
+
+// Single-sample fused kernel: exactly the reference's per-weight arithmetic.
+__global__ void adam_dense_fused_kernel(float *w, const float *g, const float *x, float *m, float *v, int n_out,
+                                        int n_col, int inputs, float l, float b1, float b2) {
+  size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (t >= (size_t)n_out * n_col) return;
+  int i = (int)(t / n_col), j = (int)(t % n_col);
+  size_t wi = (size_t)i * (inputs + 1) + j;
+  float inp = nan0(j == inputs ? 1.f : x[j]);
+  float weight = nan0(w[wi]);
+  float mm = nan0(m[wi]);
+  float vv = nan0(v[wi]);
+  float gg = clampf(nan0(g[i] * inp), -kMaxGrad, kMaxGrad);
+  float mt = nan0(b1 * mm + (1.f - b1) * gg);
+  float vt = nan0(b2 * vv + (1.f - b2) * (gg * gg));
+  float delta = nan0(l * (mt / (sqrtf(vt) + 1.0e-37f) - (kL1 * signf(weight) + kL2 * weight)));
+  if (fabsf(delta) > 0.f) w[wi] = nan0(w[wi] + delta);
+  m[wi] = mt;
+  v[wi] = vt;
+}
+
+struct AdamDenseShape {
+  int n_out, n_col, inputs;
+};
+static AdamDenseShape adam_dense_shape(const Launch &L) {
+  return AdamDenseShape{(int)L.nd.g[0], L.nd.dims > 1 ? (int)L.nd.g[1] : 1, L.i(5)};
+}
+
+static int adam_dense_apply_src(const Launch &Lc, GradSrc G) {
+  Launch &L = const_cast<Launch &>(Lc);
+  AdamDenseShape s = adam_dense_shape(L);
+  size_t nw = (size_t)(s.n_out - 1) * (s.inputs + 1) + s.n_col;
+  float *w = L.buf(0, nw), *m = L.buf(3, nw), *v = L.buf(4, nw);
+  if (!w || !m || !v) return NN_ERR_BOUNDS;
+  size_t n = (size_t)s.n_out * s.n_col;
+  adam_dense_apply_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(w, m, v, G, s.n_out, s.n_col, s.inputs, L.f(6),
+                                                                L.f(7), L.f(8));
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+static int adam_dense_apply(const Launch &L, const float *grad) {
+  return adam_dense_apply_src(L, GradSrc{grad, 1, 0, 1.f});
+}
+
+static int k_update_weights_adam(Launch &L) {
+  AdamDenseShape s = adam_dense_shape(L);
+  if (s.inputs < 0 || s.n_col > s.inputs + 1) return L.fail(NN_ERR_ARG, "UpdateWeightsAdam: bad shape");
+  size_t nw = (size_t)(s.n_out - 1) * (s.inputs + 1) + s.n_col;
+  float *w = L.buf(0, nw), *g = L.buf(1, (size_t)L.B * s.n_out), *x = L.buf(2, (size_t)L.B * s.inputs);
+  float *m = L.buf(3, nw), *v = L.buf(4, nw);
+  if (!w || !g || !x || !m || !v) return NN_ERR_BOUNDS;
+  if (L.B == 1 && !L.deferred()) {
+    size_t n = (size_t)s.n_out * s.n_col;
+    adam_dense_fused_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(w, g, x, m, v, s.n_out, s.n_col, s.inputs,
+                                                                  L.f(6), L.f(7), L.f(8));
+    NN_CHECK_LAUNCH(L);
+    return NN_OK;
+  }
+  GradSrc src;
+  int rc = wgrad_partials<false, true>(L, s.n_out, s.n_col, L.B, 1, WGLoadG{g, s.n_out, 0}, WGLoadX{x, s.inputs},
+                                       &src);
+  if (rc) return rc;
+  src.scale = 1.f / (float)L.B;
+  return finish_update(L, src, (size_t)s.n_out * s.n_col, adam_dense_apply, adam_dense_apply_src);
+}
+
+// UpdateWeightsMomentum (NeuroNet.cl:624-645); batch: G = mean_b clamp(g_b) x_b.
+__global__ void momentum_dense_kernel(float *w, float *dw, GradSrc G, const float *g, const float *x, int n_out,
+                                      int n_col, int inputs, float lr, float mom, int fused) {
+  size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (t >= (size_t)n_out * n_col) return;
+  int i = (int)(t / n_col), j = (int)(t % n_col);
+  size_t wi = (size_t)i * (inputs + 1) + j;
+  float term;
+  if (fused) {
+    float grad = clampf(g[i], -kMaxGrad, kMaxGrad);
+    term = nan0(lr * grad * (j < inputs ? x[j] : 1.f));
+  } else {
+    term = nan0(lr * G(t));
+  }
+  float delta = term + nan0(mom * dw[wi]);
+  dw[wi] = delta;
+  if (fabsf(delta) > 0.f) w[wi] = nan0(w[wi] + delta);
+}
+
+static int momentum_dense_apply_src(const Launch &Lc, GradSrc G) {
+  Launch &L = const_cast<Launch &>(Lc);
+  int n_out = (int)L.nd.g[0], n_col = L.nd.dims > 1 ? (int)L.nd.g[1] : 1, inputs = L.i(4);
+  size_t nw = (size_t)(n_out - 1) * (inputs + 1) + n_col;
+  float *w = L.buf(0, nw), *dw = L.buf(3, nw);
+  if (!w || !dw) return NN_ERR_BOUNDS;
+  size_t n = (size_t)n_out * n_col;
+  momentum_dense_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(w, dw, G, nullptr, nullptr, n_out, n_col, inputs,
+                                                              L.f(5), L.f(6), 0);
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+static int momentum_dense_apply(const Launch &L, const float *grad) {
+  return momentum_dense_apply_src(L, GradSrc{grad, 1, 0, 1.f});
+}
+
+static int k_update_weights_momentum(Launch &L) {
+  int n_out = (int)L.nd.g[0], n_col = L.nd.dims > 1 ? (int)L.nd.g[1] : 1, inputs = L.i(4);
+  if (inputs < 0 || n_col > inputs + 1) return L.fail(NN_ERR_ARG, "UpdateWeightsMomentum: bad shape");
+  size_t nw = (size_t)(n_out - 1) * (inputs + 1) + n_col;
+  float *w = L.buf(0, nw), *g = L.buf(1, (size_t)L.B * n_out), *x = L.buf(2, (size_t)L.B * inputs);
+  float *dw = L.buf(3, nw);
+  if (!w || !g || !x || !dw) return NN_ERR_BOUNDS;
+  if (L.B == 1 && !L.deferred()) {
+    size_t n = (size_t)n_out * n_col;
+    momentum_dense_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(w, dw, GradSrc{nullptr, 0, 0, 1.f}, g, x, n_out,
+                                                                n_col, inputs, L.f(5), L.f(6), 1);
+    NN_CHECK_LAUNCH(L);
+    return NN_OK;
+  }
+  GradSrc src;
+  int rc = wgrad_partials<false, true>(L, n_out, n_col, L.B, 1, WGLoadG{g, n_out, 1}, WGLoadX{x, inputs}, &src);
+  if (rc) return rc;
+  src.scale = 1.f / (float)L.B;
+  return finish_update(L, src, (size_t)n_out * n_col, momentum_dense_apply, momentum_dense_apply_src);
+}
+
+// ------------------------------------------------------- NormalizeWeights
+// NeuroNet.cl:1498-1525: rows of `dimension` weights rescaled to unit norm when
+// the norm exceeds 1; the 10x pre-scaling retry handles overflow.
+__global__ void normalize_weights_kernel(float *buf, int rows, int dim) {
+  int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  float *row = buf + (size_t)warp * dim;
+  float k = 1.f;
+  float s;
+  for (int guard = 0; guard < 64; ++guard) {
+    s = 0.f;
+    for (int i = lane; i < dim; i += 32) {
+      float q = nan0(row[i]) / k;
+      s += q * q;
+    }
+    s = warp_sum(s);
+    if (isfinite(s)) break;
+    k *= 10.f;
+  }
+  s = sqrtf(s);
+  float d = k * s;
+  if (d > 1.f)
+    for (int i = lane; i < dim; i += 32) row[i] = nan0(row[i]) / d;
+}
+
+static int k_normalize_weights(Launch &L) {
+  int rows = (int)L.nd.g[0], dim = L.i(1);
+  if (dim < 0) return L.fail(NN_ERR_ARG, "NormalizeWeights: negative dimension");
+  float *b = L.buf(0, (size_t)rows * dim);
+  if (!b) return NN_ERR_BOUNDS;
+  normalize_weights_kernel<<<ceil_div((size_t)rows * 32, 256), 256, 0, L.stream>>>(b, rows, dim);
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
+// ------------------------------------------------------------ elementwise
+__global__ void activation_kernel(const float *in, float *out, size_t n, int act) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i < n) out[i] = activate(nan0(in[i]), act);
+}
+static int k_activation(Launch &L) {  // NeuroNet.cl:5796-5808
+  size_t n = (size_t)L.nd.g[0] * L.B;
+  float *in = L.buf(0, n), *out = L.buf(1, n);
+  if (!in || !out) return NN_ERR_BOUNDS;
+  activation_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(in, out, n, L.i(2));
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
+__global__ void deactivation_kernel(const float *in, float *in_gr, const float *out_gr, size_t n, int act) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i < n) in_gr[i] = deactivate(nan0(out_gr[i]), in[i], act);
+}
+static int k_deactivation(Launch &L) {  // NeuroNet.cl:5811-5823
+  size_t n = (size_t)L.nd.g[0] * L.B;
+  float *in = L.buf(0, n), *ig = L.buf(1, n), *og = L.buf(2, n);
+  if (!in || !ig || !og) return NN_ERR_BOUNDS;
+  deactivation_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(in, ig, og, n, L.i(3));
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
+__global__ void soft_update_kernel(float *t, const float *s, size_t n, float tau) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i < n) t[i] = s[i] * tau + (1.f - tau) * t[i];
+}
+static int k_soft_update(Launch &L) {  // NeuroNet.cl:3864-3871
+  size_t n = L.nd.g[0];
+  float *t = L.buf(0, n), *s = L.buf(1, n);
+  if (!t || !s) return NN_ERR_BOUNDS;
+  soft_update_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(t, s, n, L.f(2));
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
+__global__ void soft_update_adam_kernel(float *t, const float *s, float *m, float *v, size_t n, float tau, float b1,
+                                        float b2) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float mm = m[i], vv = v[i], weight = t[i];
+  float g = s[i] - weight;
+  mm = b1 * mm + (1.f - b1) * g;
+  vv = b2 * vv + (1.f - b2) * (g * g);
+  float delta = (1.f - tau) * mm / (vv != 0.f ? sqrtf(vv) : 1.f);
+  if (fabsf(delta) > 0.f) t[i] = weight + delta;
+  m[i] = mm;
+  v[i] = vv;
+}
+static int k_soft_update_adam(Launch &L) {  // NeuroNet.cl:3875-3899
+  size_t n = L.nd.g[0];
+  float *t = L.buf(0, n), *s = L.buf(1, n), *m = L.buf(2, n), *v = L.buf(3, n);
+  if (!t || !s || !m || !v) return NN_ERR_BOUNDS;
+  soft_update_adam_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(t, s, m, v, n, L.f(4), L.f(5), L.f(6));
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
+const KernelDef kDenseKernels[] = {
+    {"FeedForward", "pppiipi", k_feedforward, false},
+    {"CalcOutputGradient", "pppif", k_calc_output_gradient, false},
+    {"CalcHiddenGradient", "ppppii", k_calc_hidden_gradient, false},
+    {"UpdateWeightsMomentum", "ppppiff", k_update_weights_momentum, false},
+    {"UpdateWeightsAdam", "pppppifff", k_update_weights_adam, false},
+    {"NormalizeWeights", "pi", k_normalize_weights, true},
+    {"Activation", "ppi", k_activation, false},
+    {"DeActivation", "pppi", k_deactivation, false},
+    {"SoftUpdate", "ppf", k_soft_update, true},
+    {"SoftUpdateAdam", "ppppfff", k_soft_update_adam, true},
+};
+const int kNumDenseKernels = sizeof(kDenseKernels) / sizeof(kDenseKernels[0]);
+
+}  // namespace nn

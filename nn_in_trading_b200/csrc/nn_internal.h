@@ -1,0 +1,101 @@
+// Internal runtime interfaces of libnn_b200.so (not part of the C ABI).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <string>
+#include <vector>
+
+namespace nn {
+
+constexpr int kMaxArgs = 16;
+
+enum ArgType : uint8_t { ARG_UNSET = 0, ARG_BUF, ARG_INT, ARG_FLOAT };
+
+struct Arg {
+  ArgType type = ARG_UNSET;
+  int i = 0;    // buffer handle or int value
+  float f = 0;  // float value
+};
+
+struct KernelDef;
+
+struct KernelInst {
+  const KernelDef *def = nullptr;
+  Arg args[kMaxArgs];
+  int batch = 1;
+};
+
+struct NDR {
+  int dims = 1;
+  size_t g[3] = {1, 1, 1};
+  size_t l[3] = {1, 1, 1};
+  bool has_local = false;
+};
+
+struct Context;
+
+// What a kernel launcher sees: resolved arguments plus validation helpers.
+// Launchers return NN_OK or a negative status after calling fail().
+struct Launch {
+  Context *ctx;
+  const KernelInst *k;
+  NDR nd;
+  cudaStream_t stream;
+  int B;  // batch
+
+  // Device pointer of buffer argument `idx`, checked to hold at least
+  // `need` floats.  Returns nullptr (and records the error) otherwise.
+  float *buf(int idx, size_t need);
+  // Buffer argument that may legitimately be unused (flags disabled).
+  float *buf_opt(int idx);
+  int i(int idx) const { return k->args[idx].i; }
+  float f(int idx) const { return k->args[idx].f; }
+  int fail(int status, const std::string &msg);
+  // Per-context scratch of at least `floats` floats (slot 0..3 independent).
+  float *scratch(int slot, size_t floats);
+  // Data-parallel deferred-update hooks (see nn_dp_update_begin).
+  bool deferred() const;
+  // Arena slot for a weight gradient of n floats, or nullptr when not deferring.
+  float *grad_slot(size_t n);
+  // Queue the apply half of a deferred update.
+  void defer(int (*apply)(const Launch &, const float *grad), const float *grad);
+  // Count of CUDA launches issued (for the launch counter).
+  void counted(int n = 1);
+};
+
+typedef int (*LaunchFn)(Launch &);
+
+struct KernelDef {
+  const char *name;
+  const char *argtypes;  // p = buffer, i = int, f = float, one char per argument
+  LaunchFn fn;
+  bool param_only;       // touches only parameter buffers (deferrable in DP mode)
+};
+
+// Kernel tables of the translation units.
+extern const KernelDef kDenseKernels[];
+extern const int kNumDenseKernels;
+extern const KernelDef kConvKernels[];
+extern const int kNumConvKernels;
+extern const KernelDef kAttnKernels[];
+extern const int kNumAttnKernels;
+extern const KernelDef kMiscKernels[];
+extern const int kNumMiscKernels;
+
+const KernelDef *find_kernel(const char *name);
+
+inline unsigned int ceil_div(size_t a, size_t b) { return (unsigned int)((a + b - 1) / b); }
+
+// Launch-config helper: grid of `n` threads with `threads` per block.
+inline dim3 grid1d(size_t n, int threads) { return dim3(ceil_div(n, threads)); }
+
+#define NN_CHECK_LAUNCH(L)                                                            \
+  do {                                                                                \
+    cudaError_t e_ = cudaGetLastError();                                              \
+    if (e_ != cudaSuccess) return (L).fail(NN_ERR_CUDA, cudaGetErrorString(e_));      \
+    (L).counted();                                                                    \
+  } while (0)
+
+}  // namespace nn

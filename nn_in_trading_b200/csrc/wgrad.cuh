@@ -1,0 +1,73 @@
+// Weight-gradient reductions shared by the dense and convolution update
+// kernels.  A batched update first reduces the per-sample weight gradients
+// sum_b A(m,b..) B(b..,n) with a split-K SIMT GEMM into per-split partials,
+// then an apply kernel sums the partials, scales by 1/batch and runs the
+// reference update arithmetic on every weight.  In a data-parallel update
+// region the summed, scaled gradient is written to the gradient arena
+// instead, averaged over ranks, and applied afterwards.
+#pragma once
+#include "gemm_simt.cuh"
+#include "nn_device.cuh"
+#include "nn_internal.h"
+
+namespace nn {
+
+struct PartialStore {
+  float *p;
+  int M, N, nz;
+  __device__ void operator()(int m, int n, int z, int split, float acc) const {
+    p[(((size_t)split * nz + z) * M + m) * N + n] = acc;
+  }
+};
+
+// Gradient source for an apply kernel: G(idx) = scale * sum_s p[s*stride + idx].
+struct GradSrc {
+  const float *p;
+  int splits;
+  size_t stride;
+  float scale;
+  __device__ __forceinline__ float operator()(size_t idx) const {
+    float s = 0.f;
+    for (int k = 0; k < splits; ++k) s += p[k * stride + idx];
+    return s * scale;
+  }
+};
+
+__global__ void reduce_partials_kernel(float *out, GradSrc src, size_t n);
+
+// Runs the split-K GEMM into scratch slot 0 and returns the gradient source
+// (not yet scaled).  M x N per z problem, K reduction length.
+template <bool AK, bool BN, class LA, class LB>
+inline int wgrad_partials(Launch &L, int M, int N, int K, int nz, LA la, LB lb, GradSrc *out) {
+  int splits = pick_splits(M, N, K, nz);
+  size_t per = (size_t)M * N * nz;
+  float *part = L.scratch(0, per * splits);
+  if (!part) return NN_ERR_CUDA;
+  GemmShape sh{M, N, K, nz, splits};
+  cudaError_t e = gemm_simt<AK, BN>(sh, la, lb, PartialStore{part, M, N, nz}, L.stream);
+  if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
+  L.counted();
+  out->p = part;
+  out->splits = splits;
+  out->stride = per;
+  out->scale = 1.f;
+  return NN_OK;
+}
+
+// Either hands `src` to `apply` directly, or (inside a data-parallel update
+// region) reduces it into an arena slot and defers `apply` until the ranks'
+// gradients have been averaged.
+inline int finish_update(Launch &L, GradSrc src, size_t n, int (*apply)(const Launch &, const float *),
+                         int (*apply_src)(const Launch &, GradSrc)) {
+  if (L.deferred()) {
+    float *slot = L.grad_slot(n);
+    if (!slot) return NN_ERR_BOUNDS;
+    reduce_partials_kernel<<<(unsigned)((n + 255) / 256), 256, 0, L.stream>>>(slot, src, n);
+    NN_CHECK_LAUNCH(L);
+    L.defer(apply, slot);
+    return NN_OK;
+  }
+  return apply_src(L, src);
+}
+
+}  // namespace nn

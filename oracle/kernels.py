@@ -1,0 +1,534 @@
+"""ORACLE TEST INFRASTRUCTURE -- numpy restatement of the NeuroNet.cl kernels.
+
+This module is the checker, never the product: only tests/, the golden-vector
+generator, __graft_entry__.smoke() and the CPU-baseline leg of bench.py may
+use it.  Each function restates one reference kernel of
+Experts/NeuroNet_DNG/NeuroNet.cl (cited per function) with the same
+positional arguments and the same NDRange meaning (`gsize`/`lsize` are the
+global and local work sizes the MQL5 host enqueues), operating in place on
+float32 numpy arrays.  Sums are reassociated (vectorised) where the
+reference sums serially; parity with the reference is therefore
+tolerance-based, and the restatement is pinned against the reference kernels
+themselves (oracle/_ref, compiled from the reference source) through the
+golden vectors in tests/golden/.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+F32 = np.float32
+L1 = F32(1.0e-4)            # NeuroNet.cl:15
+L2 = F32(1.0e-4)            # NeuroNet.cl:16
+MAX_GRAD = F32(1.0e-2)      # NeuroNet.cl:17
+LOCAL_ARRAY_SIZE = 64       # NeuroNet.cl:18
+MAX_VALUE = F32(3.4e37)     # NeuroNet.cl:20
+MIN_VALUE = F32(-3.4e37)    # NeuroNet.cl:21
+
+# ENUM_ACTIVATION, NeuroNet.cl:32-39 / NeuroNet_Definitions.mqh:3650-3669
+NONE, TANH, SIGMOID, LRELU, SOFTPLUS, GELU, MINUS_SOFTPLUS, ELU = -1, 0, 1, 2, 3, 4, 5, 6
+# ENUM_OPTIMIZATION, NeuroNet_Definitions.mqh:3671-3685
+SGD, ADAM, LS, ADAM_MINI = 0, 1, 2, 3
+
+
+def _err():
+    return np.errstate(all="ignore")
+
+
+def nan0(x, default=0.0):
+    """IsNaNOrInf (NeuroNet.cl:53-61): non-finite -> default."""
+    x = np.asarray(x, dtype=F32)
+    return np.where(np.isfinite(x), x, F32(default)).astype(F32)
+
+
+def cl_clamp(x, lo, hi):
+    """OpenCL clamp as min(max(x, lo), hi) with IEEE fmin/fmax (NaN -> lo)."""
+    return np.fmin(np.fmax(np.asarray(x, dtype=F32), F32(lo)), F32(hi)).astype(F32)
+
+
+def cl_sign(x):
+    x = np.asarray(x, dtype=F32)
+    return np.where(np.isnan(x), F32(0), np.sign(x)).astype(F32)
+
+
+def f_activation(value, act):
+    """fActivation, NeuroNet.cl:88-125."""
+    with _err():
+        r = nan0(value)
+        if act == TANH:
+            r = np.tanh(cl_clamp(r, -20.0, 20.0))
+        elif act == SIGMOID:
+            r = F32(1) / (F32(1) + np.exp(cl_clamp(-r, -20.0, 20.0)))
+        elif act == LRELU:
+            r = np.where(r < 0, r * F32(0.01), r)
+        elif act == SOFTPLUS:
+            r = np.where(r >= F32(20), r, nan0(np.log(F32(1) + np.exp(r))))
+        elif act == GELU:
+            r = r / (F32(1) + np.exp(cl_clamp(F32(-1.702) * r, -20.0, 20.0)))
+        elif act == MINUS_SOFTPLUS:
+            r = -f_activation(r, SOFTPLUS)
+        elif act == ELU:
+            r = np.where(r < 0, nan0(np.exp(r)) - F32(1), r)
+        return nan0(r)
+
+
+def deactivation(grad, inp, act):
+    """Deactivation, NeuroNet.cl:129-174 (derivative from the activation *output*)."""
+    with _err():
+        grad = np.asarray(grad, dtype=F32)
+        inp = np.asarray(inp, dtype=F32)
+        r = nan0(grad)
+        if act == TANH:
+            r = (cl_clamp(grad + inp, -1.0, 1.0) - inp) * (F32(1) - inp * inp)
+        elif act == SIGMOID:
+            r = (cl_clamp(grad + inp, 0.0, 1.0) - inp) * (inp * (F32(1) - inp))
+        elif act == LRELU:
+            r = np.where(inp < 0, r * F32(0.01), r)
+        elif act == SOFTPLUS:
+            r = r * (F32(1) - np.exp(-inp))
+        elif act == GELU:
+            r = np.where(inp < F32(0.9), r * f_activation(F32(5) * inp, SIGMOID), r)
+        elif act == MINUS_SOFTPLUS:
+            r = deactivation(-r, -inp, SOFTPLUS)
+            return r
+        elif act == ELU:
+            r = np.where(inp < 0, r * (inp + F32(1)), r)
+        r = np.where(np.isfinite(inp), r, F32(0))
+        return cl_clamp(nan0(r), -MAX_GRAD, MAX_GRAD)
+
+
+# --------------------------------------------------------------------- dense
+def FeedForward(matrix_w, matrix_i, matrix_o, inputs, activation, numeric_flags, flags_enabled,
+                gsize, lsize=None):
+    """NeuroNet.cl:430-512.  o[i] = act(sum_k w[i,k] x[k] + w[i,inputs]); rows of (inputs+1)."""
+    total_out = gsize[0]
+    with _err():
+        w = matrix_w[:total_out * (inputs + 1)].reshape(total_out, inputs + 1)
+        x = matrix_i[:inputs]
+        xs = nan0(x)
+        prod = nan0(xs[None, :] * w[:, :inputs])
+        s = prod.sum(axis=1, dtype=F32) + nan0(w[:, inputs])
+        y = f_activation(s, activation)
+        if flags_enabled:
+            bad = (~np.isfinite(x)[None, :] | ~np.isfinite(w[:, :inputs])
+                   | ~np.isfinite(x[None, :] * w[:, :inputs])).any(axis=1)
+            bad |= ~np.isfinite(w[:, inputs]) | ~np.isfinite(s) | ~np.isfinite(y)
+            numeric_flags[:total_out] = bad.astype(F32)
+        matrix_o[:total_out] = y
+
+
+def CalcOutputGradient(matrix_t, matrix_o, matrix_ig, activation, error, gsize, lsize=None):
+    """NeuroNet.cl:523-536.  ig = Deactivation(t - o, o, act) (the `error` argument is unused)."""
+    n = gsize[0]
+    with _err():
+        o = matrix_o[:n]
+        g = deactivation(matrix_t[:n] - o, o, activation)
+        matrix_ig[:n] = np.where(np.isfinite(o), g, F32(0))
+
+
+def CalcHiddenGradient(matrix_w, matrix_g, matrix_o, matrix_ig, outputs, activation, gsize, lsize=None):
+    """NeuroNet.cl:547-613.  ig[i] = Deactivation(sum_k w[k,i] g[k], o[i], act)."""
+    inputs = gsize[0]
+    with _err():
+        w = nan0(matrix_w[:outputs * (inputs + 1)].reshape(outputs, inputs + 1)[:, :inputs])
+        g = nan0(matrix_g[:outputs])
+        s = (w * g[:, None]).sum(axis=0, dtype=F32)
+        matrix_ig[:inputs] = deactivation(s, matrix_o[:inputs], activation)
+
+
+def UpdateWeightsMomentum(matrix_w, matrix_g, matrix_i, matrix_dw, inputs, learning_rates, momentum,
+                          gsize, lsize=None):
+    """NeuroNet.cl:624-645.  SGD with momentum; gradient clamped to +-MAX_GRAD per output."""
+    n_out, n_col = gsize[0], gsize[1]
+    with _err():
+        idx = (np.arange(n_out)[:, None] * (inputs + 1) + np.arange(n_col)[None, :])
+        grad = cl_clamp(matrix_g[:n_out], -MAX_GRAD, MAX_GRAD)[:, None]
+        xj = np.where(np.arange(n_col) < inputs, matrix_i[np.minimum(np.arange(n_col), inputs - 1)], F32(1))
+        delta = nan0(F32(learning_rates) * grad * xj[None, :]) + nan0(F32(momentum) * matrix_dw[idx])
+        matrix_dw[idx] = delta
+        w = matrix_w[idx]
+        matrix_w[idx] = np.where(np.abs(delta) > 0, nan0(w + delta), w)
+
+
+def adam_dense_apply(matrix_w, grad, matrix_m, matrix_v, inputs, l, b1, b2, n_out, n_col):
+    """Adam arithmetic of UpdateWeightsAdam (NeuroNet.cl:678-693) given the pre-clamp gradient
+    grad[i, j] (i < n_out, j < n_col) of the weight at row i, column j of a (inputs+1)-wide matrix."""
+    with _err():
+        idx = (np.arange(n_out)[:, None] * (inputs + 1) + np.arange(n_col)[None, :])
+        weight = nan0(matrix_w[idx])
+        m = nan0(matrix_m[idx])
+        v = nan0(matrix_v[idx])
+        g = cl_clamp(nan0(grad), -MAX_GRAD, MAX_GRAD)
+        b1, b2, l = F32(b1), F32(b2), F32(l)
+        mt = nan0(b1 * m + (F32(1) - b1) * g)
+        vt = nan0(b2 * v + (F32(1) - b2) * (g * g))
+        delta = nan0(l * (mt / (np.sqrt(vt) + F32(1e-37)) - (L1 * cl_sign(weight) + L2 * weight)))
+        w = matrix_w[idx]
+        matrix_w[idx] = np.where(np.abs(delta) > 0, nan0(w + delta), w)
+        matrix_m[idx] = mt
+        matrix_v[idx] = vt
+
+
+def UpdateWeightsAdam(matrix_w, matrix_g, matrix_i, matrix_m, matrix_v, inputs, l, b1, b2, gsize, lsize=None):
+    """NeuroNet.cl:657-694.  g = clamp(g_o * x_j); Adam with eps 1e-37 outside the root, l1/l2 decay."""
+    n_out, n_col = gsize[0], gsize[1]
+    with _err():
+        j = np.arange(n_col)
+        inp = nan0(np.where(j == inputs, F32(1), matrix_i[np.minimum(j, max(inputs - 1, 0))]))
+        grad = nan0(matrix_g[:n_out][:, None] * inp[None, :])
+    adam_dense_apply(matrix_w, grad, matrix_m, matrix_v, inputs, l, b1, b2, n_out, n_col)
+
+
+def NormalizeWeights(buffer, dimension, gsize, lsize=None):
+    """NeuroNet.cl:1498-1525.  Each row of `dimension` values is rescaled to unit L2 norm if its norm > 1;
+    a row whose sum of squares overflows is retried with the values pre-divided by 10, 100, ..."""
+    rows = gsize[0]
+    with _err():
+        b = buffer[:rows * dimension].reshape(rows, dimension)
+        x = nan0(b)
+        k = np.ones(rows, F32)
+        s = (x ** 2).sum(axis=1, dtype=F32)
+        for r in np.nonzero(~np.isfinite(s))[0]:
+            while True:
+                k[r] = F32(k[r] * 10)
+                s[r] = ((x[r] / k[r]) ** 2).sum(dtype=F32)
+                if np.isfinite(s[r]):
+                    break
+        d = k * np.sqrt(s)
+        out = np.where((d > 1)[:, None], x / d[:, None], b)
+        buffer[:rows * dimension] = out.reshape(-1)
+
+
+# ---------------------------------------------------------------------- conv
+def FeedForwardConv(matrix_w, matrix_i, matrix_o, inputs, step, window_in, window_out, activation,
+                    gsize, lsize=None):
+    """NeuroNet.cl:887-932.  Strided 1-D conv per variable; w[v][window_out][window_in+1] with bias last."""
+    units = gsize[0]
+    wout = gsize[1]
+    var = gsize[2] if len(gsize) > 2 else 1
+    with _err():
+        for v in range(var):
+            w = matrix_w[v * window_out * (window_in + 1):(v + 1) * window_out * (window_in + 1)]
+            w = w.reshape(window_out, window_in + 1)
+            x = nan0(matrix_i[v * inputs:(v + 1) * inputs])
+            out = np.empty((units, wout), dtype=F32)
+            for i in range(units):
+                si = step * i
+                stop = min(window_in, inputs - si)
+                acc = np.zeros(wout, dtype=F32)
+                if stop > 0:
+                    acc = nan0(x[si:si + stop][None, :] * w[:wout, :stop]).sum(axis=1, dtype=F32)
+                acc = acc + nan0(w[:wout, window_in])
+                out[i] = acc
+            base = v * window_out * units
+            o = matrix_o[base:base + units * window_out].reshape(units, window_out)
+            o[:, :wout] = f_activation(out, activation)
+
+
+def CalcHiddenGradientConv(matrix_w, matrix_g, matrix_o, matrix_ig, outputs, step, window_in, window_out,
+                           activation, shift_out, gsize, lsize=None):
+    """NeuroNet.cl:941-986.  Input gradient of FeedForwardConv (overlap-add over windows) + Deactivation."""
+    inputs = gsize[0]
+    var = gsize[1] if len(gsize) > 1 else 1
+    n_win = outputs // window_out
+    with _err():
+        for v in range(var):
+            w = matrix_w[v * window_out * (window_in + 1):(v + 1) * window_out * (window_in + 1)]
+            w = w.reshape(window_out, window_in + 1)
+            g = nan0(matrix_g[shift_out + v * outputs: shift_out + v * outputs + n_win * window_out])
+            g = g.reshape(n_win, window_out)
+            s = np.zeros(inputs, dtype=F32)
+            for k in range(n_win):
+                lo = k * step
+                if lo >= inputs:
+                    break
+                hi = min(lo + window_in, inputs)
+                # contribution of window k to positions lo..hi-1
+                s[lo:hi] += nan0(g[k][:, None] * w[:, :hi - lo]).sum(axis=0, dtype=F32)
+            o = matrix_o[v * inputs:(v + 1) * inputs]
+            matrix_ig[v * inputs:(v + 1) * inputs] = deactivation(s, o, activation)
+
+
+def conv_weight_grad(matrix_g, matrix_i, inputs, window_in, window_out, step, n_weights, momentum_variant=False):
+    """Per-weight gradient loops of UpdateWeightsConvAdam (NeuroNet.cl:1073-1081) and
+    UpdateWeightsConvMomentum (NeuroNet.cl:1016-1031), including their index quirks:
+    Adam uses total = (inputs-(window_in-step)+(step-1))/step and shift_out = i/(window_in+1)-v*window_out;
+    Momentum uses total = (inputs-window_in+step-1)/step and shift_out = i/(window_in+1)-v;
+    both stop at the first t with shift + t*window_in >= inputs (window_in, not step)."""
+    i = np.arange(n_weights)
+    v = i // ((window_in + 1) * window_out)
+    shift = i % (window_in + 1)
+    if momentum_variant:
+        shift_out = i // (window_in + 1) - v
+        total = (inputs - window_in + step - 1) // step
+    else:
+        shift_out = i // (window_in + 1) - v * window_out
+        total = (inputs - (window_in - step) + (step - 1)) // step
+    grad = np.zeros(n_weights, dtype=F32)
+    with _err():
+        alive = np.ones(n_weights, dtype=bool)
+        for t in range(max(total, 0)):
+            alive &= ~((shift != window_in) & (shift + t * window_in >= inputs))
+            if not alive.any():
+                break
+            gi = t * window_out + shift_out + v * total * window_out
+            xi = np.where(shift == window_in, 0, shift + t * step + v * inputs)
+            gv = matrix_g[np.clip(gi, 0, matrix_g.size - 1)]
+            xv = np.where(shift == window_in, F32(1), matrix_i[np.clip(xi, 0, matrix_i.size - 1)])
+            grad = np.where(alive, grad + nan0(gv * xv), grad).astype(F32)
+    return grad
+
+
+def UpdateWeightsConvMomentum(matrix_w, matrix_g, matrix_i, matrix_dw, inputs, learning_rates, momentum,
+                              window_in, window_out, step, gsize, lsize=None):
+    """NeuroNet.cl:996-1043."""
+    n = gsize[0]
+    grad = conv_weight_grad(matrix_g, matrix_i, inputs, window_in, window_out, step, n, momentum_variant=True)
+    with _err():
+        delta = nan0(F32(learning_rates) * grad) + F32(momentum) * matrix_dw[:n]
+        ok = ~np.isnan(delta)
+        w = matrix_w[:n]
+        matrix_dw[:n] = np.where(ok, delta, matrix_dw[:n])
+        matrix_w[:n] = np.where(ok & (np.abs(delta) > 0), nan0(w + delta), w)
+
+
+def adam_conv_apply(matrix_w, grad, matrix_m, matrix_v, l, b1, b2, n):
+    """Adam arithmetic of UpdateWeightsConvAdam (NeuroNet.cl:1082-1097): no eps, no l1/l2, vt NaN -> 1."""
+    with _err():
+        b1, b2, l = F32(b1), F32(b2), F32(l)
+        g = cl_clamp(nan0(grad), -MAX_GRAD, MAX_GRAD)
+        mt = nan0(b1 * matrix_m[:n] + (F32(1) - b1) * g)
+        vt = nan0(b2 * matrix_v[:n] + (F32(1) - b2) * (g * g), 1.0)
+        weight = nan0(matrix_w[:n] + nan0(l * mt / np.sqrt(vt)))
+        matrix_w[:n] = weight
+        matrix_m[:n] = mt
+        matrix_v[:n] = vt
+
+
+def UpdateWeightsConvAdam(matrix_w, matrix_g, matrix_i, matrix_m, matrix_v, inputs, l, b1, b2,
+                          window_in, window_out, step, gsize, lsize=None):
+    """NeuroNet.cl:1053-1098."""
+    n = gsize[0]
+    grad = conv_weight_grad(matrix_g, matrix_i, inputs, window_in, window_out, step, n)
+    adam_conv_apply(matrix_w, grad, matrix_m, matrix_v, l, b1, b2, n)
+
+
+# ---------------------------------------------------------- residual / norm
+def SumMatrix(matrix1, matrix2, matrix_out, dimension, multiplyer, shift_in1, shift_in2, shift_out,
+              numeric_flags, flags_enabled, gsize, lsize=None):
+    """NeuroNet.cl:1314-1347.  out = (a + b) * multiplyer, row i offset by i*shift_*."""
+    rows = gsize[0]
+    with _err():
+        r = np.arange(rows)[:, None]
+        index = r * dimension + np.arange(dimension)[None, :]
+        a = matrix1[r * shift_in1 + index]
+        b = matrix2[r * shift_in2 + index]
+        raw = (a + b) * F32(multiplyer)
+        if flags_enabled:
+            bad = ~np.isfinite(a) | ~np.isfinite(b) | ~np.isfinite(a + b) | ~np.isfinite(raw)
+            numeric_flags[index] = bad.astype(F32)
+        matrix_out[r * shift_out + index] = nan0(raw)
+
+
+def Normalize(buffer, dimension, gsize, lsize=None):
+    """NeuroNet.cl:1455-1486.  Row centring; divide by the (unbiased) *variance* only when it exceeds 1."""
+    rows = gsize[0]
+    if dimension < 1:
+        return
+    with _err():
+        b = buffer[:rows * dimension].reshape(rows, dimension)
+        x = nan0(b)
+        mean = x.mean(axis=1, dtype=np.float64).astype(F32)
+        var = (((x - mean[:, None]).astype(np.float64) ** 2).sum(axis=1) / (dimension - 1)).astype(F32) \
+            if dimension > 1 else np.full(rows, np.nan, F32)
+        c = b - mean[:, None]
+        out = np.where((var > 1)[:, None], c / var[:, None], c)
+        buffer[:rows * dimension] = nan0(out).reshape(-1)
+
+
+# ----------------------------------------------------------------- attention
+def MHAttentionScore(qkv, score, dimension, mask, gsize, lsize=None):
+    """NeuroNet.cl:1662-1719.  S[q,h,k] = exp(clamp(q.k/sqrt(d), +-100)), divided by the row sum only
+    when that sum exceeds 1 (no max subtraction); qkv is [unit][3][head][dimension]."""
+    units, heads = gsize[0], gsize[1]
+    koef = max(np.sqrt(F32(dimension)), F32(1))
+    with _err():
+        t = qkv[:units * 3 * heads * dimension].reshape(units, 3, heads, dimension)
+        q = nan0(t[:, 0])
+        k = nan0(t[:, 1])
+        r = np.einsum("qhd,khd->qhk", q, k).astype(F32)
+        s = np.exp(cl_clamp(r / koef, -100.0, 100.0))
+        s = np.where(np.isnan(s), F32(0), s)
+        if mask > 0:
+            keep = np.arange(units)[None, None, :] <= np.arange(units)[:, None, None]
+            s = np.where(keep, s, F32(0))
+        tot = s.sum(axis=2, dtype=F32)
+        s = np.where((tot > 1)[:, :, None], s / tot[:, :, None], s)
+        score[:units * heads * units] = s.reshape(-1)
+
+
+def MHAttentionOut(scores, qkv, out, dimension, gsize, lsize=None):
+    """NeuroNet.cl:1730-1759.  O[u,h,:] = sum_v S[u,h,v] V[v,h,:]."""
+    units, heads = gsize[0], gsize[1]
+    with _err():
+        s = scores[:units * heads * units].reshape(units, heads, units)
+        v = qkv[:units * 3 * heads * dimension].reshape(units, 3, heads, dimension)[:, 2]
+        out[:units * heads * dimension] = np.einsum("uhv,vhd->uhd", s, v).astype(F32).reshape(-1)
+
+
+def MHAttentionInsideGradients(qkv, qkv_g, scores, gradient, gsize, lsize=None):
+    """NeuroNet.cl:1777-1845.  dV = S^T g;  dQ[u,:,d] = g[u,d]/sqrt(d) sum_k S[u,k](V0[k]-A[u]) K[k,d];
+    dK[u,:,d] = sum_q g[q,d]/sqrt(d) S[q,u](V0[u]-A[q]) Q[q,d];  A[q] = sum_v S[q,v] V0[v].
+    V0 is feature 0 of V: the reference reads V at qkv[dimension*(heads*(3v+2)+h)] without +d
+    (NeuroNet.cl:1822, 1840).  The reference's triple loop sum_v S_v V0_v g (d_kv - S_k) is evaluated in
+    the algebraically equal factorised form g S_k (V0_k - A)."""
+    units, heads, dim = gsize[0], gsize[1], gsize[2]
+    koef = max(np.sqrt(F32(dim)), F32(1))
+    with _err():
+        t = qkv[:units * 3 * heads * dim].reshape(units, 3, heads, dim)
+        Q, K, V = t[:, 0], t[:, 1], t[:, 2]
+        S = scores[:units * heads * units].reshape(units, heads, units)
+        G = gradient[:units * heads * dim].reshape(units, heads, dim)
+        V0 = V[:, :, 0]                                         # [v, h]
+        A = np.einsum("uhv,vh->uh", S, V0).astype(F32)          # [u, h]
+        C = S * (V0.T[None, :, :] - A[:, :, None])              # [u, h, k]
+        dV = np.einsum("ihu,ihd->uhd", S, G).astype(F32)
+        dQ = (G * np.einsum("uhk,khd->uhd", C, K)) / koef
+        dK = np.einsum("qhu,qhd->uhd", C, G * Q) / koef
+        g = np.stack([dQ, dK, dV], axis=1).astype(F32)
+        qkv_g[:units * 3 * heads * dim] = g.reshape(-1)
+
+
+# ------------------------------------------------------------------- softmax
+def _softmax_rows(x):
+    with _err():
+        x = nan0(x, MIN_VALUE)
+        mx = x.max(axis=-1, keepdims=True)
+        e = np.where(x == MIN_VALUE, F32(0), nan0(np.exp(x - mx)))
+        s = e.sum(axis=-1, keepdims=True, dtype=F32)
+        y = np.where(s == 0, F32(0), nan0(e / s))
+        return np.where(mx == MIN_VALUE, F32(0), y).astype(F32)
+
+
+def SoftMax_FeedForward(inputs, outputs, gsize, lsize):
+    """NeuroNet.cl:2479-2492 (LocalSoftMax, NeuroNet.cl:392-408): max-subtracted softmax per head row of
+    length local_size(0)."""
+    size, heads = lsize[0], gsize[1] if len(gsize) > 1 else 1
+    outputs[:size * heads] = _softmax_rows(inputs[:size * heads].reshape(heads, size)).reshape(-1)
+
+
+def SoftMax_HiddenGradient(outputs, output_gr, input_gr, gsize, lsize):
+    """NeuroNet.cl:2496-2510 (LocalSoftMaxGrad, NeuroNet.cl:412-420): y (g - sum y g)."""
+    size, heads = lsize[0], gsize[1] if len(gsize) > 1 else 1
+    with _err():
+        y = nan0(outputs[:size * heads].reshape(heads, size))
+        g = nan0(output_gr[:size * heads].reshape(heads, size))
+        s = nan0((y * g).sum(axis=1, keepdims=True, dtype=F32))
+        input_gr[:size * heads] = nan0(y * (g - s)).reshape(-1)
+
+
+def SoftMax_OutputGradient(outputs, targets, output_gr, gsize, lsize=None):
+    """NeuroNet.cl:2514-2520.  g = t / y (0 where y == 0)."""
+    n = gsize[0]
+    with _err():
+        y = outputs[:n]
+        output_gr[:n] = np.where(y == 0, F32(0), targets[:n] / y)
+
+
+# -------------------------------------------------------------- elementwise
+def Activation(inputs, outputs, activation, gsize, lsize=None):
+    """NeuroNet.cl:5796-5808."""
+    n = gsize[0]
+    outputs[:n] = f_activation(nan0(inputs[:n]), activation)
+
+
+def DeActivation(inputs, inputs_gr, output_gr, activation, gsize, lsize=None):
+    """NeuroNet.cl:5811-5823."""
+    n = gsize[0]
+    inputs_gr[:n] = deactivation(nan0(output_gr[:n]), inputs[:n], activation)
+
+
+def SoftUpdate(target, source, tau, gsize, lsize=None):
+    """NeuroNet.cl:3864-3871.  Polyak averaging."""
+    n = gsize[0]
+    with _err():
+        tau = F32(tau)
+        target[:n] = source[:n] * tau + (F32(1) - tau) * target[:n]
+
+
+def SoftUpdateAdam(target, source, matrix_m, matrix_v, tau, b1, b2, gsize, lsize=None):
+    """NeuroNet.cl:3875-3899.  Adam-style soft update on g = source - target, step (1-tau) m/sqrt(v)."""
+    n = gsize[0]
+    with _err():
+        b1, b2, tau = F32(b1), F32(b2), F32(tau)
+        w = target[:n].copy()
+        g = source[:n] - w
+        m = b1 * matrix_m[:n] + (F32(1) - b1) * g
+        v = b2 * matrix_v[:n] + (F32(1) - b2) * (g * g)
+        delta = (F32(1) - tau) * m / np.where(v != 0, np.sqrt(v), F32(1))
+        target[:n] = np.where(np.abs(delta) > 0, w + delta, w)
+        matrix_m[:n] = m
+        matrix_v[:n] = v
+
+
+def Transpose(matrix_in, matrix_out, gsize, lsize=None):
+    """NeuroNet.cl:4237-4248."""
+    rows, cols = gsize[0], gsize[1]
+    matrix_out[:rows * cols] = matrix_in[:rows * cols].reshape(rows, cols).T.reshape(-1)
+
+
+def ConcatenateBuffers(input1, window1, input2, window2, input3, window3, input4, window4, output,
+                       gsize, lsize=None):
+    """NeuroNet.cl:1538-1576."""
+    n = gsize[0]
+    tot = window1 + window2 + window3 + window4
+    o = output[:n * tot].reshape(n, tot)
+    off = 0
+    for src, w in ((input1, window1), (input2, window2), (input3, window3), (input4, window4)):
+        if w > 0:
+            o[:, off:off + w] = nan0(src[:n * w].reshape(n, w))
+        off += w
+
+
+def DeconcatenateBuffers(output1, window1, output2, window2, output3, window3, output4, window4, inputs,
+                         gsize, lsize=None):
+    """NeuroNet.cl:1601-1650."""
+    n = gsize[0]
+    tot = window1 + window2 + window3 + window4
+    x = inputs[:n * tot].reshape(n, tot)
+    off = 0
+    for dst, w in ((output1, window1), (output2, window2), (output3, window3), (output4, window4)):
+        if w > 0:
+            dst[:n * w] = nan0(x[:, off:off + w]).reshape(-1)
+        off += w
+
+
+def RevInFeedForward(inputs, options, output, options_size, optimization, gsize, lsize=None):
+    """NeuroNet.cl:5742-5764.  y = sqrt(var) (x - beta) / max(gamma, 1e-3) + mean with BatchNorm options."""
+    n = gsize[0]
+    with _err():
+        shift = (np.arange(n) * (7 if optimization == 0 else 9)) % options_size
+        mean, var, k, beta = options[shift], options[shift + 1], options[shift + 3], options[shift + 4]
+        res = np.sqrt(var) * (inputs[:n] - beta) / np.fmax(k, F32(0.001)) + mean
+        output[:n] = np.where(np.isnan(res), F32(0), res)
+
+
+def RevInHiddenGraddient(inputs, inputs_gr, options, output_gr, options_size, optimization, activation,
+                         gsize, lsize=None):
+    """NeuroNet.cl:5767-5793."""
+    n = gsize[0]
+    with _err():
+        shift = (np.arange(n) * (7 if optimization == 0 else 9)) % options_size
+        var, k = options[shift + 1], options[shift + 3]
+        res = np.sqrt(var) * output_gr[:n]
+        res = np.where(np.abs(k) > 1, res / k, res)
+        res = np.where(np.isnan(res), F32(0), res)
+        inputs_gr[:n] = deactivation(res, inputs[:n], activation)
+
+
+KERNELS = {name: fn for name, fn in globals().items()
+           if callable(fn) and name[:1].isupper() and fn.__module__ == __name__}
+
+
+def launch(name, gsize, lsize, args):
+    """Run restated kernel `name` with the reference argument list and NDRange."""
+    KERNELS[name](*args, gsize=tuple(gsize), lsize=None if lsize is None else tuple(lsize))

@@ -1,0 +1,263 @@
+"""ORACLE TEST INFRASTRUCTURE -- numpy restatement of the reference's layer and network sequencing.
+
+Restates, over the kernels of oracle/kernels.py, the kernel sequence the MQL5
+host code issues for one training step: CNet::feedForward / backPropOCL
+(NeuroNet_Core.mqh:13246-13417, 13555-13763), CNeuronBaseOCL
+(NeuroNet_Core.mqh:15686-15984) and CNeuronMLMHAttentionOCL
+(NeuroNet_Attention.mqh:1884-2405), including the per-layer Adam step counter
+that advances after every update call.
+
+Batches follow the library's batch contract: forward and input-gradient
+kernels run per sample exactly as the reference kernel; every weight update
+averages the per-sample weight gradient over the batch, then applies the
+reference update arithmetic once.  Only tests/, __graft_entry__.smoke() and
+bench.py's CPU baseline may use this module.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+from . import kernels as K
+
+F32 = np.float32
+LR, B1, B2 = 3.0e-4, 0.9, 0.999
+MAX_LOCAL = 256
+
+
+class RefBackend:
+    """Kernel backend that runs the reference's own NeuroNet.cl kernels compiled for the CPU
+    (oracle/_ref/libnnref.so) with the same call signature as oracle.kernels."""
+
+    def __init__(self):
+        from .ref import RefKernels
+        self.ref = RefKernels()
+
+    def __getattr__(self, name):
+        if name not in self.ref.sig:
+            raise AttributeError(name)
+
+        def call(*args, gsize, lsize=None):
+            self.ref.launch(name, gsize, lsize, list(args))
+        return call
+
+
+BACKEND = K  # numpy restatement by default
+
+
+def use_backend(kind: str) -> None:
+    """'numpy' (oracle/kernels.py) or 'reference' (oracle/_ref)."""
+    global BACKEND
+    BACKEND = K if kind == "numpy" else RefBackend()
+
+
+def adam_lt(t: int) -> float:
+    """NeuroNet_Core.mqh:15903: lr*sqrt(1-b2^t)/(1-b1^t) in double, cast to float."""
+    return float(F32(LR * math.sqrt(1.0 - math.pow(B2, t)) / (1.0 - math.pow(B1, t))))
+
+
+class OLayer:
+    def __init__(self, neurons, activation=K.NONE, batch=1):
+        self.neurons, self.activation, self.batch = neurons, activation, batch
+        self.output = np.zeros((batch, neurons), F32)
+        self.gradient = np.zeros((batch, neurons), F32)
+        self.t = 1
+
+    def next_lt(self) -> float:
+        lt = adam_lt(self.t)
+        self.t += 1
+        return lt
+
+    def calc_output_gradient(self, target):
+        """CNeuronBaseOCL::calcOutputGradients, NeuroNet_Core.mqh:15800-15837."""
+        for b in range(self.batch):
+            BACKEND.CalcOutputGradient(target[b], self.output[b], self.gradient[b], self.activation, 1.0,
+                                 gsize=(self.neurons,))
+
+
+class ODense(OLayer):
+    """CNeuronBaseOCL: weights toward the next dense layer, [outputs][neurons+1]."""
+
+    def __init__(self, neurons, activation=K.NONE, batch=1, outputs=0):
+        super().__init__(neurons, activation, batch)
+        self.outputs = outputs
+        if outputs:
+            n = outputs * (neurons + 1)
+            self.weights = np.zeros(n, F32)
+            self.m = np.zeros(n, F32)
+            self.v = np.zeros(n, F32)
+
+    def forward(self, prev: "ODense"):
+        """NeuroNet_Core.mqh:15686-15740 -> FeedForward."""
+        loc = min((prev.neurons + 3) // 4, MAX_LOCAL)
+        for b in range(self.batch):
+            BACKEND.FeedForward(prev.weights, prev.output[b], self.output[b], prev.neurons, self.activation,
+                          self.output[b], 0, gsize=(self.neurons, loc), lsize=(1, loc))
+
+    def hidden_gradient(self, nxt: "ODense"):
+        """NeuroNet_Core.mqh:15744-15769 -> CalcHiddenGradient."""
+        loc = min((nxt.neurons + 3) // 4, MAX_LOCAL)
+        for b in range(self.batch):
+            BACKEND.CalcHiddenGradient(self.weights, nxt.gradient[b], self.output[b], self.gradient[b], nxt.neurons,
+                                 self.activation, gsize=(self.neurons, loc), lsize=(1, loc))
+
+    def update(self, prev: "ODense"):
+        """NeuroNet_Core.mqh:15869-15984: UpdateWeightsAdam (batch-mean gradient) + NormalizeWeights."""
+        n_out, n_col, inputs = self.neurons, prev.neurons + 1, prev.neurons
+        inps = [K.nan0(np.concatenate([prev.output[b], np.ones(1, F32)])) for b in range(self.batch)]
+        self.last_grad = np.mean([K.nan0(self.gradient[b][:, None] * inps[b][None, :]) for b in range(self.batch)],
+                                 axis=0, dtype=np.float64).astype(F32).reshape(-1)
+        # sum of |terms| of each weight's gradient: the scale of its rounding error
+        self.last_grad_abs = np.mean([np.abs(K.nan0(self.gradient[b]))[:, None] * np.abs(inps[b])[None, :]
+                                      for b in range(self.batch)], axis=0).reshape(-1)
+        if self.batch == 1:
+            BACKEND.UpdateWeightsAdam(prev.weights, self.gradient[0], prev.output[0], prev.m, prev.v, inputs,
+                                      self.next_lt(), B1, B2, gsize=(n_out, n_col))
+            BACKEND.NormalizeWeights(prev.weights, prev.neurons + 1, gsize=(self.neurons,))
+            return
+        G = self.last_grad.reshape(n_out, n_col)
+        K.adam_dense_apply(prev.weights, G, prev.m, prev.v, inputs, self.next_lt(), B1, B2, n_out, n_col)
+        BACKEND.NormalizeWeights(prev.weights, prev.neurons + 1, gsize=(self.neurons,))
+
+
+class OMLMH(OLayer):
+    """CNeuronMLMHAttentionOCL (NeuroNet_Attention.mqh:1576-2405)."""
+
+    def __init__(self, window, dk, heads, units, layers, activation=K.NONE, batch=1):
+        super().__init__(window * units, activation, batch)
+        self.W, self.D, self.H, self.U, self.L = window, dk, heads, units, layers
+        B, out = batch, window * units
+        num = 3 * dk * heads * units
+        self.counts = {"qkv": 3 * (window + 1) * dk * heads, "w0": (dk + 1) * heads * window,
+                       "ff1": 4 * (window + 1) * window, "ff2": (4 * window + 1) * window}
+        z = lambda n: np.zeros((B, n), F32)  # noqa: E731
+        self.qkv = [z(num) for _ in range(layers)]
+        self.qkv_g = [z(num) for _ in range(layers)]
+        self.scores = [z(units * units * heads) for _ in range(layers)]
+        self.ao = [z(dk * heads * units) for _ in range(layers)]
+        self.ao_g = [z(dk * heads * units) for _ in range(layers)]
+        self.ff = []
+        for i in range(layers):
+            last = i == layers - 1
+            self.ff.append([z(out), z(4 * out), self.output if last else z(out), z(out), z(4 * out),
+                            self.gradient if last else z(out)])
+        self.w = [{k: [np.zeros(n, F32), np.zeros(n, F32), np.zeros(n, F32)] for k, n in self.counts.items()}
+                  for _ in range(layers)]
+        self.last_grads = {}      # (layer, name) -> batch-mean weight gradient of the last update
+        self.last_grads_abs = {}  # (layer, name) -> the same sum over |terms|
+
+    def _conv(self, w, x, o, in_total, window, window_out, act):
+        for b in range(self.batch):
+            BACKEND.FeedForwardConv(w, x[b], o[b], in_total, window, window, window_out, act,
+                              gsize=(o.shape[1] // window_out, window_out, 1))
+
+    def _sum_norm(self, a, bm, out, normalize=True):
+        rows = self.U
+        for b in range(self.batch):
+            BACKEND.SumMatrix(a[b], bm[b], out[b], self.W, 0.5, 0, 0, 0, out[b], 0, gsize=(rows,))
+            if normalize:
+                BACKEND.Normalize(out[b], self.W, gsize=(rows,))
+
+    def forward(self, prev: OLayer):
+        W, U, H, D = self.W, self.U, self.H, self.D
+        out = W * U
+        for i in range(self.L):
+            inputs = prev.output if i == 0 else self.ff[i - 1][2]
+            ws, t = self.w[i], self.ff[i]
+            self._conv(ws["qkv"][0], inputs, self.qkv[i], out, W, 3 * D * H, K.NONE)
+            for b in range(self.batch):
+                BACKEND.MHAttentionScore(self.qkv[i][b], self.scores[i][b], D, 0, gsize=(U, H))
+                BACKEND.MHAttentionOut(self.scores[i][b], self.qkv[i][b], self.ao[i][b], D, gsize=(U, H))
+            self._conv(ws["w0"][0], self.ao[i], t[0], D * H * U, D * H, W, K.NONE)
+            self._sum_norm(t[0], inputs, t[0])
+            self._conv(ws["ff1"][0], t[0], t[1], out, W, 4 * W, K.GELU)
+            self._conv(ws["ff2"][0], t[1], t[2], 4 * out, 4 * W, W, self.activation)
+            self._sum_norm(t[2], t[0], t[2])
+
+    def _dgrad(self, w, g, x, ig, g_total, in_total, window, window_out, act):
+        for b in range(self.batch):
+            BACKEND.CalcHiddenGradientConv(w, g[b], x[b], ig[b], g_total, window, window, window_out, act, 0,
+                                     gsize=(in_total, 1))
+
+    def input_gradient(self, prev: OLayer):
+        W, U, H, D = self.W, self.U, self.H, self.D
+        out = W * U
+        out_grad = self.gradient
+        for i in range(self.L - 1, -1, -1):
+            t, ws = self.ff[i], self.w[i]
+            self._dgrad(ws["ff2"][0], out_grad, t[1], t[4], out, 4 * out, 4 * W, W, K.NONE)
+            self._dgrad(ws["ff1"][0], t[4], t[0], t[3], 4 * out, out, W, 4 * W, K.GELU)
+            self._sum_norm(out_grad, t[3], t[3], normalize=False)
+            out_grad = t[3]
+            self._dgrad(ws["w0"][0], out_grad, self.ao[i], self.ao_g[i], out, D * H * U, D * H, W, K.NONE)
+            for b in range(self.batch):
+                BACKEND.MHAttentionInsideGradients(self.qkv[i][b], self.qkv_g[i][b], self.scores[i][b], self.ao_g[i][b],
+                                             gsize=(U, H, D))
+            if i == 0:
+                inp, tmp = prev.output, prev.gradient
+            else:
+                inp, tmp = self.ff[i - 1][2], self.ff[i - 1][5]
+            self._dgrad(ws["qkv"][0], self.qkv_g[i], inp, tmp, 3 * D * H * U, out, W, 3 * D * H, K.NONE)
+            self._sum_norm(out_grad, tmp, tmp, normalize=False)
+            if i > 0:
+                out_grad = tmp
+
+    def _conv_update(self, wmv, grad, inputs, in_total, window, window_out, key=None):
+        w, m, v = wmv
+        n = (window + 1) * window_out
+        G = np.mean([K.conv_weight_grad(grad[b], inputs[b], in_total, window, window_out, window, n)
+                     for b in range(self.batch)], axis=0, dtype=np.float64).astype(F32)
+        self.last_grads[key] = G
+        self.last_grads_abs[key] = np.mean(
+            [K.conv_weight_grad(np.abs(grad[b]), np.abs(inputs[b]), in_total, window, window_out, window, n)
+             for b in range(self.batch)], axis=0, dtype=np.float64)
+        if self.batch == 1:
+            BACKEND.UpdateWeightsConvAdam(w, grad[0], inputs[0], m, v, in_total, self.next_lt(), B1, B2, window,
+                                          window_out, window, gsize=(n,))
+            BACKEND.NormalizeWeights(w, window + 1, gsize=(window_out,))
+            return
+        K.adam_conv_apply(w, G, m, v, self.next_lt(), B1, B2, n)
+        BACKEND.NormalizeWeights(w, window + 1, gsize=(window_out,))
+
+    def update(self, prev: OLayer):
+        W, U, H, D = self.W, self.U, self.H, self.D
+        out = W * U
+        inputs = prev.output
+        for l in range(self.L):
+            t, ws = self.ff[l], self.w[l]
+            self._conv_update(ws["qkv"], self.qkv_g[l], inputs, out, W, 3 * D * H, (l, "qkv"))
+            self._conv_update(ws["w0"], t[3], self.ao[l], D * H * U, D * H, W, (l, "w0"))
+            self._conv_update(ws["ff1"], t[4], t[0], out, W, 4 * W, (l, "ff1"))
+            self._conv_update(ws["ff2"], t[5], t[1], 4 * out, 4 * W, W, (l, "ff2"))
+            inputs = t[2]
+
+
+class ONet:
+    """CNet training step over oracle layers."""
+
+    def __init__(self, layers: list[OLayer]):
+        self.layers = layers
+
+    def forward(self, x):
+        self.layers[0].output[...] = x.reshape(self.layers[0].output.shape)
+        for l in range(1, len(self.layers)):
+            self.layers[l].forward(self.layers[l - 1])
+
+    def backward(self, target):
+        self.layers[-1].calc_output_gradient(target.reshape(self.layers[-1].output.shape))
+        for l in range(len(self.layers) - 2, -1, -1):
+            cur, nxt = self.layers[l], self.layers[l + 1]
+            if type(nxt) is ODense:
+                cur.hidden_gradient(nxt)
+            else:
+                nxt.input_gradient(cur)
+
+    def update(self):
+        for l in range(len(self.layers) - 1, 0, -1):
+            self.layers[l].update(self.layers[l - 1])
+
+    def step(self, x, target):
+        self.forward(x)
+        self.backward(target)
+        self.update()

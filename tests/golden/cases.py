@@ -1,0 +1,215 @@
+"""Kernel-level parity cases: one entry per (reference kernel, shape, activation).
+
+Each case lists the reference kernel's positional arguments -- float32 arrays
+(`A`) or scalars -- and the NDRange (`gsize`, `lsize`) the MQL5 host would
+enqueue.  `make_golden.py` executes every case with the reference kernels
+compiled from NeuroNet.cl (oracle/_ref) and stores inputs and outputs in
+`kernels.npz`; the tests replay the same cases through the numpy oracle (CPU)
+and through the CUDA library (GPU) and compare every array argument.
+
+Shapes follow the edge rows the reference's callers produce: 1, 3, 4, 63, 64,
+65 and non-multiples of 4, plus every activation.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+
+NONE, TANH, SIGMOID, LRELU, SOFTPLUS, GELU, MINUS_SOFTPLUS, ELU = -1, 0, 1, 2, 3, 4, 5, 6
+ACTS = [NONE, TANH, SIGMOID, LRELU, SOFTPLUS, GELU, MINUS_SOFTPLUS, ELU]
+MAX_LOCAL = 256  # GetMaxLocalSize(1) the golden vectors are generated with
+
+
+@dataclass
+class A:
+    """Array argument: size and initial distribution."""
+    size: int
+    init: str = "normal"      # normal | uniform | zeros | small | pos | unit | act:<id> | grad
+    scale: float = 1.0
+
+
+@dataclass
+class Case:
+    name: str
+    kernel: str
+    args: list
+    gsize: tuple
+    lsize: tuple | None = None
+    tol: float = 1e-4
+    meta: dict = field(default_factory=dict)
+
+
+def materialise(case: Case, seed: int) -> list:
+    """Deterministic inputs of a case (numpy float32 arrays / python scalars)."""
+    rng = np.random.default_rng(seed)
+    out = []
+    for a in case.args:
+        if not isinstance(a, A):
+            out.append(a)
+            continue
+        n = a.size
+        if a.init == "normal":
+            v = rng.standard_normal(n) * a.scale
+        elif a.init == "uniform":
+            v = rng.uniform(-a.scale, a.scale, n)
+        elif a.init == "zeros":
+            v = np.zeros(n)
+        elif a.init == "small":
+            v = rng.standard_normal(n) * 1e-3 * a.scale
+        elif a.init == "pos":
+            v = rng.uniform(0.05, 1.0, n) * a.scale
+        elif a.init == "unit":
+            v = rng.uniform(0.0, 1.0, n)
+        elif a.init == "grad":
+            v = rng.standard_normal(n) * 0.01 * a.scale
+        elif a.init.startswith("act:"):
+            # a plausible activation output for the given activation (used by Deactivation inputs)
+            act = int(a.init[4:])
+            x = rng.standard_normal(n)
+            v = {TANH: np.tanh(x), SIGMOID: 1 / (1 + np.exp(-x)), LRELU: np.where(x < 0, 0.01 * x, x),
+                 SOFTPLUS: np.log1p(np.exp(x)), GELU: x / (1 + np.exp(-1.702 * x)),
+                 MINUS_SOFTPLUS: -np.log1p(np.exp(x)), ELU: np.where(x < 0, np.exp(x) - 1, x)}.get(act, x)
+        else:
+            raise ValueError(a.init)
+        out.append(np.ascontiguousarray(v, dtype=np.float32))
+    return out
+
+
+def _dense_cases():
+    cases = []
+    for n_in, n_out in [(1, 1), (3, 4), (37, 11), (63, 65), (64, 64), (65, 3), (240, 17)]:
+        for act in ([TANH, SIGMOID, NONE] if n_in != 37 else ACTS):
+            loc = min((n_in + 3) // 4, MAX_LOCAL)
+            k = 1 / np.sqrt(n_in)
+            cases.append(Case(f"FeedForward/{n_in}x{n_out}/act{act}", "FeedForward",
+                              [A(n_out * (n_in + 1), "uniform", k), A(n_in), A(n_out, "zeros"), n_in, act,
+                               A(n_out, "zeros"), 0],
+                              (n_out, loc), (1, loc)))
+        loc = min((n_out + 3) // 4, MAX_LOCAL)
+        for act in ([TANH, SIGMOID, NONE] if n_in != 37 else ACTS):
+            cases.append(Case(f"CalcHiddenGradient/{n_in}x{n_out}/act{act}", "CalcHiddenGradient",
+                              [A(n_out * (n_in + 1), "uniform", 1 / np.sqrt(n_in)), A(n_out, "grad"),
+                               A(n_in, f"act:{act}"), A(n_in, "zeros"), n_out, act],
+                              (n_in, loc), (1, loc)))
+        cases.append(Case(f"UpdateWeightsAdam/{n_in}x{n_out}", "UpdateWeightsAdam",
+                          [A(n_out * (n_in + 1), "uniform", 1 / np.sqrt(n_in)), A(n_out, "grad"), A(n_in),
+                           A(n_out * (n_in + 1), "small"), A(n_out * (n_in + 1), "pos", 1e-5), n_in,
+                           3e-4, 0.9, 0.999],
+                          (n_out, n_in + 1)))
+        cases.append(Case(f"UpdateWeightsMomentum/{n_in}x{n_out}", "UpdateWeightsMomentum",
+                          [A(n_out * (n_in + 1), "uniform", 1 / np.sqrt(n_in)), A(n_out, "grad"), A(n_in),
+                           A(n_out * (n_in + 1), "small"), n_in, 3e-4, 0.9],
+                          (n_out, n_in + 1)))
+        cases.append(Case(f"NormalizeWeights/{n_in}x{n_out}", "NormalizeWeights",
+                          [A(n_out * (n_in + 1), "uniform", 0.5), n_in + 1], (n_out,)))
+    for act in ACTS:
+        cases.append(Case(f"CalcOutputGradient/act{act}", "CalcOutputGradient",
+                          [A(67, "unit"), A(67, f"act:{act}"), A(67, "zeros"), act, 0.5], (67,)))
+        cases.append(Case(f"Activation/act{act}", "Activation", [A(131, "normal", 3.0), A(131, "zeros"), act],
+                          (131,)))
+        cases.append(Case(f"DeActivation/act{act}", "DeActivation",
+                          [A(131, f"act:{act}"), A(131, "zeros"), A(131, "grad", 50.0), act], (131,)))
+    return cases
+
+
+def _conv_cases():
+    cases = []
+    # (inputs per variable, step, window_in, window_out, variables, activation)
+    shapes = [(64 * 5, 64, 64, 24, 1, NONE),      # MLMH 1x1 "conv": per-unit dense
+              (24 * 5, 24, 24, 64, 1, GELU),      # MLMH W0 / FF shape
+              (512, 8, 16, 12, 3, NONE),          # PatchTST patching conv, stride < window
+              (47, 5, 7, 6, 2, TANH),             # overlapping windows, two variables.  Shapes keep
+                                                  # (inputs-window) % step == 0: otherwise the reference's
+                                                  # Adam gradient loop reads one window past the buffer
+              (33, 3, 3, 5, 1, LRELU)]
+    for inputs, step, win, wout, var, act in shapes:
+        units = (inputs - win) // step + 1
+        nw = var * wout * (win + 1)
+        cases.append(Case(f"FeedForwardConv/{inputs}-{step}-{win}-{wout}-{var}", "FeedForwardConv",
+                          [A(nw, "uniform", 1 / np.sqrt(win + 1)), A(inputs * var), A(units * wout * var, "zeros"),
+                           inputs, step, win, wout, act],
+                          (units, wout, var)))
+        outputs = units * wout
+        cases.append(Case(f"CalcHiddenGradientConv/{inputs}-{step}-{win}-{wout}-{var}", "CalcHiddenGradientConv",
+                          [A(nw, "uniform", 1 / np.sqrt(win + 1)), A(outputs * var, "grad"),
+                           A(inputs * var, f"act:{act}"), A(inputs * var, "zeros"), outputs, step, win, wout, act, 0],
+                          (inputs, var)))
+        cases.append(Case(f"UpdateWeightsConvAdam/{inputs}-{step}-{win}-{wout}-{var}", "UpdateWeightsConvAdam",
+                          [A(nw, "uniform", 1 / np.sqrt(win + 1)), A(outputs * var, "grad"), A(inputs * var),
+                           A(nw, "small"), A(nw, "pos", 1e-5), inputs, 3e-4, 0.9, 0.999, win, wout, step],
+                          (nw,)))
+        cases.append(Case(f"UpdateWeightsConvMomentum/{inputs}-{step}-{win}-{wout}-{var}",
+                          "UpdateWeightsConvMomentum",
+                          [A(nw, "uniform", 1 / np.sqrt(win + 1)), A(outputs * var, "grad"), A(inputs * var),
+                           A(nw, "small"), inputs, 3e-4, 0.9, win, wout, step],
+                          (nw,)))
+    return cases
+
+
+def _attention_cases():
+    cases = []
+    for units, heads, dim in [(5, 2, 4), (12, 3, 8), (17, 2, 5), (33, 4, 16), (1, 1, 3)]:
+        n = units * 3 * heads * dim
+        for mask in (0, 1):
+            cases.append(Case(f"MHAttentionScore/{units}-{heads}-{dim}/m{mask}", "MHAttentionScore",
+                              [A(n), A(units * heads * units, "zeros"), dim, mask], (units, heads)))
+        cases.append(Case(f"MHAttentionOut/{units}-{heads}-{dim}", "MHAttentionOut",
+                          [A(units * heads * units, "unit"), A(n), A(units * heads * dim, "zeros"), dim],
+                          (units, heads)))
+        cases.append(Case(f"MHAttentionInsideGradients/{units}-{heads}-{dim}", "MHAttentionInsideGradients",
+                          [A(n), A(n, "zeros"), A(units * heads * units, "unit"), A(units * heads * dim, "grad")],
+                          (units, heads, dim), meta={"softmax_scores": 1}))
+    return cases
+
+
+def _norm_cases():
+    cases = []
+    for rows, dim in [(1, 5), (3, 64), (7, 65), (4, 1), (10, 2), (5, 128)]:
+        for scale in (0.5, 3.0):
+            cases.append(Case(f"Normalize/{rows}x{dim}/s{scale}", "Normalize", [A(rows * dim, "normal", scale), dim],
+                              (rows,)))
+        cases.append(Case(f"SumMatrix/{rows}x{dim}", "SumMatrix",
+                          [A(rows * dim), A(rows * dim), A(rows * dim, "zeros"), dim, 0.5, 0, 0, 0,
+                           A(rows * dim, "zeros"), 1],
+                          (rows,)))
+    for heads, size in [(1, 3), (2, 64), (3, 65), (4, 100), (1, 1)]:
+        cases.append(Case(f"SoftMax_FeedForward/{heads}x{size}", "SoftMax_FeedForward",
+                          [A(heads * size, "normal", 2.0), A(heads * size, "zeros")], (size, heads), (size, 1)))
+        cases.append(Case(f"SoftMax_HiddenGradient/{heads}x{size}", "SoftMax_HiddenGradient",
+                          [A(heads * size, "unit"), A(heads * size, "grad"), A(heads * size, "zeros")],
+                          (size, heads), (size, 1)))
+        cases.append(Case(f"SoftMax_OutputGradient/{heads}x{size}", "SoftMax_OutputGradient",
+                          [A(heads * size, "unit"), A(heads * size, "unit"), A(heads * size, "zeros")],
+                          (heads * size,)))
+    cases.append(Case("SoftUpdate/1000", "SoftUpdate", [A(1000), A(1000), 0.005], (1000,)))
+    cases.append(Case("SoftUpdateAdam/1000", "SoftUpdateAdam",
+                      [A(1000), A(1000), A(1000, "small"), A(1000, "pos", 1e-4), 0.005, 0.9, 0.999], (1000,)))
+    cases.append(Case("Transpose/7x13", "Transpose", [A(91), A(91, "zeros")], (7, 13)))
+    cases.append(Case("ConcatenateBuffers/5", "ConcatenateBuffers",
+                      [A(15), 3, A(20), 4, A(5), 1, A(10), 2, A(50, "zeros")], (5, 2)))
+    cases.append(Case("DeconcatenateBuffers/5", "DeconcatenateBuffers",
+                      [A(15, "zeros"), 3, A(20, "zeros"), 4, A(5, "zeros"), 1, A(10, "zeros"), 2, A(50)], (5, 2)))
+    for opt, width in ((0, 7), (1, 9)):
+        cases.append(Case(f"RevInFeedForward/opt{opt}", "RevInFeedForward",
+                          [A(96), A(12 * width, "pos"), A(96, "zeros"), 12 * width, opt], (96,)))
+        cases.append(Case(f"RevInHiddenGraddient/opt{opt}", "RevInHiddenGraddient",
+                          [A(96, "act:-1"), A(96, "zeros"), A(12 * width, "pos", 3.0), A(96, "grad"), 12 * width, opt,
+                           NONE], (96,)))
+    return cases
+
+
+def all_cases() -> list[Case]:
+    return _dense_cases() + _conv_cases() + _attention_cases() + _norm_cases()
+
+
+def prepare_inputs(case: Case, seed: int) -> list:
+    """Inputs of a case, with attention scores made row-stochastic where the case asks for it."""
+    args = materialise(case, seed)
+    if case.meta.get("softmax_scores"):
+        units, heads = case.gsize[0], case.gsize[1]
+        for i, a in enumerate(case.args):
+            if isinstance(a, A) and a.size == units * heads * units and a.init == "unit":
+                s = args[i].reshape(units * heads, units)
+                args[i] = np.ascontiguousarray((s / s.sum(axis=1, keepdims=True)).reshape(-1), dtype=np.float32)
+    return args

@@ -1,0 +1,100 @@
+"""Parity metric shared by the tests.
+
+The contract is 1e-4 relative per layer output, gradient and post-update
+weight.  Relative is taken against the magnitude of the reference tensor
+(max |ref|): summation order differs between the reference's serial /
+tree reductions, numpy and the CUDA kernels, so an element-wise relative
+test would flag harmless rounding on near-zero entries.  For tensors a
+kernel updates in place (weights, moments) the *change* is compared as
+well, relative to the largest reference change, so that a wrong update is
+not hidden by the size of the weights themselves.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+RTOL = 1e-4          # per tensor, relative to max |reference|
+DELTA_RTOL = 1e-3    # per in-place-updated tensor, relative to max |reference change|
+
+
+def rel_err(got: np.ndarray, ref: np.ndarray) -> float:
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    if got.shape != ref.shape:
+        raise AssertionError(f"shape {got.shape} != {ref.shape}")
+    bad = np.isfinite(got) != np.isfinite(ref)
+    if bad.any():
+        return float("inf")
+    fin = np.isfinite(ref)
+    if not fin.any():
+        return 0.0
+    den = max(np.abs(ref[fin]).max(), 1e-30)
+    return float(np.abs(got[fin] - ref[fin]).max() / den)
+
+
+def check_close(label: str, got, ref, before=None, rtol: float = RTOL, delta_rtol: float = DELTA_RTOL,
+                atol: float = 0.0) -> None:
+    e = rel_err(got, ref)
+    if atol > 0 and e > rtol:
+        diff = np.abs(np.asarray(got, np.float64) - np.asarray(ref, np.float64))
+        den = max(np.abs(np.asarray(ref, np.float64)).max(), 1e-30)
+        if np.all(np.isfinite(diff)) and diff.max() <= rtol * den + atol:
+            e = 0.0
+    if e > rtol:
+        idx = int(np.argmax(np.abs(np.asarray(got, np.float64) - np.asarray(ref, np.float64))))
+        raise AssertionError(f"{label}: rel err {e:.3e} > {rtol:g} (worst at {idx}: got {np.ravel(got)[idx]!r}, "
+                             f"ref {np.ravel(ref)[idx]!r})")
+    if before is not None:
+        dref = np.asarray(ref, np.float64) - np.asarray(before, np.float64)
+        if np.abs(dref).max() > 0:
+            dgot = np.asarray(got, np.float64) - np.asarray(before, np.float64)
+            de = rel_err(dgot, dref)
+            if de > delta_rtol:
+                raise AssertionError(f"{label}: change rel err {de:.3e} > {delta_rtol:g}")
+
+
+# Adam in the reference has no effective epsilon (UpdateWeightsAdam divides by sqrt(v)+1e-37,
+# UpdateWeightsConvAdam by sqrt(v)), so on early steps every weight moves by about +-3.16*lr
+# whatever the size of its gradient, and its direction is the sign of the gradient.  Where a
+# weight's batch-mean gradient G has cancelled to a small fraction of the sum of the absolute
+# values of its terms (sum|g*x|), its sign is not reproducible between two correct fp32
+# implementations: the upstream gradients carry rounding of their own, and in the attention
+# layer the reference's score-gradient formula (NeuroNet.cl:1812-1843) cancels almost completely
+# against the softmax Jacobian, leaving Q/K gradients that are accurate to ~1% of their terms.
+# A post-update weight may therefore disagree only where |G| < 1e-2 * sum|g*x|, and such weights
+# may be at most 1% of a tensor; every other weight must match within the 1e-4 tolerance.
+CANCELLED = 1e-2
+MAX_DISAGREE = 0.01
+
+
+def check_weights(label: str, got, ref, grad, grad_abs, before=None) -> None:
+    n = np.size(grad)  # weights the update touches (a buffer may be longer, e.g. the attention W0)
+    ref = np.asarray(ref, np.float64)[:n]
+    got = np.asarray(got, np.float64)[:n]
+    ratio = np.abs(np.asarray(grad, np.float64)) / np.maximum(np.asarray(grad_abs, np.float64), 1e-300)
+    cancelled = ratio < CANCELLED
+    den = max(np.abs(ref).max(), 1e-30)
+    bad = ~(np.abs(got - ref) <= RTOL * den)
+    unexplained = bad & ~cancelled
+    if unexplained.any():
+        i = int(np.argmax(np.where(unexplained, np.abs(got - ref), -1)))
+        raise AssertionError(f"{label}: {int(unexplained.sum())} weights differ beyond {RTOL:g} (worst at {i}: "
+                             f"got {got[i]!r}, ref {ref[i]!r}, |G|/sum|terms| {ratio[i]:.2e})")
+    if bad.sum() > MAX_DISAGREE * n:
+        raise AssertionError(f"{label}: {int(bad.sum())} of {n} weights took a different update direction")
+    keep = ~bad
+    if before is not None:
+        check_close(label, got[keep], ref[keep], np.asarray(before, np.float64)[:n][keep])
+
+
+# The reference's TANH and SIGMOID derivatives (NeuroNet.cl:139-147) compute
+# clamp(g + y, lo, hi) - y: the gradient is rounded to a multiple of ulp(y), the
+# spacing of floats at the activation output.  Two correct evaluations of g that
+# differ by rounding can land one such step apart, so gradients that pass through
+# these derivatives are compared with an absolute floor of two ulps of the
+# layer's largest activation output.
+def deactivation_atol(activation: int, outputs) -> float:
+    if activation not in (0, 1):  # TANH, SIGMOID
+        return 0.0
+    y = float(np.abs(np.asarray(outputs, np.float32)).max()) if np.size(outputs) else 0.0
+    return 2.0 * float(np.spacing(np.float32(max(y, 1e-30))))
