@@ -159,9 +159,8 @@ def run_ours(args, rank, world, local_rank):
     B = args.batch
     net = C.build_mlmh(ctx, spec, B, C.mlmh_weights(spec), dp=world > 1)
     if world > 1:
-        uid = [ctx.dp_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0)
-        ctx.dp_init(rank, world, uid[0])
+        from nn_in_trading_b200 import dp
+        dp.join_dp(ctx, rank, world)
 
     n_in = spec.window * spec.units
     pool = 4

@@ -7,10 +7,13 @@
 // qkv layout is the reference's [unit][3][head][dimension]
 // (NeuroNet.cl:1674, 1693, 1754); scores are [query][head][key].
 #include "../../include/nn_b200.h"
+#include "attn_smem.cuh"
 #include "nn_device.cuh"
 #include "nn_internal.h"
 
 namespace nn {
+
+constexpr size_t kSmemCap = 200 * 1024;  // dynamic shared memory one CTA may use
 
 // ------------------------------------------------------- MHAttentionScore
 // NeuroNet.cl:1662-1719: S[q,h,k] = exp(clamp(q.k / sqrt(d), +-100)) (NaN -> 0),
@@ -79,6 +82,18 @@ static int k_mh_attention_score(Launch &L) {
   if (!qkv || !score) return NN_ERR_BOUNDS;
   float koef = sqrtf((float)dim);
   if (koef < 1.f) koef = 1.f;
+  {
+    size_t sm = (size_t)(units * pad4(dim) + dim * pad4(units)) * sizeof(float);
+    int kpl = (units + 31) / 32;
+    if (sm <= kSmemCap && kpl <= 4) {
+      auto fn = kpl <= 1 ? mh_score_smem_kernel<1> : kpl == 2 ? mh_score_smem_kernel<2>
+              : kpl == 3 ? mh_score_smem_kernel<3> : mh_score_smem_kernel<4>;
+      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+      fn<<<dim3(heads, L.B), 256, sm, L.stream>>>(qkv, score, units, heads, dim, mask, koef);
+      NN_CHECK_LAUNCH(L);
+      return NN_OK;
+    }
+  }
   const int warps = 8;
   size_t smem = (size_t)(kScoreKT * (dim + 1) + warps * dim) * sizeof(float);
   if (smem > 200 * 1024) return L.fail(NN_ERR_UNSUPPORTED, "MHAttentionScore: key dimension too large");
@@ -146,6 +161,17 @@ static int k_mh_attention_out(Launch &L) {
   float *qkv = L.buf(1, (size_t)L.B * units * 3 * heads * dim);
   float *out = L.buf(2, (size_t)L.B * units * heads * dim);
   if (!scores || !qkv || !out) return NN_ERR_BOUNDS;
+  {
+    size_t sm = (size_t)(units * pad4(units) + units * dim) * sizeof(float);
+    int dpl = (dim + 31) / 32;
+    if (sm <= kSmemCap && dpl <= 2) {
+      auto fn = dpl <= 1 ? mh_out_smem_kernel<1> : mh_out_smem_kernel<2>;
+      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+      fn<<<dim3(heads, L.B), 256, sm, L.stream>>>(scores, qkv, out, units, heads, dim);
+      NN_CHECK_LAUNCH(L);
+      return NN_OK;
+    }
+  }
   const int warps = 8;
   size_t smem = (size_t)(kOutVT * dim + warps * kOutVT) * sizeof(float);
   if (smem > 48 * 1024) cudaFuncSetAttribute(mh_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -228,6 +254,17 @@ static int k_mh_attention_inside_gradients(Launch &L) {
   if (!qkv || !qkv_g || !scores || !grad) return NN_ERR_BOUNDS;
   float koef = sqrtf((float)dim);
   if (koef < 1.f) koef = 1.f;
+  {
+    size_t sm = (size_t)(units * pad4(units) + 3 * units * dim + 2 * pad4(units)) * sizeof(float);
+    int dpl = (dim + 31) / 32;
+    if (sm <= kSmemCap && dpl <= 2) {
+      auto fn = dpl <= 1 ? mh_grad_smem_kernel<1> : mh_grad_smem_kernel<2>;
+      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+      fn<<<dim3(heads, L.B), 256, sm, L.stream>>>(qkv, qkv_g, scores, grad, units, heads, dim, koef);
+      NN_CHECK_LAUNCH(L);
+      return NN_OK;
+    }
+  }
   size_t rows = (size_t)L.B * units * heads;
   float *A = L.scratch(2, rows);
   if (!A) return NN_ERR_CUDA;

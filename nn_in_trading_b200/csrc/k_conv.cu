@@ -7,6 +7,7 @@
 // with the bias last.  With a batch, every per-sample buffer holds `batch`
 // consecutive copies of that layout and the weights are shared.
 #include "../../include/nn_b200.h"
+#include "gemm_fast.cuh"
 #include "gemm_simt.cuh"
 #include "nn_device.cuh"
 #include "nn_internal.h"
@@ -44,6 +45,16 @@ struct ConvEpi {
   }
 };
 
+// Plain-layout epilogue: one variable, windows tiling the input (row m at o + m*wout).
+struct ConvEpiPlain {
+  const float *w;
+  float *o;
+  int win, wout, act;
+  __device__ __forceinline__ void operator()(int m, int n, int, int, float acc) const {
+    o[(size_t)m * wout + n] = activate(acc + nan0(w[(size_t)n * (win + 1) + win]), act);
+  }
+};
+
 static int k_feedforward_conv(Launch &L) {
   const int units = (int)L.nd.g[0];
   const int wout_g = L.nd.dims > 1 ? (int)L.nd.g[1] : 1;
@@ -54,9 +65,16 @@ static int k_feedforward_conv(Launch &L) {
   float *x = L.buf(1, (size_t)L.B * var * inputs);
   float *o = L.buf(2, (size_t)L.B * var * units * wout);
   if (!w || !x || !o) return NN_ERR_BOUNDS;
-  GemmShape sh{L.B * units, wout_g, win, var, 1};
-  cudaError_t e = gemm_simt<true, false>(sh, ConvLoadX{x, units, step, inputs, var}, ConvLoadW{w, win, wout},
-                                         ConvEpi{w, o, units, win, wout, var, act}, L.stream);
+  cudaError_t e;
+  if (var == 1 && step == win && inputs == units * step && win > 0) {
+    // windows tile the input: a plain [B*units][win] x W^T GEMM
+    FastShape fs{L.B * units, wout_g, win, 1, 1, 0, x, win, 0, w, win + 1, 0};
+    e = sgemm_fast<false, false>(fs, ConvEpiPlain{w, o, win, wout, act}, L.stream);
+  } else {
+    GemmShape sh{L.B * units, wout_g, win, var, 1};
+    e = gemm_simt<true, false>(sh, ConvLoadX{x, units, step, inputs, var}, ConvLoadW{w, win, wout},
+                               ConvEpi{w, o, units, win, wout, var, act}, L.stream);
+  }
   if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
   L.counted();
   return NN_OK;
@@ -130,9 +148,15 @@ static int k_calc_hidden_gradient_conv(Launch &L) {
   if (!w || !g || !o || !ig) return NN_ERR_BOUNDS;
   const int n_win = outputs / wout;
   if (step == win && shift_out == 0 && outputs == n_win * wout && inputs == n_win * win && win > 0) {
-    GemmShape sh{L.B * n_win, win, wout, var, 1};
-    cudaError_t e = gemm_simt<true, true>(sh, CDLoadG{g, n_win, wout, outputs, var}, CDLoadW{w, win, wout},
-                                          CDEpi{o, ig, n_win, win, inputs, var, act}, L.stream);
+    cudaError_t e;
+    if (var == 1) {
+      FastShape fs{L.B * n_win, win, wout, 1, 1, 0, g, wout, 0, w, win + 1, 0};
+      e = sgemm_fast<false, true>(fs, CDEpi{o, ig, n_win, win, inputs, var, act}, L.stream);
+    } else {
+      GemmShape sh{L.B * n_win, win, wout, var, 1};
+      e = gemm_simt<true, true>(sh, CDLoadG{g, n_win, wout, outputs, var}, CDLoadW{w, win, wout},
+                                CDEpi{o, ig, n_win, win, inputs, var, act}, L.stream);
+    }
     if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
     L.counted();
     return NN_OK;
@@ -244,6 +268,11 @@ static int k_update_weights_conv_adam(Launch &L) {
     if (!z) return NN_ERR_CUDA;
     cudaMemsetAsync(z, 0, (size_t)s.nw * sizeof(float), L.stream);
     src = GradSrc{z, 1, 0, 1.f};
+  } else if (s.var == 1 && s.step == s.win && s.inputs == s.total * s.win && s.win > 0) {
+    // windows tile the input: G = g^T [rows][wout] x X [rows][win], bias = column sums of g
+    rc = wgrad_fast(L, g, s.wout, x, s.win, s.wout, s.win, L.B * s.total, &src);
+    if (rc) return rc;
+    src.scale = 1.f / (float)L.B;
   } else {
     rc = wgrad_partials<false, true>(L, s.wout, s.win + 1, L.B * s.total, s.var,
                                      CWLoadG{g, s.total, s.wout, s.gstride},

@@ -6,6 +6,7 @@
 // Weight layout is the reference's: W[out][in+1] row-major with the bias in
 // the last column, stored on the *source* layer (NeuroNet_Core.mqh:15568).
 #include "../../include/nn_b200.h"
+#include "gemm_fast.cuh"
 #include "gemm_simt.cuh"
 #include "nn_device.cuh"
 #include "nn_internal.h"
@@ -16,6 +17,16 @@ namespace nn {
 __global__ void reduce_partials_kernel(float *out, GradSrc src, size_t n) {
   size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (i < n) out[i] = src(i);
+}
+
+__global__ void colsum_partial_kernel(float *p, const float *g, int M, int rows, long long ld, int kchunk, int ldp,
+                                      int col) {
+  int m = blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= M) return;
+  int r0 = blockIdx.y * kchunk, r1 = min(rows, r0 + kchunk);
+  float s = 0.f;
+  for (int r = r0; r < r1; ++r) s += nan0(g[(size_t)r * ld + m]);
+  p[((size_t)blockIdx.y * M + m) * ldp + col] = s;
 }
 
 // ------------------------------------------------------------ FeedForward
@@ -101,9 +112,8 @@ static int k_feedforward(Launch &L) {
     ff_rows_kernel<4><<<blocks, 256, 0, L.stream>>>(w, x, y, inputs, outputs, L.B, act);
     NN_CHECK_LAUNCH(L);
   } else {
-    GemmShape sh{L.B, outputs, inputs, 1, 1};
-    cudaError_t e = gemm_simt<true, false>(sh, FFLoadX{x, inputs}, FFLoadW{w, ld},
-                                           FFEpi{w, y, ld, inputs, outputs, act}, L.stream);
+    FastShape fs{L.B, outputs, inputs, 1, 1, 0, x, inputs, 0, w, ld, 0};
+    cudaError_t e = sgemm_fast<false, false>(fs, FFEpi{w, y, ld, inputs, outputs, act}, L.stream);
     if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
     L.counted();
   }
@@ -199,9 +209,8 @@ static int k_calc_hidden_gradient(Launch &L) {
     NN_CHECK_LAUNCH(L);
     return NN_OK;
   }
-  GemmShape sh{L.B, inputs, outputs, 1, 1};
-  cudaError_t e = gemm_simt<true, true>(sh, CHGLoadG{g, outputs}, CHGLoadW{w, ld}, CHGEpi{o, ig, inputs, act},
-                                        L.stream);
+  FastShape fs{L.B, inputs, outputs, 1, 1, 0, g, outputs, 0, w, ld, 0};
+  cudaError_t e = sgemm_fast<false, true>(fs, CHGEpi{o, ig, inputs, act}, L.stream);
   if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
   L.counted();
   return NN_OK;
@@ -303,8 +312,10 @@ static int k_update_weights_adam(Launch &L) {
     return NN_OK;
   }
   GradSrc src;
-  int rc = wgrad_partials<false, true>(L, s.n_out, s.n_col, L.B, 1, WGLoadG{g, s.n_out, 0}, WGLoadX{x, s.inputs},
-                                       &src);
+  int rc = s.n_col == s.inputs + 1
+               ? wgrad_fast(L, g, s.n_out, x, s.inputs, s.n_out, s.inputs, L.B, &src)
+               : wgrad_partials<false, true>(L, s.n_out, s.n_col, L.B, 1, WGLoadG{g, s.n_out, 0},
+                                             WGLoadX{x, s.inputs}, &src);
   if (rc) return rc;
   src.scale = 1.f / (float)L.B;
   return finish_update(L, src, (size_t)s.n_out * s.n_col, adam_dense_apply, adam_dense_apply_src);

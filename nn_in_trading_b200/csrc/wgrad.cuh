@@ -6,6 +6,7 @@
 // region the summed, scaled gradient is written to the gradient arena
 // instead, averaged over ranks, and applied afterwards.
 #pragma once
+#include "gemm_fast.cuh"
 #include "gemm_simt.cuh"
 #include "nn_device.cuh"
 #include "nn_internal.h"
@@ -34,6 +35,47 @@ struct GradSrc {
 };
 
 __global__ void reduce_partials_kernel(float *out, GradSrc src, size_t n);
+
+// Partial store for the fast GEMM: N computed columns inside rows of `ldp` (the bias
+// column N of each row is filled by colsum_partial_kernel).
+struct PartialStoreLd {
+  float *p;
+  int M, ldp, nz;
+  __device__ void operator()(int m, int n, int z, int split, float acc) const {
+    p[(((size_t)split * nz + z) * M + m) * ldp + n] = acc;
+  }
+};
+
+// Bias column of a weight gradient: per split, sum over the split's reduction
+// rows r of nan0(g[r*ld + m]) into p[(split*M + m)*ldp + col].
+__global__ void colsum_partial_kernel(float *p, const float *g, int M, int rows, long long ld, int kchunk, int ldp,
+                                      int col);
+
+// Weight gradient of a plain GEMM: G[m][n] = sum_r A[r*lda + m] * X[r*ldx + n] for n < N, and
+// G[m][N] = sum_r A[r*lda + m] (the bias column, input 1).  Partials per split into scratch 0.
+inline int wgrad_fast(Launch &L, const float *A, long long lda, const float *X, long long ldx, int M, int N, int rows,
+                      GradSrc *out) {
+  int splits = fast_splits(M, N + 1, rows, 1);
+  int kchunk = ((rows + splits - 1) / splits + 7) / 8 * 8;
+  splits = (rows + kchunk - 1) / kchunk;
+  if (splits < 1) splits = 1;
+  const int ldp = N + 1;
+  size_t per = (size_t)M * ldp;
+  float *part = L.scratch(0, per * splits);
+  if (!part) return NN_ERR_CUDA;
+  FastShape fs{M, N, rows, 1, splits, kchunk, A, lda, 0, X, ldx, 0};
+  cudaError_t e = sgemm_fast<true, true>(fs, PartialStoreLd{part, M, ldp, 1}, L.stream);
+  if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
+  L.counted();
+  dim3 grid((M + 255) / 256, splits);
+  colsum_partial_kernel<<<grid, 256, 0, L.stream>>>(part, A, M, rows, lda, kchunk, ldp, N);
+  NN_CHECK_LAUNCH(L);
+  out->p = part;
+  out->splits = splits;
+  out->stride = per;
+  out->scale = 1.f;
+  return NN_OK;
+}
 
 // Runs the split-K GEMM into scratch slot 0 and returns the gradient source
 // (not yet scaled).  M x N per z problem, K reduction length.

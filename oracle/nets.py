@@ -44,6 +44,12 @@ class RefBackend:
 
 
 BACKEND = K  # numpy restatement by default
+GRAD_HOOK = None  # optional callable G -> G applied to every batch-mean weight gradient (data-parallel mean)
+
+
+def set_grad_hook(fn) -> None:
+    global GRAD_HOOK
+    GRAD_HOOK = fn
 
 
 def use_backend(kind: str) -> None:
@@ -111,7 +117,9 @@ class ODense(OLayer):
         # sum of |terms| of each weight's gradient: the scale of its rounding error
         self.last_grad_abs = np.mean([np.abs(K.nan0(self.gradient[b]))[:, None] * np.abs(inps[b])[None, :]
                                       for b in range(self.batch)], axis=0).reshape(-1)
-        if self.batch == 1:
+        if GRAD_HOOK is not None:
+            self.last_grad = GRAD_HOOK(self.last_grad)
+        elif self.batch == 1:
             BACKEND.UpdateWeightsAdam(prev.weights, self.gradient[0], prev.output[0], prev.m, prev.v, inputs,
                                       self.next_lt(), B1, B2, gsize=(n_out, n_col))
             BACKEND.NormalizeWeights(prev.weights, prev.neurons + 1, gsize=(self.neurons,))
@@ -208,11 +216,13 @@ class OMLMH(OLayer):
         n = (window + 1) * window_out
         G = np.mean([K.conv_weight_grad(grad[b], inputs[b], in_total, window, window_out, window, n)
                      for b in range(self.batch)], axis=0, dtype=np.float64).astype(F32)
+        if GRAD_HOOK is not None:
+            G = GRAD_HOOK(G)
         self.last_grads[key] = G
         self.last_grads_abs[key] = np.mean(
             [K.conv_weight_grad(np.abs(grad[b]), np.abs(inputs[b]), in_total, window, window_out, window, n)
              for b in range(self.batch)], axis=0, dtype=np.float64)
-        if self.batch == 1:
+        if self.batch == 1 and GRAD_HOOK is None:
             BACKEND.UpdateWeightsConvAdam(w, grad[0], inputs[0], m, v, in_total, self.next_lt(), B1, B2, window,
                                           window_out, window, gsize=(n,))
             BACKEND.NormalizeWeights(w, window + 1, gsize=(window_out,))
