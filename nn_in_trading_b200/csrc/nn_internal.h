@@ -55,6 +55,15 @@ struct Launch {
   int fail(int status, const std::string &msg);
   // Per-context scratch of at least `floats` floats (slot 0..3 independent).
   float *scratch(int slot, size_t floats);
+  // Persistent side buffer attached to a buffer handle (created or grown on
+  // demand, lives until the handle is freed); `fresh` tells whether it was (re)made.
+  float *side(int key_handle, size_t floats, bool *fresh = nullptr);
+  // Existing side buffer of a handle, or nullptr; `floats` receives its size.
+  float *side_existing(int key_handle, size_t *floats);
+  // Size in floats of the buffer bound to argument idx (0 if none).
+  size_t floats(int idx) const;
+  // Buffer handle bound to argument idx.
+  int handle(int idx) const { return k->args[idx].i; }
   // Data-parallel deferred-update hooks (see nn_dp_update_begin).
   bool deferred() const;
   // Arena slot for a weight gradient of n floats, or nullptr when not deferring.
@@ -83,6 +92,11 @@ extern const KernelDef kAttnKernels[];
 extern const int kNumAttnKernels;
 extern const KernelDef kMiscKernels[];
 extern const int kNumMiscKernels;
+extern const KernelDef kLstmKernels[];
+extern const int kNumLstmKernels;
+
+// Number of data-parallel ranks (1 without a communicator).
+int dp_world();
 
 const KernelDef *find_kernel(const char *name);
 

@@ -74,6 +74,7 @@ struct Context {
   std::vector<Recorded> rec;
   float *scratch[4] = {nullptr, nullptr, nullptr, nullptr};
   size_t scratch_n[4] = {0, 0, 0, 0};
+  std::unordered_map<int, std::pair<float *, size_t>> sides;  // side buffers keyed by buffer handle
   long long launches = 0;
   // data parallel
   Nccl nccl;
@@ -127,6 +128,12 @@ float *Launch::buf_opt(int idx) {
 
 int Launch::fail(int status, const std::string &msg) { return set_err(status, msg); }
 
+size_t Launch::floats(int idx) const {
+  const Arg &a = k->args[idx];
+  if (a.type != ARG_BUF || a.i < 0 || a.i >= (int)ctx->bufs.size() || !ctx->bufs[a.i].live) return 0;
+  return ctx->bufs[a.i].bytes / sizeof(float);
+}
+
 float *Launch::scratch(int slot, size_t floats) {
   if (ctx->scratch_n[slot] < floats) {
     if (ctx->scratch[slot]) {
@@ -143,6 +150,35 @@ float *Launch::scratch(int slot, size_t floats) {
     ctx->scratch_n[slot] = n;
   }
   return ctx->scratch[slot];
+}
+
+float *Launch::side(int key, size_t floats, bool *fresh) {
+  auto it = ctx->sides.find(key);
+  if (it != ctx->sides.end() && it->second.second >= floats) {
+    if (fresh) *fresh = false;
+    return it->second.first;
+  }
+  if (it != ctx->sides.end()) {
+    cudaStreamSynchronize(ctx->stream);
+    cudaFree(it->second.first);
+    ctx->sides.erase(it);
+  }
+  float *p = nullptr;
+  if (cudaMalloc(&p, floats * sizeof(float)) != cudaSuccess) {
+    fail(NN_ERR_CUDA, "side buffer allocation failed");
+    return nullptr;
+  }
+  cudaMemsetAsync(p, 0, floats * sizeof(float), ctx->stream);
+  ctx->sides[key] = {p, floats};
+  if (fresh) *fresh = true;
+  return p;
+}
+
+float *Launch::side_existing(int key, size_t *floats) {
+  auto it = ctx->sides.find(key);
+  if (it == ctx->sides.end()) return nullptr;
+  if (floats) *floats = it->second.second;
+  return it->second.first;
 }
 
 bool Launch::deferred() const { return ctx->deferring; }
@@ -172,12 +208,15 @@ void Launch::counted(int n) { ctx->launches += n; }
 const KernelDef *find_kernel(const char *name) {
   struct Table { const KernelDef *t; int n; };
   const Table tables[] = {{kDenseKernels, kNumDenseKernels}, {kConvKernels, kNumConvKernels},
-                          {kAttnKernels, kNumAttnKernels}, {kMiscKernels, kNumMiscKernels}};
+                          {kAttnKernels, kNumAttnKernels}, {kMiscKernels, kNumMiscKernels},
+                          {kLstmKernels, kNumLstmKernels}};
   for (const Table &t : tables)
     for (int i = 0; i < t.n; ++i)
       if (std::strcmp(t.t[i].name, name) == 0) return &t.t[i];
   return nullptr;
 }
+
+int dp_world() { return g_ctx ? g_ctx->world : 1; }
 
 static int run_one(Context *c, const KernelInst &k, const NDR &nd) {
   Launch L;
@@ -241,6 +280,7 @@ int nn_shutdown(void) {
     if (b.live) cudaFree(b.ptr);
   for (int i = 0; i < 4; ++i)
     if (c->scratch[i]) cudaFree(c->scratch[i]);
+  for (auto &kv : c->sides) cudaFree(kv.second.first);
   if (c->arena) cudaFree(c->arena);
   if (c->comm && c->nccl.comm_destroy) c->nccl.comm_destroy(c->comm);
   cudaStreamDestroy(c->stream);
@@ -315,6 +355,11 @@ int nn_buffer_free(int h) {
   CUDA_TRY(cudaFree(b->ptr));
   *b = Buffer();
   g_ctx->free_bufs.push_back(h);
+  auto it = g_ctx->sides.find(h);
+  if (it != g_ctx->sides.end()) {
+    cudaFree(it->second.first);
+    g_ctx->sides.erase(it);
+  }
   return NN_OK;
 }
 

@@ -121,6 +121,12 @@ def parse_params(params: str) -> list[tuple[str, str]]:
     return out
 
 
+# Kernels whose work-groups write the same elements (LSTM_HiddenGradient writes
+# column 0 of rows >= 1 from its weight loop and, in another work-group, from
+# its bias loop): executed with work-groups in order on one thread, so that the
+# later loop's value is the one kept.
+SERIAL_KERNELS = {"LSTM_HiddenGradient"}
+
 # Data races in the reference source that a GPU hides (the work-group of these
 # helpers is a single SIMD wavefront, so every lane's load happens before any
 # lane's store) but a sequential work-item executor exposes.  Each patch adds
@@ -167,11 +173,12 @@ def generate(cl_text: str) -> str:
             else:
                 args.append(f"*(const int *)a[{idx}]")
         parts.append(f"static void call_{name}(void **a) {{ ocl::{name}({', '.join(args)}); }}")
-    parts.append("struct RefKernel { const char *name; void (*call)(void **); int uses_barrier; int nargs; const char *argtypes; };")
+    parts.append("struct RefKernel { const char *name; void (*call)(void **); int uses_barrier; int nargs; "
+                 "const char *argtypes; int serial; };")
     rows = []
     for name, plist, ub in table:
         types = "".join(k for k, _, _ in plist)
-        rows.append(f'  {{"{name}", call_{name}, {ub}, {len(plist)}, "{types}"}},')
+        rows.append(f'  {{"{name}", call_{name}, {ub}, {len(plist)}, "{types}", {int(name in SERIAL_KERNELS)}}},')
     parts.append('extern "C" const RefKernel nnref_table[] = {\n' + "\n".join(rows) + "\n};")
     parts.append(f'extern "C" const int nnref_table_size = {len(table)};')
     return "\n".join(parts) + "\n"

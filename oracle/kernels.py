@@ -525,6 +525,224 @@ def RevInHiddenGraddient(inputs, inputs_gr, options, output_gr, options_size, op
         inputs_gr[:n] = deactivation(res, inputs[:n], activation)
 
 
+# ---------------------------------------------------------------- batch norm
+def BatchFeedForward(inputs, options, output, batch, optimization, activation, training, gsize, lsize=None):
+    """NeuroNet.cl:1900-1953.  Online running mean/variance over the last `batch` calls, gamma/beta, activation.
+    With batch <= 1 in training the kernel returns without writing the output."""
+    n = gsize[0]
+    w = 7 if optimization == 0 else 9
+    with _err():
+        o = options[:n * w].reshape(n, w)
+        inp = nan0(inputs[:n])
+        if training == 0:
+            mean = nan0(o[:, 0])
+            var = nan0(o[:, 1], 1.0)
+            var = np.where(var <= 0, F32(1), var)
+            gamma = nan0(o[:, 3], 1.0)
+            gamma = np.where(gamma == 0, F32(1), gamma)
+            beta = nan0(o[:, 4])
+            nx = (inp - mean) / np.sqrt(var)
+            output[:n] = f_activation(gamma * nx + beta, activation)
+            return
+        if batch <= 1:
+            return
+        fb = F32(batch)
+        mean = (nan0(o[:, 0]) * max(fb - F32(1), F32(0)) + inp) / max(fb, F32(1))
+        delt = inp - mean
+        var = (nan0(o[:, 1] * max(fb - F32(1), F32(0))) + delt * delt) / max(fb, F32(1))
+        var = np.where(var <= 0, F32(1), var).astype(F32)
+        nx = delt / np.sqrt(var)
+        gamma = nan0(o[:, 3], 1.0)
+        o[:, 3] = np.where(gamma == 0, F32(1), o[:, 3])
+        gamma = np.where(gamma == 0, F32(1), gamma)
+        beta = nan0(o[:, 4])
+        o[:, 0], o[:, 1], o[:, 2] = mean, var, nx
+        output[:n] = f_activation(gamma * nx + beta, activation)
+
+
+def CalcHiddenGradientBatch(options, matrix_g, matrix_i, matrix_ig, activation, batch, optimization, gsize,
+                            lsize=None):
+    """NeuroNet.cl:1964-1998 (its gvar term multiplies the stored mean by the input, as written)."""
+    if batch <= 1:
+        return
+    n = gsize[0]
+    w = 7 if optimization == 0 else 9
+    with _err():
+        o = options[:n * w].reshape(n, w)
+        var = nan0(o[:, 1], 1.0)
+        inp = nan0(matrix_i[:n])
+        gnx = nan0(matrix_g[:n]) * nan0(o[:, 3], 1.0)
+        temp = np.where(var > 0, F32(1) / np.sqrt(var), F32(0))
+        gmu = -temp * gnx
+        gvar = np.where(var > 0, (nan0(o[:, 0]) * inp) / (F32(2) * np.power(var, F32(1.5))) * gnx, F32(0))
+        ratio = F32(max(batch - 1, 0)) / F32(max(batch, 1))
+        bd = F32(max(batch, 1))
+        gx = temp * gnx + gmu / bd + gvar * F32(2) * inp / bd * ratio * ratio
+        matrix_ig[:n] = deactivation(gx, inp, activation)
+
+
+def bn_adam_apply(options, G_gamma, G_beta, l, b1, b2, n):
+    """UpdateBatchOptionsAdam arithmetic (NeuroNet.cl:2061-2097) given the gamma/beta gradients; the beta
+    step copies the gamma step (delta.s1 = IsNaNOrInf(delta.s0))."""
+    with _err():
+        o = options[:n * 9].reshape(n, 9)
+        b1, b2, l = F32(b1), F32(b2), F32(l)
+        gamma = nan0(o[:, 3], 1.0)
+        gamma = np.where(gamma == 0, F32(1), gamma)
+        beta = nan0(o[:, 4])
+        mg = b1 * nan0(o[:, 5]) + (F32(1) - b1) * G_gamma
+        mb = b1 * nan0(o[:, 6]) + (F32(1) - b1) * G_beta
+        vg = nan0(b2 * nan0(o[:, 7]) + (F32(1) - b2) * (G_gamma * G_gamma), 1.0)
+        vb = nan0(b2 * nan0(o[:, 8]) + (F32(1) - b2) * (G_beta * G_beta), 1.0)
+        dg = nan0(l * mg / np.sqrt(vg))
+        db = dg
+        wg = dg - (L1 * cl_sign(gamma) + L2 * gamma / F32(n))
+        wb = db - (L1 * cl_sign(beta) + L2 * beta / F32(n))
+        o[:, 3] = nan0(gamma + wg, 1.0)
+        o[:, 4] = nan0(beta + wb)
+        o[:, 5] = nan0(mg)
+        o[:, 6] = nan0(mb)
+        o[:, 7] = vg
+        o[:, 8] = vb
+
+
+def UpdateBatchOptionsAdam(options, matrix_g, l, b1, b2, gsize, lsize=None):
+    """NeuroNet.cl:2050-2098."""
+    n = gsize[0]
+    with _err():
+        grad = cl_clamp(nan0(matrix_g[:n]), -MAX_GRAD, MAX_GRAD)
+        nx = nan0(options[:n * 9].reshape(n, 9)[:, 2])
+    bn_adam_apply(options, grad * nx, grad, l, b1, b2, n)
+
+
+def bn_momentum_apply(options, G_gamma, G_beta, lr, mom, n):
+    """UpdateBatchOptionsMomentum arithmetic (NeuroNet.cl:2019-2037)."""
+    with _err():
+        o = options[:n * 7].reshape(n, 7)
+        lr, mom = F32(lr), F32(mom)
+        d0 = nan0(lr * G_gamma + mom * nan0(o[:, 5]))
+        d1 = nan0(lr * G_beta + mom * nan0(o[:, 6]))
+        o[:, 5] = d0
+        value = nan0(o[:, 3], 1.0)
+        o[:, 3] = value + d0 - lr * (L1 * cl_sign(value) + L2 * value / F32(n))
+        o[:, 6] = d1
+        value = nan0(o[:, 4])
+        o[:, 4] = value + d1 - lr * (L1 * cl_sign(value) + L2 * value / F32(n))
+
+
+def UpdateBatchOptionsMomentum(options, matrix_g, learning_rates, momentum, gsize, lsize=None):
+    """NeuroNet.cl:2010-2038."""
+    n = gsize[0]
+    with _err():
+        grad = cl_clamp(nan0(matrix_g[:n]), -MAX_GRAD, MAX_GRAD)
+        nx = nan0(options[:n * 7].reshape(n, 7)[:, 2])
+    bn_momentum_apply(options, grad * nx, grad, learning_rates, momentum, n)
+
+
+# --------------------------------------------------------------------- LSTM
+def _lstm_input_index(H, inputs_size):
+    """Input positions the reference's gate loop reads (NeuroNet.cl:2228-2244): float4 blocks while the
+    unsigned H - i > 4, otherwise positions i..H-1 (so for inputs > H the block at i = H is skipped)."""
+    idx = []
+    for i in range(0, inputs_size, 4):
+        if ((H - i) & 0xFFFFFFFF) > 4:
+            idx += [i, i + 1, i + 2, i + 3]
+        else:
+            idx += list(range(i, H))
+    return np.array(idx, dtype=np.int64)
+
+
+def LSTM_FeedForward(inputs, inputs_size, weights, concatenated, memory, output, gsize, lsize=None):
+    """NeuroNet.cl:2189-2261.  Gate g of neuron id sums weight row g+id over (h(t-1), x(t), 1); f,i,o are
+    sigmoid and the new content tanh; c = f c + i g; h = o tanh(c).  Every gate reads h(t-1) (the reference
+    overwrites h from other work-groups while they read it)."""
+    H, V = gsize[0], gsize[2] if len(gsize) > 2 else 1
+    ins = inputs_size
+    ws = ins + H + 1
+    with _err():
+        h_prev = output[:V * H].reshape(V, H).copy()
+        xi = _lstm_input_index(H, ins)
+        flat_x = inputs
+        cat = concatenated[:V * 4 * H].reshape(V, 4, H)
+        for gate in range(4):
+            rows = np.arange(H) + gate
+            W = weights[:(H + 3) * ws].reshape(H + 3, ws)[rows]       # [H][ws]
+            hs = h_prev @ W[:, :H].T                                   # [V][H]
+            xv = np.stack([flat_x[v * ins + xi] for v in range(V)]) if xi.size else np.zeros((V, 0), F32)
+            xs = xv @ W[:, H + xi].T if xi.size else 0
+            s = hs + xs + nan0(W[:, H + ins])[None, :]
+            cat[:, gate, :] = f_activation(s.astype(F32), SIGMOID if gate < 3 else TANH)
+        mem = memory[:2 * V * H].reshape(2, V, H)
+        old = mem[0].copy()
+        mem[1] = old
+        new = nan0(old * cat[:, 0] + cat[:, 1] * cat[:, 3])
+        mem[0] = new
+        output[:V * H] = nan0(cat[:, 2] * f_activation(new, TANH)).reshape(-1)
+
+
+def LSTM_ConcatenatedGradient(gradient, concatenated_gradient, memory, concatenated, gsize, lsize=None):
+    """NeuroNet.cl:2265-2297: gate gradients from the hidden-state gradient."""
+    H, V = gsize[0], gsize[1] if len(gsize) > 1 else 1
+    with _err():
+        g = gradient[:V * H].reshape(V, H)
+        m = memory[:2 * V * H].reshape(2, V, H)
+        a = concatenated[:V * 4 * H].reshape(V, 4, H)
+        cg = concatenated_gradient[:V * 4 * H].reshape(V, 4, H)
+        t = np.tanh(m[0])
+        cg[:, 2] = g * t
+        mg = g * a[:, 2] * (F32(1) - t * t)
+        cg[:, 3] = mg * a[:, 1]
+        cg[:, 1] = mg * a[:, 3]
+        cg[:, 0] = mg * m[1]
+
+
+def LSTM_HiddenGradient(concatenated_gradient, inputs_gradient, weights_gradient, hidden_state, inputs, weights,
+                        output, hidden_size, inputs_size, gsize, lsize=None):
+    """NeuroNet.cl:2301-2441.  Derivative factors from the gradient value (cg(1-cg), cg(1-cg^2)); input
+    gradient; weight gradient summed over the series; the "bias" sum of row i written at (i+1)*(H+in+1)
+    after the weight loop (and the last one, one element past a (4H)x(H+in+1) matrix, only when the buffer
+    holds it); hidden_state <- output."""
+    H, V = gsize[0], gsize[1] if len(gsize) > 1 else 1
+    ins = inputs_size
+    ws = H + ins + 1
+    with _err():
+        cg = concatenated_gradient[:V * 4 * H].reshape(V, 4 * H)
+        a = np.concatenate([cg[:, :3 * H] * (F32(1) - cg[:, :3 * H]),
+                            cg[:, 3 * H:] * (F32(1) - cg[:, 3 * H:] ** 2)], axis=1).astype(F32)
+        W = weights[:4 * H * ws].reshape(4 * H, ws)
+        h_old = hidden_state[:V * H].reshape(V, H).copy()
+        x = inputs[:V * ins].reshape(V, ins)
+        if ins:
+            inputs_gradient[:V * ins] = (a @ W[:, H:H + ins]).astype(F32).reshape(-1)
+        opnd = np.concatenate([h_old, x], axis=1)
+        wg = weights_gradient
+        G = (a.T @ opnd).astype(F32)                       # [4H][H+in]
+        wg2 = wg[:4 * H * ws].reshape(4 * H, ws)
+        wg2[:, :H + ins] = G
+        bias = np.concatenate([cg[:, :3 * H] * (F32(1) - cg[:, :3 * H]),
+                               F32(1) - cg[:, 3 * H:] ** 2], axis=1).sum(axis=0, dtype=F32)
+        last = 4 * H if wg.size > 4 * H * ws else 4 * H - 1
+        for i in range(last):
+            wg[(i + 1) * ws] = bias[i]
+        hidden_state[:V * H] = output[:V * H]
+
+
+def LSTM_UpdateWeightsAdam(weights, weights_gradient, matrix_m, matrix_v, l, b1, b2, gsize, lsize=None):
+    """NeuroNet.cl:2450-2475: Adam over a (rows x total) block with l2 decay divided by total, raw rate."""
+    total, rows = gsize[0], gsize[1] if len(gsize) > 1 else 1
+    n = total * rows
+    with _err():
+        b1, b2, l = F32(b1), F32(b2), F32(l)
+        g = cl_clamp(nan0(weights_gradient[:n]), -MAX_GRAD, MAX_GRAD)
+        mt = b1 * nan0(matrix_m[:n]) + (F32(1) - b1) * g
+        vt = b2 * nan0(matrix_v[:n], 1.0) + (F32(1) - b2) * (g * g)
+        w = nan0(weights[:n])
+        delta = l * (mt / (np.sqrt(vt) + F32(1e-37)) - (L1 * cl_sign(w) + L2 * w / F32(total)))
+        weights[:n] = nan0(w + delta)
+        matrix_m[:n] = mt
+        matrix_v[:n] = vt
+
+
 KERNELS = {name: fn for name, fn in globals().items()
            if callable(fn) and name[:1].isupper() and fn.__module__ == __name__}
 

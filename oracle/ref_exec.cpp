@@ -33,6 +33,7 @@ struct RefKernel {
   int uses_barrier;
   int nargs;
   const char *argtypes;
+  int serial;  // work-groups in order on one thread (kernels whose groups write the same elements)
 };
 extern "C" const RefKernel nnref_table[];
 extern "C" const int nnref_table_size;
@@ -142,7 +143,7 @@ extern "C" int nnref_launch(const char *name, int work_dim, const size_t *global
     total *= ng[d];
   }
   if (total == 0) return 0;
-#pragma omp parallel for schedule(dynamic, 1)
+#pragma omp parallel for schedule(dynamic, 1) if (!k->serial)
   for (long long gi = 0; gi < (long long)total; ++gi) {
     ocl::NDRange &nd = ocl::g_nd;
     nd.dims = (ocl::uint)work_dim;

@@ -199,13 +199,64 @@ def _norm_cases():
     return cases
 
 
+def _batchnorm_cases():
+    cases = []
+    for n in (1, 37, 256):
+        for opt, width in ((0, 7), (1, 9)):
+            for batch, training in ((1, 1), (2, 1), (50, 1), (50, 0)):
+                for act in (NONE, TANH):
+                    cases.append(Case(f"BatchFeedForward/{n}/opt{opt}/b{batch}/t{training}/act{act}", "BatchFeedForward",
+                                      [A(n), A(n * width, "pos"), A(n, "zeros"), batch, opt, act, training], (n,)))
+            for batch in (1, 50):
+                cases.append(Case(f"CalcHiddenGradientBatch/{n}/opt{opt}/b{batch}", "CalcHiddenGradientBatch",
+                                  [A(n * width, "pos"), A(n, "grad"), A(n), A(n, "zeros"), NONE, batch, opt], (n,)))
+        cases.append(Case(f"UpdateBatchOptionsAdam/{n}", "UpdateBatchOptionsAdam",
+                          [A(n * 9, "pos"), A(n, "grad"), 3e-4, 0.9, 0.999], (n,)))
+        cases.append(Case(f"UpdateBatchOptionsMomentum/{n}", "UpdateBatchOptionsMomentum",
+                          [A(n * 7, "pos"), A(n, "grad"), 3e-4, 0.9], (n,)))
+    return cases
+
+
+def _lstm_cases():
+    cases = []
+    # (H, inputs, V, hidden weights zeroed).  The reference's forward reads h(t-1) from other work-groups
+    # while they overwrite it; cases with H > 1 zero the recurrent weights so the race cannot show.
+    for H, ins, V, hz in ((1, 4, 3, False), (1, 8, 2, False), (16, 8, 3, True), (6, 12, 2, True), (8, 8, 2, True)):
+        ws = ins + H + 1
+        cases.append(Case(f"LSTM_FeedForward/{H}-{ins}-{V}", "LSTM_FeedForward",
+                          [A(V * ins), ins, A((H + 3) * ws, "uniform", 0.5), A(V * 4 * H, "zeros"),
+                           A(2 * V * H, "normal", 0.5), A(V * H, "uniform", 0.9)],
+                          (H, 4, V), (1, 4, 1), meta={"lstm_hidden_zero": (H, ins) if hz else None}))
+    for H, V in ((16, 3), (5, 2)):
+        cases.append(Case(f"LSTM_ConcatenatedGradient/{H}-{V}", "LSTM_ConcatenatedGradient",
+                          [A(V * H, "grad", 10.0), A(V * 4 * H, "zeros"), A(2 * V * H), A(V * 4 * H, "unit")],
+                          (H, V)))
+    for H, ins, V in ((8, 8, 3), (4, 12, 2), (6, 4, 70)):
+        ws = H + ins + 1
+        cases.append(Case(f"LSTM_HiddenGradient/{H}-{ins}-{V}", "LSTM_HiddenGradient",
+                          [A(V * 4 * H, "unit"), A(V * ins, "zeros"), A(4 * H * ws + 1, "zeros"), A(V * H),
+                           A(V * ins), A(4 * H * ws, "uniform", 0.5), A(V * H), H, ins],
+                          (H, V), (1, V)))
+    for total, rows in ((9, 4), (17, 8), (257, 3)):
+        n = total * rows
+        cases.append(Case(f"LSTM_UpdateWeightsAdam/{total}x{rows}", "LSTM_UpdateWeightsAdam",
+                          [A(n, "uniform", 0.3), A(n, "grad"), A(n, "small"), A(n, "pos", 1e-5), 3e-4, 0.9, 0.999],
+                          (total, rows)))
+    return cases
+
+
 def all_cases() -> list[Case]:
-    return _dense_cases() + _conv_cases() + _attention_cases() + _norm_cases()
+    return _dense_cases() + _conv_cases() + _attention_cases() + _norm_cases() + _batchnorm_cases() + _lstm_cases()
 
 
 def prepare_inputs(case: Case, seed: int) -> list:
     """Inputs of a case, with attention scores made row-stochastic where the case asks for it."""
     args = materialise(case, seed)
+    hz = case.meta.get("lstm_hidden_zero")
+    if hz:
+        H, ins = hz
+        w = args[2].reshape(H + 3, ins + H + 1)
+        w[:, :H] = 0.0
     if case.meta.get("softmax_scores"):
         units, heads = case.gsize[0], case.gsize[1]
         for i, a in enumerate(case.args):
