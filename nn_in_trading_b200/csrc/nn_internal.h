@@ -94,6 +94,8 @@ extern const KernelDef kMiscKernels[];
 extern const int kNumMiscKernels;
 extern const KernelDef kLstmKernels[];
 extern const int kNumLstmKernels;
+extern const KernelDef kAttn2Kernels[];
+extern const int kNumAttn2Kernels;
 
 // Number of data-parallel ranks (1 without a communicator).
 int dp_world();

@@ -209,7 +209,7 @@ const KernelDef *find_kernel(const char *name) {
   struct Table { const KernelDef *t; int n; };
   const Table tables[] = {{kDenseKernels, kNumDenseKernels}, {kConvKernels, kNumConvKernels},
                           {kAttnKernels, kNumAttnKernels}, {kMiscKernels, kNumMiscKernels},
-                          {kLstmKernels, kNumLstmKernels}};
+                          {kLstmKernels, kNumLstmKernels}, {kAttn2Kernels, kNumAttn2Kernels}};
   for (const Table &t : tables)
     for (int i = 0; i < t.n; ++i)
       if (std::strcmp(t.t[i].name, name) == 0) return &t.t[i];

@@ -639,6 +639,117 @@ def UpdateBatchOptionsMomentum(options, matrix_g, learning_rates, momentum, gsiz
     bn_momentum_apply(options, grad * nx, grad, learning_rates, momentum, n)
 
 
+# ------------------------------------------------- legacy single-head attention
+def AttentionScore(querys, keys, score, dimension, mask, gsize, lsize=None):
+    """NeuroNet.cl:1237-1275.  S = exp(q.k/sqrt(d)) (NaN/Inf -> 0), masked k > q -> 0, row / sum when sum > 0."""
+    U, D = gsize[0], dimension
+    koef = max(np.sqrt(F32(D)), F32(1))
+    with _err():
+        q = querys[:U * D].reshape(U, D)
+        k = keys[:U * D].reshape(U, D)
+        s = nan0(np.exp((q @ k.T).astype(F32) / koef))
+        if mask > 0:
+            s = np.where(np.arange(U)[None, :] <= np.arange(U)[:, None], s, F32(0))
+        tot = s.sum(axis=1, dtype=F32)
+        s = np.where((tot > 0)[:, None], s / tot[:, None], s)
+        score[:U * U] = s.reshape(-1)
+
+
+def AttentionOut(scores, values, inputs, out, gsize, lsize=None):
+    """NeuroNet.cl:1286-1303.  out = nan0(nan0(S) nan0(V)) + inputs."""
+    U, D = gsize[0], gsize[1] if len(gsize) > 1 else 1
+    with _err():
+        s = nan0(scores[:U * U].reshape(U, U))
+        v = nan0(values[:U * D].reshape(U, D))
+        out[:U * D] = (nan0(s @ v) + inputs[:U * D].reshape(U, D)).reshape(-1)
+
+
+def AttentionInsideGradients(querys, querys_g, keys, keys_g, values, values_g, scores, gradient, gsize,
+                             lsize=None):
+    """NeuroNet.cl:1395-1443.  P = g V^T, f(s) = s(1-s) (1e-4 at 0 or 1); vg = S^T g, qg = (f(S) o P) K / koef,
+    kg = (f(S) o P)^T Q / koef, each nan0 then clamped to [-1, 1]."""
+    U, D = gsize[0], gsize[1] if len(gsize) > 1 else 1
+    koef = max(np.sqrt(F32(D)), F32(1))
+    with _err():
+        S = scores[:U * U].reshape(U, U)
+        G = gradient[:U * D].reshape(U, D)
+        V = values[:U * D].reshape(U, D)
+        Q = querys[:U * D].reshape(U, D)
+        Kk = keys[:U * D].reshape(U, D)
+        P = (G @ V.T).astype(F32)
+        f = np.where((S == 0) | (S == 1), F32(1e-4), S * (F32(1) - S))
+        M = (f * P).astype(F32)
+        values_g[:U * D] = cl_clamp(nan0(S.T @ G), -1.0, 1.0).reshape(-1)
+        querys_g[:U * D] = cl_clamp(nan0((M @ Kk) / koef), -1.0, 1.0).reshape(-1)
+        keys_g[:U * D] = cl_clamp(nan0((M.T @ Q) / koef), -1.0, 1.0).reshape(-1)
+
+
+# ------------------------------------------------------------- MH2 attention
+def MH2AttentionOut(q, kv, score, out, dimension, heads_kv, mask, gsize, lsize):
+    """NeuroNet.cl:4252-4304.  Softmax (max-subtracted, LocalSoftMax) of q.k/sqrt(d) over the keys of kv head
+    h % heads_kv, masked keys k > q excluded; out = sum_k nan0(V[k] * score)."""
+    Qn, H = gsize[0], gsize[2]
+    Kn, D, Hkv = lsize[1], dimension, heads_kv
+    koef = max(np.sqrt(F32(D)), F32(1))
+    with _err():
+        Q = q[:Qn * H * D].reshape(Qn, H, D)
+        KV = kv[:Kn * 2 * Hkv * D].reshape(Kn, 2, Hkv, D)
+        hk = np.arange(H) % Hkv
+        Kh = KV[:, 0][:, hk]                               # [K][H][D]
+        Vh = KV[:, 1][:, hk]
+        logits = nan0(np.einsum("qhd,khd->qhk", Q, Kh).astype(F32) / koef, MIN_VALUE)
+        if mask != 0:
+            keep = np.arange(Kn)[None, None, :] <= np.arange(Qn)[:, None, None]
+            logits = np.where(keep, logits, MIN_VALUE)
+        S = _softmax_rows(logits)
+        score[:Qn * H * Kn] = S.reshape(-1)
+        o = nan0(np.einsum("qhk,khd->qhkd", S, Vh)).sum(axis=2, dtype=F32)
+        out[:Qn * H * D] = nan0(o).reshape(-1)
+
+
+def MH2AttentionInsideGradients(q, q_g, kv, kv_g, scores, gradient, kunits, heads_kv, gsize, lsize=None):
+    """NeuroNet.cl:4307-4406 with its indexing as written: the query gradient reads the output gradient at
+    (q+h)*D+d, the key gradient reads head 0's score rows and q at D*(q0*H+h+r)+d (q0 = k mod Q), runs its head
+    loop H-h times, and multiplies by 1 - (sum of a softmax row), i.e. it is rounding-level."""
+    Qn, D, H = gsize[0], gsize[1], gsize[2]
+    Kn, Hkv = kunits, heads_kv
+    koef = max(np.sqrt(F32(D)), F32(1))
+    with _err():
+        S = scores[:Qn * H * Kn].reshape(Qn, H, Kn)
+        G = gradient[:Qn * H * D].reshape(Qn, H, D)
+        KV = kv[:Kn * 2 * Hkv * D].reshape(Kn, 2, Hkv, D)
+        out_kv = kv_g[:Kn * 2 * Hkv * D].reshape(Kn, 2, Hkv, D)
+        gflat = gradient
+        # values
+        for h in range(Hkv):
+            hq = np.arange(h, H, Hkv)
+            out_kv[:, 1, h, :] = np.einsum("ghd,ghv->vd", G[:, hq, :], S[:, hq, :]).astype(F32)
+        # queries
+        hk = np.arange(H) % Hkv
+        Vh = KV[:, 1][:, hk]                                 # [K][H][D]
+        Kh = KV[:, 0][:, hk]
+        A = np.einsum("qhv,vhd->qhd", S, Vh).astype(F32)
+        acc = np.einsum("qhk,khd->qhd", S, Vh * Kh) - A * np.einsum("qhk,khd->qhd", S, Kh)
+        outg = np.array([[gflat[(qi + h) * D:(qi + h) * D + D] for h in range(H)] for qi in range(Qn)], F32)
+        q_g[:Qn * H * D] = (outg * acc.astype(F32) / koef).astype(F32).reshape(-1)
+        # keys
+        row0 = S[:, 0, :]                                    # [r][k]
+        tot = row0.sum(axis=1, dtype=F32)                    # [r]
+        for k in range(Kn):
+            q0 = k % Qn
+            for h in range(Hkv):
+                val = KV[k, 1, h, :]
+                accd = np.zeros(D, F32)
+                for r in range(Qn):
+                    sc = row0[r, k]
+                    if sc == 0:
+                        continue
+                    gi = (h + r) * D
+                    qi = D * (q0 * H + h + r)
+                    accd += gflat[gi:gi + D] * val * sc * (F32(1) - tot[r]) * q[qi:qi + D]
+                out_kv[k, 0, h, :] = accd * F32(H - h) / koef
+
+
 # --------------------------------------------------------------------- LSTM
 def _lstm_input_index(H, inputs_size):
     """Input positions the reference's gate loop reads (NeuroNet.cl:2228-2244): float4 blocks while the

@@ -217,6 +217,31 @@ def _batchnorm_cases():
     return cases
 
 
+def _attention2_cases():
+    cases = []
+    for U, D in ((5, 4), (12, 8), (33, 6)):
+        for mask in (0, 1):
+            cases.append(Case(f"AttentionScore/{U}-{D}/m{mask}", "AttentionScore",
+                              [A(U * D), A(U * D), A(U * U, "zeros"), D, mask], (U,)))
+        cases.append(Case(f"AttentionOut/{U}-{D}", "AttentionOut",
+                          [A(U * U, "unit"), A(U * D), A(U * D), A(U * D, "zeros")], (U, D)))
+        cases.append(Case(f"AttentionInsideGradients/{U}-{D}", "AttentionInsideGradients",
+                          [A(U * D), A(U * D, "zeros"), A(U * D), A(U * D, "zeros"), A(U * D), A(U * D, "zeros"),
+                           A(U * U, "unit"), A(U * D, "grad", 10.0)], (U, D), meta={"softmax_rows": (U, U)}))
+    # (Q, K, H, Hkv, D)
+    for Qn, Kn, H, Hkv, D in ((4, 6, 2, 1, 4), (7, 7, 4, 2, 8), (5, 3, 3, 3, 5)):
+        for mask in (0, 1):
+            cases.append(Case(f"MH2AttentionOut/{Qn}-{Kn}-{H}-{Hkv}-{D}/m{mask}", "MH2AttentionOut",
+                              [A(Qn * H * D), A(Kn * 2 * Hkv * D), A(Qn * H * Kn, "zeros"), A(Qn * H * D, "zeros"),
+                               D, Hkv, mask], (Qn, Kn, H), (1, Kn, 1)))
+        qpad = D * ((Qn - 1) * (H + 1) + Hkv)
+        cases.append(Case(f"MH2AttentionInsideGradients/{Qn}-{Kn}-{H}-{Hkv}-{D}", "MH2AttentionInsideGradients",
+                          [A(max(Qn * H * D, qpad)), A(Qn * H * D, "zeros"), A(Kn * 2 * Hkv * D),
+                           A(Kn * 2 * Hkv * D, "zeros"), A(Qn * H * Kn, "unit"), A(Qn * H * D, "grad", 10.0), Kn, Hkv],
+                          (Qn, D, H), meta={"softmax_rows": (Qn * H, Kn), "noise_args": {3: "mh2_key_grad"}}))
+    return cases
+
+
 def _lstm_cases():
     cases = []
     # (H, inputs, V, hidden weights zeroed).  The reference's forward reads h(t-1) from other work-groups
@@ -246,12 +271,20 @@ def _lstm_cases():
 
 
 def all_cases() -> list[Case]:
-    return _dense_cases() + _conv_cases() + _attention_cases() + _norm_cases() + _batchnorm_cases() + _lstm_cases()
+    return (_dense_cases() + _conv_cases() + _attention_cases() + _norm_cases() + _batchnorm_cases() + _lstm_cases()
+            + _attention2_cases())
 
 
 def prepare_inputs(case: Case, seed: int) -> list:
     """Inputs of a case, with attention scores made row-stochastic where the case asks for it."""
     args = materialise(case, seed)
+    rows = case.meta.get("softmax_rows")
+    if rows:
+        R, C = rows
+        for i, a in enumerate(case.args):
+            if isinstance(a, A) and a.size == R * C and a.init == "unit":
+                s = args[i].reshape(R, C)
+                args[i] = np.ascontiguousarray((s / s.sum(axis=1, keepdims=True)).reshape(-1), dtype=np.float32)
     hz = case.meta.get("lstm_hidden_zero")
     if hz:
         H, ins = hz

@@ -166,3 +166,55 @@ def test_batched_update_is_mean_gradient_then_reference_update(ctx, case):
     ref = batched_update_oracle(case, samples, shared)
     for i, r in ref.items():
         check_close(f"{case.name} arg{i}", got[i], r, before[i])
+
+
+@pytest.mark.parametrize("opt", [0, 1])
+def test_batched_batchnorm_scans_samples_in_order(ctx, opt):
+    """Batched BatchFeedForward == consecutive reference calls; the batched backward and option update
+    use every sample's own statistics and the batch-mean gamma/beta gradient."""
+    rng = np.random.default_rng(11 + opt)
+    N, B, batch = 37, 4, 20
+    width = 7 if opt == 0 else 9
+    x = rng.standard_normal((B, N)).astype(np.float32)
+    opts = rng.uniform(0.05, 1.0, N * width).astype(np.float32)
+    g = (rng.standard_normal((B, N)) * 0.01).astype(np.float32)
+    # oracle: consecutive per-sample calls
+    o = opts.copy()
+    ys, hist = [], []
+    for b in range(B):
+        y = np.zeros(N, np.float32)
+        K.BatchFeedForward(x[b], o, y, batch, opt, K.TANH, 1, gsize=(N,))
+        ys.append(y)
+        hist.append(o.reshape(N, width)[:, :3].copy())
+    igs = []
+    for b in range(B):
+        ob = o.copy().reshape(N, width)
+        ob[:, :3] = hist[b]
+        ig = np.zeros(N, np.float32)
+        K.CalcHiddenGradientBatch(ob.reshape(-1), g[b], x[b], ig, K.NONE, batch, opt, gsize=(N,))
+        igs.append(ig)
+    clamp = K.cl_clamp(K.nan0(g), -K.MAX_GRAD, K.MAX_GRAD)
+    Gg = np.mean([clamp[b] * hist[b][:, 2] for b in range(B)], axis=0).astype(np.float32)
+    Gb = np.mean(clamp, axis=0).astype(np.float32)
+    o_upd = o.copy()
+    if opt == 1:
+        K.bn_adam_apply(o_upd, Gg, Gb, 3e-4, 0.9, 0.999, N)
+    else:
+        K.bn_momentum_apply(o_upd, Gg, Gb, 3e-4, 0.9, N)
+    # library, batched
+    hx, hy, ho, hg, hig = ctx.buffer(B * N), ctx.buffer(B * N), ctx.buffer(N * width), ctx.buffer(B * N), ctx.buffer(B * N)
+    ctx.write(hx, x)
+    ctx.write(ho, opts)
+    ctx.write(hg, g)
+    ctx.kernel("BatchFeedForward").args(hx, ho, hy, batch, opt, K.TANH, 1).batch(B).run((N,))
+    check_close("bn forward", ctx.read(hy, B * N), np.concatenate(ys))
+    check_close("bn options after forward", ctx.read(ho, N * width), o)
+    ctx.kernel("CalcHiddenGradientBatch").args(ho, hg, hx, hig, K.NONE, batch, opt).batch(B).run((N,))
+    check_close("bn input gradient", ctx.read(hig, B * N), np.concatenate(igs))
+    if opt == 1:
+        ctx.kernel("UpdateBatchOptionsAdam").args(ho, hg, 3e-4, 0.9, 0.999).batch(B).run((N,))
+    else:
+        ctx.kernel("UpdateBatchOptionsMomentum").args(ho, hg, 3e-4, 0.9).batch(B).run((N,))
+    check_close("bn options after update", ctx.read(ho, N * width), o_upd, o)
+    for h in (hx, hy, ho, hg, hig):
+        ctx.free(h)
