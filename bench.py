@@ -98,6 +98,13 @@ class ClockSampler:
 
 
 # --------------------------------------------------- algorithmic work model
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch, from one ncu capture
+# of the batch-256 workload:  ncu --set full --clock-control none -k regex:mh_grad_smem -s 2 -c 1
+#   python bench.py --steps 3 --warmup 3 --no-cpu-baseline
+# Keyed by the reference kernel; scaled to other batches by the sequences a launch processes.
+NCU_TRAFFIC = {"MHAttentionInsideGradients": (312.09e6, 256)}
+
+
 def op_work(op, B):
     """(flops, bytes) a launch must do at minimum: every operand read once, every result written once."""
     k = op.kernel
@@ -247,7 +254,9 @@ def run_ours(args, rank, world, local_rank):
         peaks = read_peaks()
         top = prof["top"]
         roof = {"bound": "hbm", "kernel": top["name"], "achieved": top["gbs"], "peak": peaks["hbm_gbs"],
-                "unit": "GB/s", "frac": top["gbs"] / peaks["hbm_gbs"], "traffic": None,
+                "unit": "GB/s", "frac": top["gbs"] / peaks["hbm_gbs"],
+                "traffic": (NCU_TRAFFIC[top["name"]][0] * B / NCU_TRAFFIC[top["name"]][1]
+                            if top["name"] in NCU_TRAFFIC else None),
                 "algorithmic_bytes_per_launch": top["bytes_per_launch"],
                 "avg_launch_us": top["avg_us"], "peak_source": peaks["source"]}
         result = {

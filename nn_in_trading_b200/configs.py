@@ -9,6 +9,16 @@
                 MSE against N(0,1) targets.  Weight ranges are the layer's own
                 (+-1/sqrt(window+1), FF2 +-1/sqrt(4*window+1), NeuroNet_Attention.mqh:1700-1790).
 
+  lstm_stack    2 stacked CNeuronLSTMOCL layers (input 64, hidden 256) over 1024 independent
+                series (the layer's `variables`), one time step per training step (the reference
+                trains recurrent layers bar by bar, h(t-1) enters as an input); a per-series 1x1
+                conv head 256 -> 64 predicts the next step's 64 log-returns (MSE).  Inputs are
+                N(0, 0.01) log-returns cumulated along the window.
+  patchtst      RevIN-style: BatchNorm over 32 channels x 512 bars, Conv1D patching (window 16,
+                step 8, 63 patches, embed 128, per-channel weights), 3 attention layers over the
+                63 patches of every channel (8 heads x key 16, FF 512), a shared conv head
+                63*128 -> 96 per channel, RevIN de-normalisation, MSE vs N(0,1) targets.
+
 Data is synthetic and seeded; no market data is involved.
 """
 from __future__ import annotations
@@ -18,7 +28,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from .api import ADAM, LRELU, NONE, SIGMOID, TANH, Context
-from .layers import DenseLayer, MLMHAttentionLayer
+from .layers import BatchNormLayer, ConvLayer, DenseLayer, LSTMLayer, MLMHAttentionLayer, RevINDenormLayer
 from .net import Net
 
 F32 = np.float32
@@ -98,3 +108,112 @@ def build_mlmh(ctx: Context, spec: MLMHSpec, batch: int, weights=None, dp: bool 
         for name, w in ws.items():
             enc.set_weights(i, name, w)
     return Net(ctx, [inp, enc], dp=dp)
+
+
+# ------------------------------------------------------------------ LSTM stack
+@dataclass
+class LSTMSpec:
+    inputs: int = 64
+    hidden: int = 256
+    layers: int = 2
+    series: int = 1024
+    seq: int = 240
+    seed: int = 3
+
+
+def lstm_weights(spec: LSTMSpec) -> dict:
+    """Uniform +-1/sqrt(fan_in) for the gate matrices and the head."""
+    rng = np.random.default_rng(spec.seed)
+    out = {}
+    ins = spec.inputs
+    for l in range(spec.layers):
+        ws = ins + spec.hidden + 1
+        k = 1.0 / np.sqrt(ins + spec.hidden)
+        out[f"lstm{l}"] = rng.uniform(-k, k, 4 * spec.hidden * ws).astype(F32)
+        ins = spec.hidden
+    k = 1.0 / np.sqrt(spec.hidden)
+    out["head"] = rng.uniform(-k, k, spec.inputs * (spec.hidden + 1)).astype(F32)
+    return out
+
+
+def lstm_data(spec: LSTMSpec, steps: int | None = None, seed: int | None = None):
+    """[steps+1][series][inputs] cumulated N(0, 0.01) log-returns; step t trains x_t -> x_{t+1}."""
+    rng = np.random.default_rng(spec.seed + 1 if seed is None else seed)
+    T = (spec.seq if steps is None else steps) + 1
+    r = rng.normal(0.0, 0.01, (T, spec.series, spec.inputs))
+    return np.cumsum(r, axis=0).astype(F32)
+
+
+def build_lstm(ctx: Context, spec: LSTMSpec, weights=None, dp: bool = False) -> Net:
+    w = weights if weights is not None else lstm_weights(spec)
+    V = spec.series
+    layers = [DenseLayer(ctx, spec.inputs * V, NONE, ADAM, 1, 0)]
+    ins = spec.inputs
+    for l in range(spec.layers):
+        L = LSTMLayer(ctx, spec.hidden, ins, V, ADAM, 1)
+        L.set_lstm_weights(w[f"lstm{l}"])
+        layers.append(L)
+        ins = spec.hidden
+    head = ConvLayer(ctx, spec.hidden, spec.hidden, spec.inputs, V, 1, NONE, ADAM, 1)
+    head.set_conv_weights(w["head"])
+    layers.append(head)
+    return Net(ctx, layers, dp=dp)
+
+
+# ------------------------------------------------------------ PatchTST-style
+@dataclass
+class PatchSpec:
+    channels: int = 32
+    bars: int = 512
+    patch: int = 16
+    stride: int = 8
+    embed: int = 128
+    heads: int = 8
+    dk: int = 16
+    layers: int = 3
+    horizon: int = 96
+    norm_batch: int = 1000
+    seed: int = 4
+
+    @property
+    def patches(self) -> int:
+        return (self.bars - self.patch) // self.stride + 1
+
+
+def patch_weights(spec: PatchSpec) -> dict:
+    rng = np.random.default_rng(spec.seed)
+    out = {}
+    k = 1.0 / np.sqrt(spec.patch + 1)
+    out["conv"] = rng.uniform(-k, k, (spec.patch + 1) * spec.embed * spec.channels).astype(F32)
+    enc = mlmh_weights(MLMHSpec(window=spec.embed, dk=spec.dk, heads=spec.heads, units=spec.patches,
+                                layers=spec.layers, seed=spec.seed + 7))
+    out["encoder"] = enc
+    fan = spec.patches * spec.embed
+    k = 1.0 / np.sqrt(fan + 1)
+    out["head"] = rng.uniform(-k, k, spec.horizon * (fan + 1)).astype(F32)
+    return out
+
+
+def patch_data(spec: PatchSpec, batch: int, steps: int = 1, seed: int | None = None):
+    rng = np.random.default_rng(spec.seed + 1 if seed is None else seed)
+    x = rng.standard_normal((steps, batch, spec.channels * spec.bars)).astype(F32)
+    t = rng.standard_normal((steps, batch, spec.channels * spec.horizon)).astype(F32)
+    return x, t
+
+
+def build_patch(ctx: Context, spec: PatchSpec, batch: int, weights=None, dp: bool = False) -> Net:
+    w = weights if weights is not None else patch_weights(spec)
+    C, P, E = spec.channels, spec.patches, spec.embed
+    inp = DenseLayer(ctx, C * spec.bars, NONE, ADAM, batch, 0)
+    norm = BatchNormLayer(ctx, C * spec.bars, spec.norm_batch, ADAM, batch)
+    conv = ConvLayer(ctx, spec.patch, spec.stride, E, P, C, NONE, ADAM, batch)
+    conv.set_conv_weights(w["conv"])
+    # the conv output [C][P][E] of every sample is C independent sequences of P patches
+    enc = MLMHAttentionLayer(ctx, E, spec.dk, spec.heads, P, spec.layers, NONE, ADAM, batch * C)
+    for i, ws in enumerate(w["encoder"]):
+        for name, arr in ws.items():
+            enc.set_weights(i, name, arr)
+    head = ConvLayer(ctx, P * E, P * E, spec.horizon, C, 1, NONE, ADAM, batch)
+    head.set_conv_weights(w["head"])
+    denorm = RevINDenormLayer(ctx, C * spec.horizon, norm, batch)
+    return Net(ctx, [inp, norm, conv, enc, head, denorm], dp=dp)

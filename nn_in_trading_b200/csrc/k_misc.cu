@@ -40,7 +40,14 @@ __global__ void bn_ff_kernel(const float *__restrict__ in, float *__restrict__ o
       out[idx] = activate(gamma * nx + beta, act);
       continue;
     }
-    if (batch <= 1) return;  // the reference leaves the output untouched
+    if (batch <= 1) {  // the reference leaves the output and the statistics untouched
+      if (hist) {          // a batched backward still reads this sample's (unchanged) statistics
+        hist[idx * 3 + 0] = o[0];
+        hist[idx * 3 + 1] = o[1];
+        hist[idx * 3 + 2] = o[2];
+      }
+      continue;
+    }
     float mean = (nan0(o[0]) * fmaxf(fb - 1.f, 0.f) + inp) / fmaxf(fb, 1.f);
     float delt = inp - mean;
     float variance = (nan0(o[1] * fmaxf(fb - 1.f, 0.f)) + delt * delt) / fmaxf(fb, 1.f);
@@ -71,7 +78,7 @@ static int k_batch_feed_forward(Launch &L) {
   float *in = L.buf(0, (size_t)L.B * N), *opt = L.buf(1, (size_t)N * width), *out = L.buf(2, (size_t)L.B * N);
   if (!in || !opt || !out) return NN_ERR_BOUNDS;
   float *hist = nullptr;
-  if (L.B > 1 && training != 0 && batch > 1) {
+  if (L.B > 1 && training != 0) {
     hist = L.side(L.handle(1), (size_t)L.B * N * 3);
     if (!hist) return NN_ERR_CUDA;
   }

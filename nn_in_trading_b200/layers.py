@@ -34,11 +34,19 @@ def adam_lt(t: int, lr: float = LR, b1: float = B1, b2: float = B2) -> float:
 class Op:
     """One kernel execution of a training step (a bound kernel instance plus its NDRange)."""
 
+    recordable = True  # may be recorded into a command list
+
     def __init__(self, kernel: Kernel, gsize, lsize=None):
         self.kernel, self.gsize, self.lsize = kernel, tuple(gsize), None if lsize is None else tuple(lsize)
 
+    def patches(self) -> list:
+        """Per-step scalar arguments [(index, value)] computed on the host before the launch (the
+        bias-corrected Adam rate, the BatchNorm sample count); advances host state."""
+        return []
+
     def prepare(self) -> None:
-        """Host-side work before the launch (e.g. the per-step Adam rate)."""
+        for idx, value in self.patches():
+            self.kernel.set(idx, value)
 
     def __call__(self) -> None:
         self.prepare()
@@ -60,21 +68,47 @@ class AdamOp(Op):
         self.last_lt = lt
         return lt
 
-    def prepare(self) -> None:
-        self.kernel.set(self.l_index, self.next_lt())
+    def patches(self) -> list:
+        return [(self.l_index, self.next_lt())]
 
 
 class Layer:
-    """Common state of every layer: output and gradient buffers of `neurons` floats per sample."""
+    """CNeuronBaseOCL state shared by every layer: output and gradient buffers of `neurons` floats per
+    sample and, when the next layer is dense, the weights toward it, [next][neurons+1] with the bias
+    last (NeuroNet_Core.mqh:15496-15649: every layer class derives from CNeuronBaseOCL)."""
 
     def __init__(self, ctx: Context, neurons: int, activation: int = NONE, optimization: int = ADAM,
-                 batch: int = 1):
+                 batch: int = 1, outputs: int = 0):
         self.ctx, self.neurons, self.activation = ctx, int(neurons), int(activation)
         self.optimization, self.batch = optimization, int(batch)
         self.output = ctx.buffer(self.neurons * self.batch)
         self.gradient = ctx.buffer(self.neurons * self.batch)
         self.t = 1
         self.weights = None
+        self.outputs = int(outputs)
+        if self.outputs:
+            n = self.outputs * (self.neurons + 1)
+            self.weights = ctx.buffer(n)
+            if optimization == SGD:
+                self.delta = ctx.buffer(n)
+            else:
+                self.m = ctx.buffer(n)
+                self.v = ctx.buffer(n)
+
+    def set_weights(self, w: np.ndarray) -> None:
+        self.ctx.write(self.weights, w)
+
+    def hidden_gradient_ops(self, nxt: "Layer") -> list["Op"]:
+        """calcHiddenGradients, NeuroNet_Core.mqh:15744-15769 (next layer dense)."""
+        loc = min((nxt.neurons + 3) // 4, MAX_LOCAL)
+        k = self.kernel("CalcHiddenGradient").args(self.weights, nxt.gradient, self.output, self.gradient,
+                                                   nxt.neurons, self.activation)
+        return [Op(k, (self.neurons, loc), (1, loc))]
+
+    def per_sample(self, other: "Layer") -> int:
+        """Floats per sample of `other`'s buffers counted in this layer's batch units (a layer may view its
+        neighbour's buffer as more, shorter samples, e.g. per-channel sequences)."""
+        return other.neurons * other.batch // self.batch
 
     def kernel(self, name: str) -> Kernel:
         k = self.ctx.kernel(name)
@@ -99,23 +133,7 @@ class Layer:
 
 
 class DenseLayer(Layer):
-    """CNeuronBaseOCL (NeuroNet_Core.mqh:15464-16060): a dense layer.  Its `weights` are the
-    weights *towards the next dense layer*, [next][neurons+1] with the bias last."""
-
-    def __init__(self, ctx, neurons, activation=NONE, optimization=ADAM, batch=1, outputs=0):
-        super().__init__(ctx, neurons, activation, optimization, batch)
-        self.outputs = int(outputs)
-        if self.outputs:
-            n = self.outputs * (self.neurons + 1)
-            self.weights = ctx.buffer(n)
-            if optimization == SGD:
-                self.delta = ctx.buffer(n)
-            else:
-                self.m = ctx.buffer(n)
-                self.v = ctx.buffer(n)
-
-    def set_weights(self, w: np.ndarray) -> None:
-        self.ctx.write(self.weights, w)
+    """CNeuronBaseOCL (NeuroNet_Core.mqh:15464-16060): a dense layer fed by the previous layer's weights."""
 
     def forward_ops(self, prev: "DenseLayer") -> list[Op]:
         """feedForwardChecked, NeuroNet_Core.mqh:15686-15740."""
@@ -124,14 +142,7 @@ class DenseLayer(Layer):
                                             self.output, 0)
         return [Op(k, (self.neurons, loc), (1, loc))]
 
-    def hidden_gradient_ops(self, nxt: "DenseLayer") -> list[Op]:
-        """calcHiddenGradients, NeuroNet_Core.mqh:15744-15769."""
-        loc = min((nxt.neurons + 3) // 4, MAX_LOCAL)
-        k = self.kernel("CalcHiddenGradient").args(self.weights, nxt.gradient, self.output, self.gradient,
-                                                   nxt.neurons, self.activation)
-        return [Op(k, (self.neurons, loc), (1, loc))]
-
-    def update_ops(self, prev: "DenseLayer") -> list[Op]:
+    def update_ops(self, prev: "Layer") -> list[Op]:
         """updateInputWeights, NeuroNet_Core.mqh:15869-15984: the update of prev's weights and NormalizeWeights."""
         if prev.optimization == SGD:
             k = self.kernel("UpdateWeightsMomentum").args(prev.weights, self.gradient, prev.output, prev.delta,
@@ -152,8 +163,8 @@ class MLMHAttentionLayer(Layer):
     Sum&Normalize over `units` tokens of `window` features."""
 
     def __init__(self, ctx, window, window_key, heads, units, layers, activation=NONE, optimization=ADAM,
-                 batch=1):
-        super().__init__(ctx, window * units, activation, optimization, batch)
+                 batch=1, outputs=0):
+        super().__init__(ctx, window * units, activation, optimization, batch, outputs)
         if optimization != ADAM:
             raise ValueError("MLMH attention layer: only the Adam path is built")
         self.window, self.dk, self.heads, self.units, self.layers = window, window_key, heads, units, layers
@@ -283,3 +294,204 @@ class MLMHAttentionLayer(Layer):
             ops += self._conv_update(ws["ff2"], t[5], t[1], 4 * out, 4 * W, W)
             inputs = t[2]
         return ops
+
+
+class ConvLayer(Layer):
+    """CNeuronConvOCL (NeuroNet_Core.mqh:17132-17448): strided 1-D convolution over `variables`
+    independent channels, weights [var][window_out][window+1]; no NormalizeWeights after its update."""
+
+    def __init__(self, ctx, window, step, window_out, units, variables=1, activation=NONE, optimization=ADAM,
+                 batch=1, outputs=0):
+        super().__init__(ctx, units * window_out * variables, activation, optimization, batch, outputs)
+        self.window, self.step, self.window_out, self.units, self.variables = window, step, window_out, units, variables
+        n = (window + 1) * window_out * variables
+        self.conv_w = ctx.buffer(n)
+        self.conv_m = ctx.buffer(n)
+        self.conv_v = ctx.buffer(n)
+
+    def set_conv_weights(self, w: np.ndarray) -> None:
+        self.ctx.write(self.conv_w, w)
+
+    def forward_ops(self, prev: Layer) -> list[Op]:
+        k = self.kernel("FeedForwardConv").args(self.conv_w, prev.output, self.output,
+                                                self.per_sample(prev) // self.variables,
+                                                self.step, self.window, self.window_out, self.activation)
+        return [Op(k, (self.units, self.window_out, self.variables))]
+
+    def input_gradient_ops(self, prev: Layer) -> list[Op]:
+        k = self.kernel("CalcHiddenGradientConv").args(self.conv_w, self.gradient, prev.output, prev.gradient,
+                                                       self.neurons // self.variables, self.step, self.window,
+                                                       self.window_out, prev.activation, 0)
+        return [Op(k, (self.per_sample(prev) // self.variables, self.variables))]
+
+    def update_ops(self, prev: Layer) -> list[Op]:
+        n = (self.window + 1) * self.window_out * self.variables
+        k = self.kernel("UpdateWeightsConvAdam").args(self.conv_w, self.gradient, prev.output, self.conv_m,
+                                                      self.conv_v, self.per_sample(prev) // self.variables, LR, B1, B2,
+                                                      self.window, self.window_out, self.step)
+        return [AdamOp(k, (n,), None, self, 6)]
+
+
+class SoftMaxLayer(Layer):
+    """CNeuronSoftMaxOCL (NeuroNet_Core.mqh:20037-20150): softmax over `heads` rows of neurons/heads;
+    no weights of its own."""
+
+    def __init__(self, ctx, neurons, heads=1, batch=1, outputs=0):
+        super().__init__(ctx, neurons, NONE, ADAM, batch, outputs)
+        self.heads = heads
+
+    def forward_ops(self, prev: Layer) -> list[Op]:
+        size = self.neurons // self.heads
+        k = self.kernel("SoftMax_FeedForward").args(prev.output, self.output)
+        return [Op(k, (size, self.heads), (size, 1))]
+
+    def input_gradient_ops(self, prev: Layer) -> list[Op]:
+        size = self.neurons // self.heads
+        k = self.kernel("SoftMax_HiddenGradient").args(self.output, self.gradient, prev.gradient)
+        return [Op(k, (size, self.heads), (size, 1))]
+
+    def output_gradient_ops(self, target: int) -> list[Op]:
+        """calcOutputGradients: the host copies the target into Gradient, then t / y in place."""
+        kc = self.ctx.kernel("Activation").args(target, self.gradient, NONE)
+        if self.batch != 1:
+            kc.batch(self.batch)
+        ko = self.kernel("SoftMax_OutputGradient").args(self.output, self.gradient, self.gradient)
+        return [Op(kc, (self.neurons,)), Op(ko, (self.neurons,))]
+
+
+class BatchNormLayer(Layer):
+    """CNeuronBatchNormOCL (NeuroNet_Core.mqh:19404-19590): online normalisation of every neuron over
+    the last `batch_size` samples, gamma/beta updated once 100*batch_size samples have been seen."""
+
+    def __init__(self, ctx, neurons, batch_size, optimization=ADAM, batch=1, outputs=0):
+        super().__init__(ctx, neurons, NONE, optimization, batch, outputs)
+        self.batch_size = int(batch_size)
+        self.width = 7 if optimization == SGD else 9
+        self.options = ctx.buffer(self.neurons * self.width)
+        self.count = 1  # iBatchCount
+
+    class _BNForward(Op):
+        def __init__(self, kernel, gsize, layer):
+            super().__init__(kernel, gsize)
+            self.layer = layer
+
+        def patches(self):
+            L = self.layer
+            L.count = min(L.count, L.batch_size)
+            n = L.count
+            L.count += L.batch  # one count per sample trained
+            return [(3, n)]
+
+    def forward_ops(self, prev: Layer) -> list[Op]:
+        self.activation = prev.activation if self.batch_size <= 1 else self.activation
+        k = self.kernel("BatchFeedForward").args(prev.output, self.options, self.output, self.count,
+                                                 self.optimization, self.activation, 1)
+        return [BatchNormLayer._BNForward(k, (self.neurons,), self)]
+
+    def input_gradient_ops(self, prev: Layer) -> list[Op]:
+        k = self.kernel("CalcHiddenGradientBatch").args(self.options, self.gradient, prev.output, prev.gradient,
+                                                        prev.activation, self.batch_size, self.optimization)
+        return [_BatchArgOp(k, (self.neurons,), self, 5)]
+
+    def update_ops(self, prev: Layer) -> list[Op]:
+        if self.optimization == SGD:
+            k = self.kernel("UpdateBatchOptionsMomentum").args(self.options, self.gradient, LR, MOMENTUM)
+        else:
+            k = self.kernel("UpdateBatchOptionsAdam").args(self.options, self.gradient, LR, B1, B2)
+        # updateInputWeights runs only once iBatchCount >= 100*iBatchSize; the count is re-capped at
+        # iBatchSize by every forward pass, so with iBatchSize > 1 the gate stays closed, as in the reference.
+        return [_GatedOp(k, (self.neurons,), lambda: self.count >= 100 * self.batch_size)]
+
+
+class _BatchArgOp(Op):
+    """Binds the layer's current sample count (iBatchCount, already advanced by the forward pass, as
+    CNeuronBatchNormOCL::calcInputGradients passes it) before the launch."""
+
+    def __init__(self, kernel, gsize, layer, idx):
+        super().__init__(kernel, gsize)
+        self.layer, self.idx = layer, idx
+
+    def patches(self):
+        return [(self.idx, self.layer.count)]
+
+
+class _GatedOp(Op):
+    """Runs only while `gate()` holds (the BatchNorm update waits for 100 batches)."""
+
+    recordable = False
+
+    def __init__(self, kernel, gsize, gate):
+        super().__init__(kernel, gsize)
+        self.gate = gate
+
+    def __call__(self):
+        if self.gate():
+            super().__call__()
+
+
+class RevINDenormLayer(Layer):
+    """CNeuronRevINDenormOCL (NeuroNet_Core.mqh:23006-23130): de-normalises with the running statistics
+    (options) of a BatchNorm layer elsewhere in the network; no parameters of its own."""
+
+    def __init__(self, ctx, neurons, norm_layer: BatchNormLayer, batch=1, outputs=0):
+        super().__init__(ctx, neurons, NONE, norm_layer.optimization, batch, outputs)
+        self.norm = norm_layer
+
+    def forward_ops(self, prev: Layer) -> list[Op]:
+        k = self.kernel("RevInFeedForward").args(prev.output, self.norm.options, self.output,
+                                                 self.norm.neurons * self.norm.width, self.optimization)
+        return [Op(k, (self.neurons,))]
+
+    def input_gradient_ops(self, prev: Layer) -> list[Op]:
+        k = self.kernel("RevInHiddenGraddient").args(prev.output, prev.gradient, self.norm.options, self.gradient,
+                                                     self.norm.neurons * self.norm.width, self.optimization,
+                                                     prev.activation)
+        return [Op(k, (self.neurons,))]
+
+
+class LSTMLayer(Layer):
+    """CNeuronLSTMOCL (NeuroNet_RecurrentState.mqh:678-897): one time step per forward for `variables`
+    independent series of `hidden` cells; weights [4H][in+H+1]; a batch folds into the series."""
+
+    def __init__(self, ctx, hidden, inputs, variables=1, optimization=ADAM, batch=1, outputs=0):
+        super().__init__(ctx, hidden * variables, NONE, optimization, batch, outputs)
+        self.H, self.inputs, self.variables = hidden, inputs, variables
+        V = variables * batch
+        ws = inputs + hidden + 1
+        n = 4 * hidden * ws
+        self.lstm_w = ctx.buffer(n)
+        self.lstm_m = ctx.buffer(n)
+        self.lstm_v = ctx.buffer(n)
+        self.lstm_wg = ctx.buffer(n)
+        self.memory = ctx.buffer(2 * V * hidden)
+        self.hidden_state = ctx.buffer(V * hidden)
+        self.concatenated = ctx.buffer(V * 4 * hidden)
+        self.concatenated_g = ctx.buffer(V * 4 * hidden)
+
+    def set_lstm_weights(self, w: np.ndarray) -> None:
+        self.ctx.write(self.lstm_w, w)
+
+    def forward_ops(self, prev: Layer) -> list[Op]:
+        k = self.kernel("LSTM_FeedForward").args(prev.output, self.inputs, self.lstm_w, self.concatenated,
+                                                 self.memory, self.output)
+        return [Op(k, (self.H, 4, self.variables), (1, 4, 1))]
+
+    def input_gradient_ops(self, prev: Layer) -> list[Op]:
+        kc = self.kernel("LSTM_ConcatenatedGradient").args(self.gradient, self.concatenated_g, self.memory,
+                                                           self.concatenated)
+        kh = self.kernel("LSTM_HiddenGradient").args(self.concatenated_g, prev.gradient, self.lstm_wg,
+                                                     self.hidden_state, prev.output, self.lstm_w, self.output,
+                                                     self.H, self.inputs)
+        ops = [Op(kc, (self.H, self.variables)), Op(kh, (self.H, self.variables), (1, self.variables))]
+        if prev.activation != NONE:
+            kd = self.ctx.kernel("DeActivation").args(prev.output, prev.gradient, prev.gradient, prev.activation)
+            if prev.batch != 1:
+                kd.batch(prev.batch)
+            ops.append(Op(kd, (prev.neurons,)))
+        return ops
+
+    def update_ops(self, prev: Layer) -> list[Op]:
+        """LSTM_UpdateWeightsAdam over the reference's own NDRange ((in + H*var)/var + 1, H), raw rate."""
+        total = (self.inputs + self.H * self.variables) // self.variables + 1
+        k = self.kernel("LSTM_UpdateWeightsAdam").args(self.lstm_w, self.lstm_wg, self.lstm_m, self.lstm_v, LR, B1, B2)
+        return [Op(k, (total, self.H))]

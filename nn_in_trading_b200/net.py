@@ -48,7 +48,7 @@ class Net:
         ops = list(self.layers[-1].output_gradient_ops(self.target))
         for l in range(len(self.layers) - 2, -1, -1):
             cur, nxt = self.layers[l], self.layers[l + 1]
-            if type(nxt) is DenseLayer:
+            if type(nxt) is DenseLayer:  # CNeuronBaseOCL::CalcHiddenGradients dispatch, NeuroNet_Core.mqh:15988-16014
                 ops += cur.hidden_gradient_ops(nxt)
             else:
                 ops += nxt.input_gradient_ops(cur)
@@ -95,30 +95,34 @@ class Net:
     def capture(self) -> tuple[int, int]:
         """Record the step into two command lists -- forward + backward, and the updates (nothing
         runs while recording).  Two lists so that a data-parallel update region can enclose the
-        second one."""
+        second one.  Per-step scalars (Adam rates, sample counts) are patched at every replay."""
         ctx = self.ctx
-        ctx.record_begin()
-        try:
-            for op in self.fwd_ops + self.bwd_ops:
-                op.kernel.run(op.gsize, op.lsize)
-        finally:
-            self.list_fb = ctx.record_end()
-        self.list_positions = {}
-        ctx.record_begin()
-        try:
-            for pos, op in enumerate(self.upd_ops):
-                if isinstance(op, AdamOp):
-                    self.list_positions[id(op)] = pos
-                op.kernel.run(op.gsize, op.lsize)
-        finally:
-            self.list_upd = ctx.record_end()
+        ops = self.fwd_ops + self.bwd_ops + self.upd_ops
+        if not all(op.recordable for op in ops):
+            raise RuntimeError("this network has steps that cannot be recorded (gated updates); run it eagerly")
+        self.recorded = []
+        lists = []
+        for group in (self.fwd_ops + self.bwd_ops, self.upd_ops):
+            ctx.record_begin()
+            try:
+                for pos, op in enumerate(group):
+                    self.recorded.append((len(lists), pos, op))
+                    op.kernel.run(op.gsize, op.lsize)
+            finally:
+                lists.append(ctx.record_end())
+        self.list_fb, self.list_upd = lists
         self.list_id = (self.list_fb, self.list_upd)
         return self.list_id
 
     def replay(self) -> None:
         ctx = self.ctx
-        for op in self.adam_ops:
-            ctx.list_set_float(self.list_upd, self.list_positions[id(op)], op.l_index, op.next_lt())
+        for li, pos, op in self.recorded:
+            for idx, value in op.patches():
+                lid = self.list_id[li]
+                if op.kernel.sig[idx] == "f":
+                    ctx.list_set_float(lid, pos, idx, value)
+                else:
+                    ctx._check(ctx.lib.nn_cmdlist_set_int(lid, pos, idx, int(value)))
         ctx.run_list(self.list_fb)
         if self.dp:
             ctx.dp_update_begin()

@@ -243,6 +243,21 @@ class OMLMH(OLayer):
             inputs = t[2]
 
 
+class _View:
+    """A layer's output/gradient seen at another batch granularity (same memory)."""
+
+    def __init__(self, layer, batch):
+        self.layer, self.batch = layer, batch
+        self.output = layer.output.reshape(batch, -1)
+        self.gradient = layer.gradient.reshape(batch, -1)
+        self.neurons = self.output.shape[1]
+        self.activation = layer.activation
+
+
+def _as(layer, batch):
+    return layer if layer.batch == batch else _View(layer, batch)
+
+
 class ONet:
     """CNet training step over oracle layers."""
 
@@ -252,7 +267,8 @@ class ONet:
     def forward(self, x):
         self.layers[0].output[...] = x.reshape(self.layers[0].output.shape)
         for l in range(1, len(self.layers)):
-            self.layers[l].forward(self.layers[l - 1])
+            cur = self.layers[l]
+            cur.forward(_as(self.layers[l - 1], cur.batch))
 
     def backward(self, target):
         self.layers[-1].calc_output_gradient(target.reshape(self.layers[-1].output.shape))
@@ -261,13 +277,164 @@ class ONet:
             if type(nxt) is ODense:
                 cur.hidden_gradient(nxt)
             else:
-                nxt.input_gradient(cur)
+                nxt.input_gradient(_as(cur, nxt.batch))
 
     def update(self):
         for l in range(len(self.layers) - 1, 0, -1):
-            self.layers[l].update(self.layers[l - 1])
+            cur = self.layers[l]
+            cur.update(_as(self.layers[l - 1], cur.batch))
 
     def step(self, x, target):
         self.forward(x)
         self.backward(target)
         self.update()
+
+
+def _fold(a, V):
+    """[B][var*H] sample-major buffer viewed as the LSTM's [B*var] series."""
+    return a.reshape(V, -1)
+
+
+class OConv(OLayer):
+    """CNeuronConvOCL (NeuroNet_Core.mqh:17132-17448): no NormalizeWeights after the update."""
+
+    def __init__(self, window, step, window_out, units, variables=1, activation=K.NONE, batch=1, outputs=0):
+        super().__init__(units * window_out * variables, activation, batch)
+        self.window, self.step, self.window_out, self.units, self.variables = window, step, window_out, units, variables
+        n = (window + 1) * window_out * variables
+        self.conv_w, self.conv_m, self.conv_v = np.zeros(n, F32), np.zeros(n, F32), np.zeros(n, F32)
+        self.outputs = outputs
+        if outputs:
+            self.weights = np.zeros(outputs * (self.neurons + 1), F32)
+            self.m = np.zeros_like(self.weights)
+            self.v = np.zeros_like(self.weights)
+
+    def forward(self, prev):
+        for b in range(self.batch):
+            BACKEND.FeedForwardConv(self.conv_w, prev.output[b], self.output[b], prev.neurons // self.variables,
+                                    self.step, self.window, self.window_out, self.activation,
+                                    gsize=(self.units, self.window_out, self.variables))
+
+    def input_gradient(self, prev):
+        for b in range(self.batch):
+            BACKEND.CalcHiddenGradientConv(self.conv_w, self.gradient[b], prev.output[b], prev.gradient[b],
+                                           self.neurons // self.variables, self.step, self.window, self.window_out,
+                                           prev.activation, 0, gsize=(prev.neurons // self.variables, self.variables))
+
+    def update(self, prev):
+        n = self.conv_w.size
+        inputs = prev.neurons // self.variables
+        G = np.mean([K.conv_weight_grad(self.gradient[b], prev.output[b], inputs, self.window, self.window_out,
+                                        self.step, n) for b in range(self.batch)], axis=0, dtype=np.float64).astype(F32)
+        Gabs = np.mean([K.conv_weight_grad(np.abs(self.gradient[b]), np.abs(prev.output[b]), inputs, self.window,
+                                           self.window_out, self.step, n) for b in range(self.batch)], axis=0)
+        if GRAD_HOOK is not None:
+            G = GRAD_HOOK(G)
+        self.last_grad, self.last_grad_abs = G, Gabs
+        K.adam_conv_apply(self.conv_w, G, self.conv_m, self.conv_v, self.next_lt(), B1, B2, n)
+
+    def hidden_gradient(self, nxt):
+        ODense.hidden_gradient(self, nxt)
+
+
+class OBatchNorm(OLayer):
+    """CNeuronBatchNormOCL (NeuroNet_Core.mqh:19404-19590): samples of a batch scanned in order."""
+
+    def __init__(self, neurons, batch_size, batch=1, optimization=K.ADAM, outputs=0):
+        super().__init__(neurons, K.NONE, batch)
+        self.batch_size, self.opt = batch_size, optimization
+        self.width = 7 if optimization == K.SGD else 9
+        self.options = np.zeros(neurons * self.width, F32)
+        self.count = 1
+        self.hist = None
+        self.outputs = outputs
+        if outputs:
+            self.weights = np.zeros(outputs * (neurons + 1), F32)
+            self.m = np.zeros_like(self.weights)
+            self.v = np.zeros_like(self.weights)
+
+    def forward(self, prev):
+        self.count = min(self.count, self.batch_size)
+        n = self.count
+        self.hist = []
+        for b in range(self.batch):
+            BACKEND.BatchFeedForward(prev.output[b], self.options, self.output[b], n, self.opt, self.activation, 1,
+                                     gsize=(self.neurons,))
+            self.hist.append(self.options.reshape(self.neurons, self.width)[:, :3].copy())
+        self.count += self.batch
+
+    def input_gradient(self, prev):
+        for b in range(self.batch):
+            o = self.options.copy().reshape(self.neurons, self.width)
+            if self.batch > 1:
+                o[:, :3] = self.hist[b]
+            BACKEND.CalcHiddenGradientBatch(o.reshape(-1), self.gradient[b], prev.output[b], prev.gradient[b],
+                                            prev.activation, self.count, self.opt, gsize=(self.neurons,))
+
+    def update(self, prev):
+        if self.count < 100 * self.batch_size:  # NeuroNet_Core.mqh:19558
+            return
+        raise NotImplementedError("BatchNorm update gate never opens for batch_size > 1")
+
+    def hidden_gradient(self, nxt):
+        ODense.hidden_gradient(self, nxt)
+
+
+class ORevIN(OLayer):
+    """CNeuronRevINDenormOCL (NeuroNet_Core.mqh:23006-23130)."""
+
+    def __init__(self, neurons, norm: OBatchNorm, batch=1):
+        super().__init__(neurons, K.NONE, batch)
+        self.norm = norm
+
+    def forward(self, prev):
+        for b in range(self.batch):
+            BACKEND.RevInFeedForward(prev.output[b], self.norm.options, self.output[b], self.norm.options.size,
+                                     self.norm.opt, gsize=(self.neurons,))
+
+    def input_gradient(self, prev):
+        for b in range(self.batch):
+            BACKEND.RevInHiddenGraddient(prev.output[b], prev.gradient[b], self.norm.options, self.gradient[b],
+                                         self.norm.options.size, self.norm.opt, prev.activation, gsize=(self.neurons,))
+
+    def update(self, prev):
+        pass
+
+
+class OLSTM(OLayer):
+    """CNeuronLSTMOCL (NeuroNet_RecurrentState.mqh:678-897); a batch folds into the series."""
+
+    def __init__(self, hidden, inputs, variables=1, batch=1):
+        super().__init__(hidden * variables, K.NONE, batch)
+        self.H, self.inputs, self.variables = hidden, inputs, variables
+        V = variables * batch
+        ws = inputs + hidden + 1
+        n = 4 * hidden * ws
+        self.lstm_w, self.lstm_m, self.lstm_v = np.zeros(n, F32), np.zeros(n, F32), np.zeros(n, F32)
+        self.lstm_wg = np.zeros(n, F32)
+        self.memory = np.zeros(2 * V * hidden, F32)
+        self.hidden_state = np.zeros(V * hidden, F32)
+        self.cat = np.zeros(V * 4 * hidden, F32)
+        self.cat_g = np.zeros(V * 4 * hidden, F32)
+
+    def forward(self, prev):
+        V = self.variables * self.batch
+        out = self.output.reshape(-1)
+        BACKEND.LSTM_FeedForward(prev.output.reshape(-1), self.inputs, self.lstm_w, self.cat, self.memory, out,
+                                 gsize=(self.H, 4, V), lsize=(1, 4, 1))
+
+    def input_gradient(self, prev):
+        V = self.variables * self.batch
+        BACKEND.LSTM_ConcatenatedGradient(self.gradient.reshape(-1), self.cat_g, self.memory, self.cat,
+                                          gsize=(self.H, V))
+        pg = prev.gradient.reshape(-1)
+        BACKEND.LSTM_HiddenGradient(self.cat_g, pg, self.lstm_wg, self.hidden_state, prev.output.reshape(-1),
+                                    self.lstm_w, self.output.reshape(-1), self.H, self.inputs, gsize=(self.H, V),
+                                    lsize=(1, V))
+        if prev.activation != K.NONE:
+            K.DeActivation(prev.output.reshape(-1), pg, pg.copy(), prev.activation, gsize=(pg.size,))
+
+    def update(self, prev):
+        total = (self.inputs + self.H * self.variables) // self.variables + 1
+        BACKEND.LSTM_UpdateWeightsAdam(self.lstm_w, self.lstm_wg, self.lstm_m, self.lstm_v, LR, B1, B2,
+                                       gsize=(total, self.H))
