@@ -163,6 +163,26 @@ NN_API int nn_dp_allreduce(int handle, long long offset, long long count, float 
 NN_API int nn_dp_update_begin(void);
 NN_API int nn_dp_update_end(void);
 
+/* ---- update without allocation -------------------------------------------
+ * No counterpart in the reference (its OpenCL buffers are all created by the
+ * host up front).  The batched dense UpdateWeightsAdam -- the same result as
+ * nn_execute of "UpdateWeightsAdam" with global (outputs, inputs+1) and
+ * nn_set_batch(batch) -- on plain device pointers (nn_buffer_device_ptr),
+ * with the weight-gradient partials in a fixed 8 MiB device array inside the
+ * library instead of context scratch, so the call never allocates device
+ * memory (for hosts that give all free memory to their own pool, or that
+ * cannot take an allocation's device-wide stall mid-session).
+ *   matrix_w, matrix_m, matrix_v  [outputs][inputs+1]
+ *   matrix_g [batch][outputs]   matrix_i [batch][inputs]
+ * Runs on the context stream (nn_init first).  outputs*(inputs+1) above
+ * 2,097,152 floats returns NN_ERR_BOUNDS.  The first call on a device sets up
+ * the array's address and should come before any stream capture starts.  The
+ * array is shared by every call on a device: calls that overlap in time race
+ * and must be ordered by the caller. */
+NN_API int nn_update_weights_adam_fixed(float *matrix_w, const float *matrix_g, const float *matrix_i,
+                                        float *matrix_m, float *matrix_v, int outputs, int inputs, int batch,
+                                        float l, float b1, float b2);
+
 #ifdef __cplusplus
 }
 #endif

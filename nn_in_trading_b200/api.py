@@ -81,6 +81,7 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "nn_dp_unique_id": ([c_p], c_int), "nn_dp_init": ([c_int, c_int, c_p], c_int),
         "nn_dp_shutdown": ([], c_int), "nn_dp_allreduce": ([c_int, c_ll, c_ll, c_f], c_int),
         "nn_dp_update_begin": ([], c_int), "nn_dp_update_end": ([], c_int),
+        "nn_update_weights_adam_fixed": ([c_p, c_p, c_p, c_p, c_p, c_int, c_int, c_int, c_f, c_f, c_f], c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

@@ -100,6 +100,10 @@ extern const int kNumAttn2Kernels;
 // Number of data-parallel ranks (1 without a communicator).
 int dp_world();
 
+// Records `msg` as the message nn_last_error returns and gives back `status`
+// (for entry points that run outside a kernel Launch).
+int report_error(int status, const std::string &msg);
+
 const KernelDef *find_kernel(const char *name);
 
 inline unsigned int ceil_div(size_t a, size_t b) { return (unsigned int)((a + b - 1) / b); }

@@ -218,6 +218,8 @@ const KernelDef *find_kernel(const char *name) {
 
 int dp_world() { return g_ctx ? g_ctx->world : 1; }
 
+int report_error(int status, const std::string &msg) { return set_err(status, msg); }
+
 static int run_one(Context *c, const KernelInst &k, const NDR &nd) {
   Launch L;
   L.ctx = c;
