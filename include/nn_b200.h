@@ -69,7 +69,10 @@ extern "C" {
 
 /* ---------------------------------------------------------------- context */
 /* COpenCLMy::Initialize + ContextCreate (NeuroNet_Core.mqh:241-326).
- * device: CUDA ordinal; flags: reserved (0). */
+ * device: CUDA ordinal; flags: 0, or NN_INIT_SIMT_GEMM to run the matrix
+ * products of the dense / convolution / LSTM kernels as FP32 SIMT GEMMs
+ * instead of 3xTF32 tensor-core GEMMs (both meet the 1e-4 parity bound). */
+#define NN_INIT_SIMT_GEMM 1
 NN_API int nn_init(int device, int flags);
 /* COpenCL::Shutdown: frees every buffer, kernel and list of the context. */
 NN_API int nn_shutdown(void);

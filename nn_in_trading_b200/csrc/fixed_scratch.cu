@@ -100,7 +100,7 @@ extern "C" NN_API int nn_update_weights_adam_fixed(float *matrix_w, const float 
   // G[m][n] = sum_b g[b][m] * x[b][n]  (n < inputs), partial per split
   if (N > 0) {
     FastShape fs{outputs, N, batch, 1, splits, kchunk, matrix_g, outputs, 0, matrix_i, inputs, 0};
-    cudaError_t e = sgemm_fast<true, true>(fs, PartialStoreLd{part, outputs, ldp, 1}, stream);
+    cudaError_t e = gemm_f32<true, true>(fs, PartialStoreLd{part, outputs, ldp, 1}, stream);
     if (e != cudaSuccess) return report_error(NN_ERR_CUDA, cudaGetErrorString(e));
   }
   // G[m][inputs] = sum_b g[b][m]  (the bias input is 1)

@@ -8,6 +8,7 @@
 // consecutive copies of that layout and the weights are shared.
 #include "../../include/nn_b200.h"
 #include "gemm_fast.cuh"
+#include "tc_gemm.cuh"
 #include "gemm_simt.cuh"
 #include "nn_device.cuh"
 #include "nn_internal.h"
@@ -53,6 +54,17 @@ struct ConvEpiPlain {
   __device__ __forceinline__ void operator()(int m, int n, int, int, float acc) const {
     o[(size_t)m * wout + n] = activate(acc + nan0(w[(size_t)n * (win + 1) + win]), act);
   }
+  __device__ __forceinline__ long long row(int m, int, int) const { return (long long)m * wout; }
+  __device__ __forceinline__ float col(int n, int) const { return nan0(w[(size_t)n * (win + 1) + win]); }
+  template <int R>
+  __device__ __forceinline__ void put_rows(const long long (&rb)[R], int n, const float (&v)[R], float bias,
+                                           unsigned mask) const {
+    act_dispatch(act, [&](auto A) {
+#pragma unroll
+      for (int j = 0; j < R; ++j)
+        if (mask >> j & 1u) o[rb[j] + n] = activate(v[j] + bias, decltype(A)::value);
+    });
+  }
 };
 
 static int k_feedforward_conv(Launch &L) {
@@ -69,7 +81,7 @@ static int k_feedforward_conv(Launch &L) {
   if (var == 1 && step == win && inputs == units * step && win > 0) {
     // windows tile the input: a plain [B*units][win] x W^T GEMM
     FastShape fs{L.B * units, wout_g, win, 1, 1, 0, x, win, 0, w, win + 1, 0};
-    e = sgemm_fast<false, false>(fs, ConvEpiPlain{w, o, win, wout, act}, L.stream);
+    e = gemm_f32<false, false>(fs, ConvEpiPlain{w, o, win, wout, act}, L.stream);
   } else {
     GemmShape sh{L.B * units, wout_g, win, var, 1};
     e = gemm_simt<true, false>(sh, ConvLoadX{x, units, step, inputs, var}, ConvLoadW{w, win, wout},
@@ -132,6 +144,23 @@ struct CDEpi {
     size_t idx = ((size_t)b * var + v) * inputs + (size_t)k * win + r;
     ig[idx] = deactivate(acc, o[idx], act);
   }
+  __device__ __forceinline__ long long row(int m, int v, int) const {
+    int b = m / n_win, k = m - b * n_win;
+    return ((long long)b * var + v) * inputs + (long long)k * win;
+  }
+  __device__ __forceinline__ float col(int, int) const { return 0.f; }
+  template <int R>
+  __device__ __forceinline__ void put_rows(const long long (&rb)[R], int r, const float (&v)[R], float,
+                                           unsigned mask) const {
+    float y[R];
+#pragma unroll
+    for (int j = 0; j < R; ++j) y[j] = (mask >> j & 1u) ? o[rb[j] + r] : 0.f;
+    act_dispatch(act, [&](auto A) {
+#pragma unroll
+      for (int j = 0; j < R; ++j)
+        if (mask >> j & 1u) ig[rb[j] + r] = deactivate(v[j], y[j], decltype(A)::value);
+    });
+  }
 };
 
 static int k_calc_hidden_gradient_conv(Launch &L) {
@@ -151,7 +180,7 @@ static int k_calc_hidden_gradient_conv(Launch &L) {
     cudaError_t e;
     if (var == 1) {
       FastShape fs{L.B * n_win, win, wout, 1, 1, 0, g, wout, 0, w, win + 1, 0};
-      e = sgemm_fast<false, true>(fs, CDEpi{o, ig, n_win, win, inputs, var, act}, L.stream);
+      e = gemm_f32<false, true>(fs, CDEpi{o, ig, n_win, win, inputs, var, act}, L.stream);
     } else {
       GemmShape sh{L.B * n_win, win, wout, var, 1};
       e = gemm_simt<true, true>(sh, CDLoadG{g, n_win, wout, outputs, var}, CDLoadW{w, win, wout},

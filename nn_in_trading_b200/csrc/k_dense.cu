@@ -7,6 +7,7 @@
 // the last column, stored on the *source* layer (NeuroNet_Core.mqh:15568).
 #include "../../include/nn_b200.h"
 #include "gemm_fast.cuh"
+#include "tc_gemm.cuh"
 #include "gemm_simt.cuh"
 #include "nn_device.cuh"
 #include "nn_internal.h"
@@ -74,6 +75,17 @@ struct FFEpi {
   __device__ __forceinline__ void operator()(int m, int n, int, int, float acc) const {
     y[(size_t)m * outputs + n] = activate(acc + nan0(w[(size_t)n * ld + inputs]), act);
   }
+  __device__ __forceinline__ long long row(int m, int, int) const { return (long long)m * outputs; }
+  __device__ __forceinline__ float col(int n, int) const { return nan0(w[(size_t)n * ld + inputs]); }
+  template <int R>
+  __device__ __forceinline__ void put_rows(const long long (&rb)[R], int n, const float (&v)[R], float bias,
+                                           unsigned mask) const {
+    act_dispatch(act, [&](auto A) {
+#pragma unroll
+      for (int j = 0; j < R; ++j)
+        if (mask >> j & 1u) y[rb[j] + n] = activate(v[j] + bias, decltype(A)::value);
+    });
+  }
 };
 
 __global__ void ff_flags_kernel(const float *w, const float *x, const float *y, float *flags, int inputs,
@@ -113,7 +125,7 @@ static int k_feedforward(Launch &L) {
     NN_CHECK_LAUNCH(L);
   } else {
     FastShape fs{L.B, outputs, inputs, 1, 1, 0, x, inputs, 0, w, ld, 0};
-    cudaError_t e = sgemm_fast<false, false>(fs, FFEpi{w, y, ld, inputs, outputs, act}, L.stream);
+    cudaError_t e = gemm_f32<false, false>(fs, FFEpi{w, y, ld, inputs, outputs, act}, L.stream);
     if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
     L.counted();
   }
@@ -192,6 +204,20 @@ struct CHGEpi {
     size_t idx = (size_t)m * inputs + n;
     ig[idx] = deactivate(acc, o[idx], act);
   }
+  __device__ __forceinline__ long long row(int m, int, int) const { return (long long)m * inputs; }
+  __device__ __forceinline__ float col(int, int) const { return 0.f; }
+  template <int R>
+  __device__ __forceinline__ void put_rows(const long long (&rb)[R], int n, const float (&v)[R], float,
+                                           unsigned mask) const {
+    float yv[R];
+#pragma unroll
+    for (int j = 0; j < R; ++j) yv[j] = (mask >> j & 1u) ? o[rb[j] + n] : 0.f;
+    act_dispatch(act, [&](auto A) {
+#pragma unroll
+      for (int j = 0; j < R; ++j)
+        if (mask >> j & 1u) ig[rb[j] + n] = deactivate(v[j], yv[j], decltype(A)::value);
+    });
+  }
 };
 
 static int k_calc_hidden_gradient(Launch &L) {
@@ -210,7 +236,7 @@ static int k_calc_hidden_gradient(Launch &L) {
     return NN_OK;
   }
   FastShape fs{L.B, inputs, outputs, 1, 1, 0, g, outputs, 0, w, ld, 0};
-  cudaError_t e = sgemm_fast<false, true>(fs, CHGEpi{o, ig, inputs, act}, L.stream);
+  cudaError_t e = gemm_f32<false, true>(fs, CHGEpi{o, ig, inputs, act}, L.stream);
   if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
   L.counted();
   return NN_OK;

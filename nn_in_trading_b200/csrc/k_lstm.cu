@@ -18,6 +18,7 @@
 // when the caller's buffer holds that element.
 #include "../../include/nn_b200.h"
 #include "gemm_fast.cuh"
+#include "tc_gemm.cuh"
 #include "nn_device.cuh"
 #include "nn_internal.h"
 #include "wgrad.cuh"
@@ -180,11 +181,29 @@ struct StoreStrided {
   float *p;
   long long ld;
   __device__ __forceinline__ void operator()(int m, int n, int, int, float acc) const { p[(size_t)m * ld + n] = acc; }
+  __device__ __forceinline__ long long row(int m, int, int) const { return (long long)m * ld; }
+  __device__ __forceinline__ float col(int, int) const { return 0.f; }
+  template <int R>
+  __device__ __forceinline__ void put_rows(const long long (&rb)[R], int n, const float (&v)[R], float,
+                                           unsigned mask) const {
+#pragma unroll
+    for (int j = 0; j < R; ++j)
+      if (mask >> j & 1u) p[rb[j] + n] = v[j];
+  }
 };
 struct StoreInputGrad {
   float *p;
   int in;
   __device__ __forceinline__ void operator()(int m, int n, int, int, float acc) const { p[(size_t)m * in + n] = acc; }
+  __device__ __forceinline__ long long row(int m, int, int) const { return (long long)m * in; }
+  __device__ __forceinline__ float col(int, int) const { return 0.f; }
+  template <int R>
+  __device__ __forceinline__ void put_rows(const long long (&rb)[R], int n, const float (&v)[R], float,
+                                           unsigned mask) const {
+#pragma unroll
+    for (int j = 0; j < R; ++j)
+      if (mask >> j & 1u) p[rb[j] + n] = v[j];
+  }
 };
 
 static int k_lstm_hidden_gradient(Launch &L) {
@@ -207,14 +226,14 @@ static int k_lstm_hidden_gradient(Launch &L) {
   // input gradient: dx[v][j] = sum_g a[v][g] w[g][H+j]
   if (in > 0) {
     FastShape fs{V, in, 4 * H, 1, 1, 0, a, 4LL * H, 0, w + H, ws, 0};
-    cudaError_t e = sgemm_fast<false, true>(fs, StoreInputGrad{ig, in}, L.stream);
+    cudaError_t e = gemm_f32<false, true>(fs, StoreInputGrad{ig, in}, L.stream);
     if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
     L.counted();
   }
   // weight gradient: wg[g][i] = sum_v a[v][g] opnd[v][i], i < H+in (summed over the series)
   {
     FastShape fs{4 * H, H + in, V, 1, 1, 0, a, 4LL * H, 0, opnd, (long long)H + in, 0};
-    cudaError_t e = sgemm_fast<true, true>(fs, StoreStrided{wg, ws}, L.stream);
+    cudaError_t e = gemm_f32<true, true>(fs, StoreStrided{wg, ws}, L.stream);
     if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
     L.counted();
   }

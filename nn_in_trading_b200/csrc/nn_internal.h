@@ -104,6 +104,11 @@ int dp_world();
 // (for entry points that run outside a kernel Launch).
 int report_error(int status, const std::string &msg);
 
+// Device word that kernels with bounded waits set when a wait expires (checked by nn_finish).
+int *device_status();
+// True unless the context was created with NN_INIT_SIMT_GEMM.
+bool tensor_gemm_enabled();
+
 const KernelDef *find_kernel(const char *name);
 
 inline unsigned int ceil_div(size_t a, size_t b) { return (unsigned int)((a + b - 1) / b); }

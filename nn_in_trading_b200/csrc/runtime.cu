@@ -84,6 +84,9 @@ struct Context {
   float *arena = nullptr;
   size_t arena_cap = 0, arena_used = 0;
   std::vector<DeferredOp> deferred;
+  // device status word written by kernels whose bounded waits expired (0 = fine)
+  int *status = nullptr;
+  bool simt_gemm = false;  // NN_INIT_SIMT_GEMM: FP32 SIMT GEMMs instead of 3xTF32 tensor cores
 };
 
 static Context *g_ctx = nullptr;
@@ -220,6 +223,10 @@ int dp_world() { return g_ctx ? g_ctx->world : 1; }
 
 int report_error(int status, const std::string &msg) { return set_err(status, msg); }
 
+int *device_status() { return g_ctx ? g_ctx->status : nullptr; }
+
+bool tensor_gemm_enabled() { return g_ctx && !g_ctx->simt_gemm && g_ctx->status; }
+
 static int run_one(Context *c, const KernelInst &k, const NDR &nd) {
   Launch L;
   L.ctx = c;
@@ -257,8 +264,8 @@ using namespace nn;
 extern "C" {
 
 int nn_init(int device, int flags) {
-  (void)flags;
   if (g_ctx) return set_err(NN_ERR_STATE, "context already initialised");
+  if (flags & ~NN_INIT_SIMT_GEMM) return set_err(NN_ERR_ARG, "nn_init: unknown flag bits");
   int n = 0;
   CUDA_TRY(cudaGetDeviceCount(&n));
   if (device < 0 || device >= n) return set_err(NN_ERR_ARG, "no such CUDA device");
@@ -267,6 +274,15 @@ int nn_init(int device, int flags) {
   c->device = device;
   cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
   if (e != cudaSuccess) {
+    delete c;
+    return set_err(NN_ERR_CUDA, cudaGetErrorString(e));
+  }
+  c->simt_gemm = (flags & NN_INIT_SIMT_GEMM) != 0;
+  e = cudaMalloc(&c->status, 256);
+  if (e == cudaSuccess) e = cudaMemset(c->status, 0, 256);
+  if (e != cudaSuccess) {
+    if (c->status) cudaFree(c->status);
+    cudaStreamDestroy(c->stream);
     delete c;
     return set_err(NN_ERR_CUDA, cudaGetErrorString(e));
   }
@@ -284,6 +300,7 @@ int nn_shutdown(void) {
     if (c->scratch[i]) cudaFree(c->scratch[i]);
   for (auto &kv : c->sides) cudaFree(kv.second.first);
   if (c->arena) cudaFree(c->arena);
+  if (c->status) cudaFree(c->status);
   if (c->comm && c->nccl.comm_destroy) c->nccl.comm_destroy(c->comm);
   cudaStreamDestroy(c->stream);
   delete c;
@@ -302,16 +319,26 @@ int nn_max_local_size(int dim) {
   return 1024;
 }
 
+// After the stream drained: a kernel whose bounded wait expired left a code in the status word.
+static int check_status(Context *c) {
+  int code = 0;
+  CUDA_TRY(cudaMemcpy(&code, c->status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (code == 0) return NN_OK;
+  CUDA_TRY(cudaMemset(c->status, 0, sizeof(int)));
+  return set_err(NN_ERR_TIMEOUT, "a tensor-core GEMM gave up waiting on its pipeline (code " +
+                                     std::to_string(code) + "); its output is incomplete");
+}
+
 int nn_finish(int timeout_ms) {
   NEED_CTX();
   if (timeout_ms <= 0) {
     CUDA_TRY(cudaStreamSynchronize(g_ctx->stream));
-    return NN_OK;
+    return check_status(g_ctx);
   }
   auto t0 = std::chrono::steady_clock::now();
   for (;;) {
     cudaError_t e = cudaStreamQuery(g_ctx->stream);
-    if (e == cudaSuccess) return NN_OK;
+    if (e == cudaSuccess) return check_status(g_ctx);
     if (e != cudaErrorNotReady) return set_err(NN_ERR_CUDA, cudaGetErrorString(e));
     auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count();
     if (ms > timeout_ms) return set_err(NN_ERR_TIMEOUT, "nn_finish: stream still busy after timeout");

@@ -1,0 +1,561 @@
+// FP32 GEMM on the 5th-generation tensor cores (tcgen05, kind::tf32) with the
+// 3xTF32 split, for the same strided operands and per-element epilogue as
+// sgemm_fast (gemm_fast.cuh):
+//   acc[m][n] = sum_k A(m,k) B(k,n)
+//   A(m,k) = A[m*lda + k]  (A_MCONTIG = false, K-major)   or  A[k*lda + m]  (true, MN-major)
+//   B(k,n) = B[n*ldb + k]  (B_NCONTIG = false, K-major)   or  B[k*ldb + n]  (true, MN-major)
+// blockIdx.z enumerates (split, z) exactly as in sgemm_fast.
+//
+// Accuracy.  Every operand x (after nan0) is split into hi = x with its low 13
+// mantissa bits cleared (exactly a TF32 value) and lo = x - hi (exact in FP32);
+// the tile product is lo_A*hi_B + hi_A*lo_B + hi_A*hi_B accumulated in FP32 in
+// tensor memory.  The dropped lo*lo term and the TF32 truncation of lo are
+// below 2^-21 relative per product, the same order as FP32 rounding.
+//
+// Persistent CTAs (one per SM) walk the 128 x BN output tiles, 9 warps each:
+//   warps 4-7  producers: global fp32 -> registers -> nan0 -> hi/lo split ->
+//              shared memory in the tensor cores' canonical layout, one
+//              mbarrier arrive per thread per stage of a STAGES-deep ring.
+//   warp 8     allocates 2*BN tensor-memory columns (two accumulators), issues
+//              the MMAs from one lane (3 per 8-wide k step), releases a stage
+//              with tcgen05.commit, and frees the columns at the end.
+//   warps 0-3  epilogue: tcgen05.ld of their 32 tensor-memory lanes, a
+//              transpose through shared memory, and the epilogue functor with
+//              lanes along n (coalesced stores), while the MMAs of the next
+//              tile run into the other accumulator.
+// Every mbarrier wait is bounded (about one second of clock, plus an
+// iteration cap): on expiry the thread raises a CTA-wide abort flag and writes
+// a code to `err` (read back by nn_finish), and all roles drain to the common
+// exit, where the MMA warp waits (again bounded) for the MMAs it issued
+// before freeing tensor memory.
+//
+// Shared-memory layout of one operand tile (R rows of the MN extent, BK k),
+// per float4 chunk q (a warp's 32 consecutive chunks fill 512 contiguous
+// bytes: no bank conflicts):
+//   K-major, no swizzle (8-row x 16-byte core matrices): chunk q at byte 16*q,
+//     row 8*(q / (2*BK)) + q%8, k 4*((q/8) % (BK/4)); core-matrix strides
+//     K (LBO) 128 B, MN (SBO) 32*BK B.  Global: eight 64-byte row segments.
+//   MN-major, the 128-byte swizzle with 32-byte granules (layout type 1, the
+//     one layout the tensor cores accept for MN-major 32-bit operands): atoms
+//     of 4 k-rows x 32 MN elements (512 B), the four 32-byte granules of row r
+//     of an atom XOR-permuted by r.  Chunk q: atom a = q/32 (k-group
+//     a % (BK/4), MN-group a / (BK/4)), row (q%32)/8, granule/half from q%8.
+//     Strides: MN groups (LBO) 128*BK B, k groups (SBO) 512 B.  Global: four
+//     128-byte row segments.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "gemm_fast.cuh"
+#include "nn_device.cuh"
+#include "nn_internal.h"
+
+namespace nn {
+namespace tc {
+
+constexpr long long kWaitCycles = 2000000000LL;  // ~1 s at 1.9 GHz
+constexpr uint32_t kWaitIters = 1u << 26;
+
+// codes written to the status word
+constexpr int kErrFullWait = 1, kErrEmptyWait = 2, kErrDoneWait = 3;
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity; false on expiry or abort.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
+  const long long t0 = clock64();
+  for (uint32_t it = 0; it < kWaitIters; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitCycles) return false;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Shared-memory matrix descriptor (sm100 version 1): layout 0 = no swizzle, 1 = 128-byte swizzle
+// with 32-byte granules.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | ((uint64_t)(layout & 7u) << 61);
+}
+
+// Byte offset of float4 chunk q in an operand tile, and the (row, k) of its first element.
+template <bool KMAJ, int R, int BK>
+__device__ __forceinline__ uint32_t chunk_place(int q, int &row, int &k) {
+  if (KMAJ) {
+    row = 8 * (q / (2 * BK)) + q % 8;
+    k = 4 * ((q / 8) % (BK / 4));
+    return 16u * (uint32_t)q;
+  }
+  const int a = q / 32, w = q % 32;
+  const int g = a % (BK / 4), h = a / (BK / 4);
+  const int kr = w / 8, c = w % 8;
+  row = 32 * h + 4 * c;
+  k = 4 * g + kr;
+  return (uint32_t)(h * 128 * BK + g * 512 + kr * 128 + (((c >> 1) ^ kr) * 32) + (c & 1) * 16);
+}
+
+// Instruction descriptor of kind::tf32: D f32, A/B tf32, majors, N>>3, M>>4.
+__host__ __device__ constexpr uint32_t instr_desc_tf32(int M, int N, bool a_mn, bool b_mn) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// 32 consecutive fp32 columns of this warp's 32 lanes: v[j] = D[lane][col + j].
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  // the wait names the registers so no use of them can be scheduled before it
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+        "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
+        "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+        "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+      :
+      : "memory");
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+__device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
+
+// One float4 chunk of an operand tile, zero outside [0, rows) x [kbeg, kend).
+//   KMAJ: element (row, k) at G[row*ld + k];  else at G[k*ld + row].
+template <bool KMAJ>
+__device__ __forceinline__ float4 load_chunk(const float *G, long long ld, int row, int k, int rows, int kend,
+                                             bool vec) {
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (KMAJ) {
+    if (row >= rows) return v;
+    const float *p = G + (size_t)row * ld + k;
+    if (vec && k + 3 < kend) return *reinterpret_cast<const float4 *>(p);
+    if (k < kend) v.x = p[0];
+    if (k + 1 < kend) v.y = p[1];
+    if (k + 2 < kend) v.z = p[2];
+    if (k + 3 < kend) v.w = p[3];
+  } else {
+    if (k >= kend) return v;
+    const float *p = G + (size_t)k * ld + row;
+    if (vec && row + 3 < rows) return *reinterpret_cast<const float4 *>(p);
+    if (row < rows) v.x = p[0];
+    if (row + 1 < rows) v.y = p[1];
+    if (row + 2 < rows) v.z = p[2];
+    if (row + 3 < rows) v.w = p[3];
+  }
+  return v;
+}
+
+__device__ __forceinline__ void store_split(uint8_t *hi, uint8_t *lo, uint32_t off, float4 v) {
+  float x[4] = {nan0(v.x), nan0(v.y), nan0(v.z), nan0(v.w)};
+  float4 h = make_float4(tf32_hi(x[0]), tf32_hi(x[1]), tf32_hi(x[2]), tf32_hi(x[3]));
+  float4 l = make_float4(x[0] - h.x, x[1] - h.y, x[2] - h.z, x[3] - h.w);
+  *reinterpret_cast<float4 *>(hi + off) = h;
+  *reinterpret_cast<float4 *>(lo + off) = l;
+}
+
+template <int BN, int BK, int STAGES>
+struct Cfg {
+  static constexpr int BM = 128;
+  static constexpr uint32_t A_BYTES = BM * BK * 4;  // one of hi / lo
+  static constexpr uint32_t B_BYTES = BN * BK * 4;
+  static constexpr uint32_t STAGE_BYTES = 2 * (A_BYTES + B_BYTES);
+  static constexpr uint32_t EPI_OFF = STAGES * STAGE_BYTES;
+  static constexpr uint32_t EPI_BYTES = 4 * 32 * 33 * 4;  // one 32 x 33 transpose buffer per epilogue warp
+  static constexpr uint32_t SMEM = EPI_OFF + EPI_BYTES + 1024;  // + alignment slack
+  static constexpr int A_CHUNKS = BM * BK / 4 / 128;            // float4 chunks per producer thread per stage
+  static constexpr int B_CHUNKS = BN * BK / 4 / 128;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulators: epilogue of one tile || MMAs of the next
+  static_assert(BK % 8 == 0 && BN % 32 == 0 && BN >= 32 && BN <= 256, "tile");
+  static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "swizzle atoms must stay 1024-byte aligned");
+  static_assert((BM * BK / 4) % 128 == 0 && (BN * BK / 4) % 128 == 0, "chunks per thread");
+  static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0 && TMEM_COLS >= 32 && TMEM_COLS <= 512, "tensor-memory columns");
+  static_assert(SMEM <= 232448, "shared memory per CTA");
+};
+
+// Persistent kernel: CTA i processes tiles i, i + gridDim.x, ... (n-tile fastest, so the CTAs in
+// flight share their A rows in L2).  288 threads:
+//   warps 0-3  epilogue (tensor-memory lanes 32w..32w+31 = tile rows), one accumulator at a time
+//   warps 4-7  producers, stage ring of STAGES buffers
+//   warp 8     tensor-memory owner and MMA issuer, alternating two accumulators
+// Epilogue functors give a per-row offset (`row`, computed once per tile by the lane that owns the
+// row and broadcast with shuffles), a per-column constant (`col`, e.g. the bias, once per 32-column
+// chunk), and store 8 rows of one column at a time (`put_rows`: any per-element inputs are loaded
+// for all 8 rows first, and the activation is dispatched once per call, not per element).
+template <int BN, int BK, int STAGES, bool A_MCONTIG, bool B_NCONTIG, class EP>
+__global__ void __launch_bounds__(288, 1)
+    tcgemm_kernel(FastShape s, EP ep, int *err, int vec_a, int vec_b, int tiles_n, int tiles_m, int total) {
+  using C = Cfg<BN, BK, STAGES>;
+  constexpr int BM = C::BM;
+  constexpr bool A_K = !A_MCONTIG, B_K = !B_NCONTIG;
+  // descriptor strides (bytes), layout types and the start offset of each 8-wide k step
+  constexpr uint32_t A_LBO = A_K ? 128u : 128u * BK, A_SBO = A_K ? 32u * BK : 512u;
+  constexpr uint32_t B_LBO = B_K ? 128u : 128u * BK, B_SBO = B_K ? 32u * BK : 512u;
+  constexpr uint32_t A_LAY = A_K ? 0u : 1u, B_LAY = B_K ? 0u : 1u;
+  constexpr uint32_t A_STEP = A_K ? 256u : 1024u, B_STEP = B_K ? 256u : 1024u;
+  constexpr uint32_t IDESC = instr_desc_tf32(BM, BN, A_MCONTIG, B_NCONTIG);
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // swizzle atoms are located by absolute address bits: start the stages on a 1024-byte boundary
+  uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], accf[2], acce[2], drain;
+  __shared__ uint32_t tmem_slot;
+  __shared__ volatile int abort_flag;
+
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int per_z = tiles_m * tiles_n;
+  auto decode = [&](int t, int &m0, int &n0, int &z, int &split, int &kbeg, int &kend, int &nk) {
+    const int zs = t / per_z, rem = t - zs * per_z;
+    m0 = (rem / tiles_n) * BM;
+    n0 = (rem % tiles_n) * BN;
+    z = zs % s.nz;
+    split = zs / s.nz;
+    kbeg = split * s.kchunk;
+    kend = min(s.K, kbeg + s.kchunk);
+    nk = kend > kbeg ? (kend - kbeg + BK - 1) / BK : 0;
+  };
+  auto fail = [&](int code) {
+    abort_flag = 1;
+    atomicExch(err, code);
+  };
+
+  if (tid == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 128);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accf[i], 1);
+      mbar_init(&acce[i], 128);
+    }
+    mbar_init(&drain, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 8) {
+    tmem_alloc(&tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------------------ producers
+    // Stages are loaded one ahead: the global loads of the next stage are in flight while the
+    // current one is split and stored (two register sets, used alternately).
+    const int ptid = tid - 128;
+    struct PState {
+      int t, kk, nk, kbeg, kend, Ma, Nb;
+      const float *Ab, *Bb;
+    };
+    auto start_tile = [&](PState &p) -> bool {
+      for (; p.t < total; p.t += gridDim.x) {
+        int m0, n0, z, split;
+        decode(p.t, m0, n0, z, split, p.kbeg, p.kend, p.nk);
+        if (p.nk == 0) continue;  // nothing to load; the MMA warp signals the empty accumulator
+        const float *A = s.A + (size_t)z * s.strideA;
+        const float *B = s.B + (size_t)z * s.strideB;
+        p.Ab = A + (A_K ? (size_t)m0 * s.lda : (size_t)m0);
+        p.Bb = B + (B_K ? (size_t)n0 * s.ldb : (size_t)n0);
+        p.Ma = s.M - m0;
+        p.Nb = s.N - n0;
+        p.kk = 0;
+        return true;
+      }
+      return false;
+    };
+    auto advance = [&](PState &p) -> bool {
+      if (++p.kk < p.nk) return true;
+      p.t += gridDim.x;
+      return start_tile(p);
+    };
+    auto load = [&](const PState &p, float4 (&va)[C::A_CHUNKS], float4 (&vb)[C::B_CHUNKS]) {
+      const int k0 = p.kbeg + p.kk * BK;
+#pragma unroll
+      for (int i = 0; i < C::A_CHUNKS; ++i) {
+        int row, k;
+        chunk_place<A_K, BM, BK>(ptid + 128 * i, row, k);
+        va[i] = load_chunk<A_K>(p.Ab, s.lda, row, k0 + k, p.Ma, p.kend, vec_a != 0);
+      }
+#pragma unroll
+      for (int i = 0; i < C::B_CHUNKS; ++i) {
+        int row, k;
+        chunk_place<B_K, BN, BK>(ptid + 128 * i, row, k);
+        vb[i] = load_chunk<B_K>(p.Bb, s.ldb, row, k0 + k, p.Nb, p.kend, vec_b != 0);
+      }
+    };
+    int it = 0;
+    auto put = [&](const float4 (&va)[C::A_CHUNKS], const float4 (&vb)[C::B_CHUNKS]) -> bool {
+      const int st = it % STAGES;
+      if (it >= STAGES && !mbar_wait(&empty[st], ((it / STAGES) - 1) & 1, &abort_flag)) {
+        fail(kErrEmptyWait);
+        return false;
+      }
+      uint8_t *base = smem + st * C::STAGE_BYTES;
+      int row, k;
+#pragma unroll
+      for (int i = 0; i < C::A_CHUNKS; ++i)
+        store_split(base, base + C::A_BYTES, chunk_place<A_K, BM, BK>(ptid + 128 * i, row, k), va[i]);
+#pragma unroll
+      for (int i = 0; i < C::B_CHUNKS; ++i)
+        store_split(base + 2 * C::A_BYTES, base + 2 * C::A_BYTES + C::B_BYTES,
+                    chunk_place<B_K, BN, BK>(ptid + 128 * i, row, k), vb[i]);
+      fence_proxy_async_smem();
+      mbar_arrive(&full[st]);
+      ++it;
+      return true;
+    };
+    float4 va0[C::A_CHUNKS], vb0[C::B_CHUNKS], va1[C::A_CHUNKS], vb1[C::B_CHUNKS];
+    PState p;
+    p.t = blockIdx.x;
+    bool have = start_tile(p);
+    if (have) load(p, va0, vb0);
+    while (have && !abort_flag) {
+      have = advance(p);
+      if (have) load(p, va1, vb1);
+      if (!put(va0, vb0) || !have) break;
+      have = advance(p);
+      if (have) load(p, va0, vb0);
+      if (!put(va1, vb1)) break;
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------ MMA issue
+    int it = 0, tl = 0;
+    for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x, ++tl) {
+      int m0, n0, z, split, kbeg, kend, nk;
+      decode(t, m0, n0, z, split, kbeg, kend, nk);
+      const int b = tl & 1, u = tl >> 1;
+      if (tl >= 2 && !mbar_wait(&acce[b], (u - 1) & 1, &abort_flag)) {
+        if (lane == 0) fail(kErrDoneWait);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d = tmem + (uint32_t)(b * BN);
+      bool ok = true;
+      for (int kk = 0; kk < nk; ++kk, ++it) {
+        const int st = it % STAGES;
+        if (!mbar_wait(&full[st], (it / STAGES) & 1, &abort_flag)) {
+          if (lane == 0) fail(kErrFullWait);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t base = smem_u32(smem + st * C::STAGE_BYTES);
+          const uint32_t a_hi = base, a_lo = base + C::A_BYTES;
+          const uint32_t b_hi = base + 2 * C::A_BYTES, b_lo = b_hi + C::B_BYTES;
+          const int kv = min(BK, kend - (kbeg + kk * BK));
+          const int nsub = (kv + 7) / 8;
+          for (int sub = 0; sub < nsub; ++sub) {
+            const uint64_t ah = smem_desc(a_hi + sub * A_STEP, A_LBO, A_SBO, A_LAY);
+            const uint64_t al = smem_desc(a_lo + sub * A_STEP, A_LBO, A_SBO, A_LAY);
+            const uint64_t bh = smem_desc(b_hi + sub * B_STEP, B_LBO, B_SBO, B_LAY);
+            const uint64_t bl = smem_desc(b_lo + sub * B_STEP, B_LBO, B_SBO, B_LAY);
+            mma_tf32(d, al, bh, IDESC, (kk | sub) != 0 ? 1u : 0u);
+            mma_tf32(d, ah, bl, IDESC, 1u);
+            mma_tf32(d, ah, bh, IDESC, 1u);
+          }
+          mma_commit(&empty[st]);
+        }
+        __syncwarp();
+      }
+      if (!ok) break;
+      if (lane == 0) {
+        if (nk > 0)
+          mma_commit(&accf[b]);
+        else
+          mbar_arrive(&accf[b]);
+      }
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    float *buf = reinterpret_cast<float *>(smem + C::EPI_OFF) + warp * 32 * 33;
+    int tl = 0;
+    for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x, ++tl) {
+      int m0, n0, z, split, kbeg, kend, nk;
+      decode(t, m0, n0, z, split, kbeg, kend, nk);
+      const int b = tl & 1, u = tl >> 1;
+      if (!mbar_wait(&accf[b], u & 1, &abort_flag)) {
+        fail(kErrDoneWait);
+        break;
+      }
+      tc_fence_after();
+      const int mw = m0 + warp * 32;
+      const long long my_row = (mw + lane < s.M) ? ep.row(mw + lane, z, split) : 0;
+#pragma unroll 1
+      for (int c = 0; c < BN && n0 + c < s.N; c += 32) {
+        float v[32];
+        if (nk > 0) {
+          tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(b * BN + c), v);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) buf[lane * 33 + j] = v[j];
+        __syncwarp();
+        const int n = n0 + c + lane;
+        const bool col_ok = n < s.N;
+        const int rows = min(32, s.M - mw);
+        const float cv = col_ok ? ep.col(n, z) : 0.f;
+#pragma unroll 1
+        for (int r0 = 0; r0 < 32; r0 += 8) {
+          long long rb[8];
+          float vv[8];
+          unsigned mask = 0;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            rb[j] = __shfl_sync(0xffffffffu, my_row, r0 + j);
+            vv[j] = buf[(r0 + j) * 33 + lane];
+            mask |= (col_ok && r0 + j < rows) ? 1u << j : 0u;
+          }
+          if (mask) ep.put_rows(rb, n, vv, cv, mask);
+        }
+        __syncwarp();
+      }
+      tc_fence_before();
+      mbar_arrive(&acce[b]);
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  if (warp == 8) {
+    // every MMA this thread issued must be complete before its columns are freed
+    if (lane == 0) mma_commit(&drain);
+    __syncwarp();
+    if (!mbar_wait(&drain, 0, &abort_flag) && lane == 0 && !abort_flag) atomicExch(err, kErrDoneWait);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+}  // namespace tc
+
+inline int sm_count() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int BN, int STAGES, bool A_MCONTIG, bool B_NCONTIG, class EP>
+inline cudaError_t tcgemm_launch(const FastShape &s, EP ep, cudaStream_t st, int *err, int va, int vb) {
+  constexpr int BK = 32;
+  using C = tc::Cfg<BN, BK, STAGES>;
+  auto fn = tc::tcgemm_kernel<BN, BK, STAGES, A_MCONTIG, B_NCONTIG, EP>;
+  static bool attr = false;  // per instantiation; setting it twice is harmless
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const int tiles_n = (s.N + BN - 1) / BN, tiles_m = (s.M + 127) / 128;
+  const long long total = (long long)tiles_n * tiles_m * s.nz * s.splits;
+  if (total <= 0) return cudaSuccess;
+  if (total > (1LL << 30)) return cudaErrorInvalidValue;
+  const int grid = (int)(total < sm_count() ? total : sm_count());
+  fn<<<grid, 288, C::SMEM, st>>>(s, ep, err, va, vb, tiles_n, tiles_m, (int)total);
+  return cudaGetLastError();
+}
+
+// Tile width by N (64 when that wastes less), split-K as given in `s`.
+template <bool A_MCONTIG, bool B_NCONTIG, class EP>
+inline cudaError_t tcgemm(FastShape s, EP ep, cudaStream_t st, int *err) {
+  constexpr int BK = 32;
+  if (s.M <= 0 || s.N <= 0 || s.nz <= 0) return cudaSuccess;
+  if (s.splits < 1) s.splits = 1;
+  if (s.kchunk <= 0) s.kchunk = ((s.K + s.splits - 1) / s.splits + BK - 1) / BK * BK;
+  auto aligned = [](const float *p, long long ld) { return ((uintptr_t)p % 16 == 0) && (ld % 4 == 0); };
+  const int va = aligned(s.A, s.lda) && (s.strideA % 4 == 0);
+  const int vb = aligned(s.B, s.ldb) && (s.strideB % 4 == 0);
+  const bool narrow = s.N <= 64 || (s.N % 128 != 0 && s.N % 128 <= 64);
+  if (narrow) return tcgemm_launch<64, 4, A_MCONTIG, B_NCONTIG>(s, ep, st, err, va, vb);
+  return tcgemm_launch<128, 3, A_MCONTIG, B_NCONTIG>(s, ep, st, err, va, vb);
+}
+
+// The FP32 GEMM of a call site: 3xTF32 tensor cores unless the context was created with
+// NN_INIT_SIMT_GEMM or the product is too small for a 128-row tile to pay off.
+template <bool A_MCONTIG, bool B_NCONTIG, class EP>
+inline cudaError_t gemm_f32(FastShape s, EP ep, cudaStream_t st) {
+  if (tensor_gemm_enabled() && s.M >= 64 && (long long)s.M * s.N * s.K >= (1LL << 20))
+    return tcgemm<A_MCONTIG, B_NCONTIG>(s, ep, st, device_status());
+  return sgemm_fast<A_MCONTIG, B_NCONTIG>(s, ep, st);
+}
+
+}  // namespace nn

@@ -7,6 +7,7 @@
 // instead, averaged over ranks, and applied afterwards.
 #pragma once
 #include "gemm_fast.cuh"
+#include "tc_gemm.cuh"
 #include "gemm_simt.cuh"
 #include "nn_device.cuh"
 #include "nn_internal.h"
@@ -44,6 +45,17 @@ struct PartialStoreLd {
   __device__ void operator()(int m, int n, int z, int split, float acc) const {
     p[(((size_t)split * nz + z) * M + m) * ldp + n] = acc;
   }
+  __device__ __forceinline__ long long row(int m, int z, int split) const {
+    return (((long long)split * nz + z) * M + m) * ldp;
+  }
+  __device__ __forceinline__ float col(int, int) const { return 0.f; }
+  template <int R>
+  __device__ __forceinline__ void put_rows(const long long (&rb)[R], int n, const float (&v)[R], float,
+                                           unsigned mask) const {
+#pragma unroll
+    for (int j = 0; j < R; ++j)
+      if (mask >> j & 1u) p[rb[j] + n] = v[j];
+  }
 };
 
 // Bias column of a weight gradient: per split, sum over the split's reduction
@@ -64,7 +76,7 @@ inline int wgrad_fast(Launch &L, const float *A, long long lda, const float *X, 
   float *part = L.scratch(0, per * splits);
   if (!part) return NN_ERR_CUDA;
   FastShape fs{M, N, rows, 1, splits, kchunk, A, lda, 0, X, ldx, 0};
-  cudaError_t e = sgemm_fast<true, true>(fs, PartialStoreLd{part, M, ldp, 1}, L.stream);
+  cudaError_t e = gemm_f32<true, true>(fs, PartialStoreLd{part, M, ldp, 1}, L.stream);
   if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
   L.counted();
   dim3 grid((M + 255) / 256, splits);
