@@ -28,6 +28,9 @@ struct FastShape {
   long long lda, strideA;
   const float *B;
   long long ldb, strideB;
+  // Tensor-core path only: when >= 0, column `ones_col` of B is all ones (not read from memory) and
+  // B holds ones_col real columns -- the bias input of a weight gradient folded into the GEMM.
+  int ones_col = -1;
 };
 
 template <int BN, bool A_MCONTIG, bool B_NCONTIG, bool VEC_A, bool VEC_B, class EP>

@@ -65,6 +65,23 @@ struct ConvEpiPlain {
         if (mask >> j & 1u) o[rb[j] + n] = activate(v[j] + bias, decltype(A)::value);
     });
   }
+  __host__ __device__ bool aligned4() const { return wout % 4 == 0 && ((uintptr_t)o & 15) == 0; }
+  __device__ __forceinline__ float4 col4(int n, int z) const {
+    return make_float4(col(n, z), col(n + 1, z), col(n + 2, z), col(n + 3, z));
+  }
+  template <int R>
+  __device__ __forceinline__ void put_rows4(const long long (&rb)[R], int n, const float4 (&v)[R], float4 b,
+                                            unsigned mask) const {
+    act_dispatch(act, [&](auto A) {
+      constexpr int a = decltype(A)::value;
+#pragma unroll
+      for (int j = 0; j < R; ++j)
+        if (mask >> j & 1u)
+          *reinterpret_cast<float4 *>(o + rb[j] + n) = make_float4(
+              activate(v[j].x + b.x, a), activate(v[j].y + b.y, a), activate(v[j].z + b.z, a),
+              activate(v[j].w + b.w, a));
+    });
+  }
 };
 
 static int k_feedforward_conv(Launch &L) {
@@ -81,7 +98,7 @@ static int k_feedforward_conv(Launch &L) {
   if (var == 1 && step == win && inputs == units * step && win > 0) {
     // windows tile the input: a plain [B*units][win] x W^T GEMM
     FastShape fs{L.B * units, wout_g, win, 1, 1, 0, x, win, 0, w, win + 1, 0};
-    e = gemm_f32<false, false>(fs, ConvEpiPlain{w, o, win, wout, act}, L.stream);
+    e = gemm_f32_wb<false, false>(L, fs, ConvEpiPlain{w, o, win, wout, act});
   } else {
     GemmShape sh{L.B * units, wout_g, win, var, 1};
     e = gemm_simt<true, false>(sh, ConvLoadX{x, units, step, inputs, var}, ConvLoadW{w, win, wout},
@@ -161,6 +178,27 @@ struct CDEpi {
         if (mask >> j & 1u) ig[rb[j] + r] = deactivate(v[j], y[j], decltype(A)::value);
     });
   }
+  __host__ __device__ bool aligned4() const {
+    return inputs % 4 == 0 && win % 4 == 0 && ((uintptr_t)o & 15) == 0 && ((uintptr_t)ig & 15) == 0;
+  }
+  __device__ __forceinline__ float4 col4(int, int) const { return make_float4(0.f, 0.f, 0.f, 0.f); }
+  template <int R>
+  __device__ __forceinline__ void put_rows4(const long long (&rb)[R], int r, const float4 (&v)[R], float4,
+                                            unsigned mask) const {
+    float4 y[R];
+#pragma unroll
+    for (int j = 0; j < R; ++j)
+      y[j] = (mask >> j & 1u) ? *reinterpret_cast<const float4 *>(o + rb[j] + r) : make_float4(0.f, 0.f, 0.f, 0.f);
+    act_dispatch(act, [&](auto A) {
+      constexpr int a = decltype(A)::value;
+#pragma unroll
+      for (int j = 0; j < R; ++j)
+        if (mask >> j & 1u)
+          *reinterpret_cast<float4 *>(ig + rb[j] + r) =
+              make_float4(deactivate(v[j].x, y[j].x, a), deactivate(v[j].y, y[j].y, a),
+                          deactivate(v[j].z, y[j].z, a), deactivate(v[j].w, y[j].w, a));
+    });
+  }
 };
 
 static int k_calc_hidden_gradient_conv(Launch &L) {
@@ -180,7 +218,7 @@ static int k_calc_hidden_gradient_conv(Launch &L) {
     cudaError_t e;
     if (var == 1) {
       FastShape fs{L.B * n_win, win, wout, 1, 1, 0, g, wout, 0, w, win + 1, 0};
-      e = gemm_f32<false, true>(fs, CDEpi{o, ig, n_win, win, inputs, var, act}, L.stream);
+      e = gemm_f32_wb<false, true>(L, fs, CDEpi{o, ig, n_win, win, inputs, var, act});
     } else {
       GemmShape sh{L.B * n_win, win, wout, var, 1};
       e = gemm_simt<true, true>(sh, CDLoadG{g, n_win, wout, outputs, var}, CDLoadW{w, win, wout},

@@ -86,6 +86,23 @@ struct FFEpi {
         if (mask >> j & 1u) y[rb[j] + n] = activate(v[j] + bias, decltype(A)::value);
     });
   }
+  __host__ __device__ bool aligned4() const { return outputs % 4 == 0 && ((uintptr_t)y & 15) == 0; }
+  __device__ __forceinline__ float4 col4(int n, int z) const {
+    return make_float4(col(n, z), col(n + 1, z), col(n + 2, z), col(n + 3, z));
+  }
+  template <int R>
+  __device__ __forceinline__ void put_rows4(const long long (&rb)[R], int n, const float4 (&v)[R], float4 b,
+                                            unsigned mask) const {
+    act_dispatch(act, [&](auto A) {
+      constexpr int a = decltype(A)::value;
+#pragma unroll
+      for (int j = 0; j < R; ++j)
+        if (mask >> j & 1u)
+          *reinterpret_cast<float4 *>(y + rb[j] + n) = make_float4(
+              activate(v[j].x + b.x, a), activate(v[j].y + b.y, a), activate(v[j].z + b.z, a),
+              activate(v[j].w + b.w, a));
+    });
+  }
 };
 
 __global__ void ff_flags_kernel(const float *w, const float *x, const float *y, float *flags, int inputs,
@@ -125,7 +142,7 @@ static int k_feedforward(Launch &L) {
     NN_CHECK_LAUNCH(L);
   } else {
     FastShape fs{L.B, outputs, inputs, 1, 1, 0, x, inputs, 0, w, ld, 0};
-    cudaError_t e = gemm_f32<false, false>(fs, FFEpi{w, y, ld, inputs, outputs, act}, L.stream);
+    cudaError_t e = gemm_f32_wb<false, false>(L, fs, FFEpi{w, y, ld, inputs, outputs, act});
     if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
     L.counted();
   }
@@ -218,6 +235,27 @@ struct CHGEpi {
         if (mask >> j & 1u) ig[rb[j] + n] = deactivate(v[j], yv[j], decltype(A)::value);
     });
   }
+  __host__ __device__ bool aligned4() const {
+    return inputs % 4 == 0 && ((uintptr_t)o & 15) == 0 && ((uintptr_t)ig & 15) == 0;
+  }
+  __device__ __forceinline__ float4 col4(int, int) const { return make_float4(0.f, 0.f, 0.f, 0.f); }
+  template <int R>
+  __device__ __forceinline__ void put_rows4(const long long (&rb)[R], int n, const float4 (&v)[R], float4,
+                                            unsigned mask) const {
+    float4 yv[R];
+#pragma unroll
+    for (int j = 0; j < R; ++j)
+      yv[j] = (mask >> j & 1u) ? *reinterpret_cast<const float4 *>(o + rb[j] + n) : make_float4(0.f, 0.f, 0.f, 0.f);
+    act_dispatch(act, [&](auto A) {
+      constexpr int a = decltype(A)::value;
+#pragma unroll
+      for (int j = 0; j < R; ++j)
+        if (mask >> j & 1u)
+          *reinterpret_cast<float4 *>(ig + rb[j] + n) =
+              make_float4(deactivate(v[j].x, yv[j].x, a), deactivate(v[j].y, yv[j].y, a),
+                          deactivate(v[j].z, yv[j].z, a), deactivate(v[j].w, yv[j].w, a));
+    });
+  }
 };
 
 static int k_calc_hidden_gradient(Launch &L) {
@@ -236,7 +274,7 @@ static int k_calc_hidden_gradient(Launch &L) {
     return NN_OK;
   }
   FastShape fs{L.B, inputs, outputs, 1, 1, 0, g, outputs, 0, w, ld, 0};
-  cudaError_t e = gemm_f32<false, true>(fs, CHGEpi{o, ig, inputs, act}, L.stream);
+  cudaError_t e = gemm_f32_wb<false, true>(L, fs, CHGEpi{o, ig, inputs, act});
   if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
   L.counted();
   return NN_OK;

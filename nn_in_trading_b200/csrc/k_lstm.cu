@@ -190,6 +190,15 @@ struct StoreStrided {
     for (int j = 0; j < R; ++j)
       if (mask >> j & 1u) p[rb[j] + n] = v[j];
   }
+  __host__ __device__ bool aligned4() const { return (ld) % 4 == 0 && ((uintptr_t)p & 15) == 0; }
+  __device__ __forceinline__ float4 col4(int, int) const { return make_float4(0.f, 0.f, 0.f, 0.f); }
+  template <int R>
+  __device__ __forceinline__ void put_rows4(const long long (&rb)[R], int n, const float4 (&v)[R], float4,
+                                            unsigned mask) const {
+#pragma unroll
+    for (int j = 0; j < R; ++j)
+      if (mask >> j & 1u) *reinterpret_cast<float4 *>(p + rb[j] + n) = v[j];
+  }
 };
 struct StoreInputGrad {
   float *p;
@@ -203,6 +212,15 @@ struct StoreInputGrad {
 #pragma unroll
     for (int j = 0; j < R; ++j)
       if (mask >> j & 1u) p[rb[j] + n] = v[j];
+  }
+  __host__ __device__ bool aligned4() const { return (in) % 4 == 0 && ((uintptr_t)p & 15) == 0; }
+  __device__ __forceinline__ float4 col4(int, int) const { return make_float4(0.f, 0.f, 0.f, 0.f); }
+  template <int R>
+  __device__ __forceinline__ void put_rows4(const long long (&rb)[R], int n, const float4 (&v)[R], float4,
+                                            unsigned mask) const {
+#pragma unroll
+    for (int j = 0; j < R; ++j)
+      if (mask >> j & 1u) *reinterpret_cast<float4 *>(p + rb[j] + n) = v[j];
   }
 };
 
@@ -226,7 +244,7 @@ static int k_lstm_hidden_gradient(Launch &L) {
   // input gradient: dx[v][j] = sum_g a[v][g] w[g][H+j]
   if (in > 0) {
     FastShape fs{V, in, 4 * H, 1, 1, 0, a, 4LL * H, 0, w + H, ws, 0};
-    cudaError_t e = gemm_f32<false, true>(fs, StoreInputGrad{ig, in}, L.stream);
+    cudaError_t e = gemm_f32_wb<false, true>(L, fs, StoreInputGrad{ig, in});
     if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
     L.counted();
   }

@@ -10,6 +10,7 @@
 namespace nn {
 
 constexpr int kMaxArgs = 16;
+constexpr int kScratchSlots = 5;
 
 enum ArgType : uint8_t { ARG_UNSET = 0, ARG_BUF, ARG_INT, ARG_FLOAT };
 
@@ -53,7 +54,8 @@ struct Launch {
   int i(int idx) const { return k->args[idx].i; }
   float f(int idx) const { return k->args[idx].f; }
   int fail(int status, const std::string &msg);
-  // Per-context scratch of at least `floats` floats (slot 0..3 independent).
+  // Per-context scratch of at least `floats` floats (slots 0..kScratchSlots-1 independent; slot 4
+  // holds the packed weight operand of the tensor-core GEMMs).
   float *scratch(int slot, size_t floats);
   // Persistent side buffer attached to a buffer handle (created or grown on
   // demand, lives until the handle is freed); `fresh` tells whether it was (re)made.

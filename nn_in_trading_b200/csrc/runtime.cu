@@ -72,8 +72,8 @@ struct Context {
   std::vector<CmdList> lists;
   bool recording = false;
   std::vector<Recorded> rec;
-  float *scratch[4] = {nullptr, nullptr, nullptr, nullptr};
-  size_t scratch_n[4] = {0, 0, 0, 0};
+  float *scratch[kScratchSlots] = {};
+  size_t scratch_n[kScratchSlots] = {};
   std::unordered_map<int, std::pair<float *, size_t>> sides;  // side buffers keyed by buffer handle
   long long launches = 0;
   // data parallel
@@ -296,7 +296,7 @@ int nn_shutdown(void) {
   cudaStreamSynchronize(c->stream);
   for (Buffer &b : c->bufs)
     if (b.live) cudaFree(b.ptr);
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < kScratchSlots; ++i)
     if (c->scratch[i]) cudaFree(c->scratch[i]);
   for (auto &kv : c->sides) cudaFree(kv.second.first);
   if (c->arena) cudaFree(c->arena);

@@ -95,6 +95,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
   return false;
 }
 
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+// One contiguous global -> shared copy by the bulk-copy engine, counted on `bar` (no multicast).
+__device__ __forceinline__ void bulk_copy_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
@@ -186,13 +198,21 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 
 __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
 
-// One float4 chunk of an operand tile, zero outside [0, rows) x [kbeg, kend).
+// One float4 chunk of an operand tile, zero outside [0, rows) x [kbeg, kend), and 1 in row
+// `ones_row` (for k < kend) when that row is the all-ones column of B.
 //   KMAJ: element (row, k) at G[row*ld + k];  else at G[k*ld + row].
 template <bool KMAJ>
 __device__ __forceinline__ float4 load_chunk(const float *G, long long ld, int row, int k, int rows, int kend,
-                                             bool vec) {
+                                             bool vec, int ones_row = -1) {
   float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
   if (KMAJ) {
+    if (row == ones_row) {
+      v.x = k < kend ? 1.f : 0.f;
+      v.y = k + 1 < kend ? 1.f : 0.f;
+      v.z = k + 2 < kend ? 1.f : 0.f;
+      v.w = k + 3 < kend ? 1.f : 0.f;
+      return v;
+    }
     if (row >= rows) return v;
     const float *p = G + (size_t)row * ld + k;
     if (vec && k + 3 < kend) return *reinterpret_cast<const float4 *>(p);
@@ -208,6 +228,8 @@ __device__ __forceinline__ float4 load_chunk(const float *G, long long ld, int r
     if (row + 1 < rows) v.y = p[1];
     if (row + 2 < rows) v.z = p[2];
     if (row + 3 < rows) v.w = p[3];
+    const int o = ones_row - row;
+    if (o >= 0 && o < 4) (&v.x)[o] = 1.f;
   }
   return v;
 }
@@ -227,7 +249,7 @@ struct Cfg {
   static constexpr uint32_t B_BYTES = BN * BK * 4;
   static constexpr uint32_t STAGE_BYTES = 2 * (A_BYTES + B_BYTES);
   static constexpr uint32_t EPI_OFF = STAGES * STAGE_BYTES;
-  static constexpr uint32_t EPI_BYTES = 4 * 32 * 33 * 4;  // one 32 x 33 transpose buffer per epilogue warp
+  static constexpr uint32_t EPI_BYTES = 4 * 32 * 36 * 4;  // one 32 x 36 transpose buffer per epilogue warp
   static constexpr uint32_t SMEM = EPI_OFF + EPI_BYTES + 1024;  // + alignment slack
   static constexpr int A_CHUNKS = BM * BK / 4 / 128;            // float4 chunks per producer thread per stage
   static constexpr int B_CHUNKS = BN * BK / 4 / 128;
@@ -247,10 +269,14 @@ struct Cfg {
 // Epilogue functors give a per-row offset (`row`, computed once per tile by the lane that owns the
 // row and broadcast with shuffles), a per-column constant (`col`, e.g. the bias, once per 32-column
 // chunk), and store 8 rows of one column at a time (`put_rows`: any per-element inputs are loaded
-// for all 8 rows first, and the activation is dispatched once per call, not per element).
-template <int BN, int BK, int STAGES, bool A_MCONTIG, bool B_NCONTIG, class EP>
+// for all 8 rows first, and the activation is dispatched once per call, not per element).  When
+// every output row starts on a 16-byte boundary (`aligned4`, checked on the host) full 32-column
+// chunks go out as float4s instead (`col4` / `put_rows4`: a lane stores 4 columns of 8 rows, a warp
+// instruction 4 rows x 128 bytes).
+template <int BN, int BK, int STAGES, bool A_MCONTIG, bool B_NCONTIG, bool PACKED_B, class EP>
 __global__ void __launch_bounds__(288, 1)
-    tcgemm_kernel(FastShape s, EP ep, int *err, int vec_a, int vec_b, int tiles_n, int tiles_m, int total) {
+    tcgemm_kernel(FastShape s, EP ep, int *err, int vec_a, int vec_b, int vec_out, int tiles_n, int tiles_m,
+                  int total, const uint8_t *bimg, int kstages) {
   using C = Cfg<BN, BK, STAGES>;
   constexpr int BM = C::BM;
   constexpr bool A_K = !A_MCONTIG, B_K = !B_NCONTIG;
@@ -313,9 +339,10 @@ __global__ void __launch_bounds__(288, 1)
     // current one is split and stored (two register sets, used alternately).
     const int ptid = tid - 128;
     struct PState {
-      int t, kk, nk, kbeg, kend, Ma, Nb;
+      int t, kk, nk, kbeg, kend, Ma, Nb, ones, nt;
       const float *Ab, *Bb;
     };
+    const int n_real = s.ones_col >= 0 ? s.ones_col : s.N;
     auto start_tile = [&](PState &p) -> bool {
       for (; p.t < total; p.t += gridDim.x) {
         int m0, n0, z, split;
@@ -326,7 +353,9 @@ __global__ void __launch_bounds__(288, 1)
         p.Ab = A + (A_K ? (size_t)m0 * s.lda : (size_t)m0);
         p.Bb = B + (B_K ? (size_t)n0 * s.ldb : (size_t)n0);
         p.Ma = s.M - m0;
-        p.Nb = s.N - n0;
+        p.Nb = n_real - n0;
+        p.ones = s.ones_col >= 0 ? s.ones_col - n0 : -1;
+        p.nt = n0 / BN;
         p.kk = 0;
         return true;
       }
@@ -345,29 +374,39 @@ __global__ void __launch_bounds__(288, 1)
         chunk_place<A_K, BM, BK>(ptid + 128 * i, row, k);
         va[i] = load_chunk<A_K>(p.Ab, s.lda, row, k0 + k, p.Ma, p.kend, vec_a != 0);
       }
+      if (!PACKED_B) {
 #pragma unroll
-      for (int i = 0; i < C::B_CHUNKS; ++i) {
-        int row, k;
-        chunk_place<B_K, BN, BK>(ptid + 128 * i, row, k);
-        vb[i] = load_chunk<B_K>(p.Bb, s.ldb, row, k0 + k, p.Nb, p.kend, vec_b != 0);
+        for (int i = 0; i < C::B_CHUNKS; ++i) {
+          int row, k;
+          chunk_place<B_K, BN, BK>(ptid + 128 * i, row, k);
+          vb[i] = load_chunk<B_K>(p.Bb, s.ldb, row, k0 + k, p.Nb, p.kend, vec_b != 0, p.ones);
+        }
       }
     };
     int it = 0;
-    auto put = [&](const float4 (&va)[C::A_CHUNKS], const float4 (&vb)[C::B_CHUNKS]) -> bool {
+    auto put = [&](const PState &p, const float4 (&va)[C::A_CHUNKS], const float4 (&vb)[C::B_CHUNKS]) -> bool {
       const int st = it % STAGES;
       if (it >= STAGES && !mbar_wait(&empty[st], ((it / STAGES) - 1) & 1, &abort_flag)) {
         fail(kErrEmptyWait);
         return false;
       }
       uint8_t *base = smem + st * C::STAGE_BYTES;
+      if (PACKED_B && ptid == 0) {
+        // the weight tile of this stage, already split and laid out, in one bulk copy
+        const size_t img = ((size_t)p.nt * kstages + (p.kbeg / BK + p.kk)) * (2 * C::B_BYTES);
+        mbar_expect_tx(&full[st], 2 * C::B_BYTES);
+        bulk_copy_g2s(base + 2 * C::A_BYTES, bimg + img, 2 * C::B_BYTES, &full[st]);
+      }
       int row, k;
 #pragma unroll
       for (int i = 0; i < C::A_CHUNKS; ++i)
         store_split(base, base + C::A_BYTES, chunk_place<A_K, BM, BK>(ptid + 128 * i, row, k), va[i]);
+      if (!PACKED_B) {
 #pragma unroll
-      for (int i = 0; i < C::B_CHUNKS; ++i)
-        store_split(base + 2 * C::A_BYTES, base + 2 * C::A_BYTES + C::B_BYTES,
-                    chunk_place<B_K, BN, BK>(ptid + 128 * i, row, k), vb[i]);
+        for (int i = 0; i < C::B_CHUNKS; ++i)
+          store_split(base + 2 * C::A_BYTES, base + 2 * C::A_BYTES + C::B_BYTES,
+                      chunk_place<B_K, BN, BK>(ptid + 128 * i, row, k), vb[i]);
+      }
       fence_proxy_async_smem();
       mbar_arrive(&full[st]);
       ++it;
@@ -378,13 +417,16 @@ __global__ void __launch_bounds__(288, 1)
     p.t = blockIdx.x;
     bool have = start_tile(p);
     if (have) load(p, va0, vb0);
+    PState cur;
     while (have && !abort_flag) {
+      cur = p;
       have = advance(p);
       if (have) load(p, va1, vb1);
-      if (!put(va0, vb0) || !have) break;
+      if (!put(cur, va0, vb0) || !have) break;
+      cur = p;
       have = advance(p);
       if (have) load(p, va0, vb0);
-      if (!put(va1, vb1)) break;
+      if (!put(cur, va1, vb1)) break;
     }
   } else if (warp == 8) {
     // ------------------------------------------------------------ MMA issue
@@ -438,7 +480,7 @@ __global__ void __launch_bounds__(288, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    float *buf = reinterpret_cast<float *>(smem + C::EPI_OFF) + warp * 32 * 33;
+    float *buf = reinterpret_cast<float *>(smem + C::EPI_OFF) + warp * 32 * 36;
     int tl = 0;
     for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x, ++tl) {
       int m0, n0, z, split, kbeg, kend, nk;
@@ -460,25 +502,45 @@ __global__ void __launch_bounds__(288, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = 0.f;
         }
+        // row `lane` of the chunk -> shared row `lane` (36-float stride: conflict-free float4 traffic)
 #pragma unroll
-        for (int j = 0; j < 32; ++j) buf[lane * 33 + j] = v[j];
+        for (int q = 0; q < 8; ++q)
+          *reinterpret_cast<float4 *>(&buf[lane * 36 + 4 * q]) =
+              make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
         __syncwarp();
-        const int n = n0 + c + lane;
-        const bool col_ok = n < s.N;
         const int rows = min(32, s.M - mw);
-        const float cv = col_ok ? ep.col(n, z) : 0.f;
-#pragma unroll 1
-        for (int r0 = 0; r0 < 32; r0 += 8) {
+        if (vec_out && n0 + c + 32 <= s.N) {
+          const int cq = lane & 7, rs = lane >> 3;
+          const int n = n0 + c + 4 * cq;
+          const float4 cv = ep.col4(n, z);
           long long rb[8];
-          float vv[8];
+          float4 vv[8];
           unsigned mask = 0;
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            rb[j] = __shfl_sync(0xffffffffu, my_row, r0 + j);
-            vv[j] = buf[(r0 + j) * 33 + lane];
-            mask |= (col_ok && r0 + j < rows) ? 1u << j : 0u;
+            const int r = rs + 4 * j;
+            rb[j] = __shfl_sync(0xffffffffu, my_row, r);
+            vv[j] = *reinterpret_cast<const float4 *>(&buf[r * 36 + 4 * cq]);
+            mask |= r < rows ? 1u << j : 0u;
           }
-          if (mask) ep.put_rows(rb, n, vv, cv, mask);
+          if (mask) ep.put_rows4(rb, n, vv, cv, mask);
+        } else {
+          const int n = n0 + c + lane;
+          const bool col_ok = n < s.N;
+          const float cv = col_ok ? ep.col(n, z) : 0.f;
+#pragma unroll 1
+          for (int r0 = 0; r0 < 32; r0 += 8) {
+            long long rb[8];
+            float vv[8];
+            unsigned mask = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              rb[j] = __shfl_sync(0xffffffffu, my_row, r0 + j);
+              vv[j] = buf[(r0 + j) * 36 + lane];
+              mask |= (col_ok && r0 + j < rows) ? 1u << j : 0u;
+            }
+            if (mask) ep.put_rows(rb, n, vv, cv, mask);
+          }
         }
         __syncwarp();
       }
@@ -502,6 +564,27 @@ __global__ void __launch_bounds__(288, 1)
   }
 }
 
+// Weight operand image for PACKED_B: for every (n-tile, k-stage) the split hi and lo tiles exactly as
+// a stage holds them in shared memory ([hi: BN*BK floats][lo: BN*BK floats]), so that one bulk copy
+// fills a stage.  One thread per float4 chunk of the image.
+template <int BN, int BK, bool B_K>
+__global__ void pack_b_kernel(const float *B, long long ldb, int N, int K, uint8_t *img, int tiles_n,
+                              int kstages) {
+  constexpr int CH = BN * BK / 4;  // chunks per tile image half
+  const long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (t >= (long long)tiles_n * kstages * CH) return;
+  const int q = (int)(t % CH);
+  const long long tile = t / CH;  // nt * kstages + ks
+  const int nt = (int)(tile / kstages), ks = (int)(tile % kstages);
+  int row, k;
+  const uint32_t off = chunk_place<B_K, BN, BK>(q, row, k);
+  const int n0 = nt * BN;
+  const float *Bb = B + (B_K ? (size_t)n0 * ldb : (size_t)n0);
+  const float4 v = load_chunk<B_K>(Bb, ldb, row, ks * BK + k, N - n0, K, false);
+  uint8_t *hi = img + (size_t)tile * (2 * BN * BK * 4);
+  store_split(hi, hi + BN * BK * 4, off, v);
+}
+
 }  // namespace tc
 
 inline int sm_count() {
@@ -514,11 +597,22 @@ inline int sm_count() {
   return n;
 }
 
-template <int BN, int STAGES, bool A_MCONTIG, bool B_NCONTIG, class EP>
-inline cudaError_t tcgemm_launch(const FastShape &s, EP ep, cudaStream_t st, int *err, int va, int vb) {
+// Bytes of the packed weight image tcgemm needs for `s` (0 when the weight operand is not packed:
+// split-K, or an all-ones column).
+inline size_t tcgemm_pack_bytes(const FastShape &s) {
+  if (s.splits > 1 || s.ones_col >= 0 || s.nz != 1) return 0;
+  const bool narrow = s.N <= 64 || (s.N % 128 != 0 && s.N % 128 <= 64);
+  const int BN = narrow ? 64 : 128;
+  const size_t tiles_n = (s.N + BN - 1) / BN, kstages = (s.K + 31) / 32;
+  return tiles_n * kstages * 2 * (size_t)BN * 32 * 4;
+}
+
+template <int BN, int STAGES, bool A_MCONTIG, bool B_NCONTIG, bool PACKED_B, class EP>
+inline cudaError_t tcgemm_launch(const FastShape &s, EP ep, cudaStream_t st, int *err, int va, int vb,
+                                 uint8_t *img) {
   constexpr int BK = 32;
   using C = tc::Cfg<BN, BK, STAGES>;
-  auto fn = tc::tcgemm_kernel<BN, BK, STAGES, A_MCONTIG, B_NCONTIG, EP>;
+  auto fn = tc::tcgemm_kernel<BN, BK, STAGES, A_MCONTIG, B_NCONTIG, PACKED_B, EP>;
   static bool attr = false;  // per instantiation; setting it twice is harmless
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
@@ -530,13 +624,22 @@ inline cudaError_t tcgemm_launch(const FastShape &s, EP ep, cudaStream_t st, int
   if (total <= 0) return cudaSuccess;
   if (total > (1LL << 30)) return cudaErrorInvalidValue;
   const int grid = (int)(total < sm_count() ? total : sm_count());
-  fn<<<grid, 288, C::SMEM, st>>>(s, ep, err, va, vb, tiles_n, tiles_m, (int)total);
+  const int kstages = (s.K + BK - 1) / BK;
+  if (PACKED_B) {
+    const long long n = (long long)tiles_n * kstages * (BN * BK / 4);
+    tc::pack_b_kernel<BN, BK, !B_NCONTIG><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(s.B, s.ldb, s.N, s.K, img,
+                                                                                       tiles_n, kstages);
+  }
+  fn<<<grid, 288, C::SMEM, st>>>(s, ep, err, va, vb, ep.aligned4() ? 1 : 0, tiles_n, tiles_m, (int)total, img,
+                                  kstages);
   return cudaGetLastError();
 }
 
-// Tile width by N (64 when that wastes less), split-K as given in `s`.
+// Tile width by N (64 when that wastes less), split-K as given in `s`.  With `img` (at least
+// tcgemm_pack_bytes(s) bytes, 16-byte aligned) the B operand is packed first and streamed into the
+// stages by the bulk-copy engine; without it the producer warps load and split B themselves.
 template <bool A_MCONTIG, bool B_NCONTIG, class EP>
-inline cudaError_t tcgemm(FastShape s, EP ep, cudaStream_t st, int *err) {
+inline cudaError_t tcgemm(FastShape s, EP ep, cudaStream_t st, int *err, uint8_t *img = nullptr) {
   constexpr int BK = 32;
   if (s.M <= 0 || s.N <= 0 || s.nz <= 0) return cudaSuccess;
   if (s.splits < 1) s.splits = 1;
@@ -545,17 +648,40 @@ inline cudaError_t tcgemm(FastShape s, EP ep, cudaStream_t st, int *err) {
   const int va = aligned(s.A, s.lda) && (s.strideA % 4 == 0);
   const int vb = aligned(s.B, s.ldb) && (s.strideB % 4 == 0);
   const bool narrow = s.N <= 64 || (s.N % 128 != 0 && s.N % 128 <= 64);
-  if (narrow) return tcgemm_launch<64, 4, A_MCONTIG, B_NCONTIG>(s, ep, st, err, va, vb);
-  return tcgemm_launch<128, 3, A_MCONTIG, B_NCONTIG>(s, ep, st, err, va, vb);
+  const bool packed = img != nullptr && tcgemm_pack_bytes(s) > 0 && ((uintptr_t)img & 15) == 0;
+  if (narrow) {
+    if (packed) return tcgemm_launch<64, 4, A_MCONTIG, B_NCONTIG, true>(s, ep, st, err, va, vb, img);
+    return tcgemm_launch<64, 4, A_MCONTIG, B_NCONTIG, false>(s, ep, st, err, va, vb, nullptr);
+  }
+  if (packed) return tcgemm_launch<128, 3, A_MCONTIG, B_NCONTIG, true>(s, ep, st, err, va, vb, img);
+  return tcgemm_launch<128, 3, A_MCONTIG, B_NCONTIG, false>(s, ep, st, err, va, vb, nullptr);
 }
 
-// The FP32 GEMM of a call site: 3xTF32 tensor cores unless the context was created with
+// Whether a call site's FP32 GEMM runs on the tensor cores: unless the context was created with
 // NN_INIT_SIMT_GEMM or the product is too small for a 128-row tile to pay off.
+inline bool tc_path(const FastShape &s) {
+  return tensor_gemm_enabled() && s.M >= 64 && (long long)s.M * s.N * s.K >= (1LL << 20);
+}
+
 template <bool A_MCONTIG, bool B_NCONTIG, class EP>
 inline cudaError_t gemm_f32(FastShape s, EP ep, cudaStream_t st) {
-  if (tensor_gemm_enabled() && s.M >= 64 && (long long)s.M * s.N * s.K >= (1LL << 20))
-    return tcgemm<A_MCONTIG, B_NCONTIG>(s, ep, st, device_status());
+  if (tc_path(s)) return tcgemm<A_MCONTIG, B_NCONTIG>(s, ep, st, device_status());
   return sgemm_fast<A_MCONTIG, B_NCONTIG>(s, ep, st);
+}
+
+// Same, for a B operand that every row tile re-reads (a weight matrix): on the tensor-core path B
+// is packed once into scratch slot 4 and streamed by bulk copies.
+template <bool A_MCONTIG, bool B_NCONTIG, class EP>
+inline cudaError_t gemm_f32_wb(Launch &L, FastShape s, EP ep) {
+  if (!tc_path(s)) return sgemm_fast<A_MCONTIG, B_NCONTIG>(s, ep, L.stream);
+  const size_t bytes = tcgemm_pack_bytes(s);
+  uint8_t *img = nullptr;
+  if (bytes > 0) {
+    img = reinterpret_cast<uint8_t *>(L.scratch(4, (bytes + 3) / 4));
+    if (!img) return cudaErrorMemoryAllocation;
+    L.counted();  // the pack kernel
+  }
+  return tcgemm<A_MCONTIG, B_NCONTIG>(s, ep, L.stream, device_status(), img);
 }
 
 }  // namespace nn

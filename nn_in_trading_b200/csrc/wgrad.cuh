@@ -56,6 +56,15 @@ struct PartialStoreLd {
     for (int j = 0; j < R; ++j)
       if (mask >> j & 1u) p[rb[j] + n] = v[j];
   }
+  __host__ __device__ bool aligned4() const { return (ldp) % 4 == 0 && ((uintptr_t)p & 15) == 0; }
+  __device__ __forceinline__ float4 col4(int, int) const { return make_float4(0.f, 0.f, 0.f, 0.f); }
+  template <int R>
+  __device__ __forceinline__ void put_rows4(const long long (&rb)[R], int n, const float4 (&v)[R], float4,
+                                            unsigned mask) const {
+#pragma unroll
+    for (int j = 0; j < R; ++j)
+      if (mask >> j & 1u) *reinterpret_cast<float4 *>(p + rb[j] + n) = v[j];
+  }
 };
 
 // Bias column of a weight gradient: per split, sum over the split's reduction
@@ -76,12 +85,21 @@ inline int wgrad_fast(Launch &L, const float *A, long long lda, const float *X, 
   float *part = L.scratch(0, per * splits);
   if (!part) return NN_ERR_CUDA;
   FastShape fs{M, N, rows, 1, splits, kchunk, A, lda, 0, X, ldx, 0};
-  cudaError_t e = gemm_f32<true, true>(fs, PartialStoreLd{part, M, ldp, 1}, L.stream);
-  if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
-  L.counted();
-  dim3 grid((M + 255) / 256, splits);
-  colsum_partial_kernel<<<grid, 256, 0, L.stream>>>(part, A, M, rows, lda, kchunk, ldp, N);
-  NN_CHECK_LAUNCH(L);
+  if (tc_path(fs)) {
+    // the bias input (1) is column N of X: one GEMM writes all N + 1 gradient columns
+    fs.N = N + 1;
+    fs.ones_col = N;
+    cudaError_t e = tcgemm<true, true>(fs, PartialStoreLd{part, M, ldp, 1}, L.stream, device_status());
+    if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
+    L.counted();
+  } else {
+    cudaError_t e = sgemm_fast<true, true>(fs, PartialStoreLd{part, M, ldp, 1}, L.stream);
+    if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
+    L.counted();
+    dim3 grid((M + 255) / 256, splits);
+    colsum_partial_kernel<<<grid, 256, 0, L.stream>>>(part, A, M, rows, lda, kchunk, ldp, N);
+    NN_CHECK_LAUNCH(L);
+  }
   out->p = part;
   out->splits = splits;
   out->stride = per;
