@@ -43,9 +43,11 @@
 //     Strides: MN groups (LBO) 128*BK B, k groups (SBO) 512 B.  Global: four
 //     128-byte row segments.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstring>
 
 #include "gemm_fast.cuh"
 #include "nn_device.cuh"
@@ -105,6 +107,17 @@ __device__ __forceinline__ void bulk_copy_g2s(void *dst, const void *src, uint32
                    smem_u32(dst)),
                "l"(src), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
+}
+
+// Bounded wait that ignores the abort flag: used only to drain this CTA's own asynchronous copies and
+// MMAs before it exits.
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t *bar, uint32_t parity) {
+  const long long t0 = clock64();
+  for (uint32_t it = 0; it < kWaitIters; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (clock64() - t0 > kWaitCycles) return false;
+  }
+  return false;
 }
 
 __device__ __forceinline__ void fence_barrier_init() {
@@ -254,18 +267,53 @@ struct Cfg {
   static constexpr int A_CHUNKS = BM * BK / 4 / 128;            // float4 chunks per producer thread per stage
   static constexpr int B_CHUNKS = BN * BK / 4 / 128;
   static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulators: epilogue of one tile || MMAs of the next
-  static_assert(BK % 8 == 0 && BN % 32 == 0 && BN >= 32 && BN <= 256, "tile");
+  static_assert(BK == 32, "a stage row of a K-major tile is one 128-byte swizzle row");
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "tile");
   static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "swizzle atoms must stay 1024-byte aligned");
   static_assert((BM * BK / 4) % 128 == 0 && (BN * BK / 4) % 128 == 0, "chunks per thread");
   static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0 && TMEM_COLS >= 32 && TMEM_COLS <= 512, "tensor-memory columns");
   static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
+// Where an operand's stage tiles come from.
+//   OP_REGS   producer warps load fp32 into registers, split, and store hi and lo.
+//   OP_PACKED (B only) a pre-split image in global memory, one bulk copy per stage.
+//   OP_TMA    the loader warp copies the raw fp32 tile with TMA straight into the hi slot; the
+//             producer warps then sanitise it in place and write lo = x - trunc(x).  The tensor cores
+//             read a TF32 operand by truncating the fp32 bit pattern (measured on this part), so the
+//             raw tile is the hi half as it stands.
+enum OpMode : int { OP_REGS = 0, OP_PACKED = 1, OP_TMA = 2 };
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+// 3-d tiled TMA load of box (c0, c1, c2) into shared memory, counted on `bar` (no multicast).
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *tm, int c0, int c1, int c2, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Raw tile -> (sanitised hi in place, lo): chunk f of the region, 16 bytes each.
+__device__ __forceinline__ void split_in_place(uint8_t *hi, uint8_t *lo, uint32_t off) {
+  float4 x = *reinterpret_cast<const float4 *>(hi + off);
+  if (!(isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w))) {
+    x = make_float4(nan0(x.x), nan0(x.y), nan0(x.z), nan0(x.w));
+    *reinterpret_cast<float4 *>(hi + off) = x;
+  }
+  *reinterpret_cast<float4 *>(lo + off) =
+      make_float4(x.x - tf32_hi(x.x), x.y - tf32_hi(x.y), x.z - tf32_hi(x.z), x.w - tf32_hi(x.w));
+}
+
 // Persistent kernel: CTA i processes tiles i, i + gridDim.x, ... (n-tile fastest, so the CTAs in
-// flight share their A rows in L2).  288 threads:
+// flight share their A rows in L2).  320 threads:
 //   warps 0-3  epilogue (tensor-memory lanes 32w..32w+31 = tile rows), one accumulator at a time
-//   warps 4-7  producers, stage ring of STAGES buffers
+//   warps 4-7  producers (OP_REGS loads and splits, OP_TMA in-place splits), stage ring of STAGES
 //   warp 8     tensor-memory owner and MMA issuer, alternating two accumulators
+//   warp 9     loader: TMA tiles and packed-image bulk copies
 // Epilogue functors give a per-row offset (`row`, computed once per tile by the lane that owns the
 // row and broadcast with shuffles), a per-column constant (`col`, e.g. the bias, once per 32-column
 // chunk), and store 8 rows of one column at a time (`put_rows`: any per-element inputs are loaded
@@ -273,24 +321,32 @@ struct Cfg {
 // every output row starts on a 16-byte boundary (`aligned4`, checked on the host) full 32-column
 // chunks go out as float4s instead (`col4` / `put_rows4`: a lane stores 4 columns of 8 rows, a warp
 // instruction 4 rows x 128 bytes).
-template <int BN, int BK, int STAGES, bool A_MCONTIG, bool B_NCONTIG, bool PACKED_B, class EP>
-__global__ void __launch_bounds__(288, 1)
+template <int BN, int BK, int STAGES, bool A_MCONTIG, bool B_NCONTIG, int A_MODE, int B_MODE, class EP>
+__global__ void __launch_bounds__(320, 1)
     tcgemm_kernel(FastShape s, EP ep, int *err, int vec_a, int vec_b, int vec_out, int tiles_n, int tiles_m,
-                  int total, const uint8_t *bimg, int kstages) {
+                  int total, const uint8_t *bimg, int kstages, const __grid_constant__ CUtensorMap tmA,
+                  const __grid_constant__ CUtensorMap tmB) {
   using C = Cfg<BN, BK, STAGES>;
   constexpr int BM = C::BM;
   constexpr bool A_K = !A_MCONTIG, B_K = !B_NCONTIG;
-  // descriptor strides (bytes), layout types and the start offset of each 8-wide k step
-  constexpr uint32_t A_LBO = A_K ? 128u : 128u * BK, A_SBO = A_K ? 32u * BK : 512u;
-  constexpr uint32_t B_LBO = B_K ? 128u : 128u * BK, B_SBO = B_K ? 32u * BK : 512u;
-  constexpr uint32_t A_LAY = A_K ? 0u : 1u, B_LAY = B_K ? 0u : 1u;
-  constexpr uint32_t A_STEP = A_K ? 256u : 1024u, B_STEP = B_K ? 256u : 1024u;
+  static_assert(A_MODE != OP_PACKED, "only the B operand is packed");
+  // Descriptor strides (bytes), layout types and the start offset of each 8-wide k step.
+  //   K-major TMA tiles: 128-byte swizzle, 16-byte granules (layout 2): 8-row groups 1024 B apart,
+  //   a k step moves the start 32 B along the swizzled row.  K-major register / packed tiles: no
+  //   swizzle (layout 0).  MN-major tiles in every mode: 128-byte swizzle, 32-byte granules (layout 1).
+  constexpr bool A_SW = A_K && A_MODE == OP_TMA, B_SW = B_K && B_MODE == OP_TMA;
+  constexpr uint32_t A_LBO = A_K ? (A_SW ? 16u : 128u) : 128u * BK, A_SBO = A_K ? (A_SW ? 1024u : 32u * BK) : 512u;
+  constexpr uint32_t B_LBO = B_K ? (B_SW ? 16u : 128u) : 128u * BK, B_SBO = B_K ? (B_SW ? 1024u : 32u * BK) : 512u;
+  constexpr uint32_t A_LAY = A_K ? (A_SW ? 2u : 0u) : 1u, B_LAY = B_K ? (B_SW ? 2u : 0u) : 1u;
+  constexpr uint32_t A_STEP = A_K ? (A_SW ? 32u : 256u) : 1024u, B_STEP = B_K ? (B_SW ? 32u : 256u) : 1024u;
   constexpr uint32_t IDESC = instr_desc_tf32(BM, BN, A_MCONTIG, B_NCONTIG);
+  constexpr bool ANY_TMA = A_MODE == OP_TMA || B_MODE == OP_TMA;
+  constexpr bool LOADER = ANY_TMA || B_MODE == OP_PACKED;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // swizzle atoms are located by absolute address bits: start the stages on a 1024-byte boundary
   uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], accf[2], acce[2], drain;
+  __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], tmaf[STAGES], accf[2], acce[2], drain;
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
 
@@ -315,6 +371,7 @@ __global__ void __launch_bounds__(288, 1)
     for (int i = 0; i < STAGES; ++i) {
       mbar_init(&full[i], 128);
       mbar_init(&empty[i], 1);
+      mbar_init(&tmaf[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&accf[i], 1);
@@ -332,17 +389,17 @@ __global__ void __launch_bounds__(288, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
+  const int n_real = s.ones_col >= 0 ? s.ones_col : s.N;
 
   if (warp >= 4 && warp < 8) {
     // ------------------------------------------------------------ producers
-    // Stages are loaded one ahead: the global loads of the next stage are in flight while the
-    // current one is split and stored (two register sets, used alternately).
+    // OP_REGS operands are loaded one stage ahead: the global loads of the next stage are in
+    // flight while the current one is split and stored (two register sets, used alternately).
     const int ptid = tid - 128;
     struct PState {
-      int t, kk, nk, kbeg, kend, Ma, Nb, ones, nt;
+      int t, kk, nk, kbeg, kend, Ma, Nb, ones;
       const float *Ab, *Bb;
     };
-    const int n_real = s.ones_col >= 0 ? s.ones_col : s.N;
     auto start_tile = [&](PState &p) -> bool {
       for (; p.t < total; p.t += gridDim.x) {
         int m0, n0, z, split;
@@ -355,7 +412,6 @@ __global__ void __launch_bounds__(288, 1)
         p.Ma = s.M - m0;
         p.Nb = n_real - n0;
         p.ones = s.ones_col >= 0 ? s.ones_col - n0 : -1;
-        p.nt = n0 / BN;
         p.kk = 0;
         return true;
       }
@@ -368,13 +424,15 @@ __global__ void __launch_bounds__(288, 1)
     };
     auto load = [&](const PState &p, float4 (&va)[C::A_CHUNKS], float4 (&vb)[C::B_CHUNKS]) {
       const int k0 = p.kbeg + p.kk * BK;
+      if (A_MODE == OP_REGS) {
 #pragma unroll
-      for (int i = 0; i < C::A_CHUNKS; ++i) {
-        int row, k;
-        chunk_place<A_K, BM, BK>(ptid + 128 * i, row, k);
-        va[i] = load_chunk<A_K>(p.Ab, s.lda, row, k0 + k, p.Ma, p.kend, vec_a != 0);
+        for (int i = 0; i < C::A_CHUNKS; ++i) {
+          int row, k;
+          chunk_place<A_K, BM, BK>(ptid + 128 * i, row, k);
+          va[i] = load_chunk<A_K>(p.Ab, s.lda, row, k0 + k, p.Ma, p.kend, vec_a != 0);
+        }
       }
-      if (!PACKED_B) {
+      if (B_MODE == OP_REGS) {
 #pragma unroll
         for (int i = 0; i < C::B_CHUNKS; ++i) {
           int row, k;
@@ -390,22 +448,36 @@ __global__ void __launch_bounds__(288, 1)
         fail(kErrEmptyWait);
         return false;
       }
-      uint8_t *base = smem + st * C::STAGE_BYTES;
-      if (PACKED_B && ptid == 0) {
-        // the weight tile of this stage, already split and laid out, in one bulk copy
-        const size_t img = ((size_t)p.nt * kstages + (p.kbeg / BK + p.kk)) * (2 * C::B_BYTES);
-        mbar_expect_tx(&full[st], 2 * C::B_BYTES);
-        bulk_copy_g2s(base + 2 * C::A_BYTES, bimg + img, 2 * C::B_BYTES, &full[st]);
+      if (LOADER && !mbar_wait(&tmaf[st], (it / STAGES) & 1, &abort_flag)) {
+        fail(kErrFullWait);
+        return false;
       }
+      uint8_t *base = smem + st * C::STAGE_BYTES;
+      uint8_t *b_hi = base + 2 * C::A_BYTES, *b_lo = b_hi + C::B_BYTES;
       int row, k;
+      if (A_MODE == OP_REGS) {
 #pragma unroll
-      for (int i = 0; i < C::A_CHUNKS; ++i)
-        store_split(base, base + C::A_BYTES, chunk_place<A_K, BM, BK>(ptid + 128 * i, row, k), va[i]);
-      if (!PACKED_B) {
+        for (int i = 0; i < C::A_CHUNKS; ++i)
+          store_split(base, base + C::A_BYTES, chunk_place<A_K, BM, BK>(ptid + 128 * i, row, k), va[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < C::A_CHUNKS; ++i) split_in_place(base, base + C::A_BYTES, 16u * (ptid + 128 * i));
+      }
+      if (B_MODE == OP_REGS) {
 #pragma unroll
         for (int i = 0; i < C::B_CHUNKS; ++i)
-          store_split(base + 2 * C::A_BYTES, base + 2 * C::A_BYTES + C::B_BYTES,
-                      chunk_place<B_K, BN, BK>(ptid + 128 * i, row, k), vb[i]);
+          store_split(b_hi, b_lo, chunk_place<B_K, BN, BK>(ptid + 128 * i, row, k), vb[i]);
+      } else if (B_MODE == OP_TMA) {
+#pragma unroll
+        for (int i = 0; i < C::B_CHUNKS; ++i) split_in_place(b_hi, b_lo, 16u * (ptid + 128 * i));
+        // the all-ones column lies outside the B tensor, so TMA filled it with zeros
+        if (p.ones >= 0 && p.ones < BN && ptid < BK && p.kbeg + p.kk * BK + ptid < p.kend) {
+          const int kr = ptid, j = p.ones;
+          const uint32_t off = B_K ? (uint32_t)(j * 128 + ((((kr >> 2) ^ (j & 7))) << 4) + (kr & 3) * 4)
+                                   : (uint32_t)((j >> 5) * 128 * BK + kr * 128 + ((((j & 31) >> 3) ^ (kr & 3)) << 5) +
+                                                (j & 7) * 4);
+          *reinterpret_cast<float *>(b_hi + off) = 1.f;
+        }
       }
       fence_proxy_async_smem();
       mbar_arrive(&full[st]);
@@ -427,6 +499,60 @@ __global__ void __launch_bounds__(288, 1)
       have = advance(p);
       if (have) load(p, va0, vb0);
       if (!put(cur, va1, vb1)) break;
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ loader
+    if (LOADER && lane == 0) {
+      int it = 0;
+      for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x) {
+        int m0, n0, z, split, kbeg, kend, nk;
+        decode(t, m0, n0, z, split, kbeg, kend, nk);
+        bool ok = true;
+        for (int kk = 0; kk < nk; ++kk, ++it) {
+          const int st = it % STAGES;
+          if (it >= STAGES && !mbar_wait(&empty[st], ((it / STAGES) - 1) & 1, &abort_flag)) {
+            fail(kErrEmptyWait);
+            ok = false;
+            break;
+          }
+          uint8_t *base = smem + st * C::STAGE_BYTES;
+          const int k0 = kbeg + kk * BK;
+          // every copy of the stage completes on tmaf[st]; the producers wait for it before they
+          // split and release the stage to the MMA warp
+          mbar_arrive_expect_tx(&tmaf[st], (A_MODE == OP_TMA ? C::A_BYTES : 0u) + (B_MODE == OP_TMA ? C::B_BYTES : 0u) +
+                                               (B_MODE == OP_PACKED ? 2 * C::B_BYTES : 0u));
+          {
+            if (A_MODE == OP_TMA) {
+              if (A_K) {
+                tma_load_3d(base, &tmA, k0, m0, z, &tmaf[st]);
+              } else {
+#pragma unroll
+                for (int h = 0; h < BM / 32; ++h) tma_load_3d(base + h * 128 * BK, &tmA, m0 + 32 * h, k0, z, &tmaf[st]);
+              }
+            }
+            if (B_MODE == OP_TMA) {
+              uint8_t *bdst = base + 2 * C::A_BYTES;
+              if (B_K) {
+                tma_load_3d(bdst, &tmB, k0, n0, z, &tmaf[st]);
+              } else {
+#pragma unroll
+                for (int h = 0; h < BN / 32; ++h) tma_load_3d(bdst + h * 128 * BK, &tmB, n0 + 32 * h, k0, z, &tmaf[st]);
+              }
+            }
+          }
+          if (B_MODE == OP_PACKED) {
+            // the weight tile of this stage, already split and laid out, in one bulk copy
+            const size_t img = ((size_t)(n0 / BN) * kstages + (kbeg / BK + kk)) * (2 * C::B_BYTES);
+            bulk_copy_g2s(base + 2 * C::A_BYTES, bimg + img, 2 * C::B_BYTES, &tmaf[st]);
+          }
+        }
+        if (!ok) break;
+      }
+      // before exiting, wait for every copy still in flight into this CTA's shared memory
+      for (int st = 0; st < STAGES && st < it; ++st) {
+        const int issued = (it - st - 1) / STAGES + 1;
+        if (!mbar_wait_drain(&tmaf[st], (issued - 1) & 1) && !abort_flag) fail(kErrFullWait);
+      }
     }
   } else if (warp == 8) {
     // ------------------------------------------------------------ MMA issue
@@ -554,7 +680,7 @@ __global__ void __launch_bounds__(288, 1)
     // every MMA this thread issued must be complete before its columns are freed
     if (lane == 0) mma_commit(&drain);
     __syncwarp();
-    if (!mbar_wait(&drain, 0, &abort_flag) && lane == 0 && !abort_flag) atomicExch(err, kErrDoneWait);
+    if (!mbar_wait_drain(&drain, 0) && lane == 0) atomicExch(err, kErrDoneWait);
   }
   tc_fence_before();
   __syncthreads();
@@ -607,12 +733,53 @@ inline size_t tcgemm_pack_bytes(const FastShape &s) {
   return tiles_n * kstages * 2 * (size_t)BN * 32 * 4;
 }
 
-template <int BN, int STAGES, bool A_MCONTIG, bool B_NCONTIG, bool PACKED_B, class EP>
+// Tensor maps for OP_TMA operands (the encoder is the driver's, resolved once through the runtime).
+typedef CUresult (*TmapEncodeFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+inline TmapEncodeFn tmap_encoder() {
+  static TmapEncodeFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<TmapEncodeFn>(p);
+  }
+  return fn;
+}
+
+// Whether an operand can be read by TMA: 16-byte aligned base, rows and batch strides multiples of 16
+// bytes, and (for split-K) split boundaries on stage boundaries.
+inline bool tma_ok(const float *p, long long ld, long long stride_z, int nz, const FastShape &s) {
+  if (!tmap_encoder()) return false;
+  if (((uintptr_t)p & 15) || ld % 4 || ld <= 0) return false;
+  if (nz > 1 && (stride_z % 4 || stride_z <= 0)) return false;
+  if (s.splits > 1 && s.kchunk % 32) return false;
+  return true;
+}
+
+// Fp32 tensor [nz][outer][inner] with row stride ld and batch stride stride_z (elements); box
+// 32 x box_outer, 128-byte swizzle with 16-byte (K-major) or 32-byte (MN-major) granules.
+inline bool make_tmap(CUtensorMap *tm, const float *p, long long ld, long long stride_z, int inner, int outer, int nz,
+                      int box_outer, bool mn_major) {
+  cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)outer, (cuuint64_t)nz};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)(nz > 1 ? stride_z : ld * (long long)outer) * 4};
+  cuuint32_t box[3] = {32u, (cuuint32_t)box_outer, 1u}, es[3] = {1u, 1u, 1u};
+  return tmap_encoder()(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(p), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, int STAGES, bool A_MCONTIG, bool B_NCONTIG, int A_MODE, int B_MODE, class EP>
 inline cudaError_t tcgemm_launch(const FastShape &s, EP ep, cudaStream_t st, int *err, int va, int vb,
                                  uint8_t *img) {
   constexpr int BK = 32;
   using C = tc::Cfg<BN, BK, STAGES>;
-  auto fn = tc::tcgemm_kernel<BN, BK, STAGES, A_MCONTIG, B_NCONTIG, PACKED_B, EP>;
+  auto fn = tc::tcgemm_kernel<BN, BK, STAGES, A_MCONTIG, B_NCONTIG, A_MODE, B_MODE, EP>;
   static bool attr = false;  // per instantiation; setting it twice is harmless
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
@@ -625,19 +792,47 @@ inline cudaError_t tcgemm_launch(const FastShape &s, EP ep, cudaStream_t st, int
   if (total > (1LL << 30)) return cudaErrorInvalidValue;
   const int grid = (int)(total < sm_count() ? total : sm_count());
   const int kstages = (s.K + BK - 1) / BK;
-  if (PACKED_B) {
+  CUtensorMap tmA, tmB;
+  std::memset(&tmA, 0, sizeof tmA);
+  std::memset(&tmB, 0, sizeof tmB);
+  if (A_MODE == tc::OP_TMA) {
+    const bool ok = A_MCONTIG ? make_tmap(&tmA, s.A, s.lda, s.strideA, s.M, s.K, s.nz, 32, true)
+                              : make_tmap(&tmA, s.A, s.lda, s.strideA, s.K, s.M, s.nz, 128, false);
+    if (!ok) return cudaErrorInvalidValue;
+  }
+  if (B_MODE == tc::OP_TMA) {
+    const int n_real = s.ones_col >= 0 ? s.ones_col : s.N;
+    const bool ok = B_NCONTIG ? make_tmap(&tmB, s.B, s.ldb, s.strideB, n_real, s.K, s.nz, 32, true)
+                              : make_tmap(&tmB, s.B, s.ldb, s.strideB, s.K, n_real, s.nz, BN, false);
+    if (!ok) return cudaErrorInvalidValue;
+  }
+  if (B_MODE == tc::OP_PACKED) {
     const long long n = (long long)tiles_n * kstages * (BN * BK / 4);
     tc::pack_b_kernel<BN, BK, !B_NCONTIG><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(s.B, s.ldb, s.N, s.K, img,
                                                                                        tiles_n, kstages);
   }
-  fn<<<grid, 288, C::SMEM, st>>>(s, ep, err, va, vb, ep.aligned4() ? 1 : 0, tiles_n, tiles_m, (int)total, img,
-                                  kstages);
+  fn<<<grid, 320, C::SMEM, st>>>(s, ep, err, va, vb, ep.aligned4() ? 1 : 0, tiles_n, tiles_m, (int)total, img,
+                                  kstages, tmA, tmB);
   return cudaGetLastError();
+}
+
+template <int BN, int STAGES, bool A_MCONTIG, bool B_NCONTIG, class EP>
+inline cudaError_t tcgemm_modes(const FastShape &s, EP ep, cudaStream_t st, int *err, int va, int vb, uint8_t *img,
+                                bool a_tma, bool b_tma) {
+  using namespace tc;
+  if (img) {
+    if (a_tma) return tcgemm_launch<BN, STAGES, A_MCONTIG, B_NCONTIG, OP_TMA, OP_PACKED>(s, ep, st, err, va, vb, img);
+    return tcgemm_launch<BN, STAGES, A_MCONTIG, B_NCONTIG, OP_REGS, OP_PACKED>(s, ep, st, err, va, vb, img);
+  }
+  if (a_tma && b_tma)
+    return tcgemm_launch<BN, STAGES, A_MCONTIG, B_NCONTIG, OP_TMA, OP_TMA>(s, ep, st, err, va, vb, nullptr);
+  return tcgemm_launch<BN, STAGES, A_MCONTIG, B_NCONTIG, OP_REGS, OP_REGS>(s, ep, st, err, va, vb, nullptr);
 }
 
 // Tile width by N (64 when that wastes less), split-K as given in `s`.  With `img` (at least
 // tcgemm_pack_bytes(s) bytes, 16-byte aligned) the B operand is packed first and streamed into the
-// stages by the bulk-copy engine; without it the producer warps load and split B themselves.
+// stages by bulk copies; otherwise B is loaded like A.  Operands TMA can address are copied by
+// TMA, the others by the producer warps.
 template <bool A_MCONTIG, bool B_NCONTIG, class EP>
 inline cudaError_t tcgemm(FastShape s, EP ep, cudaStream_t st, int *err, uint8_t *img = nullptr) {
   constexpr int BK = 32;
@@ -649,12 +844,10 @@ inline cudaError_t tcgemm(FastShape s, EP ep, cudaStream_t st, int *err, uint8_t
   const int vb = aligned(s.B, s.ldb) && (s.strideB % 4 == 0);
   const bool narrow = s.N <= 64 || (s.N % 128 != 0 && s.N % 128 <= 64);
   const bool packed = img != nullptr && tcgemm_pack_bytes(s) > 0 && ((uintptr_t)img & 15) == 0;
-  if (narrow) {
-    if (packed) return tcgemm_launch<64, 4, A_MCONTIG, B_NCONTIG, true>(s, ep, st, err, va, vb, img);
-    return tcgemm_launch<64, 4, A_MCONTIG, B_NCONTIG, false>(s, ep, st, err, va, vb, nullptr);
-  }
-  if (packed) return tcgemm_launch<128, 3, A_MCONTIG, B_NCONTIG, true>(s, ep, st, err, va, vb, img);
-  return tcgemm_launch<128, 3, A_MCONTIG, B_NCONTIG, false>(s, ep, st, err, va, vb, nullptr);
+  const bool a_tma = tma_ok(s.A, s.lda, s.strideA, s.nz, s);
+  const bool b_tma = !packed && tma_ok(s.B, s.ldb, s.strideB, s.nz, s);
+  if (narrow) return tcgemm_modes<64, 4, A_MCONTIG, B_NCONTIG>(s, ep, st, err, va, vb, packed ? img : nullptr, a_tma, b_tma);
+  return tcgemm_modes<128, 3, A_MCONTIG, B_NCONTIG>(s, ep, st, err, va, vb, packed ? img : nullptr, a_tma, b_tma);
 }
 
 // Whether a call site's FP32 GEMM runs on the tensor cores: unless the context was created with

@@ -77,7 +77,9 @@ __global__ void colsum_partial_kernel(float *p, const float *g, int M, int rows,
 inline int wgrad_fast(Launch &L, const float *A, long long lda, const float *X, long long ldx, int M, int N, int rows,
                       GradSrc *out) {
   int splits = fast_splits(M, N + 1, rows, 1);
-  int kchunk = ((rows + splits - 1) / splits + 7) / 8 * 8;
+  // tensor-core path: split boundaries on its 32-deep stages (so TMA can load whole stages)
+  const int gran = tc_path(FastShape{M, N, rows, 1, 1, 0, A, lda, 0, X, ldx, 0}) ? 32 : 8;
+  int kchunk = ((rows + splits - 1) / splits + gran - 1) / gran * gran;
   splits = (rows + kchunk - 1) / kchunk;
   if (splits < 1) splits = 1;
   const int ldp = N + 1;
