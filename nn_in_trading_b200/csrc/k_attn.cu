@@ -8,6 +8,7 @@
 // (NeuroNet.cl:1674, 1693, 1754); scores are [query][head][key].
 #include "../../include/nn_b200.h"
 #include "attn_smem.cuh"
+#include "tc_attn.cuh"
 #include "nn_device.cuh"
 #include "nn_internal.h"
 
@@ -82,6 +83,12 @@ static int k_mh_attention_score(Launch &L) {
   if (!qkv || !score) return NN_ERR_BOUNDS;
   float koef = sqrtf((float)dim);
   if (koef < 1.f) koef = 1.f;
+  if (attn_tc_ok(qkv, score, units, heads, dim)) {
+    cudaError_t e = attn_tc<tc::kAttnScore>(qkv, score, score, L.B, units, heads, mask, koef, L.stream);
+    if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
+    L.counted();
+    return NN_OK;
+  }
   {
     size_t sm = (size_t)(units * pad4(dim) + dim * pad4(units)) * sizeof(float);
     int kpl = (units + 31) / 32;
@@ -161,6 +168,12 @@ static int k_mh_attention_out(Launch &L) {
   float *qkv = L.buf(1, (size_t)L.B * units * 3 * heads * dim);
   float *out = L.buf(2, (size_t)L.B * units * heads * dim);
   if (!scores || !qkv || !out) return NN_ERR_BOUNDS;
+  if (attn_tc_ok(qkv, scores, units, heads, dim)) {
+    cudaError_t e = attn_tc<tc::kAttnOut>(qkv, scores, out, L.B, units, heads, 0, 1.f, L.stream);
+    if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
+    L.counted();
+    return NN_OK;
+  }
   {
     size_t sm = (size_t)(units * pad4(units) + units * dim) * sizeof(float);
     int dpl = (dim + 31) / 32;

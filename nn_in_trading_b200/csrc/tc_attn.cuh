@@ -1,0 +1,338 @@
+// Multi-head attention score and output products on the tensor cores (tcgen05, 3xTF32), for the
+// MHAttentionScore / MHAttentionOut shapes of one (sequence, head) pair per work item: up to 128
+// units and a head dimension of 32.
+//
+//   score:  S[q][k] = softmax_k(Q[q] . K[k] / koef)   M = q (128), N = k (128), K = d (32), 1 stage
+//   out:    O[q][d] = sum_k S[q][k] V[k][d]            M = q (128), N = d (32),  K = k (128), 4 stages
+//
+// Persistent CTAs walk the B*H work items; per CTA 320 threads in the roles of tc_gemm.cuh:
+// warps 0-3 epilogue (one output row per thread), warps 4-7 split the TMA-loaded raw tiles into
+// hi / lo in place, warp 8 issues the MMAs into one of two tensor-memory accumulators, warp 9
+// issues the TMA loads.  Rows and keys past `units` are loaded (they belong to the next sequence,
+// or are zero-filled past the end of the tensor) and computed, but never stored: the score
+// epilogue excludes keys >= units from the normalisation, and the out product reads scores whose
+// columns >= units are zero-filled by TMA (the score tensor's inner extent is `units`).
+#pragma once
+#include "tc_gemm.cuh"
+
+namespace nn {
+namespace tc {
+
+constexpr int kAttnScore = 0, kAttnOut = 1;
+
+template <int MODE>
+struct AttnCfg {
+  static constexpr int BM = 128, BK = 32;
+  static constexpr int BN = MODE == kAttnScore ? 128 : 32;
+  static constexpr int NK = MODE == kAttnScore ? 1 : 4;         // k stages per item
+  static constexpr int STAGES = MODE == kAttnScore ? 2 : 4;
+  static constexpr uint32_t A_BYTES = BM * BK * 4, B_BYTES = BN * BK * 4;
+  static constexpr uint32_t STAGE_BYTES = 2 * (A_BYTES + B_BYTES);
+  static constexpr uint32_t EPI_OFF = STAGES * STAGE_BYTES;
+  // score: each epilogue warp keeps its 32 rows x 128 keys of exponentials (row stride 129 floats)
+  // plus one scale per row; out: a 32 x 33 transpose buffer per warp
+  static constexpr uint32_t EPI_BYTES = MODE == kAttnScore ? 4 * 32 * 129 * 4 + 128 * 4 : 4 * 32 * 33 * 4;
+  static constexpr uint32_t SMEM = EPI_OFF + EPI_BYTES + 1024;
+  static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+  static_assert(SMEM <= 232448, "shared memory per CTA");
+  static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0, "tensor-memory columns");
+};
+
+// tmQ:  qkv as [B*U rows][3*H*D], box 32 x 128, 128-byte swizzle (K-major Q and K tiles)
+// tmS:  scores as [B*U][H][U],    box 32 x 1 x 128, 128-byte swizzle (K-major score tiles)
+// tmV:  qkv as [B*U rows][3*H*D], box 32 x 32, 128-byte swizzle / 32-byte granules (MN-major V)
+template <int MODE>
+__global__ void __launch_bounds__(320, 1)
+    attn_tc_kernel(float *__restrict__ out, int *err, int U, int H, int items, int mask, float koef,
+                   const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmS,
+                   const __grid_constant__ CUtensorMap tmV) {
+  using C = AttnCfg<MODE>;
+  constexpr int BM = C::BM, BN = C::BN, BK = C::BK, NK = C::NK, STAGES = C::STAGES;
+  constexpr int D = 32;
+  // A: K-major, 128-byte swizzle.  B: K-major swizzled (score) or MN-major 32-byte granules (out).
+  constexpr uint32_t A_LBO = 16u, A_SBO = 1024u, A_LAY = 2u, A_STEP = 32u;
+  constexpr bool B_MN = MODE == kAttnOut;
+  constexpr uint32_t B_LBO = B_MN ? 128u * BK : 16u, B_SBO = B_MN ? 512u : 1024u, B_LAY = B_MN ? 1u : 2u;
+  constexpr uint32_t B_STEP = B_MN ? 1024u : 32u;
+  constexpr uint32_t IDESC = instr_desc_tf32(BM, BN, false, B_MN);
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], tmaf[STAGES], accf[2], acce[2], drain;
+  __shared__ uint32_t tmem_slot;
+  __shared__ volatile int abort_flag;
+
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  auto fail = [&](int code) {
+    abort_flag = 1;
+    atomicExch(err, code);
+  };
+  if (tid == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&full[i], 128);
+      mbar_init(&empty[i], 1);
+      mbar_init(&tmaf[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accf[i], 1);
+      mbar_init(&acce[i], 128);
+    }
+    mbar_init(&drain, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 8) {
+    tmem_alloc(&tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+
+  if (warp == 9) {
+    // ------------------------------------------------------------ loader
+    if (lane == 0) {
+      int it = 0;
+      for (int t = blockIdx.x; t < items && !abort_flag; t += gridDim.x) {
+        const int b = t / H, h = t % H;
+        bool ok = true;
+        for (int kk = 0; kk < NK; ++kk, ++it) {
+          const int st = it % STAGES;
+          if (it >= STAGES && !mbar_wait(&empty[st], ((it / STAGES) - 1) & 1, &abort_flag)) {
+            fail(kErrEmptyWait);
+            ok = false;
+            break;
+          }
+          uint8_t *base = smem + st * C::STAGE_BYTES;
+          mbar_arrive_expect_tx(&tmaf[st], C::A_BYTES + C::B_BYTES);
+          if (MODE == kAttnScore) {
+            tma_load_3d(base, &tmQ, h * D, b * U, 0, &tmaf[st]);                          // Q rows
+            tma_load_3d(base + 2 * C::A_BYTES, &tmQ, (H + h) * D, b * U, 0, &tmaf[st]);   // K rows
+          } else {
+            tma_load_3d(base, &tmS, 32 * kk, h, b * U, &tmaf[st]);                        // S[:, 32kk..]
+            tma_load_3d(base + 2 * C::A_BYTES, &tmV, (2 * H + h) * D, b * U + 32 * kk, 0, &tmaf[st]);
+          }
+        }
+        if (!ok) break;
+      }
+      for (int st = 0; st < STAGES && st < it; ++st) {
+        const int issued = (it - st - 1) / STAGES + 1;
+        if (!mbar_wait_drain(&tmaf[st], (issued - 1) & 1) && !abort_flag) fail(kErrFullWait);
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------------------ split raw tiles into hi / lo
+    const int ptid = tid - 128;
+    int it = 0;
+    for (int t = blockIdx.x; t < items && !abort_flag; t += gridDim.x) {
+      bool ok = true;
+      for (int kk = 0; kk < NK; ++kk, ++it) {
+        const int st = it % STAGES;
+        if (it >= STAGES && !mbar_wait(&empty[st], ((it / STAGES) - 1) & 1, &abort_flag)) {
+          fail(kErrEmptyWait);
+          ok = false;
+          break;
+        }
+        if (!mbar_wait(&tmaf[st], (it / STAGES) & 1, &abort_flag)) {
+          fail(kErrFullWait);
+          ok = false;
+          break;
+        }
+        uint8_t *base = smem + st * C::STAGE_BYTES;
+#pragma unroll
+        for (uint32_t f = ptid; f < C::A_BYTES / 16; f += 128) split_in_place(base, base + C::A_BYTES, 16u * f);
+#pragma unroll
+        for (uint32_t f = ptid; f < C::B_BYTES / 16; f += 128)
+          split_in_place(base + 2 * C::A_BYTES, base + 2 * C::A_BYTES + C::B_BYTES, 16u * f);
+        fence_proxy_async_smem();
+        mbar_arrive(&full[st]);
+      }
+      if (!ok) break;
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------ MMA issue
+    int it = 0, tl = 0;
+    for (int t = blockIdx.x; t < items && !abort_flag; t += gridDim.x, ++tl) {
+      const int b = tl & 1, u = tl >> 1;
+      if (tl >= 2 && !mbar_wait(&acce[b], (u - 1) & 1, &abort_flag)) {
+        if (lane == 0) fail(kErrDoneWait);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d = tmem + (uint32_t)(b * BN);
+      bool ok = true;
+      for (int kk = 0; kk < NK; ++kk, ++it) {
+        const int st = it % STAGES;
+        if (!mbar_wait(&full[st], (it / STAGES) & 1, &abort_flag)) {
+          if (lane == 0) fail(kErrFullWait);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t base = smem_u32(smem + st * C::STAGE_BYTES);
+          const uint32_t a_hi = base, a_lo = base + C::A_BYTES;
+          const uint32_t b_hi = base + 2 * C::A_BYTES, b_lo = b_hi + C::B_BYTES;
+#pragma unroll
+          for (int sub = 0; sub < BK / 8; ++sub) {
+            const uint64_t ah = smem_desc(a_hi + sub * A_STEP, A_LBO, A_SBO, A_LAY);
+            const uint64_t al = smem_desc(a_lo + sub * A_STEP, A_LBO, A_SBO, A_LAY);
+            const uint64_t bh = smem_desc(b_hi + sub * B_STEP, B_LBO, B_SBO, B_LAY);
+            const uint64_t bl = smem_desc(b_lo + sub * B_STEP, B_LBO, B_SBO, B_LAY);
+            mma_tf32(d, al, bh, IDESC, (kk | sub) != 0 ? 1u : 0u);
+            mma_tf32(d, ah, bl, IDESC, 1u);
+            mma_tf32(d, ah, bh, IDESC, 1u);
+          }
+          mma_commit(&empty[st]);
+        }
+        __syncwarp();
+      }
+      if (!ok) break;
+      if (lane == 0) mma_commit(&accf[b]);
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (thread = row q)
+    float *buf = reinterpret_cast<float *>(smem + C::EPI_OFF) + warp * 32 * 33;  // out mode
+    int tl = 0;
+    const float inv_koef = 1.f / koef;
+    for (int t = blockIdx.x; t < items && !abort_flag; t += gridDim.x, ++tl) {
+      const int bb = t / H, h = t % H;
+      const int b = tl & 1, u = tl >> 1;
+      if (!mbar_wait(&accf[b], u & 1, &abort_flag)) {
+        fail(kErrDoneWait);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(b * BN);
+      const int q = warp * 32 + lane;  // this thread's row
+      if (MODE == kAttnScore) {
+        // MHAttentionScore (NeuroNet.cl:1662-1719): e = exp(clamp(s / koef, -100, 100)) over the
+        // unmasked keys, divided by their sum when the sum exceeds 1.  Each exponential is computed
+        // once into the warp's row buffer; the stores then go out along the keys (coalesced).
+        float *rows = reinterpret_cast<float *>(smem + C::EPI_OFF) + warp * 32 * 129;
+        float *scale = reinterpret_cast<float *>(smem + C::EPI_OFF) + 4 * 32 * 129 + warp * 32;
+        float sum = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          tmem_ld32(trow + (uint32_t)c, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int k = c + j;
+            float e = 0.f;
+            if (k < U && !(mask > 0 && k > q)) {
+              e = exp2f(clampf(v[j] * inv_koef, -100.f, 100.f) * 1.4426950408889634f);
+              if (isnan(e)) e = 0.f;
+              sum += e;
+            }
+            rows[lane * 129 + k] = e;
+          }
+        }
+        scale[lane] = sum > 1.f ? 1.f / sum : 1.f;
+        __syncwarp();
+        float *srow0 = out + (size_t)bb * U * H * U + (size_t)h * U;  // row q at srow0 + q*H*U
+        const int nrows = min(32, U - warp * 32);
+#pragma unroll 1
+        for (int r = 0; r < nrows; ++r) {
+          float *dst = srow0 + (size_t)(warp * 32 + r) * H * U;
+          const float sc = scale[r];
+#pragma unroll
+          for (int c = 0; c < BN; c += 32) {
+            const int k = c + lane;
+            if (k < U) dst[k] = rows[r * 129 + k] * sc;
+          }
+        }
+        __syncwarp();
+      } else {
+        // MHAttentionOut (NeuroNet.cl:1730-1759): O[q][h][d]
+        float v[32];
+        tmem_ld32(trow, v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) buf[lane * 33 + j] = v[j];
+        __syncwarp();
+        float *obase = out + ((size_t)bb * U * H + h) * D;  // row q at obase + q*H*D
+#pragma unroll 4
+        for (int r = 0; r < 32; ++r) {
+          const int qr = warp * 32 + r;
+          if (qr < U) obase[(size_t)qr * H * D + lane] = buf[r * 33 + lane];
+        }
+        __syncwarp();
+      }
+      tc_fence_before();
+      mbar_arrive(&acce[b]);
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  if (warp == 8) {
+    if (lane == 0) mma_commit(&drain);
+    __syncwarp();
+    if (!mbar_wait_drain(&drain, 0) && lane == 0) atomicExch(err, kErrDoneWait);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+}  // namespace tc
+
+// Whether the tensor-core attention products apply: head dimension 32, at most 128 units, every
+// tensor 16-byte aligned (units a multiple of 4 for the score rows).
+inline bool attn_tc_ok(const float *qkv, const float *scores, int U, int H, int D) {
+  return tensor_gemm_enabled() && tmap_encoder() && D == 32 && U >= 1 && U <= 128 && U % 4 == 0 && H >= 1 &&
+         ((uintptr_t)qkv & 15) == 0 && ((uintptr_t)scores & 15) == 0;
+}
+
+inline bool make_tmap2(CUtensorMap *tm, const float *p, int rank, const cuuint64_t *dims, const cuuint64_t *strides,
+                       const cuuint32_t *box, bool mn_major) {
+  cuuint32_t es[3] = {1u, 1u, 1u};
+  return tmap_encoder()(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<float *>(p), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// MODE kAttnScore: scores = softmax(Q K^T / koef); MODE kAttnOut: out = scores V.
+template <int MODE>
+inline cudaError_t attn_tc(const float *qkv, const float *scores, float *out, int B, int U, int H, int mask,
+                           float koef, cudaStream_t st) {
+  using C = tc::AttnCfg<MODE>;
+  const int D = 32;
+  CUtensorMap tmQ, tmS, tmV;
+  std::memset(&tmQ, 0, sizeof tmQ);
+  std::memset(&tmS, 0, sizeof tmS);
+  std::memset(&tmV, 0, sizeof tmV);
+  const cuuint64_t rows = (cuuint64_t)B * U, width = (cuuint64_t)3 * H * D;
+  // every map is rank 3 (the loads are 3-d; a trailing extent of 1 where the tensor is 2-d)
+  if (MODE == tc::kAttnScore) {
+    cuuint64_t dims[3] = {width, rows, 1}, strides[2] = {width * 4, width * 4 * rows};
+    cuuint32_t box[3] = {32u, 128u, 1u};
+    if (!make_tmap2(&tmQ, qkv, 3, dims, strides, box, false)) return cudaErrorInvalidValue;
+  } else {
+    cuuint64_t sd[3] = {(cuuint64_t)U, (cuuint64_t)H, rows}, ss[2] = {(cuuint64_t)U * 4, (cuuint64_t)H * U * 4};
+    cuuint32_t sb[3] = {32u, 1u, 128u};
+    if (!make_tmap2(&tmS, scores, 3, sd, ss, sb, false)) return cudaErrorInvalidValue;
+    cuuint64_t vd[3] = {width, rows, 1}, vs[2] = {width * 4, width * 4 * rows};
+    cuuint32_t vb[3] = {32u, 32u, 1u};
+    if (!make_tmap2(&tmV, qkv, 3, vd, vs, vb, true)) return cudaErrorInvalidValue;
+  }
+  auto fn = tc::attn_tc_kernel<MODE>;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::SMEM);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const int items = B * H;
+  if (items <= 0) return cudaSuccess;
+  const int grid = items < sm_count() ? items : sm_count();
+  fn<<<grid, 320, C::SMEM, st>>>(out, device_status(), U, H, items, mask, koef, tmQ, tmS, tmV);
+  return cudaGetLastError();
+}
+
+}  // namespace nn
