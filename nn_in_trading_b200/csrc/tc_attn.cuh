@@ -279,6 +279,354 @@ __global__ void __launch_bounds__(320, 1)
   }
 }
 
+// ------------------------------------------------------------------ gradient
+// MHAttentionInsideGradients (NeuroNet.cl:1777-1845) for one (sequence, head) per work item, with
+// V0[u] = V[u][0] and A[q] = sum_u S[q][u] V0[u]:
+//   dV = S^T G,   C = S o (V0^T - A),   dK = C^T (G o Q) / koef,   dQ = G o (C K) / koef.
+// Shared memory (one item at a time, 210 KB):
+//   SH / SL  S, then C: hi / lo, [u-group (4)][q row (128)][32 u], 64 KB each
+//   GH / GL  G: hi / lo, [q row][32 d], 16 KB each
+//   QR       raw Q, later raw K, [row][32 d], 16 KB
+//   XH / XL  G o Q, later K: hi / lo, 16 KB each
+//   V0, AV   128 floats each
+// S, G, Q and K tiles use the 128-byte swizzle with 32-byte granules (MN-major operands of dV and
+// dK).  For dQ, C is the K-major operand: its rows are already where the K-major layout keeps
+// them, and only the 16-byte granules inside each 128-byte row are permuted (32-byte granules
+// XOR q%4  ->  16-byte granules XOR q%8).  Score rows q >= units (the next sequence) are zeroed,
+// so they contribute nothing to the sums over q.
+struct GradCfg {
+  static constexpr uint32_t SH = 0, SL = 65536, GH = 131072, GL = 147456, QR = 163840, XH = 180224, XL = 196608;
+  static constexpr uint32_t V0 = 212992, AV = V0 + 512, END = AV + 512;
+  static constexpr uint32_t SMEM = END + 1024;
+  static_assert(SMEM <= 232448, "shared memory per CTA");
+};
+
+// byte offset of element (row r, column c) of a [row][32] tile in the 32-byte-granule swizzle
+__device__ __forceinline__ uint32_t sw32_off(int r, int c) {
+  return (uint32_t)(r * 128 + ((((c >> 3) ^ r) & 3) << 5) + (c & 7) * 4);
+}
+
+__global__ void __launch_bounds__(320, 1)
+    attn_grad_tc_kernel(const float *__restrict__ qkv, float *__restrict__ qkv_g, int *err, int U, int H, int items,
+                        float koef, const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmQKV,
+                        const __grid_constant__ CUtensorMap tmG) {
+  using C = GradCfg;
+  constexpr int D = 32;
+  constexpr uint32_t IDESC_MN = instr_desc_tf32(128, 32, true, true);   // dV, dK
+  constexpr uint32_t IDESC_KM = instr_desc_tf32(128, 32, false, true);  // dQ
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  float *V0s = reinterpret_cast<float *>(sm + C::V0), *AVs = reinterpret_cast<float *>(sm + C::AV);
+  __shared__ __align__(8) uint64_t ld1, ld2, w1, w2, w3, m1, m2, accf, ifree, qfree, wsync, drain;
+  __shared__ uint32_t tmem_slot;
+  __shared__ volatile int abort_flag;
+
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  auto fail = [&](int code) {
+    abort_flag = 1;
+    atomicExch(err, code);
+  };
+  if (tid == 0) {
+    mbar_init(&ld1, 1);
+    mbar_init(&ld2, 1);
+    mbar_init(&w1, 256);
+    mbar_init(&w2, 256);
+    mbar_init(&w3, 256);
+    mbar_init(&m1, 1);
+    mbar_init(&m2, 1);
+    mbar_init(&accf, 1);
+    mbar_init(&ifree, 256);
+    mbar_init(&qfree, 256);
+    mbar_init(&wsync, 256);
+    mbar_init(&drain, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 8) {
+    tmem_alloc(&tmem_slot, 128);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;  // dV at column 0, dK at 32, dQ at 64
+  const float inv_koef = 1.f / koef;
+  const size_t rs = (size_t)3 * H * D;  // qkv row stride
+
+  if (warp == 9) {
+    // ------------------------------------------------------------ loader
+    if (lane == 0) {
+      int n = 0, issued1 = 0, issued2 = 0;
+      for (int t = blockIdx.x; t < items && !abort_flag; t += gridDim.x, ++n) {
+        const int b = t / H, h = t % H;
+        if (n > 0 && !mbar_wait(&ifree, (n - 1) & 1, &abort_flag)) {
+          fail(kErrEmptyWait);
+          break;
+        }
+        mbar_arrive_expect_tx(&ld1, 65536u + 16384u + 16384u);
+        ++issued1;
+        for (int ug = 0; ug < 4; ++ug)
+          for (int qc = 0; qc < 4; ++qc)
+            tma_load_3d(sm + C::SH + ug * 16384 + qc * 4096, &tmS, 32 * ug, h, b * U + 32 * qc, &ld1);
+        for (int qc = 0; qc < 4; ++qc) {
+          tma_load_3d(sm + C::GH + qc * 4096, &tmG, h * D, b * U + 32 * qc, 0, &ld1);
+          tma_load_3d(sm + C::QR + qc * 4096, &tmQKV, h * D, b * U + 32 * qc, 0, &ld1);
+        }
+        // raw K into QR once the workers have consumed Q
+        if (!mbar_wait(&qfree, n & 1, &abort_flag)) {
+          fail(kErrEmptyWait);
+          break;
+        }
+        mbar_arrive_expect_tx(&ld2, 16384u);
+        ++issued2;
+        for (int uc = 0; uc < 4; ++uc)
+          tma_load_3d(sm + C::QR + uc * 4096, &tmQKV, (H + h) * D, b * U + 32 * uc, 0, &ld2);
+      }
+      // wait for the last copies into shared memory before exiting
+      if (issued1 > 0 && !mbar_wait_drain(&ld1, (issued1 - 1) & 1) && !abort_flag) fail(kErrFullWait);
+      if (issued2 > 0 && !mbar_wait_drain(&ld2, (issued2 - 1) & 1) && !abort_flag) fail(kErrFullWait);
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------ MMA issue
+    int n = 0;
+    for (int t = blockIdx.x; t < items && !abort_flag; t += gridDim.x, ++n) {
+      const uint32_t par = n & 1;
+      // dV = S^T G
+      if (!mbar_wait(&w1, par, &abort_flag)) {
+        if (lane == 0) fail(kErrFullWait);
+        break;
+      }
+      tc_fence_after();
+      if (lane == 0) {
+        for (int s = 0; s < 16; ++s) {
+          const uint64_t ah = smem_desc(smem_u32(sm + C::SH) + 1024u * s, 16384u, 512u, 1u);
+          const uint64_t al = smem_desc(smem_u32(sm + C::SL) + 1024u * s, 16384u, 512u, 1u);
+          const uint64_t bh = smem_desc(smem_u32(sm + C::GH) + 1024u * s, 4096u, 512u, 1u);
+          const uint64_t bl = smem_desc(smem_u32(sm + C::GL) + 1024u * s, 4096u, 512u, 1u);
+          mma_tf32(tmem, al, bh, IDESC_MN, s != 0 ? 1u : 0u);
+          mma_tf32(tmem, ah, bl, IDESC_MN, 1u);
+          mma_tf32(tmem, ah, bh, IDESC_MN, 1u);
+        }
+        mma_commit(&m1);
+      }
+      __syncwarp();
+      // dK' = C^T (G o Q)
+      if (!mbar_wait(&w2, par, &abort_flag)) {
+        if (lane == 0) fail(kErrFullWait);
+        break;
+      }
+      tc_fence_after();
+      if (lane == 0) {
+        for (int s = 0; s < 16; ++s) {
+          const uint64_t ah = smem_desc(smem_u32(sm + C::SH) + 1024u * s, 16384u, 512u, 1u);
+          const uint64_t al = smem_desc(smem_u32(sm + C::SL) + 1024u * s, 16384u, 512u, 1u);
+          const uint64_t bh = smem_desc(smem_u32(sm + C::XH) + 1024u * s, 4096u, 512u, 1u);
+          const uint64_t bl = smem_desc(smem_u32(sm + C::XL) + 1024u * s, 4096u, 512u, 1u);
+          mma_tf32(tmem + 32, al, bh, IDESC_MN, s != 0 ? 1u : 0u);
+          mma_tf32(tmem + 32, ah, bl, IDESC_MN, 1u);
+          mma_tf32(tmem + 32, ah, bh, IDESC_MN, 1u);
+        }
+        mma_commit(&m2);
+      }
+      __syncwarp();
+      // dQ' = C K  (C as the K-major operand: u-group s/4, 32 bytes per 8-wide k step)
+      if (!mbar_wait(&w3, par, &abort_flag)) {
+        if (lane == 0) fail(kErrFullWait);
+        break;
+      }
+      tc_fence_after();
+      if (lane == 0) {
+        for (int s = 0; s < 16; ++s) {
+          const uint32_t ao = 16384u * (s >> 2) + 32u * (s & 3);
+          const uint64_t ah = smem_desc(smem_u32(sm + C::SH) + ao, 16u, 1024u, 2u);
+          const uint64_t al = smem_desc(smem_u32(sm + C::SL) + ao, 16u, 1024u, 2u);
+          const uint64_t bh = smem_desc(smem_u32(sm + C::XH) + 1024u * s, 4096u, 512u, 1u);
+          const uint64_t bl = smem_desc(smem_u32(sm + C::XL) + 1024u * s, 4096u, 512u, 1u);
+          mma_tf32(tmem + 64, al, bh, IDESC_KM, s != 0 ? 1u : 0u);
+          mma_tf32(tmem + 64, ah, bl, IDESC_KM, 1u);
+          mma_tf32(tmem + 64, ah, bh, IDESC_KM, 1u);
+        }
+        mma_commit(&accf);
+      }
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------------------------------------ workers (warps 0-7)
+    const int wt = tid;  // 0..255
+    uint32_t nsync = 0;
+    // bounded barrier among the 256 workers (an mbarrier phase per use)
+    auto worker_sync = [&]() -> bool {
+      mbar_arrive(&wsync);
+      const bool ok = mbar_wait(&wsync, nsync & 1, &abort_flag);
+      ++nsync;
+      return ok;
+    };
+    int n = 0;
+    for (int t = blockIdx.x; t < items && !abort_flag; t += gridDim.x, ++n) {
+      const int b = t / H, h = t % H;
+      const uint32_t par = n & 1;
+      // V0 (feature 0 of V) for every unit of the tile; zero past `units`
+      if (wt < 128) V0s[wt] = wt < U ? nan0(qkv[(size_t)(b * U + wt) * rs + (size_t)(2 * H + h) * D]) : 0.f;
+      if (!mbar_wait(&ld1, par, &abort_flag)) {
+        fail(kErrFullWait);
+        break;
+      }
+      // W1: split S (rows q >= units zeroed), split G, G o Q -> XH / XL
+      for (uint32_t f = wt; f < 4096; f += 256) {  // S: 64 KB = 4096 chunks
+        const uint32_t off = 16u * f;
+        const int q = (off & 16383u) >> 7;
+        if (q >= U) {
+          *reinterpret_cast<float4 *>(sm + C::SH + off) = make_float4(0.f, 0.f, 0.f, 0.f);
+          *reinterpret_cast<float4 *>(sm + C::SL + off) = make_float4(0.f, 0.f, 0.f, 0.f);
+        } else {
+          split_in_place(sm + C::SH, sm + C::SL, off);
+        }
+      }
+      for (uint32_t f = wt; f < 1024; f += 256) {  // G and G o Q: 16 KB = 1024 chunks
+        const uint32_t off = 16u * f;
+        split_in_place(sm + C::GH, sm + C::GL, off);
+        const float4 g = *reinterpret_cast<const float4 *>(sm + C::GH + off);
+        const float4 qv = *reinterpret_cast<const float4 *>(sm + C::QR + off);
+        *reinterpret_cast<float4 *>(sm + C::XH + off) = make_float4(g.x * qv.x, g.y * qv.y, g.z * qv.z, g.w * qv.w);
+        split_in_place(sm + C::XH, sm + C::XL, off);
+      }
+      if (!worker_sync()) {
+        fail(kErrFullWait);
+        break;
+      }
+      // A[q] = sum_u S[q][u] V0[u]: a warp per row, lanes along u (one 128-byte row per u-group)
+      for (int q = warp; q < 128; q += 8) {
+        float a = 0.f;
+#pragma unroll
+        for (int ug = 0; ug < 4; ++ug) {
+          const float sv = *reinterpret_cast<const float *>(sm + C::SH + ug * 16384 + sw32_off(q, lane));
+          a = fmaf(sv, V0s[32 * ug + lane], a);
+        }
+        a = warp_sum(a);
+        if (lane == 0) AVs[q] = a;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&w1);
+      mbar_arrive(&qfree);
+      if (!worker_sync()) {  // AVs complete before W2 reads it
+        fail(kErrFullWait);
+        break;
+      }
+      // W2: C = S o (V0[u] - A[q]) in place, once the dV MMAs have read S
+      if (!mbar_wait(&m1, par, &abort_flag)) {
+        fail(kErrDoneWait);
+        break;
+      }
+      tc_fence_after();
+      for (uint32_t f = wt; f < 4096; f += 256) {
+        const uint32_t off = 16u * f;
+        const int ug = off >> 14, q = (off & 16383u) >> 7;
+        const int c0 = ((((off & 127u) >> 5) ^ q) & 3) * 8 + ((off & 31u) >> 2);  // logical column of lane 0
+        const float4 hi = *reinterpret_cast<const float4 *>(sm + C::SH + off);  // the full fp32 S
+        const float aq = AVs[q];
+        const int u0 = 32 * ug + c0;
+        float4 cv = make_float4(hi.x * (V0s[u0] - aq), hi.y * (V0s[u0 + 1] - aq), hi.z * (V0s[u0 + 2] - aq),
+                                hi.w * (V0s[u0 + 3] - aq));
+        *reinterpret_cast<float4 *>(sm + C::SH + off) = cv;
+        split_in_place(sm + C::SH, sm + C::SL, off);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&w2);
+      // W3: once dK has read C and G o Q: permute C's rows to the K-major swizzle, split raw K
+      if (!mbar_wait(&m2, par, &abort_flag)) {
+        fail(kErrDoneWait);
+        break;
+      }
+      tc_fence_after();
+      for (int row = wt; row < 1024; row += 256) {  // 2 buffers x 4 u-groups x 128 rows
+        uint8_t *base = sm + ((row & 512) ? C::SL : C::SH) + ((row >> 7) & 3) * 16384 + (row & 127) * 128;
+        const int q = row & 127;
+        float4 g[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) g[j] = *reinterpret_cast<const float4 *>(base + 16 * j);
+        // register-only select of granule i (a runtime index into g would go to local memory)
+        auto pick = [&](int i) -> float4 {
+          float4 v = g[0];
+#pragma unroll
+          for (int j = 1; j < 8; ++j) v = (i == j) ? g[j] : v;
+          return v;
+        };
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {  // destination: physical 16-byte granule p of the K-major row
+          const int l16 = (p ^ q) & 7;  // logical granule stored there
+          const int from = 2 * (((l16 >> 1) ^ q) & 3) + (l16 & 1);  // its place in the MN-major row
+          *reinterpret_cast<float4 *>(base + 16 * p) = pick(from);
+        }
+      }
+      if (!mbar_wait(&ld2, par, &abort_flag)) {
+        fail(kErrFullWait);
+        break;
+      }
+      for (uint32_t f = wt; f < 1024; f += 256) {
+        const uint32_t off = 16u * f;
+        *reinterpret_cast<float4 *>(sm + C::XH + off) = *reinterpret_cast<const float4 *>(sm + C::QR + off);
+        split_in_place(sm + C::XH, sm + C::XL, off);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&w3);
+      // epilogue: warps 0-3 dV and dK rows u, warps 4-7 dQ rows q (tensor-memory lane quarter w % 4)
+      if (!mbar_wait(&accf, par, &abort_flag)) {
+        fail(kErrDoneWait);
+        break;
+      }
+      tc_fence_after();
+      const int r = (warp & 3) * 32 + lane;
+      const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+      float *grow = qkv_g + (size_t)(b * U + r) * rs;
+      if (warp < 4) {
+        float v[32], k[32];
+        tmem_ld32(tl + 0, v);
+        tmem_ld32(tl + 32, k);
+        if (r < U) {
+          float4 *dv = reinterpret_cast<float4 *>(grow + (size_t)(2 * H + h) * D);
+          float4 *dk = reinterpret_cast<float4 *>(grow + (size_t)(H + h) * D);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            dv[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            dk[j] = make_float4(k[4 * j] * inv_koef, k[4 * j + 1] * inv_koef, k[4 * j + 2] * inv_koef,
+                                k[4 * j + 3] * inv_koef);
+          }
+        }
+      } else {
+        float v[32];
+        tmem_ld32(tl + 64, v);
+        if (r < U) {
+          float4 *dq = reinterpret_cast<float4 *>(grow + (size_t)h * D);
+          const uint8_t *gq = sm + C::GH + (r >> 5) * 4096;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float gv[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) gv[e] = *reinterpret_cast<const float *>(gq + sw32_off(r & 31, 4 * j + e));
+            dq[j] = make_float4(gv[0] * v[4 * j] * inv_koef, gv[1] * v[4 * j + 1] * inv_koef,
+                                gv[2] * v[4 * j + 2] * inv_koef, gv[3] * v[4 * j + 3] * inv_koef);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&ifree);
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  if (warp == 8) {
+    if (lane == 0) mma_commit(&drain);
+    __syncwarp();
+    if (!mbar_wait_drain(&drain, 0) && lane == 0) atomicExch(err, kErrDoneWait);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
+  }
+}
+
 }  // namespace tc
 
 // Whether the tensor-core attention products apply: head dimension 32, at most 128 units, every
@@ -332,6 +680,42 @@ inline cudaError_t attn_tc(const float *qkv, const float *scores, float *out, in
   if (items <= 0) return cudaSuccess;
   const int grid = items < sm_count() ? items : sm_count();
   fn<<<grid, 320, C::SMEM, st>>>(out, device_status(), U, H, items, mask, koef, tmQ, tmS, tmV);
+  return cudaGetLastError();
+}
+
+// MHAttentionInsideGradients on the tensor cores (same applicability as attn_tc_ok; `grad` aligned).
+inline cudaError_t attn_grad_tc(const float *qkv, float *qkv_g, const float *scores, const float *grad, int B, int U,
+                                int H, float koef, cudaStream_t st) {
+  const int D = 32;
+  CUtensorMap tmS, tmQKV, tmG;
+  const cuuint64_t rows = (cuuint64_t)B * U, width = (cuuint64_t)3 * H * D, gw = (cuuint64_t)H * D;
+  {
+    cuuint64_t d[3] = {(cuuint64_t)U, (cuuint64_t)H, rows}, s[2] = {(cuuint64_t)U * 4, (cuuint64_t)H * U * 4};
+    cuuint32_t bx[3] = {32u, 1u, 32u};
+    if (!make_tmap2(&tmS, scores, 3, d, s, bx, true)) return cudaErrorInvalidValue;
+  }
+  {
+    cuuint64_t d[3] = {width, rows, 1}, s[2] = {width * 4, width * 4 * rows};
+    cuuint32_t bx[3] = {32u, 32u, 1u};
+    if (!make_tmap2(&tmQKV, qkv, 3, d, s, bx, true)) return cudaErrorInvalidValue;
+  }
+  {
+    cuuint64_t d[3] = {gw, rows, 1}, s[2] = {gw * 4, gw * 4 * rows};
+    cuuint32_t bx[3] = {32u, 32u, 1u};
+    if (!make_tmap2(&tmG, grad, 3, d, s, bx, true)) return cudaErrorInvalidValue;
+  }
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(tc::attn_grad_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)tc::GradCfg::SMEM);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const int items = B * H;
+  if (items <= 0) return cudaSuccess;
+  const int grid = items < sm_count() ? items : sm_count();
+  tc::attn_grad_tc_kernel<<<grid, 320, tc::GradCfg::SMEM, st>>>(qkv, qkv_g, device_status(), U, H, items, koef, tmS,
+                                                                 tmQKV, tmG);
   return cudaGetLastError();
 }
 

@@ -40,3 +40,15 @@ def test_score(ctx, units, heads, batch, mask):
 @pytest.mark.parametrize("units,heads,batch", SHAPES, ids=[f"u{u}-h{h}-b{b}" for u, h, b in SHAPES])
 def test_out(ctx, units, heads, batch):
     check_batched_per_sample(ctx, out_case(units, heads), batch, 9100 + units + heads)
+
+
+def grad_case(units, heads):
+    n = units * 3 * heads * D
+    return Case(f"MHAttentionInsideGradients/{units}-{heads}-{D}", "MHAttentionInsideGradients",
+                [A(n), A(n, "zeros"), A(units * heads * units, "unit"), A(units * heads * D, "grad")],
+                (units, heads, D), meta={"softmax_scores": 1})
+
+
+@pytest.mark.parametrize("units,heads,batch", SHAPES, ids=[f"u{u}-h{h}-b{b}" for u, h, b in SHAPES])
+def test_inside_gradients(ctx, units, heads, batch):
+    check_batched_per_sample(ctx, grad_case(units, heads), batch, 9200 + units + heads)
