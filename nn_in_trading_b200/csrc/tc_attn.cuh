@@ -288,7 +288,7 @@ __global__ void __launch_bounds__(320, 1)
 //   GH / GL  G: hi / lo, [q row][32 d], 16 KB each
 //   QR       raw Q, later raw K, [row][32 d], 16 KB
 //   XH / XL  G o Q, later K: hi / lo, 16 KB each
-//   V0, AV   128 floats each
+//   V0, AV   128 floats each;  VR: V[u][0..3] per row (TMA), the source of V0
 // S, G, Q and K tiles use the 128-byte swizzle with 32-byte granules (MN-major operands of dV and
 // dK).  For dQ, C is the K-major operand: its rows are already where the K-major layout keeps
 // them, and only the 16-byte granules inside each 128-byte row are permuted (32-byte granules
@@ -296,7 +296,7 @@ __global__ void __launch_bounds__(320, 1)
 // so they contribute nothing to the sums over q.
 struct GradCfg {
   static constexpr uint32_t SH = 0, SL = 65536, GH = 131072, GL = 147456, QR = 163840, XH = 180224, XL = 196608;
-  static constexpr uint32_t V0 = 212992, AV = V0 + 512, END = AV + 512;
+  static constexpr uint32_t V0 = 212992, AV = V0 + 512, VR = AV + 512, END = VR + 2048;
   static constexpr uint32_t SMEM = END + 1024;
   static_assert(SMEM <= 232448, "shared memory per CTA");
 };
@@ -309,7 +309,7 @@ __device__ __forceinline__ uint32_t sw32_off(int r, int c) {
 __global__ void __launch_bounds__(320, 1)
     attn_grad_tc_kernel(const float *__restrict__ qkv, float *__restrict__ qkv_g, int *err, int U, int H, int items,
                         float koef, const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmQKV,
-                        const __grid_constant__ CUtensorMap tmG) {
+                        const __grid_constant__ CUtensorMap tmG, const __grid_constant__ CUtensorMap tmV0) {
   using C = GradCfg;
   constexpr int D = 32;
   constexpr uint32_t IDESC_MN = instr_desc_tf32(128, 32, true, true);   // dV, dK
@@ -363,7 +363,8 @@ __global__ void __launch_bounds__(320, 1)
           fail(kErrEmptyWait);
           break;
         }
-        mbar_arrive_expect_tx(&ld1, 65536u + 16384u + 16384u);
+        mbar_arrive_expect_tx(&ld1, 65536u + 16384u + 16384u + 2048u);
+        tma_load_3d(sm + C::VR, &tmV0, (2 * H + h) * D, b * U, 0, &ld1);
         ++issued1;
         for (int ug = 0; ug < 4; ++ug)
           for (int qc = 0; qc < 4; ++qc)
@@ -465,12 +466,12 @@ __global__ void __launch_bounds__(320, 1)
     for (int t = blockIdx.x; t < items && !abort_flag; t += gridDim.x, ++n) {
       const int b = t / H, h = t % H;
       const uint32_t par = n & 1;
-      // V0 (feature 0 of V) for every unit of the tile; zero past `units`
-      if (wt < 128) V0s[wt] = wt < U ? nan0(qkv[(size_t)(b * U + wt) * rs + (size_t)(2 * H + h) * D]) : 0.f;
       if (!mbar_wait(&ld1, par, &abort_flag)) {
         fail(kErrFullWait);
         break;
       }
+      // V0 (feature 0 of V) for every unit of the tile; zero past `units`
+      if (wt < 128) V0s[wt] = wt < U ? nan0(reinterpret_cast<const float *>(sm + C::VR)[4 * wt]) : 0.f;
       // W1: split S (rows q >= units zeroed), split G, G o Q -> XH / XL
       for (uint32_t f = wt; f < 4096; f += 256) {  // S: 64 KB = 4096 chunks
         const uint32_t off = 16u * f;
@@ -495,15 +496,26 @@ __global__ void __launch_bounds__(320, 1)
         break;
       }
       // A[q] = sum_u S[q][u] V0[u]: a warp per row, lanes along u (one 128-byte row per u-group)
-      for (int q = warp; q < 128; q += 8) {
-        float a = 0.f;
+      {
+        float v0[4];
 #pragma unroll
-        for (int ug = 0; ug < 4; ++ug) {
-          const float sv = *reinterpret_cast<const float *>(sm + C::SH + ug * 16384 + sw32_off(q, lane));
-          a = fmaf(sv, V0s[32 * ug + lane], a);
+        for (int ug = 0; ug < 4; ++ug) v0[ug] = V0s[32 * ug + lane];
+        for (int q0 = warp * 4; q0 < 128; q0 += 32) {  // four rows at a time: independent reductions
+          float a[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            a[i] = 0.f;
+#pragma unroll
+            for (int ug = 0; ug < 4; ++ug)
+              a[i] = fmaf(*reinterpret_cast<const float *>(sm + C::SH + ug * 16384 + sw32_off(q0 + i, lane)), v0[ug],
+                          a[i]);
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] += __shfl_xor_sync(0xffffffffu, a[i], o);
+          if (lane < 4) AVs[q0 + lane] = lane == 0 ? a[0] : lane == 1 ? a[1] : lane == 2 ? a[2] : a[3];
         }
-        a = warp_sum(a);
-        if (lane == 0) AVs[q] = a;
       }
       fence_proxy_async_smem();
       mbar_arrive(&w1);
@@ -524,9 +536,8 @@ __global__ void __launch_bounds__(320, 1)
         const int c0 = ((((off & 127u) >> 5) ^ q) & 3) * 8 + ((off & 31u) >> 2);  // logical column of lane 0
         const float4 hi = *reinterpret_cast<const float4 *>(sm + C::SH + off);  // the full fp32 S
         const float aq = AVs[q];
-        const int u0 = 32 * ug + c0;
-        float4 cv = make_float4(hi.x * (V0s[u0] - aq), hi.y * (V0s[u0 + 1] - aq), hi.z * (V0s[u0 + 2] - aq),
-                                hi.w * (V0s[u0 + 3] - aq));
+        const float4 v = *reinterpret_cast<const float4 *>(V0s + 32 * ug + c0);
+        float4 cv = make_float4(hi.x * (v.x - aq), hi.y * (v.y - aq), hi.z * (v.z - aq), hi.w * (v.w - aq));
         *reinterpret_cast<float4 *>(sm + C::SH + off) = cv;
         split_in_place(sm + C::SH, sm + C::SL, off);
       }
@@ -541,10 +552,13 @@ __global__ void __launch_bounds__(320, 1)
       for (int row = wt; row < 1024; row += 256) {  // 2 buffers x 4 u-groups x 128 rows
         uint8_t *base = sm + ((row & 512) ? C::SL : C::SH) + ((row >> 7) & 3) * 16384 + (row & 127) * 128;
         const int q = row & 127;
+        // g[j] = physical granule (j + q) % 8: the eight lanes of a shared-memory phase touch eight
+        // different 16-byte bank groups although their rows are 128 bytes apart
+        const int rot = q & 7;
         float4 g[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) g[j] = *reinterpret_cast<const float4 *>(base + 16 * j);
-        // register-only select of granule i (a runtime index into g would go to local memory)
+        for (int j = 0; j < 8; ++j) g[j] = *reinterpret_cast<const float4 *>(base + 16 * ((j + rot) & 7));
+        // register-only select of g[i] (a runtime index into g would go to local memory)
         auto pick = [&](int i) -> float4 {
           float4 v = g[0];
 #pragma unroll
@@ -552,10 +566,11 @@ __global__ void __launch_bounds__(320, 1)
           return v;
         };
 #pragma unroll
-        for (int p = 0; p < 8; ++p) {  // destination: physical 16-byte granule p of the K-major row
-          const int l16 = (p ^ q) & 7;  // logical granule stored there
-          const int from = 2 * (((l16 >> 1) ^ q) & 3) + (l16 & 1);  // its place in the MN-major row
-          *reinterpret_cast<float4 *>(base + 16 * p) = pick(from);
+        for (int j = 0; j < 8; ++j) {
+          const int p = (j + rot) & 7;                                 // destination: K-major granule p
+          const int l16 = (p ^ q) & 7;                                 // the logical granule stored there
+          const int from = 2 * (((l16 >> 1) ^ q) & 3) + (l16 & 1);    // its place in the MN-major row
+          *reinterpret_cast<float4 *>(base + 16 * p) = pick((from - rot) & 7);
         }
       }
       if (!mbar_wait(&ld2, par, &abort_flag)) {
@@ -597,14 +612,19 @@ __global__ void __launch_bounds__(320, 1)
         tmem_ld32(tl + 64, v);
         if (r < U) {
           float4 *dq = reinterpret_cast<float4 *>(grow + (size_t)h * D);
-          const uint8_t *gq = sm + C::GH + (r >> 5) * 4096;
+          const uint8_t *grw = sm + C::GH + (r >> 5) * 4096 + (r & 31) * 128;  // G row r (32-byte granules)
+          const int rot = r & 7;
+          float4 g[8];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float gv[4];
+          for (int j = 0; j < 8; ++j) g[j] = *reinterpret_cast<const float4 *>(grw + 16 * ((j + rot) & 7));
 #pragma unroll
-            for (int e = 0; e < 4; ++e) gv[e] = *reinterpret_cast<const float *>(gq + sw32_off(r & 31, 4 * j + e));
-            dq[j] = make_float4(gv[0] * v[4 * j] * inv_koef, gv[1] * v[4 * j + 1] * inv_koef,
-                                gv[2] * v[4 * j + 2] * inv_koef, gv[3] * v[4 * j + 3] * inv_koef);
+          for (int l16 = 0; l16 < 8; ++l16) {  // features 4*l16 .. 4*l16+3
+            const int ps = 2 * (((l16 >> 1) ^ r) & 3) + (l16 & 1), idx = (ps - rot) & 7;
+            float4 gv = g[0];
+#pragma unroll
+            for (int j = 1; j < 8; ++j) gv = (idx == j) ? g[j] : gv;
+            dq[l16] = make_float4(gv.x * v[4 * l16] * inv_koef, gv.y * v[4 * l16 + 1] * inv_koef,
+                                  gv.z * v[4 * l16 + 2] * inv_koef, gv.w * v[4 * l16 + 3] * inv_koef);
           }
         }
       }
@@ -687,8 +707,16 @@ inline cudaError_t attn_tc(const float *qkv, const float *scores, float *out, in
 inline cudaError_t attn_grad_tc(const float *qkv, float *qkv_g, const float *scores, const float *grad, int B, int U,
                                 int H, float koef, cudaStream_t st) {
   const int D = 32;
-  CUtensorMap tmS, tmQKV, tmG;
+  CUtensorMap tmS, tmQKV, tmG, tmV0;
   const cuuint64_t rows = (cuuint64_t)B * U, width = (cuuint64_t)3 * H * D, gw = (cuuint64_t)H * D;
+  {  // the first 4 features of each V row (feature 0 is V0), no swizzle: row u at 16*u bytes
+    cuuint64_t d[3] = {width, rows, 1}, s[2] = {width * 4, width * 4 * rows};
+    cuuint32_t bx[3] = {4u, 128u, 1u}, es[3] = {1u, 1u, 1u};
+    if (tmap_encoder()(&tmV0, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(qkv), d, s, bx, es,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
   {
     cuuint64_t d[3] = {(cuuint64_t)U, (cuuint64_t)H, rows}, s[2] = {(cuuint64_t)U * 4, (cuuint64_t)H * U * 4};
     cuuint32_t bx[3] = {32u, 1u, 32u};
@@ -715,7 +743,7 @@ inline cudaError_t attn_grad_tc(const float *qkv, float *qkv_g, const float *sco
   if (items <= 0) return cudaSuccess;
   const int grid = items < sm_count() ? items : sm_count();
   tc::attn_grad_tc_kernel<<<grid, 320, tc::GradCfg::SMEM, st>>>(qkv, qkv_g, device_status(), U, H, items, koef, tmS,
-                                                                 tmQKV, tmG);
+                                                                 tmQKV, tmG, tmV0);
   return cudaGetLastError();
 }
 
