@@ -6,6 +6,8 @@
 //
 // qkv layout is the reference's [unit][3][head][dimension]
 // (NeuroNet.cl:1674, 1693, 1754); scores are [query][head][key].
+#include <algorithm>
+
 #include "../../include/nn_b200.h"
 #include "attn_smem.cuh"
 #include "tc_attn.cuh"
@@ -310,6 +312,24 @@ __global__ void sum_matrix_kernel(const float *a, const float *bm, float *out, f
   out[i * so + index] = nan0(raw);
 }
 
+// Same with zero row shifts (the encoder's residual sums): a flat float4 stream.
+__global__ void sum_matrix_flat4_kernel(const float4 *a, const float4 *bm, float4 *out, float4 *flags, size_t n4,
+                                        float mult) {
+  for (size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x; t < n4; t += (size_t)gridDim.x * blockDim.x) {
+    const float4 x = a[t], y = bm[t];
+    const float r[4] = {(x.x + y.x) * mult, (x.y + y.y) * mult, (x.z + y.z) * mult, (x.w + y.w) * mult};
+    if (flags) {
+      const float xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
+      float f[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        f[e] = (!isfinite(xs[e]) || !isfinite(ys[e]) || !isfinite(xs[e] + ys[e]) || !isfinite(r[e])) ? 1.f : 0.f;
+      flags[t] = make_float4(f[0], f[1], f[2], f[3]);
+    }
+    out[t] = make_float4(nan0(r[0]), nan0(r[1]), nan0(r[2]), nan0(r[3]));
+  }
+}
+
 static int k_sum_matrix(Launch &L) {
   const int rows = (int)L.nd.g[0] * L.B;
   const int dim = L.i(3), s1 = L.i(5), s2 = L.i(6), so = L.i(7), fe = L.i(9);
@@ -324,6 +344,16 @@ static int k_sum_matrix(Launch &L) {
     if (!flags) return NN_ERR_BOUNDS;
   }
   size_t n = (size_t)rows * dim;
+  auto al16 = [](const void *p) { return ((uintptr_t)p & 15) == 0; };
+  if (s1 == 0 && s2 == 0 && so == 0 && n % 4 == 0 && al16(a) && al16(b) && al16(o) && (!flags || al16(flags))) {
+    const size_t n4 = n / 4;
+    const unsigned blocks = (unsigned)std::min<size_t>((n4 + 255) / 256, 148 * 16);
+    sum_matrix_flat4_kernel<<<blocks, 256, 0, L.stream>>>(
+        reinterpret_cast<const float4 *>(a), reinterpret_cast<const float4 *>(b), reinterpret_cast<float4 *>(o),
+        reinterpret_cast<float4 *>(flags), n4, L.f(4));
+    NN_CHECK_LAUNCH(L);
+    return NN_OK;
+  }
   sum_matrix_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(a, b, o, flags, rows, dim, L.f(4), s1, s2, so, fe);
   NN_CHECK_LAUNCH(L);
   return NN_OK;
@@ -354,12 +384,51 @@ __global__ void normalize_rows_kernel(float *buf, int rows, int dim) {
   }
 }
 
+// Same for rows of at most 32*EPL floats: the row is read once into registers.
+template <int EPL>
+__global__ void normalize_rows_reg_kernel(float *buf, int rows, int dim) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  float *row = buf + (size_t)warp * dim;
+  float x[EPL];
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int i = lane + 32 * j;
+    x[j] = i < dim ? row[i] : 0.f;
+    s += i < dim ? nan0(x[j]) : 0.f;
+  }
+  const float mean = warp_sum(s) / (float)dim;
+  float m2 = 0.f;
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int i = lane + 32 * j;
+    const float c = nan0(x[j]) - mean;
+    m2 += i < dim ? c * c : 0.f;
+  }
+  const float variance = warp_sum(m2) / (float)(dim - 1);
+  const bool scale = variance > 1.f;
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int i = lane + 32 * j;
+    const float c = x[j] - mean;
+    if (i < dim) row[i] = nan0(scale ? c / variance : c);
+  }
+}
+
 static int k_normalize(Launch &L) {
   const int rows = (int)L.nd.g[0] * L.B, dim = L.i(1);
   if (dim < 1) return NN_OK;  // the reference returns without touching the buffer
   float *b = L.buf(0, (size_t)rows * dim);
   if (!b) return NN_ERR_BOUNDS;
-  normalize_rows_kernel<<<ceil_div((size_t)rows * 32, 256), 256, 0, L.stream>>>(b, rows, dim);
+  const unsigned blocks = ceil_div((size_t)rows * 32, 256);
+  if (dim <= 64)
+    normalize_rows_reg_kernel<2><<<blocks, 256, 0, L.stream>>>(b, rows, dim);
+  else if (dim <= 128)
+    normalize_rows_reg_kernel<4><<<blocks, 256, 0, L.stream>>>(b, rows, dim);
+  else
+    normalize_rows_kernel<<<blocks, 256, 0, L.stream>>>(b, rows, dim);
   NN_CHECK_LAUNCH(L);
   return NN_OK;
 }

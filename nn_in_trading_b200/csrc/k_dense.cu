@@ -454,7 +454,7 @@ __global__ void normalize_weights_kernel(float *buf, int rows, int dim) {
   for (int guard = 0; guard < 64; ++guard) {
     s = 0.f;
     for (int i = lane; i < dim; i += 32) {
-      float q = nan0(row[i]) / k;
+      const float q = guard == 0 ? nan0(row[i]) : nan0(row[i]) / k;  // k == 1 on the first pass
       s += q * q;
     }
     s = warp_sum(s);
