@@ -99,10 +99,10 @@ class ClockSampler:
 
 # --------------------------------------------------- algorithmic work model
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch, from one ncu capture
-# of the batch-256 workload:  ncu --set full --clock-control none -k regex:mh_grad_smem -s 2 -c 1
+# of the batch-256 workload:  ncu --set full --clock-control none -k regex:attn_grad -s 4 -c 1
 #   python bench.py --steps 3 --warmup 3 --no-cpu-baseline
 # Keyed by the reference kernel; scaled to other batches by the sequences a launch processes.
-NCU_TRAFFIC = {"MHAttentionInsideGradients": (312.09e6, 256)}
+NCU_TRAFFIC = {"MHAttentionInsideGradients": (315.18e6, 256)}
 
 
 def op_work(op, B):
