@@ -1,5 +1,9 @@
-"""Smoke check used by __graft_entry__.smoke(): a tiny dense forward, backward and
-Adam step through the C ABI on cuda:0, compared with the numpy oracle."""
+"""Smoke check used by __graft_entry__.smoke(): through the C ABI on cuda:0, compared with the
+numpy oracle,
+  * a tiny dense forward, backward and Adam step (the SIMT kernels), and
+  * the attention encoder's kernels at shapes that take the tensor-core paths: MHAttentionScore,
+    MHAttentionOut and MHAttentionInsideGradients for 2 sequences x 2 heads of 120 units x 32
+    features, and a 1x1 FeedForwardConv of those 240 rows (tcgen05 GEMM)."""
 from __future__ import annotations
 
 import numpy as np
@@ -45,3 +49,43 @@ def run_smoke() -> None:
     check_close("smoke weights", got["w"][:w.size], w, w0)
     check_close("smoke m", got["m"][:w.size], m)
     check_close("smoke v", got["v"][:w.size], v)
+    run_smoke_encoder()
+
+
+def run_smoke_encoder() -> None:
+    from nn_in_trading_b200 import Context
+    rng = np.random.default_rng(11)
+    B, U, H, D, W = 2, 120, 2, 32, 64
+    nq = U * 3 * H * D
+    qkv = rng.standard_normal(B * nq).astype(np.float32)
+    gout = (rng.standard_normal(B * U * H * D) * 0.01).astype(np.float32)
+    x = rng.standard_normal(B * U * W).astype(np.float32)
+    wc = rng.uniform(-0.12, 0.12, 3 * H * D * (W + 1)).astype(np.float32)
+    with Context(0) as ctx:
+        hq, hs, ho, hg, hqg = (ctx.buffer(n) for n in (B * nq, B * U * H * U, B * U * H * D, gout.size, B * nq))
+        hx, hw, hc = ctx.buffer(x.size), ctx.buffer(wc.size), ctx.buffer(B * U * 3 * H * D)
+        for h, a in ((hq, qkv), (hg, gout), (hx, x), (hw, wc)):
+            ctx.write(h, a)
+        ctx.kernel("MHAttentionScore").args(hq, hs, D, 0).batch(B).run((U, H))
+        ctx.kernel("MHAttentionOut").args(hs, hq, ho, D).batch(B).run((U, H))
+        ctx.kernel("MHAttentionInsideGradients").args(hq, hqg, hs, hg).batch(B).run((U, H, D))
+        ctx.kernel("FeedForwardConv").args(hw, hx, hc, U * W, W, W, 3 * H * D, K.NONE).batch(B).run((U, 3 * H * D, 1))
+        got = {k: ctx.read(h) for k, h in (("s", hs), ("o", ho), ("qg", hqg), ("c", hc))}
+    for b in range(B):
+        q = qkv[b * nq:(b + 1) * nq]
+        s = np.zeros(U * H * U, np.float32)
+        K.launch("MHAttentionScore", (U, H), None, [q, s, D, 0])
+        o = np.zeros(U * H * D, np.float32)
+        K.launch("MHAttentionOut", (U, H), None, [s, q, o, D])
+        qg = np.zeros(nq, np.float32)
+        K.launch("MHAttentionInsideGradients", (U, H, D), None, [q, qg, s, gout[b * U * H * D:(b + 1) * U * H * D]])
+        c = np.zeros(U * 3 * H * D, np.float32)
+        K.launch("FeedForwardConv", (U, 3 * H * D, 1), None, [wc, x[b * U * W:(b + 1) * U * W], c, U * W, W, W,
+                                                              3 * H * D, K.NONE])
+        n = U * H * U
+        check_close(f"smoke scores {b}", got["s"][b * n:(b + 1) * n], s)
+        n = U * H * D
+        check_close(f"smoke attention out {b}", got["o"][b * n:(b + 1) * n], o)
+        check_close(f"smoke attention gradients {b}", got["qg"][b * nq:(b + 1) * nq], qg)
+        n = U * 3 * H * D
+        check_close(f"smoke 1x1 convolution {b}", got["c"][b * n:(b + 1) * n], c)
