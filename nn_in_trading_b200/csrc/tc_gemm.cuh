@@ -263,7 +263,9 @@ struct Cfg {
   static constexpr uint32_t STAGE_BYTES = 2 * (A_BYTES + B_BYTES);
   static constexpr uint32_t EPI_OFF = STAGES * STAGE_BYTES;
   static constexpr uint32_t EPI_BYTES = 4 * 32 * 36 * 4;  // one 32 x 36 transpose buffer per epilogue warp
-  static constexpr uint32_t SMEM = EPI_OFF + EPI_BYTES + 1024;  // + alignment slack
+  static constexpr uint32_t COL_OFF = EPI_OFF + EPI_BYTES;  // column constants of the whole product
+  static constexpr int COL_FLOATS = 2048;
+  static constexpr uint32_t SMEM = COL_OFF + COL_FLOATS * 4 + 1024;  // + alignment slack
   static constexpr int A_CHUNKS = BM * BK / 4 / 128;            // float4 chunks per producer thread per stage
   static constexpr int B_CHUNKS = BN * BK / 4 / 128;
   static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulators: epilogue of one tile || MMAs of the next
@@ -607,6 +609,14 @@ __global__ void __launch_bounds__(320, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     float *buf = reinterpret_cast<float *>(smem + C::EPI_OFF) + warp * 32 * 36;
+    // column constants (e.g. the bias of every output) once per CTA into shared memory, so the
+    // stores never wait on a global gather; every epilogue thread reaches this barrier exactly
+    // once, before any bounded wait
+    float *coltab = reinterpret_cast<float *>(smem + C::COL_OFF);
+    const bool use_tab = (long long)s.N * s.nz <= C::COL_FLOATS;
+    if (use_tab)
+      for (int i = tid; i < s.N * s.nz; i += 128) coltab[i] = ep.col(i % s.N, i / s.N);
+    asm volatile("bar.sync 2, 128;" ::: "memory");
     int tl = 0;
     for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x, ++tl) {
       int m0, n0, z, split, kbeg, kend, nk;
@@ -638,7 +648,8 @@ __global__ void __launch_bounds__(320, 1)
         if (vec_out && n0 + c + 32 <= s.N) {
           const int cq = lane & 7, rs = lane >> 3;
           const int n = n0 + c + 4 * cq;
-          const float4 cv = ep.col4(n, z);
+          const float *ct = coltab + (size_t)z * s.N + n;
+          const float4 cv = use_tab ? make_float4(ct[0], ct[1], ct[2], ct[3]) : ep.col4(n, z);
           long long rb[8];
           float4 vv[8];
           unsigned mask = 0;
@@ -653,7 +664,7 @@ __global__ void __launch_bounds__(320, 1)
         } else {
           const int n = n0 + c + lane;
           const bool col_ok = n < s.N;
-          const float cv = col_ok ? ep.col(n, z) : 0.f;
+          const float cv = !col_ok ? 0.f : use_tab ? coltab[(size_t)z * s.N + n] : ep.col(n, z);
 #pragma unroll 1
           for (int r0 = 0; r0 < 32; r0 += 8) {
             long long rb[8];
