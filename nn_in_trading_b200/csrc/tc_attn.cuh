@@ -5,10 +5,10 @@
 //   score:  S[q][k] = softmax_k(Q[q] . K[k] / koef)   M = q (128), N = k (128), K = d (32), 1 stage
 //   out:    O[q][d] = sum_k S[q][k] V[k][d]            M = q (128), N = d (32),  K = k (128), 4 stages
 //
-// Persistent CTAs walk the B*H work items; per CTA 320 threads in the roles of tc_gemm.cuh:
-// warps 0-3 epilogue (one output row per thread), warps 4-7 split the TMA-loaded raw tiles into
-// hi / lo in place, warp 8 issues the MMAs into one of two tensor-memory accumulators, warp 9
-// issues the TMA loads.  Rows and keys past `units` are loaded (they belong to the next sequence,
+// Persistent CTAs walk the B*H work items; per CTA 448 threads in the roles of tc_gemm.cuh:
+// warps 0-7 epilogue (one output row per thread; two warps per tensor-memory lane quarter, one
+// per half of the columns), warps 8-11 split the TMA-loaded raw tiles into hi / lo in place, warp
+// 12 issues the MMAs into one of two tensor-memory accumulators, warp 13 issues the TMA loads.  Rows and keys past `units` are loaded (they belong to the next sequence,
 // or are zero-filled past the end of the tensor) and computed, but never stored: the score
 // epilogue excludes keys >= units from the normalisation, and the out product reads scores whose
 // columns >= units are zero-filled by TMA (the score tensor's inner extent is `units`).
@@ -29,9 +29,9 @@ struct AttnCfg {
   static constexpr uint32_t A_BYTES = BM * BK * 4, B_BYTES = BN * BK * 4;
   static constexpr uint32_t STAGE_BYTES = 2 * (A_BYTES + B_BYTES);
   static constexpr uint32_t EPI_OFF = STAGES * STAGE_BYTES;
-  // score: each epilogue warp keeps its 32 rows x 128 keys of exponentials (row stride 129 floats)
-  // plus one scale per row; out: a 32 x 33 transpose buffer per warp
-  static constexpr uint32_t EPI_BYTES = MODE == kAttnScore ? 4 * 32 * 129 * 4 + 128 * 4 : 4 * 32 * 33 * 4;
+  // score: each lane quarter keeps its 32 rows x 128 keys of exponentials (row stride 129 floats)
+  // plus two partial sums per row; out: a 32 x 33 transpose buffer per lane quarter
+  static constexpr uint32_t EPI_BYTES = MODE == kAttnScore ? 4 * 32 * 129 * 4 + 256 * 4 : 4 * 32 * 33 * 4;
   static constexpr uint32_t SMEM = EPI_OFF + EPI_BYTES + 1024;
   static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
   static_assert(SMEM <= 232448, "shared memory per CTA");
@@ -42,7 +42,7 @@ struct AttnCfg {
 // tmS:  scores as [B*U][H][U],    box 32 x 1 x 128, 128-byte swizzle (K-major score tiles)
 // tmV:  qkv as [B*U rows][3*H*D], box 32 x 32, 128-byte swizzle / 32-byte granules (MN-major V)
 template <int MODE>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(448, 1)
     attn_tc_kernel(float *__restrict__ out, int *err, int U, int H, int items, int mask, float koef,
                    const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmS,
                    const __grid_constant__ CUtensorMap tmV) {
@@ -62,6 +62,9 @@ __global__ void __launch_bounds__(320, 1)
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
 
+  // roles: warps 0-7 epilogue (lane quarter w % 4, column half w / 4), 8-11 split, 12 MMA, 13 TMA
+  constexpr int kMmaWarp = 12, kLoadWarp = 13;
+  __shared__ __align__(8) uint64_t esync;
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
   auto fail = [&](int code) {
     abort_flag = 1;
@@ -75,13 +78,14 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&accf[i], 1);
-      mbar_init(&acce[i], 128);
+      mbar_init(&acce[i], 256);
     }
+    mbar_init(&esync, 256);
     mbar_init(&drain, 1);
     abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 8) {
+  if (warp == kMmaWarp) {
     tmem_alloc(&tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
   }
@@ -90,7 +94,7 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
 
-  if (warp == 9) {
+  if (warp == kLoadWarp) {
     // ------------------------------------------------------------ loader
     if (lane == 0) {
       int it = 0;
@@ -121,9 +125,9 @@ __global__ void __launch_bounds__(320, 1)
         if (!mbar_wait_drain(&tmaf[st], (issued - 1) & 1) && !abort_flag) fail(kErrFullWait);
       }
     }
-  } else if (warp >= 4 && warp < 8) {
+  } else if (warp >= 8 && warp < 12) {
     // ------------------------------------------------------------ split raw tiles into hi / lo
-    const int ptid = tid - 128;
+    const int ptid = tid - 256;
     int it = 0;
     for (int t = blockIdx.x; t < items && !abort_flag; t += gridDim.x) {
       bool ok = true;
@@ -150,7 +154,7 @@ __global__ void __launch_bounds__(320, 1)
       }
       if (!ok) break;
     }
-  } else if (warp == 8) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issue
     int it = 0, tl = 0;
     for (int t = blockIdx.x; t < items && !abort_flag; t += gridDim.x, ++tl) {
@@ -194,8 +198,10 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue (thread = row q)
-    float *buf = reinterpret_cast<float *>(smem + C::EPI_OFF) + warp * 32 * 33;  // out mode
+    const int quarter = warp & 3, half = warp >> 2;
+    float *buf = reinterpret_cast<float *>(smem + C::EPI_OFF) + quarter * 32 * 33;  // out mode
     int tl = 0;
+    uint32_t nsync = 0;
     const float inv_koef = 1.f / koef;
     for (int t = blockIdx.x; t < items && !abort_flag; t += gridDim.x, ++tl) {
       const int bb = t / H, h = t % H;
@@ -205,47 +211,66 @@ __global__ void __launch_bounds__(320, 1)
         break;
       }
       tc_fence_after();
-      const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(b * BN);
-      const int q = warp * 32 + lane;  // this thread's row
+      const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * BN);
+      const int q = quarter * 32 + lane;  // this thread's row
       if (MODE == kAttnScore) {
         // MHAttentionScore (NeuroNet.cl:1662-1719): e = exp(clamp(s / koef, -100, 100)) over the
-        // unmasked keys, divided by their sum when the sum exceeds 1.  Each exponential is computed
-        // once into the warp's row buffer; the stores then go out along the keys (coalesced).
-        float *rows = reinterpret_cast<float *>(smem + C::EPI_OFF) + warp * 32 * 129;
-        float *scale = reinterpret_cast<float *>(smem + C::EPI_OFF) + 4 * 32 * 129 + warp * 32;
+        // unmasked keys, divided by their sum when the sum exceeds 1.  The two warps of a lane
+        // quarter each exponentiate one half of the keys into the quarter's row buffer and publish
+        // a partial sum; after a bounded barrier each stores its half of the rows along the keys.
+        float *rows = reinterpret_cast<float *>(smem + C::EPI_OFF) + quarter * 32 * 129;
+        float *psum = reinterpret_cast<float *>(smem + C::EPI_OFF) + 4 * 32 * 129;  // [2][128]
+        const int kmax = mask > 0 ? min(U, q + 1) : U;  // keys that take part in row q
         float sum = 0.f;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
           float v[32];
           tmem_ld32(trow + (uint32_t)c, v);
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            const int k = c + j;
+            const int kk = c + j;
             float e = 0.f;
-            if (k < U && !(mask > 0 && k > q)) {
+            if (kk < kmax) {
               e = exp2f(clampf(v[j] * inv_koef, -100.f, 100.f) * 1.4426950408889634f);
               if (isnan(e)) e = 0.f;
               sum += e;
             }
-            rows[lane * 129 + k] = e;
+            rows[lane * 129 + kk] = e;
           }
         }
-        scale[lane] = sum > 1.f ? 1.f / sum : 1.f;
-        __syncwarp();
+        psum[half * 128 + q] = sum;
+        mbar_arrive(&esync);
+        const bool ok = mbar_wait(&esync, nsync & 1, &abort_flag);
+        ++nsync;
+        if (!ok) {
+          fail(kErrDoneWait);
+          break;
+        }
         float *srow0 = out + (size_t)bb * U * H * U + (size_t)h * U;  // row q at srow0 + q*H*U
-        const int nrows = min(32, U - warp * 32);
+        const int r0 = quarter * 32 + half * 16;
+        const int r1 = min(r0 + 16, U);
 #pragma unroll 1
-        for (int r = 0; r < nrows; ++r) {
-          float *dst = srow0 + (size_t)(warp * 32 + r) * H * U;
-          const float sc = scale[r];
+        for (int r = r0; r < r1; ++r) {
+          const float tot = psum[r] + psum[128 + r];
+          const float sc = tot > 1.f ? 1.f / tot : 1.f;
+          float *dst = srow0 + (size_t)r * H * U;
+          const float *src = rows + (r - quarter * 32) * 129;
 #pragma unroll
           for (int c = 0; c < BN; c += 32) {
-            const int k = c + lane;
-            if (k < U) dst[k] = rows[r * 129 + k] * sc;
+            const int kk = c + lane;
+            if (kk < U) dst[kk] = src[kk] * sc;
           }
         }
-        __syncwarp();
-      } else {
+        // the next item rewrites the row buffer and the partial sums: every warp finishes reading
+        // first (the next accumulator can be ready while a slower warp is still storing this one)
+        mbar_arrive(&esync);
+        const bool ok2 = mbar_wait(&esync, nsync & 1, &abort_flag);
+        ++nsync;
+        if (!ok2) {
+          fail(kErrDoneWait);
+          break;
+        }
+      } else if (half == 0) {
         // MHAttentionOut (NeuroNet.cl:1730-1759): O[q][h][d]
         float v[32];
         tmem_ld32(trow, v);
@@ -255,7 +280,7 @@ __global__ void __launch_bounds__(320, 1)
         float *obase = out + ((size_t)bb * U * H + h) * D;  // row q at obase + q*H*D
 #pragma unroll 4
         for (int r = 0; r < 32; ++r) {
-          const int qr = warp * 32 + r;
+          const int qr = quarter * 32 + r;
           if (qr < U) obase[(size_t)qr * H * D + lane] = buf[r * 33 + lane];
         }
         __syncwarp();
@@ -266,14 +291,14 @@ __global__ void __launch_bounds__(320, 1)
   }
 
   // ------------------------------------------------------------ teardown
-  if (warp == 8) {
+  if (warp == kMmaWarp) {
     if (lane == 0) mma_commit(&drain);
     __syncwarp();
     if (!mbar_wait_drain(&drain, 0) && lane == 0) atomicExch(err, kErrDoneWait);
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
@@ -699,7 +724,7 @@ inline cudaError_t attn_tc(const float *qkv, const float *scores, float *out, in
   const int items = B * H;
   if (items <= 0) return cudaSuccess;
   const int grid = items < sm_count() ? items : sm_count();
-  fn<<<grid, 320, C::SMEM, st>>>(out, device_status(), U, H, items, mask, koef, tmQ, tmS, tmV);
+  fn<<<grid, 448, C::SMEM, st>>>(out, device_status(), U, H, items, mask, koef, tmQ, tmS, tmV);
   return cudaGetLastError();
 }
 
