@@ -255,14 +255,19 @@ __device__ __forceinline__ void store_split(uint8_t *hi, uint8_t *lo, uint32_t o
   *reinterpret_cast<float4 *>(lo + off) = l;
 }
 
-template <int BN, int BK, int STAGES>
+// Epilogue warps of a tcgemm_kernel variant: 8 (two per tensor-memory lane quarter, one per half of
+// the tile's columns) when TMA or bulk copies feed the stages; 4 when producer warps load operands
+// through registers (their double-buffered loads need the register budget of a 320-thread CTA).
+__host__ __device__ constexpr int epi_warps(int a_mode, int b_mode) { return (a_mode == 0 || b_mode == 0) ? 4 : 8; }
+
+template <int BN, int BK, int STAGES, int EPIW = 4>
 struct Cfg {
   static constexpr int BM = 128;
   static constexpr uint32_t A_BYTES = BM * BK * 4;  // one of hi / lo
   static constexpr uint32_t B_BYTES = BN * BK * 4;
   static constexpr uint32_t STAGE_BYTES = 2 * (A_BYTES + B_BYTES);
   static constexpr uint32_t EPI_OFF = STAGES * STAGE_BYTES;
-  static constexpr uint32_t EPI_BYTES = 4 * 32 * 36 * 4;  // one 32 x 36 transpose buffer per epilogue warp
+  static constexpr uint32_t EPI_BYTES = EPIW * 32 * 36 * 4;  // one 32 x 36 transpose buffer per epilogue warp
   static constexpr uint32_t COL_OFF = EPI_OFF + EPI_BYTES;  // column constants of the whole product
   static constexpr int COL_FLOATS = 2048;
   static constexpr uint32_t SMEM = COL_OFF + COL_FLOATS * 4 + 1024;  // + alignment slack
@@ -324,11 +329,14 @@ __device__ __forceinline__ void split_in_place(uint8_t *hi, uint8_t *lo, uint32_
 // chunks go out as float4s instead (`col4` / `put_rows4`: a lane stores 4 columns of 8 rows, a warp
 // instruction 4 rows x 128 bytes).
 template <int BN, int BK, int STAGES, bool A_MCONTIG, bool B_NCONTIG, int A_MODE, int B_MODE, class EP>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + 6), 1)
     tcgemm_kernel(FastShape s, EP ep, int *err, int vec_a, int vec_b, int vec_out, int tiles_n, int tiles_m,
                   int total, const uint8_t *bimg, int kstages, const __grid_constant__ CUtensorMap tmA,
                   const __grid_constant__ CUtensorMap tmB) {
-  using C = Cfg<BN, BK, STAGES>;
+  constexpr int EPIW = epi_warps(A_MODE, B_MODE);
+  // roles: warps [0, EPIW) epilogue, then 4 producer warps, the MMA warp and the loader warp
+  constexpr int kProd0 = EPIW, kMma = EPIW + 4, kLoad = EPIW + 5;
+  using C = Cfg<BN, BK, STAGES, EPIW>;
   constexpr int BM = C::BM;
   constexpr bool A_K = !A_MCONTIG, B_K = !B_NCONTIG;
   static_assert(A_MODE != OP_PACKED, "only the B operand is packed");
@@ -377,13 +385,13 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&accf[i], 1);
-      mbar_init(&acce[i], 128);
+      mbar_init(&acce[i], 32 * EPIW);
     }
     mbar_init(&drain, 1);
     abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 8) {
+  if (warp == kMma) {
     tmem_alloc(&tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
   }
@@ -393,11 +401,11 @@ __global__ void __launch_bounds__(320, 1)
   const uint32_t tmem = tmem_slot;
   const int n_real = s.ones_col >= 0 ? s.ones_col : s.N;
 
-  if (warp >= 4 && warp < 8) {
+  if (warp >= kProd0 && warp < kProd0 + 4) {
     // ------------------------------------------------------------ producers
     // OP_REGS operands are loaded one stage ahead: the global loads of the next stage are in
     // flight while the current one is split and stored (two register sets, used alternately).
-    const int ptid = tid - 128;
+    const int ptid = tid - 32 * kProd0;
     struct PState {
       int t, kk, nk, kbeg, kend, Ma, Nb, ones;
       const float *Ab, *Bb;
@@ -502,7 +510,7 @@ __global__ void __launch_bounds__(320, 1)
       if (have) load(p, va0, vb0);
       if (!put(cur, va1, vb1)) break;
     }
-  } else if (warp == 9) {
+  } else if (warp == kLoad) {
     // ------------------------------------------------------------ loader
     if (LOADER && lane == 0) {
       int it = 0;
@@ -556,7 +564,7 @@ __global__ void __launch_bounds__(320, 1)
         if (!mbar_wait_drain(&tmaf[st], (issued - 1) & 1) && !abort_flag) fail(kErrFullWait);
       }
     }
-  } else if (warp == 8) {
+  } else if (warp == kMma) {
     // ------------------------------------------------------------ MMA issue
     int it = 0, tl = 0;
     for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x, ++tl) {
@@ -615,8 +623,10 @@ __global__ void __launch_bounds__(320, 1)
     float *coltab = reinterpret_cast<float *>(smem + C::COL_OFF);
     const bool use_tab = (long long)s.N * s.nz <= C::COL_FLOATS;
     if (use_tab)
-      for (int i = tid; i < s.N * s.nz; i += 128) coltab[i] = ep.col(i % s.N, i / s.N);
-    asm volatile("bar.sync 2, 128;" ::: "memory");
+      for (int i = tid; i < s.N * s.nz; i += 32 * EPIW) coltab[i] = ep.col(i % s.N, i / s.N);
+    asm volatile("bar.sync 2, %0;" ::"r"(32 * EPIW) : "memory");
+    const int quarter = warp & 3;  // tensor-memory lane quarter = rows 32*quarter .. +31 of the tile
+    const int c_begin = EPIW == 8 ? (warp >> 2) * (BN / 2) : 0, c_end = EPIW == 8 ? c_begin + BN / 2 : BN;
     int tl = 0;
     for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x, ++tl) {
       int m0, n0, z, split, kbeg, kend, nk;
@@ -627,13 +637,13 @@ __global__ void __launch_bounds__(320, 1)
         break;
       }
       tc_fence_after();
-      const int mw = m0 + warp * 32;
+      const int mw = m0 + quarter * 32;
       const long long my_row = (mw + lane < s.M) ? ep.row(mw + lane, z, split) : 0;
 #pragma unroll 1
-      for (int c = 0; c < BN && n0 + c < s.N; c += 32) {
+      for (int c = c_begin; c < c_end && n0 + c < s.N; c += 32) {
         float v[32];
         if (nk > 0) {
-          tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(b * BN + c), v);
+          tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * BN + c), v);
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = 0.f;
@@ -687,7 +697,7 @@ __global__ void __launch_bounds__(320, 1)
   }
 
   // ------------------------------------------------------------ teardown
-  if (warp == 8) {
+  if (warp == kMma) {
     // every MMA this thread issued must be complete before its columns are freed
     if (lane == 0) mma_commit(&drain);
     __syncwarp();
@@ -695,7 +705,7 @@ __global__ void __launch_bounds__(320, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == kMma) {
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
@@ -785,11 +795,14 @@ inline bool make_tmap(CUtensorMap *tm, const float *p, long long ld, long long s
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int STAGES, bool A_MCONTIG, bool B_NCONTIG, int A_MODE, int B_MODE, class EP>
+template <int BN, bool A_MCONTIG, bool B_NCONTIG, int A_MODE, int B_MODE, class EP>
 inline cudaError_t tcgemm_launch(const FastShape &s, EP ep, cudaStream_t st, int *err, int va, int vb,
                                  uint8_t *img) {
   constexpr int BK = 32;
-  using C = tc::Cfg<BN, BK, STAGES>;
+  constexpr int EPIW = tc::epi_warps(A_MODE, B_MODE);
+  // stages fill what the epilogue buffers leave of the 227 KB
+  constexpr int STAGES = BN == 128 ? (EPIW == 8 ? 2 : 3) : (EPIW == 8 ? 3 : 4);
+  using C = tc::Cfg<BN, BK, STAGES, EPIW>;
   auto fn = tc::tcgemm_kernel<BN, BK, STAGES, A_MCONTIG, B_NCONTIG, A_MODE, B_MODE, EP>;
   static bool attr = false;  // per instantiation; setting it twice is harmless
   if (!attr) {
@@ -822,22 +835,22 @@ inline cudaError_t tcgemm_launch(const FastShape &s, EP ep, cudaStream_t st, int
     tc::pack_b_kernel<BN, BK, !B_NCONTIG><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(s.B, s.ldb, s.N, s.K, img,
                                                                                        tiles_n, kstages);
   }
-  fn<<<grid, 320, C::SMEM, st>>>(s, ep, err, va, vb, ep.aligned4() ? 1 : 0, tiles_n, tiles_m, (int)total, img,
+  fn<<<grid, 32 * (EPIW + 6), C::SMEM, st>>>(s, ep, err, va, vb, ep.aligned4() ? 1 : 0, tiles_n, tiles_m, (int)total, img,
                                   kstages, tmA, tmB);
   return cudaGetLastError();
 }
 
-template <int BN, int STAGES, bool A_MCONTIG, bool B_NCONTIG, class EP>
+template <int BN, bool A_MCONTIG, bool B_NCONTIG, class EP>
 inline cudaError_t tcgemm_modes(const FastShape &s, EP ep, cudaStream_t st, int *err, int va, int vb, uint8_t *img,
                                 bool a_tma, bool b_tma) {
   using namespace tc;
   if (img) {
-    if (a_tma) return tcgemm_launch<BN, STAGES, A_MCONTIG, B_NCONTIG, OP_TMA, OP_PACKED>(s, ep, st, err, va, vb, img);
-    return tcgemm_launch<BN, STAGES, A_MCONTIG, B_NCONTIG, OP_REGS, OP_PACKED>(s, ep, st, err, va, vb, img);
+    if (a_tma) return tcgemm_launch<BN, A_MCONTIG, B_NCONTIG, OP_TMA, OP_PACKED>(s, ep, st, err, va, vb, img);
+    return tcgemm_launch<BN, A_MCONTIG, B_NCONTIG, OP_REGS, OP_PACKED>(s, ep, st, err, va, vb, img);
   }
   if (a_tma && b_tma)
-    return tcgemm_launch<BN, STAGES, A_MCONTIG, B_NCONTIG, OP_TMA, OP_TMA>(s, ep, st, err, va, vb, nullptr);
-  return tcgemm_launch<BN, STAGES, A_MCONTIG, B_NCONTIG, OP_REGS, OP_REGS>(s, ep, st, err, va, vb, nullptr);
+    return tcgemm_launch<BN, A_MCONTIG, B_NCONTIG, OP_TMA, OP_TMA>(s, ep, st, err, va, vb, nullptr);
+  return tcgemm_launch<BN, A_MCONTIG, B_NCONTIG, OP_REGS, OP_REGS>(s, ep, st, err, va, vb, nullptr);
 }
 
 // Tile width by N (64 when that wastes less), split-K as given in `s`.  With `img` (at least
@@ -857,8 +870,8 @@ inline cudaError_t tcgemm(FastShape s, EP ep, cudaStream_t st, int *err, uint8_t
   const bool packed = img != nullptr && tcgemm_pack_bytes(s) > 0 && ((uintptr_t)img & 15) == 0;
   const bool a_tma = tma_ok(s.A, s.lda, s.strideA, s.nz, s);
   const bool b_tma = !packed && tma_ok(s.B, s.ldb, s.strideB, s.nz, s);
-  if (narrow) return tcgemm_modes<64, 4, A_MCONTIG, B_NCONTIG>(s, ep, st, err, va, vb, packed ? img : nullptr, a_tma, b_tma);
-  return tcgemm_modes<128, 3, A_MCONTIG, B_NCONTIG>(s, ep, st, err, va, vb, packed ? img : nullptr, a_tma, b_tma);
+  if (narrow) return tcgemm_modes<64, A_MCONTIG, B_NCONTIG>(s, ep, st, err, va, vb, packed ? img : nullptr, a_tma, b_tma);
+  return tcgemm_modes<128, A_MCONTIG, B_NCONTIG>(s, ep, st, err, va, vb, packed ? img : nullptr, a_tma, b_tma);
 }
 
 // Whether a call site's FP32 GEMM runs on the tensor cores: unless the context was created with
