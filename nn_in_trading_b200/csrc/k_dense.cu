@@ -30,6 +30,24 @@ __global__ void colsum_partial_kernel(float *p, const float *g, int M, int rows,
   p[((size_t)blockIdx.y * M + m) * ldp + col] = s;
 }
 
+__global__ void colsum_rows_kernel(float *p, const float *g, int M, int rows, long long ld, int kchunk, int ldp,
+                                   int col) {
+  __shared__ float red[8][33];
+  const int m = blockIdx.x * 32 + threadIdx.x;
+  const int r0 = blockIdx.y * kchunk, r1 = min(rows, r0 + kchunk);
+  float s = 0.f;
+  if (m < M)
+    for (int r = r0 + (int)threadIdx.y; r < r1; r += 8) s += nan0(g[(size_t)r * ld + m]);
+  red[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y == 0 && m < M) {
+    float t = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) t += red[j][threadIdx.x];
+    p[((size_t)blockIdx.y * M + m) * ldp + col] = t;
+  }
+}
+
 // ------------------------------------------------------------ FeedForward
 // NeuroNet.cl:430-512.  y[b,o] = act(sum_k nan0(nan0(x[b,k]) w[o,k]) + nan0(w[o,in]))
 // Small batches: one warp per output row, lanes striding the row (coalesced).

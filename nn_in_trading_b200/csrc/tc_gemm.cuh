@@ -48,6 +48,7 @@
 
 #include <cstdint>
 #include <cstring>
+#include <type_traits>
 
 #include "gemm_fast.cuh"
 #include "nn_device.cuh"
@@ -254,6 +255,12 @@ __device__ __forceinline__ void store_split(uint8_t *hi, uint8_t *lo, uint32_t o
   *reinterpret_cast<float4 *>(hi + off) = h;
   *reinterpret_cast<float4 *>(lo + off) = l;
 }
+
+// Epilogue functors that store column by column straight from the accumulator rows (no transpose).
+template <class T, class = void>
+struct ep_col_major : std::false_type {};
+template <class T>
+struct ep_col_major<T, std::void_t<decltype(T::kColMajor)>> : std::integral_constant<bool, T::kColMajor> {};
 
 // Epilogue warps of a tcgemm_kernel variant: 8 (two per tensor-memory lane quarter, one per half of
 // the tile's columns) when TMA or bulk copies feed the stages; 4 when producer warps load operands
@@ -647,6 +654,15 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + 6), 1)
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = 0.f;
+        }
+        if constexpr (ep_col_major<EP>::value) {
+          // column j of the chunk: the 32 lanes (rows) write consecutive addresses
+          if (mw + lane < s.M) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n0 + c + j < s.N) ep.put_col(my_row, n0 + c + j, v[j]);
+          }
+          continue;
         }
         // row `lane` of the chunk -> shared row `lane` (36-float stride: conflict-free float4 traffic)
 #pragma unroll

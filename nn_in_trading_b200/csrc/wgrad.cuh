@@ -67,10 +67,42 @@ struct PartialStoreLd {
   }
 };
 
+// Partial store of a transposed product: the GEMM computed C^T (its rows are the gradient's columns
+// n, its columns the gradient's rows m); element (n, m) of split s goes to p[(s*M + m)*ldp + n].
+// The tensor-core epilogue stores it column by column from the accumulator rows (kColMajor), so
+// the lanes (consecutive n) write consecutive addresses.
+struct PartialStoreT {
+  static constexpr bool kColMajor = true;
+  float *p;
+  int M, ldp;
+  __device__ void operator()(int n, int m, int, int split, float acc) const {
+    p[((size_t)split * M + m) * ldp + n] = acc;
+  }
+  __device__ __forceinline__ long long row(int n, int, int split) const { return (long long)split * M * ldp + n; }
+  __device__ __forceinline__ void put_col(long long rowoff, int m, float v) const { p[rowoff + (long long)m * ldp] = v; }
+  // (the row-major protocol, unused when kColMajor)
+  __host__ __device__ bool aligned4() const { return false; }
+  __device__ __forceinline__ float col(int, int) const { return 0.f; }
+  __device__ __forceinline__ float4 col4(int, int) const { return make_float4(0.f, 0.f, 0.f, 0.f); }
+  template <int R>
+  __device__ __forceinline__ void put_rows(const long long (&rb)[R], int m, const float (&v)[R], float,
+                                           unsigned mask) const {
+#pragma unroll
+    for (int j = 0; j < R; ++j)
+      if (mask >> j & 1u) put_col(rb[j], m, v[j]);
+  }
+  template <int R>
+  __device__ __forceinline__ void put_rows4(const long long (&rb)[R], int m, const float4 (&v)[R], float4,
+                                            unsigned mask) const {}
+};
+
 // Bias column of a weight gradient: per split, sum over the split's reduction
 // rows r of nan0(g[r*ld + m]) into p[(split*M + m)*ldp + col].
 __global__ void colsum_partial_kernel(float *p, const float *g, int M, int rows, long long ld, int kchunk, int ldp,
                                       int col);
+// Same, 32 columns x 8 row lanes per block (block 32 x 8, grid (ceil(M/32), splits)).
+__global__ void colsum_rows_kernel(float *p, const float *g, int M, int rows, long long ld, int kchunk, int ldp,
+                                   int col);
 
 // Weight gradient of a plain GEMM: G[m][n] = sum_r A[r*lda + m] * X[r*ldx + n] for n < N, and
 // G[m][N] = sum_r A[r*lda + m] (the bias column, input 1).  Partials per split into scratch 0.
@@ -87,7 +119,17 @@ inline int wgrad_fast(Launch &L, const float *A, long long lda, const float *X, 
   float *part = L.scratch(0, per * splits);
   if (!part) return NN_ERR_CUDA;
   FastShape fs{M, N, rows, 1, splits, kchunk, A, lda, 0, X, ldx, 0};
-  if (tc_path(fs)) {
+  if (tc_path(fs) && M < 128 && N >= 128) {
+    // few outputs, many inputs: the transposed product X^T A^T fills the 128-row tiles with the
+    // inputs instead of padding the outputs; the bias column is a separate column sum of A
+    FastShape ft{N, M, rows, 1, splits, kchunk, X, ldx, 0, A, lda, 0};
+    cudaError_t e = tcgemm<true, true>(ft, PartialStoreT{part, M, ldp}, L.stream, device_status());
+    if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
+    L.counted();
+    colsum_rows_kernel<<<dim3((M + 31) / 32, splits), dim3(32, 8), 0, L.stream>>>(part, A, M, rows, lda, kchunk, ldp,
+                                                                                 N);
+    NN_CHECK_LAUNCH(L);
+  } else if (tc_path(fs)) {
     // the bias input (1) is column N of X: one GEMM writes all N + 1 gradient columns
     fs.N = N + 1;
     fs.ones_col = N;

@@ -2,8 +2,9 @@
 
 The shapes are large enough to take that path (at least 64 rows and M*N*K >= 2^20) and ragged in
 every GEMM dimension (partial 128-row tiles, partial 64/128-column tiles, k not a multiple of the
-32-wide stage or of the 8-wide MMA step, split-K); they cover the three operand layouts the call
-sites use (K-major x K-major, K-major x N-major, M-major x N-major).  Every result is compared with
+32-wide stage or of the 8-wide MMA step, split-K, weight gradients computed transposed); they cover
+the three operand layouts the call sites use (K-major x K-major, K-major x N-major, M-major x
+N-major).  Every result is compared with
 the numpy oracle at the 1e-4 parity bound.
 """
 import numpy as np
@@ -19,7 +20,9 @@ pytestmark = pytest.mark.gpu
 NONE, TANH, SIGMOID, LRELU = -1, 0, 1, 2
 
 # (units, window, window_out, batch, activation); step == window, one variable
-CONV_SHAPES = [(301, 37, 131, 3, TANH), (120, 64, 200, 5, NONE), (97, 65, 768, 2, LRELU), (2000, 16, 96, 4, NONE)]
+CONV_SHAPES = [(301, 37, 131, 3, TANH), (120, 64, 200, 5, NONE), (97, 65, 768, 2, LRELU), (2000, 16, 96, 4, NONE),
+               # fewer than 128 outputs, at least 128 inputs: the weight gradient runs transposed
+               (240, 256, 64, 2, NONE), (150, 130, 100, 3, TANH)]
 
 
 def conv_cases(units, win, wout, act):
