@@ -231,15 +231,24 @@ def run_ours(args, rank, world, local_rank):
         net.step()
         lib.nn_buffer_read(out_h, hy.data_ptr(), 0, B * n_in)
     barrier()
+    # Every step: H2D of its inputs and targets, the step, a blocking D2H of its output and the host
+    # MSE of that output (CNet::backPropOCL reads the output back).  The host work of step i runs
+    # while the device already executes step i+1 (enqueued right after step i's read returns).
     t0 = time.perf_counter()
     losses = []
-    for i in range(e2e_steps):
+
+    def enqueue(i):
         ctx._check(lib.nn_buffer_write(inp, hx[i % pool].data_ptr(), 0, B * n_in))
         ctx._check(lib.nn_buffer_write(net.target, ht[i % pool].data_ptr(), 0, B * n_in))
         net.step()
+
+    enqueue(0)
+    for i in range(e2e_steps):
         ctx._check(lib.nn_buffer_read(out_h, hy.data_ptr(), 0, B * n_in))
+        if i + 1 < e2e_steps:
+            enqueue(i + 1)  # hy is written again only by the next iteration's read
         d = hy.numpy() - ts[i % pool].reshape(-1)
-        losses.append(float(np.dot(d, d)) / d.size)  # host MSE, as CNet::backPropOCL reads the output
+        losses.append(float(np.dot(d, d)) / d.size)  # host MSE of step i's output
     e2e_s = time.perf_counter() - t0
     if world > 1:
         t = torch.tensor([e2e_s], dtype=torch.float64)

@@ -310,15 +310,19 @@ __global__ void __launch_bounds__(448, 1)
 //   dV = S^T G,   C = S o (V0^T - A),   dK = C^T (G o Q) / koef,   dQ = G o (C K) / koef.
 // Shared memory (one item at a time, 210 KB):
 //   SH / SL  S, then C: hi / lo, [u-group (4)][q row (128)][32 u], 64 KB each
-//   GH / GL  G: hi / lo, [q row][32 d], 16 KB each
+//   GH / GL  G: hi / lo, [q row][32 d], 16 KB each; later K (dQ's B operand)
 //   QR       raw Q, later raw K, [row][32 d], 16 KB
-//   XH / XL  G o Q, later K: hi / lo, 16 KB each
+//   XH / XL  G o Q: hi / lo, 16 KB each
 //   V0, AV   128 floats each;  VR: V[u][0..3] per row (TMA), the source of V0
 // S, G, Q and K tiles use the 128-byte swizzle with 32-byte granules (MN-major operands of dV and
 // dK).  For dQ, C is the K-major operand: its rows are already where the K-major layout keeps
 // them, and only the 16-byte granules inside each 128-byte row are permuted (32-byte granules
 // XOR q%4  ->  16-byte granules XOR q%8).  Score rows q >= units (the next sequence) are zeroed,
 // so they contribute nothing to the sums over q.
+// Overlap: dV and dK reduce over q in 8-row steps, so the workers hand S over (and take C back)
+// in four 32-row chunks of q, each with its own barrier; G o Q and A are formed while dV runs,
+// K is split while dK runs, and the next item's tiles load while this item's results are stored
+// (dQ's factor G is read from global memory, so G's buffer is free once dQ's products finish).
 struct GradCfg {
   static constexpr uint32_t SH = 0, SL = 65536, GH = 131072, GL = 147456, QR = 163840, XH = 180224, XL = 196608;
   static constexpr uint32_t V0 = 212992, AV = V0 + 512, VR = AV + 512, END = VR + 2048;
@@ -332,9 +336,10 @@ __device__ __forceinline__ uint32_t sw32_off(int r, int c) {
 }
 
 __global__ void __launch_bounds__(320, 1)
-    attn_grad_tc_kernel(const float *__restrict__ qkv, float *__restrict__ qkv_g, int *err, int U, int H, int items,
-                        float koef, const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmQKV,
-                        const __grid_constant__ CUtensorMap tmG, const __grid_constant__ CUtensorMap tmV0) {
+    attn_grad_tc_kernel(const float *__restrict__ qkv, const float *__restrict__ grad, float *__restrict__ qkv_g,
+                        int *err, int U, int H, int items, float koef, const __grid_constant__ CUtensorMap tmS,
+                        const __grid_constant__ CUtensorMap tmQKV, const __grid_constant__ CUtensorMap tmG,
+                        const __grid_constant__ CUtensorMap tmV0) {
   using C = GradCfg;
   constexpr int D = 32;
   constexpr uint32_t IDESC_MN = instr_desc_tf32(128, 32, true, true);   // dV, dK
@@ -342,7 +347,8 @@ __global__ void __launch_bounds__(320, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   float *V0s = reinterpret_cast<float *>(sm + C::V0), *AVs = reinterpret_cast<float *>(sm + C::AV);
-  __shared__ __align__(8) uint64_t ld1, ld2, w1, w2, w3, m1, m2, accf, ifree, qfree, wsync, drain;
+  // w1[j]: S and G rows of q-chunk j split (dV may read them); mq[j]: dK has read C's q-chunk j
+  __shared__ __align__(8) uint64_t ld1, ld2, w1[4], w2, w3, m1, mq[4], accf, qfree, wsync, drain;
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
 
@@ -354,13 +360,14 @@ __global__ void __launch_bounds__(320, 1)
   if (tid == 0) {
     mbar_init(&ld1, 1);
     mbar_init(&ld2, 1);
-    mbar_init(&w1, 256);
+    for (int j = 0; j < 4; ++j) {
+      mbar_init(&w1[j], 256);
+      mbar_init(&mq[j], 1);
+    }
     mbar_init(&w2, 256);
     mbar_init(&w3, 256);
     mbar_init(&m1, 1);
-    mbar_init(&m2, 1);
     mbar_init(&accf, 1);
-    mbar_init(&ifree, 256);
     mbar_init(&qfree, 256);
     mbar_init(&wsync, 256);
     mbar_init(&drain, 1);
@@ -384,7 +391,9 @@ __global__ void __launch_bounds__(320, 1)
       int n = 0, issued1 = 0, issued2 = 0;
       for (int t = blockIdx.x; t < items && !abort_flag; t += gridDim.x, ++n) {
         const int b = t / H, h = t % H;
-        if (n > 0 && !mbar_wait(&ifree, (n - 1) & 1, &abort_flag)) {
+        // the previous item's products have read S, G/K and Q/K (its epilogue reads only tensor
+        // memory and global memory), so its tiles may be overwritten
+        if (n > 0 && !mbar_wait(&accf, (n - 1) & 1, &abort_flag)) {
           fail(kErrEmptyWait);
           break;
         }
@@ -415,47 +424,55 @@ __global__ void __launch_bounds__(320, 1)
   } else if (warp == 8) {
     // ------------------------------------------------------------ MMA issue
     int n = 0;
-    for (int t = blockIdx.x; t < items && !abort_flag; t += gridDim.x, ++n) {
+    bool ok = true;
+    for (int t = blockIdx.x; t < items && ok && !abort_flag; t += gridDim.x, ++n) {
       const uint32_t par = n & 1;
-      // dV = S^T G
-      if (!mbar_wait(&w1, par, &abort_flag)) {
-        if (lane == 0) fail(kErrFullWait);
-        break;
-      }
-      tc_fence_after();
-      if (lane == 0) {
-        for (int s = 0; s < 16; ++s) {
-          const uint64_t ah = smem_desc(smem_u32(sm + C::SH) + 1024u * s, 16384u, 512u, 1u);
-          const uint64_t al = smem_desc(smem_u32(sm + C::SL) + 1024u * s, 16384u, 512u, 1u);
-          const uint64_t bh = smem_desc(smem_u32(sm + C::GH) + 1024u * s, 4096u, 512u, 1u);
-          const uint64_t bl = smem_desc(smem_u32(sm + C::GL) + 1024u * s, 4096u, 512u, 1u);
-          mma_tf32(tmem, al, bh, IDESC_MN, s != 0 ? 1u : 0u);
-          mma_tf32(tmem, ah, bl, IDESC_MN, 1u);
-          mma_tf32(tmem, ah, bh, IDESC_MN, 1u);
+      // dV = S^T G, k-steps s (q rows 8s..8s+7) issued as the workers release each 32-row chunk
+      for (int j = 0; j < 4 && ok; ++j) {
+        if (!mbar_wait(&w1[j], par, &abort_flag)) {
+          if (lane == 0) fail(kErrFullWait);
+          ok = false;
+          break;
         }
-        mma_commit(&m1);
+        tc_fence_after();
+        if (lane == 0) {
+          for (int s = 4 * j; s < 4 * j + 4; ++s) {
+            const uint64_t ah = smem_desc(smem_u32(sm + C::SH) + 1024u * s, 16384u, 512u, 1u);
+            const uint64_t al = smem_desc(smem_u32(sm + C::SL) + 1024u * s, 16384u, 512u, 1u);
+            const uint64_t bh = smem_desc(smem_u32(sm + C::GH) + 1024u * s, 4096u, 512u, 1u);
+            const uint64_t bl = smem_desc(smem_u32(sm + C::GL) + 1024u * s, 4096u, 512u, 1u);
+            mma_tf32(tmem, al, bh, IDESC_MN, s != 0 ? 1u : 0u);
+            mma_tf32(tmem, ah, bl, IDESC_MN, 1u);
+            mma_tf32(tmem, ah, bh, IDESC_MN, 1u);
+          }
+          if (j == 3) mma_commit(&m1);
+        }
+        __syncwarp();
       }
-      __syncwarp();
-      // dK' = C^T (G o Q)
+      if (!ok) break;
+      // dK' = C^T (G o Q), with a commit after each 32-row chunk of q so that the workers can
+      // permute the rows it no longer reads
       if (!mbar_wait(&w2, par, &abort_flag)) {
         if (lane == 0) fail(kErrFullWait);
         break;
       }
       tc_fence_after();
       if (lane == 0) {
-        for (int s = 0; s < 16; ++s) {
-          const uint64_t ah = smem_desc(smem_u32(sm + C::SH) + 1024u * s, 16384u, 512u, 1u);
-          const uint64_t al = smem_desc(smem_u32(sm + C::SL) + 1024u * s, 16384u, 512u, 1u);
-          const uint64_t bh = smem_desc(smem_u32(sm + C::XH) + 1024u * s, 4096u, 512u, 1u);
-          const uint64_t bl = smem_desc(smem_u32(sm + C::XL) + 1024u * s, 4096u, 512u, 1u);
-          mma_tf32(tmem + 32, al, bh, IDESC_MN, s != 0 ? 1u : 0u);
-          mma_tf32(tmem + 32, ah, bl, IDESC_MN, 1u);
-          mma_tf32(tmem + 32, ah, bh, IDESC_MN, 1u);
+        for (int j = 0; j < 4; ++j) {
+          for (int s = 4 * j; s < 4 * j + 4; ++s) {
+            const uint64_t ah = smem_desc(smem_u32(sm + C::SH) + 1024u * s, 16384u, 512u, 1u);
+            const uint64_t al = smem_desc(smem_u32(sm + C::SL) + 1024u * s, 16384u, 512u, 1u);
+            const uint64_t bh = smem_desc(smem_u32(sm + C::XH) + 1024u * s, 4096u, 512u, 1u);
+            const uint64_t bl = smem_desc(smem_u32(sm + C::XL) + 1024u * s, 4096u, 512u, 1u);
+            mma_tf32(tmem + 32, al, bh, IDESC_MN, s != 0 ? 1u : 0u);
+            mma_tf32(tmem + 32, ah, bl, IDESC_MN, 1u);
+            mma_tf32(tmem + 32, ah, bh, IDESC_MN, 1u);
+          }
+          mma_commit(&mq[j]);
         }
-        mma_commit(&m2);
       }
       __syncwarp();
-      // dQ' = C K  (C as the K-major operand: u-group s/4, 32 bytes per 8-wide k step)
+      // dQ' = C K  (C as the K-major operand: u-group s/4, 32 bytes per 8-wide k step; K split in GH/GL)
       if (!mbar_wait(&w3, par, &abort_flag)) {
         if (lane == 0) fail(kErrFullWait);
         break;
@@ -466,8 +483,8 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t ao = 16384u * (s >> 2) + 32u * (s & 3);
           const uint64_t ah = smem_desc(smem_u32(sm + C::SH) + ao, 16u, 1024u, 2u);
           const uint64_t al = smem_desc(smem_u32(sm + C::SL) + ao, 16u, 1024u, 2u);
-          const uint64_t bh = smem_desc(smem_u32(sm + C::XH) + 1024u * s, 4096u, 512u, 1u);
-          const uint64_t bl = smem_desc(smem_u32(sm + C::XL) + 1024u * s, 4096u, 512u, 1u);
+          const uint64_t bh = smem_desc(smem_u32(sm + C::GH) + 1024u * s, 4096u, 512u, 1u);
+          const uint64_t bl = smem_desc(smem_u32(sm + C::GL) + 1024u * s, 4096u, 512u, 1u);
           mma_tf32(tmem + 64, al, bh, IDESC_KM, s != 0 ? 1u : 0u);
           mma_tf32(tmem + 64, ah, bl, IDESC_KM, 1u);
           mma_tf32(tmem + 64, ah, bh, IDESC_KM, 1u);
@@ -497,26 +514,35 @@ __global__ void __launch_bounds__(320, 1)
       }
       // V0 (feature 0 of V) for every unit of the tile; zero past `units`
       if (wt < 128) V0s[wt] = wt < U ? nan0(reinterpret_cast<const float *>(sm + C::VR)[4 * wt]) : 0.f;
-      // W1: split S (rows q >= units zeroed), split G, G o Q -> XH / XL
-      for (uint32_t f = wt; f < 4096; f += 256) {  // S: 64 KB = 4096 chunks
-        const uint32_t off = 16u * f;
-        const int q = (off & 16383u) >> 7;
-        if (q >= U) {
-          *reinterpret_cast<float4 *>(sm + C::SH + off) = make_float4(0.f, 0.f, 0.f, 0.f);
-          *reinterpret_cast<float4 *>(sm + C::SL + off) = make_float4(0.f, 0.f, 0.f, 0.f);
-        } else {
-          split_in_place(sm + C::SH, sm + C::SL, off);
+      // W1, per 32-row chunk j of q: split S (rows q >= units zeroed) and G, then release the chunk
+      // to dV.  Thread wt handles row 32j + wt/8 of each u-group, 16 bytes at a time.
+      for (int j = 0; j < 4; ++j) {
+        const int q = 32 * j + (wt >> 3);
+#pragma unroll
+        for (int ug = 0; ug < 4; ++ug) {
+          const uint32_t off = 16384u * ug + 4096u * j + 16u * wt;
+          if (q >= U) {
+            *reinterpret_cast<float4 *>(sm + C::SH + off) = make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4 *>(sm + C::SL + off) = make_float4(0.f, 0.f, 0.f, 0.f);
+          } else {
+            split_in_place(sm + C::SH, sm + C::SL, off);
+          }
         }
+        split_in_place(sm + C::GH, sm + C::GL, 4096u * j + 16u * wt);
+        fence_proxy_async_smem();
+        mbar_arrive(&w1[j]);
       }
-      for (uint32_t f = wt; f < 1024; f += 256) {  // G and G o Q: 16 KB = 1024 chunks
+      // G o Q -> XH / XL (dK's B operand) while dV runs
+      for (uint32_t f = wt; f < 1024; f += 256) {
         const uint32_t off = 16u * f;
-        split_in_place(sm + C::GH, sm + C::GL, off);
         const float4 g = *reinterpret_cast<const float4 *>(sm + C::GH + off);
         const float4 qv = *reinterpret_cast<const float4 *>(sm + C::QR + off);
         *reinterpret_cast<float4 *>(sm + C::XH + off) = make_float4(g.x * qv.x, g.y * qv.y, g.z * qv.z, g.w * qv.w);
         split_in_place(sm + C::XH, sm + C::XL, off);
       }
-      if (!worker_sync()) {
+      fence_proxy_async_smem();
+      mbar_arrive(&qfree);  // raw Q consumed: the loader brings raw K into QR
+      if (!worker_sync()) {  // V0 and the zeroed score rows complete before A reads them
         fail(kErrFullWait);
         break;
       }
@@ -542,9 +568,6 @@ __global__ void __launch_bounds__(320, 1)
           if (lane < 4) AVs[q0 + lane] = lane == 0 ? a[0] : lane == 1 ? a[1] : lane == 2 ? a[2] : a[3];
         }
       }
-      fence_proxy_async_smem();
-      mbar_arrive(&w1);
-      mbar_arrive(&qfree);
       if (!worker_sync()) {  // AVs complete before W2 reads it
         fail(kErrFullWait);
         break;
@@ -568,44 +591,51 @@ __global__ void __launch_bounds__(320, 1)
       }
       fence_proxy_async_smem();
       mbar_arrive(&w2);
-      // W3: once dK has read C and G o Q: permute C's rows to the K-major swizzle, split raw K
-      if (!mbar_wait(&m2, par, &abort_flag)) {
-        fail(kErrDoneWait);
-        break;
-      }
-      tc_fence_after();
-      for (int row = wt; row < 1024; row += 256) {  // 2 buffers x 4 u-groups x 128 rows
-        uint8_t *base = sm + ((row & 512) ? C::SL : C::SH) + ((row >> 7) & 3) * 16384 + (row & 127) * 128;
-        const int q = row & 127;
-        // g[j] = physical granule (j + q) % 8: the eight lanes of a shared-memory phase touch eight
-        // different 16-byte bank groups although their rows are 128 bytes apart
-        const int rot = q & 7;
-        float4 g[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) g[j] = *reinterpret_cast<const float4 *>(base + 16 * ((j + rot) & 7));
-        // register-only select of g[i] (a runtime index into g would go to local memory)
-        auto pick = [&](int i) -> float4 {
-          float4 v = g[0];
-#pragma unroll
-          for (int j = 1; j < 8; ++j) v = (i == j) ? g[j] : v;
-          return v;
-        };
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int p = (j + rot) & 7;                                 // destination: K-major granule p
-          const int l16 = (p ^ q) & 7;                                 // the logical granule stored there
-          const int from = 2 * (((l16 >> 1) ^ q) & 3) + (l16 & 1);    // its place in the MN-major row
-          *reinterpret_cast<float4 *>(base + 16 * p) = pick((from - rot) & 7);
-        }
-      }
+      // raw K -> GH / GL (dQ's B operand) while dK runs: dV has finished reading G
       if (!mbar_wait(&ld2, par, &abort_flag)) {
         fail(kErrFullWait);
         break;
       }
       for (uint32_t f = wt; f < 1024; f += 256) {
         const uint32_t off = 16u * f;
-        *reinterpret_cast<float4 *>(sm + C::XH + off) = *reinterpret_cast<const float4 *>(sm + C::QR + off);
-        split_in_place(sm + C::XH, sm + C::XL, off);
+        *reinterpret_cast<float4 *>(sm + C::GH + off) = *reinterpret_cast<const float4 *>(sm + C::QR + off);
+        split_in_place(sm + C::GH, sm + C::GL, off);
+      }
+      // W3, per 32-row chunk j of q once dK has read it: permute C's rows to the K-major swizzle.
+      // Thread wt: buffer wt/128 (hi, lo), u-group (wt/32)%4, row q = 32j + wt%32.
+      bool ok = true;
+      for (int j = 0; j < 4; ++j) {
+        if (!mbar_wait(&mq[j], par, &abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const int q = 32 * j + (wt & 31);
+        uint8_t *base = sm + ((wt & 128) ? C::SL : C::SH) + ((wt >> 5) & 3) * 16384 + q * 128;
+        // g[j] = physical granule (j + q) % 8: the eight lanes of a shared-memory phase touch eight
+        // different 16-byte bank groups although their rows are 128 bytes apart
+        const int rot = q & 7;
+        float4 g[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) g[i] = *reinterpret_cast<const float4 *>(base + 16 * ((i + rot) & 7));
+        // register-only select of g[i] (a runtime index into g would go to local memory)
+        auto pick = [&](int i) -> float4 {
+          float4 v = g[0];
+#pragma unroll
+          for (int k = 1; k < 8; ++k) v = (i == k) ? g[k] : v;
+          return v;
+        };
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int p = (i + rot) & 7;                                 // destination: K-major granule p
+          const int l16 = (p ^ q) & 7;                                 // the logical granule stored there
+          const int from = 2 * (((l16 >> 1) ^ q) & 3) + (l16 & 1);    // its place in the MN-major row
+          *reinterpret_cast<float4 *>(base + 16 * p) = pick((from - rot) & 7);
+        }
+      }
+      if (!ok) {
+        fail(kErrDoneWait);
+        break;
       }
       fence_proxy_async_smem();
       mbar_arrive(&w3);
@@ -637,24 +667,16 @@ __global__ void __launch_bounds__(320, 1)
         tmem_ld32(tl + 64, v);
         if (r < U) {
           float4 *dq = reinterpret_cast<float4 *>(grow + (size_t)h * D);
-          const uint8_t *grw = sm + C::GH + (r >> 5) * 4096 + (r & 31) * 128;  // G row r (32-byte granules)
-          const int rot = r & 7;
-          float4 g[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) g[j] = *reinterpret_cast<const float4 *>(grw + 16 * ((j + rot) & 7));
+          const float4 *gr = reinterpret_cast<const float4 *>(grad + (size_t)(b * U + r) * H * D + (size_t)h * D);
 #pragma unroll
           for (int l16 = 0; l16 < 8; ++l16) {  // features 4*l16 .. 4*l16+3
-            const int ps = 2 * (((l16 >> 1) ^ r) & 3) + (l16 & 1), idx = (ps - rot) & 7;
-            float4 gv = g[0];
-#pragma unroll
-            for (int j = 1; j < 8; ++j) gv = (idx == j) ? g[j] : gv;
-            dq[l16] = make_float4(gv.x * v[4 * l16] * inv_koef, gv.y * v[4 * l16 + 1] * inv_koef,
-                                  gv.z * v[4 * l16 + 2] * inv_koef, gv.w * v[4 * l16 + 3] * inv_koef);
+            const float4 gv = __ldg(gr + l16);
+            dq[l16] = make_float4(nan0(gv.x) * v[4 * l16] * inv_koef, nan0(gv.y) * v[4 * l16 + 1] * inv_koef,
+                                  nan0(gv.z) * v[4 * l16 + 2] * inv_koef, nan0(gv.w) * v[4 * l16 + 3] * inv_koef);
           }
         }
       }
       tc_fence_before();
-      mbar_arrive(&ifree);
     }
   }
 
@@ -767,8 +789,8 @@ inline cudaError_t attn_grad_tc(const float *qkv, float *qkv_g, const float *sco
   const int items = B * H;
   if (items <= 0) return cudaSuccess;
   const int grid = items < sm_count() ? items : sm_count();
-  tc::attn_grad_tc_kernel<<<grid, 320, tc::GradCfg::SMEM, st>>>(qkv, qkv_g, device_status(), U, H, items, koef, tmS,
-                                                                 tmQKV, tmG, tmV0);
+  tc::attn_grad_tc_kernel<<<grid, 320, tc::GradCfg::SMEM, st>>>(qkv, grad, qkv_g, device_status(), U, H, items, koef,
+                                                                 tmS, tmQKV, tmG, tmV0);
   return cudaGetLastError();
 }
 
