@@ -144,11 +144,9 @@ __global__ void __launch_bounds__(448, 1)
           break;
         }
         uint8_t *base = smem + st * C::STAGE_BYTES;
-#pragma unroll
-        for (uint32_t f = ptid; f < C::A_BYTES / 16; f += 128) split_in_place(base, base + C::A_BYTES, 16u * f);
-#pragma unroll
-        for (uint32_t f = ptid; f < C::B_BYTES / 16; f += 128)
-          split_in_place(base + 2 * C::A_BYTES, base + 2 * C::A_BYTES + C::B_BYTES, 16u * f);
+        static_assert(C::A_BYTES % 2048 == 0 && C::B_BYTES % 2048 == 0, "whole chunks per producer thread");
+        split_chunks<C::A_BYTES / 2048>(base, base + C::A_BYTES, 16u * ptid, 2048u);
+        split_chunks<C::B_BYTES / 2048>(base + 2 * C::A_BYTES, base + 2 * C::A_BYTES + C::B_BYTES, 16u * ptid, 2048u);
         fence_proxy_async_smem();
         mbar_arrive(&full[st]);
       }
@@ -518,27 +516,32 @@ __global__ void __launch_bounds__(320, 1)
       // to dV.  Thread wt handles row 32j + wt/8 of each u-group, 16 bytes at a time.
       for (int j = 0; j < 4; ++j) {
         const int q = 32 * j + (wt >> 3);
+        const uint32_t off = 4096u * j + 16u * wt;
+        if (q >= U) {
 #pragma unroll
-        for (int ug = 0; ug < 4; ++ug) {
-          const uint32_t off = 16384u * ug + 4096u * j + 16u * wt;
-          if (q >= U) {
-            *reinterpret_cast<float4 *>(sm + C::SH + off) = make_float4(0.f, 0.f, 0.f, 0.f);
-            *reinterpret_cast<float4 *>(sm + C::SL + off) = make_float4(0.f, 0.f, 0.f, 0.f);
-          } else {
-            split_in_place(sm + C::SH, sm + C::SL, off);
+          for (int ug = 0; ug < 4; ++ug) {
+            *reinterpret_cast<float4 *>(sm + C::SH + 16384u * ug + off) = make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4 *>(sm + C::SL + 16384u * ug + off) = make_float4(0.f, 0.f, 0.f, 0.f);
           }
+        } else {
+          split_chunks<4>(sm + C::SH, sm + C::SL, off, 16384u);
         }
-        split_in_place(sm + C::GH, sm + C::GL, 4096u * j + 16u * wt);
+        split_chunks<1>(sm + C::GH, sm + C::GL, off, 0u);
         fence_proxy_async_smem();
         mbar_arrive(&w1[j]);
       }
       // G o Q -> XH / XL (dK's B operand) while dV runs
-      for (uint32_t f = wt; f < 1024; f += 256) {
-        const uint32_t off = 16u * f;
-        const float4 g = *reinterpret_cast<const float4 *>(sm + C::GH + off);
-        const float4 qv = *reinterpret_cast<const float4 *>(sm + C::QR + off);
-        *reinterpret_cast<float4 *>(sm + C::XH + off) = make_float4(g.x * qv.x, g.y * qv.y, g.z * qv.z, g.w * qv.w);
-        split_in_place(sm + C::XH, sm + C::XL, off);
+      {
+        float4 g[4], qv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          g[i] = *reinterpret_cast<const float4 *>(sm + C::GH + 16u * (wt + 256 * i));
+          qv[i] = *reinterpret_cast<const float4 *>(sm + C::QR + 16u * (wt + 256 * i));
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          store_split_full(sm + C::XH, sm + C::XL, 16u * (wt + 256 * i),
+                           make_float4(g[i].x * qv[i].x, g[i].y * qv[i].y, g[i].z * qv[i].z, g[i].w * qv[i].w));
       }
       fence_proxy_async_smem();
       mbar_arrive(&qfree);  // raw Q consumed: the loader brings raw K into QR
@@ -578,16 +581,21 @@ __global__ void __launch_bounds__(320, 1)
         break;
       }
       tc_fence_after();
-      for (uint32_t f = wt; f < 4096; f += 256) {
-        const uint32_t off = 16u * f;
-        const int ug = off >> 14, q = (off & 16383u) >> 7;
-        const int c0 = ((((off & 127u) >> 5) ^ q) & 3) * 8 + ((off & 31u) >> 2);  // logical column of lane 0
-        const float4 hi = *reinterpret_cast<const float4 *>(sm + C::SH + off);  // the full fp32 S
-        const float aq = AVs[q];
-        const float4 v = *reinterpret_cast<const float4 *>(V0s + 32 * ug + c0);
-        float4 cv = make_float4(hi.x * (v.x - aq), hi.y * (v.y - aq), hi.z * (v.z - aq), hi.w * (v.w - aq));
-        *reinterpret_cast<float4 *>(sm + C::SH + off) = cv;
-        split_in_place(sm + C::SH, sm + C::SL, off);
+      for (int f0 = 0; f0 < 16; f0 += 4) {  // four chunks at a time: their loads overlap
+        float4 sv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sv[i] = *reinterpret_cast<const float4 *>(sm + C::SH + 16u * (wt + 256 * (f0 + i)));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t off = 16u * (wt + 256 * (f0 + i));
+          const int ug = off >> 14, q = (off & 16383u) >> 7;
+          const int c0 = ((((off & 127u) >> 5) ^ q) & 3) * 8 + ((off & 31u) >> 2);  // logical column of lane 0
+          const float4 hi = sv[i];  // the full fp32 S
+          const float aq = AVs[q];
+          const float4 v = *reinterpret_cast<const float4 *>(V0s + 32 * ug + c0);
+          store_split_full(sm + C::SH, sm + C::SL, off,
+                           make_float4(hi.x * (v.x - aq), hi.y * (v.y - aq), hi.z * (v.z - aq), hi.w * (v.w - aq)));
+        }
       }
       fence_proxy_async_smem();
       mbar_arrive(&w2);
@@ -596,10 +604,12 @@ __global__ void __launch_bounds__(320, 1)
         fail(kErrFullWait);
         break;
       }
-      for (uint32_t f = wt; f < 1024; f += 256) {
-        const uint32_t off = 16u * f;
-        *reinterpret_cast<float4 *>(sm + C::GH + off) = *reinterpret_cast<const float4 *>(sm + C::QR + off);
-        split_in_place(sm + C::GH, sm + C::GL, off);
+      {
+        float4 kv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) kv[i] = *reinterpret_cast<const float4 *>(sm + C::QR + 16u * (wt + 256 * i));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) store_split_full(sm + C::GH, sm + C::GL, 16u * (wt + 256 * i), kv[i]);
       }
       // W3, per 32-row chunk j of q once dK has read it: permute C's rows to the K-major swizzle.
       // Thread wt: buffer wt/128 (hi, lo), u-group (wt/32)%4, row q = 32j + wt%32.

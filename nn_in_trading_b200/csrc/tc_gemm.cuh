@@ -311,15 +311,33 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *tm, in
       : "memory");
 }
 
-// Raw tile -> (sanitised hi in place, lo): chunk f of the region, 16 bytes each.
-__device__ __forceinline__ void split_in_place(uint8_t *hi, uint8_t *lo, uint32_t off) {
-  float4 x = *reinterpret_cast<const float4 *>(hi + off);
-  if (!(isfinite(x.x) && isfinite(x.y) && isfinite(x.z) && isfinite(x.w))) {
-    x = make_float4(nan0(x.x), nan0(x.y), nan0(x.z), nan0(x.w));
-    *reinterpret_cast<float4 *>(hi + off) = x;
-  }
+// Sanitised value -> (hi = the full fp32 value, lo = value - trunc(value)): for tiles whose hi half
+// is also read as fp32 by the CUDA cores (the tensor cores truncate it themselves).
+__device__ __forceinline__ void store_split_full(uint8_t *hi, uint8_t *lo, uint32_t off, float4 v) {
+  v = make_float4(nan0(v.x), nan0(v.y), nan0(v.z), nan0(v.w));
+  *reinterpret_cast<float4 *>(hi + off) = v;
   *reinterpret_cast<float4 *>(lo + off) =
-      make_float4(x.x - tf32_hi(x.x), x.y - tf32_hi(x.y), x.z - tf32_hi(x.z), x.w - tf32_hi(x.w));
+      make_float4(v.x - tf32_hi(v.x), v.y - tf32_hi(v.y), v.z - tf32_hi(v.z), v.w - tf32_hi(v.w));
+}
+
+// NCH chunks first, first + stride, ...: every load is issued before the first store, so the
+// shared-memory latencies overlap instead of forming a load -> store chain per chunk.
+template <int NCH>
+__device__ __forceinline__ void split_chunks(uint8_t *hi, uint8_t *lo, uint32_t first, uint32_t stride) {
+  float4 x[NCH];
+#pragma unroll
+  for (int i = 0; i < NCH; ++i) x[i] = *reinterpret_cast<const float4 *>(hi + first + i * stride);
+#pragma unroll
+  for (int i = 0; i < NCH; ++i) {
+    const uint32_t off = first + i * stride;
+    float4 v = x[i];
+    if (!(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w))) {
+      v = make_float4(nan0(v.x), nan0(v.y), nan0(v.z), nan0(v.w));
+      *reinterpret_cast<float4 *>(hi + off) = v;
+    }
+    *reinterpret_cast<float4 *>(lo + off) =
+        make_float4(v.x - tf32_hi(v.x), v.y - tf32_hi(v.y), v.z - tf32_hi(v.z), v.w - tf32_hi(v.w));
+  }
 }
 
 // Persistent kernel: CTA i processes tiles i, i + gridDim.x, ... (n-tile fastest, so the CTAs in
@@ -477,16 +495,14 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + 6), 1)
         for (int i = 0; i < C::A_CHUNKS; ++i)
           store_split(base, base + C::A_BYTES, chunk_place<A_K, BM, BK>(ptid + 128 * i, row, k), va[i]);
       } else {
-#pragma unroll
-        for (int i = 0; i < C::A_CHUNKS; ++i) split_in_place(base, base + C::A_BYTES, 16u * (ptid + 128 * i));
+        split_chunks<C::A_CHUNKS>(base, base + C::A_BYTES, 16u * ptid, 16u * 128);
       }
       if (B_MODE == OP_REGS) {
 #pragma unroll
         for (int i = 0; i < C::B_CHUNKS; ++i)
           store_split(b_hi, b_lo, chunk_place<B_K, BN, BK>(ptid + 128 * i, row, k), vb[i]);
       } else if (B_MODE == OP_TMA) {
-#pragma unroll
-        for (int i = 0; i < C::B_CHUNKS; ++i) split_in_place(b_hi, b_lo, 16u * (ptid + 128 * i));
+        split_chunks<C::B_CHUNKS>(b_hi, b_lo, 16u * ptid, 16u * 128);
         // the all-ones column lies outside the B tensor, so TMA filled it with zeros
         if (p.ones >= 0 && p.ones < BN && ptid < BK && p.kbeg + p.kk * BK + ptid < p.kend) {
           const int kr = ptid, j = p.ones;
