@@ -84,6 +84,18 @@ struct ConvEpiPlain {
   }
 };
 
+// ConvEpiPlain with the output written by TMA stores on the tensor-core path (rows of wout floats,
+// 16-byte aligned, wout and the computed columns multiples of 4; checked with tma_store_ok).
+struct ConvEpiTma : ConvEpiPlain {
+  static constexpr bool kTmaStore = true;
+  template <class F>
+  __device__ __forceinline__ void transform(F &&f) const {
+    act_dispatch(act, [&](auto A) { f([](float x, float b) { return activate(x + b, decltype(A)::value); }); });
+  }
+  __device__ __forceinline__ int zc(int z, int) const { return z; }
+  bool out_map(CUtensorMap *tm, int M, int N, int nz) const { return make_tmap(tm, o, wout, 0, N, M, nz, 32, false); }
+};
+
 static int k_feedforward_conv(Launch &L) {
   const int units = (int)L.nd.g[0];
   const int wout_g = L.nd.dims > 1 ? (int)L.nd.g[1] : 1;
@@ -98,7 +110,10 @@ static int k_feedforward_conv(Launch &L) {
   if (var == 1 && step == win && inputs == units * step && win > 0) {
     // windows tile the input: a plain [B*units][win] x W^T GEMM
     FastShape fs{L.B * units, wout_g, win, 1, 1, 0, x, win, 0, w, win + 1, 0};
-    e = gemm_f32_wb<false, false>(L, fs, ConvEpiPlain{w, o, win, wout, act});
+    if (tma_store_ok(o, wout, 0, 1, wout_g))
+      e = gemm_f32_wb<false, false>(L, fs, ConvEpiTma{{w, o, win, wout, act}});
+    else
+      e = gemm_f32_wb<false, false>(L, fs, ConvEpiPlain{w, o, win, wout, act});
   } else {
     GemmShape sh{L.B * units, wout_g, win, var, 1};
     e = gemm_simt<true, false>(sh, ConvLoadX{x, units, step, inputs, var}, ConvLoadW{w, win, wout},

@@ -123,6 +123,19 @@ struct FFEpi {
   }
 };
 
+// FFEpi with the output written by TMA stores on the tensor-core path (checked with tma_store_ok).
+struct FFEpiTma : FFEpi {
+  static constexpr bool kTmaStore = true;
+  template <class F>
+  __device__ __forceinline__ void transform(F &&f) const {
+    act_dispatch(act, [&](auto A) { f([](float x, float b) { return activate(x + b, decltype(A)::value); }); });
+  }
+  __device__ __forceinline__ int zc(int z, int) const { return z; }
+  bool out_map(CUtensorMap *tm, int M, int N, int nz) const {
+    return make_tmap(tm, y, outputs, 0, N, M, nz, 32, false);
+  }
+};
+
 __global__ void ff_flags_kernel(const float *w, const float *x, const float *y, float *flags, int inputs,
                                 int outputs, int B) {
   size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
@@ -160,7 +173,9 @@ static int k_feedforward(Launch &L) {
     NN_CHECK_LAUNCH(L);
   } else {
     FastShape fs{L.B, outputs, inputs, 1, 1, 0, x, inputs, 0, w, ld, 0};
-    cudaError_t e = gemm_f32_wb<false, false>(L, fs, FFEpi{w, y, ld, inputs, outputs, act});
+    cudaError_t e = tma_store_ok(y, outputs, 0, 1, outputs)
+                        ? gemm_f32_wb<false, false>(L, fs, FFEpiTma{{w, y, ld, inputs, outputs, act}})
+                        : gemm_f32_wb<false, false>(L, fs, FFEpi{w, y, ld, inputs, outputs, act});
     if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
     L.counted();
   }

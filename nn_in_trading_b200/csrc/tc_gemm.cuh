@@ -186,8 +186,8 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
 }
 
 // 32 consecutive fp32 columns of this warp's 32 lanes: v[j] = D[lane][col + j].
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
+// tcgen05.ld of 32 columns of the warp's 32 lanes, not yet waited for
+__device__ __forceinline__ void tmem_ld32_issue(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -197,7 +197,9 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
         "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
-  // the wait names the registers so no use of them can be scheduled before it
+}
+// tcgen05.wait::ld (every load this thread issued), naming r so that no use of it is scheduled before
+__device__ __forceinline__ void tmem_wait_into(uint32_t (&r)[32], float (&v)[32]) {
   asm volatile(
       "tcgen05.wait::ld.sync.aligned;"
       : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
@@ -208,6 +210,11 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
       : "memory");
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  tmem_ld32_issue(taddr, r);
+  tmem_wait_into(r, v);
 }
 
 __device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
@@ -262,21 +269,38 @@ struct ep_col_major : std::false_type {};
 template <class T>
 struct ep_col_major<T, std::void_t<decltype(T::kColMajor)>> : std::integral_constant<bool, T::kColMajor> {};
 
+// Epilogue functors whose output is a plain [z][row][column] fp32 tensor (row stride a multiple of 4
+// elements, 16-byte aligned base): the epilogue stages each 32 x 32 chunk in shared memory and the
+// TMA engine writes it out (kTmaStore), clipping rows and columns past the end.  Such a functor
+// provides `transform(f)`, which calls f with the per-element map (accumulator, column constant) ->
+// output (activation dispatched once), `zc(z, split)`, the tensor's outer coordinate, and on the host
+// `out_map(tm, M, N, nz)`, which encodes the tensor map with a 32 x 32 box and the 128-byte swizzle.
+template <class T, class = void>
+struct ep_tma_store : std::false_type {};
+template <class T>
+struct ep_tma_store<T, std::void_t<decltype(T::kTmaStore)>> : std::integral_constant<bool, T::kTmaStore> {};
+
 // Epilogue warps of a tcgemm_kernel variant: 8 (two per tensor-memory lane quarter, one per half of
 // the tile's columns) when TMA or bulk copies feed the stages; 4 when producer warps load operands
 // through registers (their double-buffered loads need the register budget of a 320-thread CTA).
 __host__ __device__ constexpr int epi_warps(int a_mode, int b_mode) { return (a_mode == 0 || b_mode == 0) ? 4 : 8; }
+// Producer warps: 4 when they load operands through registers; 8 when they only split tiles that TMA
+// or bulk copies brought in (more warps, fewer chunks each, a larger share of the issue slots).
+__host__ __device__ constexpr int prod_warps(int a_mode, int b_mode) { return (a_mode == 0 || b_mode == 0) ? 4 : 8; }
 
-template <int BN, int BK, int STAGES, int EPIW = 4>
+template <int BN, int BK, int STAGES, int EPIW = 4, bool TMA_ST = false>
 struct Cfg {
   static constexpr int BM = 128;
   static constexpr uint32_t A_BYTES = BM * BK * 4;  // one of hi / lo
   static constexpr uint32_t B_BYTES = BN * BK * 4;
   static constexpr uint32_t STAGE_BYTES = 2 * (A_BYTES + B_BYTES);
   static constexpr uint32_t EPI_OFF = STAGES * STAGE_BYTES;
-  static constexpr uint32_t EPI_BYTES = EPIW * 32 * 36 * 4;  // one 32 x 36 transpose buffer per epilogue warp
+  // per epilogue warp: one 32 x 36 transpose buffer, or one 4 KB TMA-store box (1024-byte aligned)
+  static constexpr uint32_t EPI_BYTES = TMA_ST ? EPIW * 4096 : EPIW * 32 * 36 * 4;
   static constexpr uint32_t COL_OFF = EPI_OFF + EPI_BYTES;  // column constants of the whole product
-  static constexpr int COL_FLOATS = 2048;
+  // (none with TMA stores: their shared memory goes to one more stage, and the constants come
+  // through L1, where every lane of a warp reads the same address)
+  static constexpr int COL_FLOATS = TMA_ST ? 0 : 2048;
   static constexpr uint32_t SMEM = COL_OFF + COL_FLOATS * 4 + 1024;  // + alignment slack
   static constexpr int A_CHUNKS = BM * BK / 4 / 128;            // float4 chunks per producer thread per stage
   static constexpr int B_CHUNKS = BN * BK / 4 / 128;
@@ -287,6 +311,7 @@ struct Cfg {
   static_assert((BM * BK / 4) % 128 == 0 && (BN * BK / 4) % 128 == 0, "chunks per thread");
   static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0 && TMEM_COLS >= 32 && TMEM_COLS <= 512, "tensor-memory columns");
   static_assert(SMEM <= 232448, "shared memory per CTA");
+  static_assert(!TMA_ST || EPI_OFF % 1024 == 0, "TMA-store boxes use the 128-byte swizzle");
 };
 
 // Where an operand's stage tiles come from.
@@ -318,6 +343,25 @@ __device__ __forceinline__ void store_split_full(uint8_t *hi, uint8_t *lo, uint3
   *reinterpret_cast<float4 *>(hi + off) = v;
   *reinterpret_cast<float4 *>(lo + off) =
       make_float4(v.x - tf32_hi(v.x), v.y - tf32_hi(v.y), v.z - tf32_hi(v.z), v.w - tf32_hi(v.w));
+}
+
+// 3-d tiled TMA store of one box from shared memory into the tensor (bulk-group completion).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *tm, const void *src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tm)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// at most N committed bulk groups may still be reading their shared-memory source
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// at most N committed bulk groups may still be incomplete
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // NCH chunks first, first + stride, ...: every load is issued before the first store, so the
@@ -354,14 +398,17 @@ __device__ __forceinline__ void split_chunks(uint8_t *hi, uint8_t *lo, uint32_t 
 // chunks go out as float4s instead (`col4` / `put_rows4`: a lane stores 4 columns of 8 rows, a warp
 // instruction 4 rows x 128 bytes).
 template <int BN, int BK, int STAGES, bool A_MCONTIG, bool B_NCONTIG, int A_MODE, int B_MODE, class EP>
-__global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + 6), 1)
+__global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + prod_warps(A_MODE, B_MODE) + 2), 1)
     tcgemm_kernel(FastShape s, EP ep, int *err, int vec_a, int vec_b, int vec_out, int tiles_n, int tiles_m,
                   int total, const uint8_t *bimg, int kstages, const __grid_constant__ CUtensorMap tmA,
-                  const __grid_constant__ CUtensorMap tmB) {
+                  const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmO) {
   constexpr int EPIW = epi_warps(A_MODE, B_MODE);
+  constexpr bool TMA_ST = ep_tma_store<EP>::value && EPIW == 8;
   // roles: warps [0, EPIW) epilogue, then 4 producer warps, the MMA warp and the loader warp
-  constexpr int kProd0 = EPIW, kMma = EPIW + 4, kLoad = EPIW + 5;
-  using C = Cfg<BN, BK, STAGES, EPIW>;
+  constexpr int PW = prod_warps(A_MODE, B_MODE), NPT = 32 * PW;
+  constexpr int kProd0 = EPIW, kMma = EPIW + PW, kLoad = EPIW + PW + 1;
+  static_assert(NPT == 128 || (A_MODE != OP_REGS && B_MODE != OP_REGS), "register loads assume 128 producers");
+  using C = Cfg<BN, BK, STAGES, EPIW, TMA_ST>;
   constexpr int BM = C::BM;
   constexpr bool A_K = !A_MCONTIG, B_K = !B_NCONTIG;
   static_assert(A_MODE != OP_PACKED, "only the B operand is packed");
@@ -404,7 +451,7 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + 6), 1)
 
   if (tid == 0) {
     for (int i = 0; i < STAGES; ++i) {
-      mbar_init(&full[i], 128);
+      mbar_init(&full[i], NPT);
       mbar_init(&empty[i], 1);
       mbar_init(&tmaf[i], 1);
     }
@@ -426,7 +473,7 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + 6), 1)
   const uint32_t tmem = tmem_slot;
   const int n_real = s.ones_col >= 0 ? s.ones_col : s.N;
 
-  if (warp >= kProd0 && warp < kProd0 + 4) {
+  if (warp >= kProd0 && warp < kProd0 + PW) {
     // ------------------------------------------------------------ producers
     // OP_REGS operands are loaded one stage ahead: the global loads of the next stage are in
     // flight while the current one is split and stored (two register sets, used alternately).
@@ -495,14 +542,14 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + 6), 1)
         for (int i = 0; i < C::A_CHUNKS; ++i)
           store_split(base, base + C::A_BYTES, chunk_place<A_K, BM, BK>(ptid + 128 * i, row, k), va[i]);
       } else {
-        split_chunks<C::A_CHUNKS>(base, base + C::A_BYTES, 16u * ptid, 16u * 128);
+        split_chunks<C::A_BYTES / 16 / NPT>(base, base + C::A_BYTES, 16u * ptid, 16u * NPT);
       }
       if (B_MODE == OP_REGS) {
 #pragma unroll
         for (int i = 0; i < C::B_CHUNKS; ++i)
           store_split(b_hi, b_lo, chunk_place<B_K, BN, BK>(ptid + 128 * i, row, k), vb[i]);
       } else if (B_MODE == OP_TMA) {
-        split_chunks<C::B_CHUNKS>(b_hi, b_lo, 16u * ptid, 16u * 128);
+        split_chunks<C::B_BYTES / 16 / NPT>(b_hi, b_lo, 16u * ptid, 16u * NPT);
         // the all-ones column lies outside the B tensor, so TMA filled it with zeros
         if (p.ones >= 0 && p.ones < BN && ptid < BK && p.kbeg + p.kk * BK + ptid < p.kend) {
           const int kr = ptid, j = p.ones;
@@ -650,6 +697,71 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + 6), 1)
     asm volatile("bar.sync 2, %0;" ::"r"(32 * EPIW) : "memory");
     const int quarter = warp & 3;  // tensor-memory lane quarter = rows 32*quarter .. +31 of the tile
     const int c_begin = EPIW == 8 ? (warp >> 2) * (BN / 2) : 0, c_end = EPIW == 8 ? c_begin + BN / 2 : BN;
+    if constexpr (TMA_ST) {
+      // each 32 x 32 chunk: accumulator -> registers -> column constant and activation -> the warp's
+      // 4 KB box in shared memory (128-byte swizzle: row r's 16-byte granule g at g ^ (r % 8),
+      // conflict-free) -> one TMA store issued by lane 0.  The box is rewritten only after the
+      // previous chunk's store has read it.
+      uint8_t *box = smem + C::EPI_OFF + warp * 4096;
+      ep.transform([&](auto tr) {
+        int tl = 0;
+        constexpr int NCH = (EPIW == 8 ? BN / 2 : BN) / 32;  // chunks per warp per tile
+        for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x, ++tl) {
+          int m0, n0, z, split, kbeg, kend, nk;
+          decode(t, m0, n0, z, split, kbeg, kend, nk);
+          const int b = tl & 1, u = tl >> 1;
+          // lane j holds the constant of column j of each of the warp's chunks, loaded before the
+          // accumulator wait so that the load latency overlaps it
+          float colv[NCH];
+#pragma unroll
+          for (int k = 0; k < NCH; ++k) {
+            const int n = n0 + c_begin + 32 * k + lane;
+            colv[k] = n < s.N ? ep.col(n, z) : 0.f;
+          }
+          if (!mbar_wait(&accf[b], u & 1, &abort_flag)) {
+            fail(kErrDoneWait);
+            break;
+          }
+          tc_fence_after();
+          const int mw = m0 + quarter * 32;
+#pragma unroll
+          for (int k = 0; k < NCH; ++k) {
+            const int c = c_begin + 32 * k;
+            if (n0 + c >= s.N) break;
+            float v[32];
+            if (nk > 0) {
+              tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * BN + c), v);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = 0.f;
+            }
+            const int nc = n0 + c;
+            if (lane == 0) bulk_wait_read<0>();
+            __syncwarp();
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              float cc[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) cc[i] = __shfl_sync(0xffffffffu, colv[k], 4 * q + i);
+              *reinterpret_cast<float4 *>(box + lane * 128 + (((q ^ lane) & 7) << 4)) =
+                  make_float4(tr(v[4 * q], cc[0]), tr(v[4 * q + 1], cc[1]), tr(v[4 * q + 2], cc[2]),
+                              tr(v[4 * q + 3], cc[3]));
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_3d(&tmO, box, nc, mw, ep.zc(z, split));
+              bulk_commit();
+            }
+          }
+          tc_fence_before();
+          mbar_arrive(&acce[b]);
+        }
+      });
+      // the boxes must be read, and the stores complete, before the CTA exits
+      if (lane == 0) bulk_wait<0>();
+      __syncwarp();
+    } else {
     int tl = 0;
     for (int t = blockIdx.x; t < total && !abort_flag; t += gridDim.x, ++tl) {
       int m0, n0, z, split, kbeg, kend, nk;
@@ -725,6 +837,7 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + 6), 1)
       }
       tc_fence_before();
       mbar_arrive(&acce[b]);
+    }
     }
   }
 
@@ -827,14 +940,23 @@ inline bool make_tmap(CUtensorMap *tm, const float *p, long long ld, long long s
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Whether an output [nz][rows][cols] with row stride ld (elements) can be written by TMA-store
+// epilogues: 16-byte aligned base, rows and z strides multiples of 16 bytes, whole float4 column
+// groups.
+inline bool tma_store_ok(const float *p, long long ld, long long stride_z, int nz, int cols) {
+  return tmap_encoder() && ((uintptr_t)p & 15) == 0 && ld % 4 == 0 && ld > 0 && cols % 4 == 0 &&
+         (nz <= 1 || (stride_z % 4 == 0 && stride_z > 0));
+}
+
 template <int BN, bool A_MCONTIG, bool B_NCONTIG, int A_MODE, int B_MODE, class EP>
 inline cudaError_t tcgemm_launch(const FastShape &s, EP ep, cudaStream_t st, int *err, int va, int vb,
                                  uint8_t *img) {
   constexpr int BK = 32;
   constexpr int EPIW = tc::epi_warps(A_MODE, B_MODE);
+  constexpr bool TMA_ST = tc::ep_tma_store<EP>::value && EPIW == 8;
   // stages fill what the epilogue buffers leave of the 227 KB
-  constexpr int STAGES = BN == 128 ? (EPIW == 8 ? 2 : 3) : (EPIW == 8 ? 3 : 4);
-  using C = tc::Cfg<BN, BK, STAGES, EPIW>;
+  constexpr int STAGES = TMA_ST ? (BN == 128 ? 3 : 4) : BN == 128 ? (EPIW == 8 ? 2 : 3) : (EPIW == 8 ? 3 : 4);
+  using C = tc::Cfg<BN, BK, STAGES, EPIW, TMA_ST>;
   auto fn = tc::tcgemm_kernel<BN, BK, STAGES, A_MCONTIG, B_NCONTIG, A_MODE, B_MODE, EP>;
   static bool attr = false;  // per instantiation; setting it twice is harmless
   if (!attr) {
@@ -848,9 +970,13 @@ inline cudaError_t tcgemm_launch(const FastShape &s, EP ep, cudaStream_t st, int
   if (total > (1LL << 30)) return cudaErrorInvalidValue;
   const int grid = (int)(total < sm_count() ? total : sm_count());
   const int kstages = (s.K + BK - 1) / BK;
-  CUtensorMap tmA, tmB;
+  CUtensorMap tmA, tmB, tmO;
   std::memset(&tmA, 0, sizeof tmA);
   std::memset(&tmB, 0, sizeof tmB);
+  std::memset(&tmO, 0, sizeof tmO);
+  if constexpr (TMA_ST) {
+    if (!ep.out_map(&tmO, s.M, s.N, s.nz * s.splits)) return cudaErrorInvalidValue;
+  }
   if (A_MODE == tc::OP_TMA) {
     const bool ok = A_MCONTIG ? make_tmap(&tmA, s.A, s.lda, s.strideA, s.M, s.K, s.nz, 32, true)
                               : make_tmap(&tmA, s.A, s.lda, s.strideA, s.K, s.M, s.nz, 128, false);
@@ -867,8 +993,8 @@ inline cudaError_t tcgemm_launch(const FastShape &s, EP ep, cudaStream_t st, int
     tc::pack_b_kernel<BN, BK, !B_NCONTIG><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(s.B, s.ldb, s.N, s.K, img,
                                                                                        tiles_n, kstages);
   }
-  fn<<<grid, 32 * (EPIW + 6), C::SMEM, st>>>(s, ep, err, va, vb, ep.aligned4() ? 1 : 0, tiles_n, tiles_m, (int)total, img,
-                                  kstages, tmA, tmB);
+  fn<<<grid, 32 * (EPIW + tc::prod_warps(A_MODE, B_MODE) + 2), C::SMEM, st>>>(s, ep, err, va, vb, ep.aligned4() ? 1 : 0, tiles_n, tiles_m, (int)total, img,
+                                  kstages, tmA, tmB, tmO);
   return cudaGetLastError();
 }
 
