@@ -170,7 +170,7 @@ static int k_mh_attention_out(Launch &L) {
   float *qkv = L.buf(1, (size_t)L.B * units * 3 * heads * dim);
   float *out = L.buf(2, (size_t)L.B * units * heads * dim);
   if (!scores || !qkv || !out) return NN_ERR_BOUNDS;
-  if (attn_tc_ok(qkv, scores, units, heads, dim)) {
+  if (attn_tc_ok(qkv, scores, units, heads, dim) && ((uintptr_t)out & 15) == 0) {
     cudaError_t e = attn_tc<tc::kAttnOut>(qkv, scores, out, L.B, units, heads, 0, 1.f, L.stream);
     if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
     L.counted();

@@ -29,23 +29,28 @@ struct AttnCfg {
   static constexpr uint32_t A_BYTES = BM * BK * 4, B_BYTES = BN * BK * 4;
   static constexpr uint32_t STAGE_BYTES = 2 * (A_BYTES + B_BYTES);
   static constexpr uint32_t EPI_OFF = STAGES * STAGE_BYTES;
-  // score: each lane quarter keeps its 32 rows x 128 keys of exponentials (row stride 129 floats)
-  // plus two partial sums per row; out: a 32 x 33 transpose buffer per lane quarter
-  static constexpr uint32_t EPI_BYTES = MODE == kAttnScore ? 4 * 32 * 129 * 4 + 256 * 4 : 4 * 32 * 33 * 4;
+  // TMA-store boxes of 32 rows x 32 floats (128-byte swizzle, 4 KB, 1024-byte aligned).  score: two
+  // per epilogue warp (its 32 rows x 64 keys) plus the two partial row sums, double-buffered by
+  // item parity; out: one per lane quarter
+  static constexpr uint32_t PSUM_OFF = 8 * 8192;
+  static constexpr uint32_t EPI_BYTES = MODE == kAttnScore ? PSUM_OFF + 2 * 256 * 4 : 4 * 4096;
   static constexpr uint32_t SMEM = EPI_OFF + EPI_BYTES + 1024;
   static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
   static_assert(SMEM <= 232448, "shared memory per CTA");
   static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0, "tensor-memory columns");
+  static_assert(EPI_OFF % 1024 == 0, "store boxes use the 128-byte swizzle");
 };
 
 // tmQ:  qkv as [B*U rows][3*H*D], box 32 x 128, 128-byte swizzle (K-major Q and K tiles)
 // tmS:  scores as [B*U][H][U],    box 32 x 1 x 128, 128-byte swizzle (K-major score tiles)
 // tmV:  qkv as [B*U rows][3*H*D], box 32 x 32, 128-byte swizzle / 32-byte granules (MN-major V)
+// tmO:  the output as [B][U][H][U] (score) or [B][U][H][D] (out), box 32 x 1 x 32 x 1, 128-byte
+//       swizzle: TMA stores clip keys and rows past `units`
 template <int MODE>
 __global__ void __launch_bounds__(448, 1)
-    attn_tc_kernel(float *__restrict__ out, int *err, int U, int H, int items, int mask, float koef,
-                   const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmS,
-                   const __grid_constant__ CUtensorMap tmV) {
+    attn_tc_kernel(int *err, int U, int H, int items, int mask, float koef, const __grid_constant__ CUtensorMap tmQ,
+                   const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmV,
+                   const __grid_constant__ CUtensorMap tmO) {
   using C = AttnCfg<MODE>;
   constexpr int BM = C::BM, BN = C::BN, BK = C::BK, NK = C::NK, STAGES = C::STAGES;
   constexpr int D = 32;
@@ -197,9 +202,7 @@ __global__ void __launch_bounds__(448, 1)
   } else {
     // ------------------------------------------------------------ epilogue (thread = row q)
     const int quarter = warp & 3, half = warp >> 2;
-    float *buf = reinterpret_cast<float *>(smem + C::EPI_OFF) + quarter * 32 * 33;  // out mode
     int tl = 0;
-    uint32_t nsync = 0;
     const float inv_koef = 1.f / koef;
     for (int t = blockIdx.x; t < items && !abort_flag; t += gridDim.x, ++tl) {
       const int bb = t / H, h = t % H;
@@ -214,78 +217,77 @@ __global__ void __launch_bounds__(448, 1)
       if (MODE == kAttnScore) {
         // MHAttentionScore (NeuroNet.cl:1662-1719): e = exp(clamp(s / koef, -100, 100)) over the
         // unmasked keys, divided by their sum when the sum exceeds 1.  The two warps of a lane
-        // quarter each exponentiate one half of the keys into the quarter's row buffer and publish
-        // a partial sum; after a bounded barrier each stores its half of the rows along the keys.
-        float *rows = reinterpret_cast<float *>(smem + C::EPI_OFF) + quarter * 32 * 129;
-        float *psum = reinterpret_cast<float *>(smem + C::EPI_OFF) + 4 * 32 * 129;  // [2][128]
+        // quarter each exponentiate one half of the keys (kept in registers) and publish a partial
+        // sum per row; after a bounded barrier each thread writes its row of the two store boxes,
+        // scaled, and lane 0 hands the boxes to TMA.
+        uint8_t *bx = smem + C::EPI_OFF + warp * 8192;
+        float *psum = reinterpret_cast<float *>(smem + C::EPI_OFF + C::PSUM_OFF) + (tl & 1) * 256;  // [2][128]
         const int kmax = mask > 0 ? min(U, q + 1) : U;  // keys that take part in row q
+        float e[2][32];
+        tmem_ld32(trow + (uint32_t)(half * 64), e[0]);
+        tmem_ld32(trow + (uint32_t)(half * 64 + 32), e[1]);
         float sum = 0.f;
-#pragma unroll 1
-        for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
-          float v[32];
-          tmem_ld32(trow + (uint32_t)c, v);
+#pragma unroll
+        for (int cb = 0; cb < 2; ++cb)
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            const int kk = c + j;
-            float e = 0.f;
-            if (kk < kmax) {
-              e = exp2f(clampf(v[j] * inv_koef, -100.f, 100.f) * 1.4426950408889634f);
-              if (isnan(e)) e = 0.f;
-              sum += e;
+            float x = 0.f;
+            if (half * 64 + 32 * cb + j < kmax) {
+              x = exp2f(clampf(e[cb][j] * inv_koef, -100.f, 100.f) * 1.4426950408889634f);
+              if (isnan(x)) x = 0.f;
+              sum += x;
             }
-            rows[lane * 129 + kk] = e;
+            e[cb][j] = x;
           }
-        }
         psum[half * 128 + q] = sum;
         mbar_arrive(&esync);
-        const bool ok = mbar_wait(&esync, nsync & 1, &abort_flag);
-        ++nsync;
+        const bool ok = mbar_wait(&esync, tl & 1, &abort_flag);
         if (!ok) {
           fail(kErrDoneWait);
           break;
         }
-        float *srow0 = out + (size_t)bb * U * H * U + (size_t)h * U;  // row q at srow0 + q*H*U
-        const int r0 = quarter * 32 + half * 16;
-        const int r1 = min(r0 + 16, U);
-#pragma unroll 1
-        for (int r = r0; r < r1; ++r) {
-          const float tot = psum[r] + psum[128 + r];
-          const float sc = tot > 1.f ? 1.f / tot : 1.f;
-          float *dst = srow0 + (size_t)r * H * U;
-          const float *src = rows + (r - quarter * 32) * 129;
+        const float tot = psum[q] + psum[128 + q];
+        const float sc = tot > 1.f ? 1.f / tot : 1.f;
+        if (lane == 0) bulk_wait_read<0>();  // the previous item's stores have read the boxes
+        __syncwarp();
 #pragma unroll
-          for (int c = 0; c < BN; c += 32) {
-            const int kk = c + lane;
-            if (kk < U) dst[kk] = src[kk] * sc;
-          }
-        }
-        // the next item rewrites the row buffer and the partial sums: every warp finishes reading
-        // first (the next accumulator can be ready while a slower warp is still storing this one)
-        mbar_arrive(&esync);
-        const bool ok2 = mbar_wait(&esync, nsync & 1, &abort_flag);
-        ++nsync;
-        if (!ok2) {
-          fail(kErrDoneWait);
-          break;
+        for (int cb = 0; cb < 2; ++cb)
+#pragma unroll
+          for (int g = 0; g < 8; ++g)
+            *reinterpret_cast<float4 *>(bx + cb * 4096 + lane * 128 + (((g ^ lane) & 7) << 4)) =
+                make_float4(e[cb][4 * g] * sc, e[cb][4 * g + 1] * sc, e[cb][4 * g + 2] * sc, e[cb][4 * g + 3] * sc);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && quarter * 32 < U) {
+#pragma unroll
+          for (int cb = 0; cb < 2; ++cb)
+            if (half * 64 + 32 * cb < U) tma_store_4d(&tmO, bx + cb * 4096, half * 64 + 32 * cb, h, quarter * 32, bb);
+          bulk_commit();
         }
       } else if (half == 0) {
-        // MHAttentionOut (NeuroNet.cl:1730-1759): O[q][h][d]
+        // MHAttentionOut (NeuroNet.cl:1730-1759): O[q][h][d], the quarter's 32 rows as one box
+        uint8_t *bx = smem + C::EPI_OFF + quarter * 4096;
         float v[32];
         tmem_ld32(trow, v);
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) buf[lane * 33 + j] = v[j];
+        for (int g = 0; g < 8; ++g)
+          *reinterpret_cast<float4 *>(bx + lane * 128 + (((g ^ lane) & 7) << 4)) =
+              make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+        fence_proxy_async_smem();
         __syncwarp();
-        float *obase = out + ((size_t)bb * U * H + h) * D;  // row q at obase + q*H*D
-#pragma unroll 4
-        for (int r = 0; r < 32; ++r) {
-          const int qr = quarter * 32 + r;
-          if (qr < U) obase[(size_t)qr * H * D + lane] = buf[r * 33 + lane];
+        if (lane == 0 && quarter * 32 < U) {
+          tma_store_4d(&tmO, bx, 0, h, quarter * 32, bb);
+          bulk_commit();
         }
-        __syncwarp();
       }
       tc_fence_before();
       mbar_arrive(&acce[b]);
     }
+    // the boxes must be read, and the stores complete, before the CTA exits
+    if (lane == 0) bulk_wait<0>();
+    __syncwarp();
   }
 
   // ------------------------------------------------------------ teardown
@@ -715,7 +717,7 @@ inline bool attn_tc_ok(const float *qkv, const float *scores, int U, int H, int 
 
 inline bool make_tmap2(CUtensorMap *tm, const float *p, int rank, const cuuint64_t *dims, const cuuint64_t *strides,
                        const cuuint32_t *box, bool mn_major) {
-  cuuint32_t es[3] = {1u, 1u, 1u};
+  cuuint32_t es[5] = {1u, 1u, 1u, 1u, 1u};
   return tmap_encoder()(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<float *>(p), dims, strides, box, es,
                         CU_TENSOR_MAP_INTERLEAVE_NONE,
                         mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
@@ -728,10 +730,17 @@ inline cudaError_t attn_tc(const float *qkv, const float *scores, float *out, in
                            float koef, cudaStream_t st) {
   using C = tc::AttnCfg<MODE>;
   const int D = 32;
-  CUtensorMap tmQ, tmS, tmV;
+  CUtensorMap tmQ, tmS, tmV, tmO;
   std::memset(&tmQ, 0, sizeof tmQ);
   std::memset(&tmS, 0, sizeof tmS);
   std::memset(&tmV, 0, sizeof tmV);
+  {  // the output, [B][U][H][inner] with inner = U keys (score) or D features (out)
+    const cuuint64_t inner = MODE == tc::kAttnScore ? (cuuint64_t)U : (cuuint64_t)D;
+    cuuint64_t od[4] = {inner, (cuuint64_t)H, (cuuint64_t)U, (cuuint64_t)B};
+    cuuint64_t os[3] = {inner * 4, inner * H * 4, inner * H * U * 4};
+    cuuint32_t ob[4] = {32u, 1u, 32u, 1u};
+    if (!make_tmap2(&tmO, out, 4, od, os, ob, false)) return cudaErrorInvalidValue;
+  }
   const cuuint64_t rows = (cuuint64_t)B * U, width = (cuuint64_t)3 * H * D;
   // every map is rank 3 (the loads are 3-d; a trailing extent of 1 where the tensor is 2-d)
   if (MODE == tc::kAttnScore) {
@@ -756,7 +765,7 @@ inline cudaError_t attn_tc(const float *qkv, const float *scores, float *out, in
   const int items = B * H;
   if (items <= 0) return cudaSuccess;
   const int grid = items < sm_count() ? items : sm_count();
-  fn<<<grid, 448, C::SMEM, st>>>(out, device_status(), U, H, items, mask, koef, tmQ, tmS, tmV);
+  fn<<<grid, 448, C::SMEM, st>>>(device_status(), U, H, items, mask, koef, tmQ, tmS, tmV, tmO);
   return cudaGetLastError();
 }
 

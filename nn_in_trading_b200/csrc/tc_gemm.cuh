@@ -352,6 +352,13 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap *tm, const void *
                "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
                : "memory");
 }
+// 4-d tiled TMA store of one box from shared memory into the tensor (bulk-group completion).
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap *tm, const void *src, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tm)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // at most N committed bulk groups may still be reading their shared-memory source
 template <int N>
