@@ -276,17 +276,42 @@ struct CWLoadX {  // B(kk=(b,t), n=k)
   }
 };
 
-__global__ void adam_conv_apply_kernel(float *w, float *m, float *v, GradSrc G, size_t n, float l, float b1,
-                                       float b2) {
-  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  float grad = clampf(nan0(G(i)), -kMaxGrad, kMaxGrad);
+// UpdateWeightsConvAdam arithmetic for one weight, given its (batch-mean) gradient before clamping.
+__device__ __forceinline__ void adam_conv_step(float *w, float *m, float *v, size_t i, float graw, float l, float b1,
+                                               float b2) {
+  float grad = clampf(nan0(graw), -kMaxGrad, kMaxGrad);
   float mt = nan0(b1 * m[i] + (1.f - b1) * grad);
   float vt = nan0(b2 * v[i] + (1.f - b2) * (grad * grad), 1.f);
   float weight = nan0(w[i] + nan0(l * mt / sqrtf(vt)));
   w[i] = weight;
   m[i] = mt;
   v[i] = vt;
+}
+
+__global__ void adam_conv_apply_kernel(float *w, float *m, float *v, GradSrc G, size_t n, float l, float b1,
+                                       float b2) {
+  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  adam_conv_step(w, m, v, i, G(i), l, b1, b2);
+}
+
+// The same when the gradient is a sum of many split-K partials: block (32 weights, 8 split
+// groups), each thread summing every 8th partial of one weight (a warp reads 128 contiguous bytes
+// per partial), then a shared-memory reduction and the update by the first group.
+__global__ void adam_conv_apply_split_kernel(float *w, float *m, float *v, GradSrc G, size_t n, float l, float b1,
+                                             float b2) {
+  __shared__ float red[8][33];
+  const size_t i = blockIdx.x * (size_t)32 + threadIdx.x;
+  float s = 0.f;
+  if (i < n)
+    for (int k = threadIdx.y; k < G.splits; k += 8) s += G.p[k * G.stride + i];
+  red[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y != 0 || i >= n) return;
+  float t = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) t += red[j][threadIdx.x];
+  adam_conv_step(w, m, v, i, t * G.scale, l, b1, b2);
 }
 
 struct ConvUpdShape {
@@ -328,7 +353,11 @@ static int adam_conv_apply_src(const Launch &Lc, GradSrc G) {
   size_t n = L.nd.g[0];
   float *w = L.buf(0, n), *m = L.buf(3, n), *v = L.buf(4, n);
   if (!w || !m || !v) return NN_ERR_BOUNDS;
-  adam_conv_apply_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(w, m, v, G, n, L.f(6), L.f(7), L.f(8));
+  if (G.splits > 4)
+    adam_conv_apply_split_kernel<<<(unsigned)((n + 31) / 32), dim3(32, 8), 0, L.stream>>>(w, m, v, G, n, L.f(6), L.f(7),
+                                                                                          L.f(8));
+  else
+    adam_conv_apply_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(w, m, v, G, n, L.f(6), L.f(7), L.f(8));
   NN_CHECK_LAUNCH(L);
   return NN_OK;
 }

@@ -15,9 +15,21 @@
 
 namespace nn {
 
+// out[i] = scale * sum_k p[k * stride + i]: block (32 entries, 8 split groups), each thread summing
+// every 8th partial of one entry, then a shared-memory reduction.
 __global__ void reduce_partials_kernel(float *out, GradSrc src, size_t n) {
-  size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  if (i < n) out[i] = src(i);
+  __shared__ float red[8][33];
+  const size_t i = blockIdx.x * (size_t)32 + threadIdx.x;
+  float s = 0.f;
+  if (i < n)
+    for (int k = threadIdx.y; k < src.splits; k += 8) s += src.p[k * src.stride + i];
+  red[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y != 0 || i >= n) return;
+  float t = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) t += red[j][threadIdx.x];
+  out[i] = t * src.scale;
 }
 
 __global__ void colsum_partial_kernel(float *p, const float *g, int M, int rows, long long ld, int kchunk, int ldp,
@@ -32,18 +44,28 @@ __global__ void colsum_partial_kernel(float *p, const float *g, int M, int rows,
 
 __global__ void colsum_rows_kernel(float *p, const float *g, int M, int rows, long long ld, int kchunk, int ldp,
                                    int col) {
-  __shared__ float red[8][33];
+  // block (32 columns, 32 row groups): every warp reads one 128-byte row segment per load, and each
+  // thread keeps four independent sums so that four loads are in flight
+  __shared__ float red[32][33];
   const int m = blockIdx.x * 32 + threadIdx.x;
   const int r0 = blockIdx.y * kchunk, r1 = min(rows, r0 + kchunk);
-  float s = 0.f;
-  if (m < M)
-    for (int r = r0 + (int)threadIdx.y; r < r1; r += 8) s += nan0(g[(size_t)r * ld + m]);
-  red[threadIdx.y][threadIdx.x] = s;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  if (m < M) {
+    int r = r0 + (int)threadIdx.y;
+    for (; r + 96 < r1; r += 128) {
+      s0 += nan0(g[(size_t)r * ld + m]);
+      s1 += nan0(g[(size_t)(r + 32) * ld + m]);
+      s2 += nan0(g[(size_t)(r + 64) * ld + m]);
+      s3 += nan0(g[(size_t)(r + 96) * ld + m]);
+    }
+    for (; r < r1; r += 32) s0 += nan0(g[(size_t)r * ld + m]);
+  }
+  red[threadIdx.y][threadIdx.x] = (s0 + s1) + (s2 + s3);
   __syncthreads();
   if (threadIdx.y == 0 && m < M) {
     float t = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) t += red[j][threadIdx.x];
+    for (int j = 0; j < 32; ++j) t += red[j][threadIdx.x];
     p[((size_t)blockIdx.y * M + m) * ldp + col] = t;
   }
 }
@@ -333,22 +355,45 @@ struct WGLoadX {  // B(k=b, n=j)
 };
 
 // UpdateWeightsAdam arithmetic (NeuroNet.cl:678-693) with a given pre-clamp gradient.
-__global__ void adam_dense_apply_kernel(float *w, float *m, float *v, GradSrc G, int n_out, int n_col, int inputs,
-                                        float l, float b1, float b2) {
-  size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  if (t >= (size_t)n_out * n_col) return;
-  int i = (int)(t / n_col), j = (int)(t % n_col);
-  size_t wi = (size_t)i * (inputs + 1) + j;
+// UpdateWeightsAdam arithmetic for one weight, given its (batch-mean) gradient before clamping.
+__device__ __forceinline__ void adam_dense_step(float *w, float *m, float *v, size_t wi, float graw, float l, float b1,
+                                                float b2) {
   float weight = nan0(w[wi]);
   float mm = nan0(m[wi]);
   float vv = nan0(v[wi]);
-  float g = clampf(nan0(G(t)), -kMaxGrad, kMaxGrad);
+  float g = clampf(nan0(graw), -kMaxGrad, kMaxGrad);
   float mt = nan0(b1 * mm + (1.f - b1) * g);
   float vt = nan0(b2 * vv + (1.f - b2) * (g * g));
   float delta = nan0(l * (mt / (sqrtf(vt) + 1.0e-37f) - (kL1 * signf(weight) + kL2 * weight)));
   if (fabsf(delta) > 0.f) w[wi] = nan0(w[wi] + delta);
   m[wi] = mt;
   v[wi] = vt;
+}
+
+__global__ void adam_dense_apply_kernel(float *w, float *m, float *v, GradSrc G, int n_out, int n_col, int inputs,
+                                        float l, float b1, float b2) {
+  size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (t >= (size_t)n_out * n_col) return;
+  int i = (int)(t / n_col), j = (int)(t % n_col);
+  adam_dense_step(w, m, v, (size_t)i * (inputs + 1) + j, G(t), l, b1, b2);
+}
+
+// The same with many split-K partials: block (32 weights, 8 split groups), as reduce_partials_kernel.
+__global__ void adam_dense_apply_split_kernel(float *w, float *m, float *v, GradSrc G, int n_out, int n_col,
+                                              int inputs, float l, float b1, float b2) {
+  __shared__ float red[8][33];
+  const size_t t = blockIdx.x * (size_t)32 + threadIdx.x, n = (size_t)n_out * n_col;
+  float s = 0.f;
+  if (t < n)
+    for (int k = threadIdx.y; k < G.splits; k += 8) s += G.p[k * G.stride + t];
+  red[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y != 0 || t >= n) return;
+  float sum = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) sum += red[j][threadIdx.x];
+  const int i = (int)(t / n_col), j = (int)(t % n_col);
+  adam_dense_step(w, m, v, (size_t)i * (inputs + 1) + j, sum * G.scale, l, b1, b2);
 }
 
 // Single-sample fused kernel: exactly the reference's per-weight arithmetic.
@@ -385,8 +430,12 @@ static int adam_dense_apply_src(const Launch &Lc, GradSrc G) {
   float *w = L.buf(0, nw), *m = L.buf(3, nw), *v = L.buf(4, nw);
   if (!w || !m || !v) return NN_ERR_BOUNDS;
   size_t n = (size_t)s.n_out * s.n_col;
-  adam_dense_apply_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(w, m, v, G, s.n_out, s.n_col, s.inputs, L.f(6),
-                                                                L.f(7), L.f(8));
+  if (G.splits > 4)
+    adam_dense_apply_split_kernel<<<(unsigned)((n + 31) / 32), dim3(32, 8), 0, L.stream>>>(
+        w, m, v, G, s.n_out, s.n_col, s.inputs, L.f(6), L.f(7), L.f(8));
+  else
+    adam_dense_apply_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(w, m, v, G, s.n_out, s.n_col, s.inputs, L.f(6),
+                                                                  L.f(7), L.f(8));
   NN_CHECK_LAUNCH(L);
   return NN_OK;
 }

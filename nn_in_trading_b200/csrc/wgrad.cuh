@@ -126,8 +126,8 @@ inline int wgrad_fast(Launch &L, const float *A, long long lda, const float *X, 
     cudaError_t e = tcgemm<true, true>(ft, PartialStoreT{part, M, ldp}, L.stream, device_status());
     if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
     L.counted();
-    colsum_rows_kernel<<<dim3((M + 31) / 32, splits), dim3(32, 8), 0, L.stream>>>(part, A, M, rows, lda, kchunk, ldp,
-                                                                                 N);
+    colsum_rows_kernel<<<dim3((M + 31) / 32, splits), dim3(32, 32), 0, L.stream>>>(part, A, M, rows, lda, kchunk, ldp,
+                                                                                  N);
     NN_CHECK_LAUNCH(L);
   } else if (tc_path(fs)) {
     // the bias input (1) is column N of X: one GEMM writes all N + 1 gradient columns
@@ -178,7 +178,7 @@ inline int finish_update(Launch &L, GradSrc src, size_t n, int (*apply)(const La
   if (L.deferred()) {
     float *slot = L.grad_slot(n);
     if (!slot) return NN_ERR_BOUNDS;
-    reduce_partials_kernel<<<(unsigned)((n + 255) / 256), 256, 0, L.stream>>>(slot, src, n);
+    reduce_partials_kernel<<<(unsigned)((n + 31) / 32), dim3(32, 8), 0, L.stream>>>(slot, src, n);
     NN_CHECK_LAUNCH(L);
     L.defer(apply, slot);
     return NN_OK;
