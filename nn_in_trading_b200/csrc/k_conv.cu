@@ -90,7 +90,7 @@ struct ConvEpiTma : ConvEpiPlain {
   static constexpr bool kTmaStore = true;
   template <class F>
   __device__ __forceinline__ void transform(F &&f) const {
-    act_dispatch(act, [&](auto A) { f([](float x, float b) { return activate(x + b, decltype(A)::value); }); });
+    act_dispatch(act, [&](auto A) { f([](float x, float b, float) { return activate(x + b, decltype(A)::value); }); });
   }
   __device__ __forceinline__ int zc(int z, int) const { return z; }
   bool out_map(CUtensorMap *tm, int M, int N, int nz) const { return make_tmap(tm, o, wout, 0, N, M, nz, 32, false); }
@@ -216,6 +216,21 @@ struct CDEpi {
   }
 };
 
+// CDEpi (one variable, rows of `win` inputs) with the input gradient written by TMA stores and the
+// activation output read as the aux tensor (checked with tma_store_ok).
+struct CDEpiTma : CDEpi {
+  static constexpr bool kTmaStore = true, kAux = true;
+  template <class F>
+  __device__ __forceinline__ void transform(F &&f) const {
+    act_dispatch(act, [&](auto A) { f([](float x, float, float y) { return deactivate(x, y, decltype(A)::value); }); });
+  }
+  __device__ __forceinline__ int zc(int z, int) const { return z; }
+  __device__ __forceinline__ float4 aux4(int m, int, int n) const {
+    return *reinterpret_cast<const float4 *>(o + (size_t)m * win + n);
+  }
+  bool out_map(CUtensorMap *tm, int M, int N, int nz) const { return make_tmap(tm, ig, win, 0, N, M, nz, 32, false); }
+};
+
 static int k_calc_hidden_gradient_conv(Launch &L) {
   const int inputs = (int)L.nd.g[0];
   const int var = L.nd.dims > 1 ? (int)L.nd.g[1] : 1;
@@ -233,7 +248,10 @@ static int k_calc_hidden_gradient_conv(Launch &L) {
     cudaError_t e;
     if (var == 1) {
       FastShape fs{L.B * n_win, win, wout, 1, 1, 0, g, wout, 0, w, win + 1, 0};
-      e = gemm_f32_wb<false, true>(L, fs, CDEpi{o, ig, n_win, win, inputs, var, act});
+      if (tma_store_ok(ig, win, 0, 1, win) && ((uintptr_t)o & 15) == 0)
+        e = gemm_f32_wb<false, true>(L, fs, CDEpiTma{{o, ig, n_win, win, inputs, var, act}});
+      else
+        e = gemm_f32_wb<false, true>(L, fs, CDEpi{o, ig, n_win, win, inputs, var, act});
     } else {
       GemmShape sh{L.B * n_win, win, wout, var, 1};
       e = gemm_simt<true, true>(sh, CDLoadG{g, n_win, wout, outputs, var}, CDLoadW{w, win, wout},

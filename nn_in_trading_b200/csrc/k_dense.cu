@@ -150,7 +150,7 @@ struct FFEpiTma : FFEpi {
   static constexpr bool kTmaStore = true;
   template <class F>
   __device__ __forceinline__ void transform(F &&f) const {
-    act_dispatch(act, [&](auto A) { f([](float x, float b) { return activate(x + b, decltype(A)::value); }); });
+    act_dispatch(act, [&](auto A) { f([](float x, float b, float) { return activate(x + b, decltype(A)::value); }); });
   }
   __device__ __forceinline__ int zc(int z, int) const { return z; }
   bool out_map(CUtensorMap *tm, int M, int N, int nz) const {
@@ -313,6 +313,23 @@ struct CHGEpi {
   }
 };
 
+// CHGEpi with the input gradient written by TMA stores and the activation output read as the aux
+// tensor (checked with tma_store_ok).
+struct CHGEpiTma : CHGEpi {
+  static constexpr bool kTmaStore = true, kAux = true;
+  template <class F>
+  __device__ __forceinline__ void transform(F &&f) const {
+    act_dispatch(act, [&](auto A) { f([](float x, float, float y) { return deactivate(x, y, decltype(A)::value); }); });
+  }
+  __device__ __forceinline__ int zc(int z, int) const { return z; }
+  __device__ __forceinline__ float4 aux4(int m, int, int n) const {
+    return *reinterpret_cast<const float4 *>(o + (size_t)m * inputs + n);
+  }
+  bool out_map(CUtensorMap *tm, int M, int N, int nz) const {
+    return make_tmap(tm, ig, inputs, 0, N, M, nz, 32, false);
+  }
+};
+
 static int k_calc_hidden_gradient(Launch &L) {
   const int inputs = (int)L.nd.g[0];
   const int outputs = L.i(4), act = L.i(5);
@@ -329,7 +346,9 @@ static int k_calc_hidden_gradient(Launch &L) {
     return NN_OK;
   }
   FastShape fs{L.B, inputs, outputs, 1, 1, 0, g, outputs, 0, w, ld, 0};
-  cudaError_t e = gemm_f32_wb<false, true>(L, fs, CHGEpi{o, ig, inputs, act});
+  cudaError_t e = tma_store_ok(ig, inputs, 0, 1, inputs) && ((uintptr_t)o & 15) == 0
+                      ? gemm_f32_wb<false, true>(L, fs, CHGEpiTma{{o, ig, inputs, act}})
+                      : gemm_f32_wb<false, true>(L, fs, CHGEpi{o, ig, inputs, act});
   if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
   L.counted();
   return NN_OK;

@@ -651,41 +651,53 @@ __global__ void __launch_bounds__(320, 1)
       }
       fence_proxy_async_smem();
       mbar_arrive(&w3);
-      // epilogue: warps 0-3 dV and dK rows u, warps 4-7 dQ rows q (tensor-memory lane quarter w % 4)
+      // epilogue: rows r of tensor-memory lane quarter w % 4; warps 0-3 store dV and the first 16
+      // features of dK, warps 4-7 dQ and the last 16 of dK.  The G row dQ needs is loaded (from L2:
+      // TMA brought it in) before the wait for the products, so its latency overlaps them.
+      const int r = (warp & 3) * 32 + lane;
+      float4 gq[8];
+      if (warp >= 4 && r < U) {
+        const float4 *gr = reinterpret_cast<const float4 *>(grad + (size_t)(b * U + r) * H * D + (size_t)h * D);
+#pragma unroll
+        for (int l16 = 0; l16 < 8; ++l16) gq[l16] = __ldg(gr + l16);
+      }
       if (!mbar_wait(&accf, par, &abort_flag)) {
         fail(kErrDoneWait);
         break;
       }
       tc_fence_after();
-      const int r = (warp & 3) * 32 + lane;
       const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
       float *grow = qkv_g + (size_t)(b * U + r) * rs;
+      float4 *dk = reinterpret_cast<float4 *>(grow + (size_t)(H + h) * D);
       if (warp < 4) {
         float v[32], k[32];
         tmem_ld32(tl + 0, v);
         tmem_ld32(tl + 32, k);
         if (r < U) {
           float4 *dv = reinterpret_cast<float4 *>(grow + (size_t)(2 * H + h) * D);
-          float4 *dk = reinterpret_cast<float4 *>(grow + (size_t)(H + h) * D);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            dv[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          for (int j = 0; j < 8; ++j) dv[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
             dk[j] = make_float4(k[4 * j] * inv_koef, k[4 * j + 1] * inv_koef, k[4 * j + 2] * inv_koef,
                                 k[4 * j + 3] * inv_koef);
-          }
         }
       } else {
-        float v[32];
+        float v[32], k[32];
         tmem_ld32(tl + 64, v);
+        tmem_ld32(tl + 32, k);
         if (r < U) {
           float4 *dq = reinterpret_cast<float4 *>(grow + (size_t)h * D);
-          const float4 *gr = reinterpret_cast<const float4 *>(grad + (size_t)(b * U + r) * H * D + (size_t)h * D);
 #pragma unroll
           for (int l16 = 0; l16 < 8; ++l16) {  // features 4*l16 .. 4*l16+3
-            const float4 gv = __ldg(gr + l16);
+            const float4 gv = gq[l16];
             dq[l16] = make_float4(nan0(gv.x) * v[4 * l16] * inv_koef, nan0(gv.y) * v[4 * l16 + 1] * inv_koef,
                                   nan0(gv.z) * v[4 * l16 + 2] * inv_koef, nan0(gv.w) * v[4 * l16 + 3] * inv_koef);
           }
+#pragma unroll
+          for (int j = 4; j < 8; ++j)
+            dk[j] = make_float4(k[4 * j] * inv_koef, k[4 * j + 1] * inv_koef, k[4 * j + 2] * inv_koef,
+                                k[4 * j + 3] * inv_koef);
         }
       }
       tc_fence_before();

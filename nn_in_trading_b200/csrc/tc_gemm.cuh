@@ -272,13 +272,20 @@ struct ep_col_major<T, std::void_t<decltype(T::kColMajor)>> : std::integral_cons
 // Epilogue functors whose output is a plain [z][row][column] fp32 tensor (row stride a multiple of 4
 // elements, 16-byte aligned base): the epilogue stages each 32 x 32 chunk in shared memory and the
 // TMA engine writes it out (kTmaStore), clipping rows and columns past the end.  Such a functor
-// provides `transform(f)`, which calls f with the per-element map (accumulator, column constant) ->
-// output (activation dispatched once), `zc(z, split)`, the tensor's outer coordinate, and on the host
-// `out_map(tm, M, N, nz)`, which encodes the tensor map with a 32 x 32 box and the 128-byte swizzle.
+// provides `transform(f)`, which calls f with the per-element map (accumulator, column constant,
+// aux) -> output (activation dispatched once), `zc(z, split)`, the tensor's outer coordinate, and on
+// the host `out_map(tm, M, N, nz)`, which encodes the tensor map with a 32 x 32 box and the 128-byte
+// swizzle.  A functor with kAux also reads a second tensor element by element (`aux4(m, z, n)`: the
+// 4 values at row m, columns n..n+3, e.g. the activation output a derivative is taken at); aux is 0
+// for the others.
 template <class T, class = void>
 struct ep_tma_store : std::false_type {};
 template <class T>
 struct ep_tma_store<T, std::void_t<decltype(T::kTmaStore)>> : std::integral_constant<bool, T::kTmaStore> {};
+template <class T, class = void>
+struct ep_has_aux : std::false_type {};
+template <class T>
+struct ep_has_aux<T, std::void_t<decltype(T::kAux)>> : std::integral_constant<bool, T::kAux> {};
 
 // Epilogue warps of a tcgemm_kernel variant: 8 (two per tensor-memory lane quarter, one per half of
 // the tile's columns) when TMA or bulk copies feed the stages; 4 when producer warps load operands
@@ -735,6 +742,24 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + prod_warps(A
           for (int k = 0; k < NCH; ++k) {
             const int c = c_begin + 32 * k;
             if (n0 + c >= s.N) break;
+            const int nc = n0 + c;
+            // the second input of this thread's row, in flight during the tensor-memory load
+            float y[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) y[j] = 0.f;
+            if constexpr (ep_has_aux<EP>::value) {
+              if (mw + lane < s.M) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                  if (nc + 4 * q < s.N) {
+                    const float4 a4 = ep.aux4(mw + lane, z, nc + 4 * q);
+                    y[4 * q] = a4.x;
+                    y[4 * q + 1] = a4.y;
+                    y[4 * q + 2] = a4.z;
+                    y[4 * q + 3] = a4.w;
+                  }
+              }
+            }
             float v[32];
             if (nk > 0) {
               tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * BN + c), v);
@@ -742,7 +767,6 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + prod_warps(A
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = 0.f;
             }
-            const int nc = n0 + c;
             if (lane == 0) bulk_wait_read<0>();
             __syncwarp();
 #pragma unroll
@@ -751,8 +775,8 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + prod_warps(A
 #pragma unroll
               for (int i = 0; i < 4; ++i) cc[i] = __shfl_sync(0xffffffffu, colv[k], 4 * q + i);
               *reinterpret_cast<float4 *>(box + lane * 128 + (((q ^ lane) & 7) << 4)) =
-                  make_float4(tr(v[4 * q], cc[0]), tr(v[4 * q + 1], cc[1]), tr(v[4 * q + 2], cc[2]),
-                              tr(v[4 * q + 3], cc[3]));
+                  make_float4(tr(v[4 * q], cc[0], y[4 * q]), tr(v[4 * q + 1], cc[1], y[4 * q + 1]),
+                              tr(v[4 * q + 2], cc[2], y[4 * q + 2]), tr(v[4 * q + 3], cc[3], y[4 * q + 3]));
             }
             fence_proxy_async_smem();
             __syncwarp();
