@@ -330,11 +330,6 @@ struct GradCfg {
   static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
-// byte offset of element (row r, column c) of a [row][32] tile in the 32-byte-granule swizzle
-__device__ __forceinline__ uint32_t sw32_off(int r, int c) {
-  return (uint32_t)(r * 128 + ((((c >> 3) ^ r) & 3) << 5) + (c & 7) * 4);
-}
-
 __global__ void __launch_bounds__(320, 1)
     attn_grad_tc_kernel(const float *__restrict__ qkv, const float *__restrict__ grad, float *__restrict__ qkv_g,
                         int *err, int U, int H, int items, float koef, const __grid_constant__ CUtensorMap tmS,
@@ -347,8 +342,8 @@ __global__ void __launch_bounds__(320, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   float *V0s = reinterpret_cast<float *>(sm + C::V0), *AVs = reinterpret_cast<float *>(sm + C::AV);
-  // w1[j]: S and G rows of q-chunk j split (dV may read them); mq[j]: dK has read C's q-chunk j
-  __shared__ __align__(8) uint64_t ld1, ld2, w1[4], w2, w3, m1, mq[4], accf, qfree, wsync, drain;
+  // w1[j]: S and G rows of q-chunk j split (dV may read them); mq[h]: dK has read C's q-chunks 2h, 2h+1
+  __shared__ __align__(8) uint64_t ld1, ld2, w1[4], w2, w3, m1, mq[2], accf, qfree, wsync, drain;
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
 
@@ -360,10 +355,8 @@ __global__ void __launch_bounds__(320, 1)
   if (tid == 0) {
     mbar_init(&ld1, 1);
     mbar_init(&ld2, 1);
-    for (int j = 0; j < 4; ++j) {
-      mbar_init(&w1[j], 256);
-      mbar_init(&mq[j], 1);
-    }
+    for (int j = 0; j < 4; ++j) mbar_init(&w1[j], 256);
+    for (int j = 0; j < 2; ++j) mbar_init(&mq[j], 1);
     mbar_init(&w2, 256);
     mbar_init(&w3, 256);
     mbar_init(&m1, 1);
@@ -450,8 +443,8 @@ __global__ void __launch_bounds__(320, 1)
         __syncwarp();
       }
       if (!ok) break;
-      // dK' = C^T (G o Q), with a commit after each 32-row chunk of q so that the workers can
-      // permute the rows it no longer reads
+      // dK' = C^T (G o Q), with a commit after every second 32-row chunk of q so that the workers
+      // can permute the rows it no longer reads
       if (!mbar_wait(&w2, par, &abort_flag)) {
         if (lane == 0) fail(kErrFullWait);
         break;
@@ -468,7 +461,7 @@ __global__ void __launch_bounds__(320, 1)
             mma_tf32(tmem + 32, ah, bl, IDESC_MN, 1u);
             mma_tf32(tmem + 32, ah, bh, IDESC_MN, 1u);
           }
-          mma_commit(&mq[j]);
+          if (j & 1) mma_commit(&mq[j >> 1]);
         }
       }
       __syncwarp();
@@ -515,10 +508,26 @@ __global__ void __launch_bounds__(320, 1)
       // V0 (feature 0 of V) for every unit of the tile; zero past `units`
       if (wt < 128) V0s[wt] = wt < U ? nan0(reinterpret_cast<const float *>(sm + C::VR)[4 * wt]) : 0.f;
       // W1, per 32-row chunk j of q: split S (rows q >= units zeroed) and G, then release the chunk
-      // to dV.  Thread wt handles row 32j + wt/8 of each u-group, 16 bytes at a time.
+      // to dV.  Thread wt handles row 32j + wt/8 of each u-group, 16 bytes at a time: the same four
+      // units u of each u-group for every j (the 32-byte granule order of a row depends on q % 4
+      // only), whose V0 it keeps in registers to form its share of A[q] = sum_u S[q][u] V0[u];
+      // the eight threads of a row (consecutive lanes) then add their shares.
+      float v0r[4][4];
+      {
+        const float *vr = reinterpret_cast<const float *>(sm + C::VR);  // V[u][0..3] per row u
+        const int c = ((((wt & 7) >> 1) ^ (wt >> 3)) & 3) * 8 + (wt & 1) * 4;
+#pragma unroll
+        for (int ug = 0; ug < 4; ++ug)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int uu = 32 * ug + c + i;
+            v0r[ug][i] = uu < U ? nan0(vr[4 * uu]) : 0.f;
+          }
+      }
       for (int j = 0; j < 4; ++j) {
         const int q = 32 * j + (wt >> 3);
         const uint32_t off = 4096u * j + 16u * wt;
+        float a = 0.f;
         if (q >= U) {
 #pragma unroll
           for (int ug = 0; ug < 4; ++ug) {
@@ -526,8 +535,23 @@ __global__ void __launch_bounds__(320, 1)
             *reinterpret_cast<float4 *>(sm + C::SL + 16384u * ug + off) = make_float4(0.f, 0.f, 0.f, 0.f);
           }
         } else {
-          split_chunks<4>(sm + C::SH, sm + C::SL, off, 16384u);
+          float4 x[4];
+#pragma unroll
+          for (int ug = 0; ug < 4; ++ug) x[ug] = *reinterpret_cast<const float4 *>(sm + C::SH + 16384u * ug + off);
+#pragma unroll
+          for (int ug = 0; ug < 4; ++ug) {
+            const float4 v = make_float4(nan0(x[ug].x), nan0(x[ug].y), nan0(x[ug].z), nan0(x[ug].w));
+            store_split_full(sm + C::SH, sm + C::SL, 16384u * ug + off, v);
+            a = fmaf(v.x, v0r[ug][0], a);
+            a = fmaf(v.y, v0r[ug][1], a);
+            a = fmaf(v.z, v0r[ug][2], a);
+            a = fmaf(v.w, v0r[ug][3], a);
+          }
         }
+        a += __shfl_xor_sync(0xffffffffu, a, 1);
+        a += __shfl_xor_sync(0xffffffffu, a, 2);
+        a += __shfl_xor_sync(0xffffffffu, a, 4);
+        if ((wt & 7) == 0) AVs[q] = a;
         split_chunks<1>(sm + C::GH, sm + C::GL, off, 0u);
         fence_proxy_async_smem();
         mbar_arrive(&w1[j]);
@@ -547,33 +571,7 @@ __global__ void __launch_bounds__(320, 1)
       }
       fence_proxy_async_smem();
       mbar_arrive(&qfree);  // raw Q consumed: the loader brings raw K into QR
-      if (!worker_sync()) {  // V0 and the zeroed score rows complete before A reads them
-        fail(kErrFullWait);
-        break;
-      }
-      // A[q] = sum_u S[q][u] V0[u]: a warp per row, lanes along u (one 128-byte row per u-group)
-      {
-        float v0[4];
-#pragma unroll
-        for (int ug = 0; ug < 4; ++ug) v0[ug] = V0s[32 * ug + lane];
-        for (int q0 = warp * 4; q0 < 128; q0 += 32) {  // four rows at a time: independent reductions
-          float a[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            a[i] = 0.f;
-#pragma unroll
-            for (int ug = 0; ug < 4; ++ug)
-              a[i] = fmaf(*reinterpret_cast<const float *>(sm + C::SH + ug * 16384 + sw32_off(q0 + i, lane)), v0[ug],
-                          a[i]);
-          }
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) a[i] += __shfl_xor_sync(0xffffffffu, a[i], o);
-          if (lane < 4) AVs[q0 + lane] = lane == 0 ? a[0] : lane == 1 ? a[1] : lane == 2 ? a[2] : a[3];
-        }
-      }
-      if (!worker_sync()) {  // AVs complete before W2 reads it
+      if (!worker_sync()) {  // V0 and A complete before W2 reads them
         fail(kErrFullWait);
         break;
       }
@@ -613,17 +611,20 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int i = 0; i < 4; ++i) store_split_full(sm + C::GH, sm + C::GL, 16u * (wt + 256 * i), kv[i]);
       }
-      // W3, per 32-row chunk j of q once dK has read it: permute C's rows to the K-major swizzle.
-      // Thread wt: buffer wt/128 (hi, lo), u-group (wt/32)%4, row q = 32j + wt%32.
+      // W3, two 32-row chunks of q at a time once dK has read them: permute C's rows to the K-major
+      // swizzle.  Only the hi (full fp32) rows are read; the permuted lo rows are computed from them.
+      // Thread wt: chunk 2s + wt/128, u-group (wt/32)%4, row q = 32 * chunk + wt%32.
       bool ok = true;
-      for (int j = 0; j < 4; ++j) {
-        if (!mbar_wait(&mq[j], par, &abort_flag)) {
+      for (int st2 = 0; st2 < 2; ++st2) {
+        if (!mbar_wait(&mq[st2], par, &abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const int q = 32 * j + (wt & 31);
-        uint8_t *base = sm + ((wt & 128) ? C::SL : C::SH) + ((wt >> 5) & 3) * 16384 + q * 128;
+        const int q = 32 * (2 * st2 + (wt >> 7)) + (wt & 31);
+        const uint32_t roff = ((wt >> 5) & 3) * 16384 + q * 128;
+        uint8_t *base = sm + C::SH + roff;
+        uint8_t *lbase = sm + C::SL + roff;
         // g[j] = physical granule (j + q) % 8: the eight lanes of a shared-memory phase touch eight
         // different 16-byte bank groups although their rows are 128 bytes apart
         const int rot = q & 7;
@@ -642,7 +643,10 @@ __global__ void __launch_bounds__(320, 1)
           const int p = (i + rot) & 7;                                 // destination: K-major granule p
           const int l16 = (p ^ q) & 7;                                 // the logical granule stored there
           const int from = 2 * (((l16 >> 1) ^ q) & 3) + (l16 & 1);    // its place in the MN-major row
-          *reinterpret_cast<float4 *>(base + 16 * p) = pick((from - rot) & 7);
+          const float4 v = pick((from - rot) & 7);
+          *reinterpret_cast<float4 *>(base + 16 * p) = v;
+          *reinterpret_cast<float4 *>(lbase + 16 * p) =
+              make_float4(v.x - tf32_hi(v.x), v.y - tf32_hi(v.y), v.z - tf32_hi(v.z), v.w - tf32_hi(v.w));
         }
       }
       if (!ok) {
