@@ -269,7 +269,7 @@ static int k_mh_attention_inside_gradients(Launch &L) {
   if (!qkv || !qkv_g || !scores || !grad) return NN_ERR_BOUNDS;
   float koef = sqrtf((float)dim);
   if (koef < 1.f) koef = 1.f;
-  if (attn_tc_ok(qkv, scores, units, heads, dim) && ((uintptr_t)grad & 15) == 0 && ((uintptr_t)qkv_g & 15) == 0) {
+  if (attn_tc_ok(qkv, scores, units, heads, dim) && ((uintptr_t)grad & 15) == 0 && ((uintptr_t)qkv_g & 31) == 0) {
     cudaError_t e = attn_grad_tc(qkv, qkv_g, scores, grad, L.B, units, heads, koef, L.stream);
     if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
     L.counted();

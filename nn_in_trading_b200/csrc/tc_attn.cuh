@@ -310,9 +310,9 @@ __global__ void __launch_bounds__(448, 1)
 //   dV = S^T G,   C = S o (V0^T - A),   dK = C^T (G o Q) / koef,   dQ = G o (C K) / koef.
 // Shared memory (one item at a time, 210 KB):
 //   SH / SL  S, then C: hi / lo, [u-group (4)][q row (128)][32 u], 64 KB each
-//   GH / GL  G: hi / lo, [q row][32 d], 16 KB each; later K (dQ's B operand)
+//   GH / GL and XH / XL  two 32 KB hi / lo pairs [q row][32 d] that swap roles from item to item:
+//            one holds G (later K, dQ's B operand), the other G o Q
 //   QR       raw Q, later raw K, [row][32 d], 16 KB
-//   XH / XL  G o Q: hi / lo, 16 KB each
 //   V0, AV   128 floats each;  VR: V[u][0..3] per row (TMA), the source of V0
 // S, G, Q and K tiles use the 128-byte swizzle with 32-byte granules (MN-major operands of dV and
 // dK).  For dQ, C is the K-major operand: its rows are already where the K-major layout keeps
@@ -320,9 +320,11 @@ __global__ void __launch_bounds__(448, 1)
 // XOR q%4  ->  16-byte granules XOR q%8).  Score rows q >= units (the next sequence) are zeroed,
 // so they contribute nothing to the sums over q.
 // Overlap: dV and dK reduce over q in 8-row steps, so the workers hand S over (and take C back)
-// in four 32-row chunks of q, each with its own barrier; G o Q and A are formed while dV runs,
-// K is split while dK runs, and the next item's tiles load while this item's results are stored
-// (dQ's factor G is read from global memory, so G's buffer is free once dQ's products finish).
+// in 32-row chunks of q, each with its own barrier; G o Q and A are formed while dV runs, K is
+// split while dK runs.  The next item's V rows, Q and G load as soon as dK has read G o Q (the
+// next G goes into that pair) and K has been split out of QR, and its S in two halves as dQ
+// passes u-groups 0-1 and finishes (dQ's factor G is read from global memory, so the epilogue
+// needs no shared tile).
 struct GradCfg {
   static constexpr uint32_t SH = 0, SL = 65536, GH = 131072, GL = 147456, QR = 163840, XH = 180224, XL = 196608;
   static constexpr uint32_t V0 = 212992, AV = V0 + 512, VR = AV + 512, END = VR + 2048;
@@ -342,8 +344,9 @@ __global__ void __launch_bounds__(320, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   float *V0s = reinterpret_cast<float *>(sm + C::V0), *AVs = reinterpret_cast<float *>(sm + C::AV);
-  // w1[j]: S and G rows of q-chunk j split (dV may read them); mq[h]: dK has read C's q-chunks 2h, 2h+1
-  __shared__ __align__(8) uint64_t ld1, ld2, w1[4], w2, w3, m1, mq[2], accf, qfree, wsync, drain;
+  // w1[j]: S and G rows of q-chunk j split (dV may read them); mq[h]: dK has read C's q-chunks 2h,
+  // 2h+1; accq: dQ has read u-groups 0-1 of C; kfree: the workers have split K out of QR
+  __shared__ __align__(8) uint64_t ld1, ld2, w1[4], w2, w3, m1, mq[2], accq, accf, qfree, kfree, wsync, drain;
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
 
@@ -360,8 +363,10 @@ __global__ void __launch_bounds__(320, 1)
     mbar_init(&w2, 256);
     mbar_init(&w3, 256);
     mbar_init(&m1, 1);
+    mbar_init(&accq, 1);
     mbar_init(&accf, 1);
     mbar_init(&qfree, 256);
+    mbar_init(&kfree, 256);
     mbar_init(&wsync, 256);
     mbar_init(&drain, 1);
     abort_flag = 0;
@@ -380,28 +385,40 @@ __global__ void __launch_bounds__(320, 1)
 
   if (warp == 9) {
     // ------------------------------------------------------------ loader
+    // Item n+1's tiles load while item n still runs: its V0 rows, Q and G once item n's dK
+    // products have read G o Q (G and G o Q swap buffers from item to item) and its workers have
+    // split K out of QR; its S u-groups 0-1 once item n's dQ products have passed them, 2-3 once
+    // they are done.  One ld1 phase per item counts all of these copies.
     if (lane == 0) {
       int n = 0, issued1 = 0, issued2 = 0;
-      for (int t = blockIdx.x; t < items && !abort_flag; t += gridDim.x, ++n) {
+      auto load_vqg = [&](int t, int nn) {
         const int b = t / H, h = t % H;
-        // the previous item's products have read S, G/K and Q/K (its epilogue reads only tensor
-        // memory and global memory), so its tiles may be overwritten
-        if (n > 0 && !mbar_wait(&accf, (n - 1) & 1, &abort_flag)) {
-          fail(kErrEmptyWait);
-          break;
-        }
+        const uint32_t gbuf = (nn & 1) ? C::XH : C::GH;
         mbar_arrive_expect_tx(&ld1, 65536u + 16384u + 16384u + 2048u);
         tma_load_3d(sm + C::VR, &tmV0, (2 * H + h) * D, b * U, 0, &ld1);
-        ++issued1;
-        for (int ug = 0; ug < 4; ++ug)
-          for (int qc = 0; qc < 4; ++qc)
-            tma_load_3d(sm + C::SH + ug * 16384 + qc * 4096, &tmS, 32 * ug, h, b * U + 32 * qc, &ld1);
         for (int qc = 0; qc < 4; ++qc) {
-          tma_load_3d(sm + C::GH + qc * 4096, &tmG, h * D, b * U + 32 * qc, 0, &ld1);
+          tma_load_3d(sm + gbuf + qc * 4096, &tmG, h * D, b * U + 32 * qc, 0, &ld1);
           tma_load_3d(sm + C::QR + qc * 4096, &tmQKV, h * D, b * U + 32 * qc, 0, &ld1);
         }
+      };
+      auto load_s = [&](int t, int ug0) {
+        const int b = t / H, h = t % H;
+        for (int ug = ug0; ug < ug0 + 2; ++ug)
+          for (int qc = 0; qc < 4; ++qc)
+            tma_load_3d(sm + C::SH + ug * 16384 + qc * 4096, &tmS, 32 * ug, h, b * U + 32 * qc, &ld1);
+      };
+      int t = blockIdx.x;
+      if (t < items) {
+        load_vqg(t, 0);
+        load_s(t, 0);
+        load_s(t, 2);
+        ++issued1;
+      }
+      for (; t < items && !abort_flag; t += gridDim.x, ++n) {
+        const int b = t / H, h = t % H;
+        const uint32_t par = n & 1;
         // raw K into QR once the workers have consumed Q
-        if (!mbar_wait(&qfree, n & 1, &abort_flag)) {
+        if (!mbar_wait(&qfree, par, &abort_flag)) {
           fail(kErrEmptyWait);
           break;
         }
@@ -409,6 +426,24 @@ __global__ void __launch_bounds__(320, 1)
         ++issued2;
         for (int uc = 0; uc < 4; ++uc)
           tma_load_3d(sm + C::QR + uc * 4096, &tmQKV, (H + h) * D, b * U + 32 * uc, 0, &ld2);
+        const int tn = t + gridDim.x;
+        if (tn >= items) continue;
+        if (!mbar_wait(&mq[1], par, &abort_flag) || !mbar_wait(&kfree, par, &abort_flag)) {
+          fail(kErrEmptyWait);
+          break;
+        }
+        load_vqg(tn, n + 1);
+        ++issued1;
+        if (!mbar_wait(&accq, par, &abort_flag)) {
+          fail(kErrEmptyWait);
+          break;
+        }
+        load_s(tn, 0);
+        if (!mbar_wait(&accf, par, &abort_flag)) {
+          fail(kErrEmptyWait);
+          break;
+        }
+        load_s(tn, 2);
       }
       // wait for the last copies into shared memory before exiting
       if (issued1 > 0 && !mbar_wait_drain(&ld1, (issued1 - 1) & 1) && !abort_flag) fail(kErrFullWait);
@@ -416,10 +451,22 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else if (warp == 8) {
     // ------------------------------------------------------------ MMA issue
+    // Operand descriptors from one shared base (address / 16) plus compile-time tile offsets: the
+    // issuing lane shares its sub-partition with two busy worker warps, so every issue instruction
+    // saved shortens the MMA chain.  MN-major S / C, G (later K) and G o Q tiles: 1024 bytes per
+    // 8 rows of q; K-major C: 16384 bytes per u-group, 32 bytes per 8-wide k step.
+    const uint32_t b16 = smem_u32(sm) >> 4;
+    auto Sm = [&](uint32_t base, int s) { return desc_at<16384u, 512u, 1u>(b16 + (base >> 4) + 64u * s); };
+    auto Tm = [&](uint32_t base, int s) { return desc_at<4096u, 512u, 1u>(b16 + (base >> 4) + 64u * s); };
+    auto Sk = [&](uint32_t base, int s) {
+      return desc_at<16u, 1024u, 2u>(b16 + (base >> 4) + 1024u * (s >> 2) + 2u * (s & 3));
+    };
     int n = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < items && ok && !abort_flag; t += gridDim.x, ++n) {
       const uint32_t par = n & 1;
+      // G (later K) and G o Q swap their 32 KB buffers from item to item
+      const uint32_t gbuf = par ? C::XH : C::GH, xbuf = par ? C::GH : C::XH;
       // dV = S^T G, k-steps s (q rows 8s..8s+7) issued as the workers release each 32-row chunk
       for (int j = 0; j < 4 && ok; ++j) {
         if (!mbar_wait(&w1[j], par, &abort_flag)) {
@@ -429,14 +476,12 @@ __global__ void __launch_bounds__(320, 1)
         }
         tc_fence_after();
         if (lane == 0) {
-          for (int s = 4 * j; s < 4 * j + 4; ++s) {
-            const uint64_t ah = smem_desc(smem_u32(sm + C::SH) + 1024u * s, 16384u, 512u, 1u);
-            const uint64_t al = smem_desc(smem_u32(sm + C::SL) + 1024u * s, 16384u, 512u, 1u);
-            const uint64_t bh = smem_desc(smem_u32(sm + C::GH) + 1024u * s, 4096u, 512u, 1u);
-            const uint64_t bl = smem_desc(smem_u32(sm + C::GL) + 1024u * s, 4096u, 512u, 1u);
-            mma_tf32(tmem, al, bh, IDESC_MN, s != 0 ? 1u : 0u);
-            mma_tf32(tmem, ah, bl, IDESC_MN, 1u);
-            mma_tf32(tmem, ah, bh, IDESC_MN, 1u);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int s = 4 * j + i;
+            mma_tf32(tmem, Sm(C::SL, s), Tm(gbuf, s), IDESC_MN, s != 0 ? 1u : 0u);
+            mma_tf32(tmem, Sm(C::SH, s), Tm(gbuf + 16384u, s), IDESC_MN, 1u);
+            mma_tf32(tmem, Sm(C::SH, s), Tm(gbuf, s), IDESC_MN, 1u);
           }
           if (j == 3) mma_commit(&m1);
         }
@@ -452,14 +497,12 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_after();
       if (lane == 0) {
         for (int j = 0; j < 4; ++j) {
-          for (int s = 4 * j; s < 4 * j + 4; ++s) {
-            const uint64_t ah = smem_desc(smem_u32(sm + C::SH) + 1024u * s, 16384u, 512u, 1u);
-            const uint64_t al = smem_desc(smem_u32(sm + C::SL) + 1024u * s, 16384u, 512u, 1u);
-            const uint64_t bh = smem_desc(smem_u32(sm + C::XH) + 1024u * s, 4096u, 512u, 1u);
-            const uint64_t bl = smem_desc(smem_u32(sm + C::XL) + 1024u * s, 4096u, 512u, 1u);
-            mma_tf32(tmem + 32, al, bh, IDESC_MN, s != 0 ? 1u : 0u);
-            mma_tf32(tmem + 32, ah, bl, IDESC_MN, 1u);
-            mma_tf32(tmem + 32, ah, bh, IDESC_MN, 1u);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int s = 4 * j + i;
+            mma_tf32(tmem + 32, Sm(C::SL, s), Tm(xbuf, s), IDESC_MN, s != 0 ? 1u : 0u);
+            mma_tf32(tmem + 32, Sm(C::SH, s), Tm(xbuf + 16384u, s), IDESC_MN, 1u);
+            mma_tf32(tmem + 32, Sm(C::SH, s), Tm(xbuf, s), IDESC_MN, 1u);
           }
           if (j & 1) mma_commit(&mq[j >> 1]);
         }
@@ -472,15 +515,12 @@ __global__ void __launch_bounds__(320, 1)
       }
       tc_fence_after();
       if (lane == 0) {
+#pragma unroll
         for (int s = 0; s < 16; ++s) {
-          const uint32_t ao = 16384u * (s >> 2) + 32u * (s & 3);
-          const uint64_t ah = smem_desc(smem_u32(sm + C::SH) + ao, 16u, 1024u, 2u);
-          const uint64_t al = smem_desc(smem_u32(sm + C::SL) + ao, 16u, 1024u, 2u);
-          const uint64_t bh = smem_desc(smem_u32(sm + C::GH) + 1024u * s, 4096u, 512u, 1u);
-          const uint64_t bl = smem_desc(smem_u32(sm + C::GL) + 1024u * s, 4096u, 512u, 1u);
-          mma_tf32(tmem + 64, al, bh, IDESC_KM, s != 0 ? 1u : 0u);
-          mma_tf32(tmem + 64, ah, bl, IDESC_KM, 1u);
-          mma_tf32(tmem + 64, ah, bh, IDESC_KM, 1u);
+          mma_tf32(tmem + 64, Sk(C::SL, s), Tm(gbuf, s), IDESC_KM, s != 0 ? 1u : 0u);
+          mma_tf32(tmem + 64, Sk(C::SH, s), Tm(gbuf + 16384u, s), IDESC_KM, 1u);
+          mma_tf32(tmem + 64, Sk(C::SH, s), Tm(gbuf, s), IDESC_KM, 1u);
+          if (s == 7) mma_commit(&accq);  // u-groups 0-1 of C read: the next item's S may land there
         }
         mma_commit(&accf);
       }
@@ -501,6 +541,8 @@ __global__ void __launch_bounds__(320, 1)
     for (int t = blockIdx.x; t < items && !abort_flag; t += gridDim.x, ++n) {
       const int b = t / H, h = t % H;
       const uint32_t par = n & 1;
+      // G (later K) and G o Q swap their 32 KB hi / lo buffers from item to item
+      const uint32_t gbuf = par ? C::XH : C::GH, xbuf = par ? C::GH : C::XH;
       if (!mbar_wait(&ld1, par, &abort_flag)) {
         fail(kErrFullWait);
         break;
@@ -552,7 +594,7 @@ __global__ void __launch_bounds__(320, 1)
         a += __shfl_xor_sync(0xffffffffu, a, 2);
         a += __shfl_xor_sync(0xffffffffu, a, 4);
         if ((wt & 7) == 0) AVs[q] = a;
-        split_chunks<1>(sm + C::GH, sm + C::GL, off, 0u);
+        split_chunks<1>(sm + gbuf, sm + gbuf + 16384u, off, 0u);
         fence_proxy_async_smem();
         mbar_arrive(&w1[j]);
       }
@@ -561,12 +603,12 @@ __global__ void __launch_bounds__(320, 1)
         float4 g[4], qv[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          g[i] = *reinterpret_cast<const float4 *>(sm + C::GH + 16u * (wt + 256 * i));
+          g[i] = *reinterpret_cast<const float4 *>(sm + gbuf + 16u * (wt + 256 * i));
           qv[i] = *reinterpret_cast<const float4 *>(sm + C::QR + 16u * (wt + 256 * i));
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i)
-          store_split_full(sm + C::XH, sm + C::XL, 16u * (wt + 256 * i),
+          store_split_full(sm + xbuf, sm + xbuf + 16384u, 16u * (wt + 256 * i),
                            make_float4(g[i].x * qv[i].x, g[i].y * qv[i].y, g[i].z * qv[i].z, g[i].w * qv[i].w));
       }
       fence_proxy_async_smem();
@@ -609,8 +651,9 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int i = 0; i < 4; ++i) kv[i] = *reinterpret_cast<const float4 *>(sm + C::QR + 16u * (wt + 256 * i));
 #pragma unroll
-        for (int i = 0; i < 4; ++i) store_split_full(sm + C::GH, sm + C::GL, 16u * (wt + 256 * i), kv[i]);
+        for (int i = 0; i < 4; ++i) store_split_full(sm + gbuf, sm + gbuf + 16384u, 16u * (wt + 256 * i), kv[i]);
       }
+      mbar_arrive(&kfree);  // QR (raw K) and VR read: the loader may bring the next item's Q and V rows
       // W3, two 32-row chunks of q at a time once dK has read them: permute C's rows to the K-major
       // swizzle.  Only the hi (full fp32) rows are read; the permuted lo rows are computed from them.
       // Thread wt: chunk 2s + wt/128, u-group (wt/32)%4, row q = 32 * chunk + wt%32.
@@ -656,7 +699,7 @@ __global__ void __launch_bounds__(320, 1)
       fence_proxy_async_smem();
       mbar_arrive(&w3);
       // epilogue: rows r of tensor-memory lane quarter w % 4; warps 0-3 store dV and the first 16
-      // features of dK, warps 4-7 dQ and the last 16 of dK.  The G row dQ needs is loaded (from L2:
+      // features of dK, warps 4-7 dQ and the last 16 of dK, 32 bytes per store.  The G row dQ needs is loaded (from L2:
       // TMA brought it in) before the wait for the products, so its latency overlaps them.
       const int r = (warp & 3) * 32 + lane;
       float4 gq[8];
@@ -671,37 +714,49 @@ __global__ void __launch_bounds__(320, 1)
       }
       tc_fence_after();
       const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-      float *grow = qkv_g + (size_t)(b * U + r) * rs;
-      float4 *dk = reinterpret_cast<float4 *>(grow + (size_t)(H + h) * D);
+      float *grow = qkv_g + (size_t)(b * U + r) * rs;  // 32-byte aligned: 3*H*D floats per row
+      float *dk = grow + (size_t)(H + h) * D;
       if (warp < 4) {
         float v[32], k[32];
         tmem_ld32(tl + 0, v);
         tmem_ld32(tl + 32, k);
         if (r < U) {
-          float4 *dv = reinterpret_cast<float4 *>(grow + (size_t)(2 * H + h) * D);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) dv[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          float *dv = grow + (size_t)(2 * H + h) * D;
 #pragma unroll
           for (int j = 0; j < 4; ++j)
-            dk[j] = make_float4(k[4 * j] * inv_koef, k[4 * j + 1] * inv_koef, k[4 * j + 2] * inv_koef,
-                                k[4 * j + 3] * inv_koef);
+            st_global_v8(dv + 8 * j, v[8 * j], v[8 * j + 1], v[8 * j + 2], v[8 * j + 3], v[8 * j + 4], v[8 * j + 5],
+                         v[8 * j + 6], v[8 * j + 7]);
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+            st_global_v8(dk + 8 * j, k[8 * j] * inv_koef, k[8 * j + 1] * inv_koef, k[8 * j + 2] * inv_koef,
+                         k[8 * j + 3] * inv_koef, k[8 * j + 4] * inv_koef, k[8 * j + 5] * inv_koef,
+                         k[8 * j + 6] * inv_koef, k[8 * j + 7] * inv_koef);
         }
       } else {
         float v[32], k[32];
         tmem_ld32(tl + 64, v);
         tmem_ld32(tl + 32, k);
         if (r < U) {
-          float4 *dq = reinterpret_cast<float4 *>(grow + (size_t)h * D);
+          float *dq = grow + (size_t)h * D;
+          float gf[32];
 #pragma unroll
-          for (int l16 = 0; l16 < 8; ++l16) {  // features 4*l16 .. 4*l16+3
-            const float4 gv = gq[l16];
-            dq[l16] = make_float4(nan0(gv.x) * v[4 * l16] * inv_koef, nan0(gv.y) * v[4 * l16 + 1] * inv_koef,
-                                  nan0(gv.z) * v[4 * l16 + 2] * inv_koef, nan0(gv.w) * v[4 * l16 + 3] * inv_koef);
+          for (int l16 = 0; l16 < 8; ++l16) {
+            gf[4 * l16] = nan0(gq[l16].x);
+            gf[4 * l16 + 1] = nan0(gq[l16].y);
+            gf[4 * l16 + 2] = nan0(gq[l16].z);
+            gf[4 * l16 + 3] = nan0(gq[l16].w);
           }
 #pragma unroll
-          for (int j = 4; j < 8; ++j)
-            dk[j] = make_float4(k[4 * j] * inv_koef, k[4 * j + 1] * inv_koef, k[4 * j + 2] * inv_koef,
-                                k[4 * j + 3] * inv_koef);
+          for (int j = 0; j < 4; ++j)
+            st_global_v8(dq + 8 * j, gf[8 * j] * v[8 * j] * inv_koef, gf[8 * j + 1] * v[8 * j + 1] * inv_koef,
+                         gf[8 * j + 2] * v[8 * j + 2] * inv_koef, gf[8 * j + 3] * v[8 * j + 3] * inv_koef,
+                         gf[8 * j + 4] * v[8 * j + 4] * inv_koef, gf[8 * j + 5] * v[8 * j + 5] * inv_koef,
+                         gf[8 * j + 6] * v[8 * j + 6] * inv_koef, gf[8 * j + 7] * v[8 * j + 7] * inv_koef);
+#pragma unroll
+          for (int j = 2; j < 4; ++j)
+            st_global_v8(dk + 8 * j, k[8 * j] * inv_koef, k[8 * j + 1] * inv_koef, k[8 * j + 2] * inv_koef,
+                         k[8 * j + 3] * inv_koef, k[8 * j + 4] * inv_koef, k[8 * j + 5] * inv_koef,
+                         k[8 * j + 6] * inv_koef, k[8 * j + 7] * inv_koef);
         }
       }
       tc_fence_before();
@@ -785,7 +840,8 @@ inline cudaError_t attn_tc(const float *qkv, const float *scores, float *out, in
   return cudaGetLastError();
 }
 
-// MHAttentionInsideGradients on the tensor cores (same applicability as attn_tc_ok; `grad` aligned).
+// MHAttentionInsideGradients on the tensor cores (same applicability as attn_tc_ok; `grad` 16-byte and
+// `qkv_g` 32-byte aligned).
 inline cudaError_t attn_grad_tc(const float *qkv, float *qkv_g, const float *scores, const float *grad, int B, int U,
                                 int H, float koef, cudaStream_t st) {
   const int D = 32;

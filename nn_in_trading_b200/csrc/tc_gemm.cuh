@@ -170,6 +170,15 @@ __host__ __device__ constexpr uint32_t instr_desc_tf32(int M, int N, bool a_mn, 
          ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// smem_desc with the strides and layout as compile-time constants and the address already divided
+// by 16: the 64-bit descriptor is one 32-bit add away from a shared base, so a loop of MMAs keeps
+// one register for all its operand tiles instead of a 64-bit descriptor per tile.
+template <uint32_t LBO, uint32_t SBO, uint32_t LAYOUT>
+__device__ __forceinline__ uint64_t desc_at(uint32_t addr16) {
+  constexpr uint32_t lo = ((LBO >> 4) & 0x3FFFu) << 16;
+  constexpr uint32_t hi = ((SBO >> 4) & 0x3FFFu) | (1u << 14) | ((LAYOUT & 7u) << 29);
+  return ((uint64_t)hi << 32) | (uint64_t)((addr16 & 0x3FFFu) | lo);
+}
 __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                          uint32_t accumulate) {
   asm volatile(
@@ -350,6 +359,15 @@ __device__ __forceinline__ void store_split_full(uint8_t *hi, uint8_t *lo, uint3
   *reinterpret_cast<float4 *>(hi + off) = v;
   *reinterpret_cast<float4 *>(lo + off) =
       make_float4(v.x - tf32_hi(v.x), v.y - tf32_hi(v.y), v.z - tf32_hi(v.z), v.w - tf32_hi(v.w));
+}
+
+// 256-bit global store of 8 consecutive floats (32-byte aligned): a whole 32-byte sector per lane,
+// where two 16-byte stores would each write half of one.
+__device__ __forceinline__ void st_global_v8(float *p, float a0, float a1, float a2, float a3, float a4, float a5,
+                                             float a6, float a7) {
+  asm volatile("st.global.v8.f32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "f"(a0), "f"(a1), "f"(a2),
+               "f"(a3), "f"(a4), "f"(a5), "f"(a6), "f"(a7)
+               : "memory");
 }
 
 // 3-d tiled TMA store of one box from shared memory into the tensor (bulk-group completion).
