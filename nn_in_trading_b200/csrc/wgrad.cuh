@@ -28,9 +28,15 @@ struct GradSrc {
   int splits;
   size_t stride;
   float scale;
+  // rows of `ncol` gradient entries stored `ld` floats apart (ld == ncol: dense, the default)
+  int ld = 0, ncol = 0;
+  __device__ __forceinline__ size_t at(size_t i) const {
+    return ld == ncol ? i : (i / (size_t)ncol) * (size_t)ld + i % (size_t)ncol;
+  }
   __device__ __forceinline__ float operator()(size_t idx) const {
+    const size_t j = at(idx);
     float s = 0.f;
-    for (int k = 0; k < splits; ++k) s += p[k * stride + idx];
+    for (int k = 0; k < splits; ++k) s += p[k * stride + j];
     return s * scale;
   }
 };
@@ -64,6 +70,20 @@ struct PartialStoreLd {
 #pragma unroll
     for (int j = 0; j < R; ++j)
       if (mask >> j & 1u) *reinterpret_cast<float4 *>(p + rb[j] + n) = v[j];
+  }
+};
+
+// PartialStoreLd through TMA stores: rows padded to a multiple of 4 floats (16-byte row stride), the
+// split as the tensor's outer coordinate.
+struct PartialStoreTma : PartialStoreLd {
+  static constexpr bool kTmaStore = true;
+  template <class F>
+  __device__ __forceinline__ void transform(F &&f) const {
+    f([](float x, float, float) { return x; });
+  }
+  __device__ __forceinline__ int zc(int z, int split) const { return split * nz + z; }
+  bool out_map(CUtensorMap *tm, int rows, int cols, int outer) const {
+    return make_tmap(tm, p, ldp, (long long)M * ldp, cols, rows, outer, 32, false);
   }
 };
 
@@ -114,12 +134,16 @@ inline int wgrad_fast(Launch &L, const float *A, long long lda, const float *X, 
   int kchunk = ((rows + splits - 1) / splits + gran - 1) / gran * gran;
   splits = (rows + kchunk - 1) / kchunk;
   if (splits < 1) splits = 1;
-  const int ldp = N + 1;
+  FastShape fs{M, N, rows, 1, splits, kchunk, A, lda, 0, X, ldx, 0};
+  const bool tc = tc_path(fs), transposed = tc && M < 128 && N >= 128;
+  // partial rows: N + 1 entries, padded to a multiple of 4 floats when the GEMM's epilogue writes
+  // them with TMA stores (the tensor-core product with the bias column folded in)
+  const int ldp = (tc && !transposed) ? (N + 1 + 3) / 4 * 4 : N + 1;
   size_t per = (size_t)M * ldp;
   float *part = L.scratch(0, per * splits);
   if (!part) return NN_ERR_CUDA;
-  FastShape fs{M, N, rows, 1, splits, kchunk, A, lda, 0, X, ldx, 0};
-  if (tc_path(fs) && M < 128 && N >= 128) {
+  out->ld = out->ncol = 0;
+  if (transposed) {
     // few outputs, many inputs: the transposed product X^T A^T fills the 128-row tiles with the
     // inputs instead of padding the outputs; the bias column is a separate column sum of A
     FastShape ft{N, M, rows, 1, splits, kchunk, X, ldx, 0, A, lda, 0};
@@ -129,13 +153,15 @@ inline int wgrad_fast(Launch &L, const float *A, long long lda, const float *X, 
     colsum_rows_kernel<<<dim3((M + 31) / 32, splits), dim3(32, 32), 0, L.stream>>>(part, A, M, rows, lda, kchunk, ldp,
                                                                                   N);
     NN_CHECK_LAUNCH(L);
-  } else if (tc_path(fs)) {
+  } else if (tc) {
     // the bias input (1) is column N of X: one GEMM writes all N + 1 gradient columns
     fs.N = N + 1;
     fs.ones_col = N;
-    cudaError_t e = tcgemm<true, true>(fs, PartialStoreLd{part, M, ldp, 1}, L.stream, device_status());
+    cudaError_t e = tcgemm<true, true>(fs, PartialStoreTma{{part, M, ldp, 1}}, L.stream, device_status());
     if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
     L.counted();
+    out->ld = ldp;
+    out->ncol = N + 1;
   } else {
     cudaError_t e = sgemm_fast<true, true>(fs, PartialStoreLd{part, M, ldp, 1}, L.stream);
     if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
