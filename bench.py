@@ -1,16 +1,21 @@
-"""Benchmark: fwd+bwd+Adam training throughput of the attention encoder (samples/s).
+"""Benchmark: fwd+bwd+Adam training throughput (samples/s) through libnn_b200.so.
 
-Workload: CNeuronMLMHAttentionOCL encoder, 4 layers, 120 bars x 64 features, 8 heads x key 32,
-FF 64->256(GELU)->64(LReLU), batch 256 independent sequences per GPU, fp32, MSE vs N(0,1)
-targets, Adam; synthetic seeded N(0,1) data.  A step = forward + backward + Adam of one batch,
-replayed from command lists through libnn_b200.so.
+Default workload (mlmh_encoder): CNeuronMLMHAttentionOCL encoder, 4 layers, 120 bars x 64
+features, 8 heads x key 32, FF 64->256(GELU)->64(LReLU), batch 256 independent sequences per GPU,
+fp32, MSE vs N(0,1) targets, Adam; synthetic seeded N(0,1) data.  A step = forward + backward +
+Adam of one batch, replayed from command lists.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch B]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload mlmh_encoder|dense_mlp|lstm_stack|patchtst] [--batch B]
 
-N > 1 (torchrun, one process per GPU): weak scaling, every rank trains its own 256 sequences and
-the weight gradients are averaged with one NCCL allreduce per step before the updates.
+Other workloads: dense_mlp (240-500-500-3 MLP, batch 1, 1000 sequential online steps), lstm_stack
+(2 LSTM layers, hidden 256, 1024 series, one bar per step, a sample = one series over 240 bars),
+patchtst (BatchNorm + Conv1D patching + 3 attention layers + head + RevIN, batch 512).
+
+N > 1 (torchrun, one process per GPU): weak scaling, every rank trains its own batch and the
+weight gradients are averaged with one NCCL allreduce per step before the updates.
 `--impl reference` times the reference's own NeuroNet.cl kernels compiled for the host CPU
-(oracle/_ref) on the same workload, one sequence per step, on rank 0 only.
+(oracle/_ref) on a bounded sample of the same workload, on rank 0 only.
 """
 from __future__ import annotations
 
@@ -29,7 +34,6 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-WORKLOAD = "mlmh_encoder_4x120x64_h8k32_ff256"
 METRIC = "fwd+bwd+Adam samples/sec"
 UNIT = "samples/s"
 
@@ -98,19 +102,27 @@ class ClockSampler:
 
 
 # --------------------------------------------------- algorithmic work model
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch, from one ncu capture
-# of the batch-256 workload:  ncu --set full --clock-control none -k regex:attn_grad -s 4 -c 1
-#   python bench.py --steps 3 --warmup 3 --no-cpu-baseline
-# Keyed by the reference kernel; scaled to other batches by the sequences a launch processes.
-NCU_TRAFFIC = {"MHAttentionInsideGradients": (311.70e6, 256)}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one call of each reference kernel
+# (every CUDA launch the call makes, weight-image packing included), from one single-pass ncu
+# capture of a whole training step of the batch-256 encoder:
+#   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum
+#       --clock-control none -s 471 -c 157 --csv python bench.py --steps 3 --warmup 3 --no-cpu-baseline
+# Keyed by workload and reference kernel; scaled to other batches by the samples a call processes.
+NCU_TRAFFIC = {"mlmh_encoder": {k: (v * 1e6, 256) for k, v in {
+    "MHAttentionInsideGradients": 309.32, "UpdateWeightsConvAdam": 64.96, "CalcHiddenGradientConv": 55.54,
+    "FeedForwardConv": 27.99, "MHAttentionScore": 122.99, "MHAttentionOut": 163.37, "SumMatrix": 15.73,
+    "Normalize": 7.87, "NormalizeWeights": 0.11, "CalcOutputGradient": 15.73}.items()}}
 
 
-def op_work(op, B):
-    """(flops, bytes) a launch must do at minimum: every operand read once, every result written once."""
+def op_work(op):
+    """(flops, bytes) a launch must do at minimum: every operand read once, every result written once.
+    B is the launch's own batch (nn_set_batch), so a layer that views its input as per-channel
+    sequences counts those sequences."""
     k = op.kernel
     name = k.name
     a = k.values
     g = op.gsize
+    B = getattr(k, "b", 1)
     f4 = 4
     if name == "FeedForwardConv":
         units, wout, var = g[0], g[1], g[2] if len(g) > 2 else 1
@@ -149,7 +161,283 @@ def op_work(op, B):
         return 0.0, f4 * 2 * g[0] * a[1]
     if name == "CalcOutputGradient":
         return 0.0, f4 * 3 * B * g[0]
+    if name == "FeedForward":  # y[out] = act(W [out][in+1] . [x, 1])
+        out, n_in = g[0], a[3]
+        return 2.0 * B * out * (n_in + 1), f4 * (out * (n_in + 1) + B * n_in + B * out)
+    if name == "CalcHiddenGradient":  # g_in[in] = Deact(W^T g_out) at x_in
+        n_in, out = g[0], a[4]
+        return 2.0 * B * out * n_in, f4 * (out * (n_in + 1) + B * out + 2 * B * n_in)
+    if name == "UpdateWeightsAdam":  # w, m, v read and written; g_out and x read
+        out, cols = g[0], g[1]
+        return 2.0 * B * out * cols, f4 * (6 * out * cols + B * out + B * (cols - 1))
+    if name == "LSTM_FeedForward":  # gate pre-activations of rows g+id (H+3 distinct rows), cell update
+        H, V, n_in = g[0], (g[2] if len(g) > 2 else 1) * B, a[1]
+        ws = n_in + H + 1
+        return (2.0 * V * (H + 3) * ws,
+                f4 * ((H + 3) * ws + V * n_in + 2 * V * H + V * 4 * H + 2 * V * H + V * H))
+    if name == "LSTM_ConcatenatedGradient":
+        H, V = g[0], (g[1] if len(g) > 1 else 1) * B
+        return 0.0, f4 * (V * H + 2 * V * H + 4 * V * H + 4 * V * H)
+    if name == "LSTM_HiddenGradient":  # dx = a W[:, H:], dW = a^T [h; x] summed over the series
+        H, V, n_in = g[0], (g[1] if len(g) > 1 else 1) * B, a[8]
+        ws = H + n_in + 1
+        return (2.0 * V * 4 * H * n_in + 2.0 * V * 4 * H * (H + n_in),
+                f4 * (V * 4 * H + 4 * H * ws + V * (H + n_in) + V * H + V * n_in + 4 * H * ws))
+    if name == "BatchFeedForward":
+        n = g[0]
+        return 0.0, f4 * (2 * B * n + 2 * 9 * n)
+    if name == "CalcHiddenGradientBatch":
+        n = g[0]
+        return 0.0, f4 * (3 * B * n + 9 * n)
+    if name in ("RevInFeedForward", "RevInHiddenGraddient"):
+        n = g[0]
+        return 0.0, f4 * ((2 if name == "RevInFeedForward" else 3) * B * n)
+    if name == "DeActivation":
+        return 0.0, f4 * 3 * B * g[0]
     return 0.0, 0.0
+
+
+# ------------------------------------------------------------- workloads
+class Workload:
+    """One training configuration: how to build it through the library, its synthetic data, what a
+    sample is, and a bounded CPU sample of the same network through the reference's own kernels."""
+
+    key = ""
+    name = ""
+    default_batch = 1
+    default_steps = 30
+    recordable = True
+
+    def __init__(self, batch):
+        self.B = batch
+
+    def samples_per_step(self) -> float:
+        return float(self.B)
+
+    def build(self, ctx, dp):
+        raise NotImplementedError
+
+    def data(self, pool, seed):
+        """([pool][n_in], [pool][n_out]) float32 arrays: inputs and targets of `pool` steps."""
+        raise NotImplementedError
+
+    def config(self, world) -> dict:
+        raise NotImplementedError
+
+    def oracle_net(self, O, K, batch):
+        raise NotImplementedError
+
+    def ref_data(self, pool):
+        return self.data(pool, 7)
+
+    def ref_sample_desc(self, n, el, backend) -> str:
+        raise NotImplementedError
+
+    def ref_samples_per_step(self, batch) -> float:
+        return float(batch)
+
+
+class MLMHWorkload(Workload):
+    key = "mlmh_encoder"
+    name = "mlmh_encoder_4x120x64_h8k32_ff256"
+    default_batch = 256
+
+    def __init__(self, batch):
+        super().__init__(batch)
+        from nn_in_trading_b200 import configs as C
+        self.C, self.spec = C, C.MLMHSpec()
+
+    def build(self, ctx, dp):
+        return self.C.build_mlmh(ctx, self.spec, self.B, self.C.mlmh_weights(self.spec), dp=dp)
+
+    def data(self, pool, seed):
+        xs, ts = self.C.mlmh_data(self.spec, self.B, pool, seed=seed)
+        return xs.reshape(pool, -1), ts.reshape(pool, -1)
+
+    def config(self, world):
+        s = self.spec
+        return {"workload": self.name, "global_batch": self.B * world, "per_gpu_batch": self.B, "seq_len": s.units,
+                "embed": s.window, "heads": s.heads, "key": s.dk, "layers": s.layers, "sample": "one sequence",
+                "parallelism": f"dp{world}",
+                "l2": "no flush: every step streams >1 GB of activations and scores, well above the 126 MB L2"}
+
+    def oracle_net(self, O, K, batch):
+        s = self.spec
+        inp = O.ODense(s.window * s.units, K.NONE, batch, 0)
+        enc = O.OMLMH(s.window, s.dk, s.heads, s.units, s.layers, s.activation, batch)
+        for i, ws in enumerate(self.C.mlmh_weights(s)):
+            for name, w in ws.items():
+                enc.w[i][name][0][:] = w
+        return O.ONet([inp, enc])
+
+    def ref_data(self, pool):
+        xs, ts = self.C.mlmh_data(self.spec, 1, pool, seed=7)
+        return xs.reshape(pool, -1), ts.reshape(pool, -1)
+
+    def ref_sample_desc(self, n, el, backend):
+        return (f"{n} training steps of one 120x64 sequence (fwd+bwd+Adam of all 4 layers) through the "
+                f"{backend}, {el:.1f} s")
+
+
+class DenseWorkload(Workload):
+    key = "dense_mlp"
+    name = "dense_mlp_240_500tanh_500sigmoid_3"
+    default_batch = 1
+    default_steps = 1000
+
+    def __init__(self, batch):
+        super().__init__(batch)
+        from nn_in_trading_b200 import configs as C
+        self.C, self.spec = C, C.DenseSpec()
+
+    def build(self, ctx, dp):
+        return self.C.build_dense(ctx, self.spec, self.B, self.C.dense_weights(self.spec), dp=dp)
+
+    def data(self, pool, seed):
+        xs, ts = self.C.dense_data(self.spec, pool, self.B, seed=seed)
+        return xs.reshape(pool, -1), ts.reshape(pool, -1)
+
+    def config(self, world):
+        return {"workload": self.name, "global_batch": self.B * world, "per_gpu_batch": self.B,
+                "sample": "one online training step (batch 1, sequential)", "parallelism":
+                f"dp{world}" if world > 1 else "replicas only: the online steps are sequential",
+                "l2": "no flush: the whole state (4.5 MB) is L2-resident, as in the reference's online loop"}
+
+    def oracle_net(self, O, K, batch):
+        s = self.spec
+        layers = []
+        for i, (n, a) in enumerate(zip(s.sizes, s.acts)):
+            outputs = s.sizes[i + 1] if i + 1 < len(s.sizes) else 0
+            layers.append(O.ODense(n, a, batch, outputs))
+        for layer, w in zip(layers, self.C.dense_weights(s)):
+            layer.weights[:] = w
+        return O.ONet(layers)
+
+    def ref_data(self, pool):
+        xs, ts = self.C.dense_data(self.spec, pool, 1, seed=7)
+        return xs.reshape(pool, -1), ts.reshape(pool, -1)
+
+    def ref_sample_desc(self, n, el, backend):
+        return f"{n} online steps of the 240-500-500-3 MLP (fwd+bwd+Adam) through the {backend}, {el:.1f} s"
+
+
+class LSTMWorkload(Workload):
+    """A step is one bar for every series (the reference trains recurrent layers bar by bar); a sample
+    is one series over the full 240-bar window, so samples/step = series / 240."""
+
+    key = "lstm_stack"
+    name = "lstm_stack_in64_h256_x2_seq240"
+    default_batch = 1024
+    default_steps = 240
+
+    def __init__(self, batch):
+        super().__init__(batch)
+        from nn_in_trading_b200 import configs as C
+        self.C, self.spec = C, C.LSTMSpec(series=batch)
+
+    def samples_per_step(self):
+        return self.B / self.spec.seq
+
+    def build(self, ctx, dp):
+        return self.C.build_lstm(ctx, self.spec, self.C.lstm_weights(self.spec), dp=dp)
+
+    def data(self, pool, seed):
+        d = self.C.lstm_data(self.spec, steps=pool, seed=seed)
+        return d[:-1].reshape(pool, -1), d[1:].reshape(pool, -1)
+
+    def config(self, world):
+        s = self.spec
+        return {"workload": self.name, "global_batch": self.B * world, "per_gpu_batch": self.B,
+                "seq_len": s.seq, "inputs": s.inputs, "hidden": s.hidden, "layers": s.layers,
+                "sample": "one series over the 240-bar window (240 bar steps)", "parallelism": f"dp{world}",
+                "l2": "no flush: the 5 MB of weights stay in L2 between bars as in any recurrent loop; "
+                      "the per-bar gate and gradient tensors (4-5 MB each) are written and read once"}
+
+    def oracle_net(self, O, K, batch):
+        s = self.spec
+        w = self.C.lstm_weights(s)
+        layers = [O.ODense(s.inputs * batch, K.NONE, 1, 0)]
+        ins = s.inputs
+        for l in range(s.layers):
+            L = O.OLSTM(s.hidden, ins, batch, 1)
+            L.lstm_w[:] = w[f"lstm{l}"]
+            layers.append(L)
+            ins = s.hidden
+        head = O.OConv(s.hidden, s.hidden, s.inputs, batch, 1, K.NONE, 1)
+        head.conv_w[:] = w["head"]
+        layers.append(head)
+        return O.ONet(layers)
+
+    def ref_data(self, pool):
+        import dataclasses
+        d = self.C.lstm_data(dataclasses.replace(self.spec, series=REF_LSTM_SERIES), steps=pool, seed=7)
+        return d[:-1].reshape(pool, -1), d[1:].reshape(pool, -1)
+
+    def ref_samples_per_step(self, batch):
+        return batch / self.spec.seq
+
+    def ref_sample_desc(self, n, el, backend):
+        return (f"{n} bar steps of {REF_LSTM_SERIES} series (fwd+bwd+Adam of both LSTM layers and the head) "
+                f"through the {backend}, {el:.1f} s; samples = series x bars / 240")
+
+
+class PatchWorkload(Workload):
+    """The BatchNorm layer's update is gated on its sample count, so the step runs eagerly."""
+
+    key = "patchtst"
+    name = "patchtst_32ch_512bars_p16s8_e128_h8k16_x3_ff512_h96"
+    default_batch = 512
+    default_steps = 10
+    recordable = False
+
+    def __init__(self, batch):
+        super().__init__(batch)
+        from nn_in_trading_b200 import configs as C
+        self.C, self.spec = C, C.PatchSpec()
+
+    def build(self, ctx, dp):
+        return self.C.build_patch(ctx, self.spec, self.B, self.C.patch_weights(self.spec), dp=dp)
+
+    def data(self, pool, seed):
+        xs, ts = self.C.patch_data(self.spec, self.B, pool, seed=seed)
+        return xs.reshape(pool, -1), ts.reshape(pool, -1)
+
+    def config(self, world):
+        s = self.spec
+        return {"workload": self.name, "global_batch": self.B * world, "per_gpu_batch": self.B,
+                "channels": s.channels, "bars": s.bars, "patches": s.patches, "embed": s.embed, "heads": s.heads,
+                "key": s.dk, "layers": s.layers, "horizon": s.horizon,
+                "sample": "one 32-channel x 512-bar window", "parallelism": f"dp{world}",
+                "l2": "no flush: every step streams tens of GB of activations, far above the 126 MB L2"}
+
+    def oracle_net(self, O, K, batch):
+        s = self.spec
+        w = self.C.patch_weights(s)
+        P, E, Cc = s.patches, s.embed, s.channels
+        inp = O.ODense(Cc * s.bars, K.NONE, batch, 0)
+        norm = O.OBatchNorm(Cc * s.bars, s.norm_batch, batch)
+        conv = O.OConv(s.patch, s.stride, E, P, Cc, K.NONE, batch)
+        conv.conv_w[:] = w["conv"]
+        enc = O.OMLMH(E, s.dk, s.heads, P, s.layers, K.NONE, batch * Cc)
+        for i, ws in enumerate(w["encoder"]):
+            for name, arr in ws.items():
+                enc.w[i][name][0][:] = arr
+        head = O.OConv(P * E, P * E, s.horizon, Cc, 1, K.NONE, batch)
+        head.conv_w[:] = w["head"]
+        denorm = O.ORevIN(Cc * s.horizon, norm, batch)
+        return O.ONet([inp, norm, conv, enc, head, denorm])
+
+    def ref_data(self, pool):
+        xs, ts = self.C.patch_data(self.spec, 1, pool, seed=7)
+        return xs.reshape(pool, -1), ts.reshape(pool, -1)
+
+    def ref_sample_desc(self, n, el, backend):
+        return f"{n} training steps of one 32x512 window (fwd+bwd+Adam) through the {backend}, {el:.1f} s"
+
+
+REF_LSTM_SERIES = 4
+REF_CAP_SECONDS = 90.0  # the reference arm stops after K steps or this long, whichever comes first
+WORKLOADS = {w.key: w for w in (MLMHWorkload, DenseWorkload, LSTMWorkload, PatchWorkload)}
 
 
 # ------------------------------------------------------------- our arm
@@ -158,32 +446,31 @@ def run_ours(args, rank, world, local_rank):
     import torch.distributed as dist
 
     from nn_in_trading_b200 import Context
-    from nn_in_trading_b200 import configs as C
 
     ctx = Context(local_rank)
     torch.cuda.set_device(local_rank)
-    spec = C.MLMHSpec()
-    B = args.batch
-    net = C.build_mlmh(ctx, spec, B, C.mlmh_weights(spec), dp=world > 1)
+    wl = WORKLOADS[args.workload](args.batch)
+    net = wl.build(ctx, world > 1)
     if world > 1:
         from nn_in_trading_b200 import dp
         dp.join_dp(ctx, rank, world)
 
-    n_in = spec.window * spec.units
     pool = 4
-    xs, ts = C.mlmh_data(spec, B, pool, seed=100 + rank)
-    resident_x = [ctx.buffer(B * n_in) for _ in range(pool)]
-    resident_t = [ctx.buffer(B * n_in) for _ in range(pool)]
+    xs, ts = wl.data(pool, 100 + rank)
+    n_in, n_out = xs.shape[1], ts.shape[1]
+    resident_x = [ctx.buffer(n_in) for _ in range(pool)]
+    resident_t = [ctx.buffer(n_out) for _ in range(pool)]
     for i in range(pool):
         ctx.write(resident_x[i], xs[i])
         ctx.write(resident_t[i], ts[i])
     inp = net.layers[0].output
 
     def load(i):
-        ctx.copy(inp, resident_x[i % pool], B * n_in)
-        ctx.copy(net.target, resident_t[i % pool], B * n_in)
+        ctx.copy(inp, resident_x[i % pool], n_in)
+        ctx.copy(net.target, resident_t[i % pool], n_out)
 
-    net.capture()
+    if wl.recordable:
+        net.capture()
     stream = torch.cuda.ExternalStream(ctx.stream(), device=local_rank)
 
     def barrier():
@@ -216,20 +503,23 @@ def run_ours(args, rank, world, local_rank):
         t = torch.tensor([ms], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_max = float(t.item())
-    value = world * B * args.steps / (ms_max / 1000.0)
+    per_step = wl.samples_per_step()
+    value = world * per_step * args.steps / (ms_max / 1000.0)
 
     # ---- e2e through the public API with host buffers (pinned) ----------
-    hx = torch.from_numpy(xs.reshape(pool, -1)).pin_memory()
-    ht = torch.from_numpy(ts.reshape(pool, -1)).pin_memory()
-    hy = torch.empty(B * n_in, dtype=torch.float32).pin_memory()
+    hx = torch.from_numpy(xs).pin_memory()
+    ht = torch.from_numpy(ts).pin_memory()
+    out_layer = net.layers[-1]
+    n_y = out_layer.neurons * out_layer.batch
+    hy = torch.empty(n_y, dtype=torch.float32).pin_memory()
     lib = ctx.lib
-    out_h = net.layers[-1].output
+    out_h = out_layer.output
     e2e_steps = max(3, args.steps // 2)
     for i in range(2):
-        lib.nn_buffer_write(inp, hx[i % pool].data_ptr(), 0, B * n_in)
-        lib.nn_buffer_write(net.target, ht[i % pool].data_ptr(), 0, B * n_in)
+        lib.nn_buffer_write(inp, hx[i % pool].data_ptr(), 0, n_in)
+        lib.nn_buffer_write(net.target, ht[i % pool].data_ptr(), 0, n_out)
         net.step()
-        lib.nn_buffer_read(out_h, hy.data_ptr(), 0, B * n_in)
+        lib.nn_buffer_read(out_h, hy.data_ptr(), 0, n_y)
     barrier()
     # Every step: H2D of its inputs and targets, the step, a blocking D2H of its output and the host
     # MSE of that output (CNet::backPropOCL reads the output back).  The host work of step i runs
@@ -238,48 +528,38 @@ def run_ours(args, rank, world, local_rank):
     losses = []
 
     def enqueue(i):
-        ctx._check(lib.nn_buffer_write(inp, hx[i % pool].data_ptr(), 0, B * n_in))
-        ctx._check(lib.nn_buffer_write(net.target, ht[i % pool].data_ptr(), 0, B * n_in))
+        ctx._check(lib.nn_buffer_write(inp, hx[i % pool].data_ptr(), 0, n_in))
+        ctx._check(lib.nn_buffer_write(net.target, ht[i % pool].data_ptr(), 0, n_out))
         net.step()
 
     enqueue(0)
     for i in range(e2e_steps):
-        ctx._check(lib.nn_buffer_read(out_h, hy.data_ptr(), 0, B * n_in))
+        ctx._check(lib.nn_buffer_read(out_h, hy.data_ptr(), 0, n_y))
         if i + 1 < e2e_steps:
             enqueue(i + 1)  # hy is written again only by the next iteration's read
-        d = hy.numpy() - ts[i % pool].reshape(-1)
+        d = hy.numpy() - ts[i % pool]
         losses.append(float(np.dot(d, d)) / d.size)  # host MSE of step i's output
     e2e_s = time.perf_counter() - t0
     if world > 1:
         t = torch.tensor([e2e_s], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e = world * B * e2e_steps / e2e_s
+    e2e = world * per_step * e2e_steps / e2e_s
 
     # ---- per-kernel profile pass (CUDA events between launches) --------
-    prof = profile_ops(ctx, net, stream, B, load, torch)
+    prof = profile_ops(ctx, net, stream, wl.B, load, torch)
     result = None
     if rank == 0:
         peaks = read_peaks()
-        top = prof["top"]
-        roof = {"bound": "hbm", "kernel": top["name"], "achieved": top["gbs"], "peak": peaks["hbm_gbs"],
-                "unit": "GB/s", "frac": top["gbs"] / peaks["hbm_gbs"],
-                "traffic": (NCU_TRAFFIC[top["name"]][0] * B / NCU_TRAFFIC[top["name"]][1]
-                            if top["name"] in NCU_TRAFFIC else None),
-                "algorithmic_bytes_per_launch": top["bytes_per_launch"],
-                "avg_launch_us": top["avg_us"], "peak_source": peaks["source"]}
         result = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "global_batch": B * world, "per_gpu_batch": B, "seq_len": spec.units,
-                       "embed": spec.window, "heads": spec.heads, "key": spec.dk, "layers": spec.layers,
-                       "parallelism": f"dp{world}",
-                       "l2": "no flush: every step streams >1 GB of activations and scores, well above the 126 MB L2"},
-            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": 2 * B * n_in * 4,
-                    "d2h_bytes_per_step": B * n_in * 4, "mse_last": losses[-1]},
+            "config": wl.config(world),
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": (n_in + n_out) * 4,
+                    "d2h_bytes_per_step": n_y * 4, "mse_last": losses[-1]},
             "gpu_launches": launches,
-            "roofline": roof,
+            "roofline": roofline(prof["top"], peaks, wl),
             "kernel_shares": prof["shares"],
             "clocks": clocks.summary(),
         }
@@ -287,6 +567,29 @@ def run_ours(args, rank, world, local_rank):
         ctx.dp_shutdown()
     ctx.close()
     return result
+
+
+def roofline(top, peaks, wl):
+    """The dominant kernel against HBM when its algorithmic intensity is below the ridge of a 3xTF32
+    tensor rate, else against that tensor rate (measured bf16 / 2 for TF32, / 3 for three MMAs)."""
+    tensor_peak = peaks["bf16_tflops"] / 6.0
+    ridge = tensor_peak * 1e12 / (peaks["hbm_gbs"] * 1e9)
+    intensity = top["flops_per_launch"] / max(top["bytes_per_launch"], 1.0)
+    traffic = None
+    measured = NCU_TRAFFIC.get(wl.key, {})
+    if top["name"] in measured:
+        t_bytes, t_batch = measured[top["name"]]
+        traffic = t_bytes * wl.B / t_batch
+    if top["bytes_per_launch"] > 0 and intensity < ridge:
+        return {"bound": "hbm", "kernel": top["name"], "achieved": top["gbs"], "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": top["gbs"] / peaks["hbm_gbs"], "traffic": traffic,
+                "algorithmic_bytes_per_launch": top["bytes_per_launch"], "avg_launch_us": top["avg_us"],
+                "peak_source": peaks["source"]}
+    return {"bound": "tensor", "kernel": top["name"], "achieved": top["tflops"], "peak": tensor_peak,
+            "unit": "TFLOP/s", "frac": top["tflops"] / tensor_peak, "traffic": traffic,
+            "algorithmic_flops_per_launch": top["flops_per_launch"], "avg_launch_us": top["avg_us"],
+            "peak_source": peaks["source"] + " bf16 / 6 (TF32 runs at half the bf16 rate; 3xTF32 issues three "
+                                             "MMAs per fp32 product)"}
 
 
 def profile_ops(ctx, net, stream, B, load, torch):
@@ -305,7 +608,7 @@ def profile_ops(ctx, net, stream, B, load, torch):
     total = 0.0
     for i, op in enumerate(ops):
         t = evs[i].elapsed_time(evs[i + 1])
-        fl, by = op_work(op, B)
+        fl, by = op_work(op)
         d = per.setdefault(op.kernel.name, {"ms": 0.0, "n": 0, "bytes": 0.0, "flops": 0.0})
         d["ms"] += t
         d["n"] += 1
@@ -317,7 +620,7 @@ def profile_ops(ctx, net, stream, B, load, torch):
     avg_s = d["ms"] / d["n"] / 1000.0
     bpl = d["bytes"] / d["n"]
     top = {"name": name, "avg_us": avg_s * 1e6, "bytes_per_launch": bpl, "gbs": bpl / avg_s / 1e9,
-           "tflops": d["flops"] / d["n"] / avg_s / 1e12}
+           "flops_per_launch": d["flops"] / d["n"], "tflops": d["flops"] / d["n"] / avg_s / 1e12}
     return {"shares": shares, "top": top, "step_ms_eager": total}
 
 
@@ -332,24 +635,18 @@ def read_peaks():
 
 
 # ------------------------------------------------------ CPU baseline arm
-def reference_sample(seconds: float, steps: int | None = None, warmup: int = 1):
+def reference_sample(wl, seconds: float, steps: int | None = None, warmup: int = 1):
     """The reference's NeuroNet.cl kernels compiled for the host (oracle/_ref), OpenMP over all host
-    cores, sequenced as the MQL5 host does for the encoder, one sequence per training step.
-    Returns (samples/s, kind, cores, description)."""
-    from nn_in_trading_b200 import configs as C
+    cores, sequenced as the MQL5 host does, on a bounded sample of the workload (one sample per step;
+    REF_LSTM_SERIES series per bar step for the LSTM stack).  Returns (samples/s, kind, cores, desc)."""
     from oracle import kernels as K
     from oracle import nets as O
     from oracle.ref import RefKernels
     kind = "reference" if RefKernels.available() else "port"
     O.use_backend("reference" if kind == "reference" else "numpy")
-    spec = C.MLMHSpec()
-    inp = O.ODense(spec.window * spec.units, K.NONE, 1, 0)
-    enc = O.OMLMH(spec.window, spec.dk, spec.heads, spec.units, spec.layers, spec.activation, 1)
-    for i, ws in enumerate(C.mlmh_weights(spec)):
-        for name, w in ws.items():
-            enc.w[i][name][0][:] = w
-    net = O.ONet([inp, enc])
-    xs, ts = C.mlmh_data(spec, 1, 4, seed=7)
+    batch = REF_LSTM_SERIES if isinstance(wl, LSTMWorkload) else 1
+    net = wl.oracle_net(O, K, batch)
+    xs, ts = wl.ref_data(4)
     for i in range(warmup):
         net.step(xs[i % 4], ts[i % 4])
     n = 0
@@ -358,24 +655,25 @@ def reference_sample(seconds: float, steps: int | None = None, warmup: int = 1):
         net.step(xs[n % 4], ts[n % 4])
         n += 1
         el = time.perf_counter() - t0
-        if (steps is not None and n >= steps) or (steps is None and el >= seconds):
+        if (steps is not None and (n >= steps or el >= REF_CAP_SECONDS)) or (steps is None and el >= seconds):
             break
     cores = RefKernels().max_threads() if kind == "reference" else 1
-    desc = (f"{n} training steps of one 120x64 sequence (fwd+bwd+Adam of all 4 layers) through the "
-            f"{'reference NeuroNet.cl kernels compiled for the CPU (OpenMP)' if kind == 'reference' else 'numpy port'}"
-            f", {el:.1f} s")
-    return n / el, kind, cores, desc
+    backend = ("reference NeuroNet.cl kernels compiled for the CPU (OpenMP)" if kind == "reference"
+               else "numpy port")
+    return n * wl.ref_samples_per_step(batch) / el, kind, cores, wl.ref_sample_desc(n, el, backend)
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return None
-    value, kind, cores, desc = reference_sample(0.0, steps=max(1, args.steps), warmup=max(0, min(args.warmup, 1)))
-    spec_cfg = {"workload": WORKLOAD, "global_batch": 1, "per_gpu_batch": 1, "seq_len": 120, "embed": 64,
-                "heads": 8, "key": 32, "layers": 4, "parallelism": "host cores"}
+    wl = WORKLOADS[args.workload](args.batch)
+    value, kind, cores, desc = reference_sample(wl, 0.0, steps=max(1, args.steps),
+                                                warmup=max(0, min(args.warmup, 1)))
+    cfg = dict(wl.config(1))
+    cfg.update({"global_batch": 1, "per_gpu_batch": 1, "parallelism": "host cores"})
     return {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic", "config": spec_cfg, "impl": "reference",
+            "dtype": "f32", "data": "synthetic", "config": cfg, "impl": "reference",
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": kind, "sample": desc},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
@@ -383,13 +681,19 @@ def run_reference(args, rank, world):
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mlmh_encoder")
+    ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    wl_cls = WORKLOADS[args.workload]
+    if args.steps is None:
+        args.steps = wl_cls.default_steps
+    if args.batch is None:
+        args.batch = wl_cls.default_batch
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     rank = env_int("RANK", 0)
@@ -407,7 +711,7 @@ def main() -> int:
             res = run_ours(args, rank, world, local_rank)
             if rank == 0 and res is not None:
                 if world == 1 and not args.no_cpu_baseline:
-                    v, kind, cores, desc = reference_sample(args.cpu_seconds)
+                    v, kind, cores, desc = reference_sample(wl_cls(args.batch), args.cpu_seconds)
                     res["cpu_baseline"] = {"value": v, "unit": UNIT, "cores": cores, "kind": kind, "sample": desc}
                 else:
                     res["cpu_baseline"] = None

@@ -232,6 +232,7 @@ class Kernel:
         self.ctx, self.id, self.name = ctx, kid, name
         self.sig = SIGNATURES[name]
         self.values = {}  # last value bound to each argument index
+        self.b = 1  # batch set with nn_set_batch
 
     def set(self, idx: int, value) -> "Kernel":
         t = self.sig[idx]
@@ -253,6 +254,7 @@ class Kernel:
 
     def batch(self, b: int) -> "Kernel":
         self.ctx._check(self.ctx.lib.nn_set_batch(self.id, int(b)))
+        self.b = int(b)
         return self
 
     def run(self, global_size, local_size=None) -> None:
