@@ -12,6 +12,7 @@
 #include "nn_device.cuh"
 #include "nn_internal.h"
 #include "wgrad.cuh"
+#include "epi_dense.cuh"
 
 namespace nn {
 
@@ -108,56 +109,6 @@ struct FFLoadW {  // B(k, n) = W[n][k]
   int ld;
   __device__ __forceinline__ float operator()(int k, int n, int) const { return nan0(w[(size_t)n * ld + k]); }
 };
-struct FFEpi {
-  const float *w;
-  float *y;
-  int ld, inputs, outputs, act;
-  __device__ __forceinline__ void operator()(int m, int n, int, int, float acc) const {
-    y[(size_t)m * outputs + n] = activate(acc + nan0(w[(size_t)n * ld + inputs]), act);
-  }
-  __device__ __forceinline__ long long row(int m, int, int) const { return (long long)m * outputs; }
-  __device__ __forceinline__ float col(int n, int) const { return nan0(w[(size_t)n * ld + inputs]); }
-  template <int R>
-  __device__ __forceinline__ void put_rows(const long long (&rb)[R], int n, const float (&v)[R], float bias,
-                                           unsigned mask) const {
-    act_dispatch(act, [&](auto A) {
-#pragma unroll
-      for (int j = 0; j < R; ++j)
-        if (mask >> j & 1u) y[rb[j] + n] = activate(v[j] + bias, decltype(A)::value);
-    });
-  }
-  __host__ __device__ bool aligned4() const { return outputs % 4 == 0 && ((uintptr_t)y & 15) == 0; }
-  __device__ __forceinline__ float4 col4(int n, int z) const {
-    return make_float4(col(n, z), col(n + 1, z), col(n + 2, z), col(n + 3, z));
-  }
-  template <int R>
-  __device__ __forceinline__ void put_rows4(const long long (&rb)[R], int n, const float4 (&v)[R], float4 b,
-                                            unsigned mask) const {
-    act_dispatch(act, [&](auto A) {
-      constexpr int a = decltype(A)::value;
-#pragma unroll
-      for (int j = 0; j < R; ++j)
-        if (mask >> j & 1u)
-          *reinterpret_cast<float4 *>(y + rb[j] + n) = make_float4(
-              activate(v[j].x + b.x, a), activate(v[j].y + b.y, a), activate(v[j].z + b.z, a),
-              activate(v[j].w + b.w, a));
-    });
-  }
-};
-
-// FFEpi with the output written by TMA stores on the tensor-core path (checked with tma_store_ok).
-struct FFEpiTma : FFEpi {
-  static constexpr bool kTmaStore = true;
-  template <class F>
-  __device__ __forceinline__ void transform(F &&f) const {
-    act_dispatch(act, [&](auto A) { f([](float x, float b, float) { return activate(x + b, decltype(A)::value); }); });
-  }
-  __device__ __forceinline__ int zc(int z, int) const { return z; }
-  bool out_map(CUtensorMap *tm, int M, int N, int nz) const {
-    return make_tmap(tm, y, outputs, 0, N, M, nz, 32, false);
-  }
-};
-
 __global__ void ff_flags_kernel(const float *w, const float *x, const float *y, float *flags, int inputs,
                                 int outputs, int B) {
   size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
@@ -228,19 +179,39 @@ static int k_calc_output_gradient(Launch &L) {
 
 // ----------------------------------------------------- CalcHiddenGradient
 // NeuroNet.cl:547-613.  ig[b,i] = Deactivation(sum_k nan0(w[k,i]) nan0(g[b,k]), o[b,i], act)
-// Small batches: CTA of 8 warps per 32 columns; warps split the k range.
+// Small batches: CTA of 16 warps per 32 columns; warps split the k range, four rows of W in flight
+// per warp (each thread still sums its k in ascending order).
+constexpr int kChgWarps = 16;
 template <int MAXB>
-__global__ void chg_cols_kernel(const float *__restrict__ w, const float *__restrict__ g, const float *__restrict__ o,
-                                float *__restrict__ ig, int inputs, int outputs, int B, int act) {
-  __shared__ float part[8][MAXB][33];
+__global__ void __launch_bounds__(kChgWarps * 32) chg_cols_kernel(const float *__restrict__ w,
+                                                                  const float *__restrict__ g,
+                                                                  const float *__restrict__ o, float *__restrict__ ig,
+                                                                  int inputs, int outputs, int B, int act) {
+  __shared__ float part[kChgWarps][MAXB][33];
   int col = blockIdx.x * 32 + (threadIdx.x & 31);
   int wv = threadIdx.x >> 5;
   float s[MAXB];
 #pragma unroll
   for (int b = 0; b < MAXB; ++b) s[b] = 0.f;
   if (col < inputs) {
-    for (int k = wv; k < outputs; k += 8) {
-      float wk = nan0(w[(size_t)k * (inputs + 1) + col]);
+    const size_t ld = (size_t)inputs + 1;
+    int k = wv;
+    for (; k + 3 * kChgWarps < outputs; k += 4 * kChgWarps) {
+      float wk[4], gk[4][MAXB];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        wk[u] = w[(size_t)(k + u * kChgWarps) * ld + col];
+#pragma unroll
+        for (int b = 0; b < MAXB; ++b) gk[u][b] = b < B ? g[(size_t)b * outputs + k + u * kChgWarps] : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int b = 0; b < MAXB; ++b)
+          if (b < B) s[b] += nan0(wk[u]) * nan0(gk[u][b]);
+    }
+    for (; k < outputs; k += kChgWarps) {
+      float wk = nan0(w[(size_t)k * ld + col]);
 #pragma unroll
       for (int b = 0; b < MAXB; ++b)
         if (b < B) s[b] += wk * nan0(g[(size_t)b * outputs + k]);
@@ -252,7 +223,7 @@ __global__ void chg_cols_kernel(const float *__restrict__ w, const float *__rest
   if (wv < MAXB && wv < B && col < inputs) {
     float t = 0.f;
 #pragma unroll
-    for (int r = 0; r < 8; ++r) t += part[r][wv][threadIdx.x & 31];
+    for (int r = 0; r < kChgWarps; ++r) t += part[r][wv][threadIdx.x & 31];
     size_t idx = (size_t)wv * inputs + col;
     ig[idx] = deactivate(t, o[idx], act);
   }
@@ -341,7 +312,7 @@ static int k_calc_hidden_gradient(Launch &L) {
   float *ig = L.buf(3, (size_t)L.B * inputs);
   if (!w || !g || !o || !ig) return NN_ERR_BOUNDS;
   if (L.B <= 4) {
-    chg_cols_kernel<4><<<ceil_div(inputs, 32), 256, 0, L.stream>>>(w, g, o, ig, inputs, outputs, L.B, act);
+    chg_cols_kernel<4><<<ceil_div(inputs, 32), kChgWarps * 32, 0, L.stream>>>(w, g, o, ig, inputs, outputs, L.B, act);
     NN_CHECK_LAUNCH(L);
     return NN_OK;
   }

@@ -22,6 +22,7 @@
 #include "nn_device.cuh"
 #include "nn_internal.h"
 #include "wgrad.cuh"
+#include "epi_dense.cuh"
 
 namespace nn {
 
@@ -83,6 +84,50 @@ static int lstm_shape(Launch &L, int *H, int *V) {
   return NN_OK;
 }
 
+// Tensor-core forward.  Gate g of neuron id reads weight row g+id, so only rows 0..H+2 are ever
+// used: one GEMM gives every pre-activation, P[v][r] = [h(t-1) | x](v) . W[r][0:H+in] + W[r][H+in]
+// for r < H+4 (row H+3 pads the row stride to a multiple of 4), and a fused kernel applies the gate
+// activations and the cell update.  The packed operand keeps exactly the inputs the reference's
+// float4 input loop reads: input j belongs to group i = j - j%4, read when (unsigned)(H-i) > 4
+// or, in the tail loop that runs otherwise, when j < H.
+__global__ void lstm_pack_hx_kernel(const float *__restrict__ h, const float *__restrict__ x,
+                                    float *__restrict__ opnd, int H, int in, int V) {
+  const size_t cols = (size_t)H + in;
+  size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (t >= (size_t)V * cols) return;
+  size_t v = t / cols;
+  int c = (int)(t % cols);
+  float val;
+  if (c < H) {
+    val = h[v * H + c];
+  } else {
+    int j = c - H, i = j - (j & 3);
+    val = ((unsigned)(H - i) > 4u || j < H) ? x[v * in + j] : 0.f;
+  }
+  opnd[t] = val;
+}
+
+__global__ void lstm_gates_cell_kernel(const float *__restrict__ P, int ldp, float *__restrict__ cat,
+                                       float *__restrict__ mem, float *__restrict__ out, int H, int V) {
+  size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (t >= (size_t)V * H) return;
+  int id = (int)(t % H);
+  size_t v = t / H;
+  const float *p = P + v * ldp + id;
+  const float f = activate(p[0], ACT_SIGMOID), ig = activate(p[1], ACT_SIGMOID);
+  const float og = activate(p[2], ACT_SIGMOID), nc = activate(p[3], ACT_TANH);
+  float *c = cat + v * 4 * H + id;
+  c[0] = f;
+  c[H] = ig;
+  c[2 * H] = og;
+  c[3 * H] = nc;
+  float m = mem[t];
+  mem[t + (size_t)V * H] = m;
+  m = nan0(m * f + ig * nc);
+  mem[t] = m;
+  out[t] = nan0(og * activate(m, ACT_TANH));
+}
+
 static int k_lstm_feed_forward(Launch &L) {
   int H = (int)L.nd.g[0];
   int V = (L.nd.dims > 2 ? (int)L.nd.g[2] : 1) * L.B;
@@ -99,6 +144,24 @@ static int k_lstm_feed_forward(Launch &L) {
   float *w = L.buf(2, (size_t)(H + 3) * ws);
   float *cat = L.buf(3, (size_t)V * 4 * H), *mem = L.buf(4, (size_t)2 * V * H), *out = L.buf(5, (size_t)V * H);
   if (!x || !w || !cat || !mem || !out) return NN_ERR_BOUNDS;
+  const int ldp = H + 4;
+  if (H % 4 == 0 && xneed <= in && L.floats(2) >= (size_t)ldp * ws) {
+    const size_t nop = (size_t)V * (H + in);
+    float *opnd = L.scratch(1, nop + (size_t)V * ldp);
+    if (!opnd) return NN_ERR_CUDA;
+    float *P = opnd + nop;  // 16-byte aligned: H + in is a multiple of 4
+    lstm_pack_hx_kernel<<<grid1d(nop, 256), 256, 0, L.stream>>>(out, x, opnd, H, in, V);
+    NN_CHECK_LAUNCH(L);
+    FastShape fs{V, ldp, H + in, 1, 1, 0, opnd, (long long)H + in, 0, w, ws, 0};
+    cudaError_t e = tma_store_ok(P, ldp, 0, 1, ldp)
+                        ? gemm_f32_wb<false, false>(L, fs, FFEpiTma{{w, P, ws, H + in, ldp, ACT_NONE}})
+                        : gemm_f32_wb<false, false>(L, fs, FFEpi{w, P, ws, H + in, ldp, ACT_NONE});
+    if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
+    L.counted();
+    lstm_gates_cell_kernel<<<grid1d((size_t)V * H, 256), 256, 0, L.stream>>>(P, ldp, cat, mem, out, H, V);
+    NN_CHECK_LAUNCH(L);
+    return NN_OK;
+  }
   lstm_gates_kernel<<<grid1d((size_t)V * 4 * H, 256), 256, 0, L.stream>>>(x, w, out, cat, H, in, V);
   NN_CHECK_LAUNCH(L);
   lstm_cell_kernel<<<grid1d((size_t)V * H, 256), 256, 0, L.stream>>>(cat, mem, out, H, V);

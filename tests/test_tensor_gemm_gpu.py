@@ -132,3 +132,21 @@ def test_lstm_hidden_gradient(ctx, H, ins, V):
     K.launch(case.kernel, case.gsize, case.lsize, args)
     for i in (1, 2):
         check_close(f"{case.name} arg{i}", got[i], args[i], before[i])
+
+
+# (H, inputs, V): tensor-core GEMM (>= 64 series), more inputs than cells (the reference's input loop
+# skips inputs H..H+3), the SIMT GEMM of a small product, and H not a multiple of 4 (per-gate kernel).
+@pytest.mark.parametrize("H,ins,V", [(64, 64, 300), (32, 64, 600), (256, 64, 96), (16, 32, 8), (6, 8, 5)])
+def test_lstm_feed_forward(ctx, H, ins, V):
+    ws = H + ins + 1
+    case = Case(f"LSTM_FeedForward/{H}-{ins}-{V}", "LSTM_FeedForward",
+                [A(V * ins), ins, A(4 * H * ws, "uniform", 1 / np.sqrt(H + ins)), A(V * 4 * H, "zeros"),
+                 A(2 * V * H), A(V * H, "uniform", 1.0)], (H, 4, V), (1, 4, 1))
+    args = prepare_inputs(case, 7100 + H + V)
+    before = [a.copy() if isinstance(a, np.ndarray) else None for a in args]
+    got = run_on_gpu(ctx, case.kernel, [a.copy() if isinstance(a, np.ndarray) else a for a in args], case.gsize,
+                     case.lsize)
+    ctx.finish()
+    K.launch(case.kernel, case.gsize, case.lsize, args)
+    for i in (3, 4, 5):
+        check_close(f"{case.name} arg{i}", got[i], args[i], before[i])
