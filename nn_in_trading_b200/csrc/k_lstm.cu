@@ -227,17 +227,36 @@ __global__ void lstm_hg_prep_kernel(const float *__restrict__ cg, float *__restr
   }
 }
 
-// bias row sums: col0 of row i+1 = sum_v (i < 3H ? cg(1-cg) : 1-cg^2), for i < rows
-__global__ void lstm_bias_kernel(const float *__restrict__ cg, float *__restrict__ wg, int H, int V, int ws,
-                                 int rows) {
-  int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= rows) return;
+// bias row sums: col0 of row i+1 = sum_v (i < 3H ? cg(1-cg) : 1-cg^2), for i < rows.  Block of
+// 32 gate columns x 32 series lanes; each lane sums its series in order, then the 32 lane sums.
+__global__ void __launch_bounds__(1024) lstm_bias_kernel(const float *__restrict__ cg, float *__restrict__ wg, int H,
+                                                         int V, int ws, int rows) {
+  __shared__ float part[32][33];
+  const int i = blockIdx.x * 32 + threadIdx.x;
   float s = 0.f;
-  for (int v = 0; v < V; ++v) {
-    float c = cg[(size_t)v * 4 * H + i];
-    s += i < 3 * H ? c * (1.f - c) : 1.f - c * c;
+  if (i < rows) {
+    const bool sig = i < 3 * H;
+    for (int v = threadIdx.y; v < V; v += 32) {
+      float c = cg[(size_t)v * 4 * H + i];
+      s += sig ? c * (1.f - c) : 1.f - c * c;
+    }
   }
-  wg[(size_t)(i + 1) * ws] = s;
+  part[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y != 0 || i >= rows) return;
+  float t = 0.f;
+#pragma unroll 8
+  for (int r = 0; r < 32; ++r) t += part[r][threadIdx.x];
+  wg[(size_t)(i + 1) * ws] = t;
+}
+
+// weight-gradient rows from split-K partials: wg[g][i] = sum_s part[s][g][i] for i < N (the last
+// column of each (H+in+1)-float row is not a gradient the reference writes)
+__global__ void lstm_wg_reduce_kernel(float *__restrict__ wg, GradSrc src, int rows, int N, int ws) {
+  const size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (t >= (size_t)rows * N) return;
+  const size_t g = t / N, i = t % N;
+  wg[g * ws + i] = src(t);
 }
 
 struct StoreStrided {
@@ -287,6 +306,16 @@ struct StoreInputGrad {
   }
 };
 
+// Split-K count for a product of `tiles` 128x128 output tiles over a reduction of K: enough slices
+// to give every SM a tile, each slice at least 128 deep.
+static int lstm_splits(long long tiles, int K) {
+  long long want = (148 + tiles - 1) / tiles, cap = K / 128;
+  if (cap < 1) cap = 1;
+  if (want > cap) want = cap;
+  if (want > 16) want = 16;
+  return (int)(want < 1 ? 1 : want);
+}
+
 static int k_lstm_hidden_gradient(Launch &L) {
   int H = (int)L.nd.g[0];
   int V = (L.nd.dims > 1 ? (int)L.nd.g[1] : 1) * L.B;
@@ -304,23 +333,59 @@ static int k_lstm_hidden_gradient(Launch &L) {
   float *opnd = a + na;
   lstm_hg_prep_kernel<<<grid1d(std::max(na, nop), 256), 256, 0, L.stream>>>(cg, a, opnd, hidden, out, x, H, in, V);
   NN_CHECK_LAUNCH(L);
-  // input gradient: dx[v][j] = sum_g a[v][g] w[g][H+j]
+  // input gradient: dx[v][j] = sum_g a[v][g] w[g][H+j]; on the tensor cores in K slices whose
+  // partials (16-byte rows when in % 4 == 0) are summed into dx
   if (in > 0) {
     FastShape fs{V, in, 4 * H, 1, 1, 0, a, 4LL * H, 0, w + H, ws, 0};
-    cudaError_t e = gemm_f32_wb<false, true>(L, fs, StoreInputGrad{ig, in});
-    if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
-    L.counted();
+    const long long tiles = (long long)((V + 127) / 128) * ((in + 127) / 128);
+    const int splits = lstm_splits(tiles, 4 * H);
+    if (tc_path(fs) && splits > 1 && in % 4 == 0) {
+      fs.splits = splits;
+      fs.kchunk = ((4 * H + splits - 1) / splits + 31) / 32 * 32;
+      fs.splits = (4 * H + fs.kchunk - 1) / fs.kchunk;
+      const size_t per = (size_t)V * in;
+      float *part = L.scratch(2, per * fs.splits);
+      if (!part) return NN_ERR_CUDA;
+      cudaError_t e = gemm_f32_wb<false, true>(L, fs, PartialStoreTma{{part, V, in, 1}});
+      if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
+      L.counted();
+      GradSrc src{part, fs.splits, per, 1.f};
+      reduce_partials_kernel<<<(unsigned)((per + 31) / 32), dim3(32, 8), 0, L.stream>>>(ig, src, per);
+      NN_CHECK_LAUNCH(L);
+    } else {
+      cudaError_t e = gemm_f32_wb<false, true>(L, fs, StoreInputGrad{ig, in});
+      if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
+      L.counted();
+    }
   }
-  // weight gradient: wg[g][i] = sum_v a[v][g] opnd[v][i], i < H+in (summed over the series)
+  // weight gradient: wg[g][i] = sum_v a[v][g] opnd[v][i], i < H+in (summed over the series), in
+  // K slices of the series on the tensor cores
   {
-    FastShape fs{4 * H, H + in, V, 1, 1, 0, a, 4LL * H, 0, opnd, (long long)H + in, 0};
-    cudaError_t e = gemm_f32<true, true>(fs, StoreStrided{wg, ws}, L.stream);
-    if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
-    L.counted();
+    const int N = H + in;
+    FastShape fs{4 * H, N, V, 1, 1, 0, a, 4LL * H, 0, opnd, (long long)N, 0};
+    const long long tiles = (long long)((4 * H + 127) / 128) * ((N + 127) / 128);
+    const int splits = lstm_splits(tiles, V);
+    if (tc_path(fs) && splits > 1 && N % 4 == 0) {
+      fs.kchunk = ((V + splits - 1) / splits + 31) / 32 * 32;
+      fs.splits = (V + fs.kchunk - 1) / fs.kchunk;
+      const size_t per = (size_t)4 * H * N;
+      float *part = L.scratch(0, per * fs.splits);
+      if (!part) return NN_ERR_CUDA;
+      cudaError_t e = tcgemm<true, true>(fs, PartialStoreTma{{part, 4 * H, N, 1}}, L.stream, device_status());
+      if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
+      L.counted();
+      GradSrc src{part, fs.splits, per, 1.f};
+      lstm_wg_reduce_kernel<<<grid1d(per, 256), 256, 0, L.stream>>>(wg, src, 4 * H, N, ws);
+      NN_CHECK_LAUNCH(L);
+    } else {
+      cudaError_t e = gemm_f32<true, true>(fs, StoreStrided{wg, ws}, L.stream);
+      if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
+      L.counted();
+    }
   }
   // the last bias write lands one element past the (4H)x(H+in+1) matrix: done only when the buffer holds it
   const int bias_rows = L.floats(2) > (size_t)4 * H * ws ? 4 * H : 4 * H - 1;
-  lstm_bias_kernel<<<grid1d(4 * H, 256), 256, 0, L.stream>>>(cg, wg, H, V, ws, bias_rows);
+  lstm_bias_kernel<<<(unsigned)((bias_rows + 31) / 32), dim3(32, 32), 0, L.stream>>>(cg, wg, H, V, ws, bias_rows);
   NN_CHECK_LAUNCH(L);
   return NN_OK;
 }

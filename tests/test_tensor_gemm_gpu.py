@@ -118,7 +118,7 @@ def test_dense_batched(ctx, n_in, n_out, B, act):
     check_batched_update(ctx, cases["UpdateWeightsAdam"], B, 6000 + n_in)
 
 
-@pytest.mark.parametrize("H,ins,V", [(64, 32, 300), (40, 13, 129)])
+@pytest.mark.parametrize("H,ins,V", [(64, 32, 300), (40, 13, 129), (128, 128, 512)])
 def test_lstm_hidden_gradient(ctx, H, ins, V):
     ws = H + ins + 1
     case = Case(f"LSTM_HiddenGradient/{H}-{ins}-{V}", "LSTM_HiddenGradient",
