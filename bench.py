@@ -221,6 +221,24 @@ class Workload:
         """([pool][n_in], [pool][n_out]) float32 arrays: inputs and targets of `pool` steps."""
         raise NotImplementedError
 
+    # -- the step's inputs and the result read back, for a network trained against targets (Net) --
+    def slots(self, pool, seed):
+        """Per input buffer: [pool][floats] float32 arrays of `pool` steps."""
+        return list(self.data(pool, seed))
+
+    def io(self, obj):
+        """(input buffer handles in the order of slots(), output buffer handle, output floats)."""
+        out = obj.layers[-1]
+        return [obj.layers[0].output, obj.target], out.output, out.neurons * out.batch
+
+    def host_metric(self, y, slots, i):
+        """(name, value) the host computes from step i's read-back result: the MSE against the targets."""
+        d = y - slots[1][i]
+        return "mse_last", float(np.dot(d, d)) / d.size
+
+    def ops(self, obj):
+        return obj.fwd_ops + obj.bwd_ops + obj.upd_ops
+
     def config(self, world) -> dict:
         raise NotImplementedError
 
@@ -435,9 +453,69 @@ class PatchWorkload(Workload):
         return f"{n} training steps of one 32x512 window (fwd+bwd+Adam) through the {backend}, {el:.1f} s"
 
 
+class SACWorkload(Workload):
+    """A step is one soft actor-critic update on one replay batch; a sample is one transition."""
+
+    key = "sac"
+    name = "sac_actor240x512x512x12_2critics246x512x512x1_tau0.005"
+    default_batch = 4096
+    default_steps = 30
+
+    def __init__(self, batch):
+        super().__init__(batch)
+        from nn_in_trading_b200 import sac as S
+        self.S, self.spec = S, S.SACSpec()
+
+    def build(self, ctx, dp):
+        return self.S.SACAgent(ctx, self.spec, self.B, self.S.sac_weights(self.spec), dp=dp)
+
+    def slots(self, pool, seed):
+        d = self.S.sac_data(self.spec, self.B, pool, seed=seed)
+        return [d[k] for k in self.S.SACAgent.INPUTS]
+
+    def io(self, obj):
+        return [getattr(obj, k) for k in obj.INPUTS], obj.critics[0][-1].output, self.B
+
+    def host_metric(self, y, slots, i):
+        return "mean_q_last", float(np.mean(y))
+
+    def ops(self, obj):
+        return [op for ops, _ in obj.phases for op in ops]
+
+    def config(self, world):
+        s = self.spec
+        return {"workload": self.name, "global_batch": self.B * world, "per_gpu_batch": self.B,
+                "state": s.state, "action": s.action, "hidden": s.hidden, "tau": s.tau, "gamma": s.gamma,
+                "alpha": s.alpha, "sample": "one replay transition (critic, actor and target updates)",
+                "parallelism": f"dp{world}",
+                "l2": "no flush: the weights (6.3 MB with moments) stay in L2 across phases as in any "
+                      "training loop; the 4096-row activations (8 MB per 512-wide layer) are streamed"}
+
+    def oracle_net(self, O, K, batch):
+        return _OracleSAC(O, self.spec, batch, self.S.sac_weights(self.spec))
+
+    def ref_data(self, pool):
+        d = self.S.sac_data(self.spec, 1, pool, seed=7)
+        return [{k: v[i] for k, v in d.items()} for i in range(pool)], None
+
+    def ref_sample_desc(self, n, el, backend):
+        return (f"{n} SAC updates of one transition (actor, 2 critics, 2 targets) through the {backend}, "
+                f"{el:.1f} s")
+
+
+class _OracleSAC:
+    """The oracle SAC agent behind the ONet step(x, target) call shape of reference_sample."""
+
+    def __init__(self, O, spec, batch, weights):
+        self.agent = O.OSACAgent(spec, batch, weights)
+
+    def step(self, batch, _target):
+        self.agent.step(batch)
+
+
 REF_LSTM_SERIES = 4
 REF_CAP_SECONDS = 90.0  # the reference arm stops after K steps or this long, whichever comes first
-WORKLOADS = {w.key: w for w in (MLMHWorkload, DenseWorkload, LSTMWorkload, PatchWorkload)}
+WORKLOADS = {w.key: w for w in (MLMHWorkload, DenseWorkload, LSTMWorkload, PatchWorkload, SACWorkload)}
 
 
 # ------------------------------------------------------------- our arm
@@ -456,18 +534,17 @@ def run_ours(args, rank, world, local_rank):
         dp.join_dp(ctx, rank, world)
 
     pool = 4
-    xs, ts = wl.data(pool, 100 + rank)
-    n_in, n_out = xs.shape[1], ts.shape[1]
-    resident_x = [ctx.buffer(n_in) for _ in range(pool)]
-    resident_t = [ctx.buffer(n_out) for _ in range(pool)]
-    for i in range(pool):
-        ctx.write(resident_x[i], xs[i])
-        ctx.write(resident_t[i], ts[i])
-    inp = net.layers[0].output
+    slots = wl.slots(pool, 100 + rank)
+    inputs, out_h, n_y = wl.io(net)
+    sizes = [int(sl.shape[1]) for sl in slots]
+    resident = [[ctx.buffer(n) for _ in range(pool)] for n in sizes]
+    for sl, res in zip(slots, resident):
+        for i in range(pool):
+            ctx.write(res[i], sl[i])
 
     def load(i):
-        ctx.copy(inp, resident_x[i % pool], n_in)
-        ctx.copy(net.target, resident_t[i % pool], n_out)
+        for h, res, n in zip(inputs, resident, sizes):
+            ctx.copy(h, res[i % pool], n)
 
     if wl.recordable:
         net.capture()
@@ -507,38 +584,31 @@ def run_ours(args, rank, world, local_rank):
     value = world * per_step * args.steps / (ms_max / 1000.0)
 
     # ---- e2e through the public API with host buffers (pinned) ----------
-    hx = torch.from_numpy(xs).pin_memory()
-    ht = torch.from_numpy(ts).pin_memory()
-    out_layer = net.layers[-1]
-    n_y = out_layer.neurons * out_layer.batch
+    hosts = [torch.from_numpy(np.ascontiguousarray(sl)).pin_memory() for sl in slots]
     hy = torch.empty(n_y, dtype=torch.float32).pin_memory()
     lib = ctx.lib
-    out_h = out_layer.output
     e2e_steps = max(3, args.steps // 2)
-    for i in range(2):
-        lib.nn_buffer_write(inp, hx[i % pool].data_ptr(), 0, n_in)
-        lib.nn_buffer_write(net.target, ht[i % pool].data_ptr(), 0, n_out)
-        net.step()
-        lib.nn_buffer_read(out_h, hy.data_ptr(), 0, n_y)
-    barrier()
-    # Every step: H2D of its inputs and targets, the step, a blocking D2H of its output and the host
-    # MSE of that output (CNet::backPropOCL reads the output back).  The host work of step i runs
-    # while the device already executes step i+1 (enqueued right after step i's read returns).
-    t0 = time.perf_counter()
-    losses = []
 
     def enqueue(i):
-        ctx._check(lib.nn_buffer_write(inp, hx[i % pool].data_ptr(), 0, n_in))
-        ctx._check(lib.nn_buffer_write(net.target, ht[i % pool].data_ptr(), 0, n_out))
+        for h, host, n in zip(inputs, hosts, sizes):
+            ctx._check(lib.nn_buffer_write(h, host[i % pool].data_ptr(), 0, n))
         net.step()
 
+    for i in range(2):
+        enqueue(i)
+        ctx._check(lib.nn_buffer_read(out_h, hy.data_ptr(), 0, n_y))
+    barrier()
+    # Every step: H2D of its inputs, the step, a blocking D2H of its result and the host metric of that
+    # result (CNet::backPropOCL reads the output back).  The host work of step i runs while the
+    # device already executes step i+1 (enqueued right after step i's read returns).
+    t0 = time.perf_counter()
+    metric = (None, None)
     enqueue(0)
     for i in range(e2e_steps):
         ctx._check(lib.nn_buffer_read(out_h, hy.data_ptr(), 0, n_y))
         if i + 1 < e2e_steps:
             enqueue(i + 1)  # hy is written again only by the next iteration's read
-        d = hy.numpy() - ts[i % pool]
-        losses.append(float(np.dot(d, d)) / d.size)  # host MSE of step i's output
+        metric = wl.host_metric(hy.numpy(), slots, i % pool)
     e2e_s = time.perf_counter() - t0
     if world > 1:
         t = torch.tensor([e2e_s], dtype=torch.float64)
@@ -547,7 +617,7 @@ def run_ours(args, rank, world, local_rank):
     e2e = world * per_step * e2e_steps / e2e_s
 
     # ---- per-kernel profile pass (CUDA events between launches) --------
-    prof = profile_ops(ctx, net, stream, wl.B, load, torch)
+    prof = profile_ops(ctx, wl.ops(net), stream, load, torch)
     result = None
     if rank == 0:
         peaks = read_peaks()
@@ -556,8 +626,8 @@ def run_ours(args, rank, world, local_rank):
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": wl.config(world),
-            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": (n_in + n_out) * 4,
-                    "d2h_bytes_per_step": n_y * 4, "mse_last": losses[-1]},
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": sum(sizes) * 4,
+                    "d2h_bytes_per_step": n_y * 4, metric[0]: metric[1]},
             "gpu_launches": launches,
             "roofline": roofline(prof["top"], peaks, wl),
             "kernel_shares": prof["shares"],
@@ -592,9 +662,8 @@ def roofline(top, peaks, wl):
                                              "MMAs per fp32 product)"}
 
 
-def profile_ops(ctx, net, stream, B, load, torch):
+def profile_ops(ctx, ops, stream, load, torch):
     """One eager step with a CUDA event after every launch; per kernel-name time and work."""
-    ops = net.fwd_ops + net.bwd_ops + net.upd_ops
     load(0)
     ctx.finish()
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(ops) + 1)]
@@ -647,6 +716,8 @@ def reference_sample(wl, seconds: float, steps: int | None = None, warmup: int =
     batch = REF_LSTM_SERIES if isinstance(wl, LSTMWorkload) else 1
     net = wl.oracle_net(O, K, batch)
     xs, ts = wl.ref_data(4)
+    if ts is None:
+        ts = [None] * 4
     for i in range(warmup):
         net.step(xs[i % 4], ts[i % 4])
     n = 0

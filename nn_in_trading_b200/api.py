@@ -36,6 +36,9 @@ SIGNATURES = {
     "UpdateBatchOptionsMomentum": "ppff", "UpdateBatchOptionsAdam": "ppfff",
     "LSTM_FeedForward": "pipppp", "LSTM_ConcatenatedGradient": "pppp",
     "LSTM_HiddenGradient": "pppppppii", "LSTM_UpdateWeightsAdam": "ppppfff",
+    "Concat_FeedForward": "ppppiii", "Concat_HiddenGradient": "ppppppiiiii",
+    "Concat_UpdateWeightsMomentum": "pppppiiff", "Concat_UpdateWeightsAdam": "ppppppiifff",
+    "SACGaussianPolicy": "ppppi", "SACTargetValue": "ppppppff", "SACPolicyGradient": "ppppppppif",
     "MH2AttentionOut": "ppppiii", "MH2AttentionInsideGradients": "ppppppii",
     "AttentionScore": "pppii", "AttentionOut": "pppp", "AttentionInsideGradients": "pppppppp",
     "Dropout": "pppi",

@@ -98,6 +98,8 @@ extern const KernelDef kLstmKernels[];
 extern const int kNumLstmKernels;
 extern const KernelDef kAttn2Kernels[];
 extern const int kNumAttn2Kernels;
+extern const KernelDef kSacKernels[];
+extern const int kNumSacKernels;
 
 // Number of data-parallel ranks (1 without a communicator).
 int dp_world();

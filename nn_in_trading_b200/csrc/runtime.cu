@@ -212,7 +212,8 @@ const KernelDef *find_kernel(const char *name) {
   struct Table { const KernelDef *t; int n; };
   const Table tables[] = {{kDenseKernels, kNumDenseKernels}, {kConvKernels, kNumConvKernels},
                           {kAttnKernels, kNumAttnKernels}, {kMiscKernels, kNumMiscKernels},
-                          {kLstmKernels, kNumLstmKernels}, {kAttn2Kernels, kNumAttn2Kernels}};
+                          {kLstmKernels, kNumLstmKernels}, {kAttn2Kernels, kNumAttn2Kernels},
+                          {kSacKernels, kNumSacKernels}};
   for (const Table &t : tables)
     for (int i = 0; i < t.n; ++i)
       if (std::strcmp(t.t[i].name, name) == 0) return &t.t[i];

@@ -126,6 +126,33 @@ class Layer:
     def update_ops(self, prev: "Layer") -> list[Op]:
         return []
 
+    def soft_update_ops(self, source: "Layer", tau: float, adam: bool | None = None) -> list["Op"]:
+        """CNeuronBaseOCL::WeightsUpdate (NeuroNet_Core.mqh:20283-20370): SoftUpdateAdam on the weights
+        toward the next layer (with this layer's moments) when Adam and tau != 1, else SoftUpdate.
+        `adam` overrides that choice (False: plain Polyak averaging whatever the optimizer)."""
+        if self.weights is None:
+            return []
+        n = self.outputs * (self.neurons + 1)
+        if adam is None:
+            adam = tau != 1.0 and self.optimization == ADAM
+        if adam:
+            k = self.ctx.kernel("SoftUpdateAdam").args(self.weights, source.weights, self.m, self.v, tau, B1, B2)
+        else:
+            k = self.ctx.kernel("SoftUpdate").args(self.weights, source.weights, tau)
+        return [Op(k, (n,))]
+
+    def param_handles(self) -> list[str]:
+        """Attribute names of the parameter buffers (weights and optimizer state)."""
+        if self.weights is None:
+            return []
+        return ["weights", "delta"] if self.optimization == SGD else ["weights", "m", "v"]
+
+    def share_params(self, source: "Layer") -> None:
+        """Use `source`'s parameter buffers (a second activation/gradient set over the same weights)."""
+        for name in self.param_handles():
+            self.ctx.free(getattr(self, name))
+            setattr(self, name, getattr(source, name))
+
     def output_gradient_ops(self, target: int) -> list[Op]:
         """CNeuronBaseOCL::calcOutputGradients (NeuroNet_Core.mqh:15800-15837)."""
         k = self.kernel("CalcOutputGradient").args(target, self.output, self.gradient, self.activation, 1.0)
@@ -155,6 +182,76 @@ class DenseLayer(Layer):
         kn = self.ctx.kernel("NormalizeWeights").args(prev.weights, prev.neurons + 1)
         ops.append(Op(kn, (self.neurons,)))
         return ops
+
+
+class ConcatLayer(Layer):
+    """CNeuronConcatenate (NeuroNet_Misc.mqh:286-680): output = act(W [x1; x2; 1]) with the previous
+    layer's output as x1 and a second input buffer x2 (`second`, `inputs2` floats per sample), its own
+    weights [neurons][inputs1 + inputs2 + 1] (bias last), no NormalizeWeights after its update.  As a
+    CNeuronBaseOCL it also holds the weights toward the next dense layer."""
+
+    def __init__(self, ctx, neurons, inputs1, inputs2, activation=NONE, optimization=ADAM, batch=1, outputs=0):
+        super().__init__(ctx, neurons, activation, optimization, batch, outputs)
+        self.inputs1, self.inputs2 = int(inputs1), int(inputs2)
+        n = self.neurons * (self.inputs1 + self.inputs2 + 1)
+        self.conc_w = ctx.buffer(n)
+        if optimization == SGD:
+            self.conc_dw = ctx.buffer(n)
+        else:
+            self.conc_m = ctx.buffer(n)
+            self.conc_v = ctx.buffer(n)
+        self.second = ctx.buffer(self.inputs2 * self.batch)        # x2 of every sample
+        self.second_grad = ctx.buffer(self.inputs2 * self.batch)   # d/dx2 written by calcInputGradients
+        self.second_activation = NONE
+
+    def set_conc_weights(self, w: np.ndarray) -> None:
+        self.ctx.write(self.conc_w, w)
+
+    def forward_ops(self, prev: Layer) -> list[Op]:
+        """feedForward, NeuroNet_Misc.mqh:386-418 -> Concat_FeedForward over the layer's outputs."""
+        k = self.kernel("Concat_FeedForward").args(self.conc_w, prev.output, self.second, self.output,
+                                                   self.per_sample(prev), self.inputs2, self.activation)
+        return [Op(k, (self.neurons,))]
+
+    def input_gradient_ops(self, prev: Layer) -> list[Op]:
+        """calcInputGradients, NeuroNet_Misc.mqh:421-462 -> Concat_HiddenGradient over inputs1 + inputs2."""
+        n1 = self.per_sample(prev)
+        k = self.kernel("Concat_HiddenGradient").args(self.conc_w, self.gradient, prev.output, self.second,
+                                                      prev.gradient, self.second_grad, self.neurons, n1,
+                                                      self.inputs2, prev.activation, self.second_activation)
+        return [Op(k, (n1 + self.inputs2,))]
+
+    def update_ops(self, prev: Layer) -> list[Op]:
+        """updateInputWeights, NeuroNet_Misc.mqh:465-560: Concat_UpdateWeightsMomentum or _Adam over
+        (neurons, inputs1 + inputs2 + 1), the Adam rate bias-corrected from this layer's step counter.
+        (The reference's SGD branch binds inputs2 into the inputs1 slot, NeuroNet_Misc.mqh:501-502; this
+        host binds both counts.)"""
+        n1 = self.per_sample(prev)
+        gsize = (self.neurons, n1 + self.inputs2 + 1)
+        if prev.optimization == SGD:
+            k = self.kernel("Concat_UpdateWeightsMomentum").args(self.conc_w, self.gradient, prev.output, self.second,
+                                                                 self.conc_dw, n1, self.inputs2, LR, MOMENTUM)
+            return [Op(k, gsize)]
+        k = self.kernel("Concat_UpdateWeightsAdam").args(self.conc_w, self.gradient, prev.output, self.second,
+                                                         self.conc_m, self.conc_v, n1, self.inputs2, LR, B1, B2)
+        return [AdamOp(k, gsize, None, self, 8)]
+
+    def soft_update_ops(self, source: "ConcatLayer", tau: float, adam: bool | None = None) -> list[Op]:
+        """WeightsUpdate, NeuroNet_Misc.mqh:628-676: the base weights, then the concat weights."""
+        ops = super().soft_update_ops(source, tau, adam)
+        if adam is None:
+            adam = tau != 1.0 and self.optimization == ADAM
+        if adam:
+            k = self.ctx.kernel("SoftUpdateAdam").args(self.conc_w, source.conc_w, self.conc_m, self.conc_v, tau,
+                                                       B1, B2)
+        else:
+            k = self.ctx.kernel("SoftUpdate").args(self.conc_w, source.conc_w, tau)
+        n = self.neurons * (self.inputs1 + self.inputs2 + 1)
+        return ops + [Op(k, (n,))]
+
+    def param_handles(self) -> list[str]:
+        return super().param_handles() + (["conc_w", "conc_dw"] if self.optimization == SGD
+                                          else ["conc_w", "conc_m", "conc_v"])
 
 
 class MLMHAttentionLayer(Layer):

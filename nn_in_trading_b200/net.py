@@ -25,10 +25,14 @@ from .layers import AdamOp, DenseLayer, Layer, Op
 
 
 class Net:
-    def __init__(self, ctx: Context, layers: list[Layer], dp: bool = False):
-        self.ctx, self.layers, self.dp = ctx, layers, dp
+    def __init__(self, ctx: Context, layers: list[Layer], dp: bool = False, target: int | None = None,
+                 loss: bool = True):
+        """`target`: an existing target buffer to train against (default: a new one).  `loss=False`:
+        the backward pass starts from whatever the last layer's gradient buffer holds (no
+        CalcOutputGradient), for networks whose output gradient comes from another kernel."""
+        self.ctx, self.layers, self.dp, self.loss = ctx, layers, dp, loss
         self.batch = layers[0].batch
-        self.target = ctx.buffer(layers[-1].neurons * self.batch)
+        self.target = target if target is not None else ctx.buffer(layers[-1].neurons * self.batch)
         self.fwd_ops = self._forward_ops()
         self.bwd_ops = self._backward_ops()
         self.upd_ops = self._update_ops()
@@ -45,7 +49,7 @@ class Net:
         return ops
 
     def _backward_ops(self) -> list[Op]:
-        ops = list(self.layers[-1].output_gradient_ops(self.target))
+        ops = list(self.layers[-1].output_gradient_ops(self.target)) if self.loss else []
         for l in range(len(self.layers) - 2, -1, -1):
             cur, nxt = self.layers[l], self.layers[l + 1]
             if type(nxt) is DenseLayer:  # CNeuronBaseOCL::CalcHiddenGradients dispatch, NeuroNet_Core.mqh:15988-16014

@@ -46,6 +46,7 @@ KERNELS = [
     "SoftUpdate", "SoftUpdateAdam",
     "Transpose", "MH2AttentionOut", "MH2AttentionInsideGradients",
     "RevInFeedForward", "RevInHiddenGraddient", "Activation", "DeActivation",
+    "Concat_FeedForward", "Concat_HiddenGradient", "Concat_UpdateWeightsMomentum", "Concat_UpdateWeightsAdam",
 ]
 
 

@@ -854,6 +854,155 @@ def LSTM_UpdateWeightsAdam(weights, weights_gradient, matrix_m, matrix_v, l, b1,
         matrix_v[:n] = vt
 
 
+# ---------------------------------------------------------------- concatenate
+def _concat_rows(matrix_w, n_out, inputs1, inputs2):
+    return matrix_w[:n_out * (inputs1 + inputs2 + 1)].reshape(n_out, inputs1 + inputs2 + 1)
+
+
+def Concat_FeedForward(matrix_w, matrix_i1, matrix_i2, matrix_o, inputs1, inputs2, activation, gsize, lsize=None):
+    """NeuroNet.cl:3628-3718.  o[i] = act(W[i] . [x1; x2; 1]) over rows of inputs1+inputs2+1 floats; the two
+    inputs are summed in float4 groups, a group whose addition makes the sum NaN is skipped, the bias is
+    added without a check and a NaN total becomes 0."""
+    n_out = gsize[0]
+    with _err():
+        w = _concat_rows(matrix_w, n_out, inputs1, inputs2)
+        s = np.zeros(n_out, F32)
+        for x, off, n in ((matrix_i1, 0, inputs1), (matrix_i2, inputs1, inputs2)):
+            for k in range(0, n, 4):
+                e = min(k + 4, n)
+                d = (w[:, off + k:off + e] * x[k:e][None, :]).sum(axis=1, dtype=F32)
+                t = (s + d).astype(F32)
+                s = np.where(np.isnan(t), s, t).astype(F32)
+        s = (s + w[:, inputs1 + inputs2]).astype(F32)
+        s = np.where(np.isnan(s), F32(0), s)
+        matrix_o[:n_out] = f_activation(s, activation)
+
+
+def Concat_HiddenGradient(matrix_w, matrix_g, matrix_o1, matrix_o2, matrix_ig1, matrix_ig2, outputs, inputs1,
+                          inputs2, activation1, activation2, gsize, lsize=None):
+    """NeuroNet.cl:3724-3785.  For input i of [x1; x2]: sum_k g[k] W[k][i] (NaN -> 0), then Deactivation
+    with the first or the second input's activation, written to the matching gradient buffer."""
+    n = min(gsize[0], inputs1 + inputs2)
+    with _err():
+        w = _concat_rows(matrix_w, outputs, inputs1, inputs2)[:, :n]
+        s = (w * matrix_g[:outputs][:, None]).sum(axis=0, dtype=F32)
+        s = np.where(np.isnan(s), F32(0), s)
+        n1 = min(n, inputs1)
+        matrix_ig1[:n1] = deactivation(s[:n1], matrix_o1[:n1], activation1)
+        if n > inputs1:
+            matrix_ig2[:n - inputs1] = deactivation(s[inputs1:n], matrix_o2[:n - inputs1], activation2)
+
+
+def _concat_inputs(matrix_i1, matrix_i2, inputs1, inputs2, n_col):
+    """[x1; x2; 1] for columns j < n_col (NeuroNet.cl:3808, 3845)."""
+    j = np.arange(n_col)
+    return np.where(j < inputs1, matrix_i1[np.minimum(j, max(inputs1 - 1, 0))] if inputs1 else F32(0),
+                    np.where(j - inputs1 < inputs2,
+                             matrix_i2[np.clip(j - inputs1, 0, max(inputs2 - 1, 0))] if inputs2 else F32(0),
+                             F32(1))).astype(F32)
+
+
+def concat_adam_apply(matrix_w, grad, matrix_m, matrix_v, inputs1, inputs2, l, b1, b2, n_out, n_col):
+    """Adam arithmetic of Concat_UpdateWeightsAdam (NeuroNet.cl:3849-3861) for the gradient grad[i, j]:
+    no clamp and no NaN guards; a weight moves only when |delta| > 0."""
+    with _err():
+        idx = np.arange(n_out)[:, None] * (inputs1 + inputs2 + 1) + np.arange(n_col)[None, :]
+        weight = matrix_w[idx]
+        g = np.asarray(grad, dtype=F32)
+        b1, b2, l = F32(b1), F32(b2), F32(l)
+        mt = (b1 * matrix_m[idx] + (F32(1) - b1) * g).astype(F32)
+        vt = (b2 * matrix_v[idx] + (F32(1) - b2) * (g * g)).astype(F32)
+        delta = (l * (mt / (np.sqrt(vt) + F32(1e-37)) - (L1 * cl_sign(weight) + L2 * weight))).astype(F32)
+        matrix_w[idx] = np.where(np.abs(delta) > 0, (weight + delta).astype(F32), weight)
+        matrix_m[idx] = mt
+        matrix_v[idx] = vt
+
+
+def Concat_UpdateWeightsAdam(matrix_w, matrix_g, matrix_i1, matrix_i2, matrix_m, matrix_v, inputs1, inputs2, l,
+                             b1, b2, gsize, lsize=None):
+    """NeuroNet.cl:3823-3862.  g = g_o[i] * [x1; x2; 1][j]; Adam as UpdateWeightsAdam but without the
+    gradient clamp."""
+    n_out, n_col = gsize[0], min(gsize[1], inputs1 + inputs2 + 1)
+    with _err():
+        inp = _concat_inputs(matrix_i1, matrix_i2, inputs1, inputs2, n_col)
+        grad = (matrix_g[:n_out][:, None] * inp[None, :]).astype(F32)
+    concat_adam_apply(matrix_w, grad, matrix_m, matrix_v, inputs1, inputs2, l, b1, b2, n_out, n_col)
+
+
+def concat_momentum_apply(matrix_w, grad, matrix_dw, inputs1, inputs2, learning_rates, momentum, n_out, n_col):
+    """Arithmetic of Concat_UpdateWeightsMomentum (NeuroNet.cl:3806-3817) for the gradient grad[i, j]."""
+    with _err():
+        idx = np.arange(n_out)[:, None] * (inputs1 + inputs2 + 1) + np.arange(n_col)[None, :]
+        delta = (F32(learning_rates) * np.asarray(grad, F32) + F32(momentum) * matrix_dw[idx]).astype(F32)
+        ok = ~np.isnan(delta)
+        matrix_dw[idx] = np.where(ok, delta, matrix_dw[idx])
+        w = matrix_w[idx]
+        matrix_w[idx] = np.where(ok & (np.abs(delta) > 0), (w + delta).astype(F32), w)
+
+
+def Concat_UpdateWeightsMomentum(matrix_w, matrix_g, matrix_i1, matrix_i2, matrix_dw, inputs1, inputs2,
+                                 learning_rates, momentum, gsize, lsize=None):
+    """NeuroNet.cl:3790-3818.  delta = lr g_o[i] [x1; x2; 1][j] + momentum dw; kept unless NaN."""
+    n_out, n_col = gsize[0], min(gsize[1], inputs1 + inputs2 + 1)
+    with _err():
+        inp = _concat_inputs(matrix_i1, matrix_i2, inputs1, inputs2, n_col)
+        grad = (matrix_g[:n_out][:, None] * inp[None, :]).astype(F32)
+    concat_momentum_apply(matrix_w, grad, matrix_dw, inputs1, inputs2, learning_rates, momentum, n_out, n_col)
+
+
+# --------------------------------------------------------- soft actor-critic
+# The library's squashed-Gaussian SAC kernels (no reference counterpart; the reference's SAC agents
+# use quantile heads).  A launch covers gsize[0] * batch samples; here gsize[0] is the sample count.
+# kernels the library defines beyond the reference (no reference output pins them; their tests are
+# known answers and a finite-difference check of the policy gradient)
+LIBRARY_KERNELS = {"SACGaussianPolicy", "SACTargetValue", "SACPolicyGradient"}
+LOG_STD_MIN, LOG_STD_MAX = F32(-20.0), F32(2.0)
+HALF_LOG_2PI = F32(0.5 * np.log(2.0 * np.pi))
+SQUASH_EPS = F32(1e-6)
+
+
+def SACGaussianPolicy(outputs, noise, actions, log_probs, action_dim, gsize, lsize=None):
+    """a = tanh(mu + exp(clamp(log_std, -20, 2)) eps); log pi = sum_j (-eps^2/2 - log_std - log(2 pi)/2
+    - log(1 - a^2 + 1e-6)) with outputs [n][2A] = (mu, log_std)."""
+    n, A = gsize[0], action_dim
+    with _err():
+        o = outputs[:n * 2 * A].reshape(n, 2 * A)
+        ls = cl_clamp(o[:, A:], LOG_STD_MIN, LOG_STD_MAX)
+        e = noise[:n * A].reshape(n, A)
+        a = np.tanh((o[:, :A] + np.exp(ls) * e).astype(F32)).astype(F32)
+        actions[:n * A] = a.reshape(-1)
+        lp = (F32(-0.5) * e * e - ls - HALF_LOG_2PI - np.log(F32(1) - a * a + SQUASH_EPS)).astype(F32)
+        log_probs[:n] = lp.sum(axis=1, dtype=F32)
+
+
+def SACTargetValue(q1, q2, reward, done, log_probs, target, gamma, alpha, gsize, lsize=None):
+    """y = r + gamma (1 - done) (min(q1, q2) - alpha log pi)."""
+    n = gsize[0]
+    with _err():
+        target[:n] = (reward[:n] + F32(gamma) * (F32(1) - done[:n])
+                      * (np.minimum(q1[:n], q2[:n]) - F32(alpha) * log_probs[:n])).astype(F32)
+
+
+def SACPolicyGradient(outputs, noise, actions, q1, q2, dq1, dq2, gradient, action_dim, alpha, gsize, lsize=None):
+    """Ascent direction of J = min(q1, q2) - alpha log pi for (mu, log_std), dq of the smaller critic,
+    each entry clamped to +-MAX_GRAD: s = dq (1 - a^2) - alpha 2a(1 - a^2)/(1 - a^2 + 1e-6);
+    dJ/dmu = s; dJ/dlog_std = s exp(log_std) eps + alpha strictly inside (-20, 2), else 0."""
+    n, A = gsize[0], action_dim
+    with _err():
+        o = outputs[:n * 2 * A].reshape(n, 2 * A)
+        a = actions[:n * A].reshape(n, A)
+        e = noise[:n * A].reshape(n, A)
+        dq = np.where((q1[:n] <= q2[:n])[:, None], dq1[:n * A].reshape(n, A), dq2[:n * A].reshape(n, A))
+        one = (F32(1) - a * a).astype(F32)
+        sgr = (dq * one - F32(alpha) * F32(2) * a * one / (one + SQUASH_EPS)).astype(F32)
+        ls_raw = o[:, A:]
+        ls = cl_clamp(ls_raw, LOG_STD_MIN, LOG_STD_MAX)
+        g = gradient[:n * 2 * A].reshape(n, 2 * A)
+        g[:, :A] = cl_clamp(nan0(sgr), -MAX_GRAD, MAX_GRAD)
+        inside = (ls_raw > LOG_STD_MIN) & (ls_raw < LOG_STD_MAX)
+        g[:, A:] = np.where(inside, cl_clamp(nan0(sgr * np.exp(ls) * e + F32(alpha)), -MAX_GRAD, MAX_GRAD), F32(0))
+
+
 KERNELS = {name: fn for name, fn in globals().items()
            if callable(fn) and name[:1].isupper() and fn.__module__ == __name__}
 

@@ -438,3 +438,166 @@ class OLSTM(OLayer):
         total = (self.inputs + self.H * self.variables) // self.variables + 1
         BACKEND.LSTM_UpdateWeightsAdam(self.lstm_w, self.lstm_wg, self.lstm_m, self.lstm_v, LR, B1, B2,
                                        gsize=(total, self.H))
+
+
+class OConcat(ODense):
+    """CNeuronConcatenate (NeuroNet_Misc.mqh:286-680): act(W [x1; x2; 1]) over its own weights
+    [neurons][inputs1 + inputs2 + 1]; `second` holds x2 of every sample; no NormalizeWeights."""
+
+    def __init__(self, neurons, inputs1, inputs2, activation=K.NONE, batch=1, outputs=0):
+        super().__init__(neurons, activation, batch, outputs)
+        self.in1, self.in2 = inputs1, inputs2
+        n = neurons * (inputs1 + inputs2 + 1)
+        self.conc_w, self.conc_m, self.conc_v = np.zeros(n, F32), np.zeros(n, F32), np.zeros(n, F32)
+        self.second = np.zeros((batch, inputs2), F32)
+        self.second_grad = np.zeros((batch, inputs2), F32)
+        self.second_activation = K.NONE
+
+    def forward(self, prev):
+        """NeuroNet_Misc.mqh:386-418 -> Concat_FeedForward."""
+        for b in range(self.batch):
+            BACKEND.Concat_FeedForward(self.conc_w, prev.output[b], self.second[b], self.output[b], self.in1,
+                                       self.in2, self.activation, gsize=(self.neurons,))
+
+    def input_gradient(self, prev):
+        """NeuroNet_Misc.mqh:421-462 -> Concat_HiddenGradient."""
+        for b in range(self.batch):
+            BACKEND.Concat_HiddenGradient(self.conc_w, self.gradient[b], prev.output[b], self.second[b],
+                                          prev.gradient[b], self.second_grad[b], self.neurons, self.in1, self.in2,
+                                          prev.activation, self.second_activation, gsize=(self.in1 + self.in2,))
+
+    def update(self, prev):
+        """NeuroNet_Misc.mqh:465-560 -> Concat_UpdateWeightsAdam on the batch-mean gradient."""
+        n_out, n_col = self.neurons, self.in1 + self.in2 + 1
+        inps = [np.concatenate([prev.output[b], self.second[b], np.ones(1, F32)]) for b in range(self.batch)]
+        self.last_grad = np.mean([self.gradient[b][:, None] * inps[b][None, :] for b in range(self.batch)],
+                                 axis=0, dtype=np.float64).astype(F32).reshape(-1)
+        self.last_grad_abs = np.mean([np.abs(self.gradient[b])[:, None] * np.abs(inps[b])[None, :]
+                                      for b in range(self.batch)], axis=0).reshape(-1)
+        if GRAD_HOOK is not None:
+            self.last_grad = GRAD_HOOK(self.last_grad)
+        elif self.batch == 1:
+            BACKEND.Concat_UpdateWeightsAdam(self.conc_w, self.gradient[0], prev.output[0], self.second[0],
+                                             self.conc_m, self.conc_v, self.in1, self.in2, self.next_lt(), B1, B2,
+                                             gsize=(n_out, n_col))
+            return
+        K.concat_adam_apply(self.conc_w, self.last_grad.reshape(n_out, n_col), self.conc_m, self.conc_v, self.in1,
+                            self.in2, self.next_lt(), B1, B2, n_out, n_col)
+
+
+def soft_update(target: OLayer, source: OLayer, tau: float, adam: bool) -> None:
+    """CNeuronBaseOCL::WeightsUpdate (NeuroNet_Core.mqh:20283-20370) and the CNeuronConcatenate
+    override (NeuroNet_Misc.mqh:628-676): SoftUpdateAdam with the target's moments, or SoftUpdate."""
+    pairs = []
+    if getattr(target, "outputs", 0):
+        pairs.append((target.weights, source.weights, target.m, target.v))
+    if isinstance(target, OConcat):
+        pairs.append((target.conc_w, source.conc_w, target.conc_m, target.conc_v))
+    for t, s, m, v in pairs:
+        if adam:
+            BACKEND.SoftUpdateAdam(t, s, m, v, tau, B1, B2, gsize=(t.size,))
+        else:
+            BACKEND.SoftUpdate(t, s, tau, gsize=(t.size,))
+
+
+def _backward_from_output_grad(net: ONet) -> None:
+    """ONet.backward without the output gradient (already in the last layer's gradient)."""
+    for l in range(len(net.layers) - 2, -1, -1):
+        cur, nxt = net.layers[l], net.layers[l + 1]
+        if type(nxt) is ODense:
+            cur.hidden_gradient(nxt)
+        else:
+            nxt.input_gradient(_as(cur, nxt.batch))
+
+
+class OSACAgent:
+    """The SAC step of nn_in_trading_b200/sac.py over oracle layers, in the same order: target value,
+    critic updates, actor update against the updated critics, Polyak averaging of the targets."""
+
+    def __init__(self, spec, batch, weights):
+        S, A, H, B = spec.state, spec.action, spec.hidden, batch
+        self.spec, self.B = spec, B
+
+        def actor():
+            return [ODense(S, K.NONE, B, H), ODense(H, K.LRELU, B, H), ODense(H, K.LRELU, B, 2 * A),
+                    ODense(2 * A, K.NONE, B, 0)]
+
+        def critic():
+            return [ODense(S, K.NONE, B, 0), OConcat(H, S, A, K.LRELU, B, H), ODense(H, K.LRELU, B, 1),
+                    ODense(1, K.NONE, B, 0)]
+
+        self.actor = ONet(actor())
+        self.actor_next = ONet(actor())
+        self.critics = [ONet(critic()) for _ in range(2)]
+        self.critics_pi = [ONet(critic()) for _ in range(2)]
+        self.targets = [ONet(critic()) for _ in range(2)]
+        for layer, w in zip(self.actor.layers[:3], weights["actor"]):
+            layer.weights[:] = w
+        for k in range(2):
+            cw = weights["critics"][k]
+            for net in (self.critics[k], self.targets[k]):
+                net.layers[1].conc_w[:] = cw["conc"]
+                net.layers[1].weights[:] = cw["w1"]
+                net.layers[2].weights[:] = cw["w2"]
+        for view, src in zip(self.actor_next.layers, self.actor.layers):
+            _share(view, src)
+        for k in range(2):
+            for view, src in zip(self.critics_pi[k].layers, self.critics[k].layers):
+                _share(view, src)
+        self.y = np.zeros(B, F32)
+
+    def step(self, batch: dict) -> None:
+        sp, B, A = self.spec, self.B, self.spec.action
+        s = batch["s"].reshape(B, -1)
+        s2 = batch["s2"].reshape(B, -1)
+        # 1. target value
+        self.actor_next.forward(s2)
+        self.a_next = np.zeros(B * A, F32)
+        self.logp_next = np.zeros(B, F32)
+        K.SACGaussianPolicy(self.actor_next.layers[-1].output.reshape(-1), batch["eps1"], self.a_next,
+                            self.logp_next, A, gsize=(B,))
+        for t in self.targets:
+            t.layers[1].second[...] = self.a_next.reshape(B, A)
+            t.forward(s2)
+        K.SACTargetValue(self.targets[0].layers[-1].output.reshape(-1), self.targets[1].layers[-1].output.reshape(-1),
+                         batch["r"], batch["done"], self.logp_next, self.y, sp.gamma, sp.alpha, gsize=(B,))
+        # 2. critics
+        for c in self.critics:
+            c.layers[1].second[...] = batch["a"].reshape(B, A)
+            c.forward(s)
+        for c in self.critics:
+            c.backward(self.y.reshape(B, 1))
+        for c in self.critics:
+            c.update()
+        # 3. actor against the updated critics
+        self.actor.forward(s)
+        self.a_pi = np.zeros(B * A, F32)
+        self.logp = np.zeros(B, F32)
+        K.SACGaussianPolicy(self.actor.layers[-1].output.reshape(-1), batch["eps2"], self.a_pi, self.logp, A,
+                            gsize=(B,))
+        for c in self.critics_pi:
+            c.layers[1].second[...] = self.a_pi.reshape(B, A)
+            c.forward(s)
+            c.layers[-1].gradient[...] = 1.0
+        for c in self.critics_pi:
+            _backward_from_output_grad(c)
+        out = self.actor.layers[-1]
+        K.SACPolicyGradient(out.output.reshape(-1), batch["eps2"], self.a_pi,
+                            self.critics_pi[0].layers[-1].output.reshape(-1),
+                            self.critics_pi[1].layers[-1].output.reshape(-1),
+                            self.critics_pi[0].layers[1].second_grad.reshape(-1),
+                            self.critics_pi[1].layers[1].second_grad.reshape(-1), out.gradient.reshape(-1), A,
+                            sp.alpha, gsize=(B,))
+        _backward_from_output_grad(self.actor)
+        self.actor.update()
+        # 4. Polyak averaging
+        for k in range(2):
+            for tl, cl in zip(self.targets[k].layers, self.critics[k].layers):
+                soft_update(tl, cl, sp.tau, sp.soft_update_adam)
+
+
+def _share(view: OLayer, src: OLayer) -> None:
+    """`view` uses `src`'s parameter arrays (the same weights under a second set of activations)."""
+    for name in ("weights", "m", "v", "conc_w", "conc_m", "conc_v"):
+        if hasattr(src, name):
+            setattr(view, name, getattr(src, name))

@@ -270,9 +270,31 @@ def _lstm_cases():
     return cases
 
 
+def _concat_cases():
+    """Concat_* (NeuroNet.cl:3628-3862): the critic input layer of state + action."""
+    cases = []
+    for in1, in2, n_out in [(240, 6, 17), (3, 5, 4), (1, 1, 2), (63, 2, 9)]:
+        nw = n_out * (in1 + in2 + 1)
+        k = 1 / np.sqrt(in1 + in2 + 1)
+        for act in (LRELU, TANH, NONE):
+            cases.append(Case(f"Concat_FeedForward/{in1}+{in2}x{n_out}/act{act}", "Concat_FeedForward",
+                              [A(nw, "uniform", k), A(in1), A(in2), A(n_out, "zeros"), in1, in2, act], (n_out,)))
+        for a1, a2 in ((LRELU, NONE), (SIGMOID, TANH)):
+            cases.append(Case(f"Concat_HiddenGradient/{in1}+{in2}x{n_out}/act{a1}-{a2}", "Concat_HiddenGradient",
+                              [A(nw, "uniform", k), A(n_out, "grad"), A(in1, f"act:{a1}"), A(in2, f"act:{a2}"),
+                               A(in1, "zeros"), A(in2, "zeros"), n_out, in1, in2, a1, a2], (in1 + in2,)))
+        cases.append(Case(f"Concat_UpdateWeightsAdam/{in1}+{in2}x{n_out}", "Concat_UpdateWeightsAdam",
+                          [A(nw, "uniform", k), A(n_out, "grad"), A(in1), A(in2), A(nw, "small"),
+                           A(nw, "pos", 1e-5), in1, in2, 3e-4, 0.9, 0.999], (n_out, in1 + in2 + 1)))
+        cases.append(Case(f"Concat_UpdateWeightsMomentum/{in1}+{in2}x{n_out}", "Concat_UpdateWeightsMomentum",
+                          [A(nw, "uniform", k), A(n_out, "grad"), A(in1), A(in2), A(nw, "small"), in1, in2,
+                           3e-4, 0.9], (n_out, in1 + in2 + 1)))
+    return cases
+
+
 def all_cases() -> list[Case]:
     return (_dense_cases() + _conv_cases() + _attention_cases() + _norm_cases() + _batchnorm_cases() + _lstm_cases()
-            + _attention2_cases())
+            + _attention2_cases() + _concat_cases())
 
 
 def prepare_inputs(case: Case, seed: int) -> list:

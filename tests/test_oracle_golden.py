@@ -39,6 +39,6 @@ def test_oracle_matches_reference_kernels(case, golden):
 
 def test_every_in_scope_kernel_has_golden_cases():
     covered = {c.kernel for c in CASES}
-    restated = set(K.KERNELS)
+    restated = set(K.KERNELS) - K.LIBRARY_KERNELS
     missing = restated - covered
     assert not missing, f"restated kernels without golden cases: {sorted(missing)}"

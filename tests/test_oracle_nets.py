@@ -78,3 +78,45 @@ def test_attention_encoder_numpy_oracle_matches_reference_kernels():
             check_weights(f"L{i} {name}", a[1].w[i][name][0], b[1].w[i][name][0], b[1].last_grads[(i, name)],
                           b[1].last_grads_abs[(i, name)])
             check_close(f"L{i} {name} v", a[1].w[i][name][2], b[1].w[i][name][2])
+
+
+def _sac_params(agent):
+    """(label, array, updating layer or None) of every parameter array of an oracle SAC agent."""
+    out = []
+    for name, net, upd in ([("actor", agent.actor, True)] + [(f"critic{k}", c, True) for k, c in enumerate(agent.critics)]
+                           + [(f"target{k}", t, False) for k, t in enumerate(agent.targets)]):
+        for li, layer in enumerate(net.layers):
+            for attr in ("weights", "m", "v", "conc_w", "conc_m", "conc_v"):
+                if hasattr(layer, attr):
+                    nxt = (layer if attr.startswith("conc") else net.layers[li + 1]) if upd else None
+                    out.append((f"{name} layer{li} {attr}", layer, attr, nxt))
+    return out
+
+
+def test_sac_step_numpy_oracle_matches_reference_kernels():
+    """The SAC step at batch 1, where every dense and Concat kernel call goes through the reference's
+    own kernels (UpdateWeightsAdam, Concat_UpdateWeightsAdam, SoftUpdate included)."""
+    from nn_in_trading_b200.sac import SACSpec, sac_data, sac_weights
+    spec = SACSpec(state=24, action=3, hidden=32)
+    w = sac_weights(spec)
+    d = sac_data(spec, 1, 4)
+    agents = {kind: O.OSACAgent(spec, 1, w) for kind in ("numpy", "reference")}
+    try:
+        for s in range(4):
+            bt = {k: v[s] for k, v in d.items()}
+            for kind in ("numpy", "reference"):
+                O.use_backend(kind)
+                agents[kind].step(bt)
+            a, b = agents["numpy"], agents["reference"]
+            check_close(f"step{s} target values", a.y, b.y)
+            check_close(f"step{s} log-probs", a.logp, b.logp)
+            check_close(f"step{s} actor output gradient", a.actor.layers[-1].gradient, b.actor.layers[-1].gradient)
+            for (label, la, attr, upd), (_, lb, _, _) in zip(_sac_params(a), _sac_params(b)):
+                got, ref = getattr(la, attr), getattr(lb, attr)
+                if upd is not None and attr in ("weights", "conc_w"):
+                    check_weights(f"step{s} {label}", got, ref, upd.last_grad, upd.last_grad_abs)
+                else:
+                    check_close(f"step{s} {label}", got, ref)
+                got[:] = ref
+    finally:
+        O.use_backend("numpy")
