@@ -110,7 +110,17 @@ NN_API void *nn_buffer_device_ptr(int handle);
 /* ---------------------------------------------------------------- kernels */
 /* COpenCL::KernelCreate(id, name) via the CreateKernel macro
  * (NeuroNet_Definitions.mqh:56-58, NeuroNet_Core.mqh:23192-23651).
- * name: a NeuroNet.cl kernel name.  id: any value in [0, 65535]. */
+ * name: a NeuroNet.cl kernel name.  id: any value in [0, 65535].
+ * Beyond the NeuroNet.cl names, three kernels of this library (no reference counterpart) serve a
+ * squashed-Gaussian soft actor-critic update; each covers global[0] * batch samples:
+ *   "SACGaussianPolicy"  (outputs, noise, actions, log_probs, int action_dim)
+ *       a = tanh(mu + exp(clamp(log_std, -20, 2)) eps), outputs [n][2A] = (mu, log_std)
+ *   "SACTargetValue"     (q1, q2, reward, done, log_probs, target, float gamma, float alpha)
+ *       y = r + gamma (1 - done) (min(q1, q2) - alpha log pi)
+ *   "SACPolicyGradient"  (outputs, noise, actions, q1, q2, dq1, dq2, gradient, int action_dim,
+ *                         float alpha)
+ *       the ascent direction of min(q1, q2) - alpha log pi for (mu, log_std), each entry
+ *       clamped to +-1e-2 like every output gradient of the reference. */
 NN_API int nn_kernel_create(int id, const char *name);
 /* Same, for callers whose strings are UTF-16 (MQL5 `string`). */
 NN_API int nn_kernel_create_w(int id, const unsigned short *name_utf16);

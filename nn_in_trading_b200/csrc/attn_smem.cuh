@@ -47,9 +47,16 @@ __device__ __forceinline__ void async_rows(float *dst, int ld, const float *src,
       }
     }
     asm volatile("cp.async.commit_group;\n" ::);
-  } else {
-    for (int r = warp; r < rows; r += nw)
-      for (int c = lane; c < cols; c += 32) dst[r * ld + c] = src[(size_t)r * stride + c];
+  } else {  // rows not 16-byte aligned: 4-byte copies, still all in flight
+    for (int r = warp; r < rows; r += nw) {
+      const float *s = src + (size_t)r * stride;
+      float *d = dst + r * ld;
+      for (int c = lane; c < cols; c += 32) {
+        unsigned saddr = (unsigned)__cvta_generic_to_shared(d + c);
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(saddr), "l"(s + c));
+      }
+    }
+    asm volatile("cp.async.commit_group;\n" ::);
   }
 }
 __device__ __forceinline__ void async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::); }
@@ -57,17 +64,21 @@ __device__ __forceinline__ void async_wait_all() { asm volatile("cp.async.wait_g
 // out[r][c] (r < R, c < N) = sum_k A[r*lda + k] * Bm[k*ldb + c], A rows via float4,
 // computed by warps over 4-row blocks and lanes over columns c = lane + 32 j.
 // The functor `emit(r, c, acc)` receives each result.  DPL = ceil(N / 32) <= 4.
-template <int DPL, class Emit>
+// SUB = 2 (N <= 16): each half-warp takes its own 4-row block, lanes c = lane % 16.
+template <int DPL, class Emit, int SUB = 1>
 __device__ __forceinline__ void rows_times_cols(const float *A, int lda, const float *Bm, int ldb, int R, int N,
                                                 int K, Emit emit) {
+  constexpr int CL = 32 / SUB;  // column lanes
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (int r0 = warp * 4; r0 < R; r0 += nw * 4) {
+  const int cl = lane % CL, sub = lane / CL;
+  for (int rb = warp * 4 * SUB; rb < R; rb += nw * 4 * SUB) {
+    const int r0 = rb + 4 * sub;
     float acc[4][DPL];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int j = 0; j < DPL; ++j) acc[i][j] = 0.f;
-    const int nr = min(4, R - r0);
+    const int nr = max(0, min(4, R - r0));
     int k = 0;
     for (; k + 4 <= K; k += 4) {
       float4 a[4];
@@ -76,7 +87,7 @@ __device__ __forceinline__ void rows_times_cols(const float *A, int lda, const f
         a[i] = (i < nr) ? *reinterpret_cast<const float4 *>(A + (r0 + i) * lda + k) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
       for (int j = 0; j < DPL; ++j) {
-        int c = lane + 32 * j;
+        int c = cl + CL * j;
         if (c < N) {
           float b0 = Bm[(k + 0) * ldb + c], b1 = Bm[(k + 1) * ldb + c];
           float b2 = Bm[(k + 2) * ldb + c], b3 = Bm[(k + 3) * ldb + c];
@@ -93,7 +104,7 @@ __device__ __forceinline__ void rows_times_cols(const float *A, int lda, const f
     for (; k < K; ++k) {
 #pragma unroll
       for (int j = 0; j < DPL; ++j) {
-        int c = lane + 32 * j;
+        int c = cl + CL * j;
         if (c < N) {
           float b = Bm[k * ldb + c];
 #pragma unroll
@@ -107,7 +118,7 @@ __device__ __forceinline__ void rows_times_cols(const float *A, int lda, const f
       if (i >= nr) break;
 #pragma unroll
       for (int j = 0; j < DPL; ++j) {
-        int c = lane + 32 * j;
+        int c = cl + CL * j;
         if (c < N) emit(r0 + i, c, acc[i][j]);
       }
     }
@@ -115,28 +126,32 @@ __device__ __forceinline__ void rows_times_cols(const float *A, int lda, const f
 }
 
 // out[r][c] = sum_k At[k*lda + r] * Bm[k*ldb + c]  (A given transposed: column
-// blocks of At read as float4 broadcasts).
-template <int DPL, class Emit>
+// blocks of At read as float4 broadcasts).  SUB as in rows_times_cols.
+template <int DPL, class Emit, int SUB = 1>
 __device__ __forceinline__ void cols_times_cols(const float *At, int lda, const float *Bm, int ldb, int R, int N,
                                                 int K, Emit emit) {
+  constexpr int CL = 32 / SUB;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (int r0 = warp * 4; r0 < R; r0 += nw * 4) {
+  const int cl = lane % CL, sub = lane / CL;
+  for (int rb = warp * 4 * SUB; rb < R; rb += nw * 4 * SUB) {
+    const int r0 = rb + 4 * sub;
     float acc[4][DPL];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int j = 0; j < DPL; ++j) acc[i][j] = 0.f;
-    const int nr = min(4, R - r0);
+    const int nr = max(0, min(4, R - r0));
+    const bool live = nr > 0;  // the float4 column block lies in the padded row
     int k = 0;
     for (; k + 4 <= K; k += 4) {  // four k per iteration: all loads issued before the FMAs
       float4 a[4];
       float b[4][DPL];
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
-        a[kk] = *reinterpret_cast<const float4 *>(At + (k + kk) * lda + r0);  // lda padded: stays in the row
+        a[kk] = live ? *reinterpret_cast<const float4 *>(At + (k + kk) * lda + r0) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int j = 0; j < DPL; ++j) {
-          int c = lane + 32 * j;
+          int c = cl + CL * j;
           b[kk][j] = c < N ? Bm[(k + kk) * ldb + c] : 0.f;
         }
       }
@@ -151,10 +166,10 @@ __device__ __forceinline__ void cols_times_cols(const float *At, int lda, const 
         }
     }
     for (; k < K; ++k) {
-      float4 a = *reinterpret_cast<const float4 *>(At + k * lda + r0);
+      float4 a = live ? *reinterpret_cast<const float4 *>(At + k * lda + r0) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
       for (int j = 0; j < DPL; ++j) {
-        int c = lane + 32 * j;
+        int c = cl + CL * j;
         if (c < N) {
           float b = Bm[k * ldb + c];
           acc[0][j] = fmaf(a.x, b, acc[0][j]);
@@ -169,7 +184,7 @@ __device__ __forceinline__ void cols_times_cols(const float *At, int lda, const 
       if (i >= nr) break;
 #pragma unroll
       for (int j = 0; j < DPL; ++j) {
-        int c = lane + 32 * j;
+        int c = cl + CL * j;
         if (c < N) emit(r0 + i, c, acc[i][j]);
       }
     }
@@ -192,9 +207,19 @@ __global__ void mh_score_smem_kernel(const float *__restrict__ qkv, float *__res
   const float *base = qkv + b * (size_t)U * 3 * H * D;
   const size_t rs = (size_t)3 * H * D;
   async_rows(Qs, ldq, base + (size_t)h * D, rs, U, D);
-  for (int e = threadIdx.x; e < U * D; e += blockDim.x) {
-    int k = e / D, d = e - k * D;
-    Kt[d * ldk + k] = nan0(base[(size_t)k * rs + (size_t)(H + h) * D + d]);
+  // K transposed into smem: eight loads of a thread in flight before its stores
+  for (int e0 = threadIdx.x; e0 < U * D; e0 += 8 * blockDim.x) {
+    float kv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int e = e0 + j * blockDim.x;
+      kv[j] = e < U * D ? base[(size_t)(e / D) * rs + (size_t)(H + h) * D + e % D] : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int e = e0 + j * blockDim.x;
+      if (e < U * D) Kt[(e % D) * ldk + e / D] = nan0(kv[j]);
+    }
   }
   for (int e = threadIdx.x; e < U * (ldq - D); e += blockDim.x) Qs[(e / (ldq - D)) * ldq + D + e % (ldq - D)] = 0.f;
   async_wait_all();
@@ -263,7 +288,7 @@ __global__ void mh_score_smem_kernel(const float *__restrict__ qkv, float *__res
 
 // -------------------------------------------------------------- out (smem)
 // O = S V for one (sample, head) (MHAttentionOut, NeuroNet.cl:1730-1759).
-template <int DPL>
+template <int DPL, int SUB>
 __global__ void mh_out_smem_kernel(const float *__restrict__ scores, const float *__restrict__ qkv,
                                    float *__restrict__ out, int U, int H, int D) {
   extern __shared__ float4 sm4[];
@@ -279,14 +304,15 @@ __global__ void mh_out_smem_kernel(const float *__restrict__ scores, const float
   async_wait_all();
   __syncthreads();
   float *ob = out + b * (size_t)U * H * D + (size_t)h * D;
-  rows_times_cols<DPL>(Ss, lds, Vs, D, U, D, U, [&](int u, int d, float acc) { ob[(size_t)u * H * D + d] = acc; });
+  auto emit = [&](int u, int d, float acc) { ob[(size_t)u * H * D + d] = acc; };
+  rows_times_cols<DPL, decltype(emit), SUB>(Ss, lds, Vs, D, U, D, U, emit);
 }
 
 // ------------------------------------------------- inside gradients (smem)
 // MHAttentionInsideGradients (NeuroNet.cl:1777-1845) for one (sample, head), in
 // the reassociated form dV = S^T g, A = S V0, C = S o (V0^T - A),
 // dQ = g o (C K) / koef, dK = C^T (g o Q) / koef.
-template <int DPL>
+template <int DPL, int SUB>
 __global__ void mh_grad_smem_kernel(const float *__restrict__ qkv, float *__restrict__ qkv_g,
                                     const float *__restrict__ scores, const float *__restrict__ grad, int U, int H,
                                     int D, float koef) {
@@ -298,7 +324,6 @@ __global__ void mh_grad_smem_kernel(const float *__restrict__ qkv, float *__rest
   float *Gs = Ks + U * D;         // [U][D]
   float *GQ = Gs + U * D;         // [U][D]   Q, then g o Q
   float *V0 = GQ + U * D;         // [lds]
-  float *Av = V0 + lds;           // [lds]
   const int h = blockIdx.x;
   const size_t b = blockIdx.y;
   const size_t rs = (size_t)3 * H * D;
@@ -315,34 +340,29 @@ __global__ void mh_grad_smem_kernel(const float *__restrict__ qkv, float *__rest
   __syncthreads();
   float *gb = qkv_g + b * (size_t)U * rs;
   // dV[u][d] = sum_i S[i][u] g[i][d]
-  cols_times_cols<DPL>(Cs, lds, Gs, D, U, D, U,
-                       [&](int u, int d, float acc) { gb[(size_t)u * rs + (size_t)(2 * H + h) * D + d] = acc; });
-  // A[q] = sum_v S[q][v] V0[v]
+  auto emit_v = [&](int u, int d, float acc) { gb[(size_t)u * rs + (size_t)(2 * H + h) * D + d] = acc; };
+  cols_times_cols<DPL, decltype(emit_v), SUB>(Cs, lds, Gs, D, U, D, U, emit_v);
+  for (int e = threadIdx.x; e < U * D; e += blockDim.x) GQ[e] *= Gs[e];  // g o Q
+  __syncthreads();  // every dV read of S is done before S becomes C
+  // per query row (one warp): A[q] = sum_v S[q][v] V0[v], then C[q][u] = S[q][u] (V0[u] - A[q])
   {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     for (int q = warp; q < U; q += nw) {
-      float s = 0.f;
-      for (int v = lane; v < U; v += 32) s += Cs[q * lds + v] * V0[v];
-      s = warp_sum(s);
-      if (lane == 0) Av[q] = s;
+      float *row = Cs + q * lds;
+      float a = 0.f;
+      for (int v = lane; v < U; v += 32) a += row[v] * V0[v];
+      a = warp_sum(a);
+      for (int u = lane; u < U; u += 32) row[u] *= (V0[u] - a);
     }
   }
   __syncthreads();
-  // C = S o (V0^T - A), GQ = g o Q
-  for (int e = threadIdx.x; e < U * U; e += blockDim.x) {
-    int q = e / U, u = e - q * U;
-    Cs[q * lds + u] *= (V0[u] - Av[q]);
-  }
-  for (int e = threadIdx.x; e < U * D; e += blockDim.x) GQ[e] *= Gs[e];
-  __syncthreads();
   const float inv = 1.f / koef;
   // dK[u][d] = sum_q C[q][u] (g o Q)[q][d] / koef
-  cols_times_cols<DPL>(Cs, lds, GQ, D, U, D, U,
-                       [&](int u, int d, float acc) { gb[(size_t)u * rs + (size_t)(H + h) * D + d] = acc * inv; });
+  auto emit_k = [&](int u, int d, float acc) { gb[(size_t)u * rs + (size_t)(H + h) * D + d] = acc * inv; };
+  cols_times_cols<DPL, decltype(emit_k), SUB>(Cs, lds, GQ, D, U, D, U, emit_k);
   // dQ[u][d] = g[u][d] / koef * sum_k C[u][k] K[k][d]
-  rows_times_cols<DPL>(Cs, lds, Ks, D, U, D, U, [&](int u, int d, float acc) {
-    gb[(size_t)u * rs + (size_t)h * D + d] = Gs[u * D + d] * acc * inv;
-  });
+  auto emit_q = [&](int u, int d, float acc) { gb[(size_t)u * rs + (size_t)h * D + d] = Gs[u * D + d] * acc * inv; };
+  rows_times_cols<DPL, decltype(emit_q), SUB>(Cs, lds, Ks, D, U, D, U, emit_q);
 }
 
 }  // namespace nn

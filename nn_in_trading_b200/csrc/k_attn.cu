@@ -180,7 +180,8 @@ static int k_mh_attention_out(Launch &L) {
     size_t sm = (size_t)(units * pad4(units) + units * dim) * sizeof(float);
     int dpl = (dim + 31) / 32;
     if (sm <= kSmemCap && dpl <= 2) {
-      auto fn = dpl <= 1 ? mh_out_smem_kernel<1> : mh_out_smem_kernel<2>;
+      // head dimensions up to 16: half-warps take separate row blocks (no idle lanes)
+      auto fn = dim <= 16 ? mh_out_smem_kernel<1, 2> : dpl <= 1 ? mh_out_smem_kernel<1, 1> : mh_out_smem_kernel<2, 1>;
       cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
       fn<<<dim3(heads, L.B), 256, sm, L.stream>>>(scores, qkv, out, units, heads, dim);
       NN_CHECK_LAUNCH(L);
@@ -279,7 +280,8 @@ static int k_mh_attention_inside_gradients(Launch &L) {
     size_t sm = (size_t)(units * pad4(units) + 3 * units * dim + 2 * pad4(units)) * sizeof(float);
     int dpl = (dim + 31) / 32;
     if (sm <= kSmemCap && dpl <= 2) {
-      auto fn = dpl <= 1 ? mh_grad_smem_kernel<1> : mh_grad_smem_kernel<2>;
+      auto fn = dim <= 16 ? mh_grad_smem_kernel<1, 2>
+                          : dpl <= 1 ? mh_grad_smem_kernel<1, 1> : mh_grad_smem_kernel<2, 1>;
       cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
       fn<<<dim3(heads, L.B), 256, sm, L.stream>>>(qkv, qkv_g, scores, grad, units, heads, dim, koef);
       NN_CHECK_LAUNCH(L);

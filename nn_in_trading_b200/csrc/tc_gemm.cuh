@@ -750,22 +750,14 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + prod_warps(A
             const int n = n0 + c_begin + 32 * k + lane;
             colv[k] = n < s.N ? ep.col(n, z) : 0.f;
           }
-          if (!mbar_wait(&accf[b], u & 1, &abort_flag)) {
-            fail(kErrDoneWait);
-            break;
-          }
-          tc_fence_after();
           const int mw = m0 + quarter * 32;
-#pragma unroll
-          for (int k = 0; k < NCH; ++k) {
-            const int c = c_begin + 32 * k;
-            if (n0 + c >= s.N) break;
-            const int nc = n0 + c;
-            // the second input of this thread's row, in flight during the tensor-memory load
-            float y[32];
+          // the second input of this thread's row for chunk k (zeros without one)
+          float y[32];
+          auto load_aux = [&](int k) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) y[j] = 0.f;
             if constexpr (ep_has_aux<EP>::value) {
+              const int nc = n0 + c_begin + 32 * k;
               if (mw + lane < s.M) {
 #pragma unroll
                 for (int q = 0; q < 8; ++q)
@@ -778,6 +770,20 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + prod_warps(A
                   }
               }
             }
+          };
+          // the first chunk's second input is in flight while the MMAs of the tile finish
+          load_aux(0);
+          if (!mbar_wait(&accf[b], u & 1, &abort_flag)) {
+            fail(kErrDoneWait);
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < NCH; ++k) {
+            const int c = c_begin + 32 * k;
+            if (n0 + c >= s.N) break;
+            const int nc = n0 + c;
+            if (k > 0) load_aux(k);  // in flight during the tensor-memory load
             float v[32];
             if (nk > 0) {
               tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(b * BN + c), v);

@@ -149,7 +149,8 @@ def _conv_cases():
 
 def _attention_cases():
     cases = []
-    for units, heads, dim in [(5, 2, 4), (12, 3, 8), (17, 2, 5), (33, 4, 16), (1, 1, 3), (120, 2, 32), (200, 1, 6)]:
+    for units, heads, dim in [(5, 2, 4), (12, 3, 8), (17, 2, 5), (33, 4, 16), (1, 1, 3), (120, 2, 32), (200, 1, 6),
+                              (63, 8, 16)]:
         n = units * 3 * heads * dim
         for mask in (0, 1):
             cases.append(Case(f"MHAttentionScore/{units}-{heads}-{dim}/m{mask}", "MHAttentionScore",
