@@ -89,3 +89,60 @@ def test_shard_rejects_uneven_split():
     assert dp.shard(256, 3, 4) == (192, 256)
     with pytest.raises(ValueError):
         dp.shard(10, 0, 3)
+
+
+def _sac_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import torch
+    from nn_in_trading_b200 import dp
+    from nn_in_trading_b200.sac import SACSpec, sac_data, sac_weights
+    from oracle import nets as O
+    dist = dp.init_host_group("gloo", timeout_s=60)
+    try:
+        spec = SACSpec(state=10, action=2, hidden=12)
+        B = 6
+        lo, hi = dp.shard(B, rank, world)
+        data = sac_data(spec, B, 2)
+        width = {"s": spec.state, "a": spec.action, "r": 1, "s2": spec.state, "done": 1, "eps1": spec.action,
+                 "eps2": spec.action}
+
+        def mean_over_ranks(G):
+            t = torch.from_numpy(np.ascontiguousarray(G, dtype=np.float64))
+            dist.all_reduce(t)
+            return (t / world).numpy().astype(np.float32)
+
+        O.use_backend("numpy")
+        O.set_grad_hook(mean_over_ranks)
+        agent = O.OSACAgent(spec, hi - lo, sac_weights(spec))
+        for s in range(2):
+            agent.step({k: v[s][lo * width[k]:hi * width[k]] for k, v in data.items()})
+        O.set_grad_hook(None)
+        np.savez(os.path.join(out_dir, f"sac{rank}.npz"), *[l.weights for l in agent.actor.layers[:3]],
+                 agent.critics[0].layers[1].conc_w, agent.targets[1].layers[1].conc_w)
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def test_two_rank_sac_equals_full_batch(tmp_path):
+    """The SAC step's two gradient averages (critics, then the actor) on CPU ranks equal one process
+    stepping the whole replay batch."""
+    world = 2
+    mp.start_processes(_sac_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method="spawn",
+                       join=True)
+    from nn_in_trading_b200.sac import SACSpec, sac_data, sac_weights
+    from oracle import nets as O
+    O.use_backend("numpy")
+    spec = SACSpec(state=10, action=2, hidden=12)
+    full = O.OSACAgent(spec, 6, sac_weights(spec))
+    data = sac_data(spec, 6, 2)
+    for s in range(2):
+        full.step({k: v[s] for k, v in data.items()})
+    ref = [l.weights for l in full.actor.layers[:3]] + [full.critics[0].layers[1].conc_w,
+                                                        full.targets[1].layers[1].conc_w]
+    r0, r1 = np.load(tmp_path / "sac0.npz"), np.load(tmp_path / "sac1.npz")
+    for i, w in enumerate(ref):
+        a, b = r0[f"arr_{i}"], r1[f"arr_{i}"]
+        np.testing.assert_array_equal(a, b)
+        np.testing.assert_allclose(a, w, rtol=0, atol=1e-5 * max(1.0, np.abs(w).max()))

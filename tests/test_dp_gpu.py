@@ -87,3 +87,74 @@ def test_two_gpu_data_parallel_equals_full_batch(tmp_path, replay):
             np.testing.assert_array_equal(a, b)
             # two steps from the same start: compare the second update against the oracle's
             check_weights(f"L{i} {n}", a, enc.w[i][n][0], enc.last_grads[(i, n)], enc.last_grads_abs[(i, n)])
+
+
+SAC_B = 8
+
+
+def _sac_spec():
+    from nn_in_trading_b200.sac import SACSpec
+    return SACSpec(state=12, action=3, hidden=16)
+
+
+def _sac_worker(rank, world, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    from nn_in_trading_b200 import Context, dp
+    from nn_in_trading_b200.sac import SACAgent, sac_data, sac_weights
+    dist = dp.init_host_group("gloo", timeout_s=120)
+    try:
+        ctx = Context(rank)
+        dp.join_dp(ctx, rank, world)
+        spec = _sac_spec()
+        lo, hi = dp.shard(SAC_B, rank, world)
+        data = sac_data(spec, SAC_B, 2)
+        width = {"s": spec.state, "a": spec.action, "r": 1, "s2": spec.state, "done": 1, "eps1": spec.action,
+                 "eps2": spec.action}
+        agent = SACAgent(ctx, spec, hi - lo, sac_weights(spec), dp=True)
+        agent.capture()
+        for s in range(2):
+            agent.set_batch({k: v[s][lo * width[k]:hi * width[k]] for k, v in data.items()})
+            agent.step()
+        out = {f"actor{i}": ctx.read(agent.actor[i].weights) for i in range(3)}
+        for k in range(2):
+            out[f"critic{k}_conc"] = ctx.read(agent.critics[k][1].conc_w)
+            out[f"critic{k}_w1"] = ctx.read(agent.critics[k][1].weights)
+            out[f"target{k}_conc"] = ctx.read(agent.targets[k][1].conc_w)
+        np.savez(os.path.join(out_dir, f"sac_rank{rank}.npz"), **out)
+        ctx.dp_shutdown()
+        ctx.close()
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
+def test_two_gpu_sac_equals_full_batch(tmp_path):
+    """Two ranks of 4 transitions: the critic and actor gradients are averaged in two update regions;
+    weights stay identical on both ranks and equal the oracle's 8-transition step."""
+    import torch.multiprocessing as mp
+
+    from nn_in_trading_b200.sac import sac_data, sac_weights
+    from oracle import nets as O
+    from tests.parity import check_close, check_weights
+    world = 2
+    mp.start_processes(_sac_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method="spawn",
+                       join=True)
+    spec = _sac_spec()
+    O.use_backend("numpy")
+    oracle = O.OSACAgent(spec, SAC_B, sac_weights(spec))
+    data = sac_data(spec, SAC_B, 2)
+    for s in range(2):
+        oracle.step({k: v[s] for k, v in data.items()})
+    r0, r1 = np.load(tmp_path / "sac_rank0.npz"), np.load(tmp_path / "sac_rank1.npz")
+    for name in r0.files:
+        np.testing.assert_array_equal(r0[name], r1[name])
+    for i in range(3):
+        upd = oracle.actor.layers[i + 1]
+        check_weights(f"actor{i}", r0[f"actor{i}"], oracle.actor.layers[i].weights, upd.last_grad, upd.last_grad_abs)
+    for k in range(2):
+        c = oracle.critics[k].layers
+        check_weights(f"critic{k} conc", r0[f"critic{k}_conc"], c[1].conc_w, c[1].last_grad, c[1].last_grad_abs)
+        check_weights(f"critic{k} w1", r0[f"critic{k}_w1"], c[1].weights, c[2].last_grad, c[2].last_grad_abs)
+        check_close(f"target{k} conc", r0[f"target{k}_conc"], oracle.targets[k].layers[1].conc_w)
