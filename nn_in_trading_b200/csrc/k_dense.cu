@@ -71,6 +71,35 @@ __global__ void colsum_rows_kernel(float *p, const float *g, int M, int rows, lo
   }
 }
 
+__global__ void wgrad_small_m_kernel(float *p, const float *A, long long lda, const float *X, long long ldx, int M,
+                                     int N, int rows, int kchunk, int ldp) {
+  __shared__ float red[8][kSmallM][33];
+  const int n = blockIdx.x * 32 + threadIdx.x;  // n == N: the bias column (input 1)
+  const int r0 = blockIdx.y * kchunk, r1 = min(rows, r0 + kchunk);
+  float s[kSmallM];
+#pragma unroll
+  for (int m = 0; m < kSmallM; ++m) s[m] = 0.f;
+  if (n <= N) {
+    for (int r = r0 + (int)threadIdx.y; r < r1; r += 8) {
+      const float x = n < N ? nan0(X[(size_t)r * ldx + n]) : 1.f;
+      const float *a = A + (size_t)r * lda;  // the same M values for the whole warp (broadcast)
+#pragma unroll
+      for (int m = 0; m < kSmallM; ++m)
+        if (m < M) s[m] += nan0(a[m]) * x;
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < kSmallM; ++m) red[threadIdx.y][m][threadIdx.x] = s[m];
+  __syncthreads();
+  if (threadIdx.y != 0 || n > N) return;
+  for (int m = 0; m < M; ++m) {
+    float t = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) t += red[j][m][threadIdx.x];
+    p[((size_t)blockIdx.y * M + m) * ldp + n] = t;
+  }
+}
+
 // ------------------------------------------------------------ FeedForward
 // NeuroNet.cl:430-512.  y[b,o] = act(sum_k nan0(nan0(x[b,k]) w[o,k]) + nan0(w[o,in]))
 // Small batches: one warp per output row, lanes striding the row (coalesced).
@@ -97,6 +126,45 @@ __global__ void ff_rows_kernel(const float *__restrict__ w, const float *__restr
     float t = warp_sum(s[b]);
     if (lane == 0) y[(size_t)b * outputs + warp] = activate(t + bias, act);
   }
+}
+
+// Many samples, at most kSkinny outputs (a value head, an action head): one warp per sample, lanes
+// striding its inputs, every output's dot product kept in registers; the same arithmetic as
+// ff_rows_kernel.
+constexpr int kSkinny = 16;
+__global__ void ff_skinny_kernel(const float *__restrict__ w, const float *__restrict__ x, float *__restrict__ y,
+                                 int inputs, int outputs, int B, int act) {
+  const int b = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+  if (b >= B) return;
+  const float *xb = x + (size_t)b * inputs;
+  float s[kSkinny];
+#pragma unroll
+  for (int o = 0; o < kSkinny; ++o) s[o] = 0.f;
+  for (int k = lane; k < inputs; k += 32) {
+    const float xk = nan0(xb[k]);
+#pragma unroll
+    for (int o = 0; o < kSkinny; ++o)
+      if (o < outputs) s[o] += nan0(xk * w[(size_t)o * (inputs + 1) + k]);
+  }
+#pragma unroll
+  for (int o = 0; o < kSkinny; ++o) {
+    if (o >= outputs) break;
+    const float t = warp_sum(s[o]);
+    if (lane == 0) y[(size_t)b * outputs + o] = activate(t + nan0(w[(size_t)o * (inputs + 1) + inputs]), act);
+  }
+}
+
+// Many samples, at most kSkinny outputs of the next layer: one thread per (sample, input), the
+// same arithmetic as chg_cols_kernel (k ascending).
+__global__ void chg_skinny_kernel(const float *__restrict__ w, const float *__restrict__ g, const float *__restrict__ o,
+                                  float *__restrict__ ig, int inputs, int outputs, int B, int act) {
+  const size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (t >= (size_t)B * inputs) return;
+  const int i = (int)(t % inputs);
+  const float *gb = g + (t / inputs) * outputs;  // the same row for a warp's inputs (broadcast)
+  float s = 0.f;
+  for (int k = 0; k < outputs; ++k) s += nan0(w[(size_t)k * (inputs + 1) + i]) * nan0(gb[k]);
+  ig[t] = deactivate(s, o[t], act);
 }
 
 struct FFLoadX {
@@ -143,6 +211,9 @@ static int k_feedforward(Launch &L) {
   if (L.B <= 4) {
     unsigned blocks = ceil_div((size_t)outputs * 32, 256);
     ff_rows_kernel<4><<<blocks, 256, 0, L.stream>>>(w, x, y, inputs, outputs, L.B, act);
+    NN_CHECK_LAUNCH(L);
+  } else if (outputs <= kSkinny) {
+    ff_skinny_kernel<<<ceil_div((size_t)L.B * 32, 256), 256, 0, L.stream>>>(w, x, y, inputs, outputs, L.B, act);
     NN_CHECK_LAUNCH(L);
   } else {
     FastShape fs{L.B, outputs, inputs, 1, 1, 0, x, inputs, 0, w, ld, 0};
@@ -239,68 +310,6 @@ struct CHGLoadW {  // B(k, n) = W[k][n]
   int ld;
   __device__ __forceinline__ float operator()(int k, int n, int) const { return nan0(w[(size_t)k * ld + n]); }
 };
-struct CHGEpi {
-  const float *o;
-  float *ig;
-  int inputs, act;
-  __device__ __forceinline__ void operator()(int m, int n, int, int, float acc) const {
-    size_t idx = (size_t)m * inputs + n;
-    ig[idx] = deactivate(acc, o[idx], act);
-  }
-  __device__ __forceinline__ long long row(int m, int, int) const { return (long long)m * inputs; }
-  __device__ __forceinline__ float col(int, int) const { return 0.f; }
-  template <int R>
-  __device__ __forceinline__ void put_rows(const long long (&rb)[R], int n, const float (&v)[R], float,
-                                           unsigned mask) const {
-    float yv[R];
-#pragma unroll
-    for (int j = 0; j < R; ++j) yv[j] = (mask >> j & 1u) ? o[rb[j] + n] : 0.f;
-    act_dispatch(act, [&](auto A) {
-#pragma unroll
-      for (int j = 0; j < R; ++j)
-        if (mask >> j & 1u) ig[rb[j] + n] = deactivate(v[j], yv[j], decltype(A)::value);
-    });
-  }
-  __host__ __device__ bool aligned4() const {
-    return inputs % 4 == 0 && ((uintptr_t)o & 15) == 0 && ((uintptr_t)ig & 15) == 0;
-  }
-  __device__ __forceinline__ float4 col4(int, int) const { return make_float4(0.f, 0.f, 0.f, 0.f); }
-  template <int R>
-  __device__ __forceinline__ void put_rows4(const long long (&rb)[R], int n, const float4 (&v)[R], float4,
-                                            unsigned mask) const {
-    float4 yv[R];
-#pragma unroll
-    for (int j = 0; j < R; ++j)
-      yv[j] = (mask >> j & 1u) ? *reinterpret_cast<const float4 *>(o + rb[j] + n) : make_float4(0.f, 0.f, 0.f, 0.f);
-    act_dispatch(act, [&](auto A) {
-      constexpr int a = decltype(A)::value;
-#pragma unroll
-      for (int j = 0; j < R; ++j)
-        if (mask >> j & 1u)
-          *reinterpret_cast<float4 *>(ig + rb[j] + n) =
-              make_float4(deactivate(v[j].x, yv[j].x, a), deactivate(v[j].y, yv[j].y, a),
-                          deactivate(v[j].z, yv[j].z, a), deactivate(v[j].w, yv[j].w, a));
-    });
-  }
-};
-
-// CHGEpi with the input gradient written by TMA stores and the activation output read as the aux
-// tensor (checked with tma_store_ok).
-struct CHGEpiTma : CHGEpi {
-  static constexpr bool kTmaStore = true, kAux = true;
-  template <class F>
-  __device__ __forceinline__ void transform(F &&f) const {
-    act_dispatch(act, [&](auto A) { f([](float x, float, float y) { return deactivate(x, y, decltype(A)::value); }); });
-  }
-  __device__ __forceinline__ int zc(int z, int) const { return z; }
-  __device__ __forceinline__ float4 aux4(int m, int, int n) const {
-    return *reinterpret_cast<const float4 *>(o + (size_t)m * inputs + n);
-  }
-  bool out_map(CUtensorMap *tm, int M, int N, int nz) const {
-    return make_tmap(tm, ig, inputs, 0, N, M, nz, 32, false);
-  }
-};
-
 static int k_calc_hidden_gradient(Launch &L) {
   const int inputs = (int)L.nd.g[0];
   const int outputs = L.i(4), act = L.i(5);
@@ -313,6 +322,11 @@ static int k_calc_hidden_gradient(Launch &L) {
   if (!w || !g || !o || !ig) return NN_ERR_BOUNDS;
   if (L.B <= 4) {
     chg_cols_kernel<4><<<ceil_div(inputs, 32), kChgWarps * 32, 0, L.stream>>>(w, g, o, ig, inputs, outputs, L.B, act);
+    NN_CHECK_LAUNCH(L);
+    return NN_OK;
+  }
+  if (outputs <= kSkinny) {
+    chg_skinny_kernel<<<grid1d((size_t)L.B * inputs, 256), 256, 0, L.stream>>>(w, g, o, ig, inputs, outputs, L.B, act);
     NN_CHECK_LAUNCH(L);
     return NN_OK;
   }

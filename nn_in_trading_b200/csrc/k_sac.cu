@@ -21,6 +21,7 @@
 #include "nn_internal.h"
 #include "tc_gemm.cuh"
 #include "wgrad.cuh"
+#include "epi_dense.cuh"
 
 namespace nn {
 
@@ -55,15 +56,17 @@ __global__ void concat_ff_rows_kernel(const float *__restrict__ w, const float *
   }
 }
 
-// [x1 | x2] per sample, the K-major operand of the batched products
+// [x1 | x2] per sample, the operand of the batched products, in rows of ldp = inputs1 + inputs2
+// rounded up to 4 floats (16-byte rows that TMA can address; the padding columns are zero)
+__host__ __device__ __forceinline__ int concat_ldp(int in1, int in2) { return (in1 + in2 + 3) & ~3; }
 __global__ void concat_pack_kernel(const float *__restrict__ x1, const float *__restrict__ x2, float *__restrict__ p,
                                    int in1, int in2, int B) {
-  const int K = in1 + in2;
+  const int ldp = concat_ldp(in1, in2);
   const size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  if (t >= (size_t)B * K) return;
-  const size_t b = t / K;
-  const int j = (int)(t % K);
-  p[t] = j < in1 ? x1[b * in1 + j] : x2[b * in2 + (j - in1)];
+  if (t >= (size_t)B * ldp) return;
+  const size_t b = t / ldp;
+  const int j = (int)(t % ldp);
+  p[t] = j < in1 ? x1[b * in1 + j] : (j - in1 < in2 ? x2[b * in2 + (j - in1)] : 0.f);
 }
 
 // Batched forward epilogue: y[m][n] = act(acc + W[n][K]), a NaN pre-activation -> 0.
@@ -123,11 +126,12 @@ static int k_concat_ff(Launch &L) {
     NN_CHECK_LAUNCH(L);
     return NN_OK;
   }
-  float *p = L.scratch(2, (size_t)L.B * K);
+  const int ldp = concat_ldp(in1, in2);
+  float *p = L.scratch(2, (size_t)L.B * ldp);
   if (!p) return NN_ERR_CUDA;
-  concat_pack_kernel<<<grid1d((size_t)L.B * K, 256), 256, 0, L.stream>>>(x1, x2, p, in1, in2, L.B);
+  concat_pack_kernel<<<grid1d((size_t)L.B * ldp, 256), 256, 0, L.stream>>>(x1, x2, p, in1, in2, L.B);
   NN_CHECK_LAUNCH(L);
-  FastShape fs{L.B, outputs, K, 1, 1, 0, p, K, 0, w, ld, 0};
+  FastShape fs{L.B, outputs, K, 1, 1, 0, p, ldp, 0, w, ld, 0};
   cudaError_t e = gemm_f32_wb<false, false>(L, fs, ConcatEpi{w, y, ld, K, outputs, act});
   if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
   L.counted();
@@ -203,6 +207,35 @@ struct ConcatHGEpi {
                                             unsigned mask) const {}
 };
 
+// Batched gradient of a short second input (inputs2 <= kCatShort): one warp per sample, lanes
+// striding the outputs k, one partial sum per second input, NaN sum -> 0, then the derivative.
+constexpr int kCatShort = 16;
+__global__ void concat_hg_second_kernel(const float *__restrict__ w, const float *__restrict__ g,
+                                        const float *__restrict__ o2, float *__restrict__ ig2, int outputs, int in1,
+                                        int in2, int B, int act2) {
+  const int b = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+  if (b >= B) return;
+  const int ld = in1 + in2 + 1;
+  const float *gb = g + (size_t)b * outputs;
+  float s[kCatShort];
+#pragma unroll
+  for (int j = 0; j < kCatShort; ++j) s[j] = 0.f;
+  for (int k = lane; k < outputs; k += 32) {
+    const float gk = gb[k];
+    const float *wr = w + (size_t)k * ld + in1;
+#pragma unroll
+    for (int j = 0; j < kCatShort; ++j)
+      if (j < in2) s[j] += wr[j] * gk;
+  }
+#pragma unroll
+  for (int j = 0; j < kCatShort; ++j) {
+    if (j >= in2) break;
+    float t = warp_sum(s[j]);
+    if (isnan(t)) t = 0.f;
+    if (lane == 0) ig2[(size_t)b * in2 + j] = deactivate(t, o2[(size_t)b * in2 + j], act2);
+  }
+}
+
 static int k_concat_hg(Launch &L) {
   const int outputs = L.i(6), in1 = L.i(7), in2 = L.i(8), act1 = L.i(9), act2 = L.i(10);
   if (outputs < 0 || in1 < 0 || in2 < 0) return L.fail(NN_ERR_ARG, "Concat_HiddenGradient: negative size");
@@ -216,6 +249,20 @@ static int k_concat_hg(Launch &L) {
     concat_hg_cols_kernel<4><<<ceil_div(K, 32), kCatWarps * 32, 0, L.stream>>>(w, g, o1, o2, ig1, ig2, outputs,
                                                                               in1, in2, L.B, act1, act2);
     NN_CHECK_LAUNCH(L);
+    return NN_OK;
+  }
+  if (in2 <= kCatShort && in1 > 0 && tma_store_ok(ig1, in1, 0, 1, in1) && ((uintptr_t)o1 & 15) == 0) {
+    // the first input's gradient as the dense hidden-gradient product (TMA-store epilogue with the
+    // activation output as its second input), the short second input by one warp per sample
+    FastShape f1{L.B, in1, outputs, 1, 1, 0, g, outputs, 0, w, K + 1, 0};
+    cudaError_t e = gemm_f32_wb<false, true>(L, f1, CHGEpiTma{{o1, ig1, in1, act1}});
+    if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
+    L.counted();
+    if (in2 > 0) {
+      concat_hg_second_kernel<<<ceil_div((size_t)L.B * 32, 256), 256, 0, L.stream>>>(w, g, o2, ig2, outputs, in1,
+                                                                                   in2, L.B, act2);
+      NN_CHECK_LAUNCH(L);
+    }
     return NN_OK;
   }
   FastShape fs{L.B, K, outputs, 1, 1, 0, g, outputs, 0, w, K + 1, 0};
@@ -349,12 +396,13 @@ static int k_concat_update(Launch &L) {
   if (s.n_col != ld)
     return L.fail(NN_ERR_UNSUPPORTED, std::string(name) + ": a batched update covers whole rows (global size 1 = "
                                                           "inputs1+inputs2+1)");
-  float *p = L.scratch(2, (size_t)L.B * K);
+  const int ldp = concat_ldp(s.in1, s.in2);
+  float *p = L.scratch(2, (size_t)L.B * ldp);
   if (!p) return NN_ERR_CUDA;
-  concat_pack_kernel<<<grid1d((size_t)L.B * K, 256), 256, 0, L.stream>>>(x1, x2, p, s.in1, s.in2, L.B);
+  concat_pack_kernel<<<grid1d((size_t)L.B * ldp, 256), 256, 0, L.stream>>>(x1, x2, p, s.in1, s.in2, L.B);
   NN_CHECK_LAUNCH(L);
   GradSrc src;
-  int rc = wgrad_fast(L, g, s.n_out, p, K, s.n_out, K, L.B, &src);
+  int rc = wgrad_fast(L, g, s.n_out, p, ldp, s.n_out, K, L.B, &src);
   if (rc) return rc;
   src.scale = 1.f / (float)L.B;
   return finish_update(L, src, n, concat_apply<ADAM>, concat_apply_src<ADAM>);

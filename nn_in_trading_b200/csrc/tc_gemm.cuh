@@ -945,9 +945,10 @@ inline int sm_count() {
 }
 
 // Bytes of the packed weight image tcgemm needs for `s` (0 when the weight operand is not packed:
-// split-K, or an all-ones column).
+// split-K slices off the 32-deep stage grid, or an all-ones column).
 inline size_t tcgemm_pack_bytes(const FastShape &s) {
-  if (s.splits > 1 || s.ones_col >= 0 || s.nz != 1) return 0;
+  // split-K slices must start on a stage boundary: the loader indexes the image by kbeg / 32 + stage
+  if ((s.splits > 1 && (s.kchunk <= 0 || s.kchunk % 32)) || s.ones_col >= 0 || s.nz != 1) return 0;
   const bool narrow = s.N <= 64 || (s.N % 128 != 0 && s.N % 128 <= 64);
   const int BN = narrow ? 64 : 128;
   const size_t tiles_n = (s.N + BN - 1) / BN, kstages = (s.K + 31) / 32;

@@ -124,6 +124,13 @@ __global__ void colsum_partial_kernel(float *p, const float *g, int M, int rows,
 __global__ void colsum_rows_kernel(float *p, const float *g, int M, int rows, long long ld, int kchunk, int ldp,
                                    int col);
 
+// Weight gradient with at most kSmallM outputs: per split, G[m][n] = sum_r nan0(A[r*lda + m])
+// nan0(X[r*ldx + n]) for n < N and the bias column G[m][N] = sum_r nan0(A[r*lda + m]), into
+// p[(split*M + m)*ldp + n].  Block (32 columns, 8 row lanes), grid (ceil((N+1)/32), splits).
+constexpr int kSmallM = 16;
+__global__ void wgrad_small_m_kernel(float *p, const float *A, long long lda, const float *X, long long ldx, int M,
+                                     int N, int rows, int kchunk, int ldp);
+
 // Weight gradient of a plain GEMM: G[m][n] = sum_r A[r*lda + m] * X[r*ldx + n] for n < N, and
 // G[m][N] = sum_r A[r*lda + m] (the bias column, input 1).  Partials per split into scratch 0.
 inline int wgrad_fast(Launch &L, const float *A, long long lda, const float *X, long long ldx, int M, int N, int rows,
@@ -162,6 +169,12 @@ inline int wgrad_fast(Launch &L, const float *A, long long lda, const float *X, 
     L.counted();
     out->ld = ldp;
     out->ncol = N + 1;
+  } else if (M <= kSmallM) {
+    // few outputs: one pass over X computes every output row (a 128-row GEMM tile would be mostly
+    // padding); the bias column is column N of the same pass
+    wgrad_small_m_kernel<<<dim3((N + 1 + 31) / 32, splits), dim3(32, 8), 0, L.stream>>>(part, A, lda, X, ldx, M, N,
+                                                                                         rows, kchunk, ldp);
+    NN_CHECK_LAUNCH(L);
   } else {
     cudaError_t e = sgemm_fast<true, true>(fs, PartialStoreLd{part, M, ldp, 1}, L.stream);
     if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));

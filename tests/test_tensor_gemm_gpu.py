@@ -110,7 +110,8 @@ def test_conv_weight_update(ctx, shape):
     check_batched_update(ctx, conv_cases(units, win, wout, act)["UpdateWeightsConvAdam"], B, 3000 + units)
 
 
-@pytest.mark.parametrize("n_in,n_out,B,act", [(300, 257, 70, TANH), (64, 500, 130, SIGMOID), (500, 3, 256, NONE)])
+@pytest.mark.parametrize("n_in,n_out,B,act", [(300, 257, 70, TANH), (64, 500, 130, SIGMOID), (500, 3, 256, NONE),
+                                            (512, 1, 1024, NONE), (512, 12, 600, LRELU)])
 def test_dense_batched(ctx, n_in, n_out, B, act):
     cases = dense_cases(n_in, n_out, act)
     check_batched_per_sample(ctx, cases["FeedForward"], B, 4000 + n_in)
