@@ -191,6 +191,114 @@ __device__ __forceinline__ void cols_times_cols(const float *At, int lda, const 
   }
 }
 
+// out[r][c] for r < R, c < N (N a multiple of 4) = sum_k A(r, k) * Bm[k*ldb + c], with
+// A(r, k) = At[k*lda + r] (A_T) or A[r*lda + k].  Each thread owns a tile of 4 rows x 4 columns and
+// reads both operands as float4, four k at a time (64 FMAs per 8 shared loads).  When the tiles are
+// fewer than half the block's threads, the k range is split across thread groups (slices of a
+// multiple of 4) and the partial tiles are summed through `red` (blockDim.x * 16 floats of shared
+// memory).  Block-wide: every thread of the block calls it; rows past R are computed from the
+// last row and never emitted.  Requires lda and ldb multiples of 4 and 16-byte aligned operands.
+template <bool A_T, class Emit>
+__device__ __forceinline__ void tile_product(const float *A, int lda, const float *Bm, int ldb, int R, int N, int K,
+                                             float *red, Emit emit) {
+  const int cgs = N >> 2, rgs = (R + 3) >> 2, tiles = rgs * cgs;
+  const int nt = blockDim.x;
+  int ks = nt / tiles;
+  if (ks > 8) ks = 8;
+  if (ks < 2) ks = 1;
+  const int kc = ks == 1 ? K : (((K + ks - 1) / ks + 3) & ~3);
+  for (int t0 = 0; t0 < (ks == 1 ? tiles : 1); t0 += nt) {
+    const int t = t0 + (int)threadIdx.x;
+    const int tile = ks == 1 ? t : t % tiles, split = ks == 1 ? 0 : t / tiles;
+    const bool live = ks == 1 ? t < tiles : split < ks;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    const int rg = tile / cgs, cg = tile - rg * cgs;
+    const int r0 = 4 * rg, c0 = 4 * cg;
+    // rows of the tile: 4 consecutive (A_T: one float4 of At per k) or, for row-major A, every
+    // rgs-th row, so that a warp's eight row groups read eight consecutive rows (conflict-free
+    // when lda is not a multiple of 32 floats)
+    auto row_of = [&](int i) { return A_T ? r0 + i : rg + i * rgs; };
+    if (live) {
+      const int kb = split * kc, ke = min(K, kb + kc);
+      int rr[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) rr[i] = min(row_of(i), R - 1);
+      int k = kb;
+      for (; k + 4 <= ke; k += 4) {
+        float a[4][4];  // a[kk][i] = A(r0 + i, k + kk)
+        if (A_T) {
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const float4 v = *reinterpret_cast<const float4 *>(A + (k + kk) * lda + r0);
+            a[kk][0] = v.x, a[kk][1] = v.y, a[kk][2] = v.z, a[kk][3] = v.w;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float4 v = *reinterpret_cast<const float4 *>(A + rr[i] * lda + k);
+            a[0][i] = v.x, a[1][i] = v.y, a[2][i] = v.z, a[3][i] = v.w;
+          }
+        }
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const float4 b = *reinterpret_cast<const float4 *>(Bm + (k + kk) * ldb + c0);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            acc[i][0] = fmaf(a[kk][i], b.x, acc[i][0]);
+            acc[i][1] = fmaf(a[kk][i], b.y, acc[i][1]);
+            acc[i][2] = fmaf(a[kk][i], b.z, acc[i][2]);
+            acc[i][3] = fmaf(a[kk][i], b.w, acc[i][3]);
+          }
+        }
+      }
+      for (; k < ke; ++k) {
+        const float4 b = *reinterpret_cast<const float4 *>(Bm + k * ldb + c0);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float av = A_T ? A[k * lda + min(r0 + i, lda - 1)] : A[rr[i] * lda + k];
+          acc[i][0] = fmaf(av, b.x, acc[i][0]);
+          acc[i][1] = fmaf(av, b.y, acc[i][1]);
+          acc[i][2] = fmaf(av, b.z, acc[i][2]);
+          acc[i][3] = fmaf(av, b.w, acc[i][3]);
+        }
+      }
+    }
+    if (ks > 1) {
+      // partial tile rows float4-major ([row i][split][tile]): consecutive threads, consecutive 16 bytes
+      float4 *red4 = reinterpret_cast<float4 *>(red);
+      const int slots = (ks - 1) * tiles;
+      if (live && split > 0) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          red4[(size_t)i * slots + (split - 1) * tiles + tile] = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+      }
+      __syncthreads();
+      if (live && split == 0)
+        for (int sp = 1; sp < ks; ++sp) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float4 v = red4[(size_t)i * slots + (sp - 1) * tiles + tile];
+            acc[i][0] += v.x, acc[i][1] += v.y, acc[i][2] += v.z, acc[i][3] += v.w;
+          }
+        }
+      __syncthreads();  // `red` is free again for the next product
+    }
+    if (live && split == 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = row_of(i);
+        if (r >= R) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) emit(r, c0 + j, acc[i][j]);
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------ score (smem)
 // S[q,h,k] of MHAttentionScore (NeuroNet.cl:1662-1719) for one (sample, head).
 // smem: Q [U][ldq] (ldq = pad4(D)), Kt [D][ldk] (ldk = pad4(U)).
@@ -288,12 +396,19 @@ __global__ void mh_score_smem_kernel(const float *__restrict__ qkv, float *__res
 
 // -------------------------------------------------------------- out (smem)
 // O = S V for one (sample, head) (MHAttentionOut, NeuroNet.cl:1730-1759).
+// Row stride of a shared [U][.] score matrix: U rounded up to 4 floats, plus 4 when that is a multiple
+// of 32 floats (row-major float4 reads of consecutive rows then hit distinct banks).
+__host__ __device__ __forceinline__ int score_lds(int U) {
+  const int l = pad4(U);
+  return (l % 32 == 0) ? l + 4 : l;
+}
+
 template <int DPL, int SUB>
-__global__ void mh_out_smem_kernel(const float *__restrict__ scores, const float *__restrict__ qkv,
+__global__ void __launch_bounds__(256, 4) mh_out_smem_kernel(const float *__restrict__ scores, const float *__restrict__ qkv,
                                    float *__restrict__ out, int U, int H, int D) {
   extern __shared__ float4 sm4[];
   float *sm = reinterpret_cast<float *>(sm4);
-  const int lds = pad4(U);
+  const int lds = D % 4 == 0 ? score_lds(U) : pad4(U);
   float *Ss = sm;              // [U][lds]
   float *Vs = sm + U * lds;    // [U][D]
   const int h = blockIdx.x;
@@ -305,7 +420,10 @@ __global__ void mh_out_smem_kernel(const float *__restrict__ scores, const float
   __syncthreads();
   float *ob = out + b * (size_t)U * H * D + (size_t)h * D;
   auto emit = [&](int u, int d, float acc) { ob[(size_t)u * H * D + d] = acc; };
-  rows_times_cols<DPL, decltype(emit), SUB>(Ss, lds, Vs, D, U, D, U, emit);
+  if (D % 4 == 0)  // 4 x 4 register tiles; `red` (blockDim.x * 16 floats) follows V
+    tile_product<false>(Ss, lds, Vs, D, U, D, U, Vs + U * D, emit);
+  else
+    rows_times_cols<DPL, decltype(emit), SUB>(Ss, lds, Vs, D, U, D, U, emit);
 }
 
 // ------------------------------------------------- inside gradients (smem)
@@ -318,12 +436,14 @@ __global__ void mh_grad_smem_kernel(const float *__restrict__ qkv, float *__rest
                                     int D, float koef) {
   extern __shared__ float4 sm4[];
   float *sm = reinterpret_cast<float *>(sm4);
-  const int lds = pad4(U);
+  const int lds = D % 4 == 0 ? score_lds(U) : pad4(U);
   float *Cs = sm;                 // [U][lds]  S, then C
   float *Ks = Cs + U * lds;       // [U][D]
   float *Gs = Ks + U * D;         // [U][D]
   float *GQ = Gs + U * D;         // [U][D]   Q, then g o Q
   float *V0 = GQ + U * D;         // [lds]
+  float *red = V0 + 2 * lds;      // [blockDim.x * 16] partial tiles of the tile products (D % 4 == 0)
+  const bool tiled = D % 4 == 0;
   const int h = blockIdx.x;
   const size_t b = blockIdx.y;
   const size_t rs = (size_t)3 * H * D;
@@ -341,7 +461,10 @@ __global__ void mh_grad_smem_kernel(const float *__restrict__ qkv, float *__rest
   float *gb = qkv_g + b * (size_t)U * rs;
   // dV[u][d] = sum_i S[i][u] g[i][d]
   auto emit_v = [&](int u, int d, float acc) { gb[(size_t)u * rs + (size_t)(2 * H + h) * D + d] = acc; };
-  cols_times_cols<DPL, decltype(emit_v), SUB>(Cs, lds, Gs, D, U, D, U, emit_v);
+  if (tiled)
+    tile_product<true>(Cs, lds, Gs, D, U, D, U, red, emit_v);
+  else
+    cols_times_cols<DPL, decltype(emit_v), SUB>(Cs, lds, Gs, D, U, D, U, emit_v);
   for (int e = threadIdx.x; e < U * D; e += blockDim.x) GQ[e] *= Gs[e];  // g o Q
   __syncthreads();  // every dV read of S is done before S becomes C
   // per query row (one warp): A[q] = sum_v S[q][v] V0[v], then C[q][u] = S[q][u] (V0[u] - A[q])
@@ -359,10 +482,15 @@ __global__ void mh_grad_smem_kernel(const float *__restrict__ qkv, float *__rest
   const float inv = 1.f / koef;
   // dK[u][d] = sum_q C[q][u] (g o Q)[q][d] / koef
   auto emit_k = [&](int u, int d, float acc) { gb[(size_t)u * rs + (size_t)(H + h) * D + d] = acc * inv; };
-  cols_times_cols<DPL, decltype(emit_k), SUB>(Cs, lds, GQ, D, U, D, U, emit_k);
   // dQ[u][d] = g[u][d] / koef * sum_k C[u][k] K[k][d]
   auto emit_q = [&](int u, int d, float acc) { gb[(size_t)u * rs + (size_t)h * D + d] = Gs[u * D + d] * acc * inv; };
-  rows_times_cols<DPL, decltype(emit_q), SUB>(Cs, lds, Ks, D, U, D, U, emit_q);
+  if (tiled) {
+    tile_product<true>(Cs, lds, GQ, D, U, D, U, red, emit_k);
+    tile_product<false>(Cs, lds, Ks, D, U, D, U, red, emit_q);
+  } else {
+    cols_times_cols<DPL, decltype(emit_k), SUB>(Cs, lds, GQ, D, U, D, U, emit_k);
+    rows_times_cols<DPL, decltype(emit_q), SUB>(Cs, lds, Ks, D, U, D, U, emit_q);
+  }
 }
 
 }  // namespace nn

@@ -177,7 +177,10 @@ static int k_mh_attention_out(Launch &L) {
     return NN_OK;
   }
   {
-    size_t sm = (size_t)(units * pad4(units) + units * dim) * sizeof(float);
+    // head dimensions that are multiples of 4 take the tiled product, with 16 floats per thread
+    // of partial tiles after V
+    const int lds = dim % 4 == 0 ? score_lds(units) : pad4(units);
+    size_t sm = (size_t)(units * lds + units * dim + (dim % 4 == 0 ? 256 * 16 : 0)) * sizeof(float);
     int dpl = (dim + 31) / 32;
     if (sm <= kSmemCap && dpl <= 2) {
       // head dimensions up to 16: half-warps take separate row blocks (no idle lanes)
@@ -277,7 +280,8 @@ static int k_mh_attention_inside_gradients(Launch &L) {
     return NN_OK;
   }
   {
-    size_t sm = (size_t)(units * pad4(units) + 3 * units * dim + 2 * pad4(units)) * sizeof(float);
+    const int lds = dim % 4 == 0 ? score_lds(units) : pad4(units);
+    size_t sm = (size_t)(units * lds + 3 * units * dim + 2 * lds + (dim % 4 == 0 ? 256 * 16 : 0)) * sizeof(float);
     int dpl = (dim + 31) / 32;
     if (sm <= kSmemCap && dpl <= 2) {
       auto fn = dim <= 16 ? mh_grad_smem_kernel<1, 2>
