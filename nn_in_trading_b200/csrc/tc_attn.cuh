@@ -98,6 +98,8 @@ __global__ void __launch_bounds__(448, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == kLoadWarp) {
     // ------------------------------------------------------------ loader
@@ -380,6 +382,8 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;  // dV at column 0, dK at 32, dQ at 64
+  pdl_wait();
+  pdl_trigger();
   const float inv_koef = 1.f / koef;
   const size_t rs = (size_t)3 * H * D;  // qkv row stride
 
@@ -836,8 +840,7 @@ inline cudaError_t attn_tc(const float *qkv, const float *scores, float *out, in
   const int items = B * H;
   if (items <= 0) return cudaSuccess;
   const int grid = items < sm_count() ? items : sm_count();
-  fn<<<grid, 448, C::SMEM, st>>>(device_status(), U, H, items, mask, koef, tmQ, tmS, tmV, tmO);
-  return cudaGetLastError();
+  return launch_pdl(fn, grid, dim3(448), C::SMEM, st, device_status(), U, H, items, mask, koef, tmQ, tmS, tmV, tmO);
 }
 
 // MHAttentionInsideGradients on the tensor cores (same applicability as attn_tc_ok; `grad` 16-byte and
@@ -880,9 +883,8 @@ inline cudaError_t attn_grad_tc(const float *qkv, float *qkv_g, const float *sco
   const int items = B * H;
   if (items <= 0) return cudaSuccess;
   const int grid = items < sm_count() ? items : sm_count();
-  tc::attn_grad_tc_kernel<<<grid, 320, tc::GradCfg::SMEM, st>>>(qkv, grad, qkv_g, device_status(), U, H, items, koef,
-                                                                 tmS, tmQKV, tmG, tmV0);
-  return cudaGetLastError();
+  return launch_pdl(tc::attn_grad_tc_kernel, grid, dim3(320), tc::GradCfg::SMEM, st, qkv, grad, qkv_g,
+                    device_status(), U, H, items, koef, tmS, tmQKV, tmG, tmV0);
 }
 
 }  // namespace nn

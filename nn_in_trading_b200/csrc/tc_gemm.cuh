@@ -49,6 +49,7 @@
 #include <cstdint>
 #include <cstring>
 #include <type_traits>
+#include <utility>
 
 #include "gemm_fast.cuh"
 #include "nn_device.cuh"
@@ -66,6 +67,15 @@ constexpr int kErrFullWait = 1, kErrEmptyWait = 2, kErrDoneWait = 3;
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+
+// Programmatic dependent launch.  The tensor-core kernels are launched with programmatic stream
+// serialization: their prologue (barrier set-up, tensor-memory allocation) may run while the
+// previous kernel in the stream drains.  pdl_wait() (every thread, before any global data is read
+// or written) returns once that kernel has completed and its memory is visible; pdl_trigger() lets
+// the next such kernel be scheduled as this grid's CTAs finish (it starts only after every CTA of
+// this grid has triggered or exited).  Both are no-ops without a programmatic dependency.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
@@ -504,6 +514,8 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + prod_warps(A
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
   const int n_real = s.ones_col >= 0 ? s.ones_col : s.N;
+  pdl_wait();
+  pdl_trigger();
 
   if (warp >= kProd0 && warp < kProd0 + PW) {
     // ------------------------------------------------------------ producers
@@ -918,6 +930,7 @@ template <int BN, int BK, bool B_K>
 __global__ void pack_b_kernel(const float *B, long long ldb, int N, int K, uint8_t *img, int tiles_n,
                               int kstages) {
   constexpr int CH = BN * BK / 4;  // chunks per tile image half
+  pdl_trigger();                   // the GEMM that consumes the image may start its prologue
   const long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   if (t >= (long long)tiles_n * kstages * CH) return;
   const int q = (int)(t % CH);
@@ -933,6 +946,25 @@ __global__ void pack_b_kernel(const float *B, long long ldb, int N, int K, uint8
 }
 
 }  // namespace tc
+
+// Launch with programmatic stream serialization (the kernel must call tc::pdl_wait before it
+// touches global data).
+template <class... KArgs, class... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
 
 inline int sm_count() {
   static int n = 0;
@@ -1049,9 +1081,8 @@ inline cudaError_t tcgemm_launch(const FastShape &s, EP ep, cudaStream_t st, int
     tc::pack_b_kernel<BN, BK, !B_NCONTIG><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(s.B, s.ldb, s.N, s.K, img,
                                                                                        tiles_n, kstages);
   }
-  fn<<<grid, 32 * (EPIW + tc::prod_warps(A_MODE, B_MODE) + 2), C::SMEM, st>>>(s, ep, err, va, vb, ep.aligned4() ? 1 : 0, tiles_n, tiles_m, (int)total, img,
-                                  kstages, tmA, tmB, tmO);
-  return cudaGetLastError();
+  return launch_pdl(fn, grid, dim3(32 * (EPIW + tc::prod_warps(A_MODE, B_MODE) + 2)), C::SMEM, st, s, ep, err, va,
+                    vb, ep.aligned4() ? 1 : 0, tiles_n, tiles_m, (int)total, img, kstages, tmA, tmB, tmO);
 }
 
 template <int BN, bool A_MCONTIG, bool B_NCONTIG, class EP>
