@@ -68,15 +68,6 @@ __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-// Programmatic dependent launch.  The tensor-core kernels are launched with programmatic stream
-// serialization: their prologue (barrier set-up, tensor-memory allocation) may run while the
-// previous kernel in the stream drains.  pdl_wait() (every thread, before any global data is read
-// or written) returns once that kernel has completed and its memory is visible; pdl_trigger() lets
-// the next such kernel be scheduled as this grid's CTAs finish (it starts only after every CTA of
-// this grid has triggered or exited).  Both are no-ops without a programmatic dependency.
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
@@ -947,7 +938,7 @@ __global__ void pack_b_kernel(const float *B, long long ldb, int N, int K, uint8
 
 }  // namespace tc
 
-// Launch with programmatic stream serialization (the kernel must call tc::pdl_wait before it
+// Launch with programmatic stream serialization (the kernel must call pdl_wait before it
 // touches global data).
 template <class... KArgs, class... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
