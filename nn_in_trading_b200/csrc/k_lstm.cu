@@ -107,15 +107,24 @@ __global__ void lstm_pack_hx_kernel(const float *__restrict__ h, const float *__
   opnd[t] = val;
 }
 
-__global__ void lstm_gates_cell_kernel(const float *__restrict__ P, int ldp, float *__restrict__ cat,
+// P = the GEMM's K-slice partials [splits][V][ldp] of the pre-activations of rows r < H+4; the
+// pre-activation of row r is their sum plus the bias nan0(W[r][H+in]).
+__global__ void lstm_gates_cell_kernel(const float *__restrict__ P, int splits, size_t pstride, int ldp,
+                                       const float *__restrict__ w, int ws, int bcol, float *__restrict__ cat,
                                        float *__restrict__ mem, float *__restrict__ out, int H, int V) {
   size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (t >= (size_t)V * H) return;
   int id = (int)(t % H);
   size_t v = t / H;
-  const float *p = P + v * ldp + id;
-  const float f = activate(p[0], ACT_SIGMOID), ig = activate(p[1], ACT_SIGMOID);
-  const float og = activate(p[2], ACT_SIGMOID), nc = activate(p[3], ACT_TANH);
+  float pre[4];
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    float a = 0.f;
+    for (int sp = 0; sp < splits; ++sp) a += P[sp * pstride + v * ldp + id + g];
+    pre[g] = a + nan0(w[(size_t)(id + g) * ws + bcol]);
+  }
+  const float f = activate(pre[0], ACT_SIGMOID), ig = activate(pre[1], ACT_SIGMOID);
+  const float og = activate(pre[2], ACT_SIGMOID), nc = activate(pre[3], ACT_TANH);
   float *c = cat + v * 4 * H + id;
   c[0] = f;
   c[H] = ig;
@@ -126,6 +135,16 @@ __global__ void lstm_gates_cell_kernel(const float *__restrict__ P, int ldp, flo
   m = nan0(m * f + ig * nc);
   mem[t] = m;
   out[t] = nan0(og * activate(m, ACT_TANH));
+}
+
+// K slices of the gate product: enough to give every SM a 128 x 64 tile, each at least 128 deep.
+static int lstm_ff_splits(int V, int N, int K) {
+  const long long tiles = (long long)((V + 127) / 128) * ((N + 63) / 64);
+  long long want = (148 + tiles - 1) / tiles, cap = K / 128;
+  if (cap < 1) cap = 1;
+  if (want > cap) want = cap;
+  if (want > 8) want = 8;
+  return (int)(want < 1 ? 1 : want);
 }
 
 static int k_lstm_feed_forward(Launch &L) {
@@ -147,18 +166,25 @@ static int k_lstm_feed_forward(Launch &L) {
   const int ldp = H + 4;
   if (H % 4 == 0 && xneed <= in && L.floats(2) >= (size_t)ldp * ws) {
     const size_t nop = (size_t)V * (H + in);
-    float *opnd = L.scratch(1, nop + (size_t)V * ldp);
+    const int K = H + in;
+    FastShape fs{V, ldp, K, 1, 1, 0, nullptr, (long long)K, 0, w, ws, 0};
+    int splits = lstm_ff_splits(V, ldp, K);
+    fs.kchunk = splits > 1 ? ((K + splits - 1) / splits + 31) / 32 * 32 : K;
+    splits = (K + fs.kchunk - 1) / fs.kchunk;
+    fs.splits = splits;
+    const size_t pstride = (size_t)V * ldp;
+    float *opnd = L.scratch(1, nop + pstride * splits);
     if (!opnd) return NN_ERR_CUDA;
     float *P = opnd + nop;  // 16-byte aligned: H + in is a multiple of 4
+    fs.A = opnd;
     lstm_pack_hx_kernel<<<grid1d(nop, 256), 256, 0, L.stream>>>(out, x, opnd, H, in, V);
     NN_CHECK_LAUNCH(L);
-    FastShape fs{V, ldp, H + in, 1, 1, 0, opnd, (long long)H + in, 0, w, ws, 0};
-    cudaError_t e = tma_store_ok(P, ldp, 0, 1, ldp)
-                        ? gemm_f32_wb<false, false>(L, fs, FFEpiTma{{w, P, ws, H + in, ldp, ACT_NONE}})
-                        : gemm_f32_wb<false, false>(L, fs, FFEpi{w, P, ws, H + in, ldp, ACT_NONE});
+    // the product's K-slice partials; the gate kernel sums them and adds the bias column
+    cudaError_t e = gemm_f32_wb<false, false>(L, fs, PartialStoreTma{{P, V, ldp, 1}});
     if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
     L.counted();
-    lstm_gates_cell_kernel<<<grid1d((size_t)V * H, 256), 256, 0, L.stream>>>(P, ldp, cat, mem, out, H, V);
+    lstm_gates_cell_kernel<<<grid1d((size_t)V * H, 256), 256, 0, L.stream>>>(P, splits, pstride, ldp, w, ws, K, cat,
+                                                                             mem, out, H, V);
     NN_CHECK_LAUNCH(L);
     return NN_OK;
   }

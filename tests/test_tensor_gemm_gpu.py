@@ -137,7 +137,8 @@ def test_lstm_hidden_gradient(ctx, H, ins, V):
 
 # (H, inputs, V): tensor-core GEMM (>= 64 series), more inputs than cells (the reference's input loop
 # skips inputs H..H+3), the SIMT GEMM of a small product, and H not a multiple of 4 (per-gate kernel).
-@pytest.mark.parametrize("H,ins,V", [(64, 64, 300), (32, 64, 600), (256, 64, 96), (16, 32, 8), (6, 8, 5)])
+@pytest.mark.parametrize("H,ins,V", [(64, 64, 300), (32, 64, 600), (256, 64, 96), (256, 256, 512), (16, 32, 8),
+                                    (6, 8, 5)])
 def test_lstm_feed_forward(ctx, H, ins, V):
     ws = H + ins + 1
     case = Case(f"LSTM_FeedForward/{H}-{ins}-{V}", "LSTM_FeedForward",
