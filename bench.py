@@ -584,31 +584,49 @@ def run_ours(args, rank, world, local_rank):
     value = world * per_step * args.steps / (ms_max / 1000.0)
 
     # ---- e2e through the public API with host buffers (pinned) ----------
+    # Every step: its inputs go host -> device (nn_buffer_write_async into one half of a device
+    # staging double buffer, concurrent with the step in flight), a device copy into the network's
+    # input buffers, the step, a device copy of the result into a staging buffer, the result
+    # device -> host (nn_buffer_read_async, concurrent with the next step) and the host metric of
+    # that result (CNet::backPropOCL reads the output back).  Two steps are in flight; a staging
+    # half is rewritten only after the read that follows its last use has landed.
     hosts = [torch.from_numpy(np.ascontiguousarray(sl)).pin_memory() for sl in slots]
-    hy = torch.empty(n_y, dtype=torch.float32).pin_memory()
+    hy = [torch.empty(n_y, dtype=torch.float32).pin_memory() for _ in range(2)]
+    stage_in = [[ctx.buffer(n) for n in sizes] for _ in range(2)]
+    stage_out = [ctx.buffer(n_y) for _ in range(2)]
     lib = ctx.lib
     e2e_steps = max(3, args.steps // 2)
 
     def enqueue(i):
-        for h, host, n in zip(inputs, hosts, sizes):
-            ctx._check(lib.nn_buffer_write(h, host[i % pool].data_ptr(), 0, n))
+        half = i % 2
+        for st, host, n in zip(stage_in[half], hosts, sizes):
+            ctx._check(lib.nn_buffer_write_async(st, host[i % pool].data_ptr(), 0, n))
+        for h, st, n in zip(inputs, stage_in[half], sizes):
+            ctx.copy(h, st, n)
         net.step()
+        ctx.copy(stage_out[half], out_h, n_y)
+        ticket = lib.nn_buffer_read_async(stage_out[half], hy[half].data_ptr(), 0, n_y)
+        if ticket < 0:
+            ctx._check(ticket)
+        return ticket
 
-    for i in range(2):
-        enqueue(i)
-        ctx._check(lib.nn_buffer_read(out_h, hy.data_ptr(), 0, n_y))
+    def run_e2e(n):
+        tickets = {0: enqueue(0)}
+        if n > 1:
+            tickets[1] = enqueue(1)
+        metric = (None, None)
+        for i in range(n):
+            ctx._check(lib.nn_transfer_wait(tickets.pop(i)))
+            metric = wl.host_metric(hy[i % 2].numpy(), slots, i % pool)
+            if i + 2 < n:
+                tickets[i + 2] = enqueue(i + 2)
+        return metric
+
+    run_e2e(2)
+    ctx.finish()
     barrier()
-    # Every step: H2D of its inputs, the step, a blocking D2H of its result and the host metric of that
-    # result (CNet::backPropOCL reads the output back).  The host work of step i runs while the
-    # device already executes step i+1 (enqueued right after step i's read returns).
     t0 = time.perf_counter()
-    metric = (None, None)
-    enqueue(0)
-    for i in range(e2e_steps):
-        ctx._check(lib.nn_buffer_read(out_h, hy.data_ptr(), 0, n_y))
-        if i + 1 < e2e_steps:
-            enqueue(i + 1)  # hy is written again only by the next iteration's read
-        metric = wl.host_metric(hy.numpy(), slots, i % pool)
+    metric = run_e2e(e2e_steps)
     e2e_s = time.perf_counter() - t0
     if world > 1:
         t = torch.tensor([e2e_s], dtype=torch.float64)

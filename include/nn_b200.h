@@ -98,6 +98,21 @@ NN_API int nn_buffer_free(int handle);
 NN_API int nn_buffer_write(int handle, const float *src, long long offset, long long count);
 /* CBufferFloat::BufferRead / COpenCL::BufferRead: blocking read. */
 NN_API int nn_buffer_read(int handle, float *dst, long long offset, long long count);
+/* Extension (no reference counterpart): overlapped transfers, for a host that feeds the next step
+ * while the current one computes.
+ * nn_buffer_write_async: host -> device copy on a transfer stream, concurrent with the executions
+ *   already enqueued; every execution enqueued afterwards waits for it.  The caller guarantees that
+ *   no earlier execution still reads or writes the range (write into the half of a double buffer
+ *   the previous step has finished with) and keeps `src` unchanged until the copy has happened
+ *   (pinned host memory keeps it asynchronous).
+ * nn_buffer_read_async: device -> host copy of the range as the executions enqueued so far leave
+ *   it, on a second transfer stream, concurrent with later executions; returns a ticket (>= 0) or a
+ *   negative status.  The caller guarantees that later executions do not write the range before
+ *   the read has landed.
+ * nn_transfer_wait: blocks until the read named by a ticket (one of the last 64) has landed. */
+NN_API int nn_buffer_write_async(int handle, const float *src, long long offset, long long count);
+NN_API int nn_buffer_read_async(int handle, float *dst, long long offset, long long count);
+NN_API int nn_transfer_wait(int ticket);
 /* Fill count floats from offset with `value` (CBufferFloat::BufferInit). */
 NN_API int nn_buffer_fill(int handle, float value, long long offset, long long count);
 /* Device-to-device copy inside the context (CopyBufferRaw role). */

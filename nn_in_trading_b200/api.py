@@ -72,6 +72,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "nn_buffer_write": ([c_int, c_p, c_ll, c_ll], c_int), "nn_buffer_read": ([c_int, c_p, c_ll, c_ll], c_int),
         "nn_buffer_fill": ([c_int, c_f, c_ll, c_ll], c_int),
         "nn_buffer_copy": ([c_int, c_ll, c_int, c_ll, c_ll], c_int),
+        "nn_buffer_write_async": ([c_int, c_p, c_ll, c_ll], c_int),
+        "nn_buffer_read_async": ([c_int, c_p, c_ll, c_ll], c_int), "nn_transfer_wait": ([c_int], c_int),
         "nn_buffer_bytes": ([c_int], c_ll), "nn_buffer_device_ptr": ([c_int], c_p),
         "nn_kernel_create": ([c_int, ctypes.c_char_p], c_int), "nn_kernel_free": ([c_int], c_int),
         "nn_set_arg_buffer": ([c_int, c_int, c_int], c_int), "nn_set_arg_int": ([c_int, c_int, c_int], c_int),

@@ -87,6 +87,12 @@ struct Context {
   // device status word written by kernels whose bounded waits expired (0 = fine)
   int *status = nullptr;
   bool simt_gemm = false;  // NN_INIT_SIMT_GEMM: FP32 SIMT GEMMs instead of 3xTF32 tensor cores
+  // overlapped transfers (nn_buffer_write_async / nn_buffer_read_async), created on first use
+  cudaStream_t xfer_in = nullptr, xfer_out = nullptr;
+  cudaEvent_t ev_in = nullptr, ev_exec = nullptr;
+  static constexpr int kReadSlots = 64;
+  cudaEvent_t ev_read[kReadSlots] = {};
+  long long reads_issued = 0;
 };
 
 static Context *g_ctx = nullptr;
@@ -303,6 +309,15 @@ int nn_shutdown(void) {
   if (c->arena) cudaFree(c->arena);
   if (c->status) cudaFree(c->status);
   if (c->comm && c->nccl.comm_destroy) c->nccl.comm_destroy(c->comm);
+  if (c->xfer_in) {
+    cudaStreamSynchronize(c->xfer_in);
+    cudaStreamSynchronize(c->xfer_out);
+    cudaStreamDestroy(c->xfer_in);
+    cudaStreamDestroy(c->xfer_out);
+    cudaEventDestroy(c->ev_in);
+    cudaEventDestroy(c->ev_exec);
+    for (cudaEvent_t &e : c->ev_read) cudaEventDestroy(e);
+  }
   cudaStreamDestroy(c->stream);
   delete c;
   g_ctx = nullptr;
@@ -424,6 +439,74 @@ int nn_buffer_read(int h, float *dst, long long offset, long long count) {
   CUDA_TRY(cudaMemcpyAsync(dst, b->ptr + offset, (size_t)count * sizeof(float), cudaMemcpyDeviceToHost,
                            g_ctx->stream));
   CUDA_TRY(cudaStreamSynchronize(g_ctx->stream));
+  return NN_OK;
+}
+
+// Transfer streams and events of the overlapped copies (once per context).
+static int transfers_ready(Context *c) {
+  if (c->xfer_in) return NN_OK;
+  cudaError_t e = cudaStreamCreateWithFlags(&c->xfer_in, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->xfer_out, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_in, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->ev_exec, cudaEventDisableTiming);
+  for (int i = 0; i < Context::kReadSlots && e == cudaSuccess; ++i)
+    e = cudaEventCreateWithFlags(&c->ev_read[i], cudaEventDisableTiming);
+  if (e != cudaSuccess) return set_err(NN_ERR_CUDA, cudaGetErrorString(e));
+  return NN_OK;
+}
+
+int nn_buffer_write_async(int h, const float *src, long long offset, long long count) {
+  NEED_CTX();
+  Context *c = g_ctx;
+  Buffer *b = get_buf(h);
+  int rc = check_range(b, offset, count, "nn_buffer_write_async");
+  if (rc) return rc;
+  if (count == 0) return NN_OK;
+  if (!src) return set_err(NN_ERR_ARG, "nn_buffer_write_async: null source");
+  rc = transfers_ready(c);
+  if (rc) return rc;
+  // on the input transfer stream, concurrent with the executions already enqueued; everything
+  // enqueued on the execution stream from now on waits for it
+  CUDA_TRY(cudaMemcpyAsync(b->ptr + offset, src, (size_t)count * sizeof(float), cudaMemcpyHostToDevice, c->xfer_in));
+  CUDA_TRY(cudaEventRecord(c->ev_in, c->xfer_in));
+  CUDA_TRY(cudaStreamWaitEvent(c->stream, c->ev_in, 0));
+  return NN_OK;
+}
+
+int nn_buffer_read_async(int h, float *dst, long long offset, long long count) {
+  NEED_CTX();
+  Context *c = g_ctx;
+  Buffer *b = get_buf(h);
+  int rc = check_range(b, offset, count, "nn_buffer_read_async");
+  if (rc) return rc;
+  if (!dst && count > 0) return set_err(NN_ERR_ARG, "nn_buffer_read_async: null destination");
+  rc = transfers_ready(c);
+  if (rc) return rc;
+  // the range as every execution enqueued so far leaves it, copied on the output transfer stream
+  // while later executions run; a ticket names the read for nn_transfer_wait
+  const long long ticket = c->reads_issued;
+  cudaEvent_t done = c->ev_read[ticket % Context::kReadSlots];
+  CUDA_TRY(cudaEventRecord(c->ev_exec, c->stream));
+  CUDA_TRY(cudaStreamWaitEvent(c->xfer_out, c->ev_exec, 0));
+  if (count > 0)
+    CUDA_TRY(cudaMemcpyAsync(dst, b->ptr + offset, (size_t)count * sizeof(float), cudaMemcpyDeviceToHost,
+                             c->xfer_out));
+  CUDA_TRY(cudaEventRecord(done, c->xfer_out));
+  c->reads_issued++;
+  return (int)(ticket % 0x40000000LL);
+}
+
+int nn_transfer_wait(int ticket) {
+  NEED_CTX();
+  Context *c = g_ctx;
+  if (ticket < 0) return set_err(NN_ERR_ARG, "nn_transfer_wait: negative ticket");
+  // tickets are issued in order; only the last kReadSlots reads can still be waited on
+  const long long issued = c->reads_issued;
+  long long t = (issued & ~0x3fffffffLL) | ticket;
+  if (t >= issued) t -= 0x40000000LL;
+  if (t < 0 || t >= issued || issued - t > Context::kReadSlots)
+    return set_err(NN_ERR_ARG, "nn_transfer_wait: ticket not among the last 64 reads");
+  CUDA_TRY(cudaEventSynchronize(c->ev_read[t % Context::kReadSlots]));
   return NN_OK;
 }
 
