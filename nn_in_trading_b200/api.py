@@ -23,7 +23,8 @@ SGD, ADAM, LS, ADAM_MINI = 0, 1, 2, 3
 # NeuroNet.cl kernel signatures: one char per positional argument (p buffer, i int, f float).
 SIGNATURES = {
     "FeedForward": "pppiipi", "CalcOutputGradient": "pppif", "CalcHiddenGradient": "ppppii",
-    "UpdateWeightsMomentum": "ppppiff", "UpdateWeightsAdam": "pppppifff", "NormalizeWeights": "pi",
+    "UpdateWeightsMomentum": "ppppiff", "UpdateWeightsAdam": "pppppifff",
+    "UpdateWeightsAdamMini": "pppppfff", "NormalizeWeights": "pi",
     "Activation": "ppi", "DeActivation": "pppi", "SoftUpdate": "ppf", "SoftUpdateAdam": "ppppfff",
     "FeedForwardConv": "pppiiiii", "CalcHiddenGradientConv": "ppppiiiiii",
     "UpdateWeightsConvAdam": "pppppifffiii", "UpdateWeightsConvMomentum": "ppppiffiii",

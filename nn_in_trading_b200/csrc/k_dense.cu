@@ -471,6 +471,97 @@ static int k_update_weights_adam(Launch &L) {
   return finish_update(L, src, (size_t)s.n_out * s.n_col, adam_dense_apply, adam_dense_apply_src);
 }
 
+// UpdateWeightsAdamMini (NeuroNet.cl:7515-7612), one sample: global (inputs+1, outputs), local
+// (inputs+1, 1).  Every output row shares the scale s of the reference's local reduction of
+// inp^2 / inputs: slot t of ls = min(64, inputs) sums local ids t, t + ls, ... that its count loop
+// reaches (the bias input 1 only when inputs % ls != 0), then the folding loop, which stops before
+// its last step, leaves s in slot 0.  One block of 64 threads reproduces that order.
+__global__ void adam_mini_scale_kernel(const float *__restrict__ x, int inputs, float *__restrict__ s_out) {
+  __shared__ float temp[64];
+  const int ls = min(64, inputs), t = threadIdx.x;
+  if (t < ls) {
+    const int counts = (inputs + ls - 1) / ls;
+    float acc = 0.f;
+    for (int count = 0; count < counts; ++count) {
+      const int i = count * ls + t;
+      if (i > inputs) break;
+      const float inp = i < inputs ? x[i] : 1.f;
+      const float term = isfinite(inp) ? inp * inp / (float)inputs : 0.f;
+      acc = (count == 0 ? 0.f : acc) + term;
+    }
+    temp[t] = acc;
+  }
+  __syncthreads();
+  int count = (ls + 1) / 2;
+  while (true) {
+    if (t < count && t + count < ls) {
+      temp[t] += temp[t + count];
+      temp[t + count] = 0.f;
+    }
+    count = (count + 1) / 2;
+    __syncthreads();
+    if (!(count > 1)) break;
+  }
+  if (t == 0) *s_out = temp[0];
+}
+
+// One block per output row: its second moment from the shared scale, then every weight of the row.
+__global__ void adam_mini_apply_kernel(float *w, const float *g, const float *x, float *m, float *v,
+                                       const float *s_in, int inputs, float l, float b1, float b2) {
+  __shared__ float vt_s, g_s;
+  const int o = blockIdx.x;
+  if (threadIdx.x == 0) {
+    float gg = g[o];
+    if (!isfinite(gg)) gg = 0.f;
+    float t0 = *s_in;
+    if (!isfinite(t0)) t0 = 1.f;
+    float vv = v[o];
+    if (!isfinite(vv)) vv = 1.f;
+    t0 = b2 * vv + (1.f - b2) * (gg * gg) * t0;
+    v[o] = t0;
+    vt_s = t0;
+    g_s = gg;
+  }
+  __syncthreads();
+  const float vt = vt_s, gg = g_s;
+  for (int i = threadIdx.x; i <= inputs; i += blockDim.x) {
+    const size_t wi = (size_t)o * (inputs + 1) + i;
+    const float inp = i < inputs ? x[i] : 1.f;
+    float weight = w[wi];
+    if (!isfinite(weight)) weight = 0.f;
+    float mm = m[wi];
+    if (!isfinite(mm)) mm = 0.f;
+    mm = b1 * mm + (1.f - b1) * gg * inp;
+    if (!isfinite(mm)) mm = 0.f;
+    float delta = l * (mm / (sqrtf(vt) + 1.0e-37f) - (kL1 * signf(weight) + kL2 * weight));
+    if (!isfinite(delta)) delta = 0.f;
+    if (delta > 0.f) w[wi] = weight + delta;
+    m[wi] = mm;
+  }
+}
+
+static int k_update_weights_adam_mini(Launch &L) {
+  if (!L.nd.has_local || L.nd.dims < 2)
+    return L.fail(NN_ERR_ARG, "UpdateWeightsAdamMini: needs global (inputs+1, outputs) and local (inputs+1, 1)");
+  const int inputs = (int)L.nd.l[0] - 1, outputs = (int)L.nd.g[1];
+  if (inputs < 1 || (int)L.nd.g[0] != inputs + 1)
+    return L.fail(NN_ERR_ARG, "UpdateWeightsAdamMini: global size 0 must equal local size 0 (inputs + 1)");
+  if (L.B != 1 || L.deferred())
+    return L.fail(NN_ERR_UNSUPPORTED, "UpdateWeightsAdamMini: one sample per execution (the reference's "
+                                      "per-row second moment has no batch-mean form here)");
+  const size_t nw = (size_t)outputs * (inputs + 1);
+  float *w = L.buf(0, nw), *g = L.buf(1, outputs), *x = L.buf(2, inputs), *m = L.buf(3, nw);
+  float *v = L.buf(4, outputs);
+  if (!w || !g || !x || !m || !v) return NN_ERR_BOUNDS;
+  float *s = L.scratch(3, 1);
+  if (!s) return NN_ERR_CUDA;
+  adam_mini_scale_kernel<<<1, 64, 0, L.stream>>>(x, inputs, s);
+  NN_CHECK_LAUNCH(L);
+  adam_mini_apply_kernel<<<outputs, 256, 0, L.stream>>>(w, g, x, m, v, s, inputs, L.f(5), L.f(6), L.f(7));
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
 // UpdateWeightsMomentum (NeuroNet.cl:624-645); batch: G = mean_b clamp(g_b) x_b.
 __global__ void momentum_dense_kernel(float *w, float *dw, GradSrc G, const float *g, const float *x, int n_out,
                                       int n_col, int inputs, float lr, float mom, int fused) {
@@ -631,6 +722,7 @@ const KernelDef kDenseKernels[] = {
     {"CalcHiddenGradient", "ppppii", k_calc_hidden_gradient, false},
     {"UpdateWeightsMomentum", "ppppiff", k_update_weights_momentum, false},
     {"UpdateWeightsAdam", "pppppifff", k_update_weights_adam, false},
+    {"UpdateWeightsAdamMini", "pppppfff", k_update_weights_adam_mini, false},
     {"NormalizeWeights", "pi", k_normalize_weights, true},
     {"Activation", "ppi", k_activation, false},
     {"DeActivation", "pppi", k_deactivation, false},

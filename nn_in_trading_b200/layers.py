@@ -16,7 +16,7 @@ import math
 
 import numpy as np
 
-from .api import ADAM, GELU, NONE, SGD, Context, Kernel
+from .api import ADAM, ADAM_MINI, GELU, NONE, SGD, Context, Kernel
 
 LR = 3.0e-4       # NeuroNet_Definitions.mqh:38
 MOMENTUM = 0.9    # NeuroNet_Definitions.mqh:40
@@ -175,6 +175,10 @@ class DenseLayer(Layer):
             k = self.kernel("UpdateWeightsMomentum").args(prev.weights, self.gradient, prev.output, prev.delta,
                                                           prev.neurons, LR, MOMENTUM)
             ops = [Op(k, (self.neurons, prev.neurons + 1))]
+        elif prev.optimization == ADAM_MINI:  # NeuroNet_Core.mqh:15939-15957: one second moment per output
+            k = self.kernel("UpdateWeightsAdamMini").args(prev.weights, self.gradient, prev.output, prev.m, prev.v,
+                                                          LR, B1, B2)
+            ops = [AdamOp(k, (prev.neurons + 1, self.neurons), (prev.neurons + 1, 1), self, 5)]
         else:
             k = self.kernel("UpdateWeightsAdam").args(prev.weights, self.gradient, prev.output, prev.m, prev.v,
                                                       prev.neurons, LR, B1, B2)

@@ -854,6 +854,69 @@ def LSTM_UpdateWeightsAdam(weights, weights_gradient, matrix_m, matrix_v, l, b1,
         matrix_v[:n] = vt
 
 
+# ------------------------------------------------------------------ ADAM_MINI
+LOCAL_ARRAY_SIZE = 64  # NeuroNet.cl:18
+
+
+def adam_mini_input_scale(x, inputs):
+    """The local reduction of UpdateWeightsAdamMini (NeuroNet.cl:7531-7558), which is the same for
+    every output row.  Slot s of ls = min(64, inputs) sums inp_i^2 / inputs over the local ids
+    i = s, s + ls, ... that its count loop reaches (the bias input, 1, only when inputs % ls != 0);
+    the folding loop stops before its last step, so the result is the first slot after the folds."""
+    ls = min(LOCAL_ARRAY_SIZE, inputs)
+    temp = np.zeros(max(ls, 1), F32)
+    with _err():
+        n_counts = -(-inputs // ls)
+        for count in range(n_counts):
+            for shift in range(ls):
+                i = count * ls + shift
+                if i > inputs:
+                    continue
+                inp = F32(x[i]) if i < inputs else F32(1)
+                term = F32(0) if not np.isfinite(inp) else F32(inp * inp) / F32(inputs)
+                temp[shift] = F32((F32(0) if count == 0 else temp[shift]) + term)
+        count = (ls + 1) // 2
+        while True:
+            for i in range(count):
+                if i + count < ls:
+                    temp[i] = F32(temp[i] + temp[i + count])
+                    temp[i + count] = 0
+            count = (count + 1) // 2
+            if not count > 1:
+                break
+    return temp[0]
+
+
+def UpdateWeightsAdamMini(matrix_w, matrix_g, matrix_i, matrix_m, matrix_v, l, b1, b2, gsize, lsize=None):
+    """NeuroNet.cl:7515-7612 over global (inputs+1, outputs), local (inputs+1, 1): one second moment
+    per output row, v = b2 v + (1-b2) g^2 s with s the input scale above; m per weight; the weight
+    moves only when delta > 0 (as written)."""
+    inputs = (lsize[0] if lsize is not None else gsize[0]) - 1
+    outputs = gsize[1]
+    with _err():
+        s = adam_mini_input_scale(matrix_i, inputs)
+        t0 = s if np.isfinite(s) else F32(1)
+        g = matrix_g[:outputs].astype(F32)
+        g = np.where(np.isfinite(g), g, F32(0)).astype(F32)
+        v = matrix_v[:outputs].astype(F32)
+        v = np.where(np.isfinite(v), v, F32(1)).astype(F32)
+        b1, b2, l = F32(b1), F32(b2), F32(l)
+        vt = (b2 * v + ((F32(1) - b2) * (g * g)) * t0).astype(F32)
+        matrix_v[:outputs] = vt
+        idx = np.arange(outputs)[:, None] * (inputs + 1) + np.arange(inputs + 1)[None, :]
+        inp = np.concatenate([matrix_i[:inputs].astype(F32), np.ones(1, F32)])[None, :]
+        weight = matrix_w[idx]
+        weight = np.where(np.isfinite(weight), weight, F32(0)).astype(F32)
+        m = matrix_m[idx]
+        m = np.where(np.isfinite(m), m, F32(0)).astype(F32)
+        m = (b1 * m + ((F32(1) - b1) * g[:, None]) * inp).astype(F32)
+        m = np.where(np.isfinite(m), m, F32(0)).astype(F32)
+        delta = (l * (m / (np.sqrt(vt)[:, None] + F32(1e-37)) - (L1 * cl_sign(weight) + L2 * weight))).astype(F32)
+        delta = np.where(np.isfinite(delta), delta, F32(0)).astype(F32)
+        matrix_w[idx] = np.where(delta > 0, (weight + delta).astype(F32), matrix_w[idx])
+        matrix_m[idx] = m
+
+
 # ---------------------------------------------------------------- concatenate
 def _concat_rows(matrix_w, n_out, inputs1, inputs2):
     return matrix_w[:n_out * (inputs1 + inputs2 + 1)].reshape(n_out, inputs1 + inputs2 + 1)

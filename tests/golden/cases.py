@@ -293,9 +293,21 @@ def _concat_cases():
     return cases
 
 
+def _adam_mini_cases():
+    """UpdateWeightsAdamMini (NeuroNet.cl:7515-7612): inputs below, at and above the 64-slot local
+    array, multiples of it (the bias input then drops out of the scale) and not."""
+    cases = []
+    for n_in, n_out in [(240, 17), (64, 9), (65, 4), (3, 5), (1, 2), (130, 7), (128, 3), (200, 6)]:
+        cases.append(Case(f"UpdateWeightsAdamMini/{n_in}x{n_out}", "UpdateWeightsAdamMini",
+                          [A(n_out * (n_in + 1), "uniform", 1 / np.sqrt(n_in)), A(n_out, "grad"), A(n_in),
+                           A(n_out * (n_in + 1), "small"), A(n_out, "pos", 1e-5), 3e-4, 0.9, 0.999],
+                          (n_in + 1, n_out), (n_in + 1, 1)))
+    return cases
+
+
 def all_cases() -> list[Case]:
     return (_dense_cases() + _conv_cases() + _attention_cases() + _norm_cases() + _batchnorm_cases() + _lstm_cases()
-            + _attention2_cases() + _concat_cases())
+            + _attention2_cases() + _concat_cases() + _adam_mini_cases())
 
 
 def prepare_inputs(case: Case, seed: int) -> list:
