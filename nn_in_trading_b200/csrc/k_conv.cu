@@ -484,7 +484,119 @@ static int k_update_weights_conv_momentum(Launch &L) {
   return momentum_conv_apply(L, grad);
 }
 
+// UpdateWeightsConvAdamMini (NeuroNet.cl:7615-7731), one sample: global (window_in+1, window_out,
+// variables), local (window_in+1, window_out_h, 1).  Per weight, the gradient over
+// total = (inputs - window_in + step - 1) / step units, stopping once i + t*window_in >= inputs (the
+// reference's test), non-finite terms skipped.
+__global__ void conv_adam_mini_grad_kernel(const float *__restrict__ g, const float *__restrict__ x,
+                                           float *__restrict__ G, int inputs, int win, int wout, int variables,
+                                           int step, int total) {
+  const size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (t >= (size_t)variables * wout * (win + 1)) return;
+  const int i = (int)(t % (win + 1));
+  const size_t r = t / (win + 1);
+  const int f = (int)(r % wout), v = (int)(r / wout);
+  const float *gv = g + (size_t)v * total * wout + f;
+  const float *xv = x + (size_t)v * inputs;
+  float acc = 0.f;
+  for (int tt = 0; tt < total; ++tt) {
+    if (i != win && i + tt * win >= inputs) break;
+    const float gt = gv[(size_t)tt * wout] * (i == win ? 1.f : xv[i + tt * step]);
+    if (isfinite(gt)) acc += gt;
+  }
+  G[t] = acc;
+}
+
+// One block per head (window_out_h rows).  The second moment is indexed by head only, so the
+// reference's work-groups of different variables race on it; here the variables take their turns in
+// order.  Each turn: the reference's slot reduction of grad^2 / (window_in * window_out_h) (rows
+// outer, the bias column only when window_in % 64 != 0, the fold stopping one step early), the
+// clamped second moment, then the head's weights: m clamped to +-1e5, w += l m / sqrt(v).
+__global__ void conv_adam_mini_apply_kernel(float *w, float *m, float *vh, const float *__restrict__ G, int win,
+                                            int wout, int wout_h, int variables, float l, float b1, float b2) {
+  __shared__ float temp[64];
+  __shared__ float vt_s;
+  const int head = blockIdx.x, t = threadIdx.x;
+  const int ls = min(64, win), counts = (win + ls - 1) / ls;
+  const float den = (float)(win * wout_h);
+  for (int v = 0; v < variables; ++v) {
+    const float *Gh = G + ((size_t)v * wout + (size_t)head * wout_h) * (win + 1);
+    if (t < ls) {
+      float acc = 0.f;
+      for (int h = 0; h < wout_h; ++h)
+        for (int count = 0; count < counts; ++count) {
+          const int i = count * ls + t;
+          if (i > win) break;
+          const float gv = Gh[(size_t)h * (win + 1) + i];
+          const float term = isfinite(gv) ? gv * gv / den : 0.f;
+          acc = ((count == 0 && h == 0) ? 0.f : acc) + term;
+        }
+      temp[t] = acc;
+    }
+    __syncthreads();
+    int count = (ls + 1) / 2;
+    while (true) {
+      if (t < count && t + count < ls) {
+        temp[t] += temp[t + count];
+        temp[t + count] = 0.f;
+      }
+      count = (count + 1) / 2;
+      __syncthreads();
+      if (!(count > 1)) break;
+    }
+    if (t == 0) {
+      float t0 = temp[0];
+      if (!isfinite(t0)) t0 = 1.f;
+      float vv = vh[head];
+      if (!isfinite(vv)) vv = 1.f;
+      t0 = fminf(fmaxf(b2 * vv + (1.f - b2) * t0, 1.0e-6f), 1.0e6f);
+      vh[head] = t0;
+      vt_s = t0;
+    }
+    __syncthreads();
+    const float vt = vt_s;
+    for (int e = t; e < wout_h * (win + 1); e += blockDim.x) {
+      const size_t wi = ((size_t)v * wout + (size_t)head * wout_h + e / (win + 1)) * (win + 1) + e % (win + 1);
+      float mt = fminf(fmaxf(b1 * m[wi] + (1.f - b1) * G[wi], -1.0e5f), 1.0e5f);
+      if (!isfinite(mt)) mt = 0.f;
+      const float wv = w[wi] + l * mt / sqrtf(vt);
+      if (isfinite(wv)) w[wi] = wv;
+      m[wi] = mt;
+    }
+    __syncthreads();  // temp and vt_s are rewritten by the next variable's turn
+  }
+}
+
+static int k_update_weights_conv_adam_mini(Launch &L) {
+  if (!L.nd.has_local || L.nd.dims < 2)
+    return L.fail(NN_ERR_ARG, "UpdateWeightsConvAdamMini: needs global (window_in+1, window_out, variables) "
+                              "and local (window_in+1, window_out_h, 1)");
+  const int win = (int)L.nd.g[0] - 1, wout = (int)L.nd.g[1];
+  const int variables = L.nd.dims > 2 ? (int)L.nd.g[2] : 1, wout_h = (int)L.nd.l[1];
+  const int inputs = L.i(5), step = L.i(9);
+  if (win < 1 || step < 1 || inputs < win || wout_h < 1 || wout % wout_h || (int)L.nd.l[0] != win + 1)
+    return L.fail(NN_ERR_ARG, "UpdateWeightsConvAdamMini: bad window, step, inputs or head size");
+  if (L.B != 1 || L.deferred())
+    return L.fail(NN_ERR_UNSUPPORTED, "UpdateWeightsConvAdamMini: one sample per execution (the reference's "
+                                      "per-head second moment has no batch-mean form here)");
+  const int total = (inputs - win + step - 1) / step;
+  const size_t nw = (size_t)variables * wout * (win + 1);
+  float *w = L.buf(0, nw), *g = L.buf(1, (size_t)variables * total * wout), *x = L.buf(2, (size_t)variables * inputs);
+  float *m = L.buf(3, nw), *v = L.buf(4, (size_t)(wout / wout_h));
+  if (!w || !g || !x || !m || !v) return NN_ERR_BOUNDS;
+  float *G = L.scratch(1, nw);
+  if (!G) return NN_ERR_CUDA;
+  conv_adam_mini_grad_kernel<<<grid1d(nw, 256), 256, 0, L.stream>>>(g, x, G, inputs, win, wout, variables, step,
+                                                                   total);
+  NN_CHECK_LAUNCH(L);
+  conv_adam_mini_apply_kernel<<<wout / wout_h, 256, 0, L.stream>>>(w, m, v, G, win, wout, wout_h, variables,
+                                                                   L.f(6), L.f(7), L.f(8));
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
 const KernelDef kConvKernels[] = {
+    {"UpdateWeightsConvAdamMini", "pppppifffi", k_update_weights_conv_adam_mini, false},
     {"FeedForwardConv", "pppiiiii", k_feedforward_conv, false},
     {"CalcHiddenGradientConv", "ppppiiiiii", k_calc_hidden_gradient_conv, false},
     {"UpdateWeightsConvAdam", "pppppifffiii", k_update_weights_conv_adam, false},

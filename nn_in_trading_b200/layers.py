@@ -427,6 +427,12 @@ class ConvLayer(Layer):
 
     def update_ops(self, prev: Layer) -> list[Op]:
         n = (self.window + 1) * self.window_out * self.variables
+        if self.optimization == ADAM_MINI:
+            # NeuroNet_Core.mqh:17355-17435: local (window+1, 1, 1), one second moment per output row
+            k = self.kernel("UpdateWeightsConvAdamMini").args(self.conv_w, self.gradient, prev.output, self.conv_m,
+                                                              self.conv_v, self.per_sample(prev) // self.variables,
+                                                              LR, B1, B2, self.step)
+            return [AdamOp(k, (self.window + 1, self.window_out, self.variables), (self.window + 1, 1, 1), self, 6)]
         k = self.kernel("UpdateWeightsConvAdam").args(self.conv_w, self.gradient, prev.output, self.conv_m,
                                                       self.conv_v, self.per_sample(prev) // self.variables, LR, B1, B2,
                                                       self.window, self.window_out, self.step)

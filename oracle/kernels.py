@@ -917,6 +917,93 @@ def UpdateWeightsAdamMini(matrix_w, matrix_g, matrix_i, matrix_m, matrix_v, l, b
         matrix_m[idx] = m
 
 
+def conv_adam_mini_grads(matrix_g, matrix_i, inputs, window_in, window_out, variables, step):
+    """Per-weight gradients of UpdateWeightsConvAdamMini (NeuroNet.cl:7632-7647): over
+    total = (inputs - window_in + step - 1) / step units, stopping once i + t*window_in >= inputs
+    (the reference's test, with window_in where the stride is step), non-finite terms skipped.
+    Returns [variables][window_out][window_in + 1]."""
+    total = (inputs - window_in + step - 1) // step
+    G = np.zeros((variables, window_out, window_in + 1), F32)
+    with _err():
+        for v in range(variables):
+            for i in range(window_in + 1):
+                acc = np.zeros(window_out, F32)
+                for t in range(total):
+                    if i != window_in and i + t * window_in >= inputs:
+                        break
+                    gr = matrix_g[v * total * window_out + t * window_out:v * total * window_out + (t + 1) * window_out]
+                    xi = F32(1) if i == window_in else F32(matrix_i[v * inputs + i + t * step])
+                    gt = (gr * xi).astype(F32)
+                    acc = np.where(np.isfinite(gt), (acc + gt).astype(F32), acc)
+                G[v, :, i] = acc
+    return G
+
+
+def conv_adam_mini_scale(G_head, window_in, window_out_h):
+    """The local reduction of UpdateWeightsConvAdamMini (NeuroNet.cl:7649-7680) for one head of one
+    variable: slot s of ls = min(64, window_in) sums grad^2 / (window_in * window_out_h) over the
+    head's rows h (outer) and the local ids i = s, s + ls, ... its count loop reaches (the bias
+    column only when window_in % ls != 0), then the fold that stops one step early."""
+    ls = min(LOCAL_ARRAY_SIZE, window_in)
+    temp = np.zeros(max(ls, 1), F32)
+    n_counts = -(-window_in // ls)
+    den = F32(window_in * window_out_h)
+    with _err():
+        for h in range(window_out_h):
+            for count in range(n_counts):
+                for shift in range(ls):
+                    i = count * ls + shift
+                    if i > window_in:
+                        continue
+                    gv = G_head[h, i]
+                    term = F32(0) if not np.isfinite(gv) else F32(gv * gv) / den
+                    temp[shift] = F32((F32(0) if (count == 0 and h == 0) else temp[shift]) + term)
+        count = (ls + 1) // 2
+        while True:
+            for i in range(count):
+                if i + count < ls:
+                    temp[i] = F32(temp[i] + temp[i + count])
+                    temp[i + count] = 0
+            count = (count + 1) // 2
+            if not count > 1:
+                break
+    return temp[0]
+
+
+def UpdateWeightsConvAdamMini(matrix_w, matrix_g, matrix_i, matrix_m, matrix_v, inputs, l, b1, b2, step, gsize,
+                              lsize=None):
+    """NeuroNet.cl:7615-7731 over global (window_in+1, window_out, variables), local
+    (window_in+1, window_out_h, 1): one second moment per head (window_out_h rows), clamped to
+    [1e-6, 1e6]; m clamped to +-1e5; w += l m / sqrt(v) with no decay.  The second moment is indexed
+    by head only, so work-groups of different variables update the same entry (a race in the
+    reference); here the variables take their turns in order."""
+    window_in, window_out = gsize[0] - 1, gsize[1]
+    variables = gsize[2] if len(gsize) > 2 else 1
+    window_out_h = lsize[1] if lsize is not None and len(lsize) > 1 else 1
+    G = conv_adam_mini_grads(matrix_g, matrix_i, inputs, window_in, window_out, variables, step)
+    b1, b2, l = F32(b1), F32(b2), F32(l)
+    with _err():
+        for v in range(variables):
+            for head in range(window_out // window_out_h):
+                f0 = head * window_out_h
+                t0 = conv_adam_mini_scale(G[v, f0:f0 + window_out_h], window_in, window_out_h)
+                if not np.isfinite(t0):
+                    t0 = F32(1)
+                vv = matrix_v[head]
+                if not np.isfinite(vv):
+                    vv = F32(1)
+                t0 = F32(cl_clamp(F32(b2 * vv + (F32(1) - b2) * t0), 1e-6, 1e6))
+                matrix_v[head] = t0
+                rows = (np.arange(f0, f0 + window_out_h) + v * window_out)[:, None] * (window_in + 1)
+                idx = rows + np.arange(window_in + 1)[None, :]
+                mt = cl_clamp((b1 * matrix_m[idx] + (F32(1) - b1) * G[v, f0:f0 + window_out_h]).astype(F32), -1e5,
+                              1e5)
+                mt = np.where(np.isfinite(mt), mt, F32(0)).astype(F32)
+                w = (matrix_w[idx] + (l * mt / np.sqrt(t0)).astype(F32)).astype(F32)
+                matrix_w[idx] = np.where(np.isfinite(w), w, matrix_w[idx])
+                matrix_m[idx] = mt
+
+
 # ---------------------------------------------------------------- concatenate
 def _concat_rows(matrix_w, n_out, inputs1, inputs2):
     return matrix_w[:n_out * (inputs1 + inputs2 + 1)].reshape(n_out, inputs1 + inputs2 + 1)

@@ -302,6 +302,19 @@ def _adam_mini_cases():
                           [A(n_out * (n_in + 1), "uniform", 1 / np.sqrt(n_in)), A(n_out, "grad"), A(n_in),
                            A(n_out * (n_in + 1), "small"), A(n_out, "pos", 1e-5), 3e-4, 0.9, 0.999],
                           (n_in + 1, n_out), (n_in + 1, 1)))
+    # UpdateWeightsConvAdamMini (NeuroNet.cl:7615-7731), one variable (several race in the reference):
+    # (inputs, window, step, window_out, heads)
+    for inputs, win, step, wout, heads in [(512, 16, 8, 32, 4), (120, 64, 64, 24, 3), (60, 6, 3, 8, 2),
+                                           (130, 65, 65, 4, 1), (96, 128, 128, 5, 5)]:
+        if win > inputs:
+            continue
+        total = (inputs - win + step - 1) // step
+        nw = wout * (win + 1)
+        cases.append(Case(f"UpdateWeightsConvAdamMini/{inputs}-{win}-{step}-{wout}-h{heads}",
+                          "UpdateWeightsConvAdamMini",
+                          [A(nw, "uniform", 1 / np.sqrt(win + 1)), A(total * wout, "grad"), A(inputs), A(nw, "small"),
+                           A(heads, "pos", 1e-5), inputs, 3e-4, 0.9, 0.999, step],
+                          (win + 1, wout, 1), (win + 1, wout // heads, 1)))
     return cases
 
 

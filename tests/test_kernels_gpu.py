@@ -218,3 +218,24 @@ def test_batched_batchnorm_scans_samples_in_order(ctx, opt):
     check_close("bn options after update", ctx.read(ho, N * width), o_upd, o)
     for h in (hx, hy, ho, hg, hig):
         ctx.free(h)
+
+
+@pytest.mark.parametrize("variables", [1, 3])
+def test_conv_adam_mini_variables_take_turns(ctx, variables):
+    """UpdateWeightsConvAdamMini with several variables: the per-head second moment is updated by
+    each variable in turn (the reference's work-groups race on it), as the oracle defines."""
+    inputs, win, step, wout, heads = 200, 20, 10, 16, 4
+    total = (inputs - win + step - 1) // step
+    rng = np.random.default_rng(40 + variables)
+    nw = variables * wout * (win + 1)
+    args = [rng.uniform(-0.2, 0.2, nw).astype(np.float32), (rng.standard_normal(variables * total * wout) * 0.01)
+            .astype(np.float32), rng.standard_normal(variables * inputs).astype(np.float32),
+            (rng.standard_normal(nw) * 1e-3).astype(np.float32), rng.uniform(0, 1e-5, heads).astype(np.float32),
+            inputs, 3e-4, 0.9, 0.999, step]
+    gsize, lsize = (win + 1, wout, variables), (win + 1, wout // heads, 1)
+    before = [a.copy() if isinstance(a, np.ndarray) else None for a in args]
+    got = run_on_gpu(ctx, "UpdateWeightsConvAdamMini", [a.copy() if isinstance(a, np.ndarray) else a for a in args],
+                     gsize, lsize)
+    K.launch("UpdateWeightsConvAdamMini", gsize, lsize, args)
+    for i in (0, 3, 4):
+        check_close(f"variables{variables} arg{i}", got[i], args[i], before[i])
