@@ -24,7 +24,8 @@ SGD, ADAM, LS, ADAM_MINI = 0, 1, 2, 3
 SIGNATURES = {
     "FeedForward": "pppiipi", "CalcOutputGradient": "pppif", "CalcHiddenGradient": "ppppii",
     "UpdateWeightsMomentum": "ppppiff", "UpdateWeightsAdam": "pppppifff",
-    "UpdateWeightsAdamMini": "pppppfff", "UpdateWeightsConvAdamMini": "pppppifffi", "NormalizeWeights": "pi",
+    "UpdateWeightsAdamMini": "pppppfff", "UpdateWeightsConvAdamMini": "pppppifffi",
+    "MatMult": "pppiiiiipi", "MatMultGrad": "pppppiiiiiii", "NormalizeWeights": "pi",
     "Activation": "ppi", "DeActivation": "pppi", "SoftUpdate": "ppf", "SoftUpdateAdam": "ppppfff",
     "FeedForwardConv": "pppiiiii", "CalcHiddenGradientConv": "ppppiiiiii",
     "UpdateWeightsConvAdam": "pppppifffiii", "UpdateWeightsConvMomentum": "ppppiffiii",

@@ -100,6 +100,8 @@ extern const KernelDef kAttn2Kernels[];
 extern const int kNumAttn2Kernels;
 extern const KernelDef kSacKernels[];
 extern const int kNumSacKernels;
+extern const KernelDef kMatKernels[];
+extern const int kNumMatKernels;
 
 // Number of data-parallel ranks (1 without a communicator).
 int dp_world();

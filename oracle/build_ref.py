@@ -47,7 +47,7 @@ KERNELS = [
     "Transpose", "MH2AttentionOut", "MH2AttentionInsideGradients",
     "RevInFeedForward", "RevInHiddenGraddient", "Activation", "DeActivation",
     "Concat_FeedForward", "Concat_HiddenGradient", "Concat_UpdateWeightsMomentum", "Concat_UpdateWeightsAdam",
-    "UpdateWeightsAdamMini", "UpdateWeightsConvAdamMini",
+    "UpdateWeightsAdamMini", "UpdateWeightsConvAdamMini", "MatMult", "MatMultGrad",
 ]
 
 

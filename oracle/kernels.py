@@ -1100,6 +1100,65 @@ def Concat_UpdateWeightsMomentum(matrix_w, matrix_g, matrix_i1, matrix_i2, matri
     concat_momentum_apply(matrix_w, grad, matrix_dw, inputs1, inputs2, learning_rates, momentum, n_out, n_col)
 
 
+# ------------------------------------------------------- general matrix products
+def _seq_sum(p, axis):
+    """Sequential float32 sums along `axis` (the reference's loop order) and their running values."""
+    if p.shape[axis] == 0:
+        shape = list(p.shape)
+        del shape[axis]
+        return np.zeros(shape, F32), np.ones(shape, bool)
+    cs = np.cumsum(p, axis=axis, dtype=F32)
+    return np.take(cs, -1, axis=axis), np.isfinite(cs).all(axis=axis)
+
+
+def MatMult(matr1, matr2, result, dimension, multvarsecond, offset_matr1, offset_matr2, offset_result,
+            numeric_flags, flags_enabled, gsize, lsize=None):
+    """NeuroNet.cl:5969-6013 over global (rows, cols, variables): result[v] = matr1[v] . matr2[v or 0],
+    every product through IsNaNOrInf(., 0) and summed in order; with flags_enabled,
+    numeric_flags[v][row][col] = 1 where an operand, a product or the running sum was not finite."""
+    rows, cols, var = (tuple(gsize) + (1, 1))[:3]
+    dim, mvs = dimension, 1 if multvarsecond else 0
+    with _err():
+        for v in range(var):
+            a = matr1[offset_matr1 + v * rows * dim:][:rows * dim].reshape(rows, dim)
+            b = matr2[offset_matr2 + mvs * v * dim * cols:][:dim * cols].reshape(dim, cols)
+            p = (a[:, :, None] * b[None, :, :]).astype(F32)           # [row][i][col]
+            fin = np.isfinite(p)
+            res, run_ok = _seq_sum(np.where(fin, p, F32(0)).astype(F32), 1)
+            result[offset_result + v * rows * cols:][:rows * cols] = res.reshape(-1)
+            if flags_enabled:
+                operands_ok = (np.isfinite(a)[:, :, None] & np.isfinite(b)[None, :, :]).all(axis=1)
+                invalid = ~(operands_ok & fin.all(axis=1) & run_ok & np.isfinite(res))
+                numeric_flags[v * rows * cols:(v + 1) * rows * cols] = invalid.reshape(-1).astype(F32)
+
+
+def MatMultGrad(matr1, matr1_gr, matr2, matr2_gr, result_gr, dimension, multvarsecond, offset_matr1,
+                offset_matr1_gr, offset_matr2, offset_matr2_gr, offset_result_gr, gsize, lsize=None):
+    """NeuroNet.cl:6018-6060 over global (rows, cols, variables): matr1_gr[v] = result_gr[v] .
+    matr2[v]^T and matr2_gr = matr1[v]^T . result_gr[v] (summed over every variable, into the one
+    shared matrix, when multvarsecond is 0); products and sums through IsNaNOrInf(., 0)."""
+    rows, cols, var = (tuple(gsize) + (1, 1))[:3]
+    dim, mvs = dimension, 1 if multvarsecond else 0
+    with _err():
+        def blocks(v):
+            a = matr1[offset_matr1 + v * rows * dim:][:rows * dim].reshape(rows, dim)
+            b = matr2[offset_matr2 + mvs * v * dim * cols:][:dim * cols].reshape(dim, cols)
+            g = result_gr[offset_result_gr + v * rows * cols:][:rows * cols].reshape(rows, cols)
+            return a, b, g
+        for v in range(var):
+            a, b, g = blocks(v)
+            p = (g[:, None, :] * b[None, :, :]).astype(F32)          # [row][feature][i]
+            s, _ = _seq_sum(nan0(p), 2)
+            matr1_gr[offset_matr1_gr + v * rows * dim:][:rows * dim] = nan0(s).reshape(-1)
+        for v in (range(var) if mvs else [0]):
+            parts = [blocks(v)] if mvs else [blocks(u) for u in range(var)]
+            a = np.concatenate([q[0] for q in parts], axis=0)             # [(v,) i][feature]
+            g = np.concatenate([q[2] for q in parts], axis=0)             # [(v,) i][col]
+            p = (a.T[:, :, None] * g[None, :, :]).astype(F32)          # [feature][i][col]
+            s, _ = _seq_sum(nan0(p), 1)
+            matr2_gr[offset_matr2_gr + v * dim * cols:][:dim * cols] = nan0(s).reshape(-1)
+
+
 # --------------------------------------------------------- soft actor-critic
 # The library's squashed-Gaussian SAC kernels (no reference counterpart; the reference's SAC agents
 # use quantile heads).  A launch covers gsize[0] * batch samples; here gsize[0] is the sample count.

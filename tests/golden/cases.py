@@ -63,6 +63,17 @@ def materialise(case: Case, seed: int) -> list:
             v = rng.uniform(0.0, 1.0, n)
         elif a.init == "grad":
             v = rng.standard_normal(n) * 0.01 * a.scale
+        elif a.init == "nanmix":
+            # normal values with a few NaN and +-inf entries (the IsNaNOrInf paths)
+            v = rng.standard_normal(n) * a.scale
+            pick = rng.uniform(0.0, 1.0, n)
+            v[pick < 0.02] = np.nan
+            v[(pick >= 0.02) & (pick < 0.03)] = np.inf
+            v[(pick >= 0.03) & (pick < 0.04)] = -np.inf
+        elif a.init == "huge":
+            # normal values, one in ten scaled to 1e20 (products of two of them overflow float)
+            v = rng.standard_normal(n) * a.scale
+            v[rng.uniform(0.0, 1.0, n) < 0.1] *= 1e20
         elif a.init.startswith("act:"):
             # a plausible activation output for the given activation (used by Deactivation inputs)
             act = int(a.init[4:])
@@ -318,9 +329,42 @@ def _adam_mini_cases():
     return cases
 
 
+def _matmul_cases():
+    """MatMult / MatMultGrad (NeuroNet.cl:5969-6060): per-variable and shared second matrices, raw
+    offsets, the ReduceNumericFlags dot product (NeuroNet_Core.mqh:18606-18636), numeric flags over
+    NaN/inf operands and over products that overflow, tensor-core and split-k sizes."""
+    cases = []
+    # (rows, dim, cols, variables, multvarsecond, (off1, off2, offr), flags, init)
+    for rows, dim, cols, var, mvs, offs, flags, init in [
+            (5, 7, 3, 1, 1, (0, 0, 0), 0, "normal"), (64, 64, 64, 2, 1, (0, 0, 0), 0, "normal"),
+            (130, 96, 72, 3, 0, (3, 5, 2), 0, "normal"), (1, 300, 1, 1, 0, (0, 0, 0), 0, "normal"),
+            (256, 128, 96, 2, 1, (0, 0, 0), 0, "normal"), (2, 5000, 3, 1, 1, (1, 0, 4), 0, "normal"),
+            (33, 20, 17, 2, 1, (0, 0, 0), 1, "nanmix"), (9, 40, 11, 2, 0, (2, 1, 0), 1, "huge"),
+            (70, 33, 65, 1, 1, (0, 0, 0), 1, "normal"), (1, 0, 4, 2, 1, (1, 1, 0), 1, "normal")]:
+        o1, o2, orr = offs
+        n_out = var * rows * cols
+        cases.append(Case(f"MatMult/{rows}x{dim}x{cols}-v{var}-m{mvs}-f{flags}-{init}", "MatMult",
+                          [A(o1 + var * rows * dim, init), A(o2 + (var if mvs else 1) * dim * cols, init),
+                           A(orr + n_out), dim, mvs, o1, o2, orr, A(n_out, "zeros"), flags],
+                          (rows, cols, var)))
+    # (rows, dim, cols, variables, multvarsecond, (off1, off1g, off2, off2g, offr), init)
+    for rows, dim, cols, var, mvs, offs, init in [
+            (5, 7, 3, 1, 1, (0, 0, 0, 0, 0), "normal"), (64, 48, 40, 3, 0, (1, 2, 3, 4, 5), "normal"),
+            (256, 128, 96, 2, 1, (0, 0, 0, 0, 0), "normal"), (1000, 16, 8, 4, 0, (0, 0, 0, 0, 0), "normal"),
+            (3, 70, 2, 2, 1, (0, 0, 0, 0, 0), "normal"), (17, 9, 33, 2, 1, (0, 0, 0, 0, 0), "nanmix")]:
+        o1, o1g, o2, o2g, orr = offs
+        n1, n2 = var * rows * dim, (var if mvs else 1) * dim * cols
+        cases.append(Case(f"MatMultGrad/{rows}x{dim}x{cols}-v{var}-m{mvs}-{init}", "MatMultGrad",
+                          [A(o1 + n1, init), A(o1g + n1, "zeros"), A(o2 + n2, init), A(o2g + n2, "zeros"),
+                           A(orr + var * rows * cols, "grad" if init == "normal" else init), dim, mvs,
+                           o1, o1g, o2, o2g, orr],
+                          (rows, cols, var)))
+    return cases
+
+
 def all_cases() -> list[Case]:
     return (_dense_cases() + _conv_cases() + _attention_cases() + _norm_cases() + _batchnorm_cases() + _lstm_cases()
-            + _attention2_cases() + _concat_cases() + _adam_mini_cases())
+            + _attention2_cases() + _concat_cases() + _adam_mini_cases() + _matmul_cases())
 
 
 def prepare_inputs(case: Case, seed: int) -> list:

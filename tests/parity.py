@@ -45,7 +45,8 @@ def check_close(label: str, got, ref, before=None, rtol: float = RTOL, delta_rto
         raise AssertionError(f"{label}: rel err {e:.3e} > {rtol:g} (worst at {idx}: got {np.ravel(got)[idx]!r}, "
                              f"ref {np.ravel(ref)[idx]!r})")
     if before is not None:
-        dref = np.asarray(ref, np.float64) - np.asarray(before, np.float64)
+        with np.errstate(invalid="ignore"):  # inf - inf where an input holds infinities
+            dref = np.asarray(ref, np.float64) - np.asarray(before, np.float64)
         if np.abs(dref).max() > 0:
             dgot = np.asarray(got, np.float64) - np.asarray(before, np.float64)
             de = rel_err(dgot, dref)
