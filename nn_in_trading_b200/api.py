@@ -25,7 +25,10 @@ SIGNATURES = {
     "FeedForward": "pppiipi", "CalcOutputGradient": "pppif", "CalcHiddenGradient": "ppppii",
     "UpdateWeightsMomentum": "ppppiff", "UpdateWeightsAdam": "pppppifff",
     "UpdateWeightsAdamMini": "pppppfff", "UpdateWeightsConvAdamMini": "pppppifffi",
-    "MatMult": "pppiiiiipi", "MatMultGrad": "pppppiiiiiii", "NormalizeWeights": "pi",
+    "MatMult": "pppiiiiipi", "MatMultGrad": "pppppiiiiiii",
+    "FQF_Cosine": "pp", "FQF_Output": "pppi", "FQF_OutputGradient": "ppppp", "FQF_QuantileGradient": "ppppp",
+    "FQF_CosineGradient": "ppp", "SAC_AlphaLogProbs": "ppppppii", "SAC_AlphaGradients": "ppppi",
+    "SAC_OutputGradient": "ppppppii", "SAC_CalcLogProbs": "pppppii", "NormalizeWeights": "pi",
     "Activation": "ppi", "DeActivation": "pppi", "SoftUpdate": "ppf", "SoftUpdateAdam": "ppppfff",
     "FeedForwardConv": "pppiiiii", "CalcHiddenGradientConv": "ppppiiiiii",
     "UpdateWeightsConvAdam": "pppppifffiii", "UpdateWeightsConvMomentum": "ppppiffiii",

@@ -1,0 +1,333 @@
+// Quantile heads of the reference's distributional agents: CNeuronFQF (fully parameterised
+// quantile function) and CNeuronSoftActorCritic's quantile-sampled actions.
+//   FQF_Cosine             cos(pi i tau_i), tau_i = sum_{t<i} p_t + p_i / 2   NeuroNet.cl:2524-2538
+//   FQF_Output             y = sum_i quantile_i dtau_i                        NeuroNet.cl:2543-2553
+//   FQF_OutputGradient     quantile and tau gradients of y                   NeuroNet.cl:2560-2573
+//   FQF_QuantileGradient   state and tau-embedding gradients of their product NeuroNet.cl:2579-2592
+//   FQF_CosineGradient     softmax gradient through every tau_t, t >= i       NeuroNet.cl:2598-2624
+//   SAC_AlphaLogProbs      sample a quantile by its probability, -alpha log p NeuroNet.cl:3903-3933
+//   SAC_AlphaGradients     gradient of alpha                                 NeuroNet.cl:3939-3951
+//   SAC_OutputGradient     gradient into the quantiles bracketing the action NeuroNet.cl:3957-4000
+//   SAC_CalcLogProbs       -alpha log p of an action between two quantiles   NeuroNet.cl:4006-4036
+// The FQF kernels run over (quants, actions): one warp per action, the running sums of the
+// fractions as warp scans (the reference loops over the prefix in every work-item).  FQF_CosineGradient's
+// inner loop is a suffix sum that does not depend on i, so it is one scan too.  The SAC kernels keep
+// one thread per action and the reference's sequential searches (the sampled quantile is the first
+// whose running probability reaches the random number, so the sums run in its order).
+// Batches: every buffer is per sample; a launch covers actions x batch rows.
+#include "../../include/nn_b200.h"
+#include "nn_device.cuh"
+#include "nn_internal.h"
+
+namespace nn {
+namespace {
+
+constexpr float kPiF = 3.14159265358979f;
+constexpr unsigned kFull = 0xffffffffu;
+
+// Exclusive prefix of x over the lanes, and the chunk total.
+__device__ __forceinline__ float warp_exclusive(float x, int lane, float *chunk_total) {
+  float inc = x;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const float y = __shfl_up_sync(kFull, inc, d);
+    if (lane >= d) inc += y;
+  }
+  *chunk_total = __shfl_sync(kFull, inc, 31);
+  const float ex = __shfl_up_sync(kFull, inc, 1);
+  return lane == 0 ? 0.f : ex;
+}
+
+__global__ void fqf_cosine_kernel(const float *__restrict__ sm, float *__restrict__ out, int total, long long rows) {
+  const long long a = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (a >= rows) return;
+  const float *s = sm + a * total;
+  float carry = 0.f;
+  for (int c0 = 0; c0 < total; c0 += 32) {
+    const int i = c0 + lane;
+    const float x = i < total ? s[i] : 0.f;
+    float ct;
+    const float ex = warp_exclusive(x, lane, &ct);
+    if (i < total) out[a * total + i] = cosf((float)i * kPiF * (carry + ex + x / 2.0f));
+    carry += ct;
+  }
+}
+
+__global__ void fqf_output_kernel(const float *__restrict__ q, const float *__restrict__ dt, float *__restrict__ y,
+                                  int total, long long rows) {
+  const long long a = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (a >= rows) return;
+  float s = 0.f;
+  for (int i = lane; i < total; i += 32) s += q[a * total + i] * dt[a * total + i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(kFull, s, o);
+  if (lane == 0) y[a] = s;
+}
+
+// out1[e] = g[e / per] * in1[e], out2[e] = g[e / per] * in2[e]  (per = total: OutputGradient;
+// per = 1: QuantileGradient, where g is itself per element)
+__global__ void fqf_pair_grad_kernel(const float *__restrict__ in1, const float *__restrict__ in2,
+                                     const float *__restrict__ g, float *__restrict__ out1, float *__restrict__ out2,
+                                     int per, long long n) {
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
+    const float gr = g[e / per];
+    out1[e] = gr * in1[e];
+    out2[e] = gr * in2[e];
+  }
+}
+
+// softmax_gr[i] += -pi i sin(pi i tau_i) g_i + sum_{t>i} -pi t sin(pi t tau_t) g_t p_t / tau_t.
+// The chunks of 32 fractions run from the last to the first so that the suffix sum is a running
+// total (a term that is not finite reaches only the i below it, as in the reference); a chunk's
+// starting tau is the row total less the later chunks (exactly 0 for rows of at most 32).
+__global__ void fqf_cosine_grad_kernel(const float *__restrict__ sm, const float *__restrict__ og,
+                                       float *__restrict__ sg, int total, long long rows) {
+  const long long a = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (a >= rows) return;
+  const float *s = sm + a * total;
+  const float *g = og + a * total;
+  const int last = total > 0 ? (total - 1) / 32 * 32 : -32;
+  float total_s = 0.f, ct;
+  for (int c0 = 0; c0 <= last; c0 += 32) {
+    const int i = c0 + lane;
+    warp_exclusive(i < total ? s[i] : 0.f, lane, &ct);
+    total_s += ct;
+  }
+  float after_s = 0.f, after_f = 0.f;
+  for (int c0 = last; c0 >= 0; c0 -= 32) {
+    const int i = c0 + lane;
+    const float x = i < total ? s[i] : 0.f;
+    const float ex = warp_exclusive(x, lane, &ct);
+    const float tau = (total_s - after_s - ct) + ex + x / 2;
+    const float fi = (float)i;
+    const float gi = i < total ? g[i] : 0.f;
+    const float sn = sinf(kPiF * fi * tau);
+    const float first = -kPiF * fi * sn * gi;
+    const float f = i < total && i > 0 ? -kPiF * fi * sn * gi * x / tau : 0.f;
+    float inc = f;  // inclusive suffix over the lanes
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const float y = __shfl_down_sync(kFull, inc, d);
+      if (lane + d < 32) inc += y;
+    }
+    const float later = __shfl_down_sync(kFull, inc, 1);
+    if (i < total) sg[a * total + i] += first + (after_f + (lane == 31 ? 0.f : later));
+    after_f += __shfl_sync(kFull, inc, 0);
+    after_s += ct;
+  }
+}
+
+__global__ void sac_alpha_log_probs_kernel(float *__restrict__ out, const float *__restrict__ q,
+                                           const float *__restrict__ probs, const float *__restrict__ alphas,
+                                           float *__restrict__ lp, const float *__restrict__ rnd, int cq, int act,
+                                           long long n) {
+  const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float *p = probs + i * cq;
+  const float r = rnd[i];
+  float prob = 0.f, value = 0.f, sum = 0.f;
+  for (int k = 0; k < cq; ++k) {
+    prob = p[k];
+    sum += prob;
+    if (sum >= r || k == cq - 1) {
+      value = q[i * cq + k];
+      break;
+    }
+  }
+  out[i] = activate(value, act);
+  lp[i] = -alphas[i] * logf(prob);
+}
+
+__global__ void sac_alpha_grad_kernel(const float *__restrict__ out, const float *__restrict__ g,
+                                      const float *__restrict__ lp, float *__restrict__ ag, int act, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    ag[i] = deactivate(-g[i] * lp[i], out[i], act);
+}
+
+__global__ void sac_output_grad_kernel(const float *__restrict__ q, const float *__restrict__ dt,
+                                       const float *__restrict__ og, float *__restrict__ qg, float *__restrict__ tg,
+                                       const float *__restrict__ out, int cq, int act, long long n) {
+  const long long a = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (a >= n) return;
+  const long long shift = a * cq;
+  float q1 = -1e37f, q2 = 1e37f;
+  long long p1 = -1, p2 = -1;
+  const float v = out[a];
+  for (int k = 0; k < cq; ++k) {
+    const float qq = activate(q[shift + k], act);
+    if (v >= qq && q1 < qq) {
+      q1 = qq;
+      p1 = shift + k;
+    }
+    if (v < qq && q2 > qq) {
+      q2 = qq;
+      p2 = shift + k;
+    }
+    qg[shift + k] = 0.f;
+    tg[shift + k] = 0.f;
+  }
+  const float gr = og[a];
+  if (q1 > -1e37f) {
+    qg[p1] = gr * dt[p1];
+    tg[p1] = gr * q1;
+  }
+  if (q2 < 1e37f) {
+    qg[p2] = gr * dt[p2];
+    tg[p2] = gr * q2;
+  }
+}
+
+__global__ void sac_calc_log_probs_kernel(const float *__restrict__ out, const float *__restrict__ q,
+                                          const float *__restrict__ probs, const float *__restrict__ alphas,
+                                          float *__restrict__ lp, int cq, int act, long long n) {
+  const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float q1 = -1e37f, q2 = 1e37f, pr1 = 0.f, pr2 = 0.f;
+  const float v = out[i];
+  for (int k = 0; k < cq; ++k) {
+    const float qq = activate(q[i * cq + k], act);
+    if (v >= qq && q1 < qq) {
+      q1 = qq;
+      pr1 = probs[i * cq + k];
+    }
+    if (v < qq && q2 > qq) {
+      q2 = qq;
+      pr2 = probs[i * cq + k];
+    }
+  }
+  float prob = fabsf(v - q1) / fabsf(q2 - q1);
+  prob = fminf(fmaxf((1.f - prob) * pr1 + prob * pr2, 1.0e-3f), 1.0f);
+  lp[i] = -alphas[i] * logf(prob);
+}
+
+dim3 warp_grid(long long rows) { return dim3((unsigned)((rows * 32 + 255) / 256)); }
+
+// (quants, actions) kernels: total = global[0], rows = actions x batch.
+void quant_shape(const Launch &L, int *total, long long *rows) {
+  *total = (int)L.nd.g[0];
+  *rows = (long long)(L.nd.dims > 1 ? L.nd.g[1] : 1) * L.B;
+}
+
+int k_fqf_cosine(Launch &L) {
+  int T;
+  long long R;
+  quant_shape(L, &T, &R);
+  float *sm = L.buf(0, (size_t)R * T), *out = L.buf(1, (size_t)R * T);
+  if (!sm || !out) return NN_ERR_BOUNDS;
+  fqf_cosine_kernel<<<warp_grid(R), 256, 0, L.stream>>>(sm, out, T, R);
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
+int k_fqf_output(Launch &L) {
+  const long long R = (long long)L.nd.g[0] * L.B;
+  const int T = L.i(3);
+  if (T < 0) return L.fail(NN_ERR_ARG, "FQF_Output: negative total");
+  float *q = L.buf(0, (size_t)R * T), *dt = L.buf(1, (size_t)R * T), *y = L.buf(2, (size_t)R);
+  if (!q || !dt || !y) return NN_ERR_BOUNDS;
+  fqf_output_kernel<<<warp_grid(R), 256, 0, L.stream>>>(q, dt, y, T, R);
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
+int k_fqf_output_grad(Launch &L) {
+  int T;
+  long long R;
+  quant_shape(L, &T, &R);
+  const size_t n = (size_t)R * T;
+  float *q = L.buf(0, n), *dt = L.buf(1, n), *og = L.buf(2, (size_t)R), *qg = L.buf(3, n), *tg = L.buf(4, n);
+  if (!q || !dt || !og || !qg || !tg) return NN_ERR_BOUNDS;
+  fqf_pair_grad_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(dt, q, og, qg, tg, T, (long long)n);
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
+int k_fqf_quantile_grad(Launch &L) {
+  int T;
+  long long R;
+  quant_shape(L, &T, &R);
+  const size_t n = (size_t)R * T;
+  float *se = L.buf(0, n), *te = L.buf(1, n), *qg = L.buf(2, n), *sg = L.buf(3, n), *tg = L.buf(4, n);
+  if (!se || !te || !qg || !sg || !tg) return NN_ERR_BOUNDS;
+  fqf_pair_grad_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(te, se, qg, sg, tg, 1, (long long)n);
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
+int k_fqf_cosine_grad(Launch &L) {
+  int T;
+  long long R;
+  quant_shape(L, &T, &R);
+  const size_t n = (size_t)R * T;
+  float *sm = L.buf(0, n), *og = L.buf(1, n), *sg = L.buf(2, n);
+  if (!sm || !og || !sg) return NN_ERR_BOUNDS;
+  fqf_cosine_grad_kernel<<<warp_grid(R), 256, 0, L.stream>>>(sm, og, sg, T, R);
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
+int k_sac_alpha_log_probs(Launch &L) {
+  const long long n = (long long)L.nd.g[0] * L.B;
+  const int cq = L.i(6), act = L.i(7);
+  if (cq < 0) return L.fail(NN_ERR_ARG, "SAC_AlphaLogProbs: negative count_quants");
+  float *out = L.buf(0, n), *q = L.buf(1, (size_t)n * cq), *p = L.buf(2, (size_t)n * cq), *al = L.buf(3, n);
+  float *lp = L.buf(4, n), *rnd = L.buf(5, n);
+  if (!out || !q || !p || !al || !lp || !rnd) return NN_ERR_BOUNDS;
+  sac_alpha_log_probs_kernel<<<grid1d(n, 128), 128, 0, L.stream>>>(out, q, p, al, lp, rnd, cq, act, n);
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
+int k_sac_alpha_grad(Launch &L) {
+  const long long n = (long long)L.nd.g[0] * L.B;
+  float *out = L.buf(0, n), *g = L.buf(1, n), *lp = L.buf(2, n), *ag = L.buf(3, n);
+  if (!out || !g || !lp || !ag) return NN_ERR_BOUNDS;
+  sac_alpha_grad_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(out, g, lp, ag, L.i(4), n);
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
+int k_sac_output_grad(Launch &L) {
+  const long long n = (long long)L.nd.g[0] * L.B;
+  const int cq = L.i(6), act = L.i(7);
+  if (cq < 0) return L.fail(NN_ERR_ARG, "SAC_OutputGradient: negative count_quants");
+  const size_t nq = (size_t)n * cq;
+  float *q = L.buf(0, nq), *dt = L.buf(1, nq), *og = L.buf(2, n), *qg = L.buf(3, nq), *tg = L.buf(4, nq);
+  float *out = L.buf(5, n);
+  if (!q || !dt || !og || !qg || !tg || !out) return NN_ERR_BOUNDS;
+  sac_output_grad_kernel<<<grid1d(n, 128), 128, 0, L.stream>>>(q, dt, og, qg, tg, out, cq, act, n);
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
+int k_sac_calc_log_probs(Launch &L) {
+  const long long n = (long long)L.nd.g[0] * L.B;
+  const int cq = L.i(5), act = L.i(6);
+  if (cq < 0) return L.fail(NN_ERR_ARG, "SAC_CalcLogProbs: negative count_quants");
+  float *out = L.buf(0, n), *q = L.buf(1, (size_t)n * cq), *p = L.buf(2, (size_t)n * cq), *al = L.buf(3, n);
+  float *lp = L.buf(4, n);
+  if (!out || !q || !p || !al || !lp) return NN_ERR_BOUNDS;
+  sac_calc_log_probs_kernel<<<grid1d(n, 128), 128, 0, L.stream>>>(out, q, p, al, lp, cq, act, n);
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
+}  // namespace
+
+const KernelDef kFqfKernels[] = {
+    {"FQF_Cosine", "pp", k_fqf_cosine, false},
+    {"FQF_Output", "pppi", k_fqf_output, false},
+    {"FQF_OutputGradient", "ppppp", k_fqf_output_grad, false},
+    {"FQF_QuantileGradient", "ppppp", k_fqf_quantile_grad, false},
+    {"FQF_CosineGradient", "ppp", k_fqf_cosine_grad, false},
+    {"SAC_AlphaLogProbs", "ppppppii", k_sac_alpha_log_probs, false},
+    {"SAC_AlphaGradients", "ppppi", k_sac_alpha_grad, false},
+    {"SAC_OutputGradient", "ppppppii", k_sac_output_grad, false},
+    {"SAC_CalcLogProbs", "pppppii", k_sac_calc_log_probs, false},
+};
+const int kNumFqfKernels = sizeof(kFqfKernels) / sizeof(kFqfKernels[0]);
+
+}  // namespace nn

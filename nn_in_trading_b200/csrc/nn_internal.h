@@ -102,6 +102,8 @@ extern const KernelDef kSacKernels[];
 extern const int kNumSacKernels;
 extern const KernelDef kMatKernels[];
 extern const int kNumMatKernels;
+extern const KernelDef kFqfKernels[];
+extern const int kNumFqfKernels;
 
 // Number of data-parallel ranks (1 without a communicator).
 int dp_world();

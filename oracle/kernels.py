@@ -1100,6 +1100,142 @@ def Concat_UpdateWeightsMomentum(matrix_w, matrix_g, matrix_i1, matrix_i2, matri
     concat_momentum_apply(matrix_w, grad, matrix_dw, inputs1, inputs2, learning_rates, momentum, n_out, n_col)
 
 
+# ------------------------------------------------------------ quantile heads
+PI_F = F32(np.pi)
+
+
+def _taus(sm):
+    """Fraction midpoints per row: sum_{t<i} p_t + p_i / 2, summed in order (float32)."""
+    cs = np.cumsum(sm, axis=1, dtype=F32)
+    return ((cs - sm).astype(F32) + sm / F32(2)).astype(F32)
+
+
+def FQF_Cosine(softmax, output, gsize, lsize=None):
+    """NeuroNet.cl:2524-2538 over global (quants, actions): cos(i pi tau_i)."""
+    T, R = gsize[0], (tuple(gsize) + (1,))[1]
+    with _err():
+        sm = softmax[:R * T].reshape(R, T).astype(F32)
+        i = np.arange(T, dtype=F32)[None, :]
+        output[:R * T] = np.cos((i * PI_F * _taus(sm)).astype(F32)).astype(F32).reshape(-1)
+
+
+def FQF_Output(quantiles, delta_taus, output, total, gsize, lsize=None):
+    """NeuroNet.cl:2543-2553 over global (actions): y = sum_i quantile_i dtau_i."""
+    R, T = gsize[0], total
+    with _err():
+        p = (quantiles[:R * T] * delta_taus[:R * T]).astype(F32).reshape(R, T)
+        output[:R] = _seq_sum(p, 1)[0]
+
+
+def FQF_OutputGradient(quantiles, delta_taus, output_gr, quantiles_gr, taus_gr, gsize, lsize=None):
+    """NeuroNet.cl:2560-2573 over global (quants, actions)."""
+    T, R = gsize[0], (tuple(gsize) + (1,))[1]
+    with _err():
+        g = np.repeat(output_gr[:R].astype(F32), T)
+        quantiles_gr[:R * T] = (g * delta_taus[:R * T]).astype(F32)
+        taus_gr[:R * T] = (g * quantiles[:R * T]).astype(F32)
+
+
+def FQF_QuantileGradient(state_embeding, taus_embeding, quantiles_gr, state_gr, taus_gr, gsize, lsize=None):
+    """NeuroNet.cl:2579-2592 over global (quants, actions)."""
+    n = gsize[0] * (tuple(gsize) + (1,))[1]
+    with _err():
+        g = quantiles_gr[:n].astype(F32)
+        state_gr[:n] = (g * taus_embeding[:n]).astype(F32)
+        taus_gr[:n] = (g * state_embeding[:n]).astype(F32)
+
+
+def FQF_CosineGradient(softmax, output_gr, softmax_gr, gsize, lsize=None):
+    """NeuroNet.cl:2598-2624 over global (quants, actions): softmax_gr[i] += -pi i sin(pi i tau_i) g_i
+    + sum_{t>i} -pi t sin(pi t tau_t) g_t p_t / tau_t (the later terms summed in order)."""
+    T, R = gsize[0], (tuple(gsize) + (1,))[1]
+    with _err():
+        sm = softmax[:R * T].reshape(R, T).astype(F32)
+        g = output_gr[:R * T].reshape(R, T).astype(F32)
+        tau = _taus(sm)
+        i = np.arange(T, dtype=F32)[None, :]
+        sn = np.sin((PI_F * i * tau).astype(F32)).astype(F32)
+        first = (-PI_F * i * sn * g).astype(F32)
+        f = ((-PI_F * i * sn * g * sm).astype(F32) / tau).astype(F32)
+        out = softmax_gr[:R * T].reshape(R, T).copy()
+        for k in range(T):
+            later, _ = _seq_sum(f[:, k + 1:], 1)
+            out[:, k] = (out[:, k] + (first[:, k] + later).astype(F32)).astype(F32)
+        softmax_gr[:R * T] = out.reshape(-1)
+
+
+def SAC_AlphaLogProbs(outputs, quantiles, probs, alphas, log_probs, random, count_quants, activation,
+                      gsize, lsize=None):
+    """NeuroNet.cl:3903-3933: the first quantile whose running probability reaches random[i] (the
+    last one otherwise), its activation, and -alpha log p of it."""
+    n, cq = gsize[0], count_quants
+    with _err():
+        for i in range(n):
+            prob = value = s = F32(0)
+            for r in range(cq):
+                prob = F32(probs[i * cq + r])
+                s = F32(s + prob)
+                if s >= random[i] or r == cq - 1:
+                    value = quantiles[i * cq + r]
+                    break
+            outputs[i] = f_activation(value, activation)
+            log_probs[i] = -alphas[i] * np.log(prob)
+
+
+def SAC_AlphaGradients(outputs, gradient, log_probs, alphas_grad, activation, gsize, lsize=None):
+    """NeuroNet.cl:3939-3951."""
+    n = gsize[0]
+    with _err():
+        alphas_grad[:n] = deactivation((-gradient[:n] * log_probs[:n]).astype(F32), outputs[:n], activation)
+
+
+def SAC_OutputGradient(quantiles, delta_taus, output_gr, quantiles_gr, taus_gr, output, count_quants, activation,
+                       gsize, lsize=None):
+    """NeuroNet.cl:3957-4000: the gradient goes to the largest activated quantile at or below the
+    action and the smallest above it; every other quantile and tau gradient is zero."""
+    n, cq = gsize[0], count_quants
+    with _err():
+        for a in range(n):
+            sh = a * cq
+            q = f_activation(quantiles[sh:sh + cq], activation)
+            v = output[a]
+            q1, q2, p1, p2 = F32(-1e37), F32(1e37), -1, -1
+            for k in range(cq):
+                if v >= q[k] and q1 < q[k]:
+                    q1, p1 = q[k], sh + k
+                if v < q[k] and q2 > q[k]:
+                    q2, p2 = q[k], sh + k
+            quantiles_gr[sh:sh + cq] = 0
+            taus_gr[sh:sh + cq] = 0
+            g = F32(output_gr[a])
+            if q1 > F32(-1e37):
+                quantiles_gr[p1] = g * delta_taus[p1]
+                taus_gr[p1] = g * q1
+            if q2 < F32(1e37):
+                quantiles_gr[p2] = g * delta_taus[p2]
+                taus_gr[p2] = g * q2
+
+
+def SAC_CalcLogProbs(outputs, quantiles, probs, alphas, log_probs, count_quants, activation, gsize, lsize=None):
+    """NeuroNet.cl:4006-4036: p interpolated between the quantiles bracketing the action, clamped
+    to [1e-3, 1], and -alpha log p."""
+    n, cq = gsize[0], count_quants
+    with _err():
+        for i in range(n):
+            sh = i * cq
+            q = f_activation(quantiles[sh:sh + cq], activation)
+            v = outputs[i]
+            q1, q2, pr1, pr2 = F32(-1e37), F32(1e37), F32(0), F32(0)
+            for k in range(cq):
+                if v >= q[k] and q1 < q[k]:
+                    q1, pr1 = q[k], probs[sh + k]
+                if v < q[k] and q2 > q[k]:
+                    q2, pr2 = q[k], probs[sh + k]
+            prob = F32(np.abs(F32(v - q1)) / np.abs(F32(q2 - q1)))
+            prob = cl_clamp(F32((F32(1) - prob) * pr1) + F32(prob * pr2), 1.0e-3, 1.0)
+            log_probs[i] = -alphas[i] * np.log(prob)
+
+
 # ------------------------------------------------------- general matrix products
 def _seq_sum(p, axis):
     """Sequential float32 sums along `axis` (the reference's loop order) and their running values."""

@@ -35,6 +35,7 @@ typedef unsigned short ushort;
 
 #define CLK_LOCAL_MEM_FENCE 1
 #define CLK_GLOBAL_MEM_FENCE 2
+#define M_PI_F 3.14159265358979323846f  /* OpenCL: pi as float */
 
 // ----------------------------------------------------------------- vectors
 struct float2 {

@@ -362,9 +362,40 @@ def _matmul_cases():
     return cases
 
 
+def _quantile_head_cases():
+    """CNeuronFQF and the quantile SAC head (NeuroNet.cl:2524-2624, 3903-4036): fractions from a
+    softmax (rows of 1, 8, 32 and 100 quants), sampled and interpolated quantiles, activations."""
+    cases = []
+    for T, R in [(32, 4), (8, 3), (100, 2), (1, 5), (33, 6)]:
+        sm = dict(softmax_rows=(R, T))
+        cases.append(Case(f"FQF_Cosine/{T}x{R}", "FQF_Cosine", [A(R * T, "unit"), A(R * T, "zeros")], (T, R),
+                          meta=sm))
+        cases.append(Case(f"FQF_Output/{T}x{R}", "FQF_Output", [A(R * T), A(R * T, "pos"), A(R, "zeros"), T], (R,)))
+        cases.append(Case(f"FQF_OutputGradient/{T}x{R}", "FQF_OutputGradient",
+                          [A(R * T), A(R * T, "pos"), A(R, "grad"), A(R * T, "zeros"), A(R * T, "zeros")], (T, R)))
+        cases.append(Case(f"FQF_QuantileGradient/{T}x{R}", "FQF_QuantileGradient",
+                          [A(R * T), A(R * T), A(R * T, "grad"), A(R * T, "zeros"), A(R * T, "zeros")], (T, R)))
+        cases.append(Case(f"FQF_CosineGradient/{T}x{R}", "FQF_CosineGradient",
+                          [A(R * T, "unit"), A(R * T, "grad"), A(R * T, "small")], (T, R), meta=sm))
+    for n, cq, act in [(16, 32, NONE), (7, 8, TANH), (40, 5, SIGMOID), (3, 1, NONE), (9, 64, LRELU)]:
+        cases.append(Case(f"SAC_AlphaLogProbs/{n}x{cq}-a{act}", "SAC_AlphaLogProbs",
+                          [A(n, "zeros"), A(n * cq), A(n * cq, "unit"), A(n, "pos"), A(n, "zeros"), A(n, "unit"),
+                           cq, act], (n,), meta=dict(softmax_rows=(n, cq))))
+        cases.append(Case(f"SAC_AlphaGradients/{n}-a{act}", "SAC_AlphaGradients",
+                          [A(n, f"act:{act}"), A(n, "grad"), A(n, "pos"), A(n, "zeros"), act], (n,)))
+        cases.append(Case(f"SAC_OutputGradient/{n}x{cq}-a{act}", "SAC_OutputGradient",
+                          [A(n * cq), A(n * cq, "pos"), A(n, "grad"), A(n * cq, "small"), A(n * cq, "small"),
+                           A(n, "normal", 0.7), cq, act], (n,)))
+        cases.append(Case(f"SAC_CalcLogProbs/{n}x{cq}-a{act}", "SAC_CalcLogProbs",
+                          [A(n, "normal", 0.7), A(n * cq), A(n * cq, "unit"), A(n, "pos"), A(n, "zeros"), cq, act],
+                          (n,), meta=dict(softmax_rows=(n, cq))))
+    return cases
+
+
 def all_cases() -> list[Case]:
     return (_dense_cases() + _conv_cases() + _attention_cases() + _norm_cases() + _batchnorm_cases() + _lstm_cases()
-            + _attention2_cases() + _concat_cases() + _adam_mini_cases() + _matmul_cases())
+            + _attention2_cases() + _concat_cases() + _adam_mini_cases() + _matmul_cases()
+            + _quantile_head_cases())
 
 
 def prepare_inputs(case: Case, seed: int) -> list:
