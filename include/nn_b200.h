@@ -150,7 +150,9 @@ NN_API int nn_set_arg_float(int id, int arg_index, float value);
  * kernel reads; parameter buffers (weights, moments, options) are shared.
  * Forward and input-gradient kernels produce the reference result for every
  * sample; weight-update kernels average the per-sample weight gradient over
- * the batch and then apply the reference update arithmetic once. */
+ * the batch and then apply the reference update arithmetic once.  MatMult and MatMultGrad
+ * take their batch in global[2] (variables; a shared second matrix with multvarsecond = 0,
+ * whose gradient MatMultGrad sums over it) and refuse a batch above 1 with NN_ERR_UNSUPPORTED. */
 NN_API int nn_set_batch(int id, int batch);
 /* COpenCL::Execute (NeuroNet_Definitions.mqh:69-90): enqueue one execution.
  * offset may be NULL (must be zero); local may be NULL. */

@@ -5,6 +5,7 @@
 //   FQF_OutputGradient     quantile and tau gradients of y                   NeuroNet.cl:2560-2573
 //   FQF_QuantileGradient   state and tau-embedding gradients of their product NeuroNet.cl:2579-2592
 //   FQF_CosineGradient     softmax gradient through every tau_t, t >= i       NeuroNet.cl:2598-2624
+//   FQF_FractionGradient   input gradient of the fraction proposal layer     NeuroNet.cl:3207-3224
 //   SAC_AlphaLogProbs      sample a quantile by its probability, -alpha log p NeuroNet.cl:3903-3933
 //   SAC_AlphaGradients     gradient of alpha                                 NeuroNet.cl:3939-3951
 //   SAC_OutputGradient     gradient into the quantiles bracketing the action NeuroNet.cl:3957-4000
@@ -14,7 +15,8 @@
 // inner loop is a suffix sum that does not depend on i, so it is one scan too.  The SAC kernels keep
 // one thread per action and the reference's sequential searches (the sampled quantile is the first
 // whose running probability reaches the random number, so the sums run in its order).
-// Batches: every buffer is per sample; a launch covers actions x batch rows.
+// Batches: every buffer is per sample (FQF_FractionGradient's weights are shared); a launch covers
+// actions x batch rows.
 #include "../../include/nn_b200.h"
 #include "nn_device.cuh"
 #include "nn_internal.h"
@@ -203,6 +205,27 @@ __global__ void sac_calc_log_probs_kernel(const float *__restrict__ out, const f
   lp[i] = -alphas[i] * logf(prob);
 }
 
+// FQF_FractionGradient: input_gr[i] = IsNaNOrInf(sum_k W[k][i] g[k], 0), W rows of inputs + 1.
+// Operands are summed as they are (a NaN weight zeroes the whole sum, as in the reference).  A CTA of
+// 8 warps per 32 columns, the warps splitting k; blockIdx.y is the sample.
+__global__ void __launch_bounds__(256) fqf_fraction_grad_kernel(const float *__restrict__ w,
+                                                                const float *__restrict__ g,
+                                                                float *__restrict__ ig, int inputs, int outputs) {
+  __shared__ float part[8][33];
+  const int col = blockIdx.x * 32 + (threadIdx.x & 31), wv = threadIdx.x >> 5;
+  const float *gb = g + (size_t)blockIdx.y * outputs;
+  float s = 0.f;
+  if (col < inputs)
+    for (int k = wv; k < outputs; k += 8) s += w[(size_t)k * (inputs + 1) + col] * gb[k];
+  part[wv][threadIdx.x & 31] = s;
+  __syncthreads();
+  if (wv == 0 && col < inputs) {
+#pragma unroll
+    for (int j = 1; j < 8; ++j) s += part[j][threadIdx.x];
+    ig[(size_t)blockIdx.y * inputs + col] = nan0(s);
+  }
+}
+
 dim3 warp_grid(long long rows) { return dim3((unsigned)((rows * 32 + 255) / 256)); }
 
 // (quants, actions) kernels: total = global[0], rows = actions x batch.
@@ -315,6 +338,17 @@ int k_sac_calc_log_probs(Launch &L) {
   return NN_OK;
 }
 
+int k_fqf_fraction_grad(Launch &L) {
+  const int inputs = (int)L.nd.g[0], outputs = L.i(3);
+  if (outputs < 0) return L.fail(NN_ERR_ARG, "FQF_FractionGradient: negative outputs");
+  float *w = L.buf(0, (size_t)outputs * (inputs + 1)), *g = L.buf(1, (size_t)L.B * outputs);
+  float *ig = L.buf(2, (size_t)L.B * inputs);
+  if (!w || !g || !ig) return NN_ERR_BOUNDS;
+  fqf_fraction_grad_kernel<<<dim3((inputs + 31) / 32, L.B), 256, 0, L.stream>>>(w, g, ig, inputs, outputs);
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
 }  // namespace
 
 const KernelDef kFqfKernels[] = {
@@ -323,6 +357,7 @@ const KernelDef kFqfKernels[] = {
     {"FQF_OutputGradient", "ppppp", k_fqf_output_grad, false},
     {"FQF_QuantileGradient", "ppppp", k_fqf_quantile_grad, false},
     {"FQF_CosineGradient", "ppp", k_fqf_cosine_grad, false},
+    {"FQF_FractionGradient", "pppi", k_fqf_fraction_grad, false},
     {"SAC_AlphaLogProbs", "ppppppii", k_sac_alpha_log_probs, false},
     {"SAC_AlphaGradients", "ppppi", k_sac_alpha_grad, false},
     {"SAC_OutputGradient", "ppppppii", k_sac_output_grad, false},

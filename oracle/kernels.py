@@ -1164,6 +1164,16 @@ def FQF_CosineGradient(softmax, output_gr, softmax_gr, gsize, lsize=None):
         softmax_gr[:R * T] = out.reshape(-1)
 
 
+def FQF_FractionGradient(matrix_w, gradient, input_gr, outputs, gsize, lsize=None):
+    """NeuroNet.cl:3207-3224 over global (inputs, 1): input_gr[i] = IsNaNOrInf(sum_k W[k][i] g[k], 0),
+    the operands summed as they are."""
+    inputs = gsize[0]
+    with _err():
+        w = matrix_w[:outputs * (inputs + 1)].reshape(outputs, inputs + 1)[:, :inputs].astype(F32)
+        p = (w * gradient[:outputs, None]).astype(F32)
+        input_gr[:inputs] = nan0(_seq_sum(p, 0)[0])
+
+
 def SAC_AlphaLogProbs(outputs, quantiles, probs, alphas, log_probs, random, count_quants, activation,
                       gsize, lsize=None):
     """NeuroNet.cl:3903-3933: the first quantile whose running probability reaches random[i] (the

@@ -377,6 +377,12 @@ def _quantile_head_cases():
                           [A(R * T), A(R * T), A(R * T, "grad"), A(R * T, "zeros"), A(R * T, "zeros")], (T, R)))
         cases.append(Case(f"FQF_CosineGradient/{T}x{R}", "FQF_CosineGradient",
                           [A(R * T, "unit"), A(R * T, "grad"), A(R * T, "small")], (T, R), meta=sm))
+    # FQF_FractionGradient (NeuroNet.cl:3207-3224): (inputs, outputs, local size along the outputs)
+    for n_in, n_out, loc, init in [(32, 64, 1, "normal"), (100, 33, 16, "normal"), (7, 300, 64, "normal"),
+                                   (65, 32, 1, "nanmix")]:
+        cases.append(Case(f"FQF_FractionGradient/{n_in}x{n_out}-l{loc}-{init}", "FQF_FractionGradient",
+                          [A(n_out * (n_in + 1), init, 0.1), A(n_out, "grad"), A(n_in, "zeros"), n_out],
+                          (n_in, loc), (1, loc)))
     for n, cq, act in [(16, 32, NONE), (7, 8, TANH), (40, 5, SIGMOID), (3, 1, NONE), (9, 64, LRELU)]:
         cases.append(Case(f"SAC_AlphaLogProbs/{n}x{cq}-a{act}", "SAC_AlphaLogProbs",
                           [A(n, "zeros"), A(n * cq), A(n * cq, "unit"), A(n, "pos"), A(n, "zeros"), A(n, "unit"),

@@ -74,7 +74,7 @@ PER_SAMPLE_KERNELS = {
     "SoftMax_FeedForward": [0, 1], "SoftMax_HiddenGradient": [0, 1, 2], "SoftMax_OutputGradient": [0, 1, 2],
     "Transpose": [0, 1], "RevInFeedForward": [0, 2], "RevInHiddenGraddient": [0, 1, 3],
     "FQF_Cosine": [0, 1], "FQF_Output": [0, 1, 2], "FQF_OutputGradient": [0, 1, 2, 3, 4],
-    "FQF_QuantileGradient": [0, 1, 2, 3, 4], "FQF_CosineGradient": [0, 1, 2],
+    "FQF_QuantileGradient": [0, 1, 2, 3, 4], "FQF_CosineGradient": [0, 1, 2], "FQF_FractionGradient": [1, 2],
     "SAC_AlphaLogProbs": [0, 1, 2, 3, 4, 5], "SAC_AlphaGradients": [0, 1, 2, 3],
     "SAC_OutputGradient": [0, 1, 2, 3, 4, 5], "SAC_CalcLogProbs": [0, 1, 2, 3, 4],
 }
