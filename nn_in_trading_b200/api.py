@@ -29,7 +29,8 @@ SIGNATURES = {
     "FQF_Cosine": "pp", "FQF_Output": "pppi", "FQF_OutputGradient": "ppppp", "FQF_QuantileGradient": "ppppp",
     "FQF_CosineGradient": "ppp", "FQF_FractionGradient": "pppi", "SAC_AlphaLogProbs": "ppppppii",
     "SAC_AlphaGradients": "ppppi",
-    "SAC_OutputGradient": "ppppppii", "SAC_CalcLogProbs": "pppppii", "NormalizeWeights": "pi",
+    "SAC_OutputGradient": "ppppppii", "SAC_CalcLogProbs": "pppppii",
+    "MHFlashAttention": "ppppiii", "MHFlashAttentionGrad": "pppppppiiii", "NormalizeWeights": "pi",
     "Activation": "ppi", "DeActivation": "pppi", "SoftUpdate": "ppf", "SoftUpdateAdam": "ppppfff",
     "FeedForwardConv": "pppiiiii", "CalcHiddenGradientConv": "ppppiiiiii",
     "UpdateWeightsConvAdam": "pppppifffiii", "UpdateWeightsConvMomentum": "ppppiffiii",

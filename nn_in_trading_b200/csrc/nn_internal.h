@@ -104,6 +104,8 @@ extern const KernelDef kMatKernels[];
 extern const int kNumMatKernels;
 extern const KernelDef kFqfKernels[];
 extern const int kNumFqfKernels;
+extern const KernelDef kFlashKernels[];
+extern const int kNumFlashKernels;
 
 // Number of data-parallel ranks (1 without a communicator).
 int dp_world();

@@ -220,7 +220,8 @@ const KernelDef *find_kernel(const char *name) {
                           {kAttnKernels, kNumAttnKernels}, {kMiscKernels, kNumMiscKernels},
                           {kLstmKernels, kNumLstmKernels}, {kAttn2Kernels, kNumAttn2Kernels},
                           {kSacKernels, kNumSacKernels}, {kMatKernels, kNumMatKernels},
-                          {kFqfKernels, kNumFqfKernels}};
+                          {kFqfKernels, kNumFqfKernels},
+                          {kFlashKernels, kNumFlashKernels}};
   for (const Table &t : tables)
     for (int i = 0; i < t.n; ++i)
       if (std::strcmp(t.t[i].name, name) == 0) return &t.t[i];

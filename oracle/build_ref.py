@@ -51,6 +51,7 @@ KERNELS = [
     "FQF_Cosine", "FQF_Output", "FQF_OutputGradient", "FQF_QuantileGradient", "FQF_CosineGradient",
     "FQF_FractionGradient",
     "SAC_AlphaLogProbs", "SAC_AlphaGradients", "SAC_OutputGradient", "SAC_CalcLogProbs",
+    "MHFlashAttention", "MHFlashAttentionGrad",
 ]
 
 
@@ -140,16 +141,23 @@ RACE_PATCHES = [
     # LocalSoftMax (NeuroNet.cl:392-408): every lane reads Temp[0] (the max
     # returned by LocalMax) and LocalSum then stores Temp[id] with no barrier
     # in between, so lane 0 may overwrite the max before lane 1 reads it.
-    ("float max=LocalMax(value,loc,Temp);", "float max=LocalMax(value,loc,Temp);\n   BarrierLoc"),
+    ("float max=LocalMax(value,loc,Temp);", "float max=LocalMax(value,loc,Temp);\n   BarrierLoc", 1),
+    # The same read of Temp[0] at the end of LocalMax / LocalMin (NeuroNet.cl:214-284), LocalSum
+    # and LocalSum4: a kernel that calls them back to back on one local array (MHFlashAttention,
+    # NeuroNet.cl:16066-16177: LocalMax, LocalSum, then LocalSum4 per feature group, per key tile)
+    # lets a lane store its next value before the others have read the result.
+    ("   return(Temp[0]);\n", "   const float result_=Temp[0];\n   BarrierLoc\n   return(result_);\n", 2),
+    ("   result=IsNaNOrInf(Temp[0],0);\n", "   result=IsNaNOrInf(Temp[0],0);\n   BarrierLoc\n", 1),
+    ("   result=IsNaNOrInf4(Temp[0],0.0f);\n", "   result=IsNaNOrInf4(Temp[0],0.0f);\n   BarrierLoc\n", 1),
 ]
 
 
 def generate(cl_text: str) -> str:
     first = cl_text.index("__kernel")
     helpers = cl_text[:first]
-    for old, new in RACE_PATCHES:
-        if helpers.count(old) != 1:
-            raise RuntimeError(f"race patch anchor not found exactly once: {old!r}")
+    for old, new, count in RACE_PATCHES:
+        if helpers.count(old) != count:
+            raise RuntimeError(f"race patch anchor not found {count} times: {old!r}")
         helpers = helpers.replace(old, new)
     parts = ["// GENERATED by oracle/build_ref.py from the reference NeuroNet.cl -- do not commit.",
              '#include "ref_shim.h"', "namespace ocl {", "#line 1 \"NeuroNet.cl\"",

@@ -1246,6 +1246,84 @@ def SAC_CalcLogProbs(outputs, quantiles, probs, alphas, log_probs, count_quants,
             log_probs[i] = -alphas[i] * np.log(prob)
 
 
+# ------------------------------------------------------------ flash attention
+def _flash_blocks(query, key_value, Q, KV, H, D):
+    q = query[:Q * H * D].reshape(Q, H, D)
+    kv = key_value[:KV * 2 * H * D].reshape(KV, 2 * H, D)
+    return q, kv[:, :H, :], kv[:, H:, :]
+
+
+def _flash_visible(Q, KV, mask_future):
+    """Which keys each query sees: all, or with mask_future the keys k >= q (NeuroNet.cl:16096)."""
+    if not mask_future:
+        return np.ones((Q, KV), bool)
+    return np.arange(Q)[:, None] <= np.arange(KV)[None, :]
+
+
+def MHFlashAttention(query, key_value, logsumexp, output, dimension, total_kv, mask_future, gsize, lsize=None):
+    """NeuroNet.cl:16066-16177 over global (queries, local, heads): softmax over the visible keys of
+    q.k / sqrt(d), the score summing IsNaNOrInf(dot) over float4 groups of sanitised features;
+    out = sum IsNaNOrInf(p v) / sum p for the first `local` features and logsumexp = max + log(sum p);
+    rows that see no key get 0."""
+    Q, loc, H = (tuple(gsize) + (1, 1))[:3]
+    D, KV = dimension, total_kv
+    with _err():
+        q, k, v = _flash_blocks(query, key_value, Q, KV, H, D)
+        Dp = (D + 3) // 4 * 4
+        qp = np.zeros((Q, H, Dp), F32)
+        kp = np.zeros((KV, H, Dp), F32)
+        qp[:, :, :D], kp[:, :, :D] = nan0(q), nan0(k)
+        prod = (qp[:, None, :, :] * kp[None, :, :, :]).astype(F32)          # [q][k][h][d]
+        groups = nan0(prod.reshape(Q, KV, H, Dp // 4, 4).sum(axis=-1, dtype=F32))
+        s = (groups.sum(axis=-1, dtype=F32) / np.sqrt(F32(D))).astype(F32)  # [q][k][h]
+        valid = np.broadcast_to(_flash_visible(Q, KV, mask_future)[:, :, None], s.shape)
+        m = np.where(valid, s, -np.inf).max(axis=1, initial=-np.inf)        # [q][h]
+        seen = np.isfinite(m)
+        m0 = np.where(seen, m, 0).astype(F32)
+        p = np.where(valid, np.exp((s - m0[:, None, :]).astype(F32)), F32(0)).astype(F32)
+        sumexp = p.sum(axis=1, dtype=F32)
+        out = nan0(p[:, :, :, None] * v.astype(F32)[None, :, :, :]).sum(axis=1, dtype=F32)
+        ok = seen & (sumexp > 0)
+        den = np.where(ok, sumexp, F32(1)).astype(F32)
+        res = np.where(ok[:, :, None], nan0(out / den[:, :, None]), F32(0)).astype(F32)
+        w = min(D, loc)
+        o = output[:Q * H * D].reshape(Q, H, D)
+        o[:, :, :w] = res[:, :, :w]
+        logsumexp[:Q * H] = np.where(ok, nan0(m0 + np.log(den)), F32(0)).astype(F32).reshape(-1)
+
+
+def MHFlashAttentionGrad(query, query_gr, key_value, key_value_gr, logsumexp, output, output_gr, dimension,
+                         total_q, total_kv, mask_future, gsize, lsize=None):
+    """NeuroNet.cl:16182-16277 over global (rows, d, heads): p = IsNaNOrInf(exp(clamp(s - lse, -120,
+    0))) with s = sum IsNaNOrInf(q k) / sqrt(d); pairs the query cannot see or with p == 0 are
+    skipped; ds = IsNaNOrInf(p (g.v - g.o)); grad_q = sum_k k ds, grad_k = sum_q q ds,
+    grad_v = sum_q p g, every product and sum sanitised; written for the first `rows` queries and
+    keys."""
+    rows, D, H = (tuple(gsize) + (1, 1))[:3]
+    Qt, KVt = total_q, total_kv
+    with _err():
+        q, k, v = _flash_blocks(query, key_value, Qt, KVt, H, D)
+        q, k, v = nan0(q), nan0(k), nan0(v)
+        g = nan0(output_gr[:Qt * H * D].reshape(Qt, H, D))
+        o = nan0(output[:Qt * H * D].reshape(Qt, H, D))
+        lse = nan0(logsumexp[:Qt * H].reshape(Qt, H))
+        Dq = nan0(g * o).sum(axis=-1, dtype=F32)                                    # [q][h]
+        s = (nan0(q[:, None] * k[None, :]).sum(axis=-1, dtype=F32) / np.sqrt(F32(D))).astype(F32)
+        p = nan0(np.exp(cl_clamp(s - lse[:, None, :], -120.0, 0.0)))                # [q][k][h]
+        use = _flash_visible(Qt, KVt, mask_future)[:, :, None] & (p != 0)
+        dp = nan0(g[:, None] * v[None, :]).sum(axis=-1, dtype=F32)
+        ds = np.where(use, nan0(p * (dp - Dq[:, None, :])), F32(0)).astype(F32)
+        gq = nan0(nan0(k[None, :] * ds[..., None]).sum(axis=1, dtype=F32))          # [q][h][d]
+        gk = nan0(nan0(q[:, None] * ds[..., None]).sum(axis=0, dtype=F32))          # [k][h][d]
+        pg = np.where(use[..., None], nan0(p[..., None] * g[:, None]), F32(0)).astype(F32)
+        gv = nan0(pg.sum(axis=0, dtype=F32))
+        nq, nk = min(rows, Qt), min(rows, KVt)
+        query_gr[:nq * H * D] = gq[:nq].reshape(-1)
+        kvg = key_value_gr[:KVt * 2 * H * D].reshape(KVt, 2 * H, D)
+        kvg[:nk, :H] = gk[:nk]
+        kvg[:nk, H:] = gv[:nk]
+
+
 # ------------------------------------------------------- general matrix products
 def _seq_sum(p, axis):
     """Sequential float32 sums along `axis` (the reference's loop order) and their running values."""

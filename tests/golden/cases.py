@@ -398,10 +398,35 @@ def _quantile_head_cases():
     return cases
 
 
+def _flash_cases():
+    """MHFlashAttention / MHFlashAttentionGrad (NeuroNet.cl:16066-16277): self and cross attention,
+    the reference's mask (keys before the query dropped), queries that see no key, head dimensions
+    that are not multiples of 4, local sizes below the dimension, NaN/inf operands."""
+    cases = []
+    # (queries, keys, dim, heads, mask, local, init)
+    for Q, KV, D, H, mask, loc, init in [(8, 8, 16, 2, 0, 16, "normal"), (10, 7, 32, 3, 1, 32, "normal"),
+                                         (33, 40, 8, 1, 0, 40, "normal"), (64, 64, 64, 2, 1, 64, "normal"),
+                                         (5, 70, 12, 2, 0, 70, "normal"), (6, 3, 20, 1, 0, 20, "normal"),
+                                         (9, 12, 24, 2, 0, 8, "normal"), (12, 12, 16, 2, 1, 16, "nanmix")]:
+        cases.append(Case(f"MHFlashAttention/{Q}x{KV}-d{D}-h{H}-m{mask}-l{loc}-{init}", "MHFlashAttention",
+                          [A(Q * H * D, init), A(KV * 2 * H * D, init), A(Q * H, "zeros"), A(Q * H * D, "zeros"),
+                           D, KV, mask], (Q, loc, H), (1, loc, 1)))
+    for Q, KV, D, H, mask, init in [(8, 8, 16, 2, 0, "normal"), (10, 7, 32, 3, 1, "normal"),
+                                    (7, 10, 32, 3, 1, "normal"), (33, 40, 8, 1, 0, "normal"),
+                                    (64, 64, 64, 2, 1, "normal"), (5, 21, 12, 2, 0, "normal"),
+                                    (12, 12, 16, 2, 1, "nanmix")]:
+        cases.append(Case(f"MHFlashAttentionGrad/{Q}x{KV}-d{D}-h{H}-m{mask}-{init}", "MHFlashAttentionGrad",
+                          [A(Q * H * D, init), A(Q * H * D, "zeros"), A(KV * 2 * H * D, init),
+                           A(KV * 2 * H * D, "zeros"), A(Q * H, "pos", 4.0), A(Q * H * D, "normal", 0.5),
+                           A(Q * H * D, "grad" if init == "normal" else init), D, Q, KV, mask],
+                          (max(Q, KV), D, H), (1, D, 1)))
+    return cases
+
+
 def all_cases() -> list[Case]:
     return (_dense_cases() + _conv_cases() + _attention_cases() + _norm_cases() + _batchnorm_cases() + _lstm_cases()
             + _attention2_cases() + _concat_cases() + _adam_mini_cases() + _matmul_cases()
-            + _quantile_head_cases())
+            + _quantile_head_cases() + _flash_cases())
 
 
 def prepare_inputs(case: Case, seed: int) -> list:
