@@ -32,6 +32,22 @@ namespace {
 
 constexpr int kFlashThreads = 128;
 
+// sum_i IsNaNOrInf(a_i b_i, 0) over n features, for sanitised (finite) operands.  Products are
+// rounded on their own, so one that overflows makes the plain sum non-finite; only then are the
+// products sanitised one by one.
+template <int N>
+__device__ __forceinline__ float dot_sanitised(const float *a, const float *b) {
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < N; ++i) s = __fadd_rn(s, __fmul_rn(a[i], b[i]));
+  if (!isfinite(s)) {
+    s = 0.f;
+#pragma unroll
+    for (int i = 0; i < N; ++i) s += nan0(__fmul_rn(a[i], b[i]));
+  }
+  return s;
+}
+
 template <int TPQ>
 __device__ __forceinline__ float group_sum(float x) {
 #pragma unroll
@@ -77,17 +93,28 @@ __global__ void __launch_bounds__(kFlashThreads) flash_fwd_kernel(const float *_
   for (int k0 = 0; k0 < KV; k0 += KT) {
     __syncthreads();
     stage_rows<KT, DP>(ks, kvb + (long long)h * D, 2LL * H * D, k0, KV, D, true);
-    stage_rows<KT, DP>(vs, kvb + (long long)(H + h) * D, 2LL * H * D, k0, KV, D, false);
+    // values sanitised here: with p in [0, 1], p * IsNaNOrInf(v) is IsNaNOrInf(p * v)
+    stage_rows<KT, DP>(vs, kvb + (long long)(H + h) * D, 2LL * H * D, k0, KV, D, true);
     __syncthreads();
     float sc[KT];
     float tmax = -FLT_MAX;
 #pragma unroll
     for (int j = 0; j < KT; ++j) {
       const float *kr = ks + j * DP + t * DPT;
-      float part = 0.f;
+      // float4 groups of products, rounded on their own: a group that is not finite makes the
+      // plain sum non-finite, and only then is each group sanitised as the reference does
+      float grp[DPT / 4], part = 0.f;
 #pragma unroll
-      for (int g = 0; g < DPT; g += 4)
-        part += nan0(qr[g] * kr[g] + qr[g + 1] * kr[g + 1] + qr[g + 2] * kr[g + 2] + qr[g + 3] * kr[g + 3]);
+      for (int g = 0; g < DPT; g += 4) {
+        grp[g / 4] = __fadd_rn(__fadd_rn(__fmul_rn(qr[g], kr[g]), __fmul_rn(qr[g + 1], kr[g + 1])),
+                               __fadd_rn(__fmul_rn(qr[g + 2], kr[g + 2]), __fmul_rn(qr[g + 3], kr[g + 3])));
+        part = __fadd_rn(part, grp[g / 4]);
+      }
+      if (!isfinite(part)) {
+        part = 0.f;
+#pragma unroll
+        for (int g = 0; g < DPT / 4; ++g) part += nan0(grp[g]);
+      }
       const float s = group_sum<TPQ>(part) / rs;
       const int kid = k0 + j;
       const bool ok = kid < KV && (mask == 0 || qi <= kid);
@@ -108,7 +135,7 @@ __global__ void __launch_bounds__(kFlashThreads) flash_fwd_kernel(const float *_
     for (int i = 0; i < DPT; ++i) {
       float v = 0.f;
 #pragma unroll
-      for (int j = 0; j < KT; ++j) v += sc[j] > 0.f ? nan0(vs[j * DP + t * DPT + i] * sc[j]) : 0.f;
+      for (int j = 0; j < KT; ++j) v = fmaf(sc[j], vs[j * DP + t * DPT + i], v);
       acc[i] = nan0(scale * acc[i] + v);
     }
     m = mnew;
@@ -161,14 +188,8 @@ __global__ void __launch_bounds__(kFlashThreads) flash_grad_q_kernel(
     for (int j = 0; j < KT; ++j) {
       const float *kr = ks + j * DP + t * DPT;
       const float *vr = vs + j * DP + t * DPT;
-      float sp = 0.f, dp = 0.f;
-#pragma unroll
-      for (int i = 0; i < DPT; ++i) {
-        sp += nan0(qr[i] * kr[i]);
-        dp += nan0(gr[i] * vr[i]);
-      }
-      const float s = group_sum<TPQ>(sp) / rs;
-      dp = group_sum<TPQ>(dp);
+      const float s = group_sum<TPQ>(dot_sanitised<DPT>(qr, kr)) / rs;
+      const float dp = group_sum<TPQ>(dot_sanitised<DPT>(gr, vr));
       const int kid = k0 + j;
       const float p = nan0(expf(fminf(fmaxf(s - l, -120.f), 0.f)));
       if (kid < KV && (mask == 0 || qi <= kid) && p != 0.f) {
@@ -230,14 +251,8 @@ __global__ void __launch_bounds__(kFlashThreads) flash_grad_kv_kernel(
     for (int j = 0; j < KT; ++j) {
       const float *qr = qs + j * DP + t * DPT;
       const float *gr = gs + j * DP + t * DPT;
-      float sp = 0.f, dp = 0.f;
-#pragma unroll
-      for (int i = 0; i < DPT; ++i) {
-        sp += nan0(qr[i] * kr[i]);
-        dp += nan0(gr[i] * vr[i]);
-      }
-      const float s = group_sum<TPQ>(sp) / rs;
-      dp = group_sum<TPQ>(dp);
+      const float s = group_sum<TPQ>(dot_sanitised<DPT>(qr, kr)) / rs;
+      const float dp = group_sum<TPQ>(dot_sanitised<DPT>(gr, vr));
       const int qi = q0 + j;
       const float p = nan0(expf(fminf(fmaxf(s - ls[j], -120.f), 0.f)));
       if (qi < Q && (mask == 0 || qi <= ki) && p != 0.f) {
