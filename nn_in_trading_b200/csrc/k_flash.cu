@@ -88,7 +88,7 @@ __global__ void __launch_bounds__(kFlashThreads) flash_fwd_kernel(const float *_
     qr[j] = (row_ok && d < D) ? nan0(qrow[d]) : 0.f;
     acc[j] = 0.f;
   }
-  const float rs = sqrtf((float)D);
+  const float rs = 1.f / sqrtf((float)D);  // scores scaled by 1/sqrt(d)
   float m = -FLT_MAX, sumexp = 0.f;
   for (int k0 = 0; k0 < KV; k0 += KT) {
     __syncthreads();
@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(kFlashThreads) flash_fwd_kernel(const float *_
 #pragma unroll
         for (int g = 0; g < DPT / 4; ++g) part += nan0(grp[g]);
       }
-      const float s = group_sum<TPQ>(part) / rs;
+      const float s = group_sum<TPQ>(part) * rs;
       const int kid = k0 + j;
       const bool ok = kid < KV && (mask == 0 || qi <= kid);
       sc[j] = ok ? s : -FLT_MAX;
@@ -178,7 +178,7 @@ __global__ void __launch_bounds__(kFlashThreads) flash_grad_q_kernel(
   }
   const float Dq = group_sum<TPQ>(dpart);
   const float l = row_ok ? nan0(lse[row]) : 0.f;
-  const float rs = sqrtf((float)D);
+  const float rs = 1.f / sqrtf((float)D);  // scores scaled by 1/sqrt(d)
   for (int k0 = 0; k0 < KV; k0 += KT) {
     __syncthreads();
     stage_rows<KT, DP>(ks, kvb + (long long)h * D, 2LL * H * D, k0, KV, D, true);
@@ -188,7 +188,7 @@ __global__ void __launch_bounds__(kFlashThreads) flash_grad_q_kernel(
     for (int j = 0; j < KT; ++j) {
       const float *kr = ks + j * DP + t * DPT;
       const float *vr = vs + j * DP + t * DPT;
-      const float s = group_sum<TPQ>(dot_sanitised<DPT>(qr, kr)) / rs;
+      const float s = group_sum<TPQ>(dot_sanitised<DPT>(qr, kr)) * rs;
       const float dp = group_sum<TPQ>(dot_sanitised<DPT>(gr, vr));
       const int kid = k0 + j;
       const float p = nan0(expf(fminf(fmaxf(s - l, -120.f), 0.f)));
@@ -235,7 +235,7 @@ __global__ void __launch_bounds__(kFlashThreads) flash_grad_kv_kernel(
     vr[j] = ok ? nan0(kv[(krow + H + h) * D + d]) : 0.f;
     gk[j] = gv[j] = 0.f;
   }
-  const float rs = sqrtf((float)D);
+  const float rs = 1.f / sqrtf((float)D);  // scores scaled by 1/sqrt(d)
   for (int q0 = 0; q0 < Q; q0 += KT) {
     __syncthreads();
     stage_rows<KT, DP>(qs, qb + (long long)h * D, (long long)H * D, q0, Q, D, true);
@@ -251,7 +251,7 @@ __global__ void __launch_bounds__(kFlashThreads) flash_grad_kv_kernel(
     for (int j = 0; j < KT; ++j) {
       const float *qr = qs + j * DP + t * DPT;
       const float *gr = gs + j * DP + t * DPT;
-      const float s = group_sum<TPQ>(dot_sanitised<DPT>(qr, kr)) / rs;
+      const float s = group_sum<TPQ>(dot_sanitised<DPT>(qr, kr)) * rs;
       const float dp = group_sum<TPQ>(dot_sanitised<DPT>(gr, vr));
       const int qi = q0 + j;
       const float p = nan0(expf(fminf(fmaxf(s - ls[j], -120.f), 0.f)));
@@ -260,7 +260,7 @@ __global__ void __launch_bounds__(kFlashThreads) flash_grad_kv_kernel(
 #pragma unroll
         for (int i = 0; i < DPT; ++i) {
           gk[i] += nan0(qr[i] * ds);
-          gv[i] += nan0(p * gr[i]);
+          gv[i] = fmaf(p, gr[i], gv[i]);  // p in [0, 1], g sanitised: the product is finite
         }
       }
     }
@@ -277,12 +277,13 @@ __global__ void __launch_bounds__(kFlashThreads) flash_grad_kv_kernel(
 }
 
 // (lanes per row, features per lane, rows per staged tile) for a head dimension; false past 1024.
+// Fewer lanes per row repeat less of the per-score work (scale, exponent, mask) across the group.
 // Each configuration stages 16 KB or less per operand pair.
 template <class F>
 bool flash_dispatch(int D, F &&f) {
   using std::integral_constant;
-  if (D <= 32) f(integral_constant<int, 4>{}, integral_constant<int, 8>{}, integral_constant<int, 32>{});
-  else if (D <= 64) f(integral_constant<int, 4>{}, integral_constant<int, 16>{}, integral_constant<int, 32>{});
+  if (D <= 32) f(integral_constant<int, 1>{}, integral_constant<int, 32>{}, integral_constant<int, 32>{});
+  else if (D <= 64) f(integral_constant<int, 2>{}, integral_constant<int, 32>{}, integral_constant<int, 32>{});
   else if (D <= 128) f(integral_constant<int, 8>{}, integral_constant<int, 16>{}, integral_constant<int, 16>{});
   else if (D <= 256) f(integral_constant<int, 16>{}, integral_constant<int, 16>{}, integral_constant<int, 8>{});
   else if (D <= 512) f(integral_constant<int, 32>{}, integral_constant<int, 16>{}, integral_constant<int, 4>{});
