@@ -27,7 +27,8 @@ SIGNATURES = {
     "UpdateWeightsAdamMini": "pppppfff", "UpdateWeightsConvAdamMini": "pppppifffi",
     "MatMult": "pppiiiiipi", "MatMultGrad": "pppppiiiiiii",
     "FQF_Cosine": "pp", "FQF_Output": "pppi", "FQF_OutputGradient": "ppppp", "FQF_QuantileGradient": "ppppp",
-    "FQF_CosineGradient": "ppp", "FQF_FractionGradient": "pppi", "SAC_AlphaLogProbs": "ppppppii",
+    "FQF_CosineGradient": "ppp", "FQF_FractionGradient": "pppi",
+    "FQF_CosineGradientSRM": "ppp", "FQF_DistributionTargetGradient": "ppppfff", "SAC_AlphaLogProbs": "ppppppii",
     "SAC_AlphaGradients": "ppppi",
     "SAC_OutputGradient": "ppppppii", "SAC_CalcLogProbs": "pppppii",
     "MHFlashAttention": "ppppiii", "MHFlashAttentionGrad": "pppppppiiii", "NormalizeWeights": "pi",

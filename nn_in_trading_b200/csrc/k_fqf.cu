@@ -5,6 +5,8 @@
 //   FQF_OutputGradient     quantile and tau gradients of y                   NeuroNet.cl:2560-2573
 //   FQF_QuantileGradient   state and tau-embedding gradients of their product NeuroNet.cl:2579-2592
 //   FQF_CosineGradient     softmax gradient through every tau_t, t >= i       NeuroNet.cl:2598-2624
+//   FQF_CosineGradientSRM  the same for the spectral-risk head              NeuroNet.cl:2630-2651
+//   FQF_DistributionTargetGradient  gradient into the quantile nearest a target  NeuroNet.cl:2663-2716
 //   FQF_FractionGradient   input gradient of the fraction proposal layer     NeuroNet.cl:3207-3224
 //   SAC_AlphaLogProbs      sample a quantile by its probability, -alpha log p NeuroNet.cl:3903-3933
 //   SAC_AlphaGradients     gradient of alpha                                 NeuroNet.cl:3939-3951
@@ -17,6 +19,8 @@
 // whose running probability reaches the random number, so the sums run in its order).
 // Batches: every buffer is per sample (FQF_FractionGradient's weights are shared); a launch covers
 // actions x batch rows.
+#include <cfloat>
+
 #include "../../include/nn_b200.h"
 #include "nn_device.cuh"
 #include "nn_internal.h"
@@ -84,6 +88,9 @@ __global__ void fqf_pair_grad_kernel(const float *__restrict__ in1, const float 
 // The chunks of 32 fractions run from the last to the first so that the suffix sum is a running
 // total (a term that is not finite reaches only the i below it, as in the reference); a chunk's
 // starting tau is the row total less the later chunks (exactly 0 for rows of at most 32).
+// SRM (FQF_CosineGradientSRM, NeuroNet.cl:2630-2651): the first term halved and the later terms
+// without p_t / tau_t.
+template <bool SRM>
 __global__ void fqf_cosine_grad_kernel(const float *__restrict__ sm, const float *__restrict__ og,
                                        float *__restrict__ sg, int total, long long rows) {
   const long long a = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
@@ -107,8 +114,8 @@ __global__ void fqf_cosine_grad_kernel(const float *__restrict__ sm, const float
     const float fi = (float)i;
     const float gi = i < total ? g[i] : 0.f;
     const float sn = sinf(kPiF * fi * tau);
-    const float first = -kPiF * fi * sn * gi;
-    const float f = i < total && i > 0 ? -kPiF * fi * sn * gi * x / tau : 0.f;
+    const float first = SRM ? -0.5f * kPiF * fi * sn * gi : -kPiF * fi * sn * gi;
+    const float f = i < total && i > 0 ? (SRM ? -kPiF * fi * sn * gi : -kPiF * fi * sn * gi * x / tau) : 0.f;
     float inc = f;  // inclusive suffix over the lanes
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
@@ -226,6 +233,45 @@ __global__ void __launch_bounds__(256) fqf_fraction_grad_kernel(const float *__r
   }
 }
 
+// FQF_DistributionTargetGradient: per row v, the quantile nearest the target (ties: the larger
+// value, then the lower index) gets value_weight (target - z) and probability_weight / (p + 1e-37);
+// every other entry 0, and the whole row 0 when the target or every quantile is not finite.  A
+// warp per row, three reductions.
+__global__ void fqf_dist_target_grad_kernel(const float *__restrict__ q, const float *__restrict__ pr,
+                                            float *__restrict__ qg, float *__restrict__ pg, float target,
+                                            float pw, float vw, int total, long long rows) {
+  const long long v = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (v >= rows) return;
+  const float *z = q + v * total;
+  const bool tv = isfinite(target);
+  float dmin = FLT_MAX;
+  for (int i = lane; i < total; i += 32)
+    if (tv && isfinite(z[i])) dmin = fminf(dmin, fabsf(z[i] - target));
+  for (int o = 16; o > 0; o >>= 1) dmin = fminf(dmin, __shfl_xor_sync(kFull, dmin, o));
+  float cmax = -FLT_MAX;
+  bool any = false;
+  for (int i = lane; i < total; i += 32)
+    if (tv && isfinite(z[i]) && fabsf(z[i] - target) == dmin) {
+      cmax = fmaxf(cmax, z[i]);
+      any = true;
+    }
+  for (int o = 16; o > 0; o >>= 1) {
+    cmax = fmaxf(cmax, __shfl_xor_sync(kFull, cmax, o));
+    any |= __shfl_xor_sync(kFull, (int)any, o) != 0;
+  }
+  int kmin = total;
+  if (any)
+    for (int i = lane; i < total; i += 32)
+      if (isfinite(z[i]) && z[i] == cmax) kmin = min(kmin, i);
+  for (int o = 16; o > 0; o >>= 1) kmin = min(kmin, __shfl_xor_sync(kFull, kmin, o));
+  for (int i = lane; i < total; i += 32) {
+    const bool hit = tv && i == kmin;
+    qg[v * total + i] = hit ? vw * (target - z[i]) : 0.f;
+    pg[v * total + i] = hit ? pw / (nan0(pr[v * total + i]) + 1.0e-37f) : 0.f;
+  }
+}
+
 dim3 warp_grid(long long rows) { return dim3((unsigned)((rows * 32 + 255) / 256)); }
 
 // (quants, actions) kernels: total = global[0], rows = actions x batch.
@@ -280,6 +326,7 @@ int k_fqf_quantile_grad(Launch &L) {
   return NN_OK;
 }
 
+template <bool SRM>
 int k_fqf_cosine_grad(Launch &L) {
   int T;
   long long R;
@@ -287,7 +334,7 @@ int k_fqf_cosine_grad(Launch &L) {
   const size_t n = (size_t)R * T;
   float *sm = L.buf(0, n), *og = L.buf(1, n), *sg = L.buf(2, n);
   if (!sm || !og || !sg) return NN_ERR_BOUNDS;
-  fqf_cosine_grad_kernel<<<warp_grid(R), 256, 0, L.stream>>>(sm, og, sg, T, R);
+  fqf_cosine_grad_kernel<SRM><<<warp_grid(R), 256, 0, L.stream>>>(sm, og, sg, T, R);
   NN_CHECK_LAUNCH(L);
   return NN_OK;
 }
@@ -349,6 +396,19 @@ int k_fqf_fraction_grad(Launch &L) {
   return NN_OK;
 }
 
+int k_fqf_dist_target_grad(Launch &L) {
+  // global (quants, rows) with the quants in one work-group
+  int T;
+  long long R;
+  quant_shape(L, &T, &R);
+  const size_t n = (size_t)R * T;
+  float *q = L.buf(0, n), *p = L.buf(1, n), *qg = L.buf(2, n), *pg = L.buf(3, n);
+  if (!q || !p || !qg || !pg) return NN_ERR_BOUNDS;
+  fqf_dist_target_grad_kernel<<<warp_grid(R), 256, 0, L.stream>>>(q, p, qg, pg, L.f(4), L.f(5), L.f(6), T, R);
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
 }  // namespace
 
 const KernelDef kFqfKernels[] = {
@@ -356,7 +416,9 @@ const KernelDef kFqfKernels[] = {
     {"FQF_Output", "pppi", k_fqf_output, false},
     {"FQF_OutputGradient", "ppppp", k_fqf_output_grad, false},
     {"FQF_QuantileGradient", "ppppp", k_fqf_quantile_grad, false},
-    {"FQF_CosineGradient", "ppp", k_fqf_cosine_grad, false},
+    {"FQF_CosineGradient", "ppp", k_fqf_cosine_grad<false>, false},
+    {"FQF_CosineGradientSRM", "ppp", k_fqf_cosine_grad<true>, false},
+    {"FQF_DistributionTargetGradient", "ppppfff", k_fqf_dist_target_grad, false},
     {"FQF_FractionGradient", "pppi", k_fqf_fraction_grad, false},
     {"SAC_AlphaLogProbs", "ppppppii", k_sac_alpha_log_probs, false},
     {"SAC_AlphaGradients", "ppppi", k_sac_alpha_grad, false},

@@ -49,7 +49,7 @@ KERNELS = [
     "Concat_FeedForward", "Concat_HiddenGradient", "Concat_UpdateWeightsMomentum", "Concat_UpdateWeightsAdam",
     "UpdateWeightsAdamMini", "UpdateWeightsConvAdamMini", "MatMult", "MatMultGrad",
     "FQF_Cosine", "FQF_Output", "FQF_OutputGradient", "FQF_QuantileGradient", "FQF_CosineGradient",
-    "FQF_FractionGradient",
+    "FQF_FractionGradient", "FQF_CosineGradientSRM", "FQF_DistributionTargetGradient",
     "SAC_AlphaLogProbs", "SAC_AlphaGradients", "SAC_OutputGradient", "SAC_CalcLogProbs",
     "MHFlashAttention", "MHFlashAttentionGrad",
 ]

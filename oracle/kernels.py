@@ -1145,6 +1145,53 @@ def FQF_QuantileGradient(state_embeding, taus_embeding, quantiles_gr, state_gr, 
         taus_gr[:n] = (g * state_embeding[:n]).astype(F32)
 
 
+def FQF_CosineGradientSRM(softmax, output_gr, softmax_gr, gsize, lsize=None):
+    """NeuroNet.cl:2630-2651 over global (quants, actions): softmax_gr[i] += -pi/2 i sin(pi i tau_i) g_i
+    + sum_{t>i} -pi t sin(pi t tau_t) g_t (the later terms summed in order)."""
+    T, R = gsize[0], (tuple(gsize) + (1,))[1]
+    with _err():
+        sm = softmax[:R * T].reshape(R, T).astype(F32)
+        g = output_gr[:R * T].reshape(R, T).astype(F32)
+        tau = _taus(sm)
+        i = np.arange(T, dtype=F32)[None, :]
+        sn = np.sin((PI_F * i * tau).astype(F32)).astype(F32)
+        first = (F32(-0.5) * PI_F * i * sn * g).astype(F32)
+        f = (-PI_F * i * sn * g).astype(F32)
+        out = softmax_gr[:R * T].reshape(R, T).copy()
+        for k in range(T):
+            later, _ = _seq_sum(f[:, k + 1:], 1)
+            out[:, k] = (out[:, k] + (first[:, k] + later).astype(F32)).astype(F32)
+        softmax_gr[:R * T] = out.reshape(-1)
+
+
+def FQF_DistributionTargetGradient(quantiles, probabilities, quantiles_gr, probabilities_gr, target,
+                                   probability_weight, value_weight, gsize, lsize=None):
+    """NeuroNet.cl:2663-2716 over global (quants, rows), one work-group per row: the finite quantile
+    nearest the target (ties: the larger value, then the lower index) gets value_weight (target - z)
+    and probability_weight / (p + 1e-37); every other entry 0 (all of them when the target is not
+    finite)."""
+    T, R = gsize[0], (tuple(gsize) + (1,))[1]
+    with _err():
+        z = quantiles[:R * T].reshape(R, T).astype(F32)
+        pr = nan0(probabilities[:R * T].reshape(R, T))
+        qg = np.zeros((R, T), F32)
+        pg = np.zeros((R, T), F32)
+        t = F32(target)
+        if np.isfinite(t):
+            for v in range(R):
+                ok = np.isfinite(z[v])
+                if not ok.any():
+                    continue
+                d = np.where(ok, np.abs((z[v] - t).astype(F32)), np.inf)
+                cand = ok & (d == d.min())
+                c = z[v][cand].max()
+                k = int(np.flatnonzero(ok & (z[v] == c))[0])
+                qg[v, k] = F32(value_weight) * F32(t - z[v, k])
+                pg[v, k] = F32(probability_weight) / F32(pr[v, k] + F32(1e-37))
+        quantiles_gr[:R * T] = qg.reshape(-1)
+        probabilities_gr[:R * T] = pg.reshape(-1)
+
+
 def FQF_CosineGradient(softmax, output_gr, softmax_gr, gsize, lsize=None):
     """NeuroNet.cl:2598-2624 over global (quants, actions): softmax_gr[i] += -pi i sin(pi i tau_i) g_i
     + sum_{t>i} -pi t sin(pi t tau_t) g_t p_t / tau_t (the later terms summed in order)."""

@@ -377,6 +377,13 @@ def _quantile_head_cases():
                           [A(R * T), A(R * T), A(R * T, "grad"), A(R * T, "zeros"), A(R * T, "zeros")], (T, R)))
         cases.append(Case(f"FQF_CosineGradient/{T}x{R}", "FQF_CosineGradient",
                           [A(R * T, "unit"), A(R * T, "grad"), A(R * T, "small")], (T, R), meta=sm))
+        cases.append(Case(f"FQF_CosineGradientSRM/{T}x{R}", "FQF_CosineGradientSRM",
+                          [A(R * T, "unit"), A(R * T, "grad"), A(R * T, "small")], (T, R), meta=sm))
+        for target, init in [(0.3, "normal"), (-1.2, "nanmix"), (float("nan"), "normal")]:
+            cases.append(Case(f"FQF_DistributionTargetGradient/{T}x{R}-t{target}-{init}",
+                              "FQF_DistributionTargetGradient",
+                              [A(R * T, init), A(R * T, "unit"), A(R * T, "small"), A(R * T, "small"), target,
+                               0.7, 1.3], (T, R), (T, 1), meta=sm))
     # FQF_FractionGradient (NeuroNet.cl:3207-3224): (inputs, outputs, local size along the outputs)
     for n_in, n_out, loc, init in [(32, 64, 1, "normal"), (100, 33, 16, "normal"), (7, 300, 64, "normal"),
                                    (65, 32, 1, "nanmix")]:
