@@ -8,6 +8,8 @@
 //   FQF_CosineGradientSRM  the same for the spectral-risk head              NeuroNet.cl:2630-2651
 //   FQF_DistributionTargetGradient  gradient into the quantile nearest a target  NeuroNet.cl:2663-2716
 //   FQF_FractionGradient   input gradient of the fraction proposal layer     NeuroNet.cl:3207-3224
+//   FQF_MonotoneRearrange  quantiles in ascending order, with diagnostics    NeuroNet.cl:20716-20817
+//   FQF_RearrangeGradient  ordered gradients back to their source quantiles  NeuroNet.cl:20823-20842
 //   SAC_AlphaLogProbs      sample a quantile by its probability, -alpha log p NeuroNet.cl:3903-3933
 //   SAC_AlphaGradients     gradient of alpha                                 NeuroNet.cl:3939-3951
 //   SAC_OutputGradient     gradient into the quantiles bracketing the action NeuroNet.cl:3957-4000
@@ -272,6 +274,79 @@ __global__ void fqf_dist_target_grad_kernel(const float *__restrict__ q, const f
   }
 }
 
+// FQF_MonotoneRearrange: per row of `total` quants (a power of two up to 64, else nothing is
+// written), the quantiles in ascending (value, index) order with their probabilities and source
+// indices; a value that is not finite sorts as 3.4e37, a probability that is not finite or below 0
+// as 0.  Six diagnostics per row: crossing rate and total magnitude (per adjacent pair), probability
+// sum, min and max, and the count of invalid probabilities.  The reference sorts bitonically; the
+// keys are distinct, so ranking each element by counting gives the same order.  A warp per row.
+constexpr float kRefMaxValue = 3.4e37f;
+__global__ void fqf_rearrange_kernel(const float *__restrict__ q, const float *__restrict__ pr,
+                                     float *__restrict__ oq, float *__restrict__ op, float *__restrict__ ord,
+                                     float *__restrict__ diag, int total, long long rows) {
+  const long long task = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (task >= rows) return;
+  const float *z = q + task * total;
+  const float *p = pr + task * total;
+  float cf = 0.f, cm = 0.f, ps = 0.f, pmin = FLT_MAX, pmax = -FLT_MAX, inv = 0.f;
+  for (int i = lane; i < total; i += 32) {
+    const float zi = isfinite(z[i]) ? z[i] : kRefMaxValue;
+    const bool pbad = !isfinite(p[i]) || p[i] < 0.f;
+    const float pi = pbad ? 0.f : p[i];
+    if (i + 1 < total) {
+      const float zn = isfinite(z[i + 1]) ? z[i + 1] : kRefMaxValue;
+      cf += zn < zi ? 1.f : 0.f;
+      cm += fmaxf(zi - zn, 0.f);
+    }
+    ps += pi;
+    pmin = fminf(pmin, pi);
+    pmax = fmaxf(pmax, pi);
+    inv += pbad ? 1.f : 0.f;
+    int rank = 0;
+    for (int j = 0; j < total; ++j) {
+      const float zj = isfinite(z[j]) ? z[j] : kRefMaxValue;
+      rank += (zj < zi || (zj == zi && j < i)) ? 1 : 0;
+    }
+    oq[task * total + rank] = zi;
+    op[task * total + rank] = pi;
+    ord[task * total + rank] = (float)i;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    cf += __shfl_xor_sync(kFull, cf, o);
+    cm += __shfl_xor_sync(kFull, cm, o);
+    ps += __shfl_xor_sync(kFull, ps, o);
+    pmin = fminf(pmin, __shfl_xor_sync(kFull, pmin, o));
+    pmax = fmaxf(pmax, __shfl_xor_sync(kFull, pmax, o));
+    inv += __shfl_xor_sync(kFull, inv, o);
+  }
+  if (lane == 0) {
+    const float dinv = total > 1 ? 1.0f / (float)(total - 1) : 0.f;
+    float *d = diag + task * 6;
+    d[0] = cf * dinv;
+    d[1] = cm * dinv;
+    d[2] = ps;
+    d[3] = pmin;
+    d[4] = pmax;
+    d[5] = inv;
+  }
+}
+
+// FQF_RearrangeGradient: gradients of the ordered entries scattered back to their source index
+// (an order entry that is not a valid index is skipped).
+__global__ void fqf_rearrange_grad_kernel(const float *__restrict__ oqg, const float *__restrict__ opg,
+                                          const float *__restrict__ ord, float *__restrict__ qg,
+                                          float *__restrict__ pg, int total, long long n) {
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
+    const float o = nan0(ord[e], -1.f);
+    const int dst = (int)o;
+    if (dst < 0 || dst >= total) continue;
+    const long long row = e / total;
+    qg[row * total + dst] = oqg[e];
+    pg[row * total + dst] = opg[e];
+  }
+}
+
 dim3 warp_grid(long long rows) { return dim3((unsigned)((rows * 32 + 255) / 256)); }
 
 // (quants, actions) kernels: total = global[0], rows = actions x batch.
@@ -409,6 +484,32 @@ int k_fqf_dist_target_grad(Launch &L) {
   return NN_OK;
 }
 
+int k_fqf_rearrange(Launch &L) {
+  int T;
+  long long R;
+  quant_shape(L, &T, &R);
+  if (T == 0 || (T & (T - 1)) != 0 || T > 64) return NN_OK;  // the reference writes nothing
+  const size_t n = (size_t)R * T;
+  float *q = L.buf(0, n), *p = L.buf(1, n), *oq = L.buf(2, n), *op = L.buf(3, n), *ord = L.buf(4, n);
+  float *diag = L.buf(5, (size_t)R * 6);
+  if (!q || !p || !oq || !op || !ord || !diag) return NN_ERR_BOUNDS;
+  fqf_rearrange_kernel<<<warp_grid(R), 256, 0, L.stream>>>(q, p, oq, op, ord, diag, T, R);
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
+int k_fqf_rearrange_grad(Launch &L) {
+  int T;
+  long long R;
+  quant_shape(L, &T, &R);
+  const size_t n = (size_t)R * T;
+  float *oqg = L.buf(0, n), *opg = L.buf(1, n), *ord = L.buf(2, n), *qg = L.buf(3, n), *pg = L.buf(4, n);
+  if (!oqg || !opg || !ord || !qg || !pg) return NN_ERR_BOUNDS;
+  fqf_rearrange_grad_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(oqg, opg, ord, qg, pg, T, (long long)n);
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
 }  // namespace
 
 const KernelDef kFqfKernels[] = {
@@ -420,6 +521,8 @@ const KernelDef kFqfKernels[] = {
     {"FQF_CosineGradientSRM", "ppp", k_fqf_cosine_grad<true>, false},
     {"FQF_DistributionTargetGradient", "ppppfff", k_fqf_dist_target_grad, false},
     {"FQF_FractionGradient", "pppi", k_fqf_fraction_grad, false},
+    {"FQF_MonotoneRearrange", "pppppp", k_fqf_rearrange, false},
+    {"FQF_RearrangeGradient", "ppppp", k_fqf_rearrange_grad, false},
     {"SAC_AlphaLogProbs", "ppppppii", k_sac_alpha_log_probs, false},
     {"SAC_AlphaGradients", "ppppi", k_sac_alpha_grad, false},
     {"SAC_OutputGradient", "ppppppii", k_sac_output_grad, false},

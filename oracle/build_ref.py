@@ -50,6 +50,7 @@ KERNELS = [
     "UpdateWeightsAdamMini", "UpdateWeightsConvAdamMini", "MatMult", "MatMultGrad",
     "FQF_Cosine", "FQF_Output", "FQF_OutputGradient", "FQF_QuantileGradient", "FQF_CosineGradient",
     "FQF_FractionGradient", "FQF_CosineGradientSRM", "FQF_DistributionTargetGradient",
+    "FQF_MonotoneRearrange", "FQF_RearrangeGradient",
     "SAC_AlphaLogProbs", "SAC_AlphaGradients", "SAC_OutputGradient", "SAC_CalcLogProbs",
     "MHFlashAttention", "MHFlashAttentionGrad",
 ]

@@ -1145,6 +1145,51 @@ def FQF_QuantileGradient(state_embeding, taus_embeding, quantiles_gr, state_gr, 
         taus_gr[:n] = (g * state_embeding[:n]).astype(F32)
 
 
+REF_MAX_VALUE = F32(3.4e37)  # MAX_VALUE, NeuroNet.cl:20
+
+
+def FQF_MonotoneRearrange(quantiles, probabilities, ordered_quantiles, ordered_probabilities, order, diagnostics,
+                          gsize, lsize=None):
+    """NeuroNet.cl:20716-20817 over global (quants, rows), one work-group per row of a power of two up
+    to 64 quants (other rows: nothing written): ascending (value, index) order, a value that is not
+    finite taken as MAX_VALUE and a probability that is not finite or negative as 0; diagnostics per
+    row: crossing rate and magnitude over adjacent pairs (/ (quants - 1)), probability sum, min, max,
+    and the invalid-probability count."""
+    T, R = gsize[0], (tuple(gsize) + (1,))[1]
+    if T == 0 or (T & (T - 1)) != 0 or T > 64:
+        return
+    with _err():
+        for v in range(R):
+            z = quantiles[v * T:(v + 1) * T].astype(F32)
+            p = probabilities[v * T:(v + 1) * T].astype(F32)
+            lz = np.where(np.isfinite(z), z, REF_MAX_VALUE).astype(F32)
+            pbad = ~np.isfinite(p) | (p < 0)
+            lp = np.where(pbad, F32(0), p).astype(F32)
+            idx = sorted(range(T), key=lambda i: (float(lz[i]), i))
+            ordered_quantiles[v * T:(v + 1) * T] = lz[idx]
+            ordered_probabilities[v * T:(v + 1) * T] = lp[idx]
+            order[v * T:(v + 1) * T] = np.asarray(idx, F32)
+            dinv = F32(1) / F32(T - 1) if T > 1 else F32(0)
+            cf = F32((lz[1:] < lz[:-1]).sum())
+            cm = np.maximum((lz[:-1] - lz[1:]).astype(F32), F32(0)).sum(dtype=F32)
+            diagnostics[v * 6:(v + 1) * 6] = [cf * dinv, cm * dinv, lp.sum(dtype=F32), lp.min(), lp.max(),
+                                              F32(pbad.sum())]
+
+
+def FQF_RearrangeGradient(ordered_quantiles_gradient, ordered_probabilities_gradient, order, quantiles_gradient,
+                          probabilities_gradient, gsize, lsize=None):
+    """NeuroNet.cl:20823-20842 over global (quants, rows): each ordered gradient goes back to the
+    index `order` names (entries that are not a valid index are skipped)."""
+    T, R = gsize[0], (tuple(gsize) + (1,))[1]
+    for v in range(R):
+        for j in range(T):
+            o = order[v * T + j]
+            d = int(o) if np.isfinite(o) else -1
+            if 0 <= d < T:
+                quantiles_gradient[v * T + d] = ordered_quantiles_gradient[v * T + j]
+                probabilities_gradient[v * T + d] = ordered_probabilities_gradient[v * T + j]
+
+
 def FQF_CosineGradientSRM(softmax, output_gr, softmax_gr, gsize, lsize=None):
     """NeuroNet.cl:2630-2651 over global (quants, actions): softmax_gr[i] += -pi/2 i sin(pi i tau_i) g_i
     + sum_{t>i} -pi t sin(pi t tau_t) g_t (the later terms summed in order)."""

@@ -74,6 +74,11 @@ def materialise(case: Case, seed: int) -> list:
             # normal values, one in ten scaled to 1e20 (products of two of them overflow float)
             v = rng.standard_normal(n) * a.scale
             v[rng.uniform(0.0, 1.0, n) < 0.1] *= 1e20
+        elif a.init == "perm":
+            # rows of int(scale) entries, each a permutation of its indices (as floats), a few NaN
+            T = int(a.scale)
+            v = np.concatenate([rng.permutation(T) for _ in range(n // T)]).astype(np.float64)
+            v[rng.uniform(0.0, 1.0, n) < 0.05] = np.nan
         elif a.init.startswith("act:"):
             # a plausible activation output for the given activation (used by Deactivation inputs)
             act = int(a.init[4:])
@@ -390,6 +395,16 @@ def _quantile_head_cases():
         cases.append(Case(f"FQF_FractionGradient/{n_in}x{n_out}-l{loc}-{init}", "FQF_FractionGradient",
                           [A(n_out * (n_in + 1), init, 0.1), A(n_out, "grad"), A(n_in, "zeros"), n_out],
                           (n_in, loc), (1, loc)))
+    # FQF_MonotoneRearrange / FQF_RearrangeGradient (NeuroNet.cl:20716-20842): rows of a power of two up
+    # to 64 quants (others are left untouched by the reference), NaN/inf quantiles and probabilities
+    for T, R, init in [(32, 5, "normal"), (8, 3, "nanmix"), (64, 2, "normal"), (1, 4, "normal"), (2, 3, "nanmix"),
+                       (12, 2, "normal"), (128, 1, "normal")]:
+        cases.append(Case(f"FQF_MonotoneRearrange/{T}x{R}-{init}", "FQF_MonotoneRearrange",
+                          [A(R * T, init), A(R * T, init), A(R * T, "small"), A(R * T, "small"), A(R * T, "small"),
+                           A(R * 6, "small")], (T, R), (T, 1)))
+        cases.append(Case(f"FQF_RearrangeGradient/{T}x{R}", "FQF_RearrangeGradient",
+                          [A(R * T, "grad"), A(R * T, "grad"), A(R * T, "perm", T), A(R * T, "small"),
+                           A(R * T, "small")], (T, R)))
     for n, cq, act in [(16, 32, NONE), (7, 8, TANH), (40, 5, SIGMOID), (3, 1, NONE), (9, 64, LRELU)]:
         cases.append(Case(f"SAC_AlphaLogProbs/{n}x{cq}-a{act}", "SAC_AlphaLogProbs",
                           [A(n, "zeros"), A(n * cq), A(n * cq, "unit"), A(n, "pos"), A(n, "zeros"), A(n, "unit"),
