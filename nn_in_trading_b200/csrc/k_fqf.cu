@@ -8,6 +8,7 @@
 //   FQF_CosineGradientSRM  the same for the spectral-risk head              NeuroNet.cl:2630-2651
 //   FQF_DistributionTargetGradient  gradient into the quantile nearest a target  NeuroNet.cl:2663-2716
 //   FQF_FractionGradient   input gradient of the fraction proposal layer     NeuroNet.cl:3207-3224
+//   FQF_SRMForward         spectral risk of the quantile distribution        NeuroNet.cl:2924-3021
 //   FQF_MonotoneRearrange  quantiles in ascending order, with diagnostics    NeuroNet.cl:20716-20817
 //   FQF_RearrangeGradient  ordered gradients back to their source quantiles  NeuroNet.cl:20823-20842
 //   SAC_AlphaLogProbs      sample a quantile by its probability, -alpha log p NeuroNet.cl:3903-3933
@@ -347,6 +348,76 @@ __global__ void fqf_rearrange_grad_kernel(const float *__restrict__ oqg, const f
   }
 }
 
+// SRMCumulative (NeuroNet.cl:2805-2850): the spectral risk measure's cumulative weight at tau for
+// the reference's five risk types (mean, CVaR, mean-CVaR mix, exponential, dual power).
+__device__ __forceinline__ float srm_cumulative(float u, int type, float param, float mean_w) {
+  constexpr float kEps = 1.0e-6f;
+  const float tau = fminf(fmaxf(u, 0.f), 1.f);
+  switch (type) {
+    case 0: return tau;
+    case 1: {
+      const float alpha = fminf(fmaxf(param, kEps), 1.f);
+      return fminf(fmaxf(fminf(tau, alpha) / alpha, 0.f), 1.f);
+    }
+    case 2: {
+      const float alpha = fminf(fmaxf(param, kEps), 1.f);
+      const float omega = fminf(fmaxf(mean_w, 0.f), 1.f);
+      return fminf(fmaxf(omega * tau + (1.f - omega) * fminf(tau, alpha) / alpha, 0.f), 1.f);
+    }
+    case 3: {
+      const float lambda = fmaxf(param, 0.f);
+      if (lambda <= kEps) return tau;
+      return fminf(fmaxf(-expm1f(-lambda * tau) / -expm1f(-lambda), 0.f), 1.f);
+    }
+    case 4: {
+      const float nu = fmaxf(param, 1.f);
+      return fminf(fmaxf(1.f - powf(1.f - tau, nu), 0.f), 1.f);
+    }
+    default: return 0.f;
+  }
+}
+
+// FQF_SRMForward: per row, the spectral risk of the quantile distribution: with P_i the running
+// sum of the (sanitised, non-negative) probabilities and M the row's mass, sum_i z_i
+// max(F(P_i / M) - F(P_{i-1} / M), 0); 0 when M <= 1e-37.  A warp per row, the running sum as a
+// warp scan.
+__global__ void fqf_srm_forward_kernel(const float *__restrict__ q, const float *__restrict__ pr,
+                                       float *__restrict__ res, int type, float param, float mean_w, int total,
+                                       long long rows) {
+  const long long task = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (task >= rows) return;
+  const float *p = pr + task * total;
+  const float *z = q + task * total;
+  float mass = 0.f, ct;
+  for (int c0 = 0; c0 < total; c0 += 32) {
+    const int i = c0 + lane;
+    warp_exclusive(i < total ? fmaxf(nan0(p[i]), 0.f) : 0.f, lane, &ct);
+    mass += ct;
+  }
+  if (!(nan0(mass) > 1.0e-37f)) {
+    if (lane == 0) res[task] = 0.f;
+    return;
+  }
+  const float inv = 1.0f / mass;
+  float carry = 0.f, risk = 0.f;
+  for (int c0 = 0; c0 < total; c0 += 32) {
+    const int i = c0 + lane;
+    const float x = i < total ? fmaxf(nan0(p[i]), 0.f) : 0.f;
+    const float ex = warp_exclusive(x, lane, &ct);
+    if (i < total) {
+      const float hi = fminf(fmaxf((carry + ex + x) * inv, 0.f), 1.f);
+      const float lo = i == 0 ? 0.f : fminf(fmaxf((carry + ex) * inv, 0.f), 1.f);
+      const float w = fmaxf(srm_cumulative(hi, type, param, mean_w) - srm_cumulative(lo, type, param, mean_w), 0.f);
+      risk += w * nan0(z[i]);
+    }
+    carry += ct;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) risk += __shfl_xor_sync(kFull, risk, o);
+  if (lane == 0) res[task] = nan0(risk);
+}
+
 dim3 warp_grid(long long rows) { return dim3((unsigned)((rows * 32 + 255) / 256)); }
 
 // (quants, actions) kernels: total = global[0], rows = actions x batch.
@@ -510,6 +581,18 @@ int k_fqf_rearrange_grad(Launch &L) {
   return NN_OK;
 }
 
+int k_fqf_srm_forward(Launch &L) {
+  int T;
+  long long R;
+  quant_shape(L, &T, &R);
+  const size_t n = (size_t)R * T;
+  float *q = L.buf(0, n), *p = L.buf(1, n), *res = L.buf(2, (size_t)R);
+  if (!q || !p || !res) return NN_ERR_BOUNDS;
+  fqf_srm_forward_kernel<<<warp_grid(R), 256, 0, L.stream>>>(q, p, res, L.i(3), L.f(4), L.f(5), T, R);
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
 }  // namespace
 
 const KernelDef kFqfKernels[] = {
@@ -523,6 +606,7 @@ const KernelDef kFqfKernels[] = {
     {"FQF_FractionGradient", "pppi", k_fqf_fraction_grad, false},
     {"FQF_MonotoneRearrange", "pppppp", k_fqf_rearrange, false},
     {"FQF_RearrangeGradient", "ppppp", k_fqf_rearrange_grad, false},
+    {"FQF_SRMForward", "pppiff", k_fqf_srm_forward, false},
     {"SAC_AlphaLogProbs", "ppppppii", k_sac_alpha_log_probs, false},
     {"SAC_AlphaGradients", "ppppi", k_sac_alpha_grad, false},
     {"SAC_OutputGradient", "ppppppii", k_sac_output_grad, false},

@@ -50,7 +50,7 @@ KERNELS = [
     "UpdateWeightsAdamMini", "UpdateWeightsConvAdamMini", "MatMult", "MatMultGrad",
     "FQF_Cosine", "FQF_Output", "FQF_OutputGradient", "FQF_QuantileGradient", "FQF_CosineGradient",
     "FQF_FractionGradient", "FQF_CosineGradientSRM", "FQF_DistributionTargetGradient",
-    "FQF_MonotoneRearrange", "FQF_RearrangeGradient",
+    "FQF_MonotoneRearrange", "FQF_RearrangeGradient", "FQF_SRMForward",
     "SAC_AlphaLogProbs", "SAC_AlphaGradients", "SAC_OutputGradient", "SAC_CalcLogProbs",
     "MHFlashAttention", "MHFlashAttentionGrad",
 ]
@@ -153,9 +153,20 @@ RACE_PATCHES = [
 ]
 
 
+# Helper functions that NeuroNet.cl defines between kernels (after the first __kernel), needed by a
+# kernel in the list above: (return type and name as written).
+LATE_HELPERS = ["float SRMCumulative("]
+
+
+def _late_helper(cl_text: str, head: str) -> str:
+    start = cl_text.index("\n" + head) + 1
+    brace = cl_text.index("{", start)
+    return cl_text[start:_match_close(cl_text, brace, "{", "}")] + "\n"
+
+
 def generate(cl_text: str) -> str:
     first = cl_text.index("__kernel")
-    helpers = cl_text[:first]
+    helpers = cl_text[:first] + "".join(_late_helper(cl_text, h) for h in LATE_HELPERS)
     for old, new, count in RACE_PATCHES:
         if helpers.count(old) != count:
             raise RuntimeError(f"race patch anchor not found {count} times: {old!r}")

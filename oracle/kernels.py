@@ -1176,6 +1176,52 @@ def FQF_MonotoneRearrange(quantiles, probabilities, ordered_quantiles, ordered_p
                                               F32(pbad.sum())]
 
 
+def srm_cumulative(u, risk_type, risk_parameter, mean_weight):
+    """SRMCumulative, NeuroNet.cl:2805-2850 (float32)."""
+    eps = F32(1e-6)
+    tau = np.clip(np.asarray(u, F32), F32(0), F32(1)).astype(F32)
+    c = lambda x: np.clip(np.asarray(x, F32), F32(0), F32(1)).astype(F32)
+    if risk_type == 0:
+        return tau
+    if risk_type == 1:
+        alpha = F32(min(max(F32(risk_parameter), eps), F32(1)))
+        return c(np.minimum(tau, alpha) / alpha)
+    if risk_type == 2:
+        alpha = F32(min(max(F32(risk_parameter), eps), F32(1)))
+        omega = F32(min(max(F32(mean_weight), F32(0)), F32(1)))
+        return c(omega * tau + (F32(1) - omega) * np.minimum(tau, alpha) / alpha)
+    if risk_type == 3:
+        lam = F32(max(F32(risk_parameter), F32(0)))
+        if lam <= eps:
+            return tau
+        return c(-np.expm1((-lam * tau).astype(F32)) / -np.expm1(-lam))
+    if risk_type == 4:
+        nu = F32(max(F32(risk_parameter), F32(1)))
+        return c(F32(1) - np.power((F32(1) - tau).astype(F32), nu))
+    return np.zeros_like(tau)
+
+
+def FQF_SRMForward(quantiles, probabilities, result, risk_type, risk_parameter, mean_weight, gsize, lsize=None):
+    """NeuroNet.cl:2924-3021 over global (quants, rows), one work-group per row: with P_i the running
+    sum of max(IsNaNOrInf(p), 0) and M the row's mass, result = sum_i IsNaNOrInf(z_i)
+    max(F(P_i / M) - F(P_{i-1} / M), 0) for the spectral weight F; 0 when M <= 1e-37."""
+    T, R = gsize[0], (tuple(gsize) + (1,))[1]
+    with _err():
+        for v in range(R):
+            p = np.maximum(nan0(probabilities[v * T:(v + 1) * T]), F32(0)).astype(F32)
+            cs = np.cumsum(p, dtype=F32)
+            mass = F32(cs[-1]) if T else F32(0)
+            if not (nan0(mass) > F32(1e-37)):
+                result[v] = 0
+                continue
+            inv = F32(1) / mass
+            hi = np.clip((cs * inv).astype(F32), F32(0), F32(1))
+            lo = np.concatenate([[F32(0)], np.clip((cs[:-1] * inv).astype(F32), F32(0), F32(1))]).astype(F32)
+            w = np.maximum(srm_cumulative(hi, risk_type, risk_parameter, mean_weight)
+                           - srm_cumulative(lo, risk_type, risk_parameter, mean_weight), F32(0)).astype(F32)
+            result[v] = nan0((w * nan0(quantiles[v * T:(v + 1) * T])).astype(F32).sum(dtype=F32))
+
+
 def FQF_RearrangeGradient(ordered_quantiles_gradient, ordered_probabilities_gradient, order, quantiles_gradient,
                           probabilities_gradient, gsize, lsize=None):
     """NeuroNet.cl:20823-20842 over global (quants, rows): each ordered gradient goes back to the

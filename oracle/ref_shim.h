@@ -90,6 +90,7 @@ inline float log(float v) { return ::logf(v); }
 inline float sqrt(float v) { return ::sqrtf(v); }
 inline float tanh(float v) { return ::tanhf(v); }
 inline float pow(float a, float b) { return ::powf(a, b); }
+inline float expm1(float v) { return ::expm1f(v); }
 inline float fabs(float v) { return ::fabsf(v); }
 inline float sin(float v) { return ::sinf(v); }
 inline float cos(float v) { return ::cosf(v); }

@@ -405,6 +405,15 @@ def _quantile_head_cases():
         cases.append(Case(f"FQF_RearrangeGradient/{T}x{R}", "FQF_RearrangeGradient",
                           [A(R * T, "grad"), A(R * T, "grad"), A(R * T, "perm", T), A(R * T, "small"),
                            A(R * T, "small")], (T, R)))
+    # FQF_SRMForward (NeuroNet.cl:2924-3021): every risk type (mean, CVaR, mean-CVaR, exponential with
+    # a large and a vanishing lambda, dual power, an unknown type), rows of 1-64 quants, zero-mass rows
+    for T, R, rt, par, mw, init in [(32, 4, 0, 0.0, 0.0, "unit"), (32, 4, 1, 0.25, 0.0, "unit"),
+                                    (16, 3, 2, 0.1, 0.4, "unit"), (64, 2, 3, 2.5, 0.0, "unit"),
+                                    (8, 5, 3, 0.0, 0.0, "unit"), (32, 3, 4, 3.0, 0.0, "unit"),
+                                    (8, 2, 7, 1.0, 0.0, "unit"), (1, 3, 1, 0.5, 0.0, "unit"),
+                                    (16, 2, 1, 0.3, 0.0, "zeros"), (32, 3, 2, 0.2, 0.5, "nanmix")]:
+        cases.append(Case(f"FQF_SRMForward/{T}x{R}-r{rt}-p{par}-{init}", "FQF_SRMForward",
+                          [A(R * T), A(R * T, init), A(R, "small"), rt, par, mw], (T, R), (T, 1)))
     for n, cq, act in [(16, 32, NONE), (7, 8, TANH), (40, 5, SIGMOID), (3, 1, NONE), (9, 64, LRELU)]:
         cases.append(Case(f"SAC_AlphaLogProbs/{n}x{cq}-a{act}", "SAC_AlphaLogProbs",
                           [A(n, "zeros"), A(n * cq), A(n * cq, "unit"), A(n, "pos"), A(n, "zeros"), A(n, "unit"),
