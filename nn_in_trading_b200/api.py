@@ -29,7 +29,8 @@ SIGNATURES = {
     "FQF_Cosine": "pp", "FQF_Output": "pppi", "FQF_OutputGradient": "ppppp", "FQF_QuantileGradient": "ppppp",
     "FQF_CosineGradient": "ppp", "FQF_FractionGradient": "pppi",
     "FQF_CosineGradientSRM": "ppp", "FQF_DistributionTargetGradient": "ppppfff",
-    "FQF_MonotoneRearrange": "pppppp", "FQF_RearrangeGradient": "ppppp", "FQF_SRMForward": "pppiff", "SAC_AlphaLogProbs": "ppppppii",
+    "FQF_MonotoneRearrange": "pppppp", "FQF_RearrangeGradient": "ppppp", "FQF_SRMForward": "pppiff",
+    "FQF_SRMGradient": "pppppiff", "SAC_AlphaLogProbs": "ppppppii",
     "SAC_AlphaGradients": "ppppi",
     "SAC_OutputGradient": "ppppppii", "SAC_CalcLogProbs": "pppppii",
     "MHFlashAttention": "ppppiii", "MHFlashAttentionGrad": "pppppppiiii", "NormalizeWeights": "pi",

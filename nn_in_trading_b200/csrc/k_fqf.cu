@@ -9,6 +9,7 @@
 //   FQF_DistributionTargetGradient  gradient into the quantile nearest a target  NeuroNet.cl:2663-2716
 //   FQF_FractionGradient   input gradient of the fraction proposal layer     NeuroNet.cl:3207-3224
 //   FQF_SRMForward         spectral risk of the quantile distribution        NeuroNet.cl:2924-3021
+//   FQF_SRMGradient        its quantile and probability gradients            NeuroNet.cl:3027-3200
 //   FQF_MonotoneRearrange  quantiles in ascending order, with diagnostics    NeuroNet.cl:20716-20817
 //   FQF_RearrangeGradient  ordered gradients back to their source quantiles  NeuroNet.cl:20823-20842
 //   SAC_AlphaLogProbs      sample a quantile by its probability, -alpha log p NeuroNet.cl:3903-3933
@@ -418,6 +419,103 @@ __global__ void fqf_srm_forward_kernel(const float *__restrict__ q, const float 
   if (lane == 0) res[task] = nan0(risk);
 }
 
+// SRMDensity (NeuroNet.cl:2855-2900): the derivative of srm_cumulative in tau.
+__device__ __forceinline__ float srm_density(float u, int type, float param, float mean_w) {
+  constexpr float kEps = 1.0e-6f;
+  const float tau = fminf(fmaxf(u, 0.f), 1.f);
+  switch (type) {
+    case 0: return 1.f;
+    case 1: {
+      const float alpha = fminf(fmaxf(param, kEps), 1.f);
+      return tau < alpha ? 1.f / alpha : 0.f;
+    }
+    case 2: {
+      const float alpha = fminf(fmaxf(param, kEps), 1.f);
+      const float omega = fminf(fmaxf(mean_w, 0.f), 1.f);
+      return tau < alpha ? omega + (1.f - omega) / alpha : omega;
+    }
+    case 3: {
+      const float lambda = fmaxf(param, 0.f);
+      if (lambda <= kEps) return 1.f;
+      return fmaxf(lambda * expf(-lambda * tau) / -expm1f(-lambda), 0.f);
+    }
+    case 4: {
+      const float nu = fmaxf(param, 1.f);
+      if (nu == 1.f) return 1.f;
+      return fmaxf(nu * powf(1.f - tau, nu - 1.f), 0.f);
+    }
+    default: return 0.f;
+  }
+}
+
+// FQF_SRMGradient: per row with upstream gradient u (rows with u == 0 or no mass get zeros):
+// quantile i gets u w_i (0 for a non-finite quantile); with b_i = u (z_i - z_{i+1}) F'(P_i / M) and
+// S_i = sum_{j >= i} b_j, probability i gets (S_i - sum_j (p_j / M) S_j) / M (0 for a non-finite or
+// negative probability).  A warp per row: the mass, then weights and b_i (held in the probability
+// gradient), then S_i from the last chunk back with the correction sum, then the final values;
+// each lane rereads only the entries it wrote.
+__global__ void fqf_srm_grad_kernel(const float *__restrict__ q, const float *__restrict__ pr,
+                                    const float *__restrict__ rg, float *__restrict__ qg, float *__restrict__ pg,
+                                    int type, float param, float mean_w, int total, long long rows) {
+  const long long task = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (task >= rows) return;
+  const float *p = pr + task * total;
+  const float *z = q + task * total;
+  float *qo = qg + task * total;
+  float *po = pg + task * total;
+  const float up = nan0(rg[task]);
+  float mass = 0.f, ct;
+  for (int c0 = 0; c0 < total; c0 += 32) {
+    const int i = c0 + lane;
+    warp_exclusive(i < total ? fmaxf(nan0(p[i]), 0.f) : 0.f, lane, &ct);
+    mass += ct;
+  }
+  mass = nan0(mass);
+  if (up == 0.f || mass <= 1.0e-37f) {
+    for (int i = lane; i < total; i += 32) qo[i] = po[i] = 0.f;
+    return;
+  }
+  const float inv = 1.0f / mass;
+  float carry = 0.f;
+  for (int c0 = 0; c0 < total; c0 += 32) {
+    const int i = c0 + lane;
+    const float x = i < total ? fmaxf(nan0(p[i]), 0.f) : 0.f;
+    const float ex = warp_exclusive(x, lane, &ct);
+    if (i < total) {
+      const float hi = fminf(fmaxf((carry + ex + x) * inv, 0.f), 1.f);
+      const float lo = i == 0 ? 0.f : fminf(fmaxf((carry + ex) * inv, 0.f), 1.f);
+      const float w = fmaxf(srm_cumulative(hi, type, param, mean_w) - srm_cumulative(lo, type, param, mean_w), 0.f);
+      qo[i] = isfinite(z[i]) ? nan0(up * w) : 0.f;
+      po[i] = i + 1 < total ? nan0(up * (nan0(z[i]) - nan0(z[i + 1])) * srm_density(hi, type, param, mean_w)) : 0.f;
+    }
+    carry += ct;
+  }
+  const int last = (total - 1) / 32 * 32;
+  float after = 0.f, corr = 0.f;
+  for (int c0 = last; c0 >= 0; c0 -= 32) {
+    const int i = c0 + lane;
+    float inc = i < total ? po[i] : 0.f;  // inclusive suffix over the lanes
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const float y = __shfl_down_sync(kFull, inc, d);
+      if (lane + d < 32) inc += y;
+    }
+    if (i < total) {
+      const float suffix = after + inc;
+      po[i] = suffix;
+      corr += (fmaxf(nan0(p[i]), 0.f) * inv) * suffix;
+    }
+    after += __shfl_sync(kFull, inc, 0);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) corr += __shfl_xor_sync(kFull, corr, o);
+  for (int i = lane; i < total; i += 32) {
+    const bool pv = isfinite(p[i]) && p[i] >= 0.f;
+    po[i] = pv ? nan0((po[i] - corr) * inv) : 0.f;
+  }
+}
+
 dim3 warp_grid(long long rows) { return dim3((unsigned)((rows * 32 + 255) / 256)); }
 
 // (quants, actions) kernels: total = global[0], rows = actions x batch.
@@ -593,6 +691,19 @@ int k_fqf_srm_forward(Launch &L) {
   return NN_OK;
 }
 
+int k_fqf_srm_grad(Launch &L) {
+  int T;
+  long long R;
+  quant_shape(L, &T, &R);
+  if (T == 0) return NN_OK;
+  const size_t n = (size_t)R * T;
+  float *q = L.buf(0, n), *p = L.buf(1, n), *rg = L.buf(2, (size_t)R), *qg = L.buf(3, n), *pg = L.buf(4, n);
+  if (!q || !p || !rg || !qg || !pg) return NN_ERR_BOUNDS;
+  fqf_srm_grad_kernel<<<warp_grid(R), 256, 0, L.stream>>>(q, p, rg, qg, pg, L.i(5), L.f(6), L.f(7), T, R);
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
 }  // namespace
 
 const KernelDef kFqfKernels[] = {
@@ -607,6 +718,7 @@ const KernelDef kFqfKernels[] = {
     {"FQF_MonotoneRearrange", "pppppp", k_fqf_rearrange, false},
     {"FQF_RearrangeGradient", "ppppp", k_fqf_rearrange_grad, false},
     {"FQF_SRMForward", "pppiff", k_fqf_srm_forward, false},
+    {"FQF_SRMGradient", "pppppiff", k_fqf_srm_grad, false},
     {"SAC_AlphaLogProbs", "ppppppii", k_sac_alpha_log_probs, false},
     {"SAC_AlphaGradients", "ppppi", k_sac_alpha_grad, false},
     {"SAC_OutputGradient", "ppppppii", k_sac_output_grad, false},

@@ -50,7 +50,7 @@ KERNELS = [
     "UpdateWeightsAdamMini", "UpdateWeightsConvAdamMini", "MatMult", "MatMultGrad",
     "FQF_Cosine", "FQF_Output", "FQF_OutputGradient", "FQF_QuantileGradient", "FQF_CosineGradient",
     "FQF_FractionGradient", "FQF_CosineGradientSRM", "FQF_DistributionTargetGradient",
-    "FQF_MonotoneRearrange", "FQF_RearrangeGradient", "FQF_SRMForward",
+    "FQF_MonotoneRearrange", "FQF_RearrangeGradient", "FQF_SRMForward", "FQF_SRMGradient",
     "SAC_AlphaLogProbs", "SAC_AlphaGradients", "SAC_OutputGradient", "SAC_CalcLogProbs",
     "MHFlashAttention", "MHFlashAttentionGrad",
 ]
@@ -155,7 +155,7 @@ RACE_PATCHES = [
 
 # Helper functions that NeuroNet.cl defines between kernels (after the first __kernel), needed by a
 # kernel in the list above: (return type and name as written).
-LATE_HELPERS = ["float SRMCumulative("]
+LATE_HELPERS = ["float SRMCumulative(", "float SRMDensity("]
 
 
 def _late_helper(cl_text: str, head: str) -> str:

@@ -1222,6 +1222,69 @@ def FQF_SRMForward(quantiles, probabilities, result, risk_type, risk_parameter, 
             result[v] = nan0((w * nan0(quantiles[v * T:(v + 1) * T])).astype(F32).sum(dtype=F32))
 
 
+def srm_density(u, risk_type, risk_parameter, mean_weight):
+    """SRMDensity, NeuroNet.cl:2855-2900 (float32)."""
+    eps = F32(1e-6)
+    tau = np.clip(np.asarray(u, F32), F32(0), F32(1)).astype(F32)
+    one = np.ones_like(tau)
+    if risk_type == 0:
+        return one
+    if risk_type == 1:
+        alpha = F32(min(max(F32(risk_parameter), eps), F32(1)))
+        return np.where(tau < alpha, F32(1) / alpha, F32(0)).astype(F32)
+    if risk_type == 2:
+        alpha = F32(min(max(F32(risk_parameter), eps), F32(1)))
+        omega = F32(min(max(F32(mean_weight), F32(0)), F32(1)))
+        return np.where(tau < alpha, omega + (F32(1) - omega) / alpha, omega).astype(F32)
+    if risk_type == 3:
+        lam = F32(max(F32(risk_parameter), F32(0)))
+        if lam <= eps:
+            return one
+        return np.maximum(lam * np.exp((-lam * tau).astype(F32)) / -np.expm1(-lam), F32(0)).astype(F32)
+    if risk_type == 4:
+        nu = F32(max(F32(risk_parameter), F32(1)))
+        if nu == F32(1):
+            return one
+        return np.maximum(nu * np.power((F32(1) - tau).astype(F32), nu - F32(1)), F32(0)).astype(F32)
+    return np.zeros_like(tau)
+
+
+def FQF_SRMGradient(quantiles, probabilities, result_gradient, quantiles_gradient, probabilities_gradient,
+                    risk_type, risk_parameter, mean_weight, gsize, lsize=None):
+    """NeuroNet.cl:3027-3200 over global (quants, rows), one work-group per row, upstream u =
+    IsNaNOrInf(result_gradient[row]) (u == 0 or no probability mass: zeros): quantile i gets
+    IsNaNOrInf(u w_i) (0 when not finite); with b_i = IsNaNOrInf(u (z_i - z_{i+1}) F'(P_i / M)) and
+    S_i = sum_{j >= i} b_j, probability i gets IsNaNOrInf((S_i - sum_j (p_j / M) S_j) / M) (0 when not
+    finite or negative)."""
+    T, R = gsize[0], (tuple(gsize) + (1,))[1]
+    with _err():
+        for v in range(R):
+            sl = slice(v * T, (v + 1) * T)
+            raw_p, raw_z = probabilities[sl].astype(F32), quantiles[sl].astype(F32)
+            p = np.maximum(nan0(raw_p), F32(0)).astype(F32)
+            z = nan0(raw_z)
+            up = nan0(result_gradient[v])
+            cs = np.cumsum(p, dtype=F32)
+            mass = nan0(cs[-1])
+            if up == 0 or mass <= F32(1e-37):
+                quantiles_gradient[sl] = 0
+                probabilities_gradient[sl] = 0
+                continue
+            inv = F32(1) / mass
+            hi = np.clip((cs * inv).astype(F32), F32(0), F32(1))
+            lo = np.concatenate([[F32(0)], np.clip((cs[:-1] * inv).astype(F32), F32(0), F32(1))])
+            w = np.maximum(srm_cumulative(hi, risk_type, risk_parameter, mean_weight)
+                           - srm_cumulative(lo.astype(F32), risk_type, risk_parameter, mean_weight), F32(0))
+            quantiles_gradient[sl] = np.where(np.isfinite(raw_z), nan0(up * w.astype(F32)), F32(0))
+            nxt = np.concatenate([z[1:], z[-1:]])
+            b = nan0((up * (z - nxt)).astype(F32) * srm_density(hi, risk_type, risk_parameter, mean_weight))
+            b[-1] = 0
+            suffix = np.cumsum(b[::-1], dtype=F32)[::-1].astype(F32)
+            corr = ((p * inv).astype(F32) * suffix).astype(F32).sum(dtype=F32)
+            pv = np.isfinite(raw_p) & (raw_p >= 0)
+            probabilities_gradient[sl] = np.where(pv, nan0(((suffix - corr) * inv).astype(F32)), F32(0))
+
+
 def FQF_RearrangeGradient(ordered_quantiles_gradient, ordered_probabilities_gradient, order, quantiles_gradient,
                           probabilities_gradient, gsize, lsize=None):
     """NeuroNet.cl:20823-20842 over global (quants, rows): each ordered gradient goes back to the

@@ -414,6 +414,9 @@ def _quantile_head_cases():
                                     (16, 2, 1, 0.3, 0.0, "zeros"), (32, 3, 2, 0.2, 0.5, "nanmix")]:
         cases.append(Case(f"FQF_SRMForward/{T}x{R}-r{rt}-p{par}-{init}", "FQF_SRMForward",
                           [A(R * T), A(R * T, init), A(R, "small"), rt, par, mw], (T, R), (T, 1)))
+        cases.append(Case(f"FQF_SRMGradient/{T}x{R}-r{rt}-p{par}-{init}", "FQF_SRMGradient",
+                          [A(R * T, "nanmix" if init == "nanmix" else "normal"), A(R * T, init), A(R, "grad"),
+                           A(R * T, "small"), A(R * T, "small"), rt, par, mw], (T, R), (T, 1)))
     for n, cq, act in [(16, 32, NONE), (7, 8, TANH), (40, 5, SIGMOID), (3, 1, NONE), (9, 64, LRELU)]:
         cases.append(Case(f"SAC_AlphaLogProbs/{n}x{cq}-a{act}", "SAC_AlphaLogProbs",
                           [A(n, "zeros"), A(n * cq), A(n * cq, "unit"), A(n, "pos"), A(n, "zeros"), A(n, "unit"),

@@ -77,7 +77,7 @@ PER_SAMPLE_KERNELS = {
     "FQF_QuantileGradient": [0, 1, 2, 3, 4], "FQF_CosineGradient": [0, 1, 2], "FQF_FractionGradient": [1, 2],
     "FQF_CosineGradientSRM": [0, 1, 2], "FQF_DistributionTargetGradient": [0, 1, 2, 3],
     "FQF_MonotoneRearrange": [0, 1, 2, 3, 4, 5], "FQF_RearrangeGradient": [0, 1, 2, 3, 4],
-    "FQF_SRMForward": [0, 1, 2],
+    "FQF_SRMForward": [0, 1, 2], "FQF_SRMGradient": [0, 1, 2, 3, 4],
     "SAC_AlphaLogProbs": [0, 1, 2, 3, 4, 5], "SAC_AlphaGradients": [0, 1, 2, 3],
     "SAC_OutputGradient": [0, 1, 2, 3, 4, 5], "SAC_CalcLogProbs": [0, 1, 2, 3, 4],
     "MHFlashAttention": [0, 1, 2, 3], "MHFlashAttentionGrad": [0, 1, 2, 3, 4, 5, 6],
