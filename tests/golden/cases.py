@@ -74,6 +74,9 @@ def materialise(case: Case, seed: int) -> list:
             # normal values, one in ten scaled to 1e20 (products of two of them overflow float)
             v = rng.standard_normal(n) * a.scale
             v[rng.uniform(0.0, 1.0, n) < 0.1] *= 1e20
+        elif a.init == "coarse":
+            # normal values on a grid of 0.5 (repeated values: the tie rules of searches and sorts)
+            v = np.round(rng.standard_normal(n) * a.scale * 2.0) / 2.0
         elif a.init == "perm":
             # rows of int(scale) entries, each a permutation of its indices (as floats), a few NaN
             T = int(a.scale)
@@ -384,7 +387,7 @@ def _quantile_head_cases():
                           [A(R * T, "unit"), A(R * T, "grad"), A(R * T, "small")], (T, R), meta=sm))
         cases.append(Case(f"FQF_CosineGradientSRM/{T}x{R}", "FQF_CosineGradientSRM",
                           [A(R * T, "unit"), A(R * T, "grad"), A(R * T, "small")], (T, R), meta=sm))
-        for target, init in [(0.3, "normal"), (-1.2, "nanmix"), (float("nan"), "normal")]:
+        for target, init in [(0.3, "normal"), (-1.2, "nanmix"), (float("nan"), "normal"), (0.25, "coarse")]:
             cases.append(Case(f"FQF_DistributionTargetGradient/{T}x{R}-t{target}-{init}",
                               "FQF_DistributionTargetGradient",
                               [A(R * T, init), A(R * T, "unit"), A(R * T, "small"), A(R * T, "small"), target,
@@ -398,7 +401,7 @@ def _quantile_head_cases():
     # FQF_MonotoneRearrange / FQF_RearrangeGradient (NeuroNet.cl:20716-20842): rows of a power of two up
     # to 64 quants (others are left untouched by the reference), NaN/inf quantiles and probabilities
     for T, R, init in [(32, 5, "normal"), (8, 3, "nanmix"), (64, 2, "normal"), (1, 4, "normal"), (2, 3, "nanmix"),
-                       (12, 2, "normal"), (128, 1, "normal")]:
+                       (12, 2, "normal"), (128, 1, "normal"), (32, 4, "coarse")]:
         cases.append(Case(f"FQF_MonotoneRearrange/{T}x{R}-{init}", "FQF_MonotoneRearrange",
                           [A(R * T, init), A(R * T, init), A(R * T, "small"), A(R * T, "small"), A(R * T, "small"),
                            A(R * 6, "small")], (T, R), (T, 1)))
