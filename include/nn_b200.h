@@ -98,6 +98,14 @@ NN_API int nn_buffer_free(int handle);
 NN_API int nn_buffer_write(int handle, const float *src, long long offset, long long count);
 /* CBufferFloat::BufferRead / COpenCL::BufferRead: blocking read. */
 NN_API int nn_buffer_read(int handle, float *dst, long long offset, long long count);
+/* COpenCLMy::BufferWrite(buffer, data, offset, start, count) and COpenCL::BufferRead with the same
+ * arguments (NeuroNet_Declarations.mqh:425-430, over MetaQuotes' CLBufferWrite / CLBufferRead):
+ * `byte_offset` is the position in the device buffer in BYTES (a multiple of 4), `start` the index
+ * of the first element of the host array `data`, `count` the number of floats.  Copies
+ * data[start .. start+count) to / from device floats byte_offset/4 .. byte_offset/4+count. */
+NN_API int nn_buffer_write_ex(int handle, const float *data, long long byte_offset, long long start,
+                              long long count);
+NN_API int nn_buffer_read_ex(int handle, float *data, long long byte_offset, long long start, long long count);
 /* Extension (no reference counterpart): overlapped transfers, for a host that feeds the next step
  * while the current one computes.
  * nn_buffer_write_async: host -> device copy on a transfer stream, concurrent with the executions
@@ -187,9 +195,14 @@ NN_API int nn_dp_shutdown(void);
 NN_API int nn_dp_allreduce(int handle, long long offset, long long count, float scale);
 /* Deferred-update region: between begin and end, weight-update kernels write
  * their batch-mean weight gradient into a gradient arena instead of applying
- * it, and their update (and any NormalizeWeights execution) is queued.  At
- * nn_dp_update_end the arena is averaged over the ranks with one NCCL
- * allreduce and the queued updates run in their original order. */
+ * it, and their update (and any NormalizeWeights execution) is queued.  The
+ * arena is averaged over the ranks in buckets: once 1 MB of new gradients has
+ * gathered, an NCCL allreduce of that bucket starts on a communication stream
+ * while the context stream goes on with the rest of backward.  At
+ * nn_dp_update_end the last bucket is reduced, the context stream waits for
+ * every bucket, and the queued updates run in their original order.  Every
+ * rank must issue the same updates in the same order (the bucket boundaries,
+ * and so the collectives, then agree). */
 NN_API int nn_dp_update_begin(void);
 NN_API int nn_dp_update_end(void);
 
@@ -205,10 +218,15 @@ NN_API int nn_dp_update_end(void);
  *   matrix_w, matrix_m, matrix_v  [outputs][inputs+1]
  *   matrix_g [batch][outputs]   matrix_i [batch][inputs]
  * Runs on the context stream (nn_init first).  outputs*(inputs+1) above
- * 2,097,152 floats returns NN_ERR_BOUNDS.  The first call on a device sets up
- * the array's address and should come before any stream capture starts.  The
- * array is shared by every call on a device: calls that overlap in time race
- * and must be ordered by the caller. */
+ * 2,097,152 floats returns NN_ERR_BOUNDS.  nn_init looks up the array's
+ * address on the context's device, which also loads the module that holds it
+ * (under lazy module loading the array is reserved then, not at the first
+ * call); if that look-up failed, the first call retries it and should come
+ * before any stream capture starts and before the host takes the device's
+ * free memory.  The array is shared by every call on a device: calls that
+ * overlap in time race and must be ordered by the caller.  The update is
+ * local to this process: inside nn_dp_update_begin .. end it returns
+ * NN_ERR_STATE instead of applying one rank's gradient. */
 NN_API int nn_update_weights_adam_fixed(float *matrix_w, const float *matrix_g, const float *matrix_i,
                                         float *matrix_m, float *matrix_v, int outputs, int inputs, int batch,
                                         float l, float b1, float b2);

@@ -51,7 +51,8 @@ SIGNATURES = {
     "SACGaussianPolicy": "ppppi", "SACTargetValue": "ppppppff", "SACPolicyGradient": "ppppppppif",
     "MH2AttentionOut": "ppppiii", "MH2AttentionInsideGradients": "ppppppii",
     "AttentionScore": "pppii", "AttentionOut": "pppp", "AttentionInsideGradients": "pppppppp",
-    "Dropout": "pppi",
+    "Dropout": "pppi", "PatchCreate": "pppiiii", "PatchHiddenGradient": "ppppiiiii",
+    "PatchUpdateWeightsAdam": "pppppifffi", "FQF_Sample": "pppp",
 }
 
 
@@ -80,6 +81,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         "nn_finish": ([c_int], c_int), "nn_stream": ([], c_p),
         "nn_buffer_create": ([c_ll], c_int), "nn_buffer_free": ([c_int], c_int),
         "nn_buffer_write": ([c_int, c_p, c_ll, c_ll], c_int), "nn_buffer_read": ([c_int, c_p, c_ll, c_ll], c_int),
+        "nn_buffer_write_ex": ([c_int, c_p, c_ll, c_ll, c_ll], c_int),
+        "nn_buffer_read_ex": ([c_int, c_p, c_ll, c_ll, c_ll], c_int),
         "nn_buffer_fill": ([c_int, c_f, c_ll, c_ll], c_int),
         "nn_buffer_copy": ([c_int, c_ll, c_int, c_ll, c_ll], c_int),
         "nn_buffer_write_async": ([c_int, c_p, c_ll, c_ll], c_int),

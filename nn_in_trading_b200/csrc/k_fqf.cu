@@ -12,6 +12,7 @@
 //   FQF_SRMGradient        its quantile and probability gradients            NeuroNet.cl:3027-3200
 //   FQF_MonotoneRearrange  quantiles in ascending order, with diagnostics    NeuroNet.cl:20716-20817
 //   FQF_RearrangeGradient  ordered gradients back to their source quantiles  NeuroNet.cl:20823-20842
+//   FQF_Sample             one draw per row from the quantile distribution   NeuroNet.cl:2722-2799
 //   SAC_AlphaLogProbs      sample a quantile by its probability, -alpha log p NeuroNet.cl:3903-3933
 //   SAC_AlphaGradients     gradient of alpha                                 NeuroNet.cl:3939-3951
 //   SAC_OutputGradient     gradient into the quantiles bracketing the action NeuroNet.cl:3957-4000
@@ -419,6 +420,61 @@ __global__ void fqf_srm_forward_kernel(const float *__restrict__ q, const float 
   if (lane == 0) res[task] = nan0(risk);
 }
 
+// FQF_Sample (NeuroNet.cl:2722-2799): per row (task), the running probability mass C_i of
+// max(IsNaNOrInf(p_i), 0) and a uniform u = clamp(IsNaNOrInf(random[task], 0.5), 0, 1); the sample
+// is the quantile of the smallest i with C_i >= u * C_last and C_{i-1} < u * C_last (the last one
+// if none), 0 when C_last <= 1e-6.  The reference forms C with a Hillis-Steele scan in local
+// memory (Temp[i] += Temp[i - d] for d = 1, 2, 4, ... below the row length); the selection
+// compares C against the threshold, so this kernel adds in exactly that order to get the same
+// rounded C: a warp per row, element i in lane i (a) and lane i - 32 (b), rows of at most 64.
+__global__ void fqf_sample_kernel(const float *__restrict__ q, const float *__restrict__ pr,
+                                  const float *__restrict__ rnd, float *__restrict__ res, int total, long long rows) {
+  const long long task = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (task >= rows) return;
+  const float *p = pr + task * total;
+  float a = lane < total ? fmaxf(nan0(p[lane]), 0.f) : 0.f;
+  float b = lane + 32 < total ? fmaxf(nan0(p[lane + 32]), 0.f) : 0.f;
+  for (int d = 1; d < total; d <<= 1) {
+    if (d < 32) {
+      // every read of the step before any write, as the reference's barrier orders them
+      const float a_lo = __shfl_up_sync(kFull, a, d);            // a[lane - d]
+      const float b_lo = __shfl_up_sync(kFull, b, d);            // b[lane - d]
+      const float a_wrap = __shfl_sync(kFull, a, (lane - d) & 31);  // a[lane - d + 32]
+      if (lane >= d) a += a_lo;
+      b += lane >= d ? b_lo : a_wrap;
+    } else {
+      b += a;  // d == 32: element lane + 32 adds element lane
+    }
+  }
+  const float last = total <= 32 ? __shfl_sync(kFull, a, total - 1) : __shfl_sync(kFull, b, total - 33);
+  const float mass = nan0(last);
+  if (mass <= 1.0e-6f) {
+    if (lane == 0) res[task] = 0.f;
+    return;
+  }
+  const float u = fminf(fmaxf(nan0(rnd[task], 0.5f), 0.f), 1.f);
+  const float threshold = u * mass;
+  const float a_prev = __shfl_up_sync(kFull, a, 1);
+  const float b_prev = lane == 0 ? __shfl_sync(kFull, a, 31) : __shfl_up_sync(kFull, b, 1);
+  int pick = total;
+  {
+    const int i = lane;
+    bool sel = i < total && a >= threshold && (i == 0 || a_prev < threshold);
+    if (i == total - 1 && a < threshold) sel = true;
+    if (sel) pick = i;
+  }
+  {
+    const int i = lane + 32;
+    bool sel = i < total && b >= threshold && b_prev < threshold;
+    if (i == total - 1 && b < threshold) sel = true;
+    if (sel) pick = min(pick, i);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) pick = min(pick, __shfl_xor_sync(kFull, pick, o));
+  if (lane == 0 && pick < total) res[task] = nan0(q[task * total + pick]);
+}
+
 // SRMDensity (NeuroNet.cl:2855-2900): the derivative of srm_cumulative in tau.
 __device__ __forceinline__ float srm_density(float u, int type, float param, float mean_w) {
   constexpr float kEps = 1.0e-6f;
@@ -691,6 +747,22 @@ int k_fqf_srm_forward(Launch &L) {
   return NN_OK;
 }
 
+// FQF_Sample over global (quants, tasks) with local (quants, 1): the row length is the local size.
+int k_fqf_sample(Launch &L) {
+  if (!L.nd.has_local || L.nd.l[0] != L.nd.g[0] || (L.nd.dims > 1 && L.nd.l[1] != 1))
+    return L.fail(NN_ERR_UNSUPPORTED, "FQF_Sample: expects local size (quants, 1) with quants = global[0]");
+  const int T = (int)L.nd.l[0];
+  if (T > 64)
+    return L.fail(NN_ERR_UNSUPPORTED, "FQF_Sample: at most 64 quants per row (the reference's local scan array)");
+  const long long R = (long long)(L.nd.dims > 1 ? L.nd.g[1] : 1) * L.B;
+  const size_t n = (size_t)R * T;
+  float *q = L.buf(0, n), *p = L.buf(1, n), *rnd = L.buf(2, (size_t)R), *res = L.buf(3, (size_t)R);
+  if (!q || !p || !rnd || !res) return NN_ERR_BOUNDS;
+  fqf_sample_kernel<<<warp_grid(R), 256, 0, L.stream>>>(q, p, rnd, res, T, R);
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
 int k_fqf_srm_grad(Launch &L) {
   int T;
   long long R;
@@ -719,6 +791,7 @@ const KernelDef kFqfKernels[] = {
     {"FQF_RearrangeGradient", "ppppp", k_fqf_rearrange_grad, false},
     {"FQF_SRMForward", "pppiff", k_fqf_srm_forward, false},
     {"FQF_SRMGradient", "pppppiff", k_fqf_srm_grad, false},
+    {"FQF_Sample", "pppp", k_fqf_sample, false},
     {"SAC_AlphaLogProbs", "ppppppii", k_sac_alpha_log_probs, false},
     {"SAC_AlphaGradients", "ppppi", k_sac_alpha_grad, false},
     {"SAC_OutputGradient", "ppppppii", k_sac_output_grad, false},

@@ -106,6 +106,8 @@ extern const KernelDef kFqfKernels[];
 extern const int kNumFqfKernels;
 extern const KernelDef kFlashKernels[];
 extern const int kNumFlashKernels;
+extern const KernelDef kPatchKernels[];
+extern const int kNumPatchKernels;
 
 // Number of data-parallel ranks (1 without a communicator).
 int dp_world();
@@ -118,6 +120,15 @@ int report_error(int status, const std::string &msg);
 int *device_status();
 // True unless the context was created with NN_INIT_SIMT_GEMM.
 bool tensor_gemm_enabled();
+// CUDA ordinal of the context (-1 without one).
+int context_device();
+// True while a data-parallel update region (nn_dp_update_begin .. end) is open.
+bool dp_update_open();
+// Adds n launches to the context's launch counter (for entry points outside a kernel Launch).
+void add_launches(int n);
+// Resolves the device address of the fixed scratch array on `device` (which is current), so that
+// its module is loaded at nn_init rather than at the first call that uses it.
+int fixed_scratch_setup(int device);
 
 const KernelDef *find_kernel(const char *name);
 

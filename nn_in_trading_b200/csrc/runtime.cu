@@ -62,6 +62,7 @@ struct Nccl {
 };
 constexpr int kNcclFloat32 = 7;  // ncclFloat32
 constexpr int kNcclSum = 0;      // ncclSum
+constexpr int kNcclAvg = 4;      // ncclAvg (NCCL >= 2.10)
 
 struct Context {
   int device = 0;
@@ -83,6 +84,14 @@ struct Context {
   bool deferring = false;
   float *arena = nullptr;
   size_t arena_cap = 0, arena_used = 0;
+  // gradient buckets: [0, arena_flushed) has been handed to NCCL on comm_stream; a bucket is
+  // flushed once kBucketFloats of new gradients have been deferred, while backward goes on
+  size_t arena_flushed = 0;
+  static constexpr size_t kBucketFloats = size_t(1) << 18;  // 1 MB
+  cudaStream_t comm_stream = nullptr;
+  cudaEvent_t ev_grads = nullptr, ev_reduced = nullptr;
+  int dp_pending = NN_OK;  // first error of a bucket flush inside the open region
+  std::string dp_pending_msg;
   std::vector<DeferredOp> deferred;
   // device status word written by kernels whose bounded waits expired (0 = fine)
   int *status = nullptr;
@@ -203,6 +212,8 @@ float *Launch::grad_slot(size_t n) {
   return ctx->arena + start;
 }
 
+static int flush_bucket(Context *c);
+
 void Launch::defer(int (*apply)(const Launch &, const float *), const float *grad) {
   DeferredOp op;
   op.k = *k;
@@ -210,6 +221,17 @@ void Launch::defer(int (*apply)(const Launch &, const float *), const float *gra
   op.apply = apply;
   op.grad = grad;
   ctx->deferred.push_back(op);
+  // every gradient written so far is final for this step: once a bucket's worth has gathered,
+  // its allreduce starts on the communication stream while the rest of backward runs
+  if (ctx->arena_used - ctx->arena_flushed >= Context::kBucketFloats && ctx->dp_pending == NN_OK) {
+    std::string saved = g_err;
+    int rc = flush_bucket(ctx);
+    if (rc) {
+      ctx->dp_pending = rc;
+      ctx->dp_pending_msg = g_err;
+    }
+    g_err = saved;
+  }
 }
 
 void Launch::counted(int n) { ctx->launches += n; }
@@ -221,7 +243,7 @@ const KernelDef *find_kernel(const char *name) {
                           {kLstmKernels, kNumLstmKernels}, {kAttn2Kernels, kNumAttn2Kernels},
                           {kSacKernels, kNumSacKernels}, {kMatKernels, kNumMatKernels},
                           {kFqfKernels, kNumFqfKernels},
-                          {kFlashKernels, kNumFlashKernels}};
+                          {kFlashKernels, kNumFlashKernels}, {kPatchKernels, kNumPatchKernels}};
   for (const Table &t : tables)
     for (int i = 0; i < t.n; ++i)
       if (std::strcmp(t.t[i].name, name) == 0) return &t.t[i];
@@ -235,6 +257,14 @@ int report_error(int status, const std::string &msg) { return set_err(status, ms
 int *device_status() { return g_ctx ? g_ctx->status : nullptr; }
 
 bool tensor_gemm_enabled() { return g_ctx && !g_ctx->simt_gemm && g_ctx->status; }
+
+int context_device() { return g_ctx ? g_ctx->device : -1; }
+
+bool dp_update_open() { return g_ctx && g_ctx->deferring; }
+
+void add_launches(int n) {
+  if (g_ctx) g_ctx->launches += n;
+}
 
 static int run_one(Context *c, const KernelInst &k, const NDR &nd) {
   Launch L;
@@ -259,6 +289,25 @@ static int run_deferred(Context *c, const DeferredOp &op) {
   L.stream = c->stream;
   L.B = op.k.batch;
   return op.apply(L, op.grad);
+}
+
+// Average arena[arena_flushed, arena_used) over the ranks on the communication stream, after the
+// context stream's launches so far (which wrote those gradients).  Every rank defers the same
+// updates in the same order, so every rank issues the same sequence of bucket allreduces.
+static int flush_bucket(Context *c) {
+  const size_t n = c->arena_used - c->arena_flushed;
+  if (n == 0) return NN_OK;
+  if (c->comm && c->world > 1) {
+    CUDA_TRY(cudaEventRecord(c->ev_grads, c->stream));
+    CUDA_TRY(cudaStreamWaitEvent(c->comm_stream, c->ev_grads, 0));
+    float *p = c->arena + c->arena_flushed;
+    int r = c->nccl.all_reduce(p, p, n, kNcclFloat32, kNcclAvg, c->comm, c->comm_stream);
+    if (r)
+      return set_err(NN_ERR_NCCL, std::string("ncclAllReduce (gradient bucket): ") +
+                                      (c->nccl.error_string ? c->nccl.error_string(r) : ""));
+  }
+  c->arena_flushed = c->arena_used;
+  return NN_OK;
 }
 
 }  // namespace nn
@@ -296,6 +345,14 @@ int nn_init(int device, int flags) {
     return set_err(NN_ERR_CUDA, cudaGetErrorString(e));
   }
   g_ctx = c;
+  // Load the module of the fixed scratch array now: under lazy module loading it would otherwise
+  // be loaded (and its array reserved) inside the first nn_update_weights_adam_fixed call, after a
+  // host may have handed all free device memory to its own pool.  A failure here is not fatal:
+  // that entry point retries the look-up and reports it.
+  if (fixed_scratch_setup(device) != NN_OK) {
+    cudaGetLastError();
+    g_err.clear();
+  }
   return NN_OK;
 }
 
@@ -310,7 +367,13 @@ int nn_shutdown(void) {
   for (auto &kv : c->sides) cudaFree(kv.second.first);
   if (c->arena) cudaFree(c->arena);
   if (c->status) cudaFree(c->status);
+  if (c->comm_stream) cudaStreamSynchronize(c->comm_stream);
   if (c->comm && c->nccl.comm_destroy) c->nccl.comm_destroy(c->comm);
+  if (c->comm_stream) {
+    cudaStreamDestroy(c->comm_stream);
+    cudaEventDestroy(c->ev_grads);
+    cudaEventDestroy(c->ev_reduced);
+  }
   if (c->xfer_in) {
     cudaStreamSynchronize(c->xfer_in);
     cudaStreamSynchronize(c->xfer_out);
@@ -442,6 +505,32 @@ int nn_buffer_read(int h, float *dst, long long offset, long long count) {
                            g_ctx->stream));
   CUDA_TRY(cudaStreamSynchronize(g_ctx->stream));
   return NN_OK;
+}
+
+// COpenCL::BufferWrite / BufferRead with the reference's meaning of their two offsets: the
+// device position is a BYTE offset into the buffer (CLBufferWrite's buffer_offset), the host
+// position an element index into the caller's array (data_offset).  Floats only, so the byte
+// offset must be a multiple of 4.
+static int ex_range(long long byte_offset, long long start, long long *elem, const char *who) {
+  if (byte_offset < 0 || (byte_offset & 3))
+    return set_err(NN_ERR_ARG, std::string(who) + ": buffer byte offset must be a non-negative multiple of 4");
+  if (start < 0) return set_err(NN_ERR_ARG, std::string(who) + ": negative array start");
+  *elem = byte_offset / 4;
+  return NN_OK;
+}
+
+int nn_buffer_write_ex(int h, const float *data, long long byte_offset, long long start, long long count) {
+  long long elem = 0;
+  int rc = ex_range(byte_offset, start, &elem, "nn_buffer_write_ex");
+  if (rc) return rc;
+  return nn_buffer_write(h, data ? data + start : nullptr, elem, count);
+}
+
+int nn_buffer_read_ex(int h, float *data, long long byte_offset, long long start, long long count) {
+  long long elem = 0;
+  int rc = ex_range(byte_offset, start, &elem, "nn_buffer_read_ex");
+  if (rc) return rc;
+  return nn_buffer_read(h, data ? data + start : nullptr, elem, count);
 }
 
 // Transfer streams and events of the overlapped copies (once per context).
@@ -805,6 +894,11 @@ int nn_dp_init(int rank, int world, const unsigned char *id128) {
   if (rc) return rc;
   NcclUid uid;
   std::memcpy(uid.internal, id128, 128);
+  if (!g_ctx->comm_stream) {
+    CUDA_TRY(cudaStreamCreateWithFlags(&g_ctx->comm_stream, cudaStreamNonBlocking));
+    CUDA_TRY(cudaEventCreateWithFlags(&g_ctx->ev_grads, cudaEventDisableTiming));
+    CUDA_TRY(cudaEventCreateWithFlags(&g_ctx->ev_reduced, cudaEventDisableTiming));
+  }
   int r = g_ctx->nccl.comm_init_rank(&g_ctx->comm, world, uid, rank);
   if (r) {
     g_ctx->comm = nullptr;
@@ -819,6 +913,7 @@ int nn_dp_shutdown(void) {
   NEED_CTX();
   if (!g_ctx->comm) return NN_OK;
   cudaStreamSynchronize(g_ctx->stream);
+  if (g_ctx->comm_stream) cudaStreamSynchronize(g_ctx->comm_stream);
   g_ctx->nccl.comm_destroy(g_ctx->comm);
   g_ctx->comm = nullptr;
   g_ctx->world = 1;
@@ -869,6 +964,9 @@ int nn_dp_update_begin(void) {
     }
   }
   c->arena_used = 0;
+  c->arena_flushed = 0;
+  c->dp_pending = NN_OK;
+  c->dp_pending_msg.clear();
   c->deferred.clear();
   c->deferring = true;
   return NN_OK;
@@ -879,8 +977,17 @@ int nn_dp_update_end(void) {
   Context *c = g_ctx;
   if (!c->deferring) return set_err(NN_ERR_STATE, "no update region open");
   c->deferring = false;
-  int rc = allreduce_ptr(c->arena, c->arena_used, 1.f / (float)c->world);
+  if (c->dp_pending) {
+    c->deferred.clear();
+    return set_err(c->dp_pending, c->dp_pending_msg);
+  }
+  int rc = flush_bucket(c);
   if (rc) return rc;
+  if (c->comm && c->world > 1) {
+    // the applies read every bucket: the context stream waits for the last allreduce
+    CUDA_TRY(cudaEventRecord(c->ev_reduced, c->comm_stream));
+    CUDA_TRY(cudaStreamWaitEvent(c->stream, c->ev_reduced, 0));
+  }
   for (size_t i = 0; i < c->deferred.size(); ++i) {
     rc = run_deferred(c, c->deferred[i]);
     if (rc) return rc;

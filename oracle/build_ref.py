@@ -14,7 +14,8 @@ only to oracle/_ref/ (git-ignored).  When the reference checkout is absent
 (e.g. on a machine that only received the built files) the script exits
 without doing anything.
 
-Usage:  python oracle/build_ref.py [--reference DIR] [--force]
+Usage:  python oracle/build_ref.py --reference DIR [--force]
+        (or NN_REFERENCE_DIR=DIR python oracle/build_ref.py)
 """
 from __future__ import annotations
 
@@ -26,7 +27,6 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.path.join(HERE, "_ref")
-DEFAULT_REFERENCE = "/root/reference"
 CL_RELPATH = os.path.join("Experts", "NeuroNet_DNG", "NeuroNet.cl")
 
 # Every kernel of the hot path (the in-scope subset of NeuroNet.cl).
@@ -52,7 +52,7 @@ KERNELS = [
     "FQF_FractionGradient", "FQF_CosineGradientSRM", "FQF_DistributionTargetGradient",
     "FQF_MonotoneRearrange", "FQF_RearrangeGradient", "FQF_SRMForward", "FQF_SRMGradient",
     "SAC_AlphaLogProbs", "SAC_AlphaGradients", "SAC_OutputGradient", "SAC_CalcLogProbs",
-    "MHFlashAttention", "MHFlashAttentionGrad",
+    "MHFlashAttention", "MHFlashAttentionGrad", "FQF_Sample", "PatchCreate", "PatchHiddenGradient",
 ]
 
 
@@ -234,9 +234,12 @@ def build(reference: str, force: bool = False) -> str | None:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("NN_REFERENCE_DIR", DEFAULT_REFERENCE))
+    ap.add_argument("--reference", default=os.environ.get("NN_REFERENCE_DIR"),
+                    help="root of the EAPrognoz/NN_in_Trading checkout (or set NN_REFERENCE_DIR)")
     ap.add_argument("--force", action="store_true")
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("give --reference DIR or set NN_REFERENCE_DIR")
     lib = build(a.reference, a.force)
     print(lib or "reference checkout not found; nothing built")
     return 0

@@ -1584,6 +1584,102 @@ def MatMultGrad(matr1, matr1_gr, matr2, matr2_gr, result_gr, dimension, multvars
             matr2_gr[offset_matr2_gr + v * dim * cols:][:dim * cols] = nan0(s).reshape(-1)
 
 
+# ------------------------------------------------ masking and patch embedding
+def Dropout(inputs, map, out, dimension, gsize, lsize=None):
+    """NeuroNet.cl:1855-1884 as written: work-item t = 0 .. gsize[0]-1 loops k over
+    [4t, min(dimension, 4t + 4)) and uses element 4t + k, i.e. 8t + j for j < 4 with 4t + j <
+    dimension; out = 0 where IsNaNOrInf(map) or IsNaNOrInf(input) is 0, else IsNaNOrInf(inp * m).
+    Elements the reference would touch past the end of the arrays are left out."""
+    G = gsize[0]
+    lim = min(len(inputs), len(map), len(out))
+    t = np.arange(G)[:, None]
+    j = np.arange(4)[None, :]
+    e = (8 * t + j)[(4 * t + j) < dimension]
+    e = e[e < lim]
+    with _err():
+        m = nan0(map[e])
+        x = nan0(inputs[e])
+        out[e] = np.where((m == 0) | (x == 0), F32(0), nan0(x * m)).astype(F32)
+
+
+def PatchCreate(inputs, weights, outputs, inputs_total, window_in, step, activation, gsize, lsize=None):
+    """NeuroNet.cl:5826-5860 over global (patches, window_out, variables): output (i*variables + v)
+    * window_out + w = fActivation(bias + sum_p x[(i*step + p)*variables + v] W[p]) over the p whose
+    input index is below inputs_total, W the row (window_in + 1)(v*window_out + w) (bias last); a NaN
+    sum becomes 0."""
+    P, WO, V = (tuple(gsize) + (1, 1))[:3]
+    with _err():
+        Wt = weights[:V * WO * (window_in + 1)].reshape(V, WO, window_in + 1)
+        for i in range(P):
+            for v in range(V):
+                idx = i * step * V + v + np.arange(window_in) * V
+                ok = idx < inputs_total
+                x = np.where(ok, inputs[np.minimum(idx, max(inputs_total - 1, 0))], F32(0)).astype(F32)
+                res = (Wt[v, :, window_in] + (Wt[v, :, :window_in] * x[None, :]).sum(axis=1, dtype=F32)).astype(F32)
+                res = np.where(np.isnan(res), F32(0), res).astype(F32)
+                outputs[(i * V + v) * WO:(i * V + v + 1) * WO] = f_activation(res, activation)
+
+
+def PatchHiddenGradient(inputs, inputs_gr, weights, outputs_gr, window_in, step, window_out, outputs_total,
+                        activation, gsize, lsize=None):
+    """NeuroNet.cl:5864-5911 over global (time, variables): input (i, v) collects
+    outputs_gr[(row*variables + v)*window_out + wo] * W[v][wo][w_start + (total-p-1)*step] over the
+    patches row = r_start + p below outputs_total, with the reference's w_start = i % step, r_start =
+    max((i - window_in + step) / step, 0) and total = min((i + step) / step, (window_in - w_start +
+    step - 1) / step) (C division, truncating toward zero), then Deactivation by the input."""
+    T, V = (tuple(gsize) + (1,))[:2]
+
+    def cdiv(a, b):
+        q = abs(a) // abs(b)
+        return q if (a >= 0) == (b > 0) else -q
+    with _err():
+        Wt = weights[:V * window_out * (window_in + 1)].reshape(V, window_out, window_in + 1)
+        for i in range(T):
+            w_start = i % step
+            r_start = max(cdiv(i - window_in + step, step), 0)
+            total = min(cdiv(i + step, step), cdiv(window_in - w_start + step - 1, step))
+            for v in range(V):
+                grad = F32(0)
+                for p in range(max(total, 0)):
+                    row = r_start + p
+                    if row >= outputs_total:
+                        break
+                    g = outputs_gr[(row * V + v) * window_out:(row * V + v + 1) * window_out]
+                    wcol = Wt[v, :, w_start + (total - p - 1) * step]
+                    grad = F32(grad + (g * wcol).sum(dtype=F32))
+                inputs_gr[i * V + v] = deactivation(grad, inputs[i * V + v], activation)
+
+
+def FQF_Sample(quantiles, probabilities, random, result, gsize, lsize=None):
+    """NeuroNet.cl:2722-2799, one work-group per task (local size = quants): C = the Hillis-Steele
+    inclusive scan of max(IsNaNOrInf(p), 0) (Temp[i] += Temp[i - d] for d = 1, 2, 4, ... below the
+    row length, each step reading the previous step's values); 0 when IsNaNOrInf(C_last) <= 1e-6,
+    else the quantile of the smallest i with C_i >= u*C_last and (i == 0 or C_{i-1} < u*C_last), the
+    last one when its C is below u*C_last, u = clamp(IsNaNOrInf(random, 0.5), 0, 1)."""
+    T = lsize[0] if lsize is not None else gsize[0]
+    R = (tuple(gsize) + (1,))[1]
+    with _err():
+        for r in range(R):
+            c = np.maximum(nan0(probabilities[r * T:(r + 1) * T]), F32(0)).astype(F32)
+            d = 1
+            while d < T:
+                c = np.concatenate([c[:d], (c[d:] + c[:-d]).astype(F32)]).astype(F32)
+                d <<= 1
+            mass = nan0(c[T - 1])
+            if mass <= F32(1e-6):
+                result[r] = 0
+                continue
+            u = F32(min(max(float(nan0(random[r], 0.5)), 0.0), 1.0))
+            thr = F32(u * mass)
+            prev = np.concatenate([[F32(0)], c[:-1]]).astype(F32)
+            sel = (c >= thr) & ((np.arange(T) == 0) | (prev < thr))
+            if c[T - 1] < thr:
+                sel[T - 1] = True
+            hit = np.nonzero(sel)[0]
+            if len(hit):
+                result[r] = nan0(quantiles[r * T + hit[0]])
+
+
 # --------------------------------------------------------- soft actor-critic
 # The library's squashed-Gaussian SAC kernels (no reference counterpart; the reference's SAC agents
 # use quantile heads).  A launch covers gsize[0] * batch samples; here gsize[0] is the sample count.

@@ -82,6 +82,9 @@ def materialise(case: Case, seed: int) -> list:
             T = int(a.scale)
             v = np.concatenate([rng.permutation(T) for _ in range(n // T)]).astype(np.float64)
             v[rng.uniform(0.0, 1.0, n) < 0.05] = np.nan
+        elif a.init == "dropmask":
+            # a dropout map as CNeuronDropoutOCL draws it: 0 with probability 0.3, else 1 / 0.7
+            v = np.where(rng.uniform(0.0, 1.0, n) < 0.3, 0.0, 1.0 / 0.7)
         elif a.init.startswith("act:"):
             # a plausible activation output for the given activation (used by Deactivation inputs)
             act = int(a.init[4:])
@@ -460,10 +463,45 @@ def _flash_cases():
     return cases
 
 
+def _patch_cases():
+    """Dropout (NeuroNet.cl:1855-1884), PatchCreate / PatchHiddenGradient (NeuroNet.cl:5826-5911) and
+    FQF_Sample (NeuroNet.cl:2722-2799)."""
+    cases = []
+    # Dropout with the host's global size (dimension + 3) / 4 (NeuroNet_Core.mqh:19168): its
+    # work-items reach about twice the dimension, so the arrays are sized to hold that reach
+    for D, init in [(1, "normal"), (3, "normal"), (4, "normal"), (7, "normal"), (63, "normal"), (64, "normal"),
+                    (65, "normal"), (100, "nanmix"), (257, "normal")]:
+        n = 2 * D + 8
+        cases.append(Case(f"Dropout/{D}-{init}", "Dropout", [A(n, init), A(n, "dropmask"), A(n, "zeros"), D],
+                          ((D + 3) // 4,)))
+    # (time, variables, window_in, step, window_out, activation): CNeuronPatching shapes, patches
+    # past the end of the series, windows wider than the step and narrower
+    for T, V, win, step, WO, act in [(32, 3, 8, 4, 5, NONE), (30, 3, 8, 4, 5, TANH), (64, 1, 16, 8, 12, GELU),
+                                     (17, 2, 4, 4, 3, SIGMOID), (20, 4, 3, 5, 7, LRELU), (9, 2, 9, 1, 4, NONE)]:
+        P = (T - win) // step + 1 if T >= win else 1
+        if act != NONE or T == 30:
+            P += 1  # one patch that runs past the end of the series
+        nw = V * WO * (win + 1)
+        cases.append(Case(f"PatchCreate/{T}x{V}-w{win}-s{step}-o{WO}-a{act}", "PatchCreate",
+                          [A(T * V), A(nw, "uniform", 1 / np.sqrt(win + 1)), A(P * V * WO, "zeros"), T * V, win,
+                           step, act], (P, WO, V)))
+        cases.append(Case(f"PatchHiddenGradient/{T}x{V}-w{win}-s{step}-o{WO}-a{act}", "PatchHiddenGradient",
+                          [A(T * V, f"act:{act}"), A(T * V, "zeros"), A(nw, "uniform", 1 / np.sqrt(win + 1)),
+                           A(P * V * WO, "grad"), win, step, WO, P, act], (T, V)))
+    # FQF_Sample: rows of 1-64 quants, zero-mass rows, NaN probabilities and random values
+    for T, R, pinit, rinit in [(1, 3, "unit", "unit"), (3, 5, "unit", "unit"), (8, 4, "unit", "unit"),
+                               (32, 6, "unit", "unit"), (33, 3, "unit", "unit"), (48, 2, "pos", "unit"),
+                               (64, 5, "unit", "unit"), (16, 3, "zeros", "unit"), (32, 6, "nanmix", "nanmix"),
+                               (64, 4, "coarse", "unit")]:
+        cases.append(Case(f"FQF_Sample/{T}x{R}-{pinit}-{rinit}", "FQF_Sample",
+                          [A(R * T), A(R * T, pinit), A(R, rinit), A(R, "zeros")], (T, R), (T, 1)))
+    return cases
+
+
 def all_cases() -> list[Case]:
     return (_dense_cases() + _conv_cases() + _attention_cases() + _norm_cases() + _batchnorm_cases() + _lstm_cases()
             + _attention2_cases() + _concat_cases() + _adam_mini_cases() + _matmul_cases()
-            + _quantile_head_cases() + _flash_cases())
+            + _quantile_head_cases() + _flash_cases() + _patch_cases())
 
 
 def prepare_inputs(case: Case, seed: int) -> list:

@@ -6,7 +6,7 @@ oracle/build_ref.py from the reference checkout) and stores, per case, the
 inputs and every array argument after the launch.  Run from the repository
 root:
 
-    python oracle/build_ref.py && python tests/golden/make_golden.py
+    python oracle/build_ref.py --reference <checkout> && python tests/golden/make_golden.py
 """
 from __future__ import annotations
 

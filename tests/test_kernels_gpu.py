@@ -81,6 +81,7 @@ PER_SAMPLE_KERNELS = {
     "SAC_AlphaLogProbs": [0, 1, 2, 3, 4, 5], "SAC_AlphaGradients": [0, 1, 2, 3],
     "SAC_OutputGradient": [0, 1, 2, 3, 4, 5], "SAC_CalcLogProbs": [0, 1, 2, 3, 4],
     "MHFlashAttention": [0, 1, 2, 3], "MHFlashAttentionGrad": [0, 1, 2, 3, 4, 5, 6],
+    "PatchCreate": [0, 2], "PatchHiddenGradient": [0, 1, 3], "FQF_Sample": [0, 1, 2, 3],
 }
 BATCH_CASES = [c for c in CASES if c.kernel in PER_SAMPLE_KERNELS]
 

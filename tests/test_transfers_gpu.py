@@ -87,3 +87,35 @@ def test_double_buffered_pipeline(ctx):
             tickets[i + 2] = enqueue(i + 2)
     for h in stage_in + stage_out + [bi, bo]:
         ctx.free(h)
+
+
+def test_buffer_write_ex_and_read_ex_take_a_device_byte_offset_and_a_host_start(ctx):
+    """COpenCLMy::BufferWrite(buffer, data, offset, start, count) semantics: `offset` is a byte
+    position in the device buffer, `start` an element index into the host array."""
+    import ctypes
+    lib = ctx.lib
+    n = 64
+    h = ctx.buffer(n)
+    ctx.fill(h, -1.0, n)
+    host = np.arange(100, dtype=np.float32) + 0.5
+    p = host.ctypes.data_as(ctypes.c_void_p)
+    # host elements 10..19 -> device floats 5..14 (byte offset 20)
+    ctx._check(lib.nn_buffer_write_ex(h, p, 20, 10, 10))
+    dev = ctx.read(h, n)
+    want = np.full(n, -1.0, np.float32)
+    want[5:15] = host[10:20]
+    np.testing.assert_array_equal(dev, want)
+    # device floats 7..12 (byte offset 28) -> host elements 40..45, the rest of the array untouched
+    out = np.full(50, 7.0, np.float32)
+    ctx._check(lib.nn_buffer_read_ex(h, out.ctypes.data_as(ctypes.c_void_p), 28, 40, 6))
+    expect = np.full(50, 7.0, np.float32)
+    expect[40:46] = want[7:13]
+    np.testing.assert_array_equal(out, expect)
+    # the whole-buffer call CBufferFloat::BufferRead issues: (0, 0, total)
+    ctx._check(lib.nn_buffer_read_ex(h, out.ctypes.data_as(ctypes.c_void_p), 0, 0, 50))
+    np.testing.assert_array_equal(out, want[:50])
+    # refused: byte offset not a multiple of 4, negative start, range past the buffer
+    assert lib.nn_buffer_write_ex(h, p, 2, 0, 1) == -2
+    assert lib.nn_buffer_write_ex(h, p, 0, -1, 1) == -2
+    assert lib.nn_buffer_read_ex(h, out.ctypes.data_as(ctypes.c_void_p), 4 * 60, 0, 5) == -5
+    ctx.free(h)
