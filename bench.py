@@ -259,6 +259,7 @@ class MLMHWorkload(Workload):
     key = "mlmh_encoder"
     name = "mlmh_encoder_4x120x64_h8k32_ff256"
     default_batch = 256
+    default_steps = 400  # about 1.2 s timed
 
     def __init__(self, batch):
         super().__init__(batch)
@@ -301,7 +302,7 @@ class DenseWorkload(Workload):
     key = "dense_mlp"
     name = "dense_mlp_240_500tanh_500sigmoid_3"
     default_batch = 1
-    default_steps = 1000
+    default_steps = 15000  # 15 runs of the 1000-step online configuration
 
     def __init__(self, batch):
         super().__init__(batch)
@@ -346,7 +347,7 @@ class LSTMWorkload(Workload):
     key = "lstm_stack"
     name = "lstm_stack_in64_h256_x2_seq240"
     default_batch = 1024
-    default_steps = 240
+    default_steps = 4800  # 20 windows of 240 bars
 
     def __init__(self, batch):
         super().__init__(batch)
@@ -405,7 +406,7 @@ class PatchWorkload(Workload):
     key = "patchtst"
     name = "patchtst_32ch_512bars_p16s8_e128_h8k16_x3_ff512_h96"
     default_batch = 512
-    default_steps = 10
+    default_steps = 15
     recordable = False
 
     def __init__(self, batch):
@@ -459,7 +460,7 @@ class SACWorkload(Workload):
     key = "sac"
     name = "sac_actor240x512x512x12_2critics246x512x512x1_tau0.005"
     default_batch = 4096
-    default_steps = 30
+    default_steps = 700
 
     def __init__(self, batch):
         super().__init__(batch)
@@ -595,7 +596,7 @@ def run_ours(args, rank, world, local_rank):
     stage_in = [[ctx.buffer(n) for n in sizes] for _ in range(2)]
     stage_out = [ctx.buffer(n_y) for _ in range(2)]
     lib = ctx.lib
-    e2e_steps = max(3, args.steps // 2)
+    e2e_steps = max(3, args.steps)
 
     def enqueue(i):
         half = i % 2

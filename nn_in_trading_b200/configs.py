@@ -14,6 +14,8 @@
                 trains recurrent layers bar by bar, h(t-1) enters as an input); a per-series 1x1
                 conv head 256 -> 64 predicts the next step's 64 log-returns (MSE).  Inputs are
                 N(0, 0.01) log-returns cumulated along the window.
+  quantile_head A state layer feeding a CNeuronFQF or CNeuronSoftActorCritic quantile head
+                (actions x quantiles), MSE of the head's output against N(0,1) targets.
   patchtst      RevIN-style: BatchNorm over 32 channels x 512 bars, Conv1D patching (window 16,
                 step 8, 63 patches, embed 128, per-channel weights), 3 attention layers over the
                 63 patches of every channel (8 heads x key 16, FF 512), a shared conv head
@@ -217,3 +219,56 @@ def build_patch(ctx: Context, spec: PatchSpec, batch: int, weights=None, dp: boo
     head.set_conv_weights(w["head"])
     denorm = RevINDenormLayer(ctx, C * spec.horizon, norm, batch)
     return Net(ctx, [inp, norm, conv, enc, head, denorm], dp=dp)
+
+
+# ------------------------------------------------------------------ quantile heads
+@dataclass
+class QuantileHeadSpec:
+    """A state layer of `inputs` neurons feeding a CNeuronFQF (sac=False) or CNeuronSoftActorCritic
+    (sac=True) head of `actions` x `quantiles`, the shape the reference's distributional agents use."""
+    inputs: int = 256
+    actions: int = 6
+    quantiles: int = 32
+    sac: bool = False
+    seed: int = 6
+
+
+def quantile_head_weights(spec: QuantileHeadSpec) -> dict:
+    """Uniform +-1/sqrt(fan_in + 1) for every weight matrix of the head (state layer toward the
+    fraction proposal, cosine embedding, both quantile layers, and the SAC head's alphas)."""
+    rng = np.random.default_rng(spec.seed)
+    A, Q, N = spec.actions, spec.quantiles, spec.inputs
+    AQ = A * Q
+
+    def u(n_out, n_in):
+        k = 1.0 / np.sqrt(n_in + 1)
+        return rng.uniform(-k, k, n_out * (n_in + 1)).astype(F32)
+    w = {"state": u(AQ, N), "cosine": u(N, AQ), "q0": u(4 * AQ, N), "q1": u(AQ, 4 * AQ)}
+    if spec.sac:
+        w["alphas"] = u(A, N + AQ)
+    return w
+
+
+def quantile_head_data(spec: QuantileHeadSpec, steps: int, batch: int = 1, seed: int | None = None):
+    """States N(0,1), targets N(0,1) per action, and the per-action uniforms of the SAC head."""
+    rng = np.random.default_rng(spec.seed + 1 if seed is None else seed)
+    x = rng.standard_normal((steps, batch, spec.inputs)).astype(F32)
+    t = rng.standard_normal((steps, batch, spec.actions)).astype(F32)
+    u = rng.uniform(0.0, 1.0, (steps, batch, spec.actions)).astype(F32)
+    return x, t, u
+
+
+def build_quantile_head(ctx: Context, spec: QuantileHeadSpec, batch: int = 1, weights=None) -> Net:
+    from .layers import FQFLayer, SoftActorCriticLayer
+    w = weights if weights is not None else quantile_head_weights(spec)
+    AQ = spec.actions * spec.quantiles
+    state = DenseLayer(ctx, spec.inputs, NONE, ADAM, batch, AQ)
+    cls = SoftActorCriticLayer if spec.sac else FQFLayer
+    head = cls(ctx, spec.actions, spec.quantiles, spec.inputs, ADAM, batch)
+    state.set_weights(w["state"])
+    head.cosine.set_weights(w["cosine"])
+    head.q0.set_weights(w["q0"])
+    head.q1.set_weights(w["q1"])
+    if spec.sac:
+        head.alphas.set_conc_weights(w["alphas"])
+    return Net(ctx, [state, head])

@@ -16,7 +16,7 @@ import math
 
 import numpy as np
 
-from .api import ADAM, ADAM_MINI, GELU, NONE, SGD, Context, Kernel
+from .api import ADAM, ADAM_MINI, GELU, LRELU, NONE, SGD, SIGMOID, Context, Kernel
 
 LR = 3.0e-4       # NeuroNet_Definitions.mqh:38
 MOMENTUM = 0.9    # NeuroNet_Definitions.mqh:40
@@ -602,3 +602,152 @@ class LSTMLayer(Layer):
         total = (self.inputs + self.H * self.variables) // self.variables + 1
         k = self.kernel("LSTM_UpdateWeightsAdam").args(self.lstm_w, self.lstm_wg, self.lstm_m, self.lstm_v, LR, B1, B2)
         return [Op(k, (total, self.H))]
+
+
+class FQFLayer(Layer):
+    """CNeuronFQF (NeuroNet_Declarations.mqh:3490-3560, NeuroNet_AgentsRL.mqh:32-248): a fully
+    parameterised quantile head over `actions` x `quantiles`.  The previous layer's weights
+    ([actions*quantiles][inputs+1]) feed the fraction proposal; its softmax gives the quantile
+    fractions, their cosine embedding (FQF_Cosine, then a dense LReLU layer of `inputs`) multiplies the
+    state element-wise (the reference's ElementMult, i.e. the Dropout kernel), two dense layers
+    (4*actions*quantiles LReLU, actions*quantiles) give the quantile values and FQF_Output their
+    fraction-weighted sum per action.  `inputs` must equal the previous layer's neurons."""
+
+    def __init__(self, ctx, actions, quantiles, inputs, optimization=ADAM, batch=1, outputs=0, activation=NONE):
+        super().__init__(ctx, actions, activation, optimization, batch, outputs)
+        A, Q, N = int(actions), int(quantiles), int(inputs)
+        self.A, self.Q, self.N = A, Q, N
+        AQ = A * Q
+        self.fraction = DenseLayer(ctx, AQ, NONE, optimization, batch)
+        self.softmax = SoftMaxLayer(ctx, AQ, heads=A, batch=batch)
+        self.cosine = Layer(ctx, AQ, NONE, optimization, batch, outputs=N)
+        self.cos_emb = DenseLayer(ctx, N, LRELU, optimization, batch)
+        self.q0 = Layer(ctx, N, NONE, optimization, batch, outputs=4 * AQ)
+        self.q1 = DenseLayer(ctx, 4 * AQ, LRELU, optimization, batch, outputs=AQ)
+        self.q2 = DenseLayer(ctx, AQ, NONE, optimization, batch)
+
+    def sublayers(self) -> dict:
+        """The inner layers by the reference's member names (weights live on cosine, q0 and q1)."""
+        return {"cFraction": self.fraction, "cSoftMax": self.softmax, "cCosine": self.cosine,
+                "cCosineEmbeding": self.cos_emb, "cQuantile0": self.q0, "cQuantile1": self.q1, "cQuantile2": self.q2}
+
+    def forward_ops(self, prev: Layer) -> list[Op]:
+        """CNeuronFQF::feedForward, NeuroNet_AgentsRL.mqh:96-151."""
+        if prev.neurons != self.N:
+            raise ValueError(f"FQF layer built for {self.N} inputs, previous layer has {prev.neurons}")
+        A, Q, N = self.A, self.Q, self.N
+        ops = self.fraction.forward_ops(prev)
+        ops += self.softmax.forward_ops(self.fraction)
+        kc = self.kernel("FQF_Cosine").args(self.softmax.output, self.cosine.output)
+        ops.append(Op(kc, (Q, A)))
+        ops += self.cos_emb.forward_ops(self.cosine)
+        # ElementMult (NeuroNet_Core.mqh:19163-19176): the Dropout kernel over the embedding's size
+        kd = self.kernel("Dropout").args(prev.output, self.cos_emb.output, self.q0.output, N)
+        ops.append(Op(kd, ((N + 3) // 4,)))
+        ops += self.q1.forward_ops(self.q0)
+        ops += self.q2.forward_ops(self.q1)
+        ko = self.kernel("FQF_Output").args(self.q2.output, self.softmax.output, self.output, Q)
+        ops.append(Op(ko, (A,)))
+        return ops
+
+    def _output_gradient_op(self) -> Op:
+        k = self.kernel("FQF_OutputGradient").args(self.q2.output, self.softmax.output, self.gradient,
+                                                   self.q2.gradient, self.softmax.gradient)
+        return Op(k, (self.Q, self.A))
+
+    def input_gradient_ops(self, prev: Layer) -> list[Op]:
+        """CNeuronFQF::calcInputGradients, NeuroNet_AgentsRL.mqh:156-224: the state receives only the
+        quantile branch's gradient (FQF_QuantileGradient); the fraction branch stops at cFraction."""
+        ops = [self._output_gradient_op()]
+        ops += self.q1.hidden_gradient_ops(self.q2)
+        ops += self.q0.hidden_gradient_ops(self.q1)
+        kq = self.kernel("FQF_QuantileGradient").args(prev.output, self.cos_emb.output, self.q0.gradient,
+                                                      prev.gradient, self.cos_emb.gradient)
+        ops.append(Op(kq, (self.N, 1)))
+        ops += self.cosine.hidden_gradient_ops(self.cos_emb)
+        kc = self.kernel("FQF_CosineGradient").args(self.softmax.output, self.cosine.gradient, self.softmax.gradient)
+        ops.append(Op(kc, (self.Q, self.A)))
+        ops += self.softmax.input_gradient_ops(self.fraction)
+        return ops
+
+    def update_ops(self, prev: Layer) -> list[Op]:
+        """CNeuronFQF::updateInputWeights, NeuroNet_AgentsRL.mqh:230-245: the fraction proposal (the
+        previous layer's weights), the cosine embedding and the two quantile layers, in that order, each
+        with its own Adam step counter."""
+        ops = self.fraction.update_ops(prev)
+        ops += self.cos_emb.update_ops(self.cosine)
+        ops += self.q1.update_ops(self.q0)
+        ops += self.q2.update_ops(self.q1)
+        return ops
+
+    def soft_update_ops(self, source: "FQFLayer", tau: float, adam: bool | None = None) -> list[Op]:
+        """CNeuronFQF::WeightsUpdate, NeuroNet_AgentsRL.mqh:1985-2010: its own weights, then every inner
+        layer's (only cosine, q0 and q1 hold weights)."""
+        ops = super().soft_update_ops(source, tau, adam)
+        for name in ("cosine", "q0", "q1"):
+            ops += getattr(self, name).soft_update_ops(getattr(source, name), tau, adam)
+        return ops
+
+
+class SoftActorCriticLayer(FQFLayer):
+    """CNeuronSoftActorCritic (NeuroNet_AgentsRL.mqh:1655-1990): the FQF head whose output is an
+    action sampled from each action's quantile distribution (SAC_AlphaLogProbs, with one host-drawn
+    uniform per action in `random`, set_random), an entropy temperature per action from a concatenate
+    layer over [cQuantile0, cQuantile2] (sigmoid), and their log-probabilities.
+
+    One deviation: the reference's calcInputGradients ends with cSoftMax.CalcHiddenGradients(cFraction)
+    (NeuroNet_AgentsRL.mqh:1981), which binds cSoftMax's weights; cSoftMax has none (created with no
+    outputs), so that call fails and the fraction layer gets no gradient.  This layer ends as
+    CNeuronFQF does, with the softmax gradient into cFraction."""
+
+    def __init__(self, ctx, actions, quantiles, inputs, optimization=ADAM, batch=1, outputs=0, activation=NONE):
+        super().__init__(ctx, actions, quantiles, inputs, optimization, batch, outputs, activation)
+        AQ = self.A * self.Q
+        self.alphas = ConcatLayer(ctx, self.A, self.N, AQ, SIGMOID, optimization, batch)
+        # cAlphas reads cQuantile2's output as its second input and writes its gradient there
+        ctx.free(self.alphas.second)
+        ctx.free(self.alphas.second_grad)
+        self.alphas.second, self.alphas.second_grad = self.q2.output, self.q2.gradient
+        self.log_probs = ctx.buffer(self.A * batch)
+        self.random = ctx.buffer(self.A * batch)
+
+    def sublayers(self) -> dict:
+        d = super().sublayers()
+        d["cAlphas"] = self.alphas
+        return d
+
+    def set_random(self, u: np.ndarray) -> None:
+        """The uniforms the host draws per action before each forward pass (MathRand()/32767)."""
+        self.ctx.write(self.random, np.asarray(u, np.float32))
+
+    def forward_ops(self, prev: Layer) -> list[Op]:
+        """CNeuronSoftActorCritic::feedForward, NeuroNet_AgentsRL.mqh:1688-1725."""
+        ops = super().forward_ops(prev)
+        ops += self.alphas.forward_ops(self.q0)
+        k = self.kernel("SAC_AlphaLogProbs").args(self.output, self.q2.output, self.softmax.output,
+                                                  self.alphas.output, self.log_probs, self.random, self.Q,
+                                                  self.activation)
+        # FQF_Output has already written the output; SAC_AlphaLogProbs overwrites it with the sample
+        ops.append(Op(k, (self.A,)))
+        return ops
+
+    def _output_gradient_op(self) -> Op:
+        k = self.kernel("SAC_OutputGradient").args(self.q2.output, self.softmax.output, self.gradient,
+                                                   self.q2.gradient, self.softmax.gradient, self.output, self.Q,
+                                                   self.activation)
+        return Op(k, (self.A,))
+
+    def alpha_gradient_ops(self, grad_layer: Layer) -> list[Op]:
+        """CNeuronSoftActorCritic::calcAlphaGradients (NeuroNet_AgentsRL.mqh:1730-1750), as CNet::
+        AlphasGradient calls it with another network's last layer: SAC_AlphaGradients from that layer's
+        gradient, then the concatenate layer's input gradients into cQuantile0 and cQuantile2."""
+        k = self.kernel("SAC_AlphaGradients").args(self.alphas.output, grad_layer.gradient, self.log_probs,
+                                                   self.alphas.gradient, SIGMOID)
+        return [Op(k, (self.A,))] + self.alphas.input_gradient_ops(self.q0)
+
+    def update_ops(self, prev: Layer) -> list[Op]:
+        """CNeuronSoftActorCritic::updateInputWeights, NeuroNet_AgentsRL.mqh:1755-1762."""
+        return super().update_ops(prev) + self.alphas.update_ops(self.q0)
+
+    def soft_update_ops(self, source: "SoftActorCriticLayer", tau: float, adam: bool | None = None) -> list[Op]:
+        return super().soft_update_ops(source, tau, adam) + self.alphas.soft_update_ops(source.alphas, tau, adam)

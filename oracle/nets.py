@@ -37,10 +37,25 @@ class RefBackend:
     def __getattr__(self, name):
         if name not in self.ref.sig:
             raise AttributeError(name)
+        if name == "Dropout":
+            return self._dropout
 
         def call(*args, gsize, lsize=None):
             self.ref.launch(name, gsize, lsize, list(args))
         return call
+
+    def _dropout(self, inputs, map, out, dimension, gsize, lsize=None):
+        """Dropout's work-items reach about twice the dimension past its arrays
+        (NeuroNet.cl:1855-1884): run the reference kernel on zero-padded copies that hold the reach
+        and keep what lands inside the real arrays."""
+        reach = 8 * int(gsize[0]) + 8
+        pads = []
+        for a in (inputs, map, out):
+            p = np.zeros(max(reach, a.size), F32)
+            p[:a.size] = a.reshape(-1)
+            pads.append(p)
+        self.ref.launch("Dropout", gsize, lsize, pads + [dimension])
+        out.reshape(-1)[...] = pads[2][:out.size]
 
 
 BACKEND = K  # numpy restatement by default
@@ -485,6 +500,110 @@ class OConcat(ODense):
                             self.in2, self.next_lt(), B1, B2, n_out, n_col)
 
 
+class OFQF(OLayer):
+    """CNeuronFQF (NeuroNet_AgentsRL.mqh:32-248) over the oracle kernels: fraction proposal from the
+    previous layer's weights, softmax per action, cosine embedding (FQF_Cosine + dense LReLU),
+    ElementMult with the state (the Dropout kernel), quantile layers 4AQ (LReLU) and AQ, FQF_Output.
+    Inner layers are ODense; the weights live on cosine, q0 and q1."""
+
+    def __init__(self, actions, quantiles, inputs, batch=1, outputs=0, activation=K.NONE):
+        super().__init__(actions, activation, batch)
+        A, Q, N = actions, quantiles, inputs
+        self.A, self.Q, self.N, self.outputs = A, Q, N, outputs
+        AQ = A * Q
+        if outputs:
+            n = outputs * (actions + 1)
+            self.weights, self.m, self.v = np.zeros(n, F32), np.zeros(n, F32), np.zeros(n, F32)
+        self.fraction = ODense(AQ, K.NONE, batch)
+        self.softmax = ODense(AQ, K.NONE, batch)
+        self.cosine = ODense(AQ, K.NONE, batch, outputs=N)
+        self.cos_emb = ODense(N, K.LRELU, batch)
+        self.q0 = ODense(N, K.NONE, batch, outputs=4 * AQ)
+        self.q1 = ODense(4 * AQ, K.LRELU, batch, outputs=AQ)
+        self.q2 = ODense(AQ, K.NONE, batch)
+
+    def forward(self, prev):
+        A, Q, N = self.A, self.Q, self.N
+        self.fraction.forward(prev)
+        for b in range(self.batch):
+            BACKEND.SoftMax_FeedForward(self.fraction.output[b], self.softmax.output[b], gsize=(Q, A), lsize=(Q, 1))
+            BACKEND.FQF_Cosine(self.softmax.output[b], self.cosine.output[b], gsize=(Q, A))
+        self.cos_emb.forward(self.cosine)
+        for b in range(self.batch):
+            BACKEND.Dropout(prev.output[b], self.cos_emb.output[b], self.q0.output[b], N, gsize=((N + 3) // 4,))
+        self.q1.forward(self.q0)
+        self.q2.forward(self.q1)
+        for b in range(self.batch):
+            BACKEND.FQF_Output(self.q2.output[b], self.softmax.output[b], self.output[b], Q, gsize=(A,))
+
+    def _output_gradient(self):
+        for b in range(self.batch):
+            BACKEND.FQF_OutputGradient(self.q2.output[b], self.softmax.output[b], self.gradient[b],
+                                       self.q2.gradient[b], self.softmax.gradient[b], gsize=(self.Q, self.A))
+
+    def input_gradient(self, prev):
+        """CNeuronFQF::calcInputGradients, NeuroNet_AgentsRL.mqh:156-224."""
+        A, Q, N = self.A, self.Q, self.N
+        self._output_gradient()
+        self.q1.hidden_gradient(self.q2)
+        self.q0.hidden_gradient(self.q1)
+        for b in range(self.batch):
+            BACKEND.FQF_QuantileGradient(prev.output[b], self.cos_emb.output[b], self.q0.gradient[b],
+                                         prev.gradient[b], self.cos_emb.gradient[b], gsize=(N, 1))
+        self.cosine.hidden_gradient(self.cos_emb)
+        for b in range(self.batch):
+            BACKEND.FQF_CosineGradient(self.softmax.output[b], self.cosine.gradient[b], self.softmax.gradient[b],
+                                       gsize=(Q, A))
+            BACKEND.SoftMax_HiddenGradient(self.softmax.output[b], self.softmax.gradient[b],
+                                           self.fraction.gradient[b], gsize=(Q, A), lsize=(Q, 1))
+
+    def update(self, prev):
+        """CNeuronFQF::updateInputWeights, NeuroNet_AgentsRL.mqh:230-245."""
+        self.fraction.update(prev)
+        self.cos_emb.update(self.cosine)
+        self.q1.update(self.q0)
+        self.q2.update(self.q1)
+
+
+class OSoftActorCritic(OFQF):
+    """CNeuronSoftActorCritic (NeuroNet_AgentsRL.mqh:1655-1990): the FQF head, SAC_AlphaLogProbs
+    sampling with `random`, alphas from an OConcat over [q0, q2] (sigmoid).  Its input gradient ends
+    as CNeuronFQF's does (the reference's last call fails for lack of weights on cSoftMax)."""
+
+    def __init__(self, actions, quantiles, inputs, batch=1, outputs=0, activation=K.NONE):
+        super().__init__(actions, quantiles, inputs, batch, outputs, activation)
+        self.alphas = OConcat(actions, inputs, actions * quantiles, K.SIGMOID, batch)
+        self.alphas.second = self.q2.output
+        self.alphas.second_grad = self.q2.gradient
+        self.log_probs = np.zeros((batch, actions), F32)
+        self.random = np.zeros((batch, actions), F32)
+
+    def forward(self, prev):
+        super().forward(prev)
+        self.alphas.forward(self.q0)
+        for b in range(self.batch):
+            BACKEND.SAC_AlphaLogProbs(self.output[b], self.q2.output[b], self.softmax.output[b],
+                                      self.alphas.output[b], self.log_probs[b], self.random[b], self.Q,
+                                      self.activation, gsize=(self.A,))
+
+    def _output_gradient(self):
+        for b in range(self.batch):
+            BACKEND.SAC_OutputGradient(self.q2.output[b], self.softmax.output[b], self.gradient[b],
+                                       self.q2.gradient[b], self.softmax.gradient[b], self.output[b], self.Q,
+                                       self.activation, gsize=(self.A,))
+
+    def alpha_gradient(self, grad_layer):
+        """calcAlphaGradients, NeuroNet_AgentsRL.mqh:1730-1750."""
+        for b in range(self.batch):
+            BACKEND.SAC_AlphaGradients(self.alphas.output[b], grad_layer.gradient[b], self.log_probs[b],
+                                       self.alphas.gradient[b], K.SIGMOID, gsize=(self.A,))
+        self.alphas.input_gradient(self.q0)
+
+    def update(self, prev):
+        super().update(prev)
+        self.alphas.update(self.q0)
+
+
 def soft_update(target: OLayer, source: OLayer, tau: float, adam: bool) -> None:
     """CNeuronBaseOCL::WeightsUpdate (NeuroNet_Core.mqh:20283-20370) and the CNeuronConcatenate
     override (NeuroNet_Misc.mqh:628-676): SoftUpdateAdam with the target's moments, or SoftUpdate."""
@@ -601,3 +720,18 @@ def _share(view: OLayer, src: OLayer) -> None:
     for name in ("weights", "m", "v", "conc_w", "conc_m", "conc_v"):
         if hasattr(src, name):
             setattr(view, name, getattr(src, name))
+
+
+def quantile_head_net(spec, weights, batch=1) -> ONet:
+    """The oracle twin of configs.build_quantile_head: a state layer and an FQF or SAC head."""
+    AQ = spec.actions * spec.quantiles
+    state = ODense(spec.inputs, K.NONE, batch, AQ)
+    cls = OSoftActorCritic if spec.sac else OFQF
+    head = cls(spec.actions, spec.quantiles, spec.inputs, batch)
+    state.weights[:] = weights["state"]
+    head.cosine.weights[:] = weights["cosine"]
+    head.q0.weights[:] = weights["q0"]
+    head.q1.weights[:] = weights["q1"]
+    if spec.sac:
+        head.alphas.conc_w[:] = weights["alphas"]
+    return ONet([state, head])

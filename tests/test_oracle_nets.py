@@ -120,3 +120,48 @@ def test_sac_step_numpy_oracle_matches_reference_kernels():
                 got[:] = ref
     finally:
         O.use_backend("numpy")
+
+
+def _head_arrays(net):
+    """(label, array) of every output, gradient and parameter of a quantile-head oracle net."""
+    state, head = net.layers
+    out = [("state gradient", state.gradient), ("state weights", state.weights), ("head output", head.output),
+           ("head gradient", head.gradient)]
+    subs = [("fraction", head.fraction), ("softmax", head.softmax), ("cosine", head.cosine),
+            ("cos_emb", head.cos_emb), ("q0", head.q0), ("q1", head.q1), ("q2", head.q2)]
+    if hasattr(head, "alphas"):
+        subs.append(("alphas", head.alphas))
+        out += [("alphas conc_w", head.alphas.conc_w), ("log_probs", head.log_probs)]
+    for name, layer in subs:
+        out += [(f"{name} output", layer.output), (f"{name} gradient", layer.gradient)]
+        if getattr(layer, "outputs", 0):
+            out += [(f"{name} weights", layer.weights), (f"{name} m", layer.m), (f"{name} v", layer.v)]
+    return out
+
+
+@pytest.mark.parametrize("sac", [False, True])
+def test_quantile_head_numpy_oracle_matches_reference_kernels(sac):
+    """CNeuronFQF / CNeuronSoftActorCritic sequencing (NeuroNet_AgentsRL.mqh:32-248, 1655-1990) over
+    the numpy kernels against the same sequencing over the reference's own kernels, 3 steps."""
+    spec = C.QuantileHeadSpec(inputs=24, actions=3, quantiles=8, sac=sac)
+    w = C.quantile_head_weights(spec)
+    xs, ts, us = C.quantile_head_data(spec, 3, 1)
+    nets = {}
+    try:
+        for kind in ("numpy", "reference"):
+            O.use_backend(kind)
+            nets[kind] = O.quantile_head_net(spec, w, 1)
+        for s in range(3):
+            for kind in ("numpy", "reference"):
+                O.use_backend(kind)
+                net = nets[kind]
+                if sac:
+                    net.layers[1].random[...] = us[s]
+                net.step(xs[s], ts[s])
+                if sac:
+                    net.layers[1].alpha_gradient(net.layers[1])
+            for (label, a), (_, b) in zip(_head_arrays(nets["numpy"]), _head_arrays(nets["reference"])):
+                check_close(f"step{s} {label}", a, b)
+                a[...] = b
+    finally:
+        O.use_backend("numpy")
