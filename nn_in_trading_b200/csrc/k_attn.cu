@@ -439,6 +439,70 @@ static int k_normalize(Launch &L) {
   return NN_OK;
 }
 
+// SumMatrix (zero row shifts, no numeric flags) immediately followed by Normalize of its output
+// (CNeuronBaseOCL::SumAndNormalize, NeuroNet_Core.mqh:17976-18075): one pass instead of two.  Each
+// warp takes one row, forms out = IsNaNOrInf((a + b) * mult) as SumMatrix does, then normalises the
+// row in registers exactly as normalize_rows_reg_kernel does, and writes it once.
+template <int EPL>
+__global__ void sum_normalize_rows_kernel(const float *__restrict__ a, const float *__restrict__ bm,
+                                          float *__restrict__ out, int rows, int dim, float mult) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const size_t base = (size_t)warp * dim;
+  float x[EPL];
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int i = lane + 32 * j;
+    x[j] = i < dim ? nan0((a[base + i] + bm[base + i]) * mult) : 0.f;
+    s += x[j];
+  }
+  const float mean = warp_sum(s) / (float)dim;
+  float m2 = 0.f;
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int i = lane + 32 * j;
+    const float c = x[j] - mean;
+    m2 += i < dim ? c * c : 0.f;
+  }
+  const float variance = warp_sum(m2) / (float)(dim - 1);
+  const bool scale = variance > 1.f;
+#pragma unroll
+  for (int j = 0; j < EPL; ++j) {
+    const int i = lane + 32 * j;
+    const float c = x[j] - mean;
+    if (i < dim) out[base + i] = nan0(scale ? c / variance : c);
+  }
+}
+
+// Whether a recorded SumMatrix and the Normalize after it can run as sum_normalize_rows_kernel: the
+// Normalize normalises exactly the rows the SumMatrix wrote (same buffer, row length and row count),
+// with no row shifts, no flags and rows of at most 128 floats.
+bool sum_normalize_fusable(const KernelInst &sm, const NDR &nsm, const KernelInst &nm, const NDR &nnm) {
+  if (sm.args[5].i != 0 || sm.args[6].i != 0 || sm.args[7].i != 0 || sm.args[9].i != 0) return false;
+  if (nm.args[0].i != sm.args[2].i || nm.args[1].i != sm.args[3].i) return false;
+  if (nm.batch != sm.batch || nnm.g[0] != nsm.g[0]) return false;
+  const int dim = sm.args[3].i;
+  return dim >= 2 && dim <= 128;
+}
+
+// The fused pair, launched for the SumMatrix execution `L` (its Normalize is skipped).
+int sum_normalize_launch(Launch &L) {
+  const int rows = (int)L.nd.g[0] * L.B, dim = L.i(3);
+  if (rows == 0) return NN_OK;
+  const size_t n = (size_t)rows * dim;
+  float *a = L.buf(0, n), *b = L.buf(1, n), *o = L.buf(2, n);
+  if (!a || !b || !o) return NN_ERR_BOUNDS;
+  const unsigned blocks = ceil_div((size_t)rows * 32, 256);
+  if (dim <= 64)
+    sum_normalize_rows_kernel<2><<<blocks, 256, 0, L.stream>>>(a, b, o, rows, dim, L.f(4));
+  else
+    sum_normalize_rows_kernel<4><<<blocks, 256, 0, L.stream>>>(a, b, o, rows, dim, L.f(4));
+  NN_CHECK_LAUNCH(L);
+  return NN_OK;
+}
+
 // ---------------------------------------------------------------- SoftMax
 // NeuroNet.cl:2479-2520 (LocalSoftMax / LocalSoftMaxGrad, NeuroNet.cl:392-420).
 // Row length is the local size of dimension 0; one warp per (sample, head) row.

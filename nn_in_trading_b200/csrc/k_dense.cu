@@ -5,6 +5,7 @@
 //
 // Weight layout is the reference's: W[out][in+1] row-major with the bias in
 // the last column, stored on the *source* layer (NeuroNet_Core.mqh:15568).
+#include <cstring>
 #include "../../include/nn_b200.h"
 #include "gemm_fast.cuh"
 #include "tc_gemm.cuh"
@@ -427,6 +428,40 @@ static AdamDenseShape adam_dense_shape(const Launch &L) {
   return AdamDenseShape{(int)L.nd.g[0], L.nd.dims > 1 ? (int)L.nd.g[1] : 1, L.i(5)};
 }
 
+// UpdateWeightsAdam on weight idx of [n_out][inputs+1] from a reduced gradient, for
+// update_normalize_rows_kernel (rows are whole: n_col == inputs + 1).
+struct DenseAdamGradStep {
+  float *w, *m, *v;
+  GradSrc G;
+  float l, b1, b2;
+  __device__ float operator()(size_t idx) const {
+    adam_dense_step(w, m, v, idx, grad_in_apply_order(G, idx), l, b1, b2);
+    return w[idx];
+  }
+};
+// The same from one sample's output gradient and inputs (the reference kernel's own arithmetic).
+struct DenseAdamSampleStep {
+  float *w, *m, *v;
+  const float *g, *x;
+  int n_col, inputs;
+  float l, b1, b2;
+  __device__ float operator()(size_t idx) const {
+    const int i = (int)(idx / n_col), j = (int)(idx % n_col);
+    float inp = nan0(j == inputs ? 1.f : x[j]);
+    float weight = nan0(w[idx]);
+    float mm = nan0(m[idx]);
+    float vv = nan0(v[idx]);
+    float gg = clampf(nan0(g[i] * inp), -kMaxGrad, kMaxGrad);
+    float mt = nan0(b1 * mm + (1.f - b1) * gg);
+    float vt = nan0(b2 * vv + (1.f - b2) * (gg * gg));
+    float delta = nan0(l * (mt / (sqrtf(vt) + 1.0e-37f) - (kL1 * signf(weight) + kL2 * weight)));
+    if (fabsf(delta) > 0.f) w[idx] = nan0(w[idx] + delta);
+    m[idx] = mt;
+    v[idx] = vt;
+    return w[idx];
+  }
+};
+
 static int adam_dense_apply_src(const Launch &Lc, GradSrc G) {
   Launch &L = const_cast<Launch &>(Lc);
   AdamDenseShape s = adam_dense_shape(L);
@@ -434,6 +469,12 @@ static int adam_dense_apply_src(const Launch &Lc, GradSrc G) {
   float *w = L.buf(0, nw), *m = L.buf(3, nw), *v = L.buf(4, nw);
   if (!w || !m || !v) return NN_ERR_BOUNDS;
   size_t n = (size_t)s.n_out * s.n_col;
+  if (L.norm_rows > 0) {
+    update_normalize_rows_kernel<<<ceil_div((size_t)L.norm_rows * 32, 256), 256, 0, L.stream>>>(
+        w, L.norm_rows, L.norm_dim, DenseAdamGradStep{w, m, v, G, L.f(6), L.f(7), L.f(8)});
+    NN_CHECK_LAUNCH(L);
+    return NN_OK;
+  }
   if (G.splits > 4)
     adam_dense_apply_split_kernel<<<(unsigned)((n + 31) / 32), dim3(32, 8), 0, L.stream>>>(
         w, m, v, G, s.n_out, s.n_col, s.inputs, L.f(6), L.f(7), L.f(8));
@@ -455,6 +496,12 @@ static int k_update_weights_adam(Launch &L) {
   float *m = L.buf(3, nw), *v = L.buf(4, nw);
   if (!w || !g || !x || !m || !v) return NN_ERR_BOUNDS;
   if (L.B == 1 && !L.deferred()) {
+    if (L.norm_rows > 0) {
+      update_normalize_rows_kernel<<<ceil_div((size_t)L.norm_rows * 32, 256), 256, 0, L.stream>>>(
+          w, L.norm_rows, L.norm_dim, DenseAdamSampleStep{w, m, v, g, x, s.n_col, s.inputs, L.f(6), L.f(7), L.f(8)});
+      NN_CHECK_LAUNCH(L);
+      return NN_OK;
+    }
     size_t n = (size_t)s.n_out * s.n_col;
     adam_dense_fused_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(w, g, x, m, v, s.n_out, s.n_col, s.inputs,
                                                                   L.f(6), L.f(7), L.f(8));
@@ -642,6 +689,23 @@ __global__ void normalize_weights_kernel(float *buf, int rows, int dim) {
   float d = k * s;
   if (d > 1.f)
     for (int i = lane; i < dim; i += 32) row[i] = nan0(row[i]) / d;
+}
+
+bool update_normalize_fusable(const KernelInst &u, const NDR &nu, const KernelInst &nw, const NDR &nnw) {
+  if (nw.args[0].type != ARG_BUF || u.args[0].type != ARG_BUF || nw.args[0].i != u.args[0].i) return false;
+  const int dim = nw.args[1].i;
+  const size_t rows = nnw.g[0];
+  if (dim <= 0 || rows == 0) return false;
+  if (std::strcmp(u.def->name, "UpdateWeightsAdam") == 0) {
+    const size_t n_out = nu.g[0], n_col = nu.dims > 1 ? nu.g[1] : 1;
+    const int inputs = u.args[5].i;
+    return n_col == (size_t)inputs + 1 && dim == inputs + 1 && rows == n_out;
+  }
+  if (std::strcmp(u.def->name, "UpdateWeightsConvAdam") == 0) {
+    const int win = u.args[9].i;
+    return dim == win + 1 && rows * (size_t)dim == nu.g[0];
+  }
+  return false;
 }
 
 static int k_normalize_weights(Launch &L) {

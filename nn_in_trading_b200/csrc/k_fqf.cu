@@ -447,7 +447,9 @@ __global__ void fqf_sample_kernel(const float *__restrict__ q, const float *__re
       b += a;  // d == 32: element lane + 32 adds element lane
     }
   }
-  const float last = total <= 32 ? __shfl_sync(kFull, a, total - 1) : __shfl_sync(kFull, b, total - 33);
+  const float last_a = __shfl_sync(kFull, a, (total - 1) & 31);
+  const float last_b = __shfl_sync(kFull, b, (total - 33) & 31);
+  const float last = total <= 32 ? last_a : last_b;
   const float mass = nan0(last);
   if (mass <= 1.0e-6f) {
     if (lane == 0) res[task] = 0.f;
@@ -455,8 +457,11 @@ __global__ void fqf_sample_kernel(const float *__restrict__ q, const float *__re
   }
   const float u = fminf(fmaxf(nan0(rnd[task], 0.5f), 0.f), 1.f);
   const float threshold = u * mass;
+  // every lane executes every shuffle (a full-mask shuffle reached by only some lanes never completes)
   const float a_prev = __shfl_up_sync(kFull, a, 1);
-  const float b_prev = lane == 0 ? __shfl_sync(kFull, a, 31) : __shfl_up_sync(kFull, b, 1);
+  const float a_top = __shfl_sync(kFull, a, 31);
+  const float b_up = __shfl_up_sync(kFull, b, 1);
+  const float b_prev = lane == 0 ? a_top : b_up;
   int pick = total;
   {
     const int i = lane;

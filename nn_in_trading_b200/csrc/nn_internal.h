@@ -45,6 +45,9 @@ struct Launch {
   NDR nd;
   cudaStream_t stream;
   int B;  // batch
+  // When > 0: a NormalizeWeights of norm_rows rows of norm_dim weights follows this weight update on
+  // the same matrix and is done by the update's apply kernel (the runner skips the NormalizeWeights).
+  int norm_rows = 0, norm_dim = 0;
 
   // Device pointer of buffer argument `idx`, checked to hold at least
   // `need` floats.  Returns nullptr (and records the error) otherwise.
@@ -131,6 +134,13 @@ void add_launches(int n);
 int fixed_scratch_setup(int device);
 
 const KernelDef *find_kernel(const char *name);
+
+// Pairs of recorded executions that a command list runs as one kernel (the reference issues them back
+// to back): SumMatrix then Normalize of its output.
+bool sum_normalize_fusable(const KernelInst &sum, const NDR &nsum, const KernelInst &norm, const NDR &nnorm);
+// ... and a dense or convolution Adam update then NormalizeWeights of the same weight rows.
+bool update_normalize_fusable(const KernelInst &upd, const NDR &nupd, const KernelInst &norm, const NDR &nnorm);
+int sum_normalize_launch(Launch &L);
 
 inline unsigned int ceil_div(size_t a, size_t b) { return (unsigned int)((a + b - 1) / b); }
 

@@ -42,6 +42,7 @@ struct DeferredOp {
   NDR nd;
   int (*apply)(const Launch &, const float *) = nullptr;  // null: plain launch
   const float *grad = nullptr;
+  int norm_rows = 0, norm_dim = 0;  // NormalizeWeights done by the apply (see Launch)
 };
 
 // ---- NCCL, resolved at nn_dp_init so the library loads without it ----------
@@ -220,6 +221,8 @@ void Launch::defer(int (*apply)(const Launch &, const float *), const float *gra
   op.nd = nd;
   op.apply = apply;
   op.grad = grad;
+  op.norm_rows = norm_rows;
+  op.norm_dim = norm_dim;
   ctx->deferred.push_back(op);
   // every gradient written so far is final for this step: once a bucket's worth has gathered,
   // its allreduce starts on the communication stream while the rest of backward runs
@@ -266,7 +269,24 @@ void add_launches(int n) {
   if (g_ctx) g_ctx->launches += n;
 }
 
-static int run_one(Context *c, const KernelInst &k, const NDR &nd) {
+static int run_one(Context *c, const KernelInst &k, const NDR &nd, int norm_rows = 0, int norm_dim = 0) {
+  Launch L;
+  L.ctx = c;
+  L.k = &k;
+  L.nd = nd;
+  L.stream = c->stream;
+  L.B = k.batch;
+  L.norm_rows = norm_rows;
+  L.norm_dim = norm_dim;
+  for (size_t i = 0; i < std::strlen(k.def->argtypes); ++i) {
+    if (k.args[i].type == ARG_UNSET)
+      return set_err(NN_ERR_ARG, std::string(k.def->name) + ": argument " + std::to_string(i) + " not set");
+  }
+  return k.def->fn(L);
+}
+
+// run_one with another launcher for the same arguments (a fused pair of recorded executions).
+static int run_as(Context *c, const KernelInst &k, const NDR &nd, LaunchFn fn) {
   Launch L;
   L.ctx = c;
   L.k = &k;
@@ -277,7 +297,7 @@ static int run_one(Context *c, const KernelInst &k, const NDR &nd) {
     if (k.args[i].type == ARG_UNSET)
       return set_err(NN_ERR_ARG, std::string(k.def->name) + ": argument " + std::to_string(i) + " not set");
   }
-  return k.def->fn(L);
+  return fn(L);
 }
 
 static int run_deferred(Context *c, const DeferredOp &op) {
@@ -288,6 +308,8 @@ static int run_deferred(Context *c, const DeferredOp &op) {
   L.nd = op.nd;
   L.stream = c->stream;
   L.B = op.k.batch;
+  L.norm_rows = op.norm_rows;
+  L.norm_dim = op.norm_dim;
   return op.apply(L, op.grad);
 }
 
@@ -793,10 +815,29 @@ int nn_cmdlist_run(int id) {
   NEED_CTX();
   CmdList *l = get_list(id);
   if (!l) return set_err(NN_ERR_HANDLE, "unknown command list");
+  static const KernelDef *k_sum = find_kernel("SumMatrix"), *k_norm = find_kernel("Normalize");
+  static const KernelDef *k_normw = find_kernel("NormalizeWeights");
   for (size_t i = 0; i < l->ops.size(); ++i) {
     Context *c = g_ctx;
     const Recorded &r = l->ops[i];
     int rc;
+    if (r.k.def == k_sum && i + 1 < l->ops.size() && l->ops[i + 1].k.def == k_norm &&
+        sum_normalize_fusable(r.k, r.nd, l->ops[i + 1].k, l->ops[i + 1].nd)) {
+      // SumMatrix + Normalize of its output: one pass over the rows
+      rc = run_as(c, r.k, r.nd, sum_normalize_launch);
+      if (rc) return set_err(rc, "command list position " + std::to_string(i) + ": " + g_err);
+      ++i;
+      continue;
+    }
+    if (i + 1 < l->ops.size() && l->ops[i + 1].k.def == k_normw &&
+        update_normalize_fusable(r.k, r.nd, l->ops[i + 1].k, l->ops[i + 1].nd)) {
+      // a weight update then NormalizeWeights of its rows: the apply kernel normalises them
+      const Recorded &n = l->ops[i + 1];
+      rc = run_one(c, r.k, r.nd, (int)n.nd.g[0], n.k.args[1].i);
+      if (rc) return set_err(rc, "command list position " + std::to_string(i) + ": " + g_err);
+      ++i;
+      continue;
+    }
     if (c->deferring && r.k.def->param_only) {
       DeferredOp op;
       op.k = r.k;

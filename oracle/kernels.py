@@ -248,12 +248,43 @@ def CalcHiddenGradientConv(matrix_w, matrix_g, matrix_o, matrix_ig, outputs, ste
             matrix_ig[v * inputs:(v + 1) * inputs] = deactivation(s, o, activation)
 
 
+def _conv_weight_grad_dense(matrix_g, matrix_i, inputs, window_in, window_out, step, n_weights):
+    """The Adam variant of conv_weight_grad as one contraction, when nothing in it needs the loop: whole
+    variables of weights, every product index inside the arrays, no window cut short by the stop test,
+    finite operands and sums.  grad[v][o][s] = sum_t g[v][t][o] x[v*inputs + t*step + s] (s < window_in)
+    and grad[v][o][window_in] = sum_t g[v][t][o]; the sums are taken in float64 and rounded once (the
+    reference's serial float32 order agrees to the tolerance the golden cases pin).  None otherwise."""
+    W1 = window_in + 1
+    per_var = W1 * window_out
+    total = (inputs - (window_in - step) + (step - 1)) // step
+    if n_weights % per_var or total <= 0 or step <= 0 or total * window_in > inputs:
+        return None
+    V = n_weights // per_var
+    if V * total * window_out > matrix_g.size or (V - 1) * inputs + (total - 1) * step + window_in > matrix_i.size:
+        return None
+    g = matrix_g[:V * total * window_out].reshape(V, total, window_out).astype(np.float64)
+    t_idx = (np.arange(V)[:, None, None] * inputs + np.arange(total)[None, :, None] * step
+             + np.arange(window_in)[None, None, :])
+    x = matrix_i[t_idx].astype(np.float64)
+    if not (np.isfinite(g).all() and np.isfinite(x).all()):
+        return None
+    out = np.empty((V, window_out, W1), np.float64)
+    out[:, :, :window_in] = np.einsum("vto,vts->vos", g, x)
+    out[:, :, window_in] = g.sum(axis=1)
+    out = out.astype(F32).reshape(-1)
+    return out if np.isfinite(out).all() else None
+
+
 def conv_weight_grad(matrix_g, matrix_i, inputs, window_in, window_out, step, n_weights, momentum_variant=False):
     """Per-weight gradient loops of UpdateWeightsConvAdam (NeuroNet.cl:1073-1081) and
     UpdateWeightsConvMomentum (NeuroNet.cl:1016-1031), including their index quirks:
     Adam uses total = (inputs-(window_in-step)+(step-1))/step and shift_out = i/(window_in+1)-v*window_out;
     Momentum uses total = (inputs-window_in+step-1)/step and shift_out = i/(window_in+1)-v;
     both stop at the first t with shift + t*window_in >= inputs (window_in, not step)."""
+    fast = None if momentum_variant else _conv_weight_grad_dense(matrix_g, matrix_i, inputs, window_in, window_out,
+                                                                 step, n_weights)
+    if fast is not None:
+        return fast
     i = np.arange(n_weights)
     v = i // ((window_in + 1) * window_out)
     shift = i % (window_in + 1)

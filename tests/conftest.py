@@ -19,3 +19,18 @@ def ctx():
     c = Context(0)
     yield c
     c.close()
+
+
+def pytest_terminal_summary(terminalreporter, exitstatus, config):
+    """How many compared elements needed each allowance of tests/parity.py in this run."""
+    from tests.parity import DRIFT, STATS
+    for label, st in DRIFT.items():
+        terminalreporter.write_line(
+            "drift {}: tensor {:.2e} (bound {:g}); element-wise p50 {:.1e} p99 {:.1e} max {:.1e}".format(
+                label, st["tensor_rel"], st["bound"], st["elem_p50"], st["elem_p99"], st["elem_max"]))
+    if STATS["checks"]:
+        terminalreporter.write_line(
+            "parity: {checks} tensors, {elements} elements compared; element-wise rel err > 1e-4: "
+            "{elem_rtol_1e-4}; accepted by the TANH/SIGMOID floor: {deact_floor}; weights with a cancelled "
+            "gradient that moved the other way: {cancelled_weights}; in-place changes checked: "
+            "{delta_checks}".format(**STATS))

@@ -1,0 +1,219 @@
+"""The five benchmark configurations trained for many steps through the C ABI beside the oracle, with
+no state copied between them: outputs, gradients, weights and Adam moments are compared at
+checkpoints along the run, so rounding differences compound as they would between two real
+training runs.  Each comparison is bounded by a stated drift bound (the worst |got - ref| over
+max|ref| of the tensor) and its element-wise distribution is reported at the end of the session
+(tests/parity.py: drift).
+
+  dense MLP      240-500-500-3, batch 1, the full 1000 online steps, against the reference's own
+                 kernels (oracle/_ref) sequenced as CNet::feedForward / backPropOCL
+  encoder        4 x (120 tokens, 64 features, 8 heads x 32, FF 256), batch 8, 20 steps
+  LSTM stack     input 64, 2 layers of 256, 64 series over the full 240-bar window
+  PatchTST-style 32 channels x 512 bars, patch 16 / stride 8, embed 128, 3 layers, batch 2, 3 steps
+  SAC            state 240, action 6, hidden 512, replay 512, 4 updates
+
+Why drift grows: the reference's Adam has no effective epsilon (m / (sqrt(v) + 1e-37)), so a weight
+moves by about lr * 3.16 in the direction of its gradient's sign whatever the gradient's size; where a
+gradient is at rounding level, two correct float32 runs can move the weight in opposite directions,
+and later steps carry that difference forward.  The bounds below are set a few times above the
+drift measured on a B200 (the session summary prints the measured values)."""
+import numpy as np
+import pytest
+
+from nn_in_trading_b200 import configs as C
+from nn_in_trading_b200.sac import SACAgent, SACSpec, sac_data, sac_weights
+from oracle import kernels as K
+from oracle import nets as O
+from oracle.ref import RefKernels
+from tests.parity import drift
+
+pytestmark = pytest.mark.gpu
+
+# drift bounds (tensor-relative) per configuration and tensor kind
+BOUNDS = {
+    "dense": {"output": 5e-2, "weights": 5e-2, "m": 2e-1, "v": 2e-1},
+    "encoder": {"output": 5e-2, "input_gradient": 2e-1, "weights": 5e-2, "m": 5e-1, "v": 5e-1},
+    "lstm": {"output": 5e-2, "memory": 5e-2, "weights": 5e-2, "head": 5e-2},
+    "patchtst": {"output": 5e-2, "encoder": 5e-2, "weights": 5e-2, "options": 5e-2},
+    "sac": {"values": 5e-2, "weights": 5e-2, "m": 5e-1, "v": 5e-1},
+}
+
+
+@pytest.fixture(autouse=True)
+def numpy_oracle():
+    O.use_backend("numpy")
+    yield
+    O.use_backend("numpy")
+
+
+def test_dense_mlp_1000_online_steps_against_the_reference_kernels(ctx):
+    if not RefKernels.available():
+        pytest.skip("oracle/_ref not built")
+    spec = C.DenseSpec()
+    w = C.dense_weights(spec)
+    steps = 1000
+    xs, ts = C.dense_data(spec, steps, 1)
+    net = C.build_dense(ctx, spec, 1, w)
+    net.capture()
+    O.use_backend("reference")
+    layers = [O.ODense(n, a, 1, spec.sizes[i + 1] if i + 1 < len(spec.sizes) else 0)
+              for i, (n, a) in enumerate(zip(spec.sizes, spec.acts))]
+    for layer, ww in zip(layers, w):
+        layer.weights[:] = ww
+    onet = O.ONet(layers)
+    b = BOUNDS["dense"]
+    checkpoints = {1, 10, 100, 250, 500, 1000}
+    for s in range(steps):
+        net.set_input(xs[s])
+        net.set_target(ts[s])
+        net.step()
+        onet.step(xs[s], ts[s])
+        if s + 1 in checkpoints:
+            tag = f"dense step{s + 1}"
+            drift(f"{tag} output", ctx.read(net.layers[-1].output, 3), onet.layers[-1].output, b["output"])
+            for li in range(3):
+                gl, ol = net.layers[li], onet.layers[li]
+                n = ol.weights.size
+                drift(f"{tag} layer{li} weights", ctx.read(gl.weights, n), ol.weights, b["weights"])
+                drift(f"{tag} layer{li} m", ctx.read(gl.m, n), ol.m, b["m"])
+                drift(f"{tag} layer{li} v", ctx.read(gl.v, n), ol.v, b["v"])
+
+
+def test_attention_encoder_20_steps_batch_8(ctx):
+    spec = C.MLMHSpec()
+    B, steps = 8, 20
+    w = C.mlmh_weights(spec)
+    net = C.build_mlmh(ctx, spec, B, w)
+    net.capture()
+    inp = O.ODense(spec.window * spec.units, K.NONE, B, 0)
+    enc = O.OMLMH(spec.window, spec.dk, spec.heads, spec.units, spec.layers, spec.activation, B)
+    for i, ws in enumerate(w):
+        for name, arr in ws.items():
+            enc.w[i][name][0][:] = arr
+    onet = O.ONet([inp, enc])
+    xs, ts = C.mlmh_data(spec, B, steps)
+    b = BOUNDS["encoder"]
+    for s in range(steps):
+        net.set_input(xs[s])
+        net.set_target(ts[s])
+        net.step()
+        onet.step(xs[s], ts[s])
+        if s + 1 in (1, 5, 10, 20):
+            tag = f"encoder step{s + 1}"
+            g_enc = net.layers[1]
+            drift(f"{tag} output", ctx.read(g_enc.output, g_enc.neurons * B), enc.output, b["output"])
+            drift(f"{tag} input gradient", ctx.read(net.layers[0].gradient, g_enc.neurons * B), inp.gradient,
+                  b["input_gradient"])
+            for i in range(spec.layers):
+                for name in ("qkv", "w0", "ff1", "ff2"):
+                    n = enc.counts[name]
+                    for j, kind in enumerate(("weights", "m", "v")):
+                        drift(f"{tag} L{i} {name} {kind}", ctx.read(g_enc.w[i][name][j], n), enc.w[i][name][j][:n],
+                              b[kind])
+
+
+def test_lstm_stack_full_window(ctx):
+    spec = C.LSTMSpec(inputs=64, hidden=256, layers=2, series=64, seq=240)
+    w = C.lstm_weights(spec)
+    net = C.build_lstm(ctx, spec, w)
+    net.capture()
+    layers = [O.ODense(spec.inputs * spec.series, K.NONE, 1, 0)]
+    ins = spec.inputs
+    for l in range(spec.layers):
+        L = O.OLSTM(spec.hidden, ins, spec.series, 1)
+        L.lstm_w[:] = w[f"lstm{l}"]
+        layers.append(L)
+        ins = spec.hidden
+    head = O.OConv(spec.hidden, spec.hidden, spec.inputs, spec.series, 1, K.NONE, 1)
+    head.conv_w[:] = w["head"]
+    layers.append(head)
+    onet = O.ONet(layers)
+    xs = C.lstm_data(spec)
+    b = BOUNDS["lstm"]
+    for t in range(spec.seq):
+        net.set_input(xs[t].reshape(-1))
+        net.set_target(xs[t + 1].reshape(-1))
+        net.step()
+        onet.step(xs[t].reshape(1, -1), xs[t + 1].reshape(1, -1))
+        if t + 1 in (1, 16, 60, 120, 240):
+            tag = f"lstm bar{t + 1}"
+            for li in (1, 2):
+                g, o = net.layers[li], onet.layers[li]
+                drift(f"{tag} lstm{li} output", ctx.read(g.output), o.output, b["output"])
+                drift(f"{tag} lstm{li} memory", ctx.read(g.memory), o.memory, b["memory"])
+                drift(f"{tag} lstm{li} weights", ctx.read(g.lstm_w), o.lstm_w, b["weights"])
+            drift(f"{tag} head output", ctx.read(net.layers[3].output), onet.layers[3].output, b["head"])
+            drift(f"{tag} head weights", ctx.read(net.layers[3].conv_w), head.conv_w, b["weights"])
+
+
+def test_patchtst_full_size_3_steps(ctx):
+    spec = C.PatchSpec()
+    B, steps = 2, 3
+    w = C.patch_weights(spec)
+    net = C.build_patch(ctx, spec, B, w)
+    P, E, Cc = spec.patches, spec.embed, spec.channels
+    inp = O.ODense(Cc * spec.bars, K.NONE, B, 0)
+    norm = O.OBatchNorm(Cc * spec.bars, spec.norm_batch, B)
+    conv = O.OConv(spec.patch, spec.stride, E, P, Cc, K.NONE, B)
+    conv.conv_w[:] = w["conv"]
+    enc = O.OMLMH(E, spec.dk, spec.heads, P, spec.layers, K.NONE, B * Cc)
+    for i, ws in enumerate(w["encoder"]):
+        for name, arr in ws.items():
+            enc.w[i][name][0][:] = arr
+    head = O.OConv(P * E, P * E, spec.horizon, Cc, 1, K.NONE, B)
+    head.conv_w[:] = w["head"]
+    onet = O.ONet([inp, norm, conv, enc, head, O.ORevIN(Cc * spec.horizon, norm, B)])
+    xs, ts = C.patch_data(spec, B, steps)
+    b = BOUNDS["patchtst"]
+    for s in range(steps):
+        net.set_input(xs[s])
+        net.set_target(ts[s])
+        net.step()
+        onet.step(xs[s], ts[s])
+        tag = f"patchtst step{s + 1}"
+        drift(f"{tag} output", ctx.read(net.layers[5].output), onet.layers[5].output, b["output"])
+        drift(f"{tag} encoder output", ctx.read(net.layers[3].output), enc.output, b["encoder"])
+        drift(f"{tag} bn options", ctx.read(net.layers[1].options), norm.options, b["options"])
+        drift(f"{tag} patch conv weights", ctx.read(net.layers[2].conv_w), conv.conv_w, b["weights"])
+        drift(f"{tag} head weights", ctx.read(net.layers[4].conv_w), head.conv_w, b["weights"])
+        for i in range(spec.layers):
+            for name in ("qkv", "w0", "ff1", "ff2"):
+                n = enc.counts[name]
+                drift(f"{tag} L{i} {name} weights", ctx.read(net.layers[3].w[i][name][0], n), enc.w[i][name][0][:n],
+                      b["weights"])
+
+
+def test_sac_full_size_replay_512(ctx):
+    spec = SACSpec()
+    B, steps = 512, 4
+    w = sac_weights(spec)
+    agent = SACAgent(ctx, spec, B, w)
+    agent.capture()
+    oracle = O.OSACAgent(spec, B, w)
+    data = sac_data(spec, B, steps=steps)
+    b = BOUNDS["sac"]
+    for s in range(steps):
+        bt = {k: v[s] for k, v in data.items()}
+        agent.set_batch(bt)
+        agent.step()
+        oracle.step(bt)
+        tag = f"sac step{s + 1}"
+        drift(f"{tag} target values", ctx.read(agent.y, B), oracle.y, b["values"])
+        drift(f"{tag} log-probs", ctx.read(agent.logp, B), oracle.logp, b["values"])
+        for k in range(2):
+            drift(f"{tag} critic{k} q", ctx.read(agent.critics[k][-1].output, B),
+                  oracle.critics[k].layers[-1].output.reshape(-1), b["values"])
+        for li in range(3):
+            gl, ol = agent.actor[li], oracle.actor.layers[li]
+            for kind in ("weights", "m", "v"):
+                arr = getattr(ol, kind)
+                drift(f"{tag} actor{li} {kind}", ctx.read(getattr(gl, kind), arr.size), arr, b[kind])
+        for k in range(2):
+            for kind, gnet, onet in (("critic", agent.critics[k], oracle.critics[k]),
+                                     ("target", agent.targets[k], oracle.targets[k])):
+                arr = onet.layers[1].conc_w
+                drift(f"{tag} {kind}{k} concat weights", ctx.read(gnet[1].conc_w, arr.size), arr, b["weights"])
+                for li in (1, 2):
+                    arr = onet.layers[li].weights
+                    drift(f"{tag} {kind}{k} layer{li} weights", ctx.read(gnet[li].weights, arr.size), arr,
+                          b["weights"])
