@@ -27,8 +27,8 @@ def _params(ctx, net):
             if isinstance(x, nnw.Record):
                 walk(x, f"{label}.{k}")
             elif k in PARAM_KEYS:
-                out += [(f"{label} {k}[{i}]", a) for i, a in enumerate(x)] if isinstance(x, list) \
-                    else [(f"{label} {k}", x)]
+                out.extend([(f"{label} {k}[{i}]", a) for i, a in enumerate(x)] if isinstance(x, list)
+                           else [(f"{label} {k}", x)])
     for i, r in enumerate(nnw.capture(net).records):
         walk(r, f"layer{i}")
     return out
