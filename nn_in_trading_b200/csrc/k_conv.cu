@@ -366,34 +366,24 @@ static int conv_upd_shape(Launch &L, int inputs_idx, int win_idx, int wout_idx, 
   return NN_OK;
 }
 
-// UpdateWeightsConvAdam on weight idx from a reduced gradient, for update_normalize_rows_kernel.
-struct ConvAdamGradStep {
-  float *w, *m, *v;
-  GradSrc G;
-  float l, b1, b2;
-  __device__ float operator()(size_t idx) const {
-    adam_conv_step(w, m, v, idx, grad_in_apply_order(G, idx), l, b1, b2);
-    return w[idx];
-  }
-};
-
 static int adam_conv_apply_src(const Launch &Lc, GradSrc G) {
   Launch &L = const_cast<Launch &>(Lc);
   size_t n = L.nd.g[0];
   float *w = L.buf(0, n), *m = L.buf(3, n), *v = L.buf(4, n);
   if (!w || !m || !v) return NN_ERR_BOUNDS;
-  if (L.norm_rows > 0) {
-    update_normalize_rows_kernel<<<ceil_div((size_t)L.norm_rows * 32, 256), 256, 0, L.stream>>>(
-        w, L.norm_rows, L.norm_dim, ConvAdamGradStep{w, m, v, G, L.f(6), L.f(7), L.f(8)});
-    NN_CHECK_LAUNCH(L);
-    return NN_OK;
-  }
   if (G.splits > 4)
     adam_conv_apply_split_kernel<<<(unsigned)((n + 31) / 32), dim3(32, 8), 0, L.stream>>>(w, m, v, G, n, L.f(6), L.f(7),
                                                                                           L.f(8));
   else
     adam_conv_apply_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(w, m, v, G, n, L.f(6), L.f(7), L.f(8));
   NN_CHECK_LAUNCH(L);
+  if (L.norm_rows > 0) {
+    // the NormalizeWeights the runner folded into this update: a reduction over many split-K partials
+    // keeps every weight its own thread, so the rows are normalised by the usual kernel afterwards
+    normalize_weights_kernel<<<ceil_div((size_t)L.norm_rows * 32, 256), 256, 0, L.stream>>>(w, L.norm_rows,
+                                                                                         L.norm_dim);
+    NN_CHECK_LAUNCH(L);
+  }
   return NN_OK;
 }
 static int adam_conv_apply(const Launch &L, const float *grad) {

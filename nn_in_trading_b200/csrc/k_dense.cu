@@ -428,18 +428,9 @@ static AdamDenseShape adam_dense_shape(const Launch &L) {
   return AdamDenseShape{(int)L.nd.g[0], L.nd.dims > 1 ? (int)L.nd.g[1] : 1, L.i(5)};
 }
 
-// UpdateWeightsAdam on weight idx of [n_out][inputs+1] from a reduced gradient, for
-// update_normalize_rows_kernel (rows are whole: n_col == inputs + 1).
-struct DenseAdamGradStep {
-  float *w, *m, *v;
-  GradSrc G;
-  float l, b1, b2;
-  __device__ float operator()(size_t idx) const {
-    adam_dense_step(w, m, v, idx, grad_in_apply_order(G, idx), l, b1, b2);
-    return w[idx];
-  }
-};
-// The same from one sample's output gradient and inputs (the reference kernel's own arithmetic).
+// UpdateWeightsAdam on weight idx of [n_out][inputs+1] (whole rows: n_col == inputs + 1) from one
+// sample's output gradient and inputs, the reference kernel's own arithmetic, for
+// update_normalize_rows_flat_kernel.
 struct DenseAdamSampleStep {
   float *w, *m, *v;
   const float *g, *x;
@@ -469,12 +460,6 @@ static int adam_dense_apply_src(const Launch &Lc, GradSrc G) {
   float *w = L.buf(0, nw), *m = L.buf(3, nw), *v = L.buf(4, nw);
   if (!w || !m || !v) return NN_ERR_BOUNDS;
   size_t n = (size_t)s.n_out * s.n_col;
-  if (L.norm_rows > 0) {
-    update_normalize_rows_kernel<<<ceil_div((size_t)L.norm_rows * 32, 256), 256, 0, L.stream>>>(
-        w, L.norm_rows, L.norm_dim, DenseAdamGradStep{w, m, v, G, L.f(6), L.f(7), L.f(8)});
-    NN_CHECK_LAUNCH(L);
-    return NN_OK;
-  }
   if (G.splits > 4)
     adam_dense_apply_split_kernel<<<(unsigned)((n + 31) / 32), dim3(32, 8), 0, L.stream>>>(
         w, m, v, G, s.n_out, s.n_col, s.inputs, L.f(6), L.f(7), L.f(8));
@@ -482,6 +467,12 @@ static int adam_dense_apply_src(const Launch &Lc, GradSrc G) {
     adam_dense_apply_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(w, m, v, G, s.n_out, s.n_col, s.inputs, L.f(6),
                                                                   L.f(7), L.f(8));
   NN_CHECK_LAUNCH(L);
+  if (L.norm_rows > 0) {
+    // the folded NormalizeWeights after a batched update (see adam_conv_apply_src)
+    normalize_weights_kernel<<<ceil_div((size_t)L.norm_rows * 32, 256), 256, 0, L.stream>>>(w, L.norm_rows,
+                                                                                         L.norm_dim);
+    NN_CHECK_LAUNCH(L);
+  }
   return NN_OK;
 }
 static int adam_dense_apply(const Launch &L, const float *grad) {
@@ -497,7 +488,7 @@ static int k_update_weights_adam(Launch &L) {
   if (!w || !g || !x || !m || !v) return NN_ERR_BOUNDS;
   if (L.B == 1 && !L.deferred()) {
     if (L.norm_rows > 0) {
-      update_normalize_rows_kernel<<<ceil_div((size_t)L.norm_rows * 32, 256), 256, 0, L.stream>>>(
+      update_normalize_rows_flat_kernel<<<L.norm_rows, 256, 0, L.stream>>>(
           w, L.norm_rows, L.norm_dim, DenseAdamSampleStep{w, m, v, g, x, s.n_col, s.inputs, L.f(6), L.f(7), L.f(8)});
       NN_CHECK_LAUNCH(L);
       return NN_OK;

@@ -43,55 +43,52 @@ struct GradSrc {
 
 __global__ void reduce_partials_kernel(float *out, GradSrc src, size_t n);
 
-// The gradient of entry idx summed in the order the apply kernels use: one running sum when there are
-// at most four partials (GradSrc::operator()), else eight running sums over every eighth partial added
-// up in order (the 8-group reduction of the split apply kernels), then scaled.
-__device__ __forceinline__ float grad_in_apply_order(const GradSrc &G, size_t idx) {
-  if (G.splits <= 4) return G(idx);
-  const size_t j = G.at(idx);
-  float t = 0.f;
-#pragma unroll
-  for (int y = 0; y < 8; ++y) {
-    float s = 0.f;
-    for (int k = y; k < G.splits; k += 8) s += G.p[k * G.stride + j];
-    t += s;
-  }
-  return t * G.scale;
-}
+// NormalizeWeights (defined with the dense kernels): rows of `dim` weights rescaled to unit norm.
+__global__ void normalize_weights_kernel(float *buf, int rows, int dim);
 
-// A weight update followed by NormalizeWeights of the rows it updated (NeuroNet_Core.mqh:15971-15977,
-// NeuroNet_Attention.mqh:2395-2399), in one kernel: a warp per row of `dim` weights; step(i) applies the
-// update arithmetic to weight i of the row-major matrix, stores it and returns what it stored; the row's
-// norm is then formed exactly as normalize_weights_kernel forms it (same lanes, same order, the same
-// retry with pre-scaling when the sum of squares overflows) and the row is rescaled when its norm
-// exceeds 1.
+// A single-sample weight update followed by NormalizeWeights of the rows it updated
+// (NeuroNet_Core.mqh:15971-15977), in one kernel: one block of 256 threads per row of `dim` weights;
+// step(i) applies the update arithmetic to weight i of the row-major matrix, stores it and returns what
+// it stored; each thread accumulates the squares of its own columns, the block sums them (in another
+// order than normalize_weights_kernel, so the norm may differ in its last bit), and the row is
+// rescaled when its norm exceeds 1, with normalize_weights_kernel's retry when the sum overflows.
 template <class Step>
-__global__ void update_normalize_rows_kernel(float *w, int rows, int dim, Step step) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (warp >= rows) return;
-  float *row = w + (size_t)warp * dim;
+__global__ void __launch_bounds__(256) update_normalize_rows_flat_kernel(float *w, int rows, int dim, Step step) {
+  __shared__ float part[8];
+  __shared__ float row_d;
+  const int row = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  if (row >= rows) return;
+  float *wr = w + (size_t)row * dim;
   float s = 0.f;
-  for (int i = lane; i < dim; i += 32) {
-    const float q = nan0(step((size_t)warp * dim + i));
+  for (int col = t; col < dim; col += 256) {
+    const float q = nan0(step((size_t)row * dim + col));
     s += q * q;
   }
   s = warp_sum(s);
-  float k = 1.f;
-  for (int guard = 1; !isfinite(s) && guard < 64; ++guard) {
-    k *= 10.f;
-    s = 0.f;
-    for (int i = lane; i < dim; i += 32) {
-      const float q = nan0(row[i]) / k;
-      s += q * q;
-    }
+  if (lane == 0) part[warp] = s;
+  __syncthreads();
+  if (warp == 0) {
+    s = lane < 8 ? part[lane] : 0.f;
     s = warp_sum(s);
+    float k = 1.f;
+    for (int guard = 1; !isfinite(s) && guard < 64; ++guard) {
+      k *= 10.f;
+      s = 0.f;
+      for (int i = lane; i < dim; i += 32) {
+        const float q = nan0(wr[i]) / k;
+        s += q * q;
+      }
+      s = warp_sum(s);
+    }
+    if (lane == 0) row_d = k * sqrtf(s);
   }
-  s = sqrtf(s);
-  const float d = k * s;
+  __syncthreads();
+  const float d = row_d;
   if (d > 1.f)
-    for (int i = lane; i < dim; i += 32) row[i] = nan0(row[i]) / d;
+    for (int i = t; i < dim; i += 256) wr[i] = nan0(wr[i]) / d;
 }
+
+
 
 // Partial store for the fast GEMM: N computed columns inside rows of `ldp` (the bias
 // column N of each row is filled by colsum_partial_kernel).
