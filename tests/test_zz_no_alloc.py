@@ -47,7 +47,7 @@ def _free_bytes(device):
     return torch.cuda.mem_get_info(device)[0]
 
 
-# (256, 256, 1100): tensor-core product split over the batch (split boundaries on 32-deep stages)
+# (256, 256, 1100): the batch split into several parts; (3, 500, 1024): few outputs, many inputs
 @pytest.mark.parametrize("outputs,inputs,batch", [(37, 53, 5), (500, 240, 64), (3, 500, 1024),
                                                   (256, 256, 1100)])
 def test_fixed_scratch_update_matches_update_weights_adam(ctx, outputs, inputs, batch):
