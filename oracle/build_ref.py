@@ -1,4 +1,4 @@
-"""ORACLE TEST INFRASTRUCTURE -- builds oracle/_ref/libnnref.so.
+"""ORACLE TEST INFRASTRUCTURE -- builds oracle/_ref/libnnref.so and libnnref_fma.so.
 
 Recipe that compiles the reference's own kernel source
 (Experts/NeuroNet_DNG/NeuroNet.cl) for the host CPU.  It reads the file where
@@ -8,6 +8,13 @@ Local* reductions) and every in-scope kernel by name, rewrites the OpenCL C
 spellings that C++ does not accept (vector literals, address-space
 qualifiers, __local arrays), and compiles the result together with
 oracle/ref_shim.h and oracle/ref_exec.cpp into oracle/_ref/libnnref.so.
+
+Two builds of the same source: libnnref.so evaluates every a*b+c as a rounded
+product and a rounded sum (-ffp-contract=off); libnnref_fma.so lets the
+compiler contract them into fused multiply-adds, as OpenCL C allows by default
+(the FP_CONTRACT pragma is ON unless a program turns it off) and as GPU
+OpenCL compilers do.  Both are valid executions of the reference; the second
+needs a host CPU with FMA instructions.
 
 Nothing from the reference is committed: the rewritten source is written
 only to oracle/_ref/ (git-ignored).  When the reference checkout is absent
@@ -209,14 +216,23 @@ def generate(cl_text: str) -> str:
     return "\n".join(parts) + "\n"
 
 
+# output name -> floating-point contraction flags
+VARIANTS = {"libnnref.so": ["-ffp-contract=off"], "libnnref_fma.so": ["-ffp-contract=fast", "-mfma"]}
+
+
 def build(reference: str, force: bool = False) -> str | None:
+    """Builds both variants; returns the path of libnnref.so (None without the reference
+    checkout and without an earlier build)."""
     cl_path = os.path.join(reference, CL_RELPATH)
     lib = os.path.join(OUT_DIR, "libnnref.so")
     if not os.path.exists(cl_path):
         return lib if os.path.exists(lib) else None
     deps = [cl_path, __file__, os.path.join(HERE, "ref_shim.h"), os.path.join(HERE, "ref_exec.cpp")]
-    if (not force and os.path.exists(lib)
-            and os.path.getmtime(lib) >= max(os.path.getmtime(d) for d in deps)):
+    newest = max(os.path.getmtime(d) for d in deps)
+    todo = [name for name in VARIANTS
+            if force or not os.path.exists(os.path.join(OUT_DIR, name))
+            or os.path.getmtime(os.path.join(OUT_DIR, name)) < newest]
+    if not todo:
         return lib
     os.makedirs(OUT_DIR, exist_ok=True)
     with open(cl_path, "r", encoding="utf-8", errors="replace") as f:
@@ -224,11 +240,12 @@ def build(reference: str, force: bool = False) -> str | None:
     gen = os.path.join(OUT_DIR, "nn_ref_gen.cpp")
     with open(gen, "w") as f:
         f.write(generate(cl_text))
-    cmd = ["g++", "-O2", "-std=c++17", "-fopenmp", "-fPIC", "-shared", "-w",
-           "-fno-fast-math", "-ffp-contract=off", "-I", HERE,
-           gen, os.path.join(HERE, "ref_exec.cpp"), "-o", lib + ".tmp"]
-    subprocess.run(cmd, check=True)
-    os.replace(lib + ".tmp", lib)
+    for name in todo:
+        out = os.path.join(OUT_DIR, name)
+        cmd = ["g++", "-O2", "-std=c++17", "-fopenmp", "-fPIC", "-shared", "-w", "-fno-fast-math",
+               *VARIANTS[name], "-I", HERE, gen, os.path.join(HERE, "ref_exec.cpp"), "-o", out + ".tmp"]
+        subprocess.run(cmd, check=True)
+        os.replace(out + ".tmp", out)
     return lib
 
 

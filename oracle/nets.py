@@ -30,9 +30,9 @@ class RefBackend:
     """Kernel backend that runs the reference's own NeuroNet.cl kernels compiled for the CPU
     (oracle/_ref/libnnref.so) with the same call signature as oracle.kernels."""
 
-    def __init__(self):
-        from .ref import RefKernels
-        self.ref = RefKernels()
+    def __init__(self, path: str | None = None):
+        from .ref import LIB_PATH, RefKernels
+        self.ref = RefKernels(path or LIB_PATH)
 
     def __getattr__(self, name):
         if name not in self.ref.sig:

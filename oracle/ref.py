@@ -18,6 +18,20 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_ref", "libnnref.so")
+# the same kernels with multiply-adds contracted into FMAs (OpenCL's default FP_CONTRACT ON)
+LIB_FMA_PATH = os.path.join(HERE, "_ref", "libnnref_fma.so")
+
+
+def host_has_fma() -> bool:
+    """Whether this CPU executes the FMA instructions libnnref_fma.so is compiled with."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("flags"):
+                    return " fma " in line + " "
+    except OSError:
+        pass
+    return False
 
 
 class RefKernels:
