@@ -23,6 +23,16 @@
 //              transpose through shared memory, and the epilogue functor with
 //              lanes along n (coalesced stores), while the MMAs of the next
 //              tile run into the other accumulator.
+// A operand in tensor memory.  When TMA brings the A tiles in (every variant whose A tensor TMA can
+// address), the producers do not split A in shared memory: each thread reads its row's 16 k values of
+// the raw tile, writes hi and lo into tensor-memory columns of the stage (tcgen05.st, 32 lanes per
+// warp; lane m = row m, one column per k) and the MMAs read A from there (tcgen05.mma with [a_tmem]).
+// Shared memory then carries the raw A tile and B only, and the tensor cores read only B from it: the
+// CTA allocates all 512 columns (two accumulators of BN columns, then 2 x 32 columns of A per stage),
+// which also frees shared memory for 4 stages at BN = 128 and 6 at BN = 64 (3 and 4 before).  An MMA
+// that reads a stage's A columns completes before the stage's empty barrier fires (tcgen05.commit), so
+// the producers overwrite the columns only after that wait; they wait for their own stores
+// (tcgen05.wait::st) before they signal the stage full.
 // Every mbarrier wait is bounded (about one second of clock, plus an
 // iteration cap): on expiry the thread raises a CTA-wide abort flag and writes
 // a code to `err` (read back by nn_finish), and all roles drain to the common
@@ -190,6 +200,30 @@ __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64
       : "memory");
 }
 
+// The same with A read from tensor memory: tmem_a addresses the 8 columns (one k step) of the A
+// tile, row m of A in lane m.
+__device__ __forceinline__ void mma_tf32_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// tcgen05.st of 16 consecutive 32-bit columns into this warp's 32 lanes (lane l gets r[] of thread l).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+// every tcgen05.st this thread issued has completed
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
@@ -305,12 +339,31 @@ __host__ __device__ constexpr int epi_warps(int a_mode, int b_mode) { return (a_
 // or bulk copies brought in (more warps, fewer chunks each, a larger share of the issue slots).
 __host__ __device__ constexpr int prod_warps(int a_mode, int b_mode) { return (a_mode == 0 || b_mode == 0) ? 4 : 8; }
 
-template <int BN, int BK, int STAGES, int EPIW = 4, bool TMA_ST = false>
+// Shared memory an epilogue of EPIW warps reserves (TMA-store boxes, or transpose buffers plus the
+// column-constant table).
+__host__ __device__ constexpr uint32_t epi_bytes(int epiw, bool tma_st) {
+  return tma_st ? (uint32_t)epiw * 4096u : (uint32_t)epiw * 32u * 36u * 4u + 2048u * 4u;
+}
+
+// Stages of a variant whose A tiles are split into tensor memory: as many as both the shared memory
+// (raw A + split B per stage) and the 512 tensor-memory columns (two BN-column accumulators, then
+// 2 * BK columns of A hi / lo per stage) hold, at most 6.
+__host__ __device__ constexpr int atm_stages(int bn, int bk, int epiw, bool tma_st) {
+  const int by_smem = (int)((232448u - 1024u - epi_bytes(epiw, tma_st)) / (uint32_t)(128 * bk * 4 + 2 * bn * bk * 4));
+  const int by_tmem = (512 - 2 * bn) / (2 * bk);
+  const int s = by_smem < by_tmem ? by_smem : by_tmem;
+  return s > 6 ? 6 : s;
+}
+
+// A_TM: the A operand's hi / lo halves live in tensor memory (the MMAs read A from there and only B
+// from shared memory); a stage's shared memory then holds the raw A tile as TMA wrote it, and B.
+template <int BN, int BK, int STAGES, int EPIW = 4, bool TMA_ST = false, bool A_TM = false>
 struct Cfg {
   static constexpr int BM = 128;
   static constexpr uint32_t A_BYTES = BM * BK * 4;  // one of hi / lo
   static constexpr uint32_t B_BYTES = BN * BK * 4;
-  static constexpr uint32_t STAGE_BYTES = 2 * (A_BYTES + B_BYTES);
+  static constexpr uint32_t B_OFF = (A_TM ? 1 : 2) * A_BYTES;  // B hi, then B lo, within a stage
+  static constexpr uint32_t STAGE_BYTES = B_OFF + 2 * B_BYTES;
   static constexpr uint32_t EPI_OFF = STAGES * STAGE_BYTES;
   // per epilogue warp: one 32 x 36 transpose buffer, or one 4 KB TMA-store box (1024-byte aligned)
   static constexpr uint32_t EPI_BYTES = TMA_ST ? EPIW * 4096 : EPIW * 32 * 36 * 4;
@@ -321,13 +374,18 @@ struct Cfg {
   static constexpr uint32_t SMEM = COL_OFF + COL_FLOATS * 4 + 1024;  // + alignment slack
   static constexpr int A_CHUNKS = BM * BK / 4 / 128;            // float4 chunks per producer thread per stage
   static constexpr int B_CHUNKS = BN * BK / 4 / 128;
-  static constexpr uint32_t TMEM_COLS = 2 * BN;  // two accumulators: epilogue of one tile || MMAs of the next
+  // two accumulators (epilogue of one tile || MMAs of the next), then with A_TM the A stages
+  static constexpr uint32_t A_COL0 = 2 * BN;
+  static constexpr uint32_t TMEM_COLS = A_TM ? 512u : 2 * BN;
   static_assert(BK == 32, "a stage row of a K-major tile is one 128-byte swizzle row");
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "tile");
   static_assert(A_BYTES % 1024 == 0 && B_BYTES % 1024 == 0, "swizzle atoms must stay 1024-byte aligned");
   static_assert((BM * BK / 4) % 128 == 0 && (BN * BK / 4) % 128 == 0, "chunks per thread");
   static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0 && TMEM_COLS >= 32 && TMEM_COLS <= 512, "tensor-memory columns");
   static_assert(SMEM <= 232448, "shared memory per CTA");
+  static_assert(!A_TM || A_COL0 + 2 * BK * STAGES <= TMEM_COLS, "A stages in tensor memory");
+  // a CTA that holds all 512 columns must be alone on its SM (no second allocation can wait on it)
+  static_assert(!A_TM || SMEM > 232448 / 2, "one CTA per SM");
   static_assert(!TMA_ST || EPI_OFF % 1024 == 0, "TMA-store boxes use the 128-byte swizzle");
 };
 
@@ -420,7 +478,7 @@ __device__ __forceinline__ void split_chunks(uint8_t *hi, uint8_t *lo, uint32_t 
 // Persistent kernel: CTA i processes tiles i, i + gridDim.x, ... (n-tile fastest, so the CTAs in
 // flight share their A rows in L2).  320 threads:
 //   warps 0-3  epilogue (tensor-memory lanes 32w..32w+31 = tile rows), one accumulator at a time
-//   warps 4-7  producers (OP_REGS loads and splits, OP_TMA in-place splits), stage ring of STAGES
+//   warps 4-7  producers (OP_REGS loads and splits; OP_TMA: A into tensor memory, B split in place), stage ring of STAGES
 //   warp 8     tensor-memory owner and MMA issuer, alternating two accumulators
 //   warp 9     loader: TMA tiles and packed-image bulk copies
 // Epilogue functors give a per-row offset (`row`, computed once per tile by the lane that owns the
@@ -441,7 +499,10 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + prod_warps(A
   constexpr int PW = prod_warps(A_MODE, B_MODE), NPT = 32 * PW;
   constexpr int kProd0 = EPIW, kMma = EPIW + PW, kLoad = EPIW + PW + 1;
   static_assert(NPT == 128 || (A_MODE != OP_REGS && B_MODE != OP_REGS), "register loads assume 128 producers");
-  using C = Cfg<BN, BK, STAGES, EPIW, TMA_ST>;
+  // TMA-loaded A tiles are split into tensor memory; only B is read by the MMAs from shared memory
+  constexpr bool A_TM = A_MODE == OP_TMA;
+  static_assert(!A_TM || PW == 8, "A in tensor memory: two producer warps per lane quarter");
+  using C = Cfg<BN, BK, STAGES, EPIW, TMA_ST, A_TM>;
   constexpr int BM = C::BM;
   constexpr bool A_K = !A_MCONTIG, B_K = !B_NCONTIG;
   static_assert(A_MODE != OP_PACKED, "only the B operand is packed");
@@ -454,7 +515,8 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + prod_warps(A
   constexpr uint32_t B_LBO = B_K ? (B_SW ? 16u : 128u) : 128u * BK, B_SBO = B_K ? (B_SW ? 1024u : 32u * BK) : 512u;
   constexpr uint32_t A_LAY = A_K ? (A_SW ? 2u : 0u) : 1u, B_LAY = B_K ? (B_SW ? 2u : 0u) : 1u;
   constexpr uint32_t A_STEP = A_K ? (A_SW ? 32u : 256u) : 1024u, B_STEP = B_K ? (B_SW ? 32u : 256u) : 1024u;
-  constexpr uint32_t IDESC = instr_desc_tf32(BM, BN, A_MCONTIG, B_NCONTIG);
+  // A in tensor memory is K-major: lane m holds row m, one column per k
+  constexpr uint32_t IDESC = instr_desc_tf32(BM, BN, A_TM ? false : A_MCONTIG, B_NCONTIG);
   constexpr bool ANY_TMA = A_MODE == OP_TMA || B_MODE == OP_TMA;
   constexpr bool LOADER = ANY_TMA || B_MODE == OP_PACKED;
 
@@ -570,12 +632,52 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + prod_warps(A
         return false;
       }
       uint8_t *base = smem + st * C::STAGE_BYTES;
-      uint8_t *b_hi = base + 2 * C::A_BYTES, *b_lo = b_hi + C::B_BYTES;
+      uint8_t *b_hi = base + C::B_OFF, *b_lo = b_hi + C::B_BYTES;
       int row, k;
       if (A_MODE == OP_REGS) {
 #pragma unroll
         for (int i = 0; i < C::A_CHUNKS; ++i)
           store_split(base, base + C::A_BYTES, chunk_place<A_K, BM, BK>(ptid + 128 * i, row, k), va[i]);
+      } else if constexpr (A_TM) {
+        // raw A tile -> registers -> nan0 -> hi / lo -> tensor memory.  Warp w may address lanes
+        // 32 (w % 4) .. +31 (A rows 32 (w % 4) + lane); the two warps of a lane quarter take the
+        // stage's k halves.  The MMAs that read this stage's columns last time have completed (the
+        // empty barrier above is their commit).
+        tc_fence_after();
+        const int q = warp & 3, half = (warp - kProd0) >> 2, m = 32 * q + lane;
+        float v[16];
+        if constexpr (A_K) {
+          // K-major, 128-byte swizzle: row m at m * 128, its 16-byte granule j at (j ^ (m % 8)) * 16
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float4 x =
+                *reinterpret_cast<const float4 *>(base + m * 128 + ((((4 * half + j) ^ (m & 7))) << 4));
+            v[4 * j] = x.x;
+            v[4 * j + 1] = x.y;
+            v[4 * j + 2] = x.z;
+            v[4 * j + 3] = x.w;
+          }
+        } else {
+          // MN-major, 128-byte swizzle with 32-byte granules (the layout of chunk_place<false>): a
+          // warp reads one 128-byte k row per load, conflict-free
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int kk = 16 * half + j;
+            v[j] = *reinterpret_cast<const float *>(base + q * 128 * BK + (kk >> 2) * 512 + (kk & 3) * 128 +
+                                                    ((((lane >> 3) ^ (kk & 3))) << 5) + ((lane >> 2) & 1) * 16 +
+                                                    (lane & 3) * 4);
+          }
+        }
+        uint32_t hi[16], lo[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float x = nan0(v[j]);
+          hi[j] = __float_as_uint(x);  // the tensor cores truncate it to TF32 themselves
+          lo[j] = __float_as_uint(x - tf32_hi(x));
+        }
+        const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + C::A_COL0 + (uint32_t)(st * 2 * BK + 16 * half);
+        tmem_st16(ta, hi);
+        tmem_st16(ta + BK, lo);
       } else {
         split_chunks<C::A_BYTES / 16 / NPT>(base, base + C::A_BYTES, 16u * ptid, 16u * NPT);
       }
@@ -595,6 +697,10 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + prod_warps(A
         }
       }
       fence_proxy_async_smem();
+      if constexpr (A_TM) {
+        tmem_wait_st();
+        tc_fence_before();
+      }
       mbar_arrive(&full[st]);
       ++it;
       return true;
@@ -646,7 +752,7 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + prod_warps(A
               }
             }
             if (B_MODE == OP_TMA) {
-              uint8_t *bdst = base + 2 * C::A_BYTES;
+              uint8_t *bdst = base + C::B_OFF;
               if (B_K) {
                 tma_load_3d(bdst, &tmB, k0, n0, z, &tmaf[st]);
               } else {
@@ -658,7 +764,7 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + prod_warps(A
           if (B_MODE == OP_PACKED) {
             // the weight tile of this stage, already split and laid out, in one bulk copy
             const size_t img = ((size_t)(n0 / BN) * kstages + (kbeg / BK + kk)) * (2 * C::B_BYTES);
-            bulk_copy_g2s(base + 2 * C::A_BYTES, bimg + img, 2 * C::B_BYTES, &tmaf[st]);
+            bulk_copy_g2s(base + C::B_OFF, bimg + img, 2 * C::B_BYTES, &tmaf[st]);
           }
         }
         if (!ok) break;
@@ -694,17 +800,25 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + prod_warps(A
         if (lane == 0) {
           const uint32_t base = smem_u32(smem + st * C::STAGE_BYTES);
           const uint32_t a_hi = base, a_lo = base + C::A_BYTES;
-          const uint32_t b_hi = base + 2 * C::A_BYTES, b_lo = b_hi + C::B_BYTES;
+          const uint32_t b_hi = base + C::B_OFF, b_lo = b_hi + C::B_BYTES;
+          // A_TM: the stage's A hi / lo columns in tensor memory (8 columns per k step)
+          const uint32_t ta_hi = tmem + C::A_COL0 + (uint32_t)(st * 2 * BK), ta_lo = ta_hi + BK;
           const int kv = min(BK, kend - (kbeg + kk * BK));
           const int nsub = (kv + 7) / 8;
           for (int sub = 0; sub < nsub; ++sub) {
-            const uint64_t ah = smem_desc(a_hi + sub * A_STEP, A_LBO, A_SBO, A_LAY);
-            const uint64_t al = smem_desc(a_lo + sub * A_STEP, A_LBO, A_SBO, A_LAY);
             const uint64_t bh = smem_desc(b_hi + sub * B_STEP, B_LBO, B_SBO, B_LAY);
             const uint64_t bl = smem_desc(b_lo + sub * B_STEP, B_LBO, B_SBO, B_LAY);
-            mma_tf32(d, al, bh, IDESC, (kk | sub) != 0 ? 1u : 0u);
-            mma_tf32(d, ah, bl, IDESC, 1u);
-            mma_tf32(d, ah, bh, IDESC, 1u);
+            if constexpr (A_TM) {
+              mma_tf32_ta(d, ta_lo + 8 * sub, bh, IDESC, (kk | sub) != 0 ? 1u : 0u);
+              mma_tf32_ta(d, ta_hi + 8 * sub, bl, IDESC, 1u);
+              mma_tf32_ta(d, ta_hi + 8 * sub, bh, IDESC, 1u);
+            } else {
+              const uint64_t ah = smem_desc(a_hi + sub * A_STEP, A_LBO, A_SBO, A_LAY);
+              const uint64_t al = smem_desc(a_lo + sub * A_STEP, A_LBO, A_SBO, A_LAY);
+              mma_tf32(d, al, bh, IDESC, (kk | sub) != 0 ? 1u : 0u);
+              mma_tf32(d, ah, bl, IDESC, 1u);
+              mma_tf32(d, ah, bh, IDESC, 1u);
+            }
           }
           mma_commit(&empty[st]);
         }
@@ -1034,8 +1148,12 @@ inline cudaError_t tcgemm_launch(const FastShape &s, EP ep, cudaStream_t st, int
   constexpr int EPIW = tc::epi_warps(A_MODE, B_MODE);
   constexpr bool TMA_ST = tc::ep_tma_store<EP>::value && EPIW == 8;
   // stages fill what the epilogue buffers leave of the 227 KB
-  constexpr int STAGES = TMA_ST ? (BN == 128 ? 3 : 4) : BN == 128 ? (EPIW == 8 ? 2 : 3) : (EPIW == 8 ? 3 : 4);
-  using C = tc::Cfg<BN, BK, STAGES, EPIW, TMA_ST>;
+  constexpr bool A_TM = A_MODE == tc::OP_TMA;
+  constexpr int STAGES = A_TM     ? tc::atm_stages(BN, BK, EPIW, TMA_ST)
+                         : TMA_ST ? (BN == 128 ? 3 : 4)
+                         : BN == 128 ? (EPIW == 8 ? 2 : 3)
+                                     : (EPIW == 8 ? 3 : 4);
+  using C = tc::Cfg<BN, BK, STAGES, EPIW, TMA_ST, A_TM>;
   auto fn = tc::tcgemm_kernel<BN, BK, STAGES, A_MCONTIG, B_NCONTIG, A_MODE, B_MODE, EP>;
   static bool attr = false;  // per instantiation; setting it twice is harmless
   if (!attr) {
