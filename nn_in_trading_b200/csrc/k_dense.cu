@@ -155,8 +155,8 @@ __global__ void ff_skinny_kernel(const float *__restrict__ w, const float *__res
   }
 }
 
-// Many samples, at most kSkinny outputs of the next layer: one thread per (sample, input), the
-// same arithmetic as chg_cols_kernel (k ascending).
+// Many samples, at most kSkinny outputs of the next layer: one thread per (sample, input), k
+// ascending.
 __global__ void chg_skinny_kernel(const float *__restrict__ w, const float *__restrict__ g, const float *__restrict__ o,
                                   float *__restrict__ ig, int inputs, int outputs, int B, int act) {
   const size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
@@ -251,53 +251,50 @@ static int k_calc_output_gradient(Launch &L) {
 
 // ----------------------------------------------------- CalcHiddenGradient
 // NeuroNet.cl:547-613.  ig[b,i] = Deactivation(sum_k nan0(w[k,i]) nan0(g[b,k]), o[b,i], act)
-// Small batches: CTA of 16 warps per 32 columns; warps split the k range, four rows of W in flight
-// per warp (each thread still sums its k in ascending order).
+// Small batches: a CTA of 16 warps per CPB columns.  Lane l of a warp takes column l % CPB and k
+// lane l / CPB, so the CTA splits the k range KS = 16 * 32 / CPB ways (each thread sums its k in
+// ascending order, KS apart); a warp load reads 32 / CPB rows of W, CPB floats each.  Narrow
+// column groups spread a batch-1 product of a few hundred columns over about a hundred CTAs
+// instead of a dozen.  The KS partials of each (sample, column) are summed by one warp in a fixed
+// shuffle order.
 constexpr int kChgWarps = 16;
-template <int MAXB>
+template <int MAXB, int CPB>
 __global__ void __launch_bounds__(kChgWarps * 32) chg_cols_kernel(const float *__restrict__ w,
                                                                   const float *__restrict__ g,
                                                                   const float *__restrict__ o, float *__restrict__ ig,
                                                                   int inputs, int outputs, int B, int act) {
-  __shared__ float part[kChgWarps][MAXB][33];
-  int col = blockIdx.x * 32 + (threadIdx.x & 31);
-  int wv = threadIdx.x >> 5;
+  constexpr int KL = 32 / CPB, KS = kChgWarps * KL;
+  __shared__ float part[MAXB][CPB][KS + 1];
+  const int lane = threadIdx.x & 31, wv = threadIdx.x >> 5;
+  const int c = lane % CPB, kid = wv * KL + lane / CPB;
+  const int col = blockIdx.x * CPB + c;
   float s[MAXB];
 #pragma unroll
   for (int b = 0; b < MAXB; ++b) s[b] = 0.f;
   if (col < inputs) {
     const size_t ld = (size_t)inputs + 1;
-    int k = wv;
-    for (; k + 3 * kChgWarps < outputs; k += 4 * kChgWarps) {
-      float wk[4], gk[4][MAXB];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        wk[u] = w[(size_t)(k + u * kChgWarps) * ld + col];
-#pragma unroll
-        for (int b = 0; b < MAXB; ++b) gk[u][b] = b < B ? g[(size_t)b * outputs + k + u * kChgWarps] : 0.f;
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-#pragma unroll
-        for (int b = 0; b < MAXB; ++b)
-          if (b < B) s[b] += nan0(wk[u]) * nan0(gk[u][b]);
-    }
-    for (; k < outputs; k += kChgWarps) {
-      float wk = nan0(w[(size_t)k * ld + col]);
+#pragma unroll 4
+    for (int k = kid; k < outputs; k += KS) {
+      const float wk = nan0(w[(size_t)k * ld + col]);
 #pragma unroll
       for (int b = 0; b < MAXB; ++b)
         if (b < B) s[b] += wk * nan0(g[(size_t)b * outputs + k]);
     }
   }
 #pragma unroll
-  for (int b = 0; b < MAXB; ++b) part[wv][b][threadIdx.x & 31] = s[b];
+  for (int b = 0; b < MAXB; ++b) part[b][c][kid] = s[b];
   __syncthreads();
-  if (wv < MAXB && wv < B && col < inputs) {
+  // warp wv reduces the (sample, column) pairs wv, wv + 16, ...
+  for (int pr = wv; pr < B * CPB; pr += kChgWarps) {
+    const int b = pr / CPB, cc = pr % CPB, col2 = blockIdx.x * CPB + cc;
     float t = 0.f;
+    for (int r = lane; r < KS; r += 32) t += part[b][cc][r];
 #pragma unroll
-    for (int r = 0; r < kChgWarps; ++r) t += part[r][wv][threadIdx.x & 31];
-    size_t idx = (size_t)wv * inputs + col;
-    ig[idx] = deactivate(t, o[idx], act);
+    for (int off = 16; off > 0; off >>= 1) t += __shfl_down_sync(0xffffffffu, t, off);
+    if (lane == 0 && col2 < inputs) {
+      const size_t idx = (size_t)b * inputs + col2;
+      ig[idx] = deactivate(t, o[idx], act);
+    }
   }
 }
 
@@ -322,7 +319,16 @@ static int k_calc_hidden_gradient(Launch &L) {
   float *ig = L.buf(3, (size_t)L.B * inputs);
   if (!w || !g || !o || !ig) return NN_ERR_BOUNDS;
   if (L.B <= 4) {
-    chg_cols_kernel<4><<<ceil_div(inputs, 32), kChgWarps * 32, 0, L.stream>>>(w, g, o, ig, inputs, outputs, L.B, act);
+    // column groups as wide as still give most SMs a CTA
+    if (inputs >= 32 * 148)
+      chg_cols_kernel<4, 32><<<ceil_div(inputs, 32), kChgWarps * 32, 0, L.stream>>>(w, g, o, ig, inputs, outputs, L.B,
+                                                                                   act);
+    else if (inputs >= 8 * 74)
+      chg_cols_kernel<4, 8><<<ceil_div(inputs, 8), kChgWarps * 32, 0, L.stream>>>(w, g, o, ig, inputs, outputs, L.B,
+                                                                                 act);
+    else
+      chg_cols_kernel<4, 4><<<ceil_div(inputs, 4), kChgWarps * 32, 0, L.stream>>>(w, g, o, ig, inputs, outputs, L.B,
+                                                                                 act);
     NN_CHECK_LAUNCH(L);
     return NN_OK;
   }

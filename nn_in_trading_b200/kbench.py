@@ -18,7 +18,7 @@ import os
 
 import numpy as np
 
-from .api import Context
+from .api import NONE, Context
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
@@ -70,6 +70,31 @@ def _matmult(rows, dim, cols, var, grad):
             4.0 * (2 * a.size + 2 * b.size + r.size), "tf32x3_tflops")
 
 
+def _conv(kind, units, window, window_out, batch):
+    """One 1x1 convolution of the attention encoder (FeedForwardConv, CalcHiddenGradientConv or
+    UpdateWeightsConvAdam with step = window) over `batch` sequences of `units` rows."""
+    rng = np.random.default_rng(7)
+    rows = batch * units
+    w = (rng.standard_normal(window_out * (window + 1)) * 0.1).astype(np.float32)
+    x = rng.standard_normal(batch * units * window).astype(np.float32)
+    y = rng.standard_normal(batch * units * window_out).astype(np.float32)
+    in_total, out_total = units * window, units * window_out
+    flops = 2.0 * rows * window_out * (window + 1)
+    if kind == "ff":
+        args = [w, x, np.zeros_like(y), in_total, window, window, window_out, NONE]
+        return ("FeedForwardConv", args, (units, window_out, 1), None, batch, flops,
+                4.0 * (x.size + y.size + w.size), "tf32x3_tflops")
+    if kind == "dgrad":
+        args = [w, y, x, np.zeros_like(x), out_total, window, window, window_out, NONE, 0]
+        return ("CalcHiddenGradientConv", args, (in_total, 1), None, batch, flops,
+                4.0 * (y.size + 2 * x.size + w.size), "tf32x3_tflops")
+    m = np.zeros_like(w)
+    v = np.zeros_like(w)
+    args = [w, y, x, m, v, in_total, 3e-4, 0.9, 0.999, window, window_out, window]
+    return ("UpdateWeightsConvAdam", args, ((window + 1) * window_out,), None, batch, flops,
+            4.0 * (y.size + x.size + 6 * w.size), "tf32x3_tflops")
+
+
 CASES = {
     # CCrossMHFlashAttention-shaped self attention: 4 sequences of 512 positions, 8 heads of 64
     "flash_fwd_b4_512x512_h8_d64": lambda: _flash(4, 512, 512, 8, 64, 0, False),
@@ -77,6 +102,14 @@ CASES = {
     # four 4096 x 1024 by 1024 x 1024 products
     "matmult_v4_4096x1024x1024": lambda: _matmult(4096, 1024, 1024, 4, False),
     "matmult_grad_v4_4096x1024x1024": lambda: _matmult(4096, 1024, 1024, 4, True),
+    # the attention encoder's 1x1 convolutions at batch 256 (120 bars x 64 features, 8 heads x 32):
+    # Q/K/V 64 -> 768 and FF2 256 -> 64
+    "conv_ff_qkv_b256": lambda: _conv("ff", 120, 64, 768, 256),
+    "conv_dgrad_qkv_b256": lambda: _conv("dgrad", 120, 64, 768, 256),
+    "conv_wgrad_adam_qkv_b256": lambda: _conv("wgrad", 120, 64, 768, 256),
+    "conv_ff_ff2_b256": lambda: _conv("ff", 120, 256, 64, 256),
+    "conv_dgrad_ff2_b256": lambda: _conv("dgrad", 120, 256, 64, 256),
+    "conv_wgrad_adam_ff2_b256": lambda: _conv("wgrad", 120, 256, 64, 256),
 }
 
 
