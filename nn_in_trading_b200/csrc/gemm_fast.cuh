@@ -31,6 +31,11 @@ struct FastShape {
   // Tensor-core path only: when >= 0, column `ones_col` of B is all ones (not read from memory) and
   // B holds ones_col real columns -- the bias input of a weight gradient folded into the GEMM.
   int ones_col = -1;
+  // Tensor-core path with TMA-loaded A and B only: when >= 0, the producers also write the sum of
+  // A(m, k) over each split's k range into column `rowsum_col` of the output (the bias column of a
+  // weight gradient, without an MMA column for it).  The epilogue functor stores single elements;
+  // N must be a multiple of 32, so that no TMA-store box of the epilogue covers that column.
+  int rowsum_col = -1;
 };
 
 template <int BN, bool A_MCONTIG, bool B_NCONTIG, bool VEC_A, bool VEC_B, class EP>

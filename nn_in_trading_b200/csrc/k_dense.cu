@@ -103,10 +103,15 @@ __global__ void wgrad_small_m_kernel(float *p, const float *A, long long lda, co
 
 // ------------------------------------------------------------ FeedForward
 // NeuroNet.cl:430-512.  y[b,o] = act(sum_k nan0(nan0(x[b,k]) w[o,k]) + nan0(w[o,in]))
-// Small batches: one warp per output row, lanes striding the row (coalesced).
+// Small batches: one warp per output row, lanes striding the row (coalesced).  Launched with
+// programmatic dependent launch, like the other kernels of a batch-1 step (the output gradient, the
+// hidden gradient, the fused update): each waits for its predecessor's writes before its first read
+// and lets its successor launch at once.
 template <int MAXB>
 __global__ void ff_rows_kernel(const float *__restrict__ w, const float *__restrict__ x, float *__restrict__ y,
                                int inputs, int outputs, int B, int act) {
+  pdl_wait();
+  pdl_trigger();
   int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   int lane = threadIdx.x & 31;
   if (warp >= outputs) return;
@@ -114,6 +119,7 @@ __global__ void ff_rows_kernel(const float *__restrict__ w, const float *__restr
   float s[MAXB];
 #pragma unroll
   for (int b = 0; b < MAXB; ++b) s[b] = 0.f;
+#pragma unroll 4
   for (int k = lane; k < inputs; k += 32) {
     float wk = row[k];
 #pragma unroll
@@ -211,8 +217,8 @@ static int k_feedforward(Launch &L) {
   }
   if (L.B <= 4) {
     unsigned blocks = ceil_div((size_t)outputs * 32, 256);
-    ff_rows_kernel<4><<<blocks, 256, 0, L.stream>>>(w, x, y, inputs, outputs, L.B, act);
-    NN_CHECK_LAUNCH(L);
+    cudaError_t e = launch_pdl(ff_rows_kernel<4>, blocks, 256, 0, L.stream, w, x, y, inputs, outputs, L.B, act);
+    if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
   } else if (outputs <= kSkinny) {
     ff_skinny_kernel<<<ceil_div((size_t)L.B * 32, 256), 256, 0, L.stream>>>(w, x, y, inputs, outputs, L.B, act);
     NN_CHECK_LAUNCH(L);
@@ -234,6 +240,8 @@ static int k_feedforward(Launch &L) {
 // ----------------------------------------------------- CalcOutputGradient
 // NeuroNet.cl:523-536.  ig = Deactivation(t - o, o, act); the `error` argument is unused.
 __global__ void out_grad_kernel(const float *t, const float *o, float *ig, size_t n, int act) {
+  pdl_wait();
+  pdl_trigger();
   size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (i >= n) return;
   float out = o[i];
@@ -244,8 +252,8 @@ static int k_calc_output_gradient(Launch &L) {
   size_t n = (size_t)L.nd.g[0] * L.B;
   float *t = L.buf(0, n), *o = L.buf(1, n), *ig = L.buf(2, n);
   if (!t || !o || !ig) return NN_ERR_BOUNDS;
-  out_grad_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(t, o, ig, n, L.i(3));
-  NN_CHECK_LAUNCH(L);
+  cudaError_t e = launch_pdl(out_grad_kernel, grid1d(n, 256), 256, 0, L.stream, t, o, ig, n, L.i(3));
+  if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
   return NN_OK;
 }
 
@@ -265,6 +273,8 @@ __global__ void __launch_bounds__(kChgWarps * 32) chg_cols_kernel(const float *_
                                                                   int inputs, int outputs, int B, int act) {
   constexpr int KL = 32 / CPB, KS = kChgWarps * KL;
   __shared__ float part[MAXB][CPB][KS + 1];
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31, wv = threadIdx.x >> 5;
   const int c = lane % CPB, kid = wv * KL + lane / CPB;
   const int col = blockIdx.x * CPB + c;
@@ -320,16 +330,17 @@ static int k_calc_hidden_gradient(Launch &L) {
   if (!w || !g || !o || !ig) return NN_ERR_BOUNDS;
   if (L.B <= 4) {
     // column groups as wide as still give most SMs a CTA
+    cudaError_t e;
     if (inputs >= 32 * 148)
-      chg_cols_kernel<4, 32><<<ceil_div(inputs, 32), kChgWarps * 32, 0, L.stream>>>(w, g, o, ig, inputs, outputs, L.B,
-                                                                                   act);
+      e = launch_pdl(chg_cols_kernel<4, 32>, ceil_div(inputs, 32), kChgWarps * 32, 0, L.stream, w, g, o, ig, inputs,
+                     outputs, L.B, act);
     else if (inputs >= 8 * 74)
-      chg_cols_kernel<4, 8><<<ceil_div(inputs, 8), kChgWarps * 32, 0, L.stream>>>(w, g, o, ig, inputs, outputs, L.B,
-                                                                                 act);
+      e = launch_pdl(chg_cols_kernel<4, 8>, ceil_div(inputs, 8), kChgWarps * 32, 0, L.stream, w, g, o, ig, inputs,
+                     outputs, L.B, act);
     else
-      chg_cols_kernel<4, 4><<<ceil_div(inputs, 4), kChgWarps * 32, 0, L.stream>>>(w, g, o, ig, inputs, outputs, L.B,
-                                                                                 act);
-    NN_CHECK_LAUNCH(L);
+      e = launch_pdl(chg_cols_kernel<4, 4>, ceil_div(inputs, 4), kChgWarps * 32, 0, L.stream, w, g, o, ig, inputs,
+                     outputs, L.B, act);
+    if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
     return NN_OK;
   }
   if (outputs <= kSkinny) {
@@ -494,9 +505,10 @@ static int k_update_weights_adam(Launch &L) {
   if (!w || !g || !x || !m || !v) return NN_ERR_BOUNDS;
   if (L.B == 1 && !L.deferred()) {
     if (L.norm_rows > 0) {
-      update_normalize_rows_flat_kernel<<<L.norm_rows, 256, 0, L.stream>>>(
-          w, L.norm_rows, L.norm_dim, DenseAdamSampleStep{w, m, v, g, x, s.n_col, s.inputs, L.f(6), L.f(7), L.f(8)});
-      NN_CHECK_LAUNCH(L);
+      cudaError_t e = launch_pdl(update_normalize_rows_flat_kernel<DenseAdamSampleStep>, L.norm_rows, 256, 0, L.stream,
+                                 w, L.norm_rows, L.norm_dim,
+                                 DenseAdamSampleStep{w, m, v, g, x, s.n_col, s.inputs, L.f(6), L.f(7), L.f(8)});
+      if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
       return NN_OK;
     }
     size_t n = (size_t)s.n_out * s.n_col;

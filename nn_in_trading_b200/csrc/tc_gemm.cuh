@@ -29,7 +29,8 @@
 // warp; lane m = row m, one column per k) and the MMAs read A from there (tcgen05.mma with [a_tmem]).
 // Shared memory then carries the raw A tile and B only, and the tensor cores read only B from it: the
 // CTA allocates all 512 columns (two accumulators of BN columns, then 2 x 32 columns of A per stage),
-// which also frees shared memory for 4 stages at BN = 128 and 6 at BN = 64 (3 and 4 before).  An MMA
+// which also frees shared memory for 4 stages at BN = 128 and 6 at BN = 64 (3 and 4 with A split in
+// shared memory).  An MMA
 // that reads a stage's A columns completes before the stage's empty barrier fires (tcgen05.commit), so
 // the producers overwrite the columns only after that wait; they wait for their own stores
 // (tcgen05.wait::st) before they signal the stage full.
@@ -221,6 +222,18 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
 }
+// tcgen05.st of 32 consecutive 32-bit columns into this warp's 32 lanes.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
 // every tcgen05.st this thread issued has completed
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -326,6 +339,12 @@ template <class T, class = void>
 struct ep_tma_store : std::false_type {};
 template <class T>
 struct ep_tma_store<T, std::void_t<decltype(T::kTmaStore)>> : std::integral_constant<bool, T::kTmaStore> {};
+// Functors that store single elements (operator()(m, n, z, split, value)) and accept the producers'
+// row sums of A as column rowsum_col (kRowSum).
+template <class T, class = void>
+struct ep_row_sum : std::false_type {};
+template <class T>
+struct ep_row_sum<T, std::void_t<decltype(T::kRowSum)>> : std::integral_constant<bool, T::kRowSum> {};
 template <class T, class = void>
 struct ep_has_aux : std::false_type {};
 template <class T>
@@ -502,6 +521,8 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + prod_warps(A
   // TMA-loaded A tiles are split into tensor memory; only B is read by the MMAs from shared memory
   constexpr bool A_TM = A_MODE == OP_TMA;
   static_assert(!A_TM || PW == 8, "A in tensor memory: two producer warps per lane quarter");
+  // with a TMA-loaded B, four producer warps put A into tensor memory and four split B
+  constexpr bool A_SPLIT4 = A_TM && B_MODE == OP_TMA;
   using C = Cfg<BN, BK, STAGES, EPIW, TMA_ST, A_TM>;
   constexpr int BM = C::BM;
   constexpr bool A_K = !A_MCONTIG, B_K = !B_NCONTIG;
@@ -576,7 +597,7 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + prod_warps(A
     // flight while the current one is split and stored (two register sets, used alternately).
     const int ptid = tid - 32 * kProd0;
     struct PState {
-      int t, kk, nk, kbeg, kend, Ma, Nb, ones;
+      int t, kk, nk, kbeg, kend, Ma, Nb, ones, m0, n0, z, split;
       const float *Ab, *Bb;
     };
     auto start_tile = [&](PState &p) -> bool {
@@ -591,6 +612,10 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + prod_warps(A
         p.Ma = s.M - m0;
         p.Nb = n_real - n0;
         p.ones = s.ones_col >= 0 ? s.ones_col - n0 : -1;
+        p.m0 = m0;
+        p.n0 = n0;
+        p.z = z;
+        p.split = split;
         p.kk = 0;
         return true;
       }
@@ -621,6 +646,7 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + prod_warps(A
       }
     };
     int it = 0;
+    float rsum = 0.f;  // A_SPLIT4: this thread's row sum of A over the current tile's k range
     auto put = [&](const PState &p, const float4 (&va)[C::A_CHUNKS], const float4 (&vb)[C::B_CHUNKS]) -> bool {
       const int st = it % STAGES;
       if (it >= STAGES && !mbar_wait(&empty[st], ((it / STAGES) - 1) & 1, &abort_flag)) {
@@ -640,44 +666,61 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + prod_warps(A
           store_split(base, base + C::A_BYTES, chunk_place<A_K, BM, BK>(ptid + 128 * i, row, k), va[i]);
       } else if constexpr (A_TM) {
         // raw A tile -> registers -> nan0 -> hi / lo -> tensor memory.  Warp w may address lanes
-        // 32 (w % 4) .. +31 (A rows 32 (w % 4) + lane); the two warps of a lane quarter take the
-        // stage's k halves.  The MMAs that read this stage's columns last time have completed (the
-        // empty barrier above is their commit).
+        // 32 (w % 4) .. +31 (A rows 32 (w % 4) + lane).  With a TMA-loaded B the first four producer
+        // warps take all 32 k of their rows (in two passes of 16) and the other four split B; with a
+        // packed B (nothing to split) the two warps of a lane quarter take the stage's k halves.
+        // The MMAs that read this stage's columns last time have completed (the empty barrier above
+        // is their commit).
         tc_fence_after();
-        const int q = warp & 3, half = (warp - kProd0) >> 2, m = 32 * q + lane;
-        float v[16];
-        if constexpr (A_K) {
-          // K-major, 128-byte swizzle: row m at m * 128, its 16-byte granule j at (j ^ (m % 8)) * 16
+        const int pw = warp - kProd0, q = warp & 3, m = 32 * q + lane;
+        if (!A_SPLIT4 || pw < 4) {
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float4 x =
-                *reinterpret_cast<const float4 *>(base + m * 128 + ((((4 * half + j) ^ (m & 7))) << 4));
-            v[4 * j] = x.x;
-            v[4 * j + 1] = x.y;
-            v[4 * j + 2] = x.z;
-            v[4 * j + 3] = x.w;
+          for (int pass = 0; pass < (A_SPLIT4 ? 2 : 1); ++pass) {
+            const int half = A_SPLIT4 ? pass : (pw >> 2);
+            float v[16];
+            if constexpr (A_K) {
+              // K-major, 128-byte swizzle: row m at m * 128, its 16-byte granule j at (j ^ (m % 8)) * 16
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float4 x =
+                    *reinterpret_cast<const float4 *>(base + m * 128 + ((((4 * half + j) ^ (m & 7))) << 4));
+                v[4 * j] = x.x;
+                v[4 * j + 1] = x.y;
+                v[4 * j + 2] = x.z;
+                v[4 * j + 3] = x.w;
+              }
+            } else {
+              // MN-major, 128-byte swizzle with 32-byte granules (the layout of chunk_place<false>): a
+              // warp reads one 128-byte k row per load, conflict-free
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const int kk = 16 * half + j;
+                v[j] = *reinterpret_cast<const float *>(base + q * 128 * BK + (kk >> 2) * 512 + (kk & 3) * 128 +
+                                                        ((((lane >> 3) ^ (kk & 3))) << 5) + ((lane >> 2) & 1) * 16 +
+                                                        (lane & 3) * 4);
+              }
+            }
+            uint32_t hi[16], lo[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float x = nan0(v[j]);
+              if constexpr (A_SPLIT4 && ep_row_sum<EP>::value) rsum += x;  // k ascending within the row
+              hi[j] = __float_as_uint(x);  // the tensor cores truncate it to TF32 themselves
+              lo[j] = __float_as_uint(x - tf32_hi(x));
+            }
+            const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + C::A_COL0 + (uint32_t)(st * 2 * BK + 16 * half);
+            tmem_st16(ta, hi);
+            tmem_st16(ta + BK, lo);
           }
-        } else {
-          // MN-major, 128-byte swizzle with 32-byte granules (the layout of chunk_place<false>): a
-          // warp reads one 128-byte k row per load, conflict-free
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int kk = 16 * half + j;
-            v[j] = *reinterpret_cast<const float *>(base + q * 128 * BK + (kk >> 2) * 512 + (kk & 3) * 128 +
-                                                    ((((lane >> 3) ^ (kk & 3))) << 5) + ((lane >> 2) & 1) * 16 +
-                                                    (lane & 3) * 4);
+          if constexpr (A_SPLIT4 && ep_row_sum<EP>::value) {
+            // the row sums of A over the split's k range: column rowsum_col of the output (written
+            // once per (m-tile, split), by the first n-tile's CTA)
+            if (p.kk + 1 == p.nk) {
+              if (s.rowsum_col >= 0 && p.n0 == 0 && m < p.Ma) ep(p.m0 + m, s.rowsum_col, p.z, p.split, rsum);
+              rsum = 0.f;
+            }
           }
         }
-        uint32_t hi[16], lo[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const float x = nan0(v[j]);
-          hi[j] = __float_as_uint(x);  // the tensor cores truncate it to TF32 themselves
-          lo[j] = __float_as_uint(x - tf32_hi(x));
-        }
-        const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + C::A_COL0 + (uint32_t)(st * 2 * BK + 16 * half);
-        tmem_st16(ta, hi);
-        tmem_st16(ta + BK, lo);
       } else {
         split_chunks<C::A_BYTES / 16 / NPT>(base, base + C::A_BYTES, 16u * ptid, 16u * NPT);
       }
@@ -686,14 +729,19 @@ __global__ void __launch_bounds__(32 * (epi_warps(A_MODE, B_MODE) + prod_warps(A
         for (int i = 0; i < C::B_CHUNKS; ++i)
           store_split(b_hi, b_lo, chunk_place<B_K, BN, BK>(ptid + 128 * i, row, k), vb[i]);
       } else if (B_MODE == OP_TMA) {
-        split_chunks<C::B_BYTES / 16 / NPT>(b_hi, b_lo, 16u * ptid, 16u * NPT);
-        // the all-ones column lies outside the B tensor, so TMA filled it with zeros
-        if (p.ones >= 0 && p.ones < BN && ptid < BK && p.kbeg + p.kk * BK + ptid < p.kend) {
-          const int kr = ptid, j = p.ones;
-          const uint32_t off = B_K ? (uint32_t)(j * 128 + ((((kr >> 2) ^ (j & 7))) << 4) + (kr & 3) * 4)
-                                   : (uint32_t)((j >> 5) * 128 * BK + kr * 128 + ((((j & 31) >> 3) ^ (kr & 3)) << 5) +
-                                                (j & 7) * 4);
-          *reinterpret_cast<float *>(b_hi + off) = 1.f;
+        // A_SPLIT4: producer warps 4-7 split B; otherwise all of them
+        constexpr int BT = A_SPLIT4 ? 128 : NPT;
+        const int bt = A_SPLIT4 ? ptid - 128 : ptid;
+        if (bt >= 0) {
+          split_chunks<C::B_BYTES / 16 / BT>(b_hi, b_lo, 16u * bt, 16u * BT);
+          // the all-ones column lies outside the B tensor, so TMA filled it with zeros
+          if (p.ones >= 0 && p.ones < BN && bt < BK && p.kbeg + p.kk * BK + bt < p.kend) {
+            const int kr = bt, j = p.ones;
+            const uint32_t off = B_K ? (uint32_t)(j * 128 + ((((kr >> 2) ^ (j & 7))) << 4) + (kr & 3) * 4)
+                                     : (uint32_t)((j >> 5) * 128 * BK + kr * 128 +
+                                                  ((((j & 31) >> 3) ^ (kr & 3)) << 5) + (j & 7) * 4);
+            *reinterpret_cast<float *>(b_hi + off) = 1.f;
+          }
         }
       }
       fence_proxy_async_smem();
@@ -1085,7 +1133,7 @@ inline int sm_count() {
 // split-K slices off the 32-deep stage grid, or an all-ones column).
 inline size_t tcgemm_pack_bytes(const FastShape &s) {
   // split-K slices must start on a stage boundary: the loader indexes the image by kbeg / 32 + stage
-  if ((s.splits > 1 && (s.kchunk <= 0 || s.kchunk % 32)) || s.ones_col >= 0 || s.nz != 1) return 0;
+  if ((s.splits > 1 && (s.kchunk <= 0 || s.kchunk % 32)) || s.ones_col >= 0 || s.rowsum_col >= 0 || s.nz != 1) return 0;
   const bool narrow = s.N <= 64 || (s.N % 128 != 0 && s.N % 128 <= 64);
   const int BN = narrow ? 64 : 128;
   const size_t tiles_n = (s.N + BN - 1) / BN, kstages = (s.K + 31) / 32;
@@ -1224,8 +1272,17 @@ inline cudaError_t tcgemm(FastShape s, EP ep, cudaStream_t st, int *err, uint8_t
   const bool packed = img != nullptr && tcgemm_pack_bytes(s) > 0 && ((uintptr_t)img & 15) == 0;
   const bool a_tma = tma_ok(s.A, s.lda, s.strideA, s.nz, s);
   const bool b_tma = !packed && tma_ok(s.B, s.ldb, s.strideB, s.nz, s);
+  // row sums come from the producers of the TMA path only (callers check tcgemm_row_sum_ok)
+  if (s.rowsum_col >= 0 && !(a_tma && b_tma && tensor_gemm_enabled() && s.N % 32 == 0 && s.rowsum_col >= s.N))
+    return cudaErrorInvalidValue;
   if (narrow) return tcgemm_modes<64, A_MCONTIG, B_NCONTIG>(s, ep, st, err, va, vb, packed ? img : nullptr, a_tma, b_tma);
   return tcgemm_modes<128, A_MCONTIG, B_NCONTIG>(s, ep, st, err, va, vb, packed ? img : nullptr, a_tma, b_tma);
+}
+
+// Whether tcgemm can compute the row sums of A (FastShape::rowsum_col) for this product: both
+// operands loaded by TMA and B not packed.
+inline bool tcgemm_row_sum_ok(const FastShape &s) {
+  return tensor_gemm_enabled() && tma_ok(s.A, s.lda, s.strideA, s.nz, s) && tma_ok(s.B, s.ldb, s.strideB, s.nz, s);
 }
 
 // Whether a call site's FP32 GEMM runs on the tensor cores: unless the context was created with

@@ -57,6 +57,8 @@ __global__ void __launch_bounds__(256) update_normalize_rows_flat_kernel(float *
   __shared__ float part[8];
   __shared__ float row_d;
   const int row = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  pdl_wait();  // a no-op unless launched with programmatic dependent launch
+  pdl_trigger();
   if (row >= rows) return;
   float *wr = w + (size_t)row * dim;
   float s = 0.f;
@@ -124,6 +126,7 @@ struct PartialStoreLd {
 // split as the tensor's outer coordinate.
 struct PartialStoreTma : PartialStoreLd {
   static constexpr bool kTmaStore = true;
+  static constexpr bool kRowSum = true;
   template <class F>
   __device__ __forceinline__ void transform(F &&f) const {
     f([](float x, float, float) { return x; });
@@ -208,9 +211,17 @@ inline int wgrad_fast(Launch &L, const float *A, long long lda, const float *X, 
                                                                                   N);
     NN_CHECK_LAUNCH(L);
   } else if (tc) {
-    // the bias input (1) is column N of X: one GEMM writes all N + 1 gradient columns
-    fs.N = N + 1;
-    fs.ones_col = N;
+    if (N % 32 == 0 && tcgemm_row_sum_ok(fs)) {
+      // the bias input (1): its gradient column is the row sum of A, which the GEMM's producer warps
+      // accumulate while they split A, so the MMAs cover the N real columns only.  The epilogue's
+      // 32-column TMA-store boxes then end at column N: a box clipped inside a row would share a
+      // 16-byte chunk with the bias column, and its store could land after the producers' one.
+      fs.rowsum_col = N;
+    } else {
+      // the bias input (1) is column N of X: one GEMM writes all N + 1 gradient columns
+      fs.N = N + 1;
+      fs.ones_col = N;
+    }
     cudaError_t e = tcgemm<true, true>(fs, PartialStoreTma{{part, M, ldp, 1}}, L.stream, device_status());
     if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
     L.counted();
