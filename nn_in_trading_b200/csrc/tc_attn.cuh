@@ -347,8 +347,9 @@ __global__ void __launch_bounds__(320, 1)
   uint8_t *sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   float *V0s = reinterpret_cast<float *>(sm + C::V0), *AVs = reinterpret_cast<float *>(sm + C::AV);
   // w1[j]: S and G rows of q-chunk j split (dV may read them); mq[h]: dK has read C's q-chunks 2h,
-  // 2h+1; accq: dQ has read u-groups 0-1 of C; kfree: the workers have split K out of QR
-  __shared__ __align__(8) uint64_t ld1, ld2, w1[4], w2, w3, m1, mq[2], accq, accf, qfree, kfree, wsync, drain;
+  // 2h+1; w3: C is in tensor memory and K split (dQ may run, the next S may land); kfree: the workers
+  // have split K out of QR
+  __shared__ __align__(8) uint64_t ld1, ld2, w1[4], w2, w3, m1, mq[2], accf, qfree, kfree, wsync, drain;
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
 
@@ -365,7 +366,6 @@ __global__ void __launch_bounds__(320, 1)
     mbar_init(&w2, 256);
     mbar_init(&w3, 256);
     mbar_init(&m1, 1);
-    mbar_init(&accq, 1);
     mbar_init(&accf, 1);
     mbar_init(&qfree, 256);
     mbar_init(&kfree, 256);
@@ -375,13 +375,13 @@ __global__ void __launch_bounds__(320, 1)
     fence_barrier_init();
   }
   if (warp == 8) {
-    tmem_alloc(&tmem_slot, 128);
+    tmem_alloc(&tmem_slot, 512);  // one CTA per SM (217 KB of shared memory)
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = tmem_slot;  // dV at column 0, dK at 32, dQ at 64
+  const uint32_t tmem = tmem_slot;  // dV at column 0, dK at 32, dQ at 64; C hi at 128, lo at 256
   pdl_wait();
   pdl_trigger();
   const float inv_koef = 1.f / koef;
@@ -438,15 +438,13 @@ __global__ void __launch_bounds__(320, 1)
         }
         load_vqg(tn, n + 1);
         ++issued1;
-        if (!mbar_wait(&accq, par, &abort_flag)) {
+        // S / C's shared tiles are free once dK has read them (mq[1], above) and the workers have
+        // copied C into tensor memory (w3)
+        if (!mbar_wait(&w3, par, &abort_flag)) {
           fail(kErrEmptyWait);
           break;
         }
         load_s(tn, 0);
-        if (!mbar_wait(&accf, par, &abort_flag)) {
-          fail(kErrEmptyWait);
-          break;
-        }
         load_s(tn, 2);
       }
       // wait for the last copies into shared memory before exiting
@@ -462,9 +460,6 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t b16 = smem_u32(sm) >> 4;
     auto Sm = [&](uint32_t base, int s) { return desc_at<16384u, 512u, 1u>(b16 + (base >> 4) + 64u * s); };
     auto Tm = [&](uint32_t base, int s) { return desc_at<4096u, 512u, 1u>(b16 + (base >> 4) + 64u * s); };
-    auto Sk = [&](uint32_t base, int s) {
-      return desc_at<16u, 1024u, 2u>(b16 + (base >> 4) + 1024u * (s >> 2) + 2u * (s & 3));
-    };
     int n = 0;
     bool ok = true;
     for (int t = blockIdx.x; t < items && ok && !abort_flag; t += gridDim.x, ++n) {
@@ -512,7 +507,7 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
       __syncwarp();
-      // dQ' = C K  (C as the K-major operand: u-group s/4, 32 bytes per 8-wide k step; K split in GH/GL)
+      // dQ' = C K  (C from tensor memory, lane q = row q, 8 columns of u per k step; K split in GH/GL)
       if (!mbar_wait(&w3, par, &abort_flag)) {
         if (lane == 0) fail(kErrFullWait);
         break;
@@ -521,10 +516,9 @@ __global__ void __launch_bounds__(320, 1)
       if (lane == 0) {
 #pragma unroll
         for (int s = 0; s < 16; ++s) {
-          mma_tf32(tmem + 64, Sk(C::SL, s), Tm(gbuf, s), IDESC_KM, s != 0 ? 1u : 0u);
-          mma_tf32(tmem + 64, Sk(C::SH, s), Tm(gbuf + 16384u, s), IDESC_KM, 1u);
-          mma_tf32(tmem + 64, Sk(C::SH, s), Tm(gbuf, s), IDESC_KM, 1u);
-          if (s == 7) mma_commit(&accq);  // u-groups 0-1 of C read: the next item's S may land there
+          mma_tf32_ta(tmem + 64, tmem + 256 + 8 * s, Tm(gbuf, s), IDESC_KM, s != 0 ? 1u : 0u);
+          mma_tf32_ta(tmem + 64, tmem + 128 + 8 * s, Tm(gbuf + 16384u, s), IDESC_KM, 1u);
+          mma_tf32_ta(tmem + 64, tmem + 128 + 8 * s, Tm(gbuf, s), IDESC_KM, 1u);
         }
         mma_commit(&accf);
       }
@@ -658,48 +652,44 @@ __global__ void __launch_bounds__(320, 1)
         for (int i = 0; i < 4; ++i) store_split_full(sm + gbuf, sm + gbuf + 16384u, 16u * (wt + 256 * i), kv[i]);
       }
       mbar_arrive(&kfree);  // QR (raw K) and VR read: the loader may bring the next item's Q and V rows
-      // W3, two 32-row chunks of q at a time once dK has read them: permute C's rows to the K-major
-      // swizzle.  Only the hi (full fp32) rows are read; the permuted lo rows are computed from them.
-      // Thread wt: chunk 2s + wt/128, u-group (wt/32)%4, row q = 32 * chunk + wt%32.
-      bool ok = true;
-      for (int st2 = 0; st2 < 2; ++st2) {
-        if (!mbar_wait(&mq[st2], par, &abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const int q = 32 * (2 * st2 + (wt >> 7)) + (wt & 31);
-        const uint32_t roff = ((wt >> 5) & 3) * 16384 + q * 128;
-        uint8_t *base = sm + C::SH + roff;
-        uint8_t *lbase = sm + C::SL + roff;
-        // g[j] = physical granule (j + q) % 8: the eight lanes of a shared-memory phase touch eight
-        // different 16-byte bank groups although their rows are 128 bytes apart
-        const int rot = q & 7;
-        float4 g[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) g[i] = *reinterpret_cast<const float4 *>(base + 16 * ((i + rot) & 7));
-        // register-only select of g[i] (a runtime index into g would go to local memory)
-        auto pick = [&](int i) -> float4 {
-          float4 v = g[0];
-#pragma unroll
-          for (int k = 1; k < 8; ++k) v = (i == k) ? g[k] : v;
-          return v;
-        };
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int p = (i + rot) & 7;                                 // destination: K-major granule p
-          const int l16 = (p ^ q) & 7;                                 // the logical granule stored there
-          const int from = 2 * (((l16 >> 1) ^ q) & 3) + (l16 & 1);    // its place in the MN-major row
-          const float4 v = pick((from - rot) & 7);
-          *reinterpret_cast<float4 *>(base + 16 * p) = v;
-          *reinterpret_cast<float4 *>(lbase + 16 * p) =
-              make_float4(v.x - tf32_hi(v.x), v.y - tf32_hi(v.y), v.z - tf32_hi(v.z), v.w - tf32_hi(v.w));
-        }
-      }
-      if (!ok) {
-        fail(kErrDoneWait);
+      // W3: C's rows into tensor memory as dQ's A operand (lane q = row q, one column per u: hi at
+      // columns 128-255, lo at 256-383), read from the hi tiles W2 wrote (dK reads the same tiles
+      // meanwhile; nothing waits for it).  Warp w takes rows 32 (w % 4) .. +31, its tensor-memory
+      // lanes, and u-groups 2 (w / 4) and 2 (w / 4) + 1.  Every thread's W2 rows are written first.
+      if (!worker_sync()) {
+        fail(kErrFullWait);
         break;
       }
+      {
+        const int q = 32 * (warp & 3) + lane;
+        const uint32_t trow = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int ug = 2 * (warp >> 2) + h2;
+          const uint8_t *row = sm + C::SH + 16384u * ug + 128u * q;
+          uint32_t hi[32], lo[32];
+#pragma unroll
+          for (int gi = 0; gi < 4; ++gi)
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+              // logical 32-byte granule gi of an MN-major row sits at granule gi ^ (q % 4)
+              const float4 v = *reinterpret_cast<const float4 *>(row + 16 * ((((gi ^ q) & 3) << 1) | hf));
+              const int u = 8 * gi + 4 * hf;
+              hi[u] = __float_as_uint(v.x);
+              hi[u + 1] = __float_as_uint(v.y);
+              hi[u + 2] = __float_as_uint(v.z);
+              hi[u + 3] = __float_as_uint(v.w);
+              lo[u] = __float_as_uint(v.x - tf32_hi(v.x));
+              lo[u + 1] = __float_as_uint(v.y - tf32_hi(v.y));
+              lo[u + 2] = __float_as_uint(v.z - tf32_hi(v.z));
+              lo[u + 3] = __float_as_uint(v.w - tf32_hi(v.w));
+            }
+          tmem_st32(trow + 128 + 32 * ug, hi);
+          tmem_st32(trow + 256 + 32 * ug, lo);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
       fence_proxy_async_smem();
       mbar_arrive(&w3);
       // epilogue: rows r of tensor-memory lane quarter w % 4; warps 0-3 store dV and the first 16
@@ -777,7 +767,7 @@ __global__ void __launch_bounds__(320, 1)
   __syncthreads();
   if (warp == 8) {
     tc_fence_after();
-    tmem_dealloc(tmem, 128);
+    tmem_dealloc(tmem, 512);
   }
 }
 
