@@ -316,17 +316,17 @@ __global__ void __launch_bounds__(448, 1)
 //            one holds G (later K, dQ's B operand), the other G o Q
 //   QR       raw Q, later raw K, [row][32 d], 16 KB
 //   V0, AV   128 floats each;  VR: V[u][0..3] per row (TMA), the source of V0
+// Tensor memory (512 columns): dV, dK, dQ accumulators at columns 0, 32, 64; C's rows hi / lo at
+// 128-255 / 256-383 (lane q = row q, column u), dQ's A operand.
 // S, G, Q and K tiles use the 128-byte swizzle with 32-byte granules (MN-major operands of dV and
-// dK).  For dQ, C is the K-major operand: its rows are already where the K-major layout keeps
-// them, and only the 16-byte granules inside each 128-byte row are permuted (32-byte granules
-// XOR q%4  ->  16-byte granules XOR q%8).  Score rows q >= units (the next sequence) are zeroed,
-// so they contribute nothing to the sums over q.
-// Overlap: dV and dK reduce over q in 8-row steps, so the workers hand S over (and take C back)
-// in 32-row chunks of q, each with its own barrier; G o Q and A are formed while dV runs, K is
-// split while dK runs.  The next item's V rows, Q and G load as soon as dK has read G o Q (the
-// next G goes into that pair) and K has been split out of QR, and its S in two halves as dQ
-// passes u-groups 0-1 and finishes (dQ's factor G is read from global memory, so the epilogue
-// needs no shared tile).
+// dK).  Score rows q >= units (the next sequence) are zeroed, so they contribute nothing to the sums
+// over q.
+// Overlap: dV reduces over q in 8-row steps, so the workers hand S over in 32-row chunks of q, each
+// with its own barrier; G o Q and A are formed while dV runs, K is split and C copied into tensor
+// memory while dK runs.  The next item's V rows, Q and G load as soon as dK has read G o Q (the next
+// G goes into that pair) and K has been split out of QR, and its S once dK has read C and the
+// workers have copied it (dQ's factor G is read from global memory, so the epilogue needs no shared
+// tile).
 struct GradCfg {
   static constexpr uint32_t SH = 0, SL = 65536, GH = 131072, GL = 147456, QR = 163840, XH = 180224, XL = 196608;
   static constexpr uint32_t V0 = 212992, AV = V0 + 512, VR = AV + 512, END = VR + 2048;
