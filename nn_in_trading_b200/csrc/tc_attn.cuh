@@ -639,6 +639,21 @@ __global__ void __launch_bounds__(320, 1)
       }
       fence_proxy_async_smem();
       mbar_arrive(&w2);
+      // Results leave as soon as their products are complete, each warp storing half of its rows'
+      // 32 features (warps 0-3 the first 16, warps 4-7 the last): row r of tensor-memory lane
+      // quarter w % 4, 64 bytes per row and result.  dV is complete (m1, waited above).
+      const int r = (warp & 3) * 32 + lane, f0 = 16 * (warp >> 2);
+      const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)f0;
+      float *grow = qkv_g + (size_t)(b * U + r) * rs + f0;  // 32-byte aligned: 3*H*D floats per row
+      {
+        float v[16];
+        tmem_ld16(tl + 0, v);
+        if (r < U) {
+          float *dv = grow + (size_t)(2 * H + h) * D;
+          st_global_v8(dv, v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7]);
+          st_global_v8(dv + 8, v[8], v[9], v[10], v[11], v[12], v[13], v[14], v[15]);
+        }
+      }
       // raw K -> GH / GL (dQ's B operand) while dK runs: dV has finished reading G
       if (!mbar_wait(&ld2, par, &abort_flag)) {
         fail(kErrFullWait);
@@ -692,65 +707,55 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_before();
       fence_proxy_async_smem();
       mbar_arrive(&w3);
-      // epilogue: rows r of tensor-memory lane quarter w % 4; warps 0-3 store dV and the first 16
-      // features of dK, warps 4-7 dQ and the last 16 of dK, 32 bytes per store.  The G row dQ needs is loaded (from L2:
-      // TMA brought it in) before the wait for the products, so its latency overlaps them.
-      const int r = (warp & 3) * 32 + lane;
-      float4 gq[8];
-      if (warp >= 4 && r < U) {
-        const float4 *gr = reinterpret_cast<const float4 *>(grad + (size_t)(b * U + r) * H * D + (size_t)h * D);
+      // dK, once its products are complete, while dQ runs; dQ's factor G (its row in global memory:
+      // TMA brought it into L2) loads before the wait for dQ, so its latency overlaps the products
+      float4 gq[4];
+      if (r < U) {
+        const float4 *gr =
+            reinterpret_cast<const float4 *>(grad + (size_t)(b * U + r) * H * D + (size_t)h * D + f0);
 #pragma unroll
-        for (int l16 = 0; l16 < 8; ++l16) gq[l16] = __ldg(gr + l16);
+        for (int l16 = 0; l16 < 4; ++l16) gq[l16] = __ldg(gr + l16);
+      }
+      if (!mbar_wait(&mq[1], par, &abort_flag)) {
+        fail(kErrDoneWait);
+        break;
+      }
+      tc_fence_after();
+      {
+        float k[16];
+        tmem_ld16(tl + 32, k);
+        if (r < U) {
+          float *dk = grow + (size_t)(H + h) * D;
+          st_global_v8(dk, k[0] * inv_koef, k[1] * inv_koef, k[2] * inv_koef, k[3] * inv_koef, k[4] * inv_koef,
+                       k[5] * inv_koef, k[6] * inv_koef, k[7] * inv_koef);
+          st_global_v8(dk + 8, k[8] * inv_koef, k[9] * inv_koef, k[10] * inv_koef, k[11] * inv_koef,
+                       k[12] * inv_koef, k[13] * inv_koef, k[14] * inv_koef, k[15] * inv_koef);
+        }
       }
       if (!mbar_wait(&accf, par, &abort_flag)) {
         fail(kErrDoneWait);
         break;
       }
       tc_fence_after();
-      const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-      float *grow = qkv_g + (size_t)(b * U + r) * rs;  // 32-byte aligned: 3*H*D floats per row
-      float *dk = grow + (size_t)(H + h) * D;
-      if (warp < 4) {
-        float v[32], k[32];
-        tmem_ld32(tl + 0, v);
-        tmem_ld32(tl + 32, k);
+      {
+        float v[16];
+        tmem_ld16(tl + 64, v);
         if (r < U) {
-          float *dv = grow + (size_t)(2 * H + h) * D;
+          float gf[16];
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            st_global_v8(dv + 8 * j, v[8 * j], v[8 * j + 1], v[8 * j + 2], v[8 * j + 3], v[8 * j + 4], v[8 * j + 5],
-                         v[8 * j + 6], v[8 * j + 7]);
-#pragma unroll
-          for (int j = 0; j < 2; ++j)
-            st_global_v8(dk + 8 * j, k[8 * j] * inv_koef, k[8 * j + 1] * inv_koef, k[8 * j + 2] * inv_koef,
-                         k[8 * j + 3] * inv_koef, k[8 * j + 4] * inv_koef, k[8 * j + 5] * inv_koef,
-                         k[8 * j + 6] * inv_koef, k[8 * j + 7] * inv_koef);
-        }
-      } else {
-        float v[32], k[32];
-        tmem_ld32(tl + 64, v);
-        tmem_ld32(tl + 32, k);
-        if (r < U) {
-          float *dq = grow + (size_t)h * D;
-          float gf[32];
-#pragma unroll
-          for (int l16 = 0; l16 < 8; ++l16) {
+          for (int l16 = 0; l16 < 4; ++l16) {
             gf[4 * l16] = nan0(gq[l16].x);
             gf[4 * l16 + 1] = nan0(gq[l16].y);
             gf[4 * l16 + 2] = nan0(gq[l16].z);
             gf[4 * l16 + 3] = nan0(gq[l16].w);
           }
+          float *dq = grow + (size_t)h * D;
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
+          for (int j = 0; j < 2; ++j)
             st_global_v8(dq + 8 * j, gf[8 * j] * v[8 * j] * inv_koef, gf[8 * j + 1] * v[8 * j + 1] * inv_koef,
                          gf[8 * j + 2] * v[8 * j + 2] * inv_koef, gf[8 * j + 3] * v[8 * j + 3] * inv_koef,
                          gf[8 * j + 4] * v[8 * j + 4] * inv_koef, gf[8 * j + 5] * v[8 * j + 5] * inv_koef,
                          gf[8 * j + 6] * v[8 * j + 6] * inv_koef, gf[8 * j + 7] * v[8 * j + 7] * inv_koef);
-#pragma unroll
-          for (int j = 2; j < 4; ++j)
-            st_global_v8(dk + 8 * j, k[8 * j] * inv_koef, k[8 * j + 1] * inv_koef, k[8 * j + 2] * inv_koef,
-                         k[8 * j + 3] * inv_koef, k[8 * j + 4] * inv_koef, k[8 * j + 5] * inv_koef,
-                         k[8 * j + 6] * inv_koef, k[8 * j + 7] * inv_koef);
         }
       }
       tc_fence_before();
