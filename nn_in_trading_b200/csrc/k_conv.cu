@@ -308,6 +308,8 @@ __device__ __forceinline__ void adam_conv_step(float *w, float *m, float *v, siz
 
 __global__ void adam_conv_apply_kernel(float *w, float *m, float *v, GradSrc G, size_t n, float l, float b1,
                                        float b2) {
+  pdl_wait();
+  pdl_trigger();
   size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (i >= n) return;
   adam_conv_step(w, m, v, i, G(i), l, b1, b2);
@@ -318,6 +320,8 @@ __global__ void adam_conv_apply_kernel(float *w, float *m, float *v, GradSrc G, 
 // per partial), then a shared-memory reduction and the update by the first group.
 __global__ void adam_conv_apply_split_kernel(float *w, float *m, float *v, GradSrc G, size_t n, float l, float b1,
                                              float b2) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[8][33];
   const size_t i = blockIdx.x * (size_t)32 + threadIdx.x;
   float s = 0.f;
@@ -372,17 +376,14 @@ static int adam_conv_apply_src(const Launch &Lc, GradSrc G) {
   float *w = L.buf(0, n), *m = L.buf(3, n), *v = L.buf(4, n);
   if (!w || !m || !v) return NN_ERR_BOUNDS;
   if (G.splits > 4)
-    adam_conv_apply_split_kernel<<<(unsigned)((n + 31) / 32), dim3(32, 8), 0, L.stream>>>(w, m, v, G, n, L.f(6), L.f(7),
-                                                                                          L.f(8));
+    NN_LAUNCH_PDL(L, adam_conv_apply_split_kernel, (unsigned)((n + 31) / 32), dim3(32, 8), 0, L.stream, w, m, v, G, n,
+                  L.f(6), L.f(7), L.f(8));
   else
-    adam_conv_apply_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(w, m, v, G, n, L.f(6), L.f(7), L.f(8));
-  NN_CHECK_LAUNCH(L);
+    NN_LAUNCH_PDL(L, adam_conv_apply_kernel, grid1d(n, 256), 256, 0, L.stream, w, m, v, G, n, L.f(6), L.f(7), L.f(8));
   if (L.norm_rows > 0) {
     // the NormalizeWeights the runner folded into this update: a reduction over many split-K partials
     // keeps every weight its own thread, so the rows are normalised by the usual kernel afterwards
-    normalize_weights_kernel<<<ceil_div((size_t)L.norm_rows * 32, 256), 256, 0, L.stream>>>(w, L.norm_rows,
-                                                                                         L.norm_dim);
-    NN_CHECK_LAUNCH(L);
+    NN_LAUNCH_PDL(L, normalize_weights_kernel, ceil_div((size_t)L.norm_rows * 32, 256), 256, 0, L.stream, w, L.norm_rows, L.norm_dim);
   }
   return NN_OK;
 }

@@ -20,6 +20,8 @@ namespace nn {
 // out[i] = scale * sum_k p[k * stride + i]: block (32 entries, 8 split groups), each thread summing
 // every 8th partial of one entry, then a shared-memory reduction.
 __global__ void reduce_partials_kernel(float *out, GradSrc src, size_t n) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[8][33];
   const size_t i = blockIdx.x * (size_t)32 + threadIdx.x;
   float s = 0.f;
@@ -36,6 +38,8 @@ __global__ void reduce_partials_kernel(float *out, GradSrc src, size_t n) {
 
 __global__ void colsum_partial_kernel(float *p, const float *g, int M, int rows, long long ld, int kchunk, int ldp,
                                       int col) {
+  pdl_wait();
+  pdl_trigger();
   int m = blockIdx.x * blockDim.x + threadIdx.x;
   if (m >= M) return;
   int r0 = blockIdx.y * kchunk, r1 = min(rows, r0 + kchunk);
@@ -46,6 +50,8 @@ __global__ void colsum_partial_kernel(float *p, const float *g, int M, int rows,
 
 __global__ void colsum_rows_kernel(float *p, const float *g, int M, int rows, long long ld, int kchunk, int ldp,
                                    int col) {
+  pdl_wait();
+  pdl_trigger();
   // block (32 columns, 32 row groups): every warp reads one 128-byte row segment per load, and each
   // thread keeps four independent sums so that four loads are in flight
   __shared__ float red[32][33];
@@ -74,6 +80,8 @@ __global__ void colsum_rows_kernel(float *p, const float *g, int M, int rows, lo
 
 __global__ void wgrad_small_m_kernel(float *p, const float *A, long long lda, const float *X, long long ldx, int M,
                                      int N, int rows, int kchunk, int ldp) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[8][kSmallM][33];
   const int n = blockIdx.x * 32 + threadIdx.x;  // n == N: the bias column (input 1)
   const int r0 = blockIdx.y * kchunk, r1 = min(rows, r0 + kchunk);
@@ -141,6 +149,8 @@ __global__ void ff_rows_kernel(const float *__restrict__ w, const float *__restr
 constexpr int kSkinny = 16;
 __global__ void ff_skinny_kernel(const float *__restrict__ w, const float *__restrict__ x, float *__restrict__ y,
                                  int inputs, int outputs, int B, int act) {
+  pdl_wait();
+  pdl_trigger();
   const int b = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
   if (b >= B) return;
   const float *xb = x + (size_t)b * inputs;
@@ -165,6 +175,8 @@ __global__ void ff_skinny_kernel(const float *__restrict__ w, const float *__res
 // ascending.
 __global__ void chg_skinny_kernel(const float *__restrict__ w, const float *__restrict__ g, const float *__restrict__ o,
                                   float *__restrict__ ig, int inputs, int outputs, int B, int act) {
+  pdl_wait();
+  pdl_trigger();
   const size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (t >= (size_t)B * inputs) return;
   const int i = (int)(t % inputs);
@@ -217,11 +229,9 @@ static int k_feedforward(Launch &L) {
   }
   if (L.B <= 4) {
     unsigned blocks = ceil_div((size_t)outputs * 32, 256);
-    cudaError_t e = launch_pdl(ff_rows_kernel<4>, blocks, 256, 0, L.stream, w, x, y, inputs, outputs, L.B, act);
-    if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
+    NN_LAUNCH_PDL(L, ff_rows_kernel<4>, blocks, 256, 0, L.stream, w, x, y, inputs, outputs, L.B, act);
   } else if (outputs <= kSkinny) {
-    ff_skinny_kernel<<<ceil_div((size_t)L.B * 32, 256), 256, 0, L.stream>>>(w, x, y, inputs, outputs, L.B, act);
-    NN_CHECK_LAUNCH(L);
+    NN_LAUNCH_PDL(L, ff_skinny_kernel, ceil_div((size_t)L.B * 32, 256), 256, 0, L.stream, w, x, y, inputs, outputs, L.B, act);
   } else {
     FastShape fs{L.B, outputs, inputs, 1, 1, 0, x, inputs, 0, w, ld, 0};
     cudaError_t e = tma_store_ok(y, outputs, 0, 1, outputs)
@@ -252,8 +262,7 @@ static int k_calc_output_gradient(Launch &L) {
   size_t n = (size_t)L.nd.g[0] * L.B;
   float *t = L.buf(0, n), *o = L.buf(1, n), *ig = L.buf(2, n);
   if (!t || !o || !ig) return NN_ERR_BOUNDS;
-  cudaError_t e = launch_pdl(out_grad_kernel, grid1d(n, 256), 256, 0, L.stream, t, o, ig, n, L.i(3));
-  if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
+  NN_LAUNCH_PDL(L, out_grad_kernel, grid1d(n, 256), 256, 0, L.stream, t, o, ig, n, L.i(3));
   return NN_OK;
 }
 
@@ -330,22 +339,19 @@ static int k_calc_hidden_gradient(Launch &L) {
   if (!w || !g || !o || !ig) return NN_ERR_BOUNDS;
   if (L.B <= 4) {
     // column groups as wide as still give most SMs a CTA
-    cudaError_t e;
     if (inputs >= 32 * 148)
-      e = launch_pdl(chg_cols_kernel<4, 32>, ceil_div(inputs, 32), kChgWarps * 32, 0, L.stream, w, g, o, ig, inputs,
-                     outputs, L.B, act);
+      NN_LAUNCH_PDL(L, (chg_cols_kernel<4, 32>), ceil_div(inputs, 32), kChgWarps * 32, 0, L.stream, w, g, o, ig,
+                    inputs, outputs, L.B, act);
     else if (inputs >= 8 * 74)
-      e = launch_pdl(chg_cols_kernel<4, 8>, ceil_div(inputs, 8), kChgWarps * 32, 0, L.stream, w, g, o, ig, inputs,
-                     outputs, L.B, act);
+      NN_LAUNCH_PDL(L, (chg_cols_kernel<4, 8>), ceil_div(inputs, 8), kChgWarps * 32, 0, L.stream, w, g, o, ig, inputs,
+                    outputs, L.B, act);
     else
-      e = launch_pdl(chg_cols_kernel<4, 4>, ceil_div(inputs, 4), kChgWarps * 32, 0, L.stream, w, g, o, ig, inputs,
-                     outputs, L.B, act);
-    if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
+      NN_LAUNCH_PDL(L, (chg_cols_kernel<4, 4>), ceil_div(inputs, 4), kChgWarps * 32, 0, L.stream, w, g, o, ig, inputs,
+                    outputs, L.B, act);
     return NN_OK;
   }
   if (outputs <= kSkinny) {
-    chg_skinny_kernel<<<grid1d((size_t)L.B * inputs, 256), 256, 0, L.stream>>>(w, g, o, ig, inputs, outputs, L.B, act);
-    NN_CHECK_LAUNCH(L);
+    NN_LAUNCH_PDL(L, chg_skinny_kernel, grid1d((size_t)L.B * inputs, 256), 256, 0, L.stream, w, g, o, ig, inputs, outputs, L.B, act);
     return NN_OK;
   }
   FastShape fs{L.B, inputs, outputs, 1, 1, 0, g, outputs, 0, w, ld, 0};
@@ -394,6 +400,8 @@ __device__ __forceinline__ void adam_dense_step(float *w, float *m, float *v, si
 
 __global__ void adam_dense_apply_kernel(float *w, float *m, float *v, GradSrc G, int n_out, int n_col, int inputs,
                                         float l, float b1, float b2) {
+  pdl_wait();
+  pdl_trigger();
   size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (t >= (size_t)n_out * n_col) return;
   int i = (int)(t / n_col), j = (int)(t % n_col);
@@ -403,6 +411,8 @@ __global__ void adam_dense_apply_kernel(float *w, float *m, float *v, GradSrc G,
 // The same with many split-K partials: block (32 weights, 8 split groups), as reduce_partials_kernel.
 __global__ void adam_dense_apply_split_kernel(float *w, float *m, float *v, GradSrc G, int n_out, int n_col,
                                               int inputs, float l, float b1, float b2) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[8][33];
   const size_t t = blockIdx.x * (size_t)32 + threadIdx.x, n = (size_t)n_out * n_col;
   float s = 0.f;
@@ -421,6 +431,8 @@ __global__ void adam_dense_apply_split_kernel(float *w, float *m, float *v, Grad
 // Single-sample fused kernel: exactly the reference's per-weight arithmetic.
 __global__ void adam_dense_fused_kernel(float *w, const float *g, const float *x, float *m, float *v, int n_out,
                                         int n_col, int inputs, float l, float b1, float b2) {
+  pdl_wait();
+  pdl_trigger();
   size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (t >= (size_t)n_out * n_col) return;
   int i = (int)(t / n_col), j = (int)(t % n_col);
@@ -478,17 +490,13 @@ static int adam_dense_apply_src(const Launch &Lc, GradSrc G) {
   if (!w || !m || !v) return NN_ERR_BOUNDS;
   size_t n = (size_t)s.n_out * s.n_col;
   if (G.splits > 4)
-    adam_dense_apply_split_kernel<<<(unsigned)((n + 31) / 32), dim3(32, 8), 0, L.stream>>>(
-        w, m, v, G, s.n_out, s.n_col, s.inputs, L.f(6), L.f(7), L.f(8));
+    NN_LAUNCH_PDL(L, adam_dense_apply_split_kernel, (unsigned)((n + 31) / 32), dim3(32, 8), 0, L.stream, w, m, v, G,
+                  s.n_out, s.n_col, s.inputs, L.f(6), L.f(7), L.f(8));
   else
-    adam_dense_apply_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(w, m, v, G, s.n_out, s.n_col, s.inputs, L.f(6),
-                                                                  L.f(7), L.f(8));
-  NN_CHECK_LAUNCH(L);
+    NN_LAUNCH_PDL(L, adam_dense_apply_kernel, grid1d(n, 256), 256, 0, L.stream, w, m, v, G, s.n_out, s.n_col, s.inputs, L.f(6), L.f(7), L.f(8));
   if (L.norm_rows > 0) {
     // the folded NormalizeWeights after a batched update (see adam_conv_apply_src)
-    normalize_weights_kernel<<<ceil_div((size_t)L.norm_rows * 32, 256), 256, 0, L.stream>>>(w, L.norm_rows,
-                                                                                         L.norm_dim);
-    NN_CHECK_LAUNCH(L);
+    NN_LAUNCH_PDL(L, normalize_weights_kernel, ceil_div((size_t)L.norm_rows * 32, 256), 256, 0, L.stream, w, L.norm_rows, L.norm_dim);
   }
   return NN_OK;
 }
@@ -505,16 +513,13 @@ static int k_update_weights_adam(Launch &L) {
   if (!w || !g || !x || !m || !v) return NN_ERR_BOUNDS;
   if (L.B == 1 && !L.deferred()) {
     if (L.norm_rows > 0) {
-      cudaError_t e = launch_pdl(update_normalize_rows_flat_kernel<DenseAdamSampleStep>, L.norm_rows, 256, 0, L.stream,
-                                 w, L.norm_rows, L.norm_dim,
-                                 DenseAdamSampleStep{w, m, v, g, x, s.n_col, s.inputs, L.f(6), L.f(7), L.f(8)});
-      if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
+      NN_LAUNCH_PDL(L, update_normalize_rows_flat_kernel<DenseAdamSampleStep>, L.norm_rows, 256, 0, L.stream, w,
+                    L.norm_rows, L.norm_dim,
+                    DenseAdamSampleStep{w, m, v, g, x, s.n_col, s.inputs, L.f(6), L.f(7), L.f(8)});
       return NN_OK;
     }
     size_t n = (size_t)s.n_out * s.n_col;
-    adam_dense_fused_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(w, g, x, m, v, s.n_out, s.n_col, s.inputs,
-                                                                  L.f(6), L.f(7), L.f(8));
-    NN_CHECK_LAUNCH(L);
+    NN_LAUNCH_PDL(L, adam_dense_fused_kernel, grid1d(n, 256), 256, 0, L.stream, w, g, x, m, v, s.n_out, s.n_col, s.inputs, L.f(6), L.f(7), L.f(8));
     return NN_OK;
   }
   GradSrc src;
@@ -678,6 +683,8 @@ static int k_update_weights_momentum(Launch &L) {
 // NeuroNet.cl:1498-1525: rows of `dimension` weights rescaled to unit norm when
 // the norm exceeds 1; the 10x pre-scaling retry handles overflow.
 __global__ void normalize_weights_kernel(float *buf, int rows, int dim) {
+  pdl_wait();
+  pdl_trigger();
   int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   int lane = threadIdx.x & 31;
   if (warp >= rows) return;
@@ -722,8 +729,7 @@ static int k_normalize_weights(Launch &L) {
   if (dim < 0) return L.fail(NN_ERR_ARG, "NormalizeWeights: negative dimension");
   float *b = L.buf(0, (size_t)rows * dim);
   if (!b) return NN_ERR_BOUNDS;
-  normalize_weights_kernel<<<ceil_div((size_t)rows * 32, 256), 256, 0, L.stream>>>(b, rows, dim);
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, normalize_weights_kernel, ceil_div((size_t)rows * 32, 256), 256, 0, L.stream, b, rows, dim);
   return NN_OK;
 }
 
@@ -755,6 +761,8 @@ static int k_deactivation(Launch &L) {  // NeuroNet.cl:5811-5823
 }
 
 __global__ void soft_update_kernel(float *t, const float *s, size_t n, float tau) {
+  pdl_wait();
+  pdl_trigger();
   size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (i < n) t[i] = s[i] * tau + (1.f - tau) * t[i];
 }
@@ -762,13 +770,14 @@ static int k_soft_update(Launch &L) {  // NeuroNet.cl:3864-3871
   size_t n = L.nd.g[0];
   float *t = L.buf(0, n), *s = L.buf(1, n);
   if (!t || !s) return NN_ERR_BOUNDS;
-  soft_update_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(t, s, n, L.f(2));
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, soft_update_kernel, grid1d(n, 256), 256, 0, L.stream, t, s, n, L.f(2));
   return NN_OK;
 }
 
 __global__ void soft_update_adam_kernel(float *t, const float *s, float *m, float *v, size_t n, float tau, float b1,
                                         float b2) {
+  pdl_wait();
+  pdl_trigger();
   size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (i >= n) return;
   float mm = m[i], vv = v[i], weight = t[i];
@@ -784,8 +793,7 @@ static int k_soft_update_adam(Launch &L) {  // NeuroNet.cl:3875-3899
   size_t n = L.nd.g[0];
   float *t = L.buf(0, n), *s = L.buf(1, n), *m = L.buf(2, n), *v = L.buf(3, n);
   if (!t || !s || !m || !v) return NN_ERR_BOUNDS;
-  soft_update_adam_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(t, s, m, v, n, L.f(4), L.f(5), L.f(6));
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, soft_update_adam_kernel, grid1d(n, 256), 256, 0, L.stream, t, s, m, v, n, L.f(4), L.f(5), L.f(6));
   return NN_OK;
 }
 

@@ -30,6 +30,8 @@ namespace nn {
 // gates: one thread per (v, gate, neuron), reads h(t-1) and x(t), writes concatenated.
 __global__ void lstm_gates_kernel(const float *__restrict__ x, const float *__restrict__ w,
                                   const float *__restrict__ h, float *__restrict__ cat, int H, int in, int V) {
+  pdl_wait();
+  pdl_trigger();
   size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (t >= (size_t)V * 4 * H) return;
   int id = (int)(t % H);
@@ -66,6 +68,8 @@ __global__ void lstm_gates_kernel(const float *__restrict__ x, const float *__re
 // cell: memory and output update from the gate values.
 __global__ void lstm_cell_kernel(const float *__restrict__ cat, float *__restrict__ mem, float *__restrict__ out,
                                  int H, int V) {
+  pdl_wait();
+  pdl_trigger();
   size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (t >= (size_t)V * H) return;
   int id = (int)(t % H);
@@ -92,6 +96,8 @@ static int lstm_shape(Launch &L, int *H, int *V) {
 // or, in the tail loop that runs otherwise, when j < H.
 __global__ void lstm_pack_hx_kernel(const float *__restrict__ h, const float *__restrict__ x,
                                     float *__restrict__ opnd, int H, int in, int V) {
+  pdl_wait();
+  pdl_trigger();
   const size_t cols = (size_t)H + in;
   size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (t >= (size_t)V * cols) return;
@@ -112,6 +118,8 @@ __global__ void lstm_pack_hx_kernel(const float *__restrict__ h, const float *__
 __global__ void lstm_gates_cell_kernel(const float *__restrict__ P, int splits, size_t pstride, int ldp,
                                        const float *__restrict__ w, int ws, int bcol, float *__restrict__ cat,
                                        float *__restrict__ mem, float *__restrict__ out, int H, int V) {
+  pdl_wait();
+  pdl_trigger();
   size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (t >= (size_t)V * H) return;
   int id = (int)(t % H);
@@ -177,21 +185,16 @@ static int k_lstm_feed_forward(Launch &L) {
     if (!opnd) return NN_ERR_CUDA;
     float *P = opnd + nop;  // 16-byte aligned: H + in is a multiple of 4
     fs.A = opnd;
-    lstm_pack_hx_kernel<<<grid1d(nop, 256), 256, 0, L.stream>>>(out, x, opnd, H, in, V);
-    NN_CHECK_LAUNCH(L);
+    NN_LAUNCH_PDL(L, lstm_pack_hx_kernel, grid1d(nop, 256), 256, 0, L.stream, out, x, opnd, H, in, V);
     // the product's K-slice partials; the gate kernel sums them and adds the bias column
     cudaError_t e = gemm_f32_wb<false, false>(L, fs, PartialStoreTma{{P, V, ldp, 1}});
     if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
     L.counted();
-    lstm_gates_cell_kernel<<<grid1d((size_t)V * H, 256), 256, 0, L.stream>>>(P, splits, pstride, ldp, w, ws, K, cat,
-                                                                             mem, out, H, V);
-    NN_CHECK_LAUNCH(L);
+    NN_LAUNCH_PDL(L, lstm_gates_cell_kernel, grid1d((size_t)V * H, 256), 256, 0, L.stream, P, splits, pstride, ldp, w, ws, K, cat, mem, out, H, V);
     return NN_OK;
   }
-  lstm_gates_kernel<<<grid1d((size_t)V * 4 * H, 256), 256, 0, L.stream>>>(x, w, out, cat, H, in, V);
-  NN_CHECK_LAUNCH(L);
-  lstm_cell_kernel<<<grid1d((size_t)V * H, 256), 256, 0, L.stream>>>(cat, mem, out, H, V);
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, lstm_gates_kernel, grid1d((size_t)V * 4 * H, 256), 256, 0, L.stream, x, w, out, cat, H, in, V);
+  NN_LAUNCH_PDL(L, lstm_cell_kernel, grid1d((size_t)V * H, 256), 256, 0, L.stream, cat, mem, out, H, V);
   return NN_OK;
 }
 
@@ -199,6 +202,8 @@ static int k_lstm_feed_forward(Launch &L) {
 // NeuroNet.cl:2265-2297
 __global__ void lstm_cat_grad_kernel(const float *__restrict__ grad, float *__restrict__ cg,
                                      const float *__restrict__ mem, const float *__restrict__ cat, int H, int V) {
+  pdl_wait();
+  pdl_trigger();
   size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (t >= (size_t)V * H) return;
   int id = (int)(t % H);
@@ -221,8 +226,7 @@ static int k_lstm_concatenated_gradient(Launch &L) {
   float *g = L.buf(0, (size_t)V * H), *cg = L.buf(1, (size_t)V * 4 * H), *mem = L.buf(2, (size_t)2 * V * H);
   float *cat = L.buf(3, (size_t)V * 4 * H);
   if (!g || !cg || !mem || !cat) return NN_ERR_BOUNDS;
-  lstm_cat_grad_kernel<<<grid1d((size_t)V * H, 256), 256, 0, L.stream>>>(g, cg, mem, cat, H, V);
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, lstm_cat_grad_kernel, grid1d((size_t)V * H, 256), 256, 0, L.stream, g, cg, mem, cat, H, V);
   return NN_OK;
 }
 
@@ -232,6 +236,8 @@ static int k_lstm_concatenated_gradient(Launch &L) {
 __global__ void lstm_hg_prep_kernel(const float *__restrict__ cg, float *__restrict__ a, float *__restrict__ opnd,
                                     float *__restrict__ hidden, const float *__restrict__ out,
                                     const float *__restrict__ x, int H, int in, int V) {
+  pdl_wait();
+  pdl_trigger();
   size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   const size_t na = (size_t)V * 4 * H;
   if (t < na) {
@@ -257,6 +263,8 @@ __global__ void lstm_hg_prep_kernel(const float *__restrict__ cg, float *__restr
 // 32 gate columns x 32 series lanes; each lane sums its series in order, then the 32 lane sums.
 __global__ void __launch_bounds__(1024) lstm_bias_kernel(const float *__restrict__ cg, float *__restrict__ wg, int H,
                                                          int V, int ws, int rows) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float part[32][33];
   const int i = blockIdx.x * 32 + threadIdx.x;
   float s = 0.f;
@@ -279,6 +287,8 @@ __global__ void __launch_bounds__(1024) lstm_bias_kernel(const float *__restrict
 // weight-gradient rows from split-K partials: wg[g][i] = sum_s part[s][g][i] for i < N (the last
 // column of each (H+in+1)-float row is not a gradient the reference writes)
 __global__ void lstm_wg_reduce_kernel(float *__restrict__ wg, GradSrc src, int rows, int N, int ws) {
+  pdl_wait();
+  pdl_trigger();
   const size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (t >= (size_t)rows * N) return;
   const size_t g = t / N, i = t % N;
@@ -357,8 +367,7 @@ static int k_lstm_hidden_gradient(Launch &L) {
   float *a = L.scratch(1, na + nop);
   if (!a) return NN_ERR_CUDA;
   float *opnd = a + na;
-  lstm_hg_prep_kernel<<<grid1d(std::max(na, nop), 256), 256, 0, L.stream>>>(cg, a, opnd, hidden, out, x, H, in, V);
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, lstm_hg_prep_kernel, grid1d(std::max(na, nop), 256), 256, 0, L.stream, cg, a, opnd, hidden, out, x, H, in, V);
   // input gradient: dx[v][j] = sum_g a[v][g] w[g][H+j]; on the tensor cores in K slices whose
   // partials (16-byte rows when in % 4 == 0) are summed into dx
   if (in > 0) {
@@ -376,8 +385,7 @@ static int k_lstm_hidden_gradient(Launch &L) {
       if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
       L.counted();
       GradSrc src{part, fs.splits, per, 1.f};
-      reduce_partials_kernel<<<(unsigned)((per + 31) / 32), dim3(32, 8), 0, L.stream>>>(ig, src, per);
-      NN_CHECK_LAUNCH(L);
+      NN_LAUNCH_PDL(L, reduce_partials_kernel, (unsigned)((per + 31) / 32), dim3(32, 8), 0, L.stream, ig, src, per);
     } else {
       cudaError_t e = gemm_f32_wb<false, true>(L, fs, StoreInputGrad{ig, in});
       if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
@@ -401,8 +409,7 @@ static int k_lstm_hidden_gradient(Launch &L) {
       if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
       L.counted();
       GradSrc src{part, fs.splits, per, 1.f};
-      lstm_wg_reduce_kernel<<<grid1d(per, 256), 256, 0, L.stream>>>(wg, src, 4 * H, N, ws);
-      NN_CHECK_LAUNCH(L);
+      NN_LAUNCH_PDL(L, lstm_wg_reduce_kernel, grid1d(per, 256), 256, 0, L.stream, wg, src, 4 * H, N, ws);
     } else {
       cudaError_t e = gemm_f32<true, true>(fs, StoreStrided{wg, ws}, L.stream);
       if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
@@ -411,8 +418,7 @@ static int k_lstm_hidden_gradient(Launch &L) {
   }
   // the last bias write lands one element past the (4H)x(H+in+1) matrix: done only when the buffer holds it
   const int bias_rows = L.floats(2) > (size_t)4 * H * ws ? 4 * H : 4 * H - 1;
-  lstm_bias_kernel<<<(unsigned)((bias_rows + 31) / 32), dim3(32, 32), 0, L.stream>>>(cg, wg, H, V, ws, bias_rows);
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, lstm_bias_kernel, (unsigned)((bias_rows + 31) / 32), dim3(32, 32), 0, L.stream, cg, wg, H, V, ws, bias_rows);
   return NN_OK;
 }
 
@@ -420,6 +426,8 @@ static int k_lstm_hidden_gradient(Launch &L) {
 // NeuroNet.cl:2450-2475: elementwise over global (total, rows), l2 decay / total, raw rate.
 __global__ void lstm_adam_kernel(float *w, const float *wg, float *m, float *v, int total, int rows, float l, float b1,
                                  float b2) {
+  pdl_wait();
+  pdl_trigger();
   size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (t >= (size_t)total * rows) return;
   float g = clampf(nan0(wg[t]), -kMaxGrad, kMaxGrad);
@@ -438,12 +446,13 @@ static int lstm_adam_apply(const Launch &Lc, const float *grad) {
   size_t n = (size_t)total * rows;
   float *w = L.buf(0, n), *m = L.buf(2, n), *v = L.buf(3, n);
   if (!w || !m || !v) return NN_ERR_BOUNDS;
-  lstm_adam_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(w, grad, m, v, total, rows, L.f(4), L.f(5), L.f(6));
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, lstm_adam_kernel, grid1d(n, 256), 256, 0, L.stream, w, grad, m, v, total, rows, L.f(4), L.f(5), L.f(6));
   return NN_OK;
 }
 
 __global__ void scaled_copy_kernel(float *dst, const float *src, size_t n, float s) {
+  pdl_wait();
+  pdl_trigger();
   size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (i < n) dst[i] = src[i] * s;
 }
@@ -457,8 +466,7 @@ static int k_lstm_update_weights_adam(Launch &L) {
     // the weight gradient is a sum over series: the ranks' sums are summed (mean x world)
     float *slot = L.grad_slot(n);
     if (!slot) return NN_ERR_BOUNDS;
-    scaled_copy_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(slot, wg, n, (float)dp_world());
-    NN_CHECK_LAUNCH(L);
+    NN_LAUNCH_PDL(L, scaled_copy_kernel, grid1d(n, 256), 256, 0, L.stream, slot, wg, n, (float)dp_world());
     L.defer(lstm_adam_apply, slot);
     return NN_OK;
   }

@@ -32,6 +32,8 @@ namespace nn {
 __global__ void concat_ff_rows_kernel(const float *__restrict__ w, const float *__restrict__ x1,
                                       const float *__restrict__ x2, float *__restrict__ y, int in1, int in2,
                                       int outputs, int B, int act) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
   if (warp >= outputs * B) return;
   const int b = warp / outputs, i = warp % outputs;
@@ -61,6 +63,8 @@ __global__ void concat_ff_rows_kernel(const float *__restrict__ w, const float *
 __host__ __device__ __forceinline__ int concat_ldp(int in1, int in2) { return (in1 + in2 + 3) & ~3; }
 __global__ void concat_pack_kernel(const float *__restrict__ x1, const float *__restrict__ x2, float *__restrict__ p,
                                    int in1, int in2, int B) {
+  pdl_wait();
+  pdl_trigger();
   const int ldp = concat_ldp(in1, in2);
   const size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (t >= (size_t)B * ldp) return;
@@ -121,16 +125,13 @@ static int k_concat_ff(Launch &L) {
   float *y = L.buf(3, (size_t)L.B * outputs);
   if (!w || !x1 || !x2 || !y) return NN_ERR_BOUNDS;
   if (L.B <= 4) {
-    concat_ff_rows_kernel<<<ceil_div((size_t)outputs * L.B * 32, 256), 256, 0, L.stream>>>(w, x1, x2, y, in1, in2,
-                                                                                         outputs, L.B, act);
-    NN_CHECK_LAUNCH(L);
+    NN_LAUNCH_PDL(L, concat_ff_rows_kernel, ceil_div((size_t)outputs * L.B * 32, 256), 256, 0, L.stream, w, x1, x2, y, in1, in2, outputs, L.B, act);
     return NN_OK;
   }
   const int ldp = concat_ldp(in1, in2);
   float *p = L.scratch(2, (size_t)L.B * ldp);
   if (!p) return NN_ERR_CUDA;
-  concat_pack_kernel<<<grid1d((size_t)L.B * ldp, 256), 256, 0, L.stream>>>(x1, x2, p, in1, in2, L.B);
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, concat_pack_kernel, grid1d((size_t)L.B * ldp, 256), 256, 0, L.stream, x1, x2, p, in1, in2, L.B);
   FastShape fs{L.B, outputs, K, 1, 1, 0, p, ldp, 0, w, ld, 0};
   cudaError_t e = gemm_f32_wb<false, false>(L, fs, ConcatEpi{w, y, ld, K, outputs, act});
   if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
@@ -147,6 +148,8 @@ __global__ void __launch_bounds__(kCatWarps * 32)
     concat_hg_cols_kernel(const float *__restrict__ w, const float *__restrict__ g, const float *__restrict__ o1,
                           const float *__restrict__ o2, float *__restrict__ ig1, float *__restrict__ ig2, int outputs,
                           int in1, int in2, int B, int act1, int act2) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float part[kCatWarps][MAXB][33];
   const int K = in1 + in2;
   const int col = blockIdx.x * 32 + (threadIdx.x & 31), wv = threadIdx.x >> 5;
@@ -213,6 +216,8 @@ constexpr int kCatShort = 16;
 __global__ void concat_hg_second_kernel(const float *__restrict__ w, const float *__restrict__ g,
                                         const float *__restrict__ o2, float *__restrict__ ig2, int outputs, int in1,
                                         int in2, int B, int act2) {
+  pdl_wait();
+  pdl_trigger();
   const int b = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
   if (b >= B) return;
   const int ld = in1 + in2 + 1;
@@ -246,9 +251,7 @@ static int k_concat_hg(Launch &L) {
   float *ig1 = L.buf(4, (size_t)L.B * in1), *ig2 = L.buf(5, (size_t)L.B * in2);
   if (!w || !g || !o1 || !o2 || !ig1 || !ig2) return NN_ERR_BOUNDS;
   if (L.B <= 4) {
-    concat_hg_cols_kernel<4><<<ceil_div(K, 32), kCatWarps * 32, 0, L.stream>>>(w, g, o1, o2, ig1, ig2, outputs,
-                                                                              in1, in2, L.B, act1, act2);
-    NN_CHECK_LAUNCH(L);
+    NN_LAUNCH_PDL(L, concat_hg_cols_kernel<4>, ceil_div(K, 32), kCatWarps * 32, 0, L.stream, w, g, o1, o2, ig1, ig2, outputs, in1, in2, L.B, act1, act2);
     return NN_OK;
   }
   if (in2 <= kCatShort && in1 > 0 && tma_store_ok(ig1, in1, 0, 1, in1) && ((uintptr_t)o1 & 15) == 0) {
@@ -259,9 +262,7 @@ static int k_concat_hg(Launch &L) {
     if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
     L.counted();
     if (in2 > 0) {
-      concat_hg_second_kernel<<<ceil_div((size_t)L.B * 32, 256), 256, 0, L.stream>>>(w, g, o2, ig2, outputs, in1,
-                                                                                   in2, L.B, act2);
-      NN_CHECK_LAUNCH(L);
+      NN_LAUNCH_PDL(L, concat_hg_second_kernel, ceil_div((size_t)L.B * 32, 256), 256, 0, L.stream, w, g, o2, ig2, outputs, in1, in2, L.B, act2);
     }
     return NN_OK;
   }
@@ -302,6 +303,8 @@ __device__ __forceinline__ void concat_momentum_step(float *w, float *dw, size_t
 __global__ void concat_adam_fused_kernel(float *w, const float *g, const float *x1, const float *x2, float *m,
                                          float *v, int n_out, int n_col, int in1, int in2, float l, float b1,
                                          float b2) {
+  pdl_wait();
+  pdl_trigger();
   const size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (t >= (size_t)n_out * n_col) return;
   const int i = (int)(t / n_col), j = (int)(t % n_col);
@@ -310,6 +313,8 @@ __global__ void concat_adam_fused_kernel(float *w, const float *g, const float *
 
 __global__ void concat_momentum_fused_kernel(float *w, const float *g, const float *x1, const float *x2, float *dw,
                                              int n_out, int n_col, int in1, int in2, float lr, float mom) {
+  pdl_wait();
+  pdl_trigger();
   const size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (t >= (size_t)n_out * n_col) return;
   const int i = (int)(t / n_col), j = (int)(t % n_col);
@@ -320,6 +325,8 @@ __global__ void concat_momentum_fused_kernel(float *w, const float *g, const flo
 template <bool ADAM>
 __global__ void concat_apply_kernel(float *w, float *m, float *v, GradSrc G, int n_out, int n_col, int ld, float a,
                                     float b1, float b2) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[8][33];
   const size_t t = blockIdx.x * (size_t)32 + threadIdx.x, n = (size_t)n_out * n_col;
   float s = 0.f;
@@ -357,12 +364,10 @@ static int concat_apply_src(const Launch &Lc, GradSrc G) {
   if (!w || !m || (ADAM && !v)) return NN_ERR_BOUNDS;
   const size_t n = (size_t)s.n_out * s.n_col;
   if (ADAM)
-    concat_apply_kernel<true><<<(unsigned)((n + 31) / 32), dim3(32, 8), 0, L.stream>>>(
-        w, m, v, G, s.n_out, s.n_col, ld, L.f(8), L.f(9), L.f(10));
+    NN_LAUNCH_PDL(L, concat_apply_kernel<true>, (unsigned)((n + 31) / 32), dim3(32, 8), 0, L.stream, w, m, v, G,
+                  s.n_out, s.n_col, ld, L.f(8), L.f(9), L.f(10));
   else
-    concat_apply_kernel<false><<<(unsigned)((n + 31) / 32), dim3(32, 8), 0, L.stream>>>(
-        w, m, nullptr, G, s.n_out, s.n_col, ld, L.f(7), L.f(8), 0.f);
-  NN_CHECK_LAUNCH(L);
+    NN_LAUNCH_PDL(L, concat_apply_kernel<false>, (unsigned)((n + 31) / 32), dim3(32, 8), 0, L.stream, w, m, nullptr, G, s.n_out, s.n_col, ld, L.f(7), L.f(8), 0.f);
   return NN_OK;
 }
 template <bool ADAM>
@@ -385,12 +390,10 @@ static int k_concat_update(Launch &L) {
   const size_t n = (size_t)s.n_out * s.n_col;
   if (L.B == 1 && !L.deferred()) {
     if (ADAM)
-      concat_adam_fused_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(w, g, x1, x2, m, v, s.n_out, s.n_col, s.in1,
-                                                                     s.in2, L.f(8), L.f(9), L.f(10));
+      NN_LAUNCH_PDL(L, concat_adam_fused_kernel, grid1d(n, 256), 256, 0, L.stream, w, g, x1, x2, m, v, s.n_out,
+                    s.n_col, s.in1, s.in2, L.f(8), L.f(9), L.f(10));
     else
-      concat_momentum_fused_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(w, g, x1, x2, m, s.n_out, s.n_col, s.in1,
-                                                                         s.in2, L.f(7), L.f(8));
-    NN_CHECK_LAUNCH(L);
+      NN_LAUNCH_PDL(L, concat_momentum_fused_kernel, grid1d(n, 256), 256, 0, L.stream, w, g, x1, x2, m, s.n_out, s.n_col, s.in1, s.in2, L.f(7), L.f(8));
     return NN_OK;
   }
   if (s.n_col != ld)
@@ -399,8 +402,7 @@ static int k_concat_update(Launch &L) {
   const int ldp = concat_ldp(s.in1, s.in2);
   float *p = L.scratch(2, (size_t)L.B * ldp);
   if (!p) return NN_ERR_CUDA;
-  concat_pack_kernel<<<grid1d((size_t)L.B * ldp, 256), 256, 0, L.stream>>>(x1, x2, p, s.in1, s.in2, L.B);
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, concat_pack_kernel, grid1d((size_t)L.B * ldp, 256), 256, 0, L.stream, x1, x2, p, s.in1, s.in2, L.B);
   GradSrc src;
   int rc = wgrad_fast(L, g, s.n_out, p, ldp, s.n_out, K, L.B, &src);
   if (rc) return rc;
@@ -416,6 +418,8 @@ constexpr float kSquashEps = 1.0e-6f;
 // outputs [n][2A] = (mu, log_std); noise [n][A]; actions [n][A]; log_probs [n]
 __global__ void sac_policy_kernel(const float *__restrict__ out, const float *__restrict__ noise,
                                   float *__restrict__ actions, float *__restrict__ logp, int A, int n) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= n) return;
   const float *o = out + (size_t)b * 2 * A;
@@ -437,13 +441,14 @@ static int k_sac_policy(Launch &L) {
   float *out = L.buf(0, (size_t)n * 2 * A), *noise = L.buf(1, (size_t)n * A), *act = L.buf(2, (size_t)n * A);
   float *lp = L.buf(3, (size_t)n);
   if (!out || !noise || !act || !lp) return NN_ERR_BOUNDS;
-  sac_policy_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(out, noise, act, lp, A, n);
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, sac_policy_kernel, grid1d(n, 256), 256, 0, L.stream, out, noise, act, lp, A, n);
   return NN_OK;
 }
 
 __global__ void sac_target_kernel(const float *q1, const float *q2, const float *r, const float *done,
                                   const float *logp, float *y, int n, float gamma, float alpha) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= n) return;
   y[b] = r[b] + gamma * (1.f - done[b]) * (fminf(q1[b], q2[b]) - alpha * logp[b]);
@@ -454,8 +459,7 @@ static int k_sac_target(Launch &L) {
   float *q1 = L.buf(0, n), *q2 = L.buf(1, n), *r = L.buf(2, n), *d = L.buf(3, n), *lp = L.buf(4, n);
   float *y = L.buf(5, n);
   if (!q1 || !q2 || !r || !d || !lp || !y) return NN_ERR_BOUNDS;
-  sac_target_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(q1, q2, r, d, lp, y, n, L.f(6), L.f(7));
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, sac_target_kernel, grid1d(n, 256), 256, 0, L.stream, q1, q2, r, d, lp, y, n, L.f(6), L.f(7));
   return NN_OK;
 }
 
@@ -468,6 +472,8 @@ __global__ void sac_policy_grad_kernel(const float *__restrict__ out, const floa
                                        const float *__restrict__ q2, const float *__restrict__ dq1,
                                        const float *__restrict__ dq2, float *__restrict__ grad, int A, int n,
                                        float alpha) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= n * A) return;
   const int b = t / A, j = t % A;
@@ -490,9 +496,7 @@ static int k_sac_policy_grad(Launch &L) {
   float *q1 = L.buf(3, n), *q2 = L.buf(4, n), *dq1 = L.buf(5, (size_t)n * A), *dq2 = L.buf(6, (size_t)n * A);
   float *grad = L.buf(7, (size_t)n * 2 * A);
   if (!out || !noise || !act || !q1 || !q2 || !dq1 || !dq2 || !grad) return NN_ERR_BOUNDS;
-  sac_policy_grad_kernel<<<grid1d((size_t)n * A, 256), 256, 0, L.stream>>>(out, noise, act, q1, q2, dq1, dq2, grad,
-                                                                          A, n, L.f(9));
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, sac_policy_grad_kernel, grid1d((size_t)n * A, 256), 256, 0, L.stream, out, noise, act, q1, q2, dq1, dq2, grad, A, n, L.f(9));
   return NN_OK;
 }
 

@@ -1132,6 +1132,16 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
+// Launch with programmatic stream serialization from a reference-kernel implementation (a function
+// with a Launch `L` that returns an NN_ status): failures return through L.fail, successes count as
+// one of the library's launches.  A kernel name with template commas goes in parentheses.
+#define NN_LAUNCH_PDL(L, ...)                                                        \
+  do {                                                                               \
+    cudaError_t e_ = launch_pdl(__VA_ARGS__);                                        \
+    if (e_ != cudaSuccess) return (L).fail(NN_ERR_CUDA, cudaGetErrorString(e_));     \
+    (L).counted();                                                                   \
+  } while (0)
+
 inline int sm_count() {
   static int n = 0;
   if (n == 0) {

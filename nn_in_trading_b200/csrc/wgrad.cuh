@@ -207,9 +207,7 @@ inline int wgrad_fast(Launch &L, const float *A, long long lda, const float *X, 
     cudaError_t e = tcgemm<true, true>(ft, PartialStoreT{part, M, ldp}, L.stream, device_status());
     if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
     L.counted();
-    colsum_rows_kernel<<<dim3((M + 31) / 32, splits), dim3(32, 32), 0, L.stream>>>(part, A, M, rows, lda, kchunk, ldp,
-                                                                                  N);
-    NN_CHECK_LAUNCH(L);
+    NN_LAUNCH_PDL(L, colsum_rows_kernel, dim3((M + 31) / 32, splits), dim3(32, 32), 0, L.stream, part, A, M, rows, lda, kchunk, ldp, N);
   } else if (tc) {
     if (N % 32 == 0 && tcgemm_row_sum_ok(fs)) {
       // the bias input (1): its gradient column is the row sum of A, which the GEMM's producer warps
@@ -230,16 +228,13 @@ inline int wgrad_fast(Launch &L, const float *A, long long lda, const float *X, 
   } else if (M <= kSmallM) {
     // few outputs: one pass over X computes every output row (a 128-row GEMM tile would be mostly
     // padding); the bias column is column N of the same pass
-    wgrad_small_m_kernel<<<dim3((N + 1 + 31) / 32, splits), dim3(32, 8), 0, L.stream>>>(part, A, lda, X, ldx, M, N,
-                                                                                         rows, kchunk, ldp);
-    NN_CHECK_LAUNCH(L);
+    NN_LAUNCH_PDL(L, wgrad_small_m_kernel, dim3((N + 1 + 31) / 32, splits), dim3(32, 8), 0, L.stream, part, A, lda, X, ldx, M, N, rows, kchunk, ldp);
   } else {
     cudaError_t e = sgemm_fast<true, true>(fs, PartialStoreLd{part, M, ldp, 1}, L.stream);
     if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
     L.counted();
     dim3 grid((M + 255) / 256, splits);
-    colsum_partial_kernel<<<grid, 256, 0, L.stream>>>(part, A, M, rows, lda, kchunk, ldp, N);
-    NN_CHECK_LAUNCH(L);
+    NN_LAUNCH_PDL(L, colsum_partial_kernel, grid, 256, 0, L.stream, part, A, M, rows, lda, kchunk, ldp, N);
   }
   out->p = part;
   out->splits = splits;
@@ -275,8 +270,7 @@ inline int finish_update(Launch &L, GradSrc src, size_t n, int (*apply)(const La
   if (L.deferred()) {
     float *slot = L.grad_slot(n);
     if (!slot) return NN_ERR_BOUNDS;
-    reduce_partials_kernel<<<(unsigned)((n + 31) / 32), dim3(32, 8), 0, L.stream>>>(slot, src, n);
-    NN_CHECK_LAUNCH(L);
+    NN_LAUNCH_PDL(L, reduce_partials_kernel, (unsigned)((n + 31) / 32), dim3(32, 8), 0, L.stream, slot, src, n);
     L.defer(apply, slot);
     return NN_OK;
   }
