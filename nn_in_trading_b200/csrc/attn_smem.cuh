@@ -305,6 +305,8 @@ __device__ __forceinline__ void tile_product(const float *A, int lda, const floa
 template <int KPL>
 __global__ void mh_score_smem_kernel(const float *__restrict__ qkv, float *__restrict__ score, int U, int H, int D,
                                      int mask, float koef) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float4 sm4[];
   float *sm = reinterpret_cast<float *>(sm4);
   const int ldq = pad4(D), ldk = pad4(U);
@@ -406,6 +408,8 @@ __host__ __device__ __forceinline__ int score_lds(int U) {
 template <int DPL, int SUB>
 __global__ void __launch_bounds__(256, 4) mh_out_smem_kernel(const float *__restrict__ scores, const float *__restrict__ qkv,
                                    float *__restrict__ out, int U, int H, int D) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float4 sm4[];
   float *sm = reinterpret_cast<float *>(sm4);
   const int lds = D % 4 == 0 ? score_lds(U) : pad4(U);
@@ -434,6 +438,8 @@ template <int DPL, int SUB>
 __global__ void mh_grad_smem_kernel(const float *__restrict__ qkv, float *__restrict__ qkv_g,
                                     const float *__restrict__ scores, const float *__restrict__ grad, int U, int H,
                                     int D, float koef) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float4 sm4[];
   float *sm = reinterpret_cast<float *>(sm4);
   const int lds = D % 4 == 0 ? score_lds(U) : pad4(U);

@@ -27,6 +27,8 @@ constexpr int kScoreKT = 128;
 
 __global__ void mh_score_kernel(const float *__restrict__ qkv, float *__restrict__ score, int units, int heads,
                                 int dim, int mask, float koef) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float sm[];
   const int dp = dim + 1;
   float *Ks = sm;                    // [kScoreKT][dim+1]
@@ -98,8 +100,7 @@ static int k_mh_attention_score(Launch &L) {
       auto fn = kpl <= 1 ? mh_score_smem_kernel<1> : kpl == 2 ? mh_score_smem_kernel<2>
               : kpl == 3 ? mh_score_smem_kernel<3> : mh_score_smem_kernel<4>;
       cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-      fn<<<dim3(heads, L.B), 256, sm, L.stream>>>(qkv, score, units, heads, dim, mask, koef);
-      NN_CHECK_LAUNCH(L);
+      NN_LAUNCH_PDL(L, fn, dim3(heads, L.B), 256, sm, L.stream, qkv, score, units, heads, dim, mask, koef);
       return NN_OK;
     }
   }
@@ -108,8 +109,7 @@ static int k_mh_attention_score(Launch &L) {
   if (smem > 200 * 1024) return L.fail(NN_ERR_UNSUPPORTED, "MHAttentionScore: key dimension too large");
   if (smem > 48 * 1024) cudaFuncSetAttribute(mh_score_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid(ceil_div(units, warps), heads, L.B);
-  mh_score_kernel<<<grid, warps * 32, smem, L.stream>>>(qkv, score, units, heads, dim, mask, koef);
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, mh_score_kernel, grid, warps * 32, smem, L.stream, qkv, score, units, heads, dim, mask, koef);
   return NN_OK;
 }
 
@@ -118,6 +118,8 @@ static int k_mh_attention_score(Launch &L) {
 constexpr int kOutVT = 64;
 __global__ void mh_out_kernel(const float *__restrict__ scores, const float *__restrict__ qkv, float *__restrict__ out,
                               int units, int heads, int dim) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float sm[];
   float *Vs = sm;                         // [kOutVT][dim]
   float *Ss = sm + kOutVT * dim;          // [warps][kOutVT]
@@ -186,8 +188,7 @@ static int k_mh_attention_out(Launch &L) {
       // head dimensions up to 16: half-warps take separate row blocks (no idle lanes)
       auto fn = dim <= 16 ? mh_out_smem_kernel<1, 2> : dpl <= 1 ? mh_out_smem_kernel<1, 1> : mh_out_smem_kernel<2, 1>;
       cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-      fn<<<dim3(heads, L.B), 256, sm, L.stream>>>(scores, qkv, out, units, heads, dim);
-      NN_CHECK_LAUNCH(L);
+      NN_LAUNCH_PDL(L, fn, dim3(heads, L.B), 256, sm, L.stream, scores, qkv, out, units, heads, dim);
       return NN_OK;
     }
   }
@@ -195,8 +196,7 @@ static int k_mh_attention_out(Launch &L) {
   size_t smem = (size_t)(kOutVT * dim + warps * kOutVT) * sizeof(float);
   if (smem > 48 * 1024) cudaFuncSetAttribute(mh_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid(ceil_div(units, warps), heads, L.B);
-  mh_out_kernel<<<grid, warps * 32, smem, L.stream>>>(scores, qkv, out, units, heads, dim);
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, mh_out_kernel, grid, warps * 32, smem, L.stream, scores, qkv, out, units, heads, dim);
   return NN_OK;
 }
 
@@ -209,6 +209,8 @@ static int k_mh_attention_out(Launch &L) {
 //   dK[u,d] = 1/koef * sum_q S[q,u] (V0[u]-A[q]) g[q,d] Q[q,d]
 __global__ void mh_grad_rowsum_kernel(const float *__restrict__ qkv, const float *__restrict__ scores,
                                       float *__restrict__ A, int units, int heads, int dim, int B) {
+  pdl_wait();
+  pdl_trigger();
   int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   int lane = threadIdx.x & 31;
   int rows = B * units * heads;  // (b, q, h)
@@ -227,6 +229,8 @@ __global__ void mh_grad_rowsum_kernel(const float *__restrict__ qkv, const float
 __global__ void mh_grad_kernel(const float *__restrict__ qkv, float *__restrict__ qkv_g,
                                const float *__restrict__ scores, const float *__restrict__ grad,
                                const float *__restrict__ A, int units, int heads, int dim, float koef, int B) {
+  pdl_wait();
+  pdl_trigger();
   size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   size_t total = (size_t)B * units * heads * dim;
   if (t >= total) return;
@@ -287,20 +291,16 @@ static int k_mh_attention_inside_gradients(Launch &L) {
       auto fn = dim <= 16 ? mh_grad_smem_kernel<1, 2>
                           : dpl <= 1 ? mh_grad_smem_kernel<1, 1> : mh_grad_smem_kernel<2, 1>;
       cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-      fn<<<dim3(heads, L.B), 256, sm, L.stream>>>(qkv, qkv_g, scores, grad, units, heads, dim, koef);
-      NN_CHECK_LAUNCH(L);
+      NN_LAUNCH_PDL(L, fn, dim3(heads, L.B), 256, sm, L.stream, qkv, qkv_g, scores, grad, units, heads, dim, koef);
       return NN_OK;
     }
   }
   size_t rows = (size_t)L.B * units * heads;
   float *A = L.scratch(2, rows);
   if (!A) return NN_ERR_CUDA;
-  mh_grad_rowsum_kernel<<<ceil_div(rows * 32, 256), 256, 0, L.stream>>>(qkv, scores, A, units, heads, dim, L.B);
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, mh_grad_rowsum_kernel, ceil_div(rows * 32, 256), 256, 0, L.stream, qkv, scores, A, units, heads, dim, L.B);
   size_t total = rows * dim;
-  mh_grad_kernel<<<grid1d(total, 256), 256, 0, L.stream>>>(qkv, qkv_g, scores, grad, A, units, heads, dim, koef,
-                                                           L.B);
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, mh_grad_kernel, grid1d(total, 256), 256, 0, L.stream, qkv, qkv_g, scores, grad, A, units, heads, dim, koef, L.B);
   return NN_OK;
 }
 
@@ -308,6 +308,8 @@ static int k_mh_attention_inside_gradients(Launch &L) {
 // NeuroNet.cl:1314-1347: out[i*so + i*dim + k] = nan0((a[i*s1 + i*dim + k] + b[i*s2 + i*dim + k]) * mult)
 __global__ void sum_matrix_kernel(const float *a, const float *bm, float *out, float *flags, int rows, int dim,
                                   float mult, int s1, int s2, int so, int fe) {
+  pdl_wait();
+  pdl_trigger();
   size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (t >= (size_t)rows * dim) return;
   size_t i = t / dim;
@@ -321,6 +323,8 @@ __global__ void sum_matrix_kernel(const float *a, const float *bm, float *out, f
 // Same with zero row shifts (the encoder's residual sums): a flat float4 stream.
 __global__ void sum_matrix_flat4_kernel(const float4 *a, const float4 *bm, float4 *out, float4 *flags, size_t n4,
                                         float mult) {
+  pdl_wait();
+  pdl_trigger();
   for (size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x; t < n4; t += (size_t)gridDim.x * blockDim.x) {
     const float4 x = a[t], y = bm[t];
     const float r[4] = {(x.x + y.x) * mult, (x.y + y.y) * mult, (x.z + y.z) * mult, (x.w + y.w) * mult};
@@ -354,14 +358,10 @@ static int k_sum_matrix(Launch &L) {
   if (s1 == 0 && s2 == 0 && so == 0 && n % 4 == 0 && al16(a) && al16(b) && al16(o) && (!flags || al16(flags))) {
     const size_t n4 = n / 4;
     const unsigned blocks = (unsigned)std::min<size_t>((n4 + 255) / 256, 148 * 16);
-    sum_matrix_flat4_kernel<<<blocks, 256, 0, L.stream>>>(
-        reinterpret_cast<const float4 *>(a), reinterpret_cast<const float4 *>(b), reinterpret_cast<float4 *>(o),
-        reinterpret_cast<float4 *>(flags), n4, L.f(4));
-    NN_CHECK_LAUNCH(L);
+    NN_LAUNCH_PDL(L, sum_matrix_flat4_kernel, blocks, 256, 0, L.stream, reinterpret_cast<const float4 *>(a), reinterpret_cast<const float4 *>(b), reinterpret_cast<float4 *>(o), reinterpret_cast<float4 *>(flags), n4, L.f(4));
     return NN_OK;
   }
-  sum_matrix_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(a, b, o, flags, rows, dim, L.f(4), s1, s2, so, fe);
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, sum_matrix_kernel, grid1d(n, 256), 256, 0, L.stream, a, b, o, flags, rows, dim, L.f(4), s1, s2, so, fe);
   return NN_OK;
 }
 
@@ -369,6 +369,8 @@ static int k_sum_matrix(Launch &L) {
 // NeuroNet.cl:1455-1486: per row, centre on the mean and divide by the
 // unbiased *variance* (not its root) only when it exceeds 1.  One warp per row.
 __global__ void normalize_rows_kernel(float *buf, int rows, int dim) {
+  pdl_wait();
+  pdl_trigger();
   int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   int lane = threadIdx.x & 31;
   if (warp >= rows) return;
@@ -393,6 +395,8 @@ __global__ void normalize_rows_kernel(float *buf, int rows, int dim) {
 // Same for rows of at most 32*EPL floats: the row is read once into registers.
 template <int EPL>
 __global__ void normalize_rows_reg_kernel(float *buf, int rows, int dim) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
@@ -430,12 +434,11 @@ static int k_normalize(Launch &L) {
   if (!b) return NN_ERR_BOUNDS;
   const unsigned blocks = ceil_div((size_t)rows * 32, 256);
   if (dim <= 64)
-    normalize_rows_reg_kernel<2><<<blocks, 256, 0, L.stream>>>(b, rows, dim);
+    NN_LAUNCH_PDL(L, normalize_rows_reg_kernel<2>, blocks, 256, 0, L.stream, b, rows, dim);
   else if (dim <= 128)
-    normalize_rows_reg_kernel<4><<<blocks, 256, 0, L.stream>>>(b, rows, dim);
+    NN_LAUNCH_PDL(L, normalize_rows_reg_kernel<4>, blocks, 256, 0, L.stream, b, rows, dim);
   else
-    normalize_rows_kernel<<<blocks, 256, 0, L.stream>>>(b, rows, dim);
-  NN_CHECK_LAUNCH(L);
+    NN_LAUNCH_PDL(L, normalize_rows_kernel, blocks, 256, 0, L.stream, b, rows, dim);
   return NN_OK;
 }
 
@@ -446,6 +449,8 @@ static int k_normalize(Launch &L) {
 template <int EPL>
 __global__ void sum_normalize_rows_kernel(const float *__restrict__ a, const float *__restrict__ bm,
                                           float *__restrict__ out, int rows, int dim, float mult) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
@@ -496,10 +501,9 @@ int sum_normalize_launch(Launch &L) {
   if (!a || !b || !o) return NN_ERR_BOUNDS;
   const unsigned blocks = ceil_div((size_t)rows * 32, 256);
   if (dim <= 64)
-    sum_normalize_rows_kernel<2><<<blocks, 256, 0, L.stream>>>(a, b, o, rows, dim, L.f(4));
+    NN_LAUNCH_PDL(L, sum_normalize_rows_kernel<2>, blocks, 256, 0, L.stream, a, b, o, rows, dim, L.f(4));
   else
-    sum_normalize_rows_kernel<4><<<blocks, 256, 0, L.stream>>>(a, b, o, rows, dim, L.f(4));
-  NN_CHECK_LAUNCH(L);
+    NN_LAUNCH_PDL(L, sum_normalize_rows_kernel<4>, blocks, 256, 0, L.stream, a, b, o, rows, dim, L.f(4));
   return NN_OK;
 }
 
@@ -507,6 +511,8 @@ int sum_normalize_launch(Launch &L) {
 // NeuroNet.cl:2479-2520 (LocalSoftMax / LocalSoftMaxGrad, NeuroNet.cl:392-420).
 // Row length is the local size of dimension 0; one warp per (sample, head) row.
 __global__ void softmax_fwd_kernel(const float *in, float *out, int rows, int size) {
+  pdl_wait();
+  pdl_trigger();
   int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   int lane = threadIdx.x & 31;
   if (warp >= rows) return;
@@ -534,6 +540,8 @@ __global__ void softmax_fwd_kernel(const float *in, float *out, int rows, int si
 }
 
 __global__ void softmax_bwd_kernel(const float *outp, const float *og, float *ig, int rows, int size) {
+  pdl_wait();
+  pdl_trigger();
   int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   int lane = threadIdx.x & 31;
   if (warp >= rows) return;
@@ -563,8 +571,7 @@ static int k_softmax_ff(Launch &L) {
   if (rc) return rc;
   float *in = L.buf(0, (size_t)size * rows), *out = L.buf(1, (size_t)size * rows);
   if (!in || !out) return NN_ERR_BOUNDS;
-  softmax_fwd_kernel<<<ceil_div((size_t)rows * 32, 256), 256, 0, L.stream>>>(in, out, rows, size);
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, softmax_fwd_kernel, ceil_div((size_t)rows * 32, 256), 256, 0, L.stream, in, out, rows, size);
   return NN_OK;
 }
 
@@ -575,12 +582,13 @@ static int k_softmax_hg(Launch &L) {
   size_t n = (size_t)size * rows;
   float *y = L.buf(0, n), *og = L.buf(1, n), *ig = L.buf(2, n);
   if (!y || !og || !ig) return NN_ERR_BOUNDS;
-  softmax_bwd_kernel<<<ceil_div((size_t)rows * 32, 256), 256, 0, L.stream>>>(y, og, ig, rows, size);
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, softmax_bwd_kernel, ceil_div((size_t)rows * 32, 256), 256, 0, L.stream, y, og, ig, rows, size);
   return NN_OK;
 }
 
 __global__ void softmax_og_kernel(const float *y, const float *t, float *g, size_t n) {
+  pdl_wait();
+  pdl_trigger();
   size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (i < n) g[i] = (y[i] == 0.f) ? 0.f : t[i] / y[i];
 }
@@ -588,14 +596,15 @@ static int k_softmax_og(Launch &L) {
   size_t n = (size_t)L.nd.g[0] * L.B;
   float *y = L.buf(0, n), *t = L.buf(1, n), *g = L.buf(2, n);
   if (!y || !t || !g) return NN_ERR_BOUNDS;
-  softmax_og_kernel<<<grid1d(n, 256), 256, 0, L.stream>>>(y, t, g, n);
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, softmax_og_kernel, grid1d(n, 256), 256, 0, L.stream, y, t, g, n);
   return NN_OK;
 }
 
 // -------------------------------------------------------------- Transpose
 // NeuroNet.cl:4237-4248, smem-tiled, per sample.
 __global__ void transpose_kernel(const float *in, float *out, int rows, int cols) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float tile[32][33];
   size_t b = blockIdx.z;
   const float *src = in + b * (size_t)rows * cols;
@@ -614,8 +623,7 @@ static int k_transpose(Launch &L) {
   float *in = L.buf(0, n), *out = L.buf(1, n);
   if (!in || !out) return NN_ERR_BOUNDS;
   dim3 grid(ceil_div(cols, 32), ceil_div(rows, 32), L.B);
-  transpose_kernel<<<grid, dim3(32, 8), 0, L.stream>>>(in, out, rows, cols);
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, transpose_kernel, grid, dim3(32, 8), 0, L.stream, in, out, rows, cols);
   return NN_OK;
 }
 
@@ -626,6 +634,8 @@ struct Parts {
   int w[4];
 };
 __global__ void concat_kernel(Parts parts, float *out, int n, int tot, int split) {
+  pdl_wait();
+  pdl_trigger();
   size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (t >= (size_t)n * tot) return;
   int row = (int)(t / tot), c = (int)(t % tot);
@@ -657,8 +667,7 @@ static int concat_common(Launch &L, bool split) {
   if (tot == 0 || n == 0) return NN_OK;
   float *o = L.buf(8, (size_t)n * tot);
   if (!o) return NN_ERR_BOUNDS;
-  concat_kernel<<<grid1d((size_t)n * tot, 256), 256, 0, L.stream>>>(parts, o, n, tot, split ? 1 : 0);
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, concat_kernel, grid1d((size_t)n * tot, 256), 256, 0, L.stream, parts, o, n, tot, split ? 1 : 0);
   return NN_OK;
 }
 static int k_concat(Launch &L) { return concat_common(L, false); }

@@ -22,6 +22,8 @@ namespace nn {
 // NeuroNet.cl:1900-1953
 __global__ void bn_ff_kernel(const float *__restrict__ in, float *__restrict__ opt, float *__restrict__ out,
                              float *__restrict__ hist, int N, int B, int batch, int width, int act, int training) {
+  pdl_wait();
+  pdl_trigger();
   int n = blockIdx.x * blockDim.x + threadIdx.x;
   if (n >= N) return;
   float *o = opt + (size_t)n * width;
@@ -82,8 +84,7 @@ static int k_batch_feed_forward(Launch &L) {
     hist = L.side(L.handle(1), (size_t)L.B * N * 3);
     if (!hist) return NN_ERR_CUDA;
   }
-  bn_ff_kernel<<<grid1d(N, 256), 256, 0, L.stream>>>(in, opt, out, hist, N, L.B, batch, width, act, training);
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, bn_ff_kernel, grid1d(N, 256), 256, 0, L.stream, in, opt, out, hist, N, L.B, batch, width, act, training);
   return NN_OK;
 }
 
@@ -102,6 +103,8 @@ static const float *bn_history(Launch &L, int opt_idx, int N) {
 __global__ void bn_hg_kernel(const float *__restrict__ opt, const float *__restrict__ g, const float *__restrict__ in,
                              float *__restrict__ ig, const float *__restrict__ hist, int N, int B, int width, int act,
                              int batch) {
+  pdl_wait();
+  pdl_trigger();
   int n = blockIdx.x * blockDim.x + threadIdx.x;
   if (n >= N) return;
   const float *o = opt + (size_t)n * width;
@@ -130,14 +133,15 @@ static int k_calc_hidden_gradient_batch(Launch &L) {
   if (!opt || !g || !in || !ig) return NN_ERR_BOUNDS;
   const float *hist = bn_history(L, 0, N);
   if (L.B > 1 && !hist) return NN_ERR_STATE;
-  bn_hg_kernel<<<grid1d(N, 256), 256, 0, L.stream>>>(opt, g, in, ig, hist, N, L.B, width, act, batch);
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, bn_hg_kernel, grid1d(N, 256), 256, 0, L.stream, opt, g, in, ig, hist, N, L.B, width, act, batch);
   return NN_OK;
 }
 
 // Per-neuron batch-mean gradients of gamma and beta: G[2n] = mean_b clamp(g_b) nx_b, G[2n+1] = mean_b clamp(g_b).
 __global__ void bn_grad_kernel(float *G, const float *__restrict__ opt, const float *__restrict__ g,
                                const float *__restrict__ hist, int N, int B, int width) {
+  pdl_wait();
+  pdl_trigger();
   int n = blockIdx.x * blockDim.x + threadIdx.x;
   if (n >= N) return;
   float sg = 0.f, sb = 0.f;
@@ -154,6 +158,8 @@ __global__ void bn_grad_kernel(float *G, const float *__restrict__ opt, const fl
 
 // UpdateBatchOptionsAdam arithmetic, NeuroNet.cl:2050-2098 (delta of beta copies delta of gamma).
 __global__ void bn_adam_apply_kernel(float *opt, const float *G, int N, float l, float b1, float b2) {
+  pdl_wait();
+  pdl_trigger();
   int n = blockIdx.x * blockDim.x + threadIdx.x;
   if (n >= N) return;
   float *o = opt + (size_t)n * 9;
@@ -179,6 +185,8 @@ __global__ void bn_adam_apply_kernel(float *opt, const float *G, int N, float l,
 
 // UpdateBatchOptionsMomentum arithmetic, NeuroNet.cl:2010-2038.
 __global__ void bn_momentum_apply_kernel(float *opt, const float *G, int N, float lr, float mom) {
+  pdl_wait();
+  pdl_trigger();
   int n = blockIdx.x * blockDim.x + threadIdx.x;
   if (n >= N) return;
   float *o = opt + (size_t)n * 7;
@@ -197,8 +205,7 @@ static int bn_adam_apply(const Launch &Lc, const float *G) {
   const int N = (int)L.nd.g[0];
   float *opt = L.buf(0, (size_t)N * 9);
   if (!opt) return NN_ERR_BOUNDS;
-  bn_adam_apply_kernel<<<grid1d(N, 256), 256, 0, L.stream>>>(opt, G, N, L.f(2), L.f(3), L.f(4));
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, bn_adam_apply_kernel, grid1d(N, 256), 256, 0, L.stream, opt, G, N, L.f(2), L.f(3), L.f(4));
   return NN_OK;
 }
 static int bn_momentum_apply(const Launch &Lc, const float *G) {
@@ -206,8 +213,7 @@ static int bn_momentum_apply(const Launch &Lc, const float *G) {
   const int N = (int)L.nd.g[0];
   float *opt = L.buf(0, (size_t)N * 7);
   if (!opt) return NN_ERR_BOUNDS;
-  bn_momentum_apply_kernel<<<grid1d(N, 256), 256, 0, L.stream>>>(opt, G, N, L.f(2), L.f(3));
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, bn_momentum_apply_kernel, grid1d(N, 256), 256, 0, L.stream, opt, G, N, L.f(2), L.f(3));
   return NN_OK;
 }
 
@@ -219,8 +225,7 @@ static int bn_update(Launch &L, int width, int (*apply)(const Launch &, const fl
   if (L.B > 1 && !hist) return NN_ERR_STATE;
   float *G = L.deferred() ? L.grad_slot((size_t)2 * N) : L.scratch(3, (size_t)2 * N);
   if (!G) return NN_ERR_BOUNDS;
-  bn_grad_kernel<<<grid1d(N, 256), 256, 0, L.stream>>>(G, opt, g, hist, N, L.B, width);
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, bn_grad_kernel, grid1d(N, 256), 256, 0, L.stream, G, opt, g, hist, N, L.B, width);
   if (L.deferred()) {
     L.defer(apply, G);
     return NN_OK;
@@ -233,6 +238,8 @@ static int k_update_batch_options_momentum(Launch &L) { return bn_update(L, 7, b
 // NeuroNet.cl:5742-5764: y = sqrt(var) (x - beta) / max(gamma, 1e-3) + mean
 __global__ void revin_ff_kernel(const float *in, const float *opt, float *out, int n, int B, int options_size,
                                 int width) {
+  pdl_wait();
+  pdl_trigger();
   size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (t >= (size_t)n * B) return;
   int i = (int)(t % n);
@@ -245,6 +252,8 @@ __global__ void revin_ff_kernel(const float *in, const float *opt, float *out, i
 // NeuroNet.cl:5767-5793
 __global__ void revin_hg_kernel(const float *in, float *in_gr, const float *opt, const float *out_gr, int n, int B,
                                 int options_size, int width, int act) {
+  pdl_wait();
+  pdl_trigger();
   size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
   if (t >= (size_t)n * B) return;
   int i = (int)(t % n);
@@ -272,8 +281,7 @@ static int k_revin_ff(Launch &L) {
   if (rc) return rc;
   float *in = L.buf(0, (size_t)n * L.B), *opt = L.buf(1, opt_need(osz, width)), *out = L.buf(2, (size_t)n * L.B);
   if (!in || !opt || !out) return NN_ERR_BOUNDS;
-  revin_ff_kernel<<<grid1d((size_t)n * L.B, 256), 256, 0, L.stream>>>(in, opt, out, n, L.B, osz, width);
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, revin_ff_kernel, grid1d((size_t)n * L.B, 256), 256, 0, L.stream, in, opt, out, n, L.B, osz, width);
   return NN_OK;
 }
 
@@ -284,8 +292,7 @@ static int k_revin_hg(Launch &L) {
   float *in = L.buf(0, (size_t)n * L.B), *ig = L.buf(1, (size_t)n * L.B), *opt = L.buf(2, opt_need(osz, width));
   float *og = L.buf(3, (size_t)n * L.B);
   if (!in || !ig || !opt || !og) return NN_ERR_BOUNDS;
-  revin_hg_kernel<<<grid1d((size_t)n * L.B, 256), 256, 0, L.stream>>>(in, ig, opt, og, n, L.B, osz, width, L.i(6));
-  NN_CHECK_LAUNCH(L);
+  NN_LAUNCH_PDL(L, revin_hg_kernel, grid1d((size_t)n * L.B, 256), 256, 0, L.stream, in, ig, opt, og, n, L.B, osz, width, L.i(6));
   return NN_OK;
 }
 

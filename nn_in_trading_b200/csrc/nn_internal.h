@@ -5,6 +5,7 @@
 #include <cstddef>
 #include <cstdint>
 #include <string>
+#include <utility>
 #include <vector>
 
 namespace nn {
@@ -153,5 +154,35 @@ inline dim3 grid1d(size_t n, int threads) { return dim3(ceil_div(n, threads)); }
     if (e_ != cudaSuccess) return (L).fail(NN_ERR_CUDA, cudaGetErrorString(e_));      \
     (L).counted();                                                                    \
   } while (0)
+
+// Launch with programmatic stream serialization (the kernel must call pdl_wait before it
+// touches global data).
+template <class... KArgs, class... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+// Launch with programmatic stream serialization from a reference-kernel implementation (a function
+// with a Launch `L` that returns an NN_ status): failures return through L.fail, successes count as
+// one of the library's launches.  A kernel name with template commas goes in parentheses.
+#define NN_LAUNCH_PDL(L, ...)                                                        \
+  do {                                                                               \
+    cudaError_t e_ = launch_pdl(__VA_ARGS__);                                        \
+    if (e_ != cudaSuccess) return (L).fail(NN_ERR_CUDA, cudaGetErrorString(e_));     \
+    (L).counted();                                                                   \
+  } while (0)
+
 
 }  // namespace nn

@@ -1097,6 +1097,7 @@ __global__ void pack_b_kernel(const float *B, long long ldb, int N, int K, uint8
                               int kstages) {
   constexpr int CH = BN * BK / 4;  // chunks per tile image half
   pdl_trigger();                   // the GEMM that consumes the image may start its prologue
+  pdl_wait();                      // the weights are final (the previous kernel may have updated them)
   const long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   if (t >= (long long)tiles_n * kstages * CH) return;
   const int q = (int)(t % CH);
@@ -1112,35 +1113,6 @@ __global__ void pack_b_kernel(const float *B, long long ldb, int N, int K, uint8
 }
 
 }  // namespace tc
-
-// Launch with programmatic stream serialization (the kernel must call pdl_wait before it
-// touches global data).
-template <class... KArgs, class... Args>
-inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-                              Args &&...args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
-  return e != cudaSuccess ? e : cudaGetLastError();
-}
-
-// Launch with programmatic stream serialization from a reference-kernel implementation (a function
-// with a Launch `L` that returns an NN_ status): failures return through L.fail, successes count as
-// one of the library's launches.  A kernel name with template commas goes in parentheses.
-#define NN_LAUNCH_PDL(L, ...)                                                        \
-  do {                                                                               \
-    cudaError_t e_ = launch_pdl(__VA_ARGS__);                                        \
-    if (e_ != cudaSuccess) return (L).fail(NN_ERR_CUDA, cudaGetErrorString(e_));     \
-    (L).counted();                                                                   \
-  } while (0)
 
 inline int sm_count() {
   static int n = 0;
@@ -1258,8 +1230,9 @@ inline cudaError_t tcgemm_launch(const FastShape &s, EP ep, cudaStream_t st, int
   }
   if (B_MODE == tc::OP_PACKED) {
     const long long n = (long long)tiles_n * kstages * (BN * BK / 4);
-    tc::pack_b_kernel<BN, BK, !B_NCONTIG><<<(unsigned)((n + 255) / 256), 256, 0, st>>>(s.B, s.ldb, s.N, s.K, img,
-                                                                                       tiles_n, kstages);
+    cudaError_t pe = launch_pdl(tc::pack_b_kernel<BN, BK, !B_NCONTIG>, (unsigned)((n + 255) / 256), 256, 0, st, s.B,
+                                s.ldb, s.N, s.K, img, tiles_n, kstages);
+    if (pe != cudaSuccess) return pe;
   }
   return launch_pdl(fn, grid, dim3(32 * (EPIW + tc::prod_warps(A_MODE, B_MODE) + 2)), C::SMEM, st, s, ep, err, va,
                     vb, ep.aligned4() ? 1 : 0, tiles_n, tiles_m, (int)total, img, kstages, tmA, tmB, tmO);
