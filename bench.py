@@ -259,7 +259,7 @@ class MLMHWorkload(Workload):
     key = "mlmh_encoder"
     name = "mlmh_encoder_4x120x64_h8k32_ff256"
     default_batch = 256
-    default_steps = 400  # about 1.2 s timed
+    default_steps = 400  # about 1.05 s timed
 
     def __init__(self, batch):
         super().__init__(batch)
@@ -302,7 +302,7 @@ class DenseWorkload(Workload):
     key = "dense_mlp"
     name = "dense_mlp_240_500tanh_500sigmoid_3"
     default_batch = 1
-    default_steps = 15000  # 15 runs of the 1000-step online configuration
+    default_steps = 25000  # 25 runs of the 1000-step online configuration, about 1.05 s timed
 
     def __init__(self, batch):
         super().__init__(batch)
@@ -347,7 +347,7 @@ class LSTMWorkload(Workload):
     key = "lstm_stack"
     name = "lstm_stack_in64_h256_x2_seq240"
     default_batch = 1024
-    default_steps = 4800  # 20 windows of 240 bars
+    default_steps = 5760  # 24 windows of 240 bars, about 1.15 s timed
 
     def __init__(self, batch):
         super().__init__(batch)
@@ -460,7 +460,7 @@ class SACWorkload(Workload):
     key = "sac"
     name = "sac_actor240x512x512x12_2critics246x512x512x1_tau0.005"
     default_batch = 4096
-    default_steps = 700
+    default_steps = 800  # about 1.07 s timed
 
     def __init__(self, batch):
         super().__init__(batch)
