@@ -89,6 +89,7 @@ __global__ void wgrad_small_m_kernel(float *p, const float *A, long long lda, co
 #pragma unroll
   for (int m = 0; m < kSmallM; ++m) s[m] = 0.f;
   if (n <= N) {
+#pragma unroll 4
     for (int r = r0 + (int)threadIdx.y; r < r1; r += 8) {
       const float x = n < N ? nan0(X[(size_t)r * ldx + n]) : 1.f;
       const float *a = A + (size_t)r * lda;  // the same M values for the whole warp (broadcast)
@@ -157,6 +158,7 @@ __global__ void ff_skinny_kernel(const float *__restrict__ w, const float *__res
   float s[kSkinny];
 #pragma unroll
   for (int o = 0; o < kSkinny; ++o) s[o] = 0.f;
+#pragma unroll 4
   for (int k = lane; k < inputs; k += 32) {
     const float xk = nan0(xb[k]);
 #pragma unroll
@@ -182,6 +184,7 @@ __global__ void chg_skinny_kernel(const float *__restrict__ w, const float *__re
   const int i = (int)(t % inputs);
   const float *gb = g + (t / inputs) * outputs;  // the same row for a warp's inputs (broadcast)
   float s = 0.f;
+#pragma unroll 4
   for (int k = 0; k < outputs; ++k) s += nan0(w[(size_t)k * (inputs + 1) + i]) * nan0(gb[k]);
   ig[t] = deactivate(s, o[t], act);
 }

@@ -225,6 +225,7 @@ __global__ void concat_hg_second_kernel(const float *__restrict__ w, const float
   float s[kCatShort];
 #pragma unroll
   for (int j = 0; j < kCatShort; ++j) s[j] = 0.f;
+#pragma unroll 4
   for (int k = lane; k < outputs; k += 32) {
     const float gk = gb[k];
     const float *wr = w + (size_t)k * ld + in1;
