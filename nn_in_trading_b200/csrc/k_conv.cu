@@ -325,8 +325,11 @@ __global__ void adam_conv_apply_split_kernel(float *w, float *m, float *v, GradS
   __shared__ float red[8][33];
   const size_t i = blockIdx.x * (size_t)32 + threadIdx.x;
   float s = 0.f;
-  if (i < n)
-    for (int k = threadIdx.y; k < G.splits; k += 8) s += G.p[k * G.stride + G.at(i)];
+  if (i < n) {
+    const size_t ga = G.at(i);
+#pragma unroll 4
+    for (int k = threadIdx.y; k < G.splits; k += 8) s += G.p[k * G.stride + ga];
+  }
   red[threadIdx.y][threadIdx.x] = s;
   __syncthreads();
   if (threadIdx.y != 0 || i >= n) return;

@@ -25,8 +25,11 @@ __global__ void reduce_partials_kernel(float *out, GradSrc src, size_t n) {
   __shared__ float red[8][33];
   const size_t i = blockIdx.x * (size_t)32 + threadIdx.x;
   float s = 0.f;
-  if (i < n)
-    for (int k = threadIdx.y; k < src.splits; k += 8) s += src.p[k * src.stride + src.at(i)];
+  if (i < n) {
+    const size_t j = src.at(i);
+#pragma unroll 4
+    for (int k = threadIdx.y; k < src.splits; k += 8) s += src.p[k * src.stride + j];
+  }
   red[threadIdx.y][threadIdx.x] = s;
   __syncthreads();
   if (threadIdx.y != 0 || i >= n) return;
@@ -419,8 +422,11 @@ __global__ void adam_dense_apply_split_kernel(float *w, float *m, float *v, Grad
   __shared__ float red[8][33];
   const size_t t = blockIdx.x * (size_t)32 + threadIdx.x, n = (size_t)n_out * n_col;
   float s = 0.f;
-  if (t < n)
-    for (int k = threadIdx.y; k < G.splits; k += 8) s += G.p[k * G.stride + G.at(t)];
+  if (t < n) {
+    const size_t ga = G.at(t);
+#pragma unroll 4
+    for (int k = threadIdx.y; k < G.splits; k += 8) s += G.p[k * G.stride + ga];
+  }
   red[threadIdx.y][threadIdx.x] = s;
   __syncthreads();
   if (threadIdx.y != 0 || t >= n) return;

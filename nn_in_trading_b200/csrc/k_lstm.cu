@@ -128,6 +128,7 @@ __global__ void lstm_gates_cell_kernel(const float *__restrict__ P, int splits, 
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
     float a = 0.f;
+#pragma unroll 4
     for (int sp = 0; sp < splits; ++sp) a += P[sp * pstride + v * ldp + id + g];
     pre[g] = a + nan0(w[(size_t)(id + g) * ws + bcol]);
   }

@@ -331,8 +331,11 @@ __global__ void concat_apply_kernel(float *w, float *m, float *v, GradSrc G, int
   __shared__ float red[8][33];
   const size_t t = blockIdx.x * (size_t)32 + threadIdx.x, n = (size_t)n_out * n_col;
   float s = 0.f;
-  if (t < n)
-    for (int k = threadIdx.y; k < G.splits; k += 8) s += G.p[k * G.stride + G.at(t)];
+  if (t < n) {
+    const size_t ga = G.at(t);
+#pragma unroll 4
+    for (int k = threadIdx.y; k < G.splits; k += 8) s += G.p[k * G.stride + ga];
+  }
   red[threadIdx.y][threadIdx.x] = s;
   __syncthreads();
   if (threadIdx.y != 0 || t >= n) return;

@@ -36,6 +36,7 @@ struct GradSrc {
   __device__ __forceinline__ float operator()(size_t idx) const {
     const size_t j = at(idx);
     float s = 0.f;
+#pragma unroll 4
     for (int k = 0; k < splits; ++k) s += p[k * stride + j];
     return s * scale;
   }
