@@ -150,6 +150,67 @@ __global__ void conv_dgrad_direct_kernel(const float *__restrict__ w, const floa
   ig[t] = deactivate(sum, o[t], act);
 }
 
+// Overlapping windows: one CTA of 256 threads per (sample, variable).  The row's output gradient
+// (n_win windows x wout channels, nan0) and the variable's weights go to shared memory; each window's
+// contribution P[k][r] = sum_h g[k][h] W[h][r] (r < window_in) is formed once, four windows' entries
+// per thread at a time, then every input adds the windows that cover it, k ascending, and takes the
+// derivative.  Every product keeps the reference's guard (a zero gradient adds nothing) and nan0; the
+// sum runs over h per window, then over the windows (the direct form interleaves the two).
+// Shared memory: n_win*wout + wout*(win+1) + n_win*win floats.
+__global__ void __launch_bounds__(256) conv_dgrad_overlap_kernel(const float *__restrict__ w,
+                                                                 const float *__restrict__ g,
+                                                                 const float *__restrict__ o, float *__restrict__ ig,
+                                                                 int inputs, int var, int outputs, int step, int win,
+                                                                 int wout, int act, int shift_out) {
+  extern __shared__ float sm[];
+  pdl_wait();
+  pdl_trigger();
+  const int n_win = outputs / wout;
+  const size_t bv = blockIdx.x;  // sample b, variable v: bv = b * var + v
+  const int v = (int)(bv % var);
+  float *gs_s = sm;                      // [n_win][wout]
+  float *ws_s = gs_s + n_win * wout;     // [wout][win + 1]
+  float *p_s = ws_s + wout * (win + 1);  // [n_win][win]
+  const float *gs = g + shift_out + bv * (size_t)outputs;
+  const float *ws = w + (size_t)v * wout * (win + 1);
+  for (int t = threadIdx.x; t < n_win * wout; t += 256) gs_s[t] = nan0(gs[t]);
+  for (int t = threadIdx.x; t < wout * (win + 1); t += 256) ws_s[t] = ws[t];
+  __syncthreads();
+  const int np = n_win * win;
+  for (int q0 = threadIdx.x; q0 < np; q0 += 4 * 256) {
+    int kq[4], rq[4];
+    float acc[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int q = min(q0 + 256 * j, np - 1);  // past the end: a duplicate, not stored
+      kq[j] = q / win;
+      rq[j] = q - kq[j] * win;
+      acc[j] = 0.f;
+    }
+#pragma unroll 2
+    for (int h = 0; h < wout; ++h) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float gr = gs_s[kq[j] * wout + h];
+        if (fabsf(gr) > 0.f) acc[j] += nan0(gr * ws_s[h * (win + 1) + rq[j]]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (q0 + 256 * j < np) p_s[q0 + 256 * j] = acc[j];
+  }
+  __syncthreads();
+  const float *ob = o + bv * (size_t)inputs;
+  float *igb = ig + bv * (size_t)inputs;
+  for (int i = threadIdx.x; i < inputs; i += 256) {
+    const int start = i < win ? 0 : (i - win) / step + 1;
+    const int stop = min(i / step + 1, n_win);
+    float sum = 0.f;
+    for (int k = start; k < stop; ++k) sum += p_s[k * win + i - k * step];
+    igb[i] = deactivate(sum, ob[i], act);
+  }
+}
+
 // Non-overlapping windows (step == window_in, input fully tiled): one GEMM per
 // variable, rows (sample, window), columns window offset, k output channel.
 struct CDLoadG {
@@ -259,6 +320,12 @@ static int k_calc_hidden_gradient_conv(Launch &L) {
     }
     if (e != cudaSuccess) return L.fail(NN_ERR_CUDA, cudaGetErrorString(e));
     L.counted();
+    return NN_OK;
+  }
+  const size_t smem = ((size_t)n_win * wout + (size_t)wout * (win + 1) + (size_t)n_win * win) * sizeof(float);
+  if (win > 0 && n_win > 0 && smem <= 48 * 1024 && (size_t)L.B * var <= 0x7fffffffu) {
+    NN_LAUNCH_PDL(L, conv_dgrad_overlap_kernel, (unsigned)((size_t)L.B * var), 256, smem, L.stream, w, g, o, ig,
+                  inputs, var, outputs, step, win, wout, act, shift_out);
     return NN_OK;
   }
   size_t total = (size_t)L.B * var * inputs;
