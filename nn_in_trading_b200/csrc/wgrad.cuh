@@ -182,11 +182,38 @@ constexpr int kSmallM = 16;
 __global__ void wgrad_small_m_kernel(float *p, const float *A, long long lda, const float *X, long long ldx, int M,
                                      int N, int rows, int kchunk, int ldp);
 
+// Split-K count of a weight gradient (the reduction runs over the batch's rows, few output tiles): the
+// fewest splits whose work items fill whole waves of the SMs within 3 % of the best of one, two or
+// three waves, at least 256 rows per split.  (A fixed target of two waves capped at 64 splits left
+// 64 of 148 SMs busy for a single 128 x 128 tile over a million rows.)
+inline int wgrad_splits(int M, int N, int K) {
+  const long long sms = 148;
+  const long long tiles = (long long)((M + 127) / 128) * ((N + 127) / 128);
+  if (tiles >= sms) return 1;
+  long long cap = K / 256;
+  if (cap < 1) cap = 1;
+  long long cand[3];
+  double eff[3], best = 0.0;
+  for (int w = 1; w <= 3; ++w) {
+    long long sp = w * sms / tiles;
+    if (sp > cap) sp = cap;
+    if (sp < 1) sp = 1;
+    const long long items = tiles * sp;
+    cand[w - 1] = sp;
+    eff[w - 1] = (double)items / (double)(sms * ((items + sms - 1) / sms));
+    if (eff[w - 1] > best) best = eff[w - 1];
+  }
+  long long pick = cand[2];
+  for (int i = 0; i < 3; ++i)
+    if (eff[i] >= best - 0.03 && cand[i] < pick) pick = cand[i];
+  return (int)pick;
+}
+
 // Weight gradient of a plain GEMM: G[m][n] = sum_r A[r*lda + m] * X[r*ldx + n] for n < N, and
 // G[m][N] = sum_r A[r*lda + m] (the bias column, input 1).  Partials per split into scratch 0.
 inline int wgrad_fast(Launch &L, const float *A, long long lda, const float *X, long long ldx, int M, int N, int rows,
                       GradSrc *out) {
-  int splits = fast_splits(M, N + 1, rows, 1);
+  int splits = wgrad_splits(M, N, rows);
   // tensor-core path: split boundaries on its 32-deep stages (so TMA can load whole stages)
   const int gran = tc_path(FastShape{M, N, rows, 1, 1, 0, A, lda, 0, X, ldx, 0}) ? 32 : 8;
   int kchunk = ((rows + splits - 1) / splits + gran - 1) / gran * gran;
