@@ -146,14 +146,11 @@ __global__ void lstm_gates_cell_kernel(const float *__restrict__ P, int splits, 
   out[t] = nan0(og * activate(m, ACT_TANH));
 }
 
-// K slices of the gate product: enough to give every SM a 128 x 64 tile, each at least 128 deep.
+// K slices of the gate product over 128 x 64 tiles: whole waves of the SMs, each slice at least 128
+// deep, at most 8 slices.
 static int lstm_ff_splits(int V, int N, int K) {
   const long long tiles = (long long)((V + 127) / 128) * ((N + 63) / 64);
-  long long want = (148 + tiles - 1) / tiles, cap = K / 128;
-  if (cap < 1) cap = 1;
-  if (want > cap) want = cap;
-  if (want > 8) want = 8;
-  return (int)(want < 1 ? 1 : want);
+  return wave_splits(tiles, std::min(K / 128, 8));
 }
 
 static int k_lstm_feed_forward(Launch &L) {
@@ -343,15 +340,9 @@ struct StoreInputGrad {
   }
 };
 
-// Split-K count for a product of `tiles` 128x128 output tiles over a reduction of K: enough slices
-// to give every SM a tile, each slice at least 128 deep.
-static int lstm_splits(long long tiles, int K) {
-  long long want = (148 + tiles - 1) / tiles, cap = K / 128;
-  if (cap < 1) cap = 1;
-  if (want > cap) want = cap;
-  if (want > 16) want = 16;
-  return (int)(want < 1 ? 1 : want);
-}
+// Split-K count for a product of `tiles` 128x128 output tiles over a reduction of K: whole waves of
+// the SMs, each slice at least 128 deep, at most 16 slices.
+static int lstm_splits(long long tiles, int K) { return wave_splits(tiles, std::min(K / 128, 16)); }
 
 static int k_lstm_hidden_gradient(Launch &L) {
   int H = (int)L.nd.g[0];

@@ -182,15 +182,13 @@ constexpr int kSmallM = 16;
 __global__ void wgrad_small_m_kernel(float *p, const float *A, long long lda, const float *X, long long ldx, int M,
                                      int N, int rows, int kchunk, int ldp);
 
-// Split-K count of a weight gradient (the reduction runs over the batch's rows, few output tiles): the
-// fewest splits whose work items fill whole waves of the SMs within 3 % of the best of one, two or
-// three waves, at least 256 rows per split.  (A fixed target of two waves capped at 64 splits left
-// 64 of 148 SMs busy for a single 128 x 128 tile over a million rows.)
-inline int wgrad_splits(int M, int N, int K) {
+// Split-K count of a product with `tiles` output tiles: the fewest splits (at most `cap`) whose work
+// items fill whole waves of the 148 SMs within 3 % of the best of one, two or three waves.  The time of
+// a split product goes as tiles / (SMs x wave efficiency), so equal efficiencies cost the same and the
+// fewer partials to sum win.
+inline int wave_splits(long long tiles, long long cap) {
   const long long sms = 148;
-  const long long tiles = (long long)((M + 127) / 128) * ((N + 127) / 128);
   if (tiles >= sms) return 1;
-  long long cap = K / 256;
   if (cap < 1) cap = 1;
   long long cand[3];
   double eff[3], best = 0.0;
@@ -207,6 +205,14 @@ inline int wgrad_splits(int M, int N, int K) {
   for (int i = 0; i < 3; ++i)
     if (eff[i] >= best - 0.03 && cand[i] < pick) pick = cand[i];
   return (int)pick;
+}
+
+// Split-K count of a weight gradient (the reduction runs over the batch's rows, few 128 x 128 output
+// tiles): whole waves as above, at least 256 rows per split.  (A fixed target of two waves capped at 64
+// splits left 64 of 148 SMs busy for a single tile over a million rows.)
+inline int wgrad_splits(int M, int N, int K) {
+  const long long tiles = (long long)((M + 127) / 128) * ((N + 127) / 128);
+  return wave_splits(tiles, K / 256);
 }
 
 // Weight gradient of a plain GEMM: G[m][n] = sum_r A[r*lda + m] * X[r*ldx + n] for n < N, and
