@@ -208,17 +208,52 @@ def _norm_cases():
     cases.append(Case("SoftUpdate/1000", "SoftUpdate", [A(1000), A(1000), 0.005], (1000,)))
     cases.append(Case("SoftUpdateAdam/1000", "SoftUpdateAdam",
                       [A(1000), A(1000), A(1000, "small"), A(1000, "pos", 1e-4), 0.005, 0.9, 0.999], (1000,)))
+    for n in (1, 3, 4, 63, 64, 65):
+        cases.append(Case(f"SoftUpdate/{n}", "SoftUpdate", [A(n), A(n), 0.005], (n,)))
+        cases.append(Case(f"SoftUpdateAdam/{n}", "SoftUpdateAdam",
+                          [A(n), A(n), A(n, "small"), A(n, "pos", 1e-4), 0.005, 0.9, 0.999], (n,)))
+    # tau = 1: the target becomes the source (a hard copy)
+    cases.append(Case("SoftUpdate/65-tau1", "SoftUpdate", [A(65), A(65), 1.0], (65,)))
     cases.append(Case("Transpose/7x13", "Transpose", [A(91), A(91, "zeros")], (7, 13)))
+    for rows, cols in ((1, 1), (1, 65), (65, 1), (3, 4), (63, 64), (64, 65), (33, 97)):
+        cases.append(Case(f"Transpose/{rows}x{cols}", "Transpose", [A(rows * cols), A(rows * cols, "zeros")],
+                          (rows, cols)))
     cases.append(Case("ConcatenateBuffers/5", "ConcatenateBuffers",
                       [A(15), 3, A(20), 4, A(5), 1, A(10), 2, A(50, "zeros")], (5, 2)))
     cases.append(Case("DeconcatenateBuffers/5", "DeconcatenateBuffers",
                       [A(15, "zeros"), 3, A(20, "zeros"), 4, A(5, "zeros"), 1, A(10, "zeros"), 2, A(50)], (5, 2)))
+    # (rows, windows, work-items per row); a zero window leaves its buffer untouched; NaN and inf
+    # entries become 0 on the way through
+    for n, ws, tw, init in ((1, (1, 0, 0, 0), 1, "normal"), (3, (3, 4, 63, 64), 4, "normal"),
+                            (4, (65, 1, 0, 2), 3, "nanmix"), (2, (0, 64, 0, 1), 64, "normal"),
+                            (7, (4, 4, 4, 4), 5, "nanmix")):
+        tot = sum(ws)
+        parts = []
+        for w in ws:
+            parts += [A(max(n * w, 1), init), w]
+        cases.append(Case(f"ConcatenateBuffers/{n}-{'-'.join(map(str, ws))}", "ConcatenateBuffers",
+                          parts + [A(n * tot, "zeros")], (n, tw)))
+        parts = []
+        for w in ws:
+            parts += [A(max(n * w, 1), "zeros"), w]
+        cases.append(Case(f"DeconcatenateBuffers/{n}-{'-'.join(map(str, ws))}", "DeconcatenateBuffers",
+                          parts + [A(n * tot, init)], (n, tw)))
     for opt, width in ((0, 7), (1, 9)):
         cases.append(Case(f"RevInFeedForward/opt{opt}", "RevInFeedForward",
                           [A(96), A(12 * width, "pos"), A(96, "zeros"), 12 * width, opt], (96,)))
         cases.append(Case(f"RevInHiddenGraddient/opt{opt}", "RevInHiddenGraddient",
                           [A(96, "act:-1"), A(96, "zeros"), A(12 * width, "pos", 3.0), A(96, "grad"), 12 * width, opt,
                            NONE], (96,)))
+        # options_size a whole number of option records (reads stay inside it), or 3 floats past one
+        # (the kernels then read options[shift + 4] up to options_size + 3: the array holds 4 more)
+        for n, size in ((1, width), (63, 5 * width), (64, 5 * width + 3), (65, 12 * width)):
+            arr = size + (0 if size % width == 0 else 4)
+            cases.append(Case(f"RevInFeedForward/opt{opt}/{n}-{size}", "RevInFeedForward",
+                              [A(n), A(arr, "pos"), A(n, "zeros"), size, opt], (n,)))
+            for act in (NONE, TANH):
+                cases.append(Case(f"RevInHiddenGraddient/opt{opt}/{n}-{size}/act{act}", "RevInHiddenGraddient",
+                                  [A(n, f"act:{act}"), A(n, "zeros"), A(arr, "pos", 3.0), A(n, "grad"), size, opt,
+                                   act], (n,)))
     return cases
 
 
@@ -275,7 +310,7 @@ def _lstm_cases():
                           [A(V * ins), ins, A((H + 3) * ws, "uniform", 0.5), A(V * 4 * H, "zeros"),
                            A(2 * V * H, "normal", 0.5), A(V * H, "uniform", 0.9)],
                           (H, 4, V), (1, 4, 1), meta={"lstm_hidden_zero": (H, ins) if hz else None}))
-    for H, V in ((16, 3), (5, 2)):
+    for H, V in ((16, 3), (5, 2), (1, 1), (3, 2), (4, 1), (63, 2), (64, 3), (65, 1)):
         cases.append(Case(f"LSTM_ConcatenatedGradient/{H}-{V}", "LSTM_ConcatenatedGradient",
                           [A(V * H, "grad", 10.0), A(V * 4 * H, "zeros"), A(2 * V * H), A(V * 4 * H, "unit")],
                           (H, V)))
