@@ -1,6 +1,7 @@
 """The oracle's restatement of the host sequencing, run over its numpy kernels, against the same
 sequencing run over the reference's own kernels (oracle/_ref, NeuroNet.cl compiled for the CPU):
-pins the numpy kernels at the real layer shapes of the dense MLP and the attention encoder."""
+pins the numpy kernels at the real layer shapes of the dense MLP and the attention encoder, and the
+sequencing of the LSTM stack and of the PatchTST-style network at reduced shapes."""
 import numpy as np
 import pytest
 
@@ -163,5 +164,116 @@ def test_quantile_head_numpy_oracle_matches_reference_kernels(sac):
             for (label, a), (_, b) in zip(_head_arrays(nets["numpy"]), _head_arrays(nets["reference"])):
                 check_close(f"step{s} {label}", a, b)
                 a[...] = b
+    finally:
+        O.use_backend("numpy")
+
+
+def _lstm_stack(spec, w):
+    layers = [O.ODense(spec.inputs * spec.series, K.NONE, 1, 0)]
+    ins = spec.inputs
+    for l in range(spec.layers):
+        L = O.OLSTM(spec.hidden, ins, spec.series, 1)
+        L.lstm_w[:] = w[f"lstm{l}"]
+        layers.append(L)
+        ins = spec.hidden
+    head = O.OConv(spec.hidden, spec.hidden, spec.inputs, spec.series, 1, K.NONE, 1)
+    head.conv_w[:] = w["head"]
+    layers.append(head)
+    return O.ONet(layers)
+
+
+def test_lstm_stack_numpy_oracle_matches_reference_kernels():
+    """Two LSTM layers and the 1x1-conv head over six series, bar by bar: every LSTM kernel
+    (LSTM_FeedForward, LSTM_ConcatenatedGradient, LSTM_HiddenGradient, LSTM_UpdateWeightsAdam) and
+    the head's conv kernels are the reference's own in one run and the numpy restatement in the
+    other.  The cell memory carries over from bar to bar in both runs.
+
+    The reference's LSTM_FeedForward reads h(t-1) from the output buffer that its other work-groups
+    overwrite with h(t) (NeuroNet.cl:2189-2261); the CPU executor runs work-groups in order, so with
+    several neurons per series the reference run would read a mix of h(t-1) and h(t) where the
+    restatement (and the CUDA library) read h(t-1).  Both runs therefore zero the recurrent weight
+    columns before every bar, which hides that race and nothing else; the golden cases with one
+    neuron per series pin the recurrent product itself."""
+    spec = C.LSTMSpec(inputs=8, hidden=32, layers=2, series=6, seq=6)
+    w = C.lstm_weights(spec)
+    xs = C.lstm_data(spec)
+    nets = {}
+    try:
+        for kind in ("numpy", "reference"):
+            O.use_backend(kind)
+            nets[kind] = _lstm_stack(spec, w)
+        for t in range(spec.seq):
+            for kind in ("numpy", "reference"):
+                for L in nets[kind].layers[1:3]:
+                    L.lstm_w.reshape(4 * L.H, L.inputs + L.H + 1)[:, :L.H] = 0.0
+                O.use_backend(kind)
+                nets[kind].step(xs[t].reshape(1, -1), xs[t + 1].reshape(1, -1))
+            a, b = nets["numpy"].layers, nets["reference"].layers
+            for li in (1, 2):
+                check_close(f"t{t} lstm{li} output", a[li].output, b[li].output)
+                check_close(f"t{t} lstm{li} memory", a[li].memory, b[li].memory)
+                check_close(f"t{t} lstm{li} weight gradient", a[li].lstm_wg, b[li].lstm_wg)
+                check_close(f"t{t} lstm{li} weights", a[li].lstm_w, b[li].lstm_w)
+                for name in ("lstm_w", "lstm_m", "lstm_v"):
+                    getattr(a[li], name)[:] = getattr(b[li], name)
+            check_close(f"t{t} head output", a[3].output, b[3].output)
+            check_close(f"t{t} input gradient", a[0].gradient, b[0].gradient)
+            for name in ("conv_w", "conv_m", "conv_v"):
+                getattr(a[3], name)[:] = getattr(b[3], name)
+    finally:
+        O.use_backend("numpy")
+
+
+def _patch_net(spec, B, w):
+    P, E, Cc = spec.patches, spec.embed, spec.channels
+    inp = O.ODense(Cc * spec.bars, K.NONE, B, 0)
+    norm = O.OBatchNorm(Cc * spec.bars, spec.norm_batch, B)
+    conv = O.OConv(spec.patch, spec.stride, E, P, Cc, K.NONE, B)
+    conv.conv_w[:] = w["conv"]
+    enc = O.OMLMH(E, spec.dk, spec.heads, P, spec.layers, K.NONE, B * Cc)
+    for i, ws in enumerate(w["encoder"]):
+        for name, arr in ws.items():
+            enc.w[i][name][0][:] = arr
+    head = O.OConv(P * E, P * E, spec.horizon, Cc, 1, K.NONE, B)
+    head.conv_w[:] = w["head"]
+    denorm = O.ORevIN(Cc * spec.horizon, norm, B)
+    return O.ONet([inp, norm, conv, enc, head, denorm])
+
+
+def test_patchtst_style_numpy_oracle_matches_reference_kernels():
+    """Batch norm, the overlapping-window patch convolution, one attention encoder layer over the
+    channels' patch sequences (7 patches, 2 heads of 8: the shared-memory attention shapes), the
+    flattening conv head and RevIN: every forward and backward kernel call is the reference's own in
+    one run and the numpy restatement in the other (batch 2: the weight updates are the mean
+    gradient's, formed in numpy in both runs)."""
+    spec = C.PatchSpec(channels=3, bars=64, patch=16, stride=8, embed=16, heads=2, dk=8, layers=1, horizon=12,
+                       norm_batch=5)
+    B = 2
+    w = C.patch_weights(spec)
+    xs, ts = C.patch_data(spec, B, 3)
+    nets = {}
+    try:
+        for kind in ("numpy", "reference"):
+            O.use_backend(kind)
+            nets[kind] = _patch_net(spec, B, w)
+        names = ["input", "batchnorm", "conv", "encoder", "head", "revin"]
+        for s in range(3):
+            for kind in ("numpy", "reference"):
+                O.use_backend(kind)
+                nets[kind].step(xs[s], ts[s])
+            a, b = nets["numpy"].layers, nets["reference"].layers
+            for li, name in enumerate(names):
+                check_close(f"s{s} {name} output", a[li].output, b[li].output)
+                check_close(f"s{s} {name} gradient", a[li].gradient, b[li].gradient)
+            check_close(f"s{s} bn options", a[1].options, b[1].options)
+            a[1].options[:] = b[1].options
+            for li in (2, 4):
+                check_close(f"s{s} layer{li} conv weights", a[li].conv_w, b[li].conv_w)
+                for name in ("conv_w", "conv_m", "conv_v"):
+                    getattr(a[li], name)[:] = getattr(b[li], name)
+            for i in range(spec.layers):
+                for name in ("qkv", "w0", "ff1", "ff2"):
+                    for j in range(3):
+                        a[3].w[i][name][j][:] = b[3].w[i][name][j]
     finally:
         O.use_backend("numpy")
