@@ -37,6 +37,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <exception>
 #include <fstream>
 #include <sstream>
 #include <string>
@@ -83,8 +84,18 @@ std::vector<int> parse_ints(const std::string &line) {
   std::vector<int> out;
   std::stringstream ss(line);
   std::string item;
-  while (std::getline(ss, item, ','))
-    if (!item.empty()) out.push_back(std::stoi(item));
+  while (std::getline(ss, item, ',')) {
+    if (item.empty()) continue;
+    size_t used = 0;
+    int v = 0;
+    try {
+      v = std::stoi(item, &used);
+    } catch (const std::exception &) {
+      used = 0;
+    }
+    if (used == 0 || item.find_first_not_of(" \t\r", used) != std::string::npos) die("not an integer: '" + item + "'");
+    out.push_back(v);
+  }
   return out;
 }
 
@@ -256,13 +267,27 @@ class DenseNet {
   std::vector<Upd> updates_;
 };
 
-int run_files(const std::string &dir, int steps) {
+struct NetSpec {
+  std::vector<int> sizes, acts;
+};
+
+// D/net.txt, read before the library is initialised so that a bad file costs no device work.
+NetSpec read_spec(const std::string &dir) {
   std::ifstream spec(dir + "/net.txt");
   if (!spec) die("cannot open " + dir + "/net.txt");
   std::string l1, l2;
   std::getline(spec, l1);
   std::getline(spec, l2);
-  const std::vector<int> sizes = parse_ints(l1), acts = parse_ints(l2);
+  NetSpec ns{parse_ints(l1), parse_ints(l2)};
+  if (ns.sizes.size() < 2 || ns.sizes.size() != ns.acts.size())
+    die(dir + "/net.txt: need at least two layer sizes and one activation per layer");
+  for (int n : ns.sizes)
+    if (n <= 0) die(dir + "/net.txt: layer sizes must be positive");
+  return ns;
+}
+
+int run_files(const std::string &dir, const NetSpec &ns, int steps) {
+  const std::vector<int> &sizes = ns.sizes, &acts = ns.acts;
   DenseNet net(sizes, acts);
   for (size_t l = 0; l + 1 < net.size(); ++l)
     net.set_weights(l, read_f32(dir + "/w" + std::to_string(l) + ".f32", (size_t)net.weight_count(l)));
@@ -336,8 +361,10 @@ int main(int argc, char **argv) {
     else die("unknown argument " + a + " (usage: --dir D --steps N | --synthetic --steps N; [--device K])");
   }
   if (steps <= 0 || (dir.empty() && !synthetic)) die("usage: --dir D --steps N | --synthetic --steps N; [--device K]");
+  NetSpec ns;
+  if (!synthetic) ns = read_spec(dir);
   NN(nn_init(device, 0));
-  const int rc = synthetic ? run_synthetic(steps) : run_files(dir, steps);
+  const int rc = synthetic ? run_synthetic(steps) : run_files(dir, ns, steps);
   NN(nn_shutdown());
   return rc;
 }

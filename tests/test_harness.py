@@ -34,3 +34,14 @@ def test_harness_rejects_bad_arguments(binary, args):
     r = subprocess.run([binary, *args], capture_output=True, text=True, timeout=60)
     assert r.returncode == 1
     assert "dense_online:" in r.stderr and "usage" in r.stderr
+
+
+@pytest.mark.parametrize("text,message", [("240,5x0,3\n-1,0,-1\n", "not an integer: '5x0'"),
+                                          ("240,500\n-1\n", "one activation per layer"),
+                                          ("240,0,3\n-1,0,-1\n", "layer sizes must be positive")])
+def test_harness_rejects_a_malformed_network_file(binary, tmp_path, text, message):
+    """The network file is checked before the library is initialised (no device work for a bad file)."""
+    (tmp_path / "net.txt").write_text(text)
+    r = subprocess.run([binary, "--dir", str(tmp_path), "--steps", "1"], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 1
+    assert message in r.stderr
